@@ -1,0 +1,390 @@
+// capi.cu -- the extern "C" surface declared in include/fhessm.h.
+//
+// Every entry point catches the engine's exceptions and turns them into a status code plus
+// a thread-local message; no C++ exception crosses the boundary.
+#include <cstring>
+#include <string>
+
+#include "../../include/fhessm.h"
+#include "engine.h"
+
+struct fhe_ctx {
+    fhe::Context cx;
+    explicit fhe_ctx(const fhe::Params& p) : cx(p) {}
+};
+struct fhe_ct {
+    fhe::Ciphertext c;
+    fhe_ctx* owner;
+};
+struct fhe_pt {
+    fhe::Plaintext p;
+    fhe_ctx* owner;
+};
+
+static thread_local std::string g_err;
+
+template <class F>
+static int guard(F&& f) {
+    try {
+        f();
+        return FHE_OK;
+    } catch (const fhe::Error& e) {
+        g_err = e.what();
+        return e.code < 0 ? e.code : FHE_ERR_ARG;
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return FHE_ERR_ARG;
+    }
+}
+
+#define REQUIRE(cond, msg) \
+    do {                   \
+        if (!(cond)) throw fhe::Error(msg, FHE_ERR_ARG); \
+    } while (0)
+
+static int nl_of(const fhe::Context& cx, int level) {
+    if (level < 0 || level >= cx.L) throw fhe::Error("level out of range", FHE_ERR_ARG);
+    return cx.L - level;
+}
+static void bind(fhe_ctx* c) { CUDA_CHECK(cudaSetDevice(c->cx.device)); }
+
+static fhe_ct* wrap(fhe_ctx* c, fhe::Ciphertext&& x) {
+    auto* r = new fhe_ct{std::move(x), c};
+    return r;
+}
+
+extern "C" {
+
+const char* fhe_last_error(void) { return g_err.c_str(); }
+
+int fhe_ctx_create(const fhe_params* p, fhe_ctx** out) {
+    return guard([&] {
+        REQUIRE(p && out, "null argument");
+        fhe::Params q;
+        q.logN = p->logN; q.L = p->L; q.K = p->K; q.alpha = p->alpha;
+        q.q0bits = p->q0bits; q.qbits = p->qbits; q.pbits = p->pbits;
+        q.hw = p->hw; q.sigma = p->sigma; q.device = p->device;
+        *out = new fhe_ctx(q);
+    });
+}
+void fhe_ctx_destroy(fhe_ctx* cx) {
+    if (!cx) return;
+    try { delete cx; } catch (...) {}
+}
+int fhe_ctx_moduli(const fhe_ctx* cx, uint64_t* out) {
+    return guard([&] {
+        REQUIRE(cx && out, "null argument");
+        std::memcpy(out, cx->cx.mods.data(), cx->cx.mods.size() * 8);
+    });
+}
+double fhe_ctx_scale(const fhe_ctx* cx, int level) {
+    if (!cx || level < 0 || level >= cx->cx.L) return 0.0;
+    return cx->cx.scale_at[cx->cx.L - level];
+}
+int fhe_ctx_sync(fhe_ctx* cx) {
+    return guard([&] {
+        REQUIRE(cx, "null argument");
+        bind(cx);
+        CUDA_CHECK(cudaStreamSynchronize(cx->cx.stream));
+    });
+}
+long long fhe_ctx_launches(const fhe_ctx* cx) { return cx ? cx->cx.launches : 0; }
+
+int fhe_keygen(fhe_ctx* cx, const uint8_t seed[32]) {
+    return guard([&] {
+        REQUIRE(cx && seed, "null argument");
+        bind(cx);
+        fhe::keygen(cx->cx, seed);
+    });
+}
+int fhe_keygen_rotations(fhe_ctx* cx, const int32_t* steps, int n, int conj) {
+    return guard([&] {
+        REQUIRE(cx && (steps || n == 0), "null argument");
+        bind(cx);
+        std::vector<int> v(steps, steps + n);
+        fhe::keygen_rotations(cx->cx, v.data(), n, conj != 0);
+    });
+}
+static fhe::SwitchKey* find_key(fhe::Context& c, uint64_t which) {
+    if (which == 0) {
+        if (!c.rlk) throw fhe::Error("no relinearisation key", FHE_ERR_KEY);
+        return c.rlk.get();
+    }
+    auto it = c.rot_keys.find(which);
+    if (it == c.rot_keys.end()) throw fhe::Error("no key for automorphism " + std::to_string(which), FHE_ERR_KEY);
+    return it->second.get();
+}
+int fhe_key_export(fhe_ctx* cx, uint64_t which, uint64_t* words) {
+    return guard([&] {
+        REQUIRE(cx && words, "null argument");
+        bind(cx);
+        auto& c = cx->cx;
+        fhe::SwitchKey* k = find_key(c, which);
+        fhe::DevBuf t(k->buf.words, c.stream);
+        CUDA_CHECK(cudaMemcpyAsync(t.p, k->buf.p, k->buf.words * 8, cudaMemcpyDeviceToDevice, c.stream));
+        fhe::key_to_mont(c, t.p, false);
+        fhe::download(c, words, t.p, t.words);
+    });
+}
+int fhe_key_import(fhe_ctx* cx, uint64_t which, const uint64_t* words) {
+    return guard([&] {
+        REQUIRE(cx && words, "null argument");
+        bind(cx);
+        auto& c = cx->cx;
+        auto key = std::make_unique<fhe::SwitchKey>();
+        const size_t w = (size_t)c.dnum_top * 2 * (c.L + c.K) * c.N;
+        key->buf = fhe::DevBuf(w, c.stream);
+        key->index = which;
+        fhe::upload(c, key->buf.p, words, w);
+        fhe::key_to_mont(c, key->buf.p, true);
+        if (which == 0) c.rlk = std::move(key);
+        else c.rot_keys[which] = std::move(key);
+    });
+}
+int fhe_secret_export(fhe_ctx* cx, int8_t* coeffs) {
+    return guard([&] {
+        REQUIRE(cx && coeffs, "null argument");
+        REQUIRE(!cx->cx.sk_coeff.empty(), "no secret key");
+        std::memcpy(coeffs, cx->cx.sk_coeff.data(), cx->cx.sk_coeff.size());
+    });
+}
+int fhe_pubkey_export(fhe_ctx* cx, uint64_t* words) {
+    return guard([&] {
+        REQUIRE(cx && words, "null argument");
+        REQUIRE(cx->cx.pk.p, "no public key");
+        bind(cx);
+        fhe::download(cx->cx, words, cx->cx.pk.p, cx->cx.pk.words);
+    });
+}
+uint64_t fhe_rot_index(const fhe_ctx* cx, int32_t step) { return cx ? fhe::rot_index(cx->cx, step) : 0; }
+
+int fhe_encode(fhe_ctx* cx, const double* re, const double* im, int n, int level, double scale, fhe_pt** out) {
+    return guard([&] {
+        REQUIRE(cx && re && out && n > 0, "null argument");
+        bind(cx);
+        auto& c = cx->cx;
+        const int nl = nl_of(c, level);
+        std::vector<std::complex<double>> z(n);
+        for (int i = 0; i < n; i++) z[i] = std::complex<double>(re[i], im ? im[i] : 0.0);
+        const double sc = scale > 0 ? scale : c.scale_at[nl];
+        *out = new fhe_pt{fhe::encode(c, z.data(), n, nl, sc), cx};
+    });
+}
+int fhe_decode(fhe_ctx* cx, const fhe_pt* pt, double* re, double* im) {
+    return guard([&] {
+        REQUIRE(cx && pt && re, "null argument");
+        bind(cx);
+        auto& c = cx->cx;
+        std::vector<std::complex<double>> z(c.N / 2);
+        fhe::decode(c, pt->p, z.data());
+        for (int i = 0; i < c.N / 2; i++) {
+            re[i] = z[i].real();
+            if (im) im[i] = z[i].imag();
+        }
+    });
+}
+void fhe_pt_free(fhe_pt* pt) { delete pt; }
+int fhe_pt_level(const fhe_pt* pt) { return pt ? pt->owner->cx.L - pt->p.nl : -1; }
+
+int fhe_encrypt(fhe_ctx* cx, const fhe_pt* pt, fhe_ct** out) {
+    return guard([&] {
+        REQUIRE(cx && pt && out, "null argument");
+        bind(cx);
+        *out = wrap(cx, fhe::encrypt(cx->cx, pt->p));
+    });
+}
+int fhe_decrypt(fhe_ctx* cx, const fhe_ct* ct, fhe_pt** out) {
+    return guard([&] {
+        REQUIRE(cx && ct && out, "null argument");
+        bind(cx);
+        *out = new fhe_pt{fhe::decrypt(cx->cx, ct->c), cx};
+    });
+}
+void fhe_ct_free(fhe_ct* ct) { delete ct; }
+int fhe_ct_level(const fhe_ct* ct) { return ct ? ct->owner->cx.L - ct->c.nl : -1; }
+double fhe_ct_scale(const fhe_ct* ct) { return ct ? ct->c.scale : 0.0; }
+int fhe_ct_copy(fhe_ctx* cx, const fhe_ct* a, fhe_ct** out) {
+    return guard([&] {
+        REQUIRE(cx && a && out, "null argument");
+        bind(cx);
+        *out = wrap(cx, fhe::ct_copy(cx->cx, a->c));
+    });
+}
+
+#define BINOP(name, fn)                                                     \
+    int name(fhe_ctx* cx, const fhe_ct* a, const fhe_ct* b, fhe_ct** out) { \
+        return guard([&] {                                                  \
+            REQUIRE(cx && a && b && out, "null argument");                  \
+            bind(cx);                                                       \
+            fhe::Ciphertext r;                                              \
+            fn(cx->cx, a->c, b->c, r);                                      \
+            *out = wrap(cx, std::move(r));                                  \
+        });                                                                 \
+    }
+BINOP(fhe_add, fhe::ct_add)
+BINOP(fhe_sub, fhe::ct_sub)
+BINOP(fhe_mul_ct_ct_relin, fhe::ct_mul_relin)
+
+int fhe_mul_ct_pt(fhe_ctx* cx, const fhe_ct* a, const fhe_pt* pt, fhe_ct** out) {
+    return guard([&] {
+        REQUIRE(cx && a && pt && out, "null argument");
+        bind(cx);
+        fhe::Ciphertext r;
+        fhe::ct_mul_pt(cx->cx, a->c, pt->p, r);
+        *out = wrap(cx, std::move(r));
+    });
+}
+int fhe_add_pt(fhe_ctx* cx, const fhe_ct* a, const fhe_pt* pt, fhe_ct** out) {
+    return guard([&] {
+        REQUIRE(cx && a && pt && out, "null argument");
+        bind(cx);
+        fhe::Ciphertext r;
+        fhe::ct_add_pt(cx->cx, a->c, pt->p, r);
+        *out = wrap(cx, std::move(r));
+    });
+}
+int fhe_mul_const(fhe_ctx* cx, const fhe_ct* a, double v, double scale, fhe_ct** out) {
+    return guard([&] {
+        REQUIRE(cx && a && out, "null argument");
+        bind(cx);
+        fhe::Ciphertext r;
+        const double sc = scale > 0 ? scale : cx->cx.scale_at[a->c.nl];
+        fhe::ct_mul_const(cx->cx, a->c, v, sc, r);
+        *out = wrap(cx, std::move(r));
+    });
+}
+int fhe_add_const(fhe_ctx* cx, const fhe_ct* a, double v, fhe_ct** out) {
+    return guard([&] {
+        REQUIRE(cx && a && out, "null argument");
+        bind(cx);
+        fhe::Ciphertext r;
+        fhe::ct_add_const(cx->cx, a->c, v, r);
+        *out = wrap(cx, std::move(r));
+    });
+}
+int fhe_rescale(fhe_ctx* cx, fhe_ct* ct) {
+    return guard([&] {
+        REQUIRE(cx && ct, "null argument");
+        bind(cx);
+        fhe::ct_rescale(cx->cx, ct->c);
+    });
+}
+int fhe_level_reduce(fhe_ctx* cx, fhe_ct* ct, int levels) {
+    return guard([&] {
+        REQUIRE(cx && ct && levels >= 0, "bad argument");
+        bind(cx);
+        fhe::ct_level_drop(cx->cx, ct->c, ct->c.nl - levels);
+    });
+}
+int fhe_rotate(fhe_ctx* cx, const fhe_ct* a, int32_t k, fhe_ct** out) {
+    return guard([&] {
+        REQUIRE(cx && a && out, "null argument");
+        bind(cx);
+        fhe::Ciphertext r;
+        fhe::ct_rotate(cx->cx, a->c, k, r);
+        *out = wrap(cx, std::move(r));
+    });
+}
+int fhe_rotate_hoisted(fhe_ctx* cx, const fhe_ct* a, const int32_t* ks, int n, fhe_ct** outs) {
+    return guard([&] {
+        REQUIRE(cx && a && ks && outs && n > 0, "null argument");
+        bind(cx);
+        std::vector<fhe::Ciphertext> r(n);
+        std::vector<int> v(ks, ks + n);
+        fhe::ct_rotate_hoisted(cx->cx, a->c, v.data(), n, r.data());
+        for (int i = 0; i < n; i++) outs[i] = wrap(cx, std::move(r[i]));
+    });
+}
+int fhe_conjugate(fhe_ctx* cx, const fhe_ct* a, fhe_ct** out) {
+    return guard([&] {
+        REQUIRE(cx && a && out, "null argument");
+        bind(cx);
+        fhe::Ciphertext r;
+        fhe::ct_conjugate(cx->cx, a->c, r);
+        *out = wrap(cx, std::move(r));
+    });
+}
+
+int fhe_ct_import(fhe_ctx* cx, const uint64_t* words, int level, double scale, fhe_ct** out) {
+    return guard([&] {
+        REQUIRE(cx && words && out, "null argument");
+        bind(cx);
+        auto& c = cx->cx;
+        const int nl = nl_of(c, level);
+        fhe::Ciphertext r = fhe::ct_alloc(c, nl);
+        r.scale = scale;
+        fhe::upload(c, r.buf.p, words, (size_t)2 * nl * c.N);
+        *out = wrap(cx, std::move(r));
+    });
+}
+int fhe_ct_export(fhe_ctx* cx, const fhe_ct* ct, uint64_t* words) {
+    return guard([&] {
+        REQUIRE(cx && ct && words, "null argument");
+        bind(cx);
+        auto& c = cx->cx;
+        const size_t w = (size_t)ct->c.nl * c.N;
+        fhe::download(c, words, ct->c.c(0), w);
+        fhe::download(c, words + w, ct->c.c(1), w);
+    });
+}
+int fhe_pt_import(fhe_ctx* cx, const uint64_t* words, int level, double scale, fhe_pt** out) {
+    return guard([&] {
+        REQUIRE(cx && words && out, "null argument");
+        bind(cx);
+        auto& c = cx->cx;
+        const int nl = nl_of(c, level);
+        fhe::Plaintext p;
+        p.buf = fhe::DevBuf((size_t)nl * c.N, c.stream);
+        p.nl = nl;
+        p.scale = scale;
+        fhe::upload(c, p.buf.p, words, (size_t)nl * c.N);
+        *out = new fhe_pt{std::move(p), cx};
+    });
+}
+int fhe_pt_export(fhe_ctx* cx, const fhe_pt* pt, uint64_t* words) {
+    return guard([&] {
+        REQUIRE(cx && pt && words, "null argument");
+        bind(cx);
+        fhe::download(cx->cx, words, pt->p.buf.p, (size_t)pt->p.nl * (cx->cx.N >> pt->p.log_rep));
+    });
+}
+int fhe_ntt_host(fhe_ctx* cx, uint64_t* words, int n, const int* mod_idx, int inverse) {
+    return guard([&] {
+        REQUIRE(cx && words && mod_idx && n > 0, "null argument");
+        bind(cx);
+        auto& c = cx->cx;
+        for (int i = 0; i < n; i++) REQUIRE(mod_idx[i] >= 0 && mod_idx[i] < c.L + c.K, "modulus index out of range");
+        fhe::DevBuf d((size_t)n * c.N, c.stream);
+        fhe::upload(c, d.p, words, d.words);
+        // one launch per run of <= 64 limbs sharing a LimbMap
+        for (int s = 0; s < n; s += fhe::kMaxMod) {
+            const int cnt = std::min(n - s, fhe::kMaxMod);
+            fhe::LimbMap mp{};
+            mp.base = d.p + (size_t)s * c.N; mp.poly_stride = 0; mp.nl = cnt;
+            for (int i = 0; i < cnt; i++) mp.mod[i] = (uint8_t)mod_idx[s + i];
+            fhe::ntt(c, mp, 1, inverse != 0, c.stream);
+        }
+        fhe::download(c, words, d.p, d.words);
+    });
+}
+int fhe_keyswitch_host(fhe_ctx* cx, const uint64_t* d, int level, const uint64_t* key, uint64_t* out0,
+                       uint64_t* out1) {
+    return guard([&] {
+        REQUIRE(cx && d && key && out0 && out1, "null argument");
+        bind(cx);
+        auto& c = cx->cx;
+        const int nl = nl_of(c, level);
+        fhe::SwitchKey k;
+        const size_t kw = (size_t)c.dnum_top * 2 * (c.L + c.K) * c.N;
+        k.buf = fhe::DevBuf(kw, c.stream);
+        fhe::upload(c, k.buf.p, key, kw);
+        fhe::key_to_mont(c, k.buf.p, true);
+        fhe::DevBuf dd((size_t)nl * c.N, c.stream), o((size_t)2 * nl * c.N, c.stream);
+        fhe::upload(c, dd.p, d, dd.words);
+        fhe::keyswitch(c, dd.p, nl, k, nullptr, nullptr, o.p, o.p + (size_t)nl * c.N, 1);
+        fhe::download(c, out0, o.p, (size_t)nl * c.N);
+        fhe::download(c, out1, o.p + (size_t)nl * c.N, (size_t)nl * c.N);
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,181 @@
+// engine.h -- the B200 CKKS evaluation engine: context, device objects and operations.
+//
+// One Context owns one CUDA device and one stream.  Every ciphertext / plaintext / key
+// lives in that device's HBM; the host only drives launches.  Words are uint64 residues
+// (canonical, [0, q)).  Layouts:
+//   polynomial with nl limbs : [limb][N]                     (limb i uses modulus q_i)
+//   ciphertext               : 2 polynomials, poly p at d + p * stride
+//   extended basis Q_l u P   : limbs 0..nl-1 are q_0..q_{nl-1}, then the K special primes
+//   switching key            : [digit][2 (b, a)][L + K][N], Montgomery form (x * 2^64 mod q)
+#pragma once
+#include <cuda_runtime.h>
+
+#include <complex>
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "modarith.cuh"
+
+namespace fhe {
+
+struct Error : std::runtime_error {
+    int code;
+    explicit Error(const std::string& s, int c = -1) : std::runtime_error(s), code(c) {}
+};
+
+#define CUDA_CHECK(x)                                                                            \
+    do {                                                                                         \
+        cudaError_t err__ = (x);                                                                 \
+        if (err__ != cudaSuccess)                                                                \
+            throw ::fhe::Error(std::string("CUDA error: ") + cudaGetErrorString(err__) + " at " + \
+                                   __FILE__ + ":" + std::to_string(__LINE__),                    \
+                               -3);                                                              \
+    } while (0)
+
+constexpr int kMaxMod = 64;
+
+// constant-memory copy of every modulus' constants (index: Q chain then P chain)
+// defined once: the library is one translation unit (fhessm.cu)
+__constant__ ModConst c_mod[kMaxMod];
+
+// Which limbs a batched kernel walks: count = npoly * nl limb-polynomials.
+struct LimbMap {
+    uint64_t* base;
+    long long poly_stride;   // words between consecutive polynomials
+    int nl;                  // limbs per polynomial
+    int skip_alpha;          // >0: skip limbs [poly*alpha, min(poly*alpha+alpha, skip_nq)) (ModUp own digit)
+    int skip_nq;
+    uint8_t mod[kMaxMod];    // modulus index of limb l
+};
+
+struct Params {
+    int logN = 16;
+    int L = 20;        // Q limbs at the top level
+    int K = 4;         // special primes
+    int alpha = 4;     // limbs per key-switching digit
+    int q0bits = 60, qbits = 45, pbits = 60;
+    int hw = 192;      // secret Hamming weight (0: uniform ternary)
+    double sigma = 3.19;
+    int device = 0;
+};
+
+struct Context;
+
+// ---- device objects -------------------------------------------------------------------
+struct DevBuf {
+    uint64_t* p = nullptr;
+    size_t words = 0;
+    cudaStream_t st = nullptr;
+    DevBuf() = default;
+    DevBuf(size_t w, cudaStream_t s);
+    ~DevBuf();
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+    DevBuf(DevBuf&& o) noexcept { *this = std::move(o); }
+    DevBuf& operator=(DevBuf&& o) noexcept;
+};
+
+struct Ciphertext {
+    DevBuf buf;
+    int nl = 0;            // current limb count
+    size_t stride = 0;     // words between c0 and c1
+    double scale = 1.0;
+    uint64_t* c(int p) const { return buf.p + (size_t)p * stride; }
+};
+
+struct Plaintext {
+    DevBuf buf;            // [nl][N] eval form (or [nl][N/rep] when compressed)
+    int nl = 0;
+    double scale = 1.0;
+    int log_rep = 0;       // >0: REP-periodic compressed plaintext, word i of a limb = comp[i >> log_rep]
+};
+
+struct SwitchKey {
+    DevBuf buf;            // [dnum_top][2][L+K][N], Montgomery form
+    uint64_t index = 0;    // automorphism index (0 for relinearisation)
+};
+
+// ---- context ----------------------------------------------------------------------------
+struct Context {
+    Params prm;
+    int logN = 0, N = 0, L = 0, K = 0, alpha = 0, dnum_top = 0;
+    std::vector<uint64_t> mods;      // L + K
+    std::vector<ModConst> mc;
+    std::vector<uint64_t> psi;       // minimal primitive 2N-th roots
+    std::vector<double> scale_at;    // FLEXIBLEAUTO-style scaling factor by limb count (index nl)
+    cudaStream_t stream = nullptr;
+    int device = 0;
+    uint64_t *d_tw = nullptr, *d_twp = nullptr, *d_itw = nullptr, *d_itwp = nullptr, *d_ninv = nullptr;
+    // ModDown / rescale constants (level independent): see build_tables()
+    uint64_t* d_md = nullptr;        // ModDown: [K] phatinv (+shoup), [L][K] phat mod q_i (+shoup), [L] Pinv (+shoup)
+    uint64_t* d_rs = nullptr;        // rescale: [L][L] (ql mod qi, ql^-1 mod qi, shoup)
+    std::map<int, uint64_t*> modup_tab;   // per nl: [dnum][alpha][2] qhat^-1, [dnum][ne][alpha][2] qhat mod t
+    // keys
+    DevBuf sk;                       // secret, eval form over all L+K moduli, [L+K][N]
+    std::vector<int8_t> sk_coeff;    // signed coefficients (client side)
+    DevBuf pk;                       // [2][L][N]
+    std::unique_ptr<SwitchKey> rlk;
+    std::map<uint64_t, std::unique_ptr<SwitchKey>> rot_keys;   // by automorphism index
+    uint8_t master[32] = {0};
+    uint32_t enc_counter = 0;
+    int launches = 0;                // kernel launches issued (for the launch count claim)
+
+    explicit Context(const Params& p);
+    ~Context();
+    Context(const Context&) = delete;
+
+    int dnum(int nl) const { return (nl + alpha - 1) / alpha; }
+    int ext_mod(int nl, int e) const { return e < nl ? e : L + (e - nl); }
+    const uint64_t* modup_table(int nl);
+    LimbMap qmap(uint64_t* base, int nl, long long poly_stride) const;
+    LimbMap extmap(uint64_t* base, int nl, long long poly_stride) const;   // Q_l u P
+};
+
+enum EwOp : int { EW_ADD = 0, EW_SUB = 1, EW_MULPT = 2, EW_ADDPT = 3, EW_NEG = 4 };
+
+// ---- low-level launches (ntt.cu, kernels.cu) ---------------------------------------------
+void ntt(const Context& cx, const LimbMap& mp, int npoly, bool inv, cudaStream_t st);
+
+// ---- operations (engine.cu) ---------------------------------------------------------------
+// key switching of d (nl limbs, eval) -> (out0, out1) added into add0/add1 (may be null),
+// then permuted by the automorphism `perm_k` (1 = identity).  out may alias add.
+void keyswitch(Context& cx, const uint64_t* d, int nl, const SwitchKey& key, const uint64_t* add0,
+               const uint64_t* add1, uint64_t* out0, uint64_t* out1, uint64_t perm_k);
+
+Ciphertext ct_alloc(Context& cx, int nl);
+Ciphertext ct_copy(Context& cx, const Ciphertext& a);
+void ct_add(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out);
+void ct_sub(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out);
+void ct_mul_pt(Context& cx, const Ciphertext& a, const Plaintext& pt, Ciphertext& out);
+void ct_add_pt(Context& cx, const Ciphertext& a, const Plaintext& pt, Ciphertext& out);
+void ct_mul_relin(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out);
+void ct_rescale(Context& cx, Ciphertext& a);
+void ct_level_drop(Context& cx, Ciphertext& a, int nl_target);   // drop limbs, no scaling
+void ct_automorph(Context& cx, const Ciphertext& a, uint64_t k, Ciphertext& out);
+void ct_rotate(Context& cx, const Ciphertext& a, int r, Ciphertext& out);
+void ct_conjugate(Context& cx, const Ciphertext& a, Ciphertext& out);
+void ct_rotate_hoisted(Context& cx, const Ciphertext& a, const int* rs, int n, Ciphertext* outs);
+void ct_mul_const(Context& cx, const Ciphertext& a, double v, double scale, Ciphertext& out);  // by round(v*scale)
+void ct_add_const(Context& cx, const Ciphertext& a, double v, Ciphertext& out);
+void ct_mul_int(Context& cx, const Ciphertext& a, int64_t v, Ciphertext& out);
+
+// encoding (host special FFT + device reduction/NTT)
+Plaintext encode(Context& cx, const std::complex<double>* z, int nslots, int nl, double scale);
+void decode(Context& cx, const Plaintext& pt, std::complex<double>* z);
+// client-side crypto (keys held by the context)
+void keygen(Context& cx, const uint8_t seed[32]);
+void keygen_rotations(Context& cx, const int* rs, int n, bool conj);
+uint64_t rot_index(const Context& cx, int r);
+Ciphertext encrypt(Context& cx, const Plaintext& pt);
+Plaintext decrypt(Context& cx, const Ciphertext& ct);
+
+// raw access (parity tests)
+void upload(Context& cx, uint64_t* dst, const uint64_t* src, size_t words);
+void download(Context& cx, uint64_t* dst, const uint64_t* src, size_t words);
+void key_to_mont(Context& cx, uint64_t* key, bool to_mont);   // in place, [dnum_top][2][L+K][N]
+
+}  // namespace fhe

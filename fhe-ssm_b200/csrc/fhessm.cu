@@ -1,0 +1,6 @@
+// fhessm.cu -- single translation unit of libfhessm.so (the kernels share one
+// __constant__ table of moduli, so the sources are compiled together).
+#include "kernels.cu"
+#include "ntt.cu"
+#include "engine.cu"
+#include "capi.cu"

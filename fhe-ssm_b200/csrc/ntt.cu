@@ -1,0 +1,262 @@
+// ntt.cu -- batched negacyclic NTT / inverse NTT for RNS limbs, N = 2^12 .. 2^16.
+//
+// Ordering (the reference's encoder states it for OpenFHE, hpc_gpu_port/periodic_encode.hpp:
+// 141-161 and :240-260): the forward transform takes natural-order coefficients to
+// bit-reversed evaluations with the root table Tab[brev(i)] = psi^i (Cooley-Tukey); the
+// inverse takes bit-reversed evaluations back to natural-order coefficients
+// (Gentleman-Sande) and multiplies by N^-1.
+//
+// Decomposition.  With N = R * 256 (R = 2^(logN-8), 16 <= R <= 256) the transform splits in
+// two kernels of 4096-word tiles held in shared memory, 256 threads, 16 words per thread:
+//   phase "col": the logN-8 stages with butterfly distance >= 256.  The limb is an R x 256
+//                row-major matrix and each column is an independent R-point transform;
+//                a tile is R rows x (4096/R) columns (>= 16 columns: 128-byte row segments).
+//   phase "row": the last 8 stages, distance < 256: each 256-word block is independent.
+// Inside a tile each thread runs 4 stages on 16 registers, the tile is exchanged through
+// shared memory, and the thread runs the remaining stages on another 16 registers.  Every
+// twiddle is Shoup-precomputed; all residues stay canonical.
+#include "engine.h"
+
+namespace fhe {
+
+template <bool INV>
+__device__ __forceinline__ void bfly(uint64_t& lo, uint64_t& hi, uint64_t w, uint64_t wp, uint64_t q) {
+    if (!INV) {
+        const uint64_t x = mul_shoup(hi, w, wp, q);
+        const uint64_t u = lo;
+        lo = mod_add(u, x, q);
+        hi = mod_sub(u, x, q);
+    } else {
+        const uint64_t u = lo, v = hi;
+        lo = mod_add(u, v, q);
+        hi = mul_shoup(mod_sub(u, v, q), w, wp, q);
+    }
+}
+
+__device__ __forceinline__ bool limb_skipped(const LimbMap& mp, int poly, int limb) {
+    if (mp.skip_alpha == 0) return false;
+    const int lo = poly * mp.skip_alpha;
+    return limb >= lo && limb < min(lo + mp.skip_alpha, mp.skip_nq);
+}
+
+// ---- phase "col": stages with distance >= 256 ----------------------------------------
+template <int LOGN, bool INV>
+__global__ void __launch_bounds__(256) k_ntt_col(LimbMap mp, const uint64_t* __restrict__ tw,
+                                                  const uint64_t* __restrict__ twp, const uint64_t* __restrict__ ninv) {
+    constexpr int N = 1 << LOGN;
+    constexpr int R = N >> 8;            // rows
+    constexpr int TC = 4096 / R;         // columns per tile
+    constexpr int G = R / 16;            // row groups (part A stride)
+    __shared__ uint64_t sm[4096];
+    const int y = blockIdx.y;
+    const int poly = y / mp.nl, limb = y % mp.nl;
+    if (limb_skipped(mp, poly, limb)) return;
+    const int m = mp.mod[limb];
+    uint64_t* a = mp.base + (size_t)poly * mp.poly_stride + (size_t)limb * N;
+    const uint64_t q = c_mod[m].q;
+    const uint64_t* T = tw + (size_t)m * N;
+    const uint64_t* Tp = twp + (size_t)m * N;
+    const int t = threadIdx.x;
+    const int c = t % TC, g = t / TC;    // part A: column c, rows g + G*k
+    const int col = blockIdx.x * TC + c;
+    uint64_t x[16];
+    if (!INV) {
+#pragma unroll
+        for (int k = 0; k < 16; k++) x[k] = a[(size_t)(g + G * k) * 256 + col];
+        // part A: distances R/2 .. R/16 (register stride h = 8,4,2,1); twiddle 2^s + k/(2h)
+#pragma unroll
+        for (int s = 0; s < 4; s++) {
+            const int h = 8 >> s;
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                if (k & h) continue;
+                const int idx = (1 << s) + k / (2 * h);
+                bfly<false>(x[k], x[k + h], T[idx], Tp[idx], q);
+            }
+        }
+        if (R == 16) {
+#pragma unroll
+            for (int k = 0; k < 16; k++) a[(size_t)(g + G * k) * 256 + col] = x[k];
+            return;
+        }
+#pragma unroll
+        for (int k = 0; k < 16; k++) sm[(g + G * k) * TC + c] = x[k];
+        __syncthreads();
+        const int a2 = t / TC;           // part B: rows 16*a2 + k
+#pragma unroll
+        for (int k = 0; k < 16; k++) x[k] = sm[(16 * a2 + k) * TC + c];
+        // part B: distances R/32 .. 1 (h = t_r), m_row = R/(2h), twiddle m_row + a2*(8/h) + k/(2h)
+#pragma unroll
+        for (int h = R / 32; h >= 1; h >>= 1) {
+            const int mrow = R / (2 * h);
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                if (k & h) continue;
+                const int idx = mrow + a2 * (8 / h) + k / (2 * h);
+                bfly<false>(x[k], x[k + h], T[idx], Tp[idx], q);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 16; k++) a[(size_t)(16 * a2 + k) * 256 + col] = x[k];
+    } else {
+        const int a2 = t / TC;
+        if (R == 16) {
+#pragma unroll
+            for (int k = 0; k < 16; k++) x[k] = a[(size_t)(g + G * k) * 256 + col];
+        } else {
+#pragma unroll
+            for (int k = 0; k < 16; k++) x[k] = a[(size_t)(16 * a2 + k) * 256 + col];
+            // inverse part B first: distances 1 .. R/32
+#pragma unroll
+            for (int h = 1; h <= R / 32; h <<= 1) {
+                const int mrow = R / (2 * h);
+#pragma unroll
+                for (int k = 0; k < 16; k++) {
+                    if (k & h) continue;
+                    const int idx = mrow + a2 * (8 / h) + k / (2 * h);
+                    bfly<true>(x[k], x[k + h], T[idx], Tp[idx], q);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 16; k++) sm[(16 * a2 + k) * TC + c] = x[k];
+            __syncthreads();
+#pragma unroll
+            for (int k = 0; k < 16; k++) x[k] = sm[(g + G * k) * TC + c];
+        }
+#pragma unroll
+        for (int s = 3; s >= 0; s--) {
+            const int h = 8 >> s;
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                if (k & h) continue;
+                const int idx = (1 << s) + k / (2 * h);
+                bfly<true>(x[k], x[k + h], T[idx], Tp[idx], q);
+            }
+        }
+        const uint64_t ni = ninv[2 * m], nip = ninv[2 * m + 1];
+#pragma unroll
+        for (int k = 0; k < 16; k++) a[(size_t)(g + G * k) * 256 + col] = mul_shoup(x[k], ni, nip, q);
+    }
+}
+
+// ---- phase "row": the last 8 stages, 256-word blocks ---------------------------------------
+template <int LOGN, bool INV>
+__global__ void __launch_bounds__(256) k_ntt_row(LimbMap mp, const uint64_t* __restrict__ tw,
+                                                  const uint64_t* __restrict__ twp) {
+    constexpr int N = 1 << LOGN;
+    constexpr int S1 = LOGN - 8;
+    __shared__ uint64_t sm[4096];
+    const int y = blockIdx.y;
+    const int poly = y / mp.nl, limb = y % mp.nl;
+    if (limb_skipped(mp, poly, limb)) return;
+    const int m = mp.mod[limb];
+    uint64_t* a = mp.base + (size_t)poly * mp.poly_stride + (size_t)limb * N + (size_t)blockIdx.x * 4096;
+    const uint64_t q = c_mod[m].q;
+    const uint64_t* T = tw + (size_t)m * N;
+    const uint64_t* Tp = twp + (size_t)m * N;
+    const int t = threadIdx.x;
+    const int b = t >> 4, r0 = t & 15;
+    const int bg = blockIdx.x * 16 + b;  // global 256-block index
+    uint64_t x[16];
+    if (!INV) {
+#pragma unroll
+        for (int k = 0; k < 16; k++) x[k] = a[b * 256 + r0 + 16 * k];
+        // part A: distances 128,64,32,16 (h = 8..1), twiddle 2^(S1+s) + bg*2^s + k/(2h)
+#pragma unroll
+        for (int s = 0; s < 4; s++) {
+            const int h = 8 >> s;
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                if (k & h) continue;
+                const int idx = (1 << (S1 + s)) + (bg << s) + k / (2 * h);
+                bfly<false>(x[k], x[k + h], T[idx], Tp[idx], q);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 16; k++) sm[b * 256 + r0 + 16 * k] = x[k];
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) x[k] = sm[b * 256 + 16 * r0 + k];
+        // part B: distances 8,4,2,1 (h), stage s' = 3 - log2 h: m = 2^(S1+4+s'), i = bg*2^(4+s') + r0*(8/h) + k/(2h)
+#pragma unroll
+        for (int sp = 0; sp < 4; sp++) {
+            const int h = 8 >> sp;
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                if (k & h) continue;
+                const int idx = (1 << (S1 + 4 + sp)) + (bg << (4 + sp)) + r0 * (8 / h) + k / (2 * h);
+                bfly<false>(x[k], x[k + h], T[idx], Tp[idx], q);
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) sm[b * 256 + 16 * r0 + k] = x[k];
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) a[b * 256 + r0 + 16 * k] = sm[b * 256 + r0 + 16 * k];
+    } else {
+#pragma unroll
+        for (int k = 0; k < 16; k++) sm[b * 256 + r0 + 16 * k] = a[b * 256 + r0 + 16 * k];
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) x[k] = sm[b * 256 + 16 * r0 + k];
+#pragma unroll
+        for (int sp = 3; sp >= 0; sp--) {
+            const int h = 8 >> sp;
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                if (k & h) continue;
+                const int idx = (1 << (S1 + 4 + sp)) + (bg << (4 + sp)) + r0 * (8 / h) + k / (2 * h);
+                bfly<true>(x[k], x[k + h], T[idx], Tp[idx], q);
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) sm[b * 256 + 16 * r0 + k] = x[k];
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; k++) x[k] = sm[b * 256 + r0 + 16 * k];
+#pragma unroll
+        for (int s = 3; s >= 0; s--) {
+            const int h = 8 >> s;
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                if (k & h) continue;
+                const int idx = (1 << (S1 + s)) + (bg << s) + k / (2 * h);
+                bfly<true>(x[k], x[k + h], T[idx], Tp[idx], q);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 16; k++) a[b * 256 + r0 + 16 * k] = x[k];
+    }
+}
+
+template <int LOGN>
+static void launch_ntt(const Context& cx, const LimbMap& mp, int count, bool inv, cudaStream_t st) {
+    constexpr int N = 1 << LOGN;
+    constexpr int R = N >> 8;
+    dim3 gcol(R / 16, count), grow(N / 4096, count);
+    if (!inv) {
+        k_ntt_col<LOGN, false><<<gcol, 256, 0, st>>>(mp, cx.d_tw, cx.d_twp, cx.d_ninv);
+        k_ntt_row<LOGN, false><<<grow, 256, 0, st>>>(mp, cx.d_tw, cx.d_twp);
+    } else {
+        k_ntt_row<LOGN, true><<<grow, 256, 0, st>>>(mp, cx.d_itw, cx.d_itwp);
+        k_ntt_col<LOGN, true><<<gcol, 256, 0, st>>>(mp, cx.d_itw, cx.d_itwp, cx.d_ninv);
+    }
+}
+
+void ntt(const Context& cx, const LimbMap& mp, int npoly, bool inv, cudaStream_t st) {
+    const int count = npoly * mp.nl;
+    if (count == 0) return;
+    switch (cx.logN) {
+        case 12: launch_ntt<12>(cx, mp, count, inv, st); break;
+        case 13: launch_ntt<13>(cx, mp, count, inv, st); break;
+        case 14: launch_ntt<14>(cx, mp, count, inv, st); break;
+        case 15: launch_ntt<15>(cx, mp, count, inv, st); break;
+        case 16: launch_ntt<16>(cx, mp, count, inv, st); break;
+        default: throw Error("ntt: logN must be in [12, 16]");
+    }
+    CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace fhe

@@ -1,0 +1,342 @@
+"""fhessm -- Python binding of the B200 CKKS evaluation engine (libfhessm.so, C-ABI in
+include/fhessm.h).
+
+The class ``CryptoContext`` mirrors the OpenFHE CryptoContext calls that the reference's
+server makes on its hot path (hpc_gpu_port/gpu_real_model.cu: KeyGen/EvalMultKeyGen
+:1293-1298, EvalRotateKeyGen :1299-1336, MakeCKKSPackedPlaintext :1577-1589,
+Encrypt/Decrypt :2202-2221, EvalMult + RescaleInPlace :2629-2632, EvalAdd :2692-2743,
+EvalRotate :2762-2765), with the same argument meaning: levels count consumed levels,
+rotation k moves slot i+k to slot i.  Errors raise ``FheError`` carrying the engine's
+status code and message; nothing falls back to another implementation.  The CUDA library
+must be built (``python -c "import __graft_entry__ as g; g.build()"``); importing this
+package on a machine without it raises.
+"""
+import ctypes as C
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libfhessm.so")
+
+_U64P = C.POINTER(C.c_uint64)
+_DP = C.POINTER(C.c_double)
+_VP = C.c_void_p
+
+
+class FheError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+class Params(C.Structure):
+    _fields_ = [("logN", C.c_int), ("L", C.c_int), ("K", C.c_int), ("alpha", C.c_int),
+                ("q0bits", C.c_int), ("qbits", C.c_int), ("pbits", C.c_int), ("hw", C.c_int),
+                ("sigma", C.c_double), ("device", C.c_int)]
+
+
+_SIGS = {
+    "fhe_last_error": (C.c_char_p, []),
+    "fhe_ctx_create": (C.c_int, [C.POINTER(Params), C.POINTER(_VP)]),
+    "fhe_ctx_destroy": (None, [_VP]),
+    "fhe_ctx_moduli": (C.c_int, [_VP, _U64P]),
+    "fhe_ctx_scale": (C.c_double, [_VP, C.c_int]),
+    "fhe_ctx_sync": (C.c_int, [_VP]),
+    "fhe_ctx_launches": (C.c_longlong, [_VP]),
+    "fhe_keygen": (C.c_int, [_VP, C.c_char_p]),
+    "fhe_keygen_rotations": (C.c_int, [_VP, C.POINTER(C.c_int32), C.c_int, C.c_int]),
+    "fhe_key_export": (C.c_int, [_VP, C.c_uint64, _U64P]),
+    "fhe_key_import": (C.c_int, [_VP, C.c_uint64, _U64P]),
+    "fhe_secret_export": (C.c_int, [_VP, C.POINTER(C.c_int8)]),
+    "fhe_pubkey_export": (C.c_int, [_VP, _U64P]),
+    "fhe_rot_index": (C.c_uint64, [_VP, C.c_int32]),
+    "fhe_encode": (C.c_int, [_VP, _DP, _DP, C.c_int, C.c_int, C.c_double, C.POINTER(_VP)]),
+    "fhe_decode": (C.c_int, [_VP, _VP, _DP, _DP]),
+    "fhe_pt_free": (None, [_VP]),
+    "fhe_pt_level": (C.c_int, [_VP]),
+    "fhe_encrypt": (C.c_int, [_VP, _VP, C.POINTER(_VP)]),
+    "fhe_decrypt": (C.c_int, [_VP, _VP, C.POINTER(_VP)]),
+    "fhe_ct_free": (None, [_VP]),
+    "fhe_ct_level": (C.c_int, [_VP]),
+    "fhe_ct_scale": (C.c_double, [_VP]),
+    "fhe_ct_copy": (C.c_int, [_VP, _VP, C.POINTER(_VP)]),
+    "fhe_mul_ct_pt": (C.c_int, [_VP, _VP, _VP, C.POINTER(_VP)]),
+    "fhe_mul_ct_ct_relin": (C.c_int, [_VP, _VP, _VP, C.POINTER(_VP)]),
+    "fhe_add": (C.c_int, [_VP, _VP, _VP, C.POINTER(_VP)]),
+    "fhe_sub": (C.c_int, [_VP, _VP, _VP, C.POINTER(_VP)]),
+    "fhe_add_pt": (C.c_int, [_VP, _VP, _VP, C.POINTER(_VP)]),
+    "fhe_mul_const": (C.c_int, [_VP, _VP, C.c_double, C.c_double, C.POINTER(_VP)]),
+    "fhe_add_const": (C.c_int, [_VP, _VP, C.c_double, C.POINTER(_VP)]),
+    "fhe_rescale": (C.c_int, [_VP, _VP]),
+    "fhe_level_reduce": (C.c_int, [_VP, _VP, C.c_int]),
+    "fhe_rotate": (C.c_int, [_VP, _VP, C.c_int32, C.POINTER(_VP)]),
+    "fhe_rotate_hoisted": (C.c_int, [_VP, _VP, C.POINTER(C.c_int32), C.c_int, C.POINTER(_VP)]),
+    "fhe_conjugate": (C.c_int, [_VP, _VP, C.POINTER(_VP)]),
+    "fhe_ct_import": (C.c_int, [_VP, _U64P, C.c_int, C.c_double, C.POINTER(_VP)]),
+    "fhe_ct_export": (C.c_int, [_VP, _VP, _U64P]),
+    "fhe_pt_import": (C.c_int, [_VP, _U64P, C.c_int, C.c_double, C.POINTER(_VP)]),
+    "fhe_pt_export": (C.c_int, [_VP, _VP, _U64P]),
+    "fhe_ntt_host": (C.c_int, [_VP, _U64P, C.c_int, C.POINTER(C.c_int), C.c_int]),
+    "fhe_keyswitch_host": (C.c_int, [_VP, _U64P, C.c_int, _U64P, _U64P, _U64P]),
+}
+
+_lib_handle = None
+
+
+def lib():
+    """The loaded CUDA engine.  Raises if libfhessm.so has not been built."""
+    global _lib_handle
+    if _lib_handle is None:
+        if not os.path.exists(LIB_PATH):
+            raise FheError(-1, f"libfhessm.so not built at {LIB_PATH}: run __graft_entry__.build()")
+        h = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            f = getattr(h, name)
+            f.restype = res
+            f.argtypes = args
+        _lib_handle = h
+    return _lib_handle
+
+
+def _check(rc):
+    if rc != 0:
+        raise FheError(rc, lib().fhe_last_error().decode())
+
+
+def _u64(a):
+    a = np.ascontiguousarray(a, dtype=np.uint64)
+    return a, a.ctypes.data_as(_U64P)
+
+
+class Plaintext:
+    def __init__(self, ctx, h):
+        self.ctx, self.h = ctx, h
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().fhe_pt_free(self.h)
+            self.h = None
+
+    @property
+    def level(self):
+        return lib().fhe_pt_level(self.h)
+
+
+class Ciphertext:
+    def __init__(self, ctx, h):
+        self.ctx, self.h = ctx, h
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().fhe_ct_free(self.h)
+            self.h = None
+
+    @property
+    def level(self):
+        return lib().fhe_ct_level(self.h)
+
+    @property
+    def scale(self):
+        return lib().fhe_ct_scale(self.h)
+
+    def words(self):
+        nl = self.ctx.L - self.level
+        out = np.empty((2, nl, self.ctx.N), dtype=np.uint64)
+        _check(lib().fhe_ct_export(self.ctx.h, self.h, out.ctypes.data_as(_U64P)))
+        return out
+
+
+def seed32(seed) -> bytes:
+    """32-byte seed from an int (little-endian, zero padded) or bytes."""
+    if isinstance(seed, (bytes, bytearray)):
+        assert len(seed) == 32
+        return bytes(seed)
+    return int(seed).to_bytes(8, "little") + bytes(24)
+
+
+class CryptoContext:
+    """One engine context (one GPU).  Names follow the OpenFHE calls of the reference."""
+
+    def __init__(self, logN=16, L=20, K=4, alpha=4, q0bits=60, qbits=45, pbits=60, hw=192, sigma=3.19, device=0):
+        self.p = Params(logN, L, K, alpha, q0bits, qbits, pbits, hw, sigma, device)
+        h = _VP()
+        _check(lib().fhe_ctx_create(C.byref(self.p), C.byref(h)))
+        self.h = h
+        self.logN, self.N, self.L, self.K, self.alpha = logN, 1 << logN, L, K, alpha
+        self.slots = self.N // 2
+        self.dnum = (L + alpha - 1) // alpha
+        m = np.empty(L + K, dtype=np.uint64)
+        _check(lib().fhe_ctx_moduli(self.h, m.ctypes.data_as(_U64P)))
+        self.moduli = m
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().fhe_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    # ---- context info
+    def GetScalingFactorReal(self, level):
+        return lib().fhe_ctx_scale(self.h, level)
+
+    def sync(self):
+        _check(lib().fhe_ctx_sync(self.h))
+
+    def launches(self):
+        return lib().fhe_ctx_launches(self.h)
+
+    def rot_index(self, k):
+        return lib().fhe_rot_index(self.h, k)
+
+    # ---- keys
+    def KeyGen(self, seed=1):
+        _check(lib().fhe_keygen(self.h, seed32(seed)))
+
+    def EvalRotateKeyGen(self, steps, conj=False):
+        arr = (C.c_int32 * len(steps))(*steps)
+        _check(lib().fhe_keygen_rotations(self.h, arr, len(steps), 1 if conj else 0))
+
+    def key_words(self, which=0):
+        out = np.empty((self.dnum, 2, self.L + self.K, self.N), dtype=np.uint64)
+        _check(lib().fhe_key_export(self.h, which, out.ctypes.data_as(_U64P)))
+        return out
+
+    def import_key(self, which, words):
+        w, p = _u64(words)
+        _check(lib().fhe_key_import(self.h, which, p))
+
+    def secret_coeffs(self):
+        s = np.empty(self.N, dtype=np.int8)
+        _check(lib().fhe_secret_export(self.h, s.ctypes.data_as(C.POINTER(C.c_int8))))
+        return s
+
+    def public_key_words(self):
+        out = np.empty((2, self.L, self.N), dtype=np.uint64)
+        _check(lib().fhe_pubkey_export(self.h, out.ctypes.data_as(_U64P)))
+        return out
+
+    # ---- encoding / encryption
+    def MakeCKKSPackedPlaintext(self, values, level=0, scale=0.0):
+        z = np.asarray(values, dtype=np.complex128).ravel()
+        re = np.ascontiguousarray(z.real)
+        im = np.ascontiguousarray(z.imag)
+        h = _VP()
+        _check(lib().fhe_encode(self.h, re.ctypes.data_as(_DP), im.ctypes.data_as(_DP), len(z), level, scale,
+                                C.byref(h)))
+        return Plaintext(self, h)
+
+    def Decode(self, pt):
+        re = np.empty(self.slots)
+        im = np.empty(self.slots)
+        _check(lib().fhe_decode(self.h, pt.h, re.ctypes.data_as(_DP), im.ctypes.data_as(_DP)))
+        return re + 1j * im
+
+    def Encrypt(self, pt):
+        h = _VP()
+        _check(lib().fhe_encrypt(self.h, pt.h, C.byref(h)))
+        return Ciphertext(self, h)
+
+    def Decrypt(self, ct):
+        h = _VP()
+        _check(lib().fhe_decrypt(self.h, ct.h, C.byref(h)))
+        return self.Decode(Plaintext(self, h))
+
+    def decrypt_pt(self, ct):
+        h = _VP()
+        _check(lib().fhe_decrypt(self.h, ct.h, C.byref(h)))
+        return Plaintext(self, h)
+
+    # ---- evaluation
+    def _bin(self, fn, a, b):
+        h = _VP()
+        _check(fn(self.h, a.h, b.h, C.byref(h)))
+        return Ciphertext(self, h)
+
+    def EvalMult(self, a, b):
+        if isinstance(b, Plaintext):
+            return self._bin(lib().fhe_mul_ct_pt, a, b)
+        return self._bin(lib().fhe_mul_ct_ct_relin, a, b)
+
+    def EvalAdd(self, a, b):
+        if isinstance(b, Plaintext):
+            return self._bin(lib().fhe_add_pt, a, b)
+        return self._bin(lib().fhe_add, a, b)
+
+    def EvalSub(self, a, b):
+        return self._bin(lib().fhe_sub, a, b)
+
+    def EvalMultConst(self, a, v, scale=0.0):
+        h = _VP()
+        _check(lib().fhe_mul_const(self.h, a.h, float(v), float(scale), C.byref(h)))
+        return Ciphertext(self, h)
+
+    def EvalAddConst(self, a, v):
+        h = _VP()
+        _check(lib().fhe_add_const(self.h, a.h, float(v), C.byref(h)))
+        return Ciphertext(self, h)
+
+    def RescaleInPlace(self, ct):
+        _check(lib().fhe_rescale(self.h, ct.h))
+
+    def LevelReduceInPlace(self, ct, levels):
+        _check(lib().fhe_level_reduce(self.h, ct.h, levels))
+
+    def EvalRotate(self, ct, k):
+        h = _VP()
+        _check(lib().fhe_rotate(self.h, ct.h, k, C.byref(h)))
+        return Ciphertext(self, h)
+
+    def EvalFastRotation(self, ct, ks):
+        n = len(ks)
+        arr = (C.c_int32 * n)(*ks)
+        outs = (_VP * n)()
+        _check(lib().fhe_rotate_hoisted(self.h, ct.h, arr, n, outs))
+        return [Ciphertext(self, outs[i]) for i in range(n)]
+
+    def EvalConj(self, ct):
+        h = _VP()
+        _check(lib().fhe_conjugate(self.h, ct.h, C.byref(h)))
+        return Ciphertext(self, h)
+
+    def Copy(self, ct):
+        h = _VP()
+        _check(lib().fhe_ct_copy(self.h, ct.h, C.byref(h)))
+        return Ciphertext(self, h)
+
+    # ---- raw words
+    def ct_from_words(self, words, level, scale=1.0):
+        w, p = _u64(words)
+        h = _VP()
+        _check(lib().fhe_ct_import(self.h, p, level, scale, C.byref(h)))
+        return Ciphertext(self, h)
+
+    def pt_from_words(self, words, level, scale=1.0):
+        w, p = _u64(words)
+        h = _VP()
+        _check(lib().fhe_pt_import(self.h, p, level, scale, C.byref(h)))
+        return Plaintext(self, h)
+
+    def pt_words(self, pt):
+        nl = self.L - pt.level
+        out = np.empty((nl, self.N), dtype=np.uint64)
+        _check(lib().fhe_pt_export(self.h, pt.h, out.ctypes.data_as(_U64P)))
+        return out
+
+    def ntt(self, words, mod_idx, inverse=False):
+        w = np.ascontiguousarray(words, dtype=np.uint64).copy()
+        n = w.size // self.N
+        mi = (C.c_int * n)(*[int(x) for x in mod_idx])
+        _check(lib().fhe_ntt_host(self.h, w.ctypes.data_as(_U64P), n, mi, 1 if inverse else 0))
+        return w
+
+    def keyswitch_raw(self, d, level, key):
+        d, dp = _u64(d)
+        k, kp = _u64(key)
+        nl = self.L - level
+        o0 = np.empty((nl, self.N), dtype=np.uint64)
+        o1 = np.empty_like(o0)
+        _check(lib().fhe_keyswitch_host(self.h, dp, level, kp, o0.ctypes.data_as(_U64P), o1.ctypes.data_as(_U64P)))
+        return o0, o1

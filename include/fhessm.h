@@ -1,0 +1,145 @@
+/*
+ * fhessm.h -- C-ABI of the B200 CKKS evaluation engine (libfhessm.so).
+ *
+ * The drop-in boundary for the hot path of xelananv/fhe-ssm.  The reference's server calls
+ * the OpenFHE / FIDESlib CryptoContext API with C++ shared pointers and exceptions
+ * (hpc_gpu_port/gpu_real_model.cu, harness/cpu_real_model.cpp); this header exports the same
+ * operations as plain C: opaque handles, host pointers and sizes, integer status codes.
+ * Each entry point names the reference call it replaces (file:line in the reference tree).
+ *
+ * Conventions
+ *  - Every function returns FHE_OK (0) or a negative status; fhe_last_error() returns the
+ *    message of the last failure on the calling thread.  Nothing degrades silently: a
+ *    request the engine cannot serve exactly is refused (the reference's "refuse loudly"
+ *    rule, gpu_real_model.cu:924-928, :975-993).
+ *  - A context owns one CUDA device and one stream; every handle it creates lives in that
+ *    device's memory.  Calls on one context must come from one thread at a time.
+ *  - "level" counts consumed levels as the reference's TrackedCt::used does
+ *    (gpu_real_model.cu:1547-1551): level 0 = all L limbs, level L-1 = one limb.
+ *  - Word layouts for raw import/export: a polynomial is [limb][N] uint64 residues in
+ *    evaluation (NTT) form, bit-reversed order; a ciphertext is [2][limbs][N]; a switching
+ *    key is [digit][2 (b, a)][L + K][N] with digit = ceil(L / alpha).
+ *  - Handles are freed with their fhe_*_free function; freeing NULL is a no-op.
+ */
+#ifndef FHESSM_H
+#define FHESSM_H
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FHE_OK 0
+#define FHE_ERR_ARG (-1)        /* bad argument */
+#define FHE_ERR_CUDA (-3)       /* CUDA runtime error */
+#define FHE_ERR_LEVEL (-4)      /* level / scale mismatch between operands */
+#define FHE_ERR_KEY (-5)        /* a required key is missing */
+#define FHE_ERR_RANGE (-6)      /* value out of the encodable range (refused) */
+#define FHE_ERR_PROTO (-7)      /* malformed request / file (server step) */
+
+typedef struct fhe_ctx fhe_ctx;
+typedef struct fhe_ct fhe_ct;
+typedef struct fhe_pt fhe_pt;
+
+typedef struct {
+    int logN;       /* ring degree 2^logN, 12..16 */
+    int L;          /* Q limbs at the top level (q0 + L-1 scaling primes) */
+    int K;          /* special primes */
+    int alpha;      /* limbs per key-switching digit (dnum = ceil(L / alpha)) */
+    int q0bits;     /* first modulus size (60) */
+    int qbits;      /* scaling modulus size (45) */
+    int pbits;      /* special modulus size (60) */
+    int hw;         /* secret Hamming weight (192); 0 = uniform ternary */
+    double sigma;   /* error width (3.19) */
+    int device;     /* CUDA device ordinal */
+} fhe_params;
+
+const char* fhe_last_error(void);
+
+/* ---- context ----------------------------------------------------------------------------
+ * replaces CCParams + GenCryptoContext + Enable (gpu_real_model.cu:1138-1164) and
+ * LoadContext / SetDevices (:1530, :1161): the chain, NTT tables and keys live on `device`. */
+int fhe_ctx_create(const fhe_params* p, fhe_ctx** out);
+void fhe_ctx_destroy(fhe_ctx* cx);
+/* the moduli chain: L Q-moduli then K special moduli */
+int fhe_ctx_moduli(const fhe_ctx* cx, uint64_t* out);
+/* FLEXIBLEAUTO scaling factor at `level` (CryptoParametersRNS::GetScalingFactorReal) */
+double fhe_ctx_scale(const fhe_ctx* cx, int level);
+int fhe_ctx_sync(fhe_ctx* cx);
+/* kernel launches issued by this context so far */
+long long fhe_ctx_launches(const fhe_ctx* cx);
+
+/* ---- keys -------------------------------------------------------------------------------
+ * replaces KeyGen + EvalMultKeyGen (gpu_real_model.cu:1293-1298); all randomness from the
+ * 32-byte seed through the ChaCha20 expander of hpc_gpu_port/seeded_keys.hpp:36-49. */
+int fhe_keygen(fhe_ctx* cx, const uint8_t seed[32]);
+/* replaces EvalRotateKeyGen(rots) (:1299-1336); conj != 0 adds the conjugation key */
+int fhe_keygen_rotations(fhe_ctx* cx, const int32_t* steps, int n, int conj);
+/* raw key material (canonical residues), for parity checks and key files:
+ * which = 0: relinearisation key; otherwise the automorphism index (5^r mod 2N, or 2N-1). */
+int fhe_key_export(fhe_ctx* cx, uint64_t which, uint64_t* words);
+int fhe_key_import(fhe_ctx* cx, uint64_t which, const uint64_t* words);
+int fhe_secret_export(fhe_ctx* cx, int8_t* coeffs);
+int fhe_pubkey_export(fhe_ctx* cx, uint64_t* words);   /* [2][L][N] (b, a) */
+uint64_t fhe_rot_index(const fhe_ctx* cx, int32_t step);
+
+/* ---- encoding ---------------------------------------------------------------------------
+ * replaces MakeCKKSPackedPlaintext(v, 1, level) (gpu_real_model.cu:1577-1589): n complex
+ * slot values (n divides N/2; a shorter vector repeats across the slots) encoded at `level`
+ * with the given scale (scale <= 0: the level's FLEXIBLEAUTO factor). */
+int fhe_encode(fhe_ctx* cx, const double* re, const double* im, int n, int level, double scale, fhe_pt** out);
+/* replaces Plaintext::GetRealPackedValue / GetCKKSPackedValue (:2211): N/2 slots */
+int fhe_decode(fhe_ctx* cx, const fhe_pt* pt, double* re, double* im);
+void fhe_pt_free(fhe_pt* pt);
+int fhe_pt_level(const fhe_pt* pt);
+
+/* ---- encryption -------------------------------------------------------------------------
+ * replaces Encrypt(pk, pt) / Decrypt(sk, ct) (gpu_real_model.cu:2202-2221, encCh/decCh) */
+int fhe_encrypt(fhe_ctx* cx, const fhe_pt* pt, fhe_ct** out);
+int fhe_decrypt(fhe_ctx* cx, const fhe_ct* ct, fhe_pt** out);
+void fhe_ct_free(fhe_ct* ct);
+int fhe_ct_level(const fhe_ct* ct);
+double fhe_ct_scale(const fhe_ct* ct);
+int fhe_ct_copy(fhe_ctx* cx, const fhe_ct* a, fhe_ct** out);
+
+/* ---- evaluation -------------------------------------------------------------------------
+ * EvalMult(ct, pt) without rescale (mulPt = this + fhe_rescale, gpu_real_model.cu:2629-2632) */
+int fhe_mul_ct_pt(fhe_ctx* cx, const fhe_ct* a, const fhe_pt* pt, fhe_ct** out);
+/* EvalMult(ct, ct) with relinearisation, no rescale (rmsnorm x^2 :3520, polyGate3 :4627) */
+int fhe_mul_ct_ct_relin(fhe_ctx* cx, const fhe_ct* a, const fhe_ct* b, fhe_ct** out);
+/* EvalAdd / EvalSub at equal level and scale (addAligned :2692-2743 aligns first) */
+int fhe_add(fhe_ctx* cx, const fhe_ct* a, const fhe_ct* b, fhe_ct** out);
+int fhe_sub(fhe_ctx* cx, const fhe_ct* a, const fhe_ct* b, fhe_ct** out);
+/* EvalAdd(ct, pt) (addPtV :2756-2759) */
+int fhe_add_pt(fhe_ctx* cx, const fhe_ct* a, const fhe_pt* pt, fhe_ct** out);
+/* EvalMult by a real constant encoded at `scale` (scale <= 0: the ct's level factor), no rescale */
+int fhe_mul_const(fhe_ctx* cx, const fhe_ct* a, double v, double scale, fhe_ct** out);
+/* EvalAdd of a real constant in every slot */
+int fhe_add_const(fhe_ctx* cx, const fhe_ct* a, double v, fhe_ct** out);
+/* RescaleInPlace (:2631, :2820) */
+int fhe_rescale(fhe_ctx* cx, fhe_ct* ct);
+/* LevelReduceInternalInPlace (experimental/gpu_real_model_x.cu:2778): drop limbs, no rescale */
+int fhe_level_reduce(fhe_ctx* cx, fhe_ct* ct, int levels);
+/* EvalRotate(ct, k) (:2762-2765): slot i of the result = slot i+k of the input */
+int fhe_rotate(fhe_ctx* cx, const fhe_ct* a, int32_t k, fhe_ct** out);
+/* hoisted rotations: one ModUp shared by n rotations (EvalFastRotation; used by the BSGS babies) */
+int fhe_rotate_hoisted(fhe_ctx* cx, const fhe_ct* a, const int32_t* ks, int n, fhe_ct** outs);
+/* EvalConj: complex conjugation of every slot (automorphism 2N-1, :1355-1369) */
+int fhe_conjugate(fhe_ctx* cx, const fhe_ct* a, fhe_ct** out);
+
+/* ---- raw words (parity tests, serialisation) -------------------------------------------- */
+int fhe_ct_import(fhe_ctx* cx, const uint64_t* words, int level, double scale, fhe_ct** out);
+int fhe_ct_export(fhe_ctx* cx, const fhe_ct* ct, uint64_t* words);
+int fhe_pt_import(fhe_ctx* cx, const uint64_t* words, int level, double scale, fhe_pt** out);
+int fhe_pt_export(fhe_ctx* cx, const fhe_pt* pt, uint64_t* words);
+/* forward / inverse NTT of n limb-polynomials in host memory; mod_idx[i] names the modulus
+ * (0..L-1: q_i, L..L+K-1: p_{i-L}) of polynomial i */
+int fhe_ntt_host(fhe_ctx* cx, uint64_t* words, int n, const int* mod_idx, int inverse);
+/* key switching of one polynomial (limbs = L - level, eval form) with a raw key
+ * ([digit][2][L+K][N], canonical) -> out0, out1 (same limbs) */
+int fhe_keyswitch_host(fhe_ctx* cx, const uint64_t* d, int level, const uint64_t* key, uint64_t* out0,
+                       uint64_t* out1);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
