@@ -89,6 +89,42 @@ int fhe_ctx_sync(fhe_ctx* cx) {
     });
 }
 long long fhe_ctx_launches(const fhe_ctx* cx) { return cx ? cx->cx.launches : 0; }
+void* fhe_ctx_stream(const fhe_ctx* cx) { return cx ? (void*)cx->cx.stream : nullptr; }
+int fhe_prof_enable(fhe_ctx* cx, int on) {
+    return guard([&] {
+        REQUIRE(cx, "null argument");
+        cx->cx.prof = on != 0;
+    });
+}
+int fhe_prof_collect(fhe_ctx* cx, char* buf, int cap) {
+    return guard([&] {
+        REQUIRE(cx && buf && cap > 2, "null argument");
+        bind(cx);
+        auto& c = cx->cx;
+        CUDA_CHECK(cudaStreamSynchronize(c.stream));
+        std::string js = "{";
+        bool first = true;
+        for (auto& kv : c.prof_acc) {
+            auto& e = kv.second;
+            for (auto& pr : e.pending) {
+                float ms = 0.f;
+                CUDA_CHECK(cudaEventElapsedTime(&ms, pr.first, pr.second));
+                e.ms += ms;
+                cudaEventDestroy(pr.first);
+                cudaEventDestroy(pr.second);
+            }
+            e.pending.clear();
+            if (!first) js += ", ";
+            first = false;
+            js += "\"" + kv.first + "\": [" + std::to_string(e.launches) + ", " + std::to_string(e.ms) + ", " +
+                  std::to_string(e.bytes) + "]";
+        }
+        js += "}";
+        c.prof_acc.clear();
+        REQUIRE((int)js.size() < cap, "buffer too small");
+        std::memcpy(buf, js.c_str(), js.size() + 1);
+    });
+}
 
 int fhe_keygen(fhe_ctx* cx, const uint8_t seed[32]) {
     return guard([&] {
@@ -356,12 +392,11 @@ int fhe_ntt_host(fhe_ctx* cx, uint64_t* words, int n, const int* mod_idx, int in
         for (int i = 0; i < n; i++) REQUIRE(mod_idx[i] >= 0 && mod_idx[i] < c.L + c.K, "modulus index out of range");
         fhe::DevBuf d((size_t)n * c.N, c.stream);
         fhe::upload(c, d.p, words, d.words);
-        // one launch per run of <= 64 limbs sharing a LimbMap
-        for (int s = 0; s < n; s += fhe::kMaxMod) {
-            const int cnt = std::min(n - s, fhe::kMaxMod);
+        // one transform per limb (each limb names its own modulus)
+        for (int s = 0; s < n; s++) {
             fhe::LimbMap mp{};
-            mp.base = d.p + (size_t)s * c.N; mp.poly_stride = 0; mp.nl = cnt;
-            for (int i = 0; i < cnt; i++) mp.mod[i] = (uint8_t)mod_idx[s + i];
+            mp.base = d.p + (size_t)s * c.N; mp.poly_stride = 0; mp.nl = 1;
+            mp.split = 1; mp.off0 = mod_idx[s]; mp.off1 = 0;
             fhe::ntt(c, mp, 1, inverse != 0, c.stream);
         }
         fhe::download(c, words, d.p, d.words);

@@ -277,13 +277,13 @@ const uint64_t* Context::modup_table(int nl) {
 LimbMap Context::qmap(uint64_t* base, int nl, long long poly_stride) const {
     LimbMap mp{};
     mp.base = base; mp.poly_stride = poly_stride; mp.nl = nl; mp.skip_alpha = 0; mp.skip_nq = 0;
-    for (int i = 0; i < nl; i++) mp.mod[i] = (uint8_t)i;
+    mp.split = nl; mp.off0 = 0; mp.off1 = 0;
     return mp;
 }
 LimbMap Context::extmap(uint64_t* base, int nl, long long poly_stride) const {
     LimbMap mp{};
     mp.base = base; mp.poly_stride = poly_stride; mp.nl = nl + K; mp.skip_alpha = 0; mp.skip_nq = nl;
-    for (int e = 0; e < nl + K; e++) mp.mod[e] = (uint8_t)ext_mod(nl, e);
+    mp.split = nl; mp.off0 = 0; mp.off1 = L;
     return mp;
 }
 
@@ -296,15 +296,21 @@ static void moddown(Context& cx, uint64_t* ip, int nl, const uint64_t* add0, con
     cudaStream_t st = cx.stream;
     LimbMap pm{};
     pm.base = ip + (size_t)nl * N; pm.poly_stride = (long long)ne * N; pm.nl = K;
-    for (int k = 0; k < K; k++) pm.mod[k] = (uint8_t)(L + k);
+    pm.split = 0; pm.off0 = 0; pm.off1 = L;
     ntt(cx, pm, 2, true, st);
     DevBuf y((size_t)2 * nl * N, st);
-    k_moddown_bconv<<<g2(cx, 2), 256, 0, st>>>(ip, y.p, cx.d_md, nl, ne, L, K, cx.logN);
+    {
+        ProfScope ps(cx, "moddown_bconv", 8.0 * N * (2 * K + 2 * nl));
+        k_moddown_bconv<<<g2(cx, 2), 256, 0, st>>>(ip, y.p, cx.d_md, nl, ne, L, K, cx.logN);
+    }
     ntt(cx, cx.qmap(y.p, nl, (long long)nl * N), 2, false, st);
-    k_moddown_final<<<g2(cx, nl, 2), 256, 0, st>>>(ip, y.p, add0, add1, out0, out1, cx.d_md, nl, ne, L, K, cx.logN,
-                                                   perm_k);
+    {
+        ProfScope ps(cx, "moddown_final", 8.0 * N * nl * (6 + (add0 ? 1 : 0) + (add1 ? 1 : 0)));
+        k_moddown_final<<<g2(cx, nl, 2), 256, 0, st>>>(ip, y.p, add0, add1, out0, out1, cx.d_md, nl, ne, L, K,
+                                                       cx.logN, perm_k);
+    }
     CUDA_CHECK(cudaGetLastError());
-    cx.launches += 8;
+    cx.launches += 2;
 }
 
 // ModUp of d (nl limbs, eval form): ext [dnum][nl+K][N], eval form
@@ -315,12 +321,16 @@ static DevBuf modup(Context& cx, const uint64_t* d, int nl) {
     CUDA_CHECK(cudaMemcpyAsync(dc.p, d, (size_t)nl * N * 8, cudaMemcpyDeviceToDevice, st));
     ntt(cx, cx.qmap(dc.p, nl, (long long)nl * N), 1, true, st);
     DevBuf ext((size_t)dn * ne * N, st);
-    k_modup_bconv<<<g2(cx, dn), 256, 0, st>>>(dc.p, d, ext.p, cx.modup_table(nl), nl, ne, cx.alpha, cx.L, cx.logN);
+    {
+        ProfScope ps(cx, "modup_bconv", 8.0 * N * (2 * nl + (double)dn * ne));
+        k_modup_bconv<<<g2(cx, dn), 256, 0, st>>>(dc.p, d, ext.p, cx.modup_table(nl), nl, ne, cx.alpha, cx.L,
+                                                  cx.logN);
+    }
     LimbMap em = cx.extmap(ext.p, nl, (long long)ne * N);
     em.skip_alpha = cx.alpha;
     ntt(cx, em, dn, false, st);
     CUDA_CHECK(cudaGetLastError());
-    cx.launches += 5;
+    cx.launches += 1;
     return ext;
 }
 
@@ -329,7 +339,10 @@ static void inner_moddown(Context& cx, const DevBuf& ext, int nl, const SwitchKe
     const int N = cx.N, K = cx.K, ne = nl + K, dn = cx.dnum(nl);
     cudaStream_t st = cx.stream;
     DevBuf ip((size_t)2 * ne * N, st);
-    k_key_inner<<<g2(cx, ne), 256, 0, st>>>(ext.p, key.buf.p, ip.p, nl, ne, dn, cx.L, K, cx.logN);
+    {
+        ProfScope ps(cx, "key_inner", 8.0 * N * ((double)dn * ne * 3 + 2 * ne));
+        k_key_inner<<<g2(cx, ne), 256, 0, st>>>(ext.p, key.buf.p, ip.p, nl, ne, dn, cx.L, K, cx.logN);
+    }
     cx.launches += 1;
     moddown(cx, ip.p, nl, add0, add1, out0, out1, perm_k);
 }
@@ -411,8 +424,11 @@ void ct_mul_relin(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphert
     const double sc = a.scale * b.scale;
     Ciphertext t = ct_alloc(cx, nl);
     DevBuf d2((size_t)nl * cx.N, cx.stream);
-    k_tensor<<<g2(cx, nl), 256, 0, cx.stream>>>(a.buf.p, (long long)a.stride, b.buf.p, (long long)b.stride, t.buf.p,
-                                                (long long)t.stride, d2.p, cx.logN);
+    {
+        ProfScope ps(cx, "tensor", 8.0 * cx.N * nl * 7);
+        k_tensor<<<g2(cx, nl), 256, 0, cx.stream>>>(a.buf.p, (long long)a.stride, b.buf.p, (long long)b.stride,
+                                                    t.buf.p, (long long)t.stride, d2.p, cx.logN);
+    }
     CUDA_CHECK(cudaGetLastError());
     cx.launches++;
     keyswitch(cx, d2.p, nl, *cx.rlk, t.c(0), t.c(1), t.c(0), t.c(1), 1);
@@ -428,14 +444,14 @@ void ct_rescale(Context& cx, Ciphertext& a) {
     CUDA_CHECK(cudaMemcpyAsync(last.p, a.c(0) + (size_t)l * N, N * 8, cudaMemcpyDeviceToDevice, st));
     CUDA_CHECK(cudaMemcpyAsync(last.p + N, a.c(1) + (size_t)l * N, N * 8, cudaMemcpyDeviceToDevice, st));
     LimbMap lm{};
-    lm.base = last.p; lm.poly_stride = N; lm.nl = 1; lm.mod[0] = (uint8_t)l;
+    lm.base = last.p; lm.poly_stride = N; lm.nl = 1; lm.split = 1; lm.off0 = l; lm.off1 = 0;
     ntt(cx, lm, 2, true, st);
     DevBuf y((size_t)2 * l * N, st);
     k_rescale_lift<<<g2(cx, l, 2), 256, 0, st>>>(last.p, y.p, l, l, cx.logN);
     ntt(cx, cx.qmap(y.p, l, (long long)l * N), 2, false, st);
     k_rescale_final<<<g2(cx, l, 2), 256, 0, st>>>(a.buf.p, (long long)a.stride, y.p, cx.d_rs, l, l, cx.L, cx.logN);
     CUDA_CHECK(cudaGetLastError());
-    cx.launches += 6;
+    cx.launches += 2;
     a.scale /= (double)cx.mods[l];
     a.nl = l;
 }
@@ -645,7 +661,7 @@ Plaintext encode(Context& cx, const std::complex<double>* z, int nslots, int nl,
     CUDA_CHECK(cudaGetLastError());
     ntt(cx, mp, 1, false, cx.stream);
     CUDA_CHECK(cudaStreamSynchronize(cx.stream));   // coef is a host temporary
-    cx.launches += 3;
+    cx.launches += 1;
     return pt;
 }
 
@@ -680,13 +696,13 @@ static void small_to_eval(Context& cx, const int64_t* h, int npoly, LimbMap mp) 
     CUDA_CHECK(cudaGetLastError());
     ntt(cx, mp, npoly, false, cx.stream);
     CUDA_CHECK(cudaStreamSynchronize(cx.stream));
-    cx.launches += 3;
+    cx.launches += 1;
 }
 
 static LimbMap fullmap(const Context& cx, uint64_t* base) {
     LimbMap mp{};
     mp.base = base; mp.poly_stride = (long long)(cx.L + cx.K) * cx.N; mp.nl = cx.L + cx.K;
-    for (int m = 0; m < cx.L + cx.K; m++) mp.mod[m] = (uint8_t)m;
+    mp.split = cx.L + cx.K; mp.off0 = 0; mp.off1 = 0;
     return mp;
 }
 

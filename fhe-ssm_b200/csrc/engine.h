@@ -49,7 +49,9 @@ struct LimbMap {
     int nl;                  // limbs per polynomial
     int skip_alpha;          // >0: skip limbs [poly*alpha, min(poly*alpha+alpha, skip_nq)) (ModUp own digit)
     int skip_nq;
-    uint8_t mod[kMaxMod];    // modulus index of limb l
+    // modulus index of limb l: l < split ? l + off0 : l - split + off1
+    int split, off0, off1;
+    __host__ __device__ int mod(int l) const { return l < split ? l + off0 : l - split + off1; }
 };
 
 struct Params {
@@ -122,7 +124,15 @@ struct Context {
     std::map<uint64_t, std::unique_ptr<SwitchKey>> rot_keys;   // by automorphism index
     uint8_t master[32] = {0};
     uint32_t enc_counter = 0;
-    int launches = 0;                // kernel launches issued (for the launch count claim)
+    mutable long long launches = 0;  // kernel launches issued (for the launch count claim)
+    // optional per-kernel CUDA-event timing (bench roofline): name -> pending event pairs
+    struct ProfEntry {
+        std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pending;
+        long long launches = 0;
+        double ms = 0.0, bytes = 0.0;
+    };
+    bool prof = false;
+    mutable std::map<std::string, ProfEntry> prof_acc;
 
     explicit Context(const Params& p);
     ~Context();
@@ -136,6 +146,29 @@ struct Context {
 };
 
 enum EwOp : int { EW_ADD = 0, EW_SUB = 1, EW_MULPT = 2, EW_ADDPT = 3, EW_NEG = 4 };
+
+// Brackets the launches of one kernel (or kernel pair) with CUDA events on the context's
+// stream when profiling is on; `bytes` is the algorithmic DRAM traffic of the bracket.
+struct ProfScope {
+    const Context& cx;
+    cudaEvent_t a = nullptr, b = nullptr;
+    const char* name;
+    double bytes;
+    ProfScope(const Context& c, const char* n, double by) : cx(c), name(n), bytes(by) {
+        if (!cx.prof) return;
+        cudaEventCreate(&a);
+        cudaEventCreate(&b);
+        cudaEventRecord(a, cx.stream);
+    }
+    ~ProfScope() {
+        if (!cx.prof) return;
+        cudaEventRecord(b, cx.stream);
+        auto& e = cx.prof_acc[name];
+        e.pending.emplace_back(a, b);
+        e.launches++;
+        e.bytes += bytes;
+    }
+};
 
 // ---- low-level launches (ntt.cu, kernels.cu) ---------------------------------------------
 void ntt(const Context& cx, const LimbMap& mp, int npoly, bool inv, cudaStream_t st);

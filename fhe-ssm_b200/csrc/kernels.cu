@@ -24,9 +24,10 @@ __device__ __forceinline__ uint32_t auto_src(uint32_t i, uint64_t k, int logN) {
 // ext[j][e] for digit j: own limbs copied from deval, all others base-converted (coefficient
 // form, NTT'd afterwards).  tab: [dnum][alpha][2] (qhat^-1 mod q_i, shoup) then
 // [dnum][ne][alpha][2] (qhat mod t, shoup).
-__global__ void k_modup_bconv(const uint64_t* __restrict__ dcoef, const uint64_t* __restrict__ deval,
-                              uint64_t* __restrict__ ext, const uint64_t* __restrict__ tab, int nl, int ne,
-                              int alpha, int L, int logN) {
+__global__ void __launch_bounds__(256) k_modup_bconv(const uint64_t* __restrict__ dcoef,
+                                                     const uint64_t* __restrict__ deval, uint64_t* __restrict__ ext,
+                                                     const uint64_t* __restrict__ tab, int nl, int ne, int alpha, int L,
+                                                     int logN) {
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int j = blockIdx.y;
@@ -34,6 +35,9 @@ __global__ void k_modup_bconv(const uint64_t* __restrict__ dcoef, const uint64_t
     const int lo = j * alpha, sz = min(alpha, nl - lo);
     const uint64_t* qhinv = tab + (size_t)j * alpha * 2;
     const uint64_t* qh = tab + (size_t)dn * alpha * 2 + (size_t)j * ne * alpha * 2;
+    __shared__ uint64_t sw[kMaxMod * 8 * 2];   // this digit's [ne][alpha][2] constants
+    for (int i = threadIdx.x; i < ne * alpha * 2; i += blockDim.x) sw[i] = qh[i];
+    __syncthreads();
     uint64_t t[8];
 #pragma unroll
     for (int a = 0; a < 8; a++) {
@@ -50,12 +54,12 @@ __global__ void k_modup_bconv(const uint64_t* __restrict__ dcoef, const uint64_t
         }
         const int m = e < nl ? e : L + (e - nl);
         const uint64_t q = c_mod[m].q;
-        const uint64_t* w = qh + (size_t)e * alpha * 2;
+        const uint64_t* w = sw + e * alpha * 2;
         uint64_t s = 0;
 #pragma unroll
         for (int a = 0; a < 8; a++)
-            if (a < sz) s += mul_shoup_lazy(t[a], w[2 * a], w[2 * a + 1], q);   // < 2q each, sum < 16q < 2^64
-        out[(size_t)e * N + x] = reduce64(s, c_mod[m]);
+            if (a < sz) s += mul_shoup_lazy(t[a], w[2 * a], w[2 * a + 1], q);   // < 2q each: s < 16q < 2^64
+        out[(size_t)e * N + x] = reduce_lazy16(s, q);
     }
 }
 
@@ -105,7 +109,7 @@ __global__ void k_moddown_bconv(const uint64_t* __restrict__ buf, uint64_t* __re
 #pragma unroll
         for (int k = 0; k < 8; k++)
             if (k < K) s += mul_shoup_lazy(t[k], w[2 * k], w[2 * k + 1], q);
-        y[((size_t)c * nl + i) * N + x] = reduce64(s, c_mod[i]);
+        y[((size_t)c * nl + i) * N + x] = reduce_lazy16(s, q);
     }
 }
 
@@ -219,7 +223,7 @@ __global__ void k_signed_to_limbs(const int64_t* __restrict__ s, uint64_t* out, 
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int y = blockIdx.y;
     const int poly = y / mp.nl, limb = y % mp.nl;
-    const ModConst mc = c_mod[mp.mod[limb]];
+    const ModConst mc = c_mod[mp.mod(limb)];
     const int64_t v = s[(size_t)poly * N + x];
     const uint64_t r = v >= 0 ? reduce64((uint64_t)v, mc) : mod_neg(reduce64((uint64_t)(-v), mc), mc.q);
     out[(size_t)poly * mp.poly_stride + (size_t)limb * N + x] = r;

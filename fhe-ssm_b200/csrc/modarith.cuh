@@ -47,6 +47,13 @@ __device__ __forceinline__ uint64_t barrett128(uint64_t hi, uint64_t lo, const M
     if (r >= m.q) r -= m.q;
     return r;
 }
+// s < 16q (a sum of up to eight lazy Shoup products) -> [0, q); needs 16q < 2^64
+__device__ __forceinline__ uint64_t reduce_lazy16(uint64_t s, uint64_t q) {
+    if (s >= (q << 3)) s -= (q << 3);
+    if (s >= (q << 2)) s -= (q << 2);
+    if (s >= (q << 1)) s -= (q << 1);
+    return s >= q ? s - q : s;
+}
 // any 64-bit value mod q (valid for q >= 2^32: 64 <= 2k)
 __device__ __forceinline__ uint64_t reduce64(uint64_t v, const ModConst& m) { return barrett128(0, v, m); }
 __device__ __forceinline__ uint64_t mul_barrett(uint64_t a, uint64_t b, const ModConst& m) {

@@ -19,18 +19,30 @@
 
 namespace fhe {
 
+// Harvey lazy butterflies: forward inputs in [0, 4q) -> outputs in [0, 4q); inverse inputs in
+// [0, 2q) -> outputs in [0, 2q).  4q < 2^62 for the 60-bit moduli; the transforms correct to
+// [0, q) at their output.
 template <bool INV>
 __device__ __forceinline__ void bfly(uint64_t& lo, uint64_t& hi, uint64_t w, uint64_t wp, uint64_t q) {
+    const uint64_t q2 = q << 1;
     if (!INV) {
-        const uint64_t x = mul_shoup(hi, w, wp, q);
-        const uint64_t u = lo;
-        lo = mod_add(u, x, q);
-        hi = mod_sub(u, x, q);
+        uint64_t u = lo;
+        if (u >= q2) u -= q2;
+        const uint64_t x = mul_shoup_lazy(hi, w, wp, q);
+        lo = u + x;
+        hi = u - x + q2;
     } else {
-        const uint64_t u = lo, v = hi;
-        lo = mod_add(u, v, q);
-        hi = mul_shoup(mod_sub(u, v, q), w, wp, q);
+        uint64_t u = lo + hi;
+        if (u >= q2) u -= q2;
+        const uint64_t t = lo - hi + q2;
+        hi = mul_shoup_lazy(t, w, wp, q);
+        lo = u;
     }
+}
+__device__ __forceinline__ uint64_t canon4(uint64_t v, uint64_t q) {   // [0, 4q) -> [0, q)
+    const uint64_t q2 = q << 1;
+    if (v >= q2) v -= q2;
+    return v >= q ? v - q : v;
 }
 
 __device__ __forceinline__ bool limb_skipped(const LimbMap& mp, int poly, int limb) {
@@ -41,7 +53,7 @@ __device__ __forceinline__ bool limb_skipped(const LimbMap& mp, int poly, int li
 
 // ---- phase "col": stages with distance >= 256 ----------------------------------------
 template <int LOGN, bool INV>
-__global__ void __launch_bounds__(256) k_ntt_col(LimbMap mp, const uint64_t* __restrict__ tw,
+__global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const uint64_t* __restrict__ tw,
                                                   const uint64_t* __restrict__ twp, const uint64_t* __restrict__ ninv) {
     constexpr int N = 1 << LOGN;
     constexpr int R = N >> 8;            // rows
@@ -51,7 +63,7 @@ __global__ void __launch_bounds__(256) k_ntt_col(LimbMap mp, const uint64_t* __r
     const int y = blockIdx.y;
     const int poly = y / mp.nl, limb = y % mp.nl;
     if (limb_skipped(mp, poly, limb)) return;
-    const int m = mp.mod[limb];
+    const int m = mp.mod(limb);
     uint64_t* a = mp.base + (size_t)poly * mp.poly_stride + (size_t)limb * N;
     const uint64_t q = c_mod[m].q;
     const uint64_t* T = tw + (size_t)m * N;
@@ -141,7 +153,7 @@ __global__ void __launch_bounds__(256) k_ntt_col(LimbMap mp, const uint64_t* __r
 
 // ---- phase "row": the last 8 stages, 256-word blocks ---------------------------------------
 template <int LOGN, bool INV>
-__global__ void __launch_bounds__(256) k_ntt_row(LimbMap mp, const uint64_t* __restrict__ tw,
+__global__ void __launch_bounds__(256, 4) k_ntt_row(LimbMap mp, const uint64_t* __restrict__ tw,
                                                   const uint64_t* __restrict__ twp) {
     constexpr int N = 1 << LOGN;
     constexpr int S1 = LOGN - 8;
@@ -149,7 +161,7 @@ __global__ void __launch_bounds__(256) k_ntt_row(LimbMap mp, const uint64_t* __r
     const int y = blockIdx.y;
     const int poly = y / mp.nl, limb = y % mp.nl;
     if (limb_skipped(mp, poly, limb)) return;
-    const int m = mp.mod[limb];
+    const int m = mp.mod(limb);
     uint64_t* a = mp.base + (size_t)poly * mp.poly_stride + (size_t)limb * N + (size_t)blockIdx.x * 4096;
     const uint64_t q = c_mod[m].q;
     const uint64_t* T = tw + (size_t)m * N;
@@ -190,7 +202,7 @@ __global__ void __launch_bounds__(256) k_ntt_row(LimbMap mp, const uint64_t* __r
         }
         __syncthreads();
 #pragma unroll
-        for (int k = 0; k < 16; k++) sm[b * 256 + 16 * r0 + k] = x[k];
+        for (int k = 0; k < 16; k++) sm[b * 256 + 16 * r0 + k] = canon4(x[k], q);
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 16; k++) a[b * 256 + r0 + 16 * k] = sm[b * 256 + r0 + 16 * k];
@@ -248,6 +260,10 @@ static void launch_ntt(const Context& cx, const LimbMap& mp, int count, bool inv
 void ntt(const Context& cx, const LimbMap& mp, int npoly, bool inv, cudaStream_t st) {
     const int count = npoly * mp.nl;
     if (count == 0) return;
+    int work = count;   // limb-polynomials actually transformed (ModUp skips its own digit)
+    if (mp.skip_alpha)
+        for (int p = 0; p < npoly; p++) work -= std::max(0, std::min(mp.skip_alpha, mp.skip_nq - p * mp.skip_alpha));
+    ProfScope ps(cx, inv ? "ntt_inv" : "ntt_fwd", 16.0 * cx.N * work);
     switch (cx.logN) {
         case 12: launch_ntt<12>(cx, mp, count, inv, st); break;
         case 13: launch_ntt<13>(cx, mp, count, inv, st); break;
@@ -257,6 +273,7 @@ void ntt(const Context& cx, const LimbMap& mp, int npoly, bool inv, cudaStream_t
         default: throw Error("ntt: logN must be in [12, 16]");
     }
     CUDA_CHECK(cudaGetLastError());
+    cx.launches += 2;
 }
 
 }  // namespace fhe

@@ -44,6 +44,9 @@ _SIGS = {
     "fhe_ctx_scale": (C.c_double, [_VP, C.c_int]),
     "fhe_ctx_sync": (C.c_int, [_VP]),
     "fhe_ctx_launches": (C.c_longlong, [_VP]),
+    "fhe_ctx_stream": (_VP, [_VP]),
+    "fhe_prof_enable": (C.c_int, [_VP, C.c_int]),
+    "fhe_prof_collect": (C.c_int, [_VP, C.c_char_p, C.c_int]),
     "fhe_keygen": (C.c_int, [_VP, C.c_char_p]),
     "fhe_keygen_rotations": (C.c_int, [_VP, C.POINTER(C.c_int32), C.c_int, C.c_int]),
     "fhe_key_export": (C.c_int, [_VP, C.c_uint64, _U64P]),
@@ -190,6 +193,20 @@ class CryptoContext:
 
     def rot_index(self, k):
         return lib().fhe_rot_index(self.h, k)
+
+    def stream_ptr(self):
+        """The engine's cudaStream_t (an int), e.g. for torch.cuda.ExternalStream."""
+        return lib().fhe_ctx_stream(self.h)
+
+    def profile(self, on=True):
+        _check(lib().fhe_prof_enable(self.h, 1 if on else 0))
+
+    def profile_collect(self):
+        """{kernel: (launches, total_ms, algorithmic_bytes)} since the last collect."""
+        import json
+        buf = C.create_string_buffer(1 << 16)
+        _check(lib().fhe_prof_collect(self.h, buf, len(buf)))
+        return {k: tuple(v) for k, v in json.loads(buf.value.decode()).items()}
 
     # ---- keys
     def KeyGen(self, seed=1):

@@ -67,6 +67,13 @@ double fhe_ctx_scale(const fhe_ctx* cx, int level);
 int fhe_ctx_sync(fhe_ctx* cx);
 /* kernel launches issued by this context so far */
 long long fhe_ctx_launches(const fhe_ctx* cx);
+/* the context's CUDA stream (cudaStream_t), for callers that time it with CUDA events */
+void* fhe_ctx_stream(const fhe_ctx* cx);
+/* per-kernel CUDA-event timing on the context's stream (off by default).  collect
+ * synchronises, writes {"kernel": [launches, total_ms, algorithmic_bytes], ...} as JSON
+ * into buf (cap bytes) and resets the counters. */
+int fhe_prof_enable(fhe_ctx* cx, int on);
+int fhe_prof_collect(fhe_ctx* cx, char* buf, int cap);
 
 /* ---- keys -------------------------------------------------------------------------------
  * replaces KeyGen + EvalMultKeyGen (gpu_real_model.cu:1293-1298); all randomness from the
