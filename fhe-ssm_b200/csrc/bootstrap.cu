@@ -1,0 +1,354 @@
+// bootstrap.cu -- full-slot CKKS bootstrapping (replaces EvalBootstrap, gpu_real_model.cu
+// :2535-2556, whose refresh rule is :2573-2599).
+//
+// Pipeline (baseline config 3): ModRaise -> CoeffToSlot (3 merged FFT levels) -> split into
+// real / imaginary parts -> EvalMod (degree-59 Chebyshev interpolant of a scaled cosine + 3
+// double-angle steps) -> merge -> SlotToCoeff (3 merged FFT levels).
+//
+//  * ModRaise: the ciphertext is reduced to the first modulus q0 and its centred residues are
+//    lifted to all L limbs, so it decrypts to t = m + q0 I with |I| small (sparse secret).
+//  * CoeffToSlot evaluates (1/n) Stages_inv, the special FFT's inverse without its final
+//    bit reversal (slot order stays bit-reversed; EvalMod is slot-wise so the order is free)
+//    and SlotToCoeff evaluates Stages_fwd, the forward special FFT without its initial bit
+//    reversal.  15 butterfly stages are merged into 3 levels of 5 stages: each level is a
+//    sum of at most 63 rotated diagonals, evaluated by baby-step / giant-step (7 hoisted
+//    babies, 7 giants).  CoeffToSlot keeps the ciphertext at scale q0 (the plaintext scale of
+//    each level is the level's prime), so its plaintexts carry 45 bits of precision.
+//  * EvalMod: with y = t / q0, sin(2 pi y) = cos(2 pi (y - 1/4)) is computed as the 8-fold
+//    angle of cos(2 pi (y - 1/4) / 8), whose Chebyshev interpolant on [-B, B] is degree 59.
+//    sin(2 pi y) ~ 2 pi m / q0; the factor q0 / (2 pi Delta) is folded into SlotToCoeff.
+#include <cmath>
+#include <set>
+
+#include "engine.h"
+
+namespace fhe {
+
+// circuit.cu
+double canon(const Context& cx, int nl);
+void align(Context& cx, Ciphertext& a, int nl_t, double target);
+void split_complex(Context& cx, const Ciphertext& z, Ciphertext& re, Ciphertext& im, bool halve);
+void merge_complex(Context& cx, Ciphertext re, Ciphertext im, Ciphertext& z);
+void cheb_eval(Context& cx, const Ciphertext& x, const std::vector<double>& coeffs, Ciphertext& out);
+std::vector<double> cheb_fit(double (*f)(double, const void*), const void* arg, double a, double b, int n);
+void mul_integer(Context& cx, const Ciphertext& a, long double M, Ciphertext& out);
+void mul_rescale(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out);
+__global__ void k_rescale_lift(const uint64_t*, uint64_t*, int, int, int);
+
+using cvec = std::vector<std::complex<double>>;
+using Diags = std::map<int, cvec>;   // signed rotation offset -> diagonal
+
+static cvec rotv(const cvec& d, int s) {   // rot(d, s)[p] = d[(p + s) mod n]
+    const int n = (int)d.size();
+    cvec r(n);
+    for (int p = 0; p < n; p++) r[p] = d[((p + s) % n + n) % n];
+    return r;
+}
+static int signed_off(int o, int n) {
+    o = ((o % n) + n) % n;
+    return o > n / 2 ? o - n : o;
+}
+
+// one butterfly stage of the special FFT as three diagonals (offsets 0, +lenh, -lenh)
+static Diags stage(int n, int M, int len, bool inverse) {
+    const int lenh = len / 2, lenq = len * 4, gap = M / lenq;
+    std::vector<uint64_t> rg(n);
+    uint64_t g = 1;
+    for (int j = 0; j < n; j++) { rg[j] = g; g = (g * 5) % (uint64_t)M; }
+    cvec d0(n), dp(n), dm(n);
+    for (int i = 0; i < n; i += len)
+        for (int j = 0; j < lenh; j++) {
+            const int p = i + j, p2 = i + j + lenh;
+            if (!inverse) {
+                const uint64_t idx = (rg[j] % (uint64_t)lenq) * (uint64_t)gap;
+                const std::complex<double> w(std::cos(2 * M_PI * idx / M), std::sin(2 * M_PI * idx / M));
+                d0[p] = 1.0; dp[p] = w;          // out[p]  = v[p] + w v[p+lenh]
+                dm[p2] = 1.0; d0[p2] = -w;       // out[p2] = v[p] - w v[p2]
+            } else {
+                const uint64_t idx = ((uint64_t)lenq - (rg[j] % (uint64_t)lenq)) * (uint64_t)gap;
+                const std::complex<double> w(std::cos(2 * M_PI * idx / M), std::sin(2 * M_PI * idx / M));
+                d0[p] = 0.5; dp[p] = 0.5;        // out[p]  = (v[p] + v[p+lenh]) / 2
+                dm[p2] = 0.5 * w; d0[p2] = -0.5 * w;   // out[p2] = (v[p] - v[p2]) w / 2
+            }
+        }
+    // +lenh and -lenh coincide mod n when lenh = n/2: the two diagonals have disjoint
+    // supports, so they are summed into one
+    Diags D;
+    D[0] = d0;
+    for (auto* pr : {&dp, &dm}) {
+        const int o = signed_off(pr == &dp ? lenh : -lenh, n);
+        auto& dst = D[o];
+        if (dst.empty()) dst.assign(n, 0.0);
+        for (int p = 0; p < n; p++) dst[p] += (*pr)[p];
+    }
+    return D;
+}
+
+// (A o B): sum_{a,b} (A_a . rot(B_b, a)) at offset a + b
+static Diags compose(const Diags& A, const Diags& B, int n) {
+    Diags R;
+    for (auto& a : A)
+        for (auto& b : B) {
+            const int o = signed_off(a.first + b.first, n);
+            cvec rb = rotv(b.second, a.first);
+            auto& dst = R[o];
+            if (dst.empty()) dst.assign(n, 0.0);
+            for (int p = 0; p < n; p++) dst[p] += a.second[p] * rb[p];
+        }
+    return R;
+}
+
+struct BootLevel {
+    int base = 1, b1 = 8;
+    int nl_in = 0;
+    double s_in = 0, s_out = 0;
+    std::map<std::pair<int, int>, Plaintext> pts;   // (g, j) -> plaintext of rot(D_k, -g b1 base)
+    std::vector<int> gs;                            // giant indices in use
+};
+
+struct BootCtx {
+    double B = 24.0;
+    int r = 3, deg = 59;
+    std::vector<double> cheb;
+    std::vector<BootLevel> cts, stc;
+    int nl_stc = 0, nl_out = 0;
+    double delta_in = 0, stc_s_in = 0;
+};
+
+static double cos_target(double x, const void* arg) {
+    const double B = *(const double*)arg;
+    return std::cos(2 * M_PI * (B * x - 0.25) / 8.0);
+}
+
+// rotation steps the bootstrap needs (babies j*base, giants g*b1*base)
+std::vector<int> boot_rotations(const Context& cx) {
+    const int n = cx.N / 2;
+    int logn = 0;
+    while ((1 << logn) < n) logn++;
+    std::vector<int> r;
+    const int per = (logn + 2) / 3;   // stages per level (5 at n = 2^15)
+    for (int lv = 0; lv < 3; lv++) {
+        const int lo = lv * per;
+        if (lo >= logn) break;
+        const int base = 1 << lo;
+        for (int j = 1; j < 8; j++) r.push_back(j * base);
+        for (int g = -4; g <= 3; g++) if (g) r.push_back(g * 8 * base);
+    }
+    return r;
+}
+
+// build one merged level (stages with lenh = 2^lo .. 2^hi-1) as BSGS plaintexts
+static BootLevel build_level(Context& cx, int lo, int hi, bool inverse, int nl_in, double s_in, double s_out,
+                             std::complex<double> fold) {
+    const int n = cx.N / 2, M = 2 * cx.N;
+    Diags D;
+    bool first = true;
+    if (inverse) {   // CoeffToSlot applies the largest lenh first
+        for (int e = hi - 1; e >= lo; e--) {
+            Diags S = stage(n, M, 2 << e, true);
+            D = first ? S : compose(S, D, n);
+            first = false;
+        }
+    } else {
+        for (int e = lo; e < hi; e++) {
+            Diags S = stage(n, M, 2 << e, false);
+            D = first ? S : compose(S, D, n);
+            first = false;
+        }
+    }
+    BootLevel L;
+    L.base = 1 << lo;
+    L.b1 = 8;
+    L.nl_in = nl_in;
+    L.s_in = s_in;
+    L.s_out = s_out;
+    const double spt = s_out * (double)cx.mods[nl_in - 1] / s_in;
+    std::set<int> gset;
+    for (auto& kv : D) {
+        const int o = kv.first;
+        if (o % L.base) throw Error("bootstrap: merged offset not a multiple of the level base");
+        const int k = o / L.base;
+        const int g = (int)std::floor((double)k / L.b1), j = k - g * L.b1;
+        cvec d = rotv(kv.second, -g * L.b1 * L.base);
+        for (auto& x : d) x *= fold;
+        L.pts.emplace(std::make_pair(g, j), encode(cx, d.data(), n, nl_in, spt));
+        gset.insert(g);
+    }
+    L.gs.assign(gset.begin(), gset.end());
+    return L;
+}
+
+static void eval_level(Context& cx, const BootLevel& L, const Ciphertext& v, Ciphertext& out) {
+    if (v.nl != L.nl_in) throw Error("bootstrap: level mismatch in linear transform", -4);
+    std::vector<int> steps;
+    for (int j = 1; j < L.b1; j++) steps.push_back(j * L.base);
+    std::vector<Ciphertext> baby(L.b1);
+    baby[0] = ct_copy(cx, v);
+    {
+        std::vector<Ciphertext> rs(steps.size());
+        ct_rotate_hoisted(cx, v, steps.data(), (int)steps.size(), rs.data());
+        for (size_t i = 0; i < rs.size(); i++) baby[i + 1] = std::move(rs[i]);
+    }
+    Ciphertext acc;
+    bool have = false;
+    for (int g : L.gs) {
+        Ciphertext inner;
+        bool hi = false;
+        for (int j = 0; j < L.b1; j++) {
+            auto it = L.pts.find(std::make_pair(g, j));
+            if (it == L.pts.end()) continue;
+            Ciphertext t;
+            ct_mul_pt(cx, baby[j], it->second, t);
+            if (!hi) { inner = std::move(t); hi = true; }
+            else { Ciphertext u; ct_add(cx, inner, t, u); inner = std::move(u); }
+        }
+        if (!hi) continue;
+        if (g != 0) {
+            Ciphertext r;
+            ct_rotate(cx, inner, g * L.b1 * L.base, r);
+            inner = std::move(r);
+        }
+        if (!have) { acc = std::move(inner); have = true; }
+        else { Ciphertext u; ct_add(cx, acc, inner, u); acc = std::move(u); }
+    }
+    ct_rescale(cx, acc);
+    acc.scale = L.s_out;
+    out = std::move(acc);
+}
+
+void bootstrap_setup(Context& cx, double B, int deg) {
+    auto bc = std::make_shared<BootCtx>();
+    bc->B = B;
+    bc->deg = deg;
+    const int n = cx.N / 2;
+    int logn = 0;
+    while ((1 << logn) < n) logn++;
+    const int per = (logn + 2) / 3;
+    const int Lt = cx.L;
+    const double q0 = (double)cx.mods[0];
+    // CoeffToSlot at scale q0 throughout (each level's plaintext scale is its own prime)
+    int nl = Lt;
+    for (int lv = 0; lv < 3; lv++) {
+        const int hi = logn - lv * per, lo = std::max(0, hi - per);
+        bc->cts.push_back(build_level(cx, lo, hi, true, nl, q0, q0, 1.0));
+        nl--;
+    }
+    nl--;   // 1/(2B) as an exact integer product, landing on the canonical scale
+    const int nl_em = nl;
+    bc->cheb = cheb_fit(cos_target, &bc->B, -1.0, 1.0, deg);
+    // EvalMod depth: Chebyshev (ceil(log2(deg+1)) + 1) + r double angles
+    int cd = 0;
+    while ((1 << cd) < deg + 1) cd++;
+    nl = nl_em - (cd + 1) - bc->r;
+    // SlotToCoeff is built on the first bootstrap, when the (data-independent) scale of the
+    // EvalMod output is known; its first level absorbs that scale and q0 / (2 pi Delta_in)
+    bc->delta_in = canon(cx, 1);
+    bc->nl_stc = nl;
+    bc->nl_out = nl - 3;
+    cx.boot = bc;
+}
+
+static void build_stc(Context& cx, BootCtx* bc, double s_in) {
+    const int n = cx.N / 2;
+    int logn = 0;
+    while ((1 << logn) < n) logn++;
+    const int per = (logn + 2) / 3;
+    const double q0 = (double)cx.mods[0];
+    const std::complex<double> fold(q0 / (2 * M_PI * bc->delta_in));
+    bc->stc.clear();
+    int nl = bc->nl_stc;
+    for (int lv = 0; lv < 3; lv++) {
+        const int lo = lv * per, hi = std::min(logn, lo + per);
+        bc->stc.push_back(build_level(cx, lo, hi, false, nl, lv == 0 ? s_in : canon(cx, nl), canon(cx, nl - 1),
+                                      lv == 0 ? fold : 1.0));
+        nl--;
+    }
+    bc->stc_s_in = s_in;
+}
+
+int bootstrap_levels_after(const Context& cx) {
+    auto* bc = (BootCtx*)cx.boot.get();
+    return bc ? bc->nl_out : 0;
+}
+
+// ct (any level, nl >= 2 or canonical at 1 limb) -> refreshed ct at nl_out limbs, canonical scale.
+// upto < 4 stops early (diagnostics): 1 after ModRaise, 2 after CoeffToSlot, 3 after EvalMod.
+void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto);
+void bootstrap(Context& cx, const Ciphertext& in, Ciphertext& out) { bootstrap_upto(cx, in, out, 4); }
+
+void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto) {
+    auto* bc = (BootCtx*)cx.boot.get();
+    if (!bc) throw Error("bootstrap: no bootstrap precomputation (call bootstrap_setup)", -5);
+    const int N = cx.N;
+    Ciphertext a = ct_copy(cx, in);
+    // 1. to one limb at the canonical scale of level L-1
+    if (a.nl > 1) align(cx, a, 1, bc->delta_in);
+    else {
+        const double r = a.scale / bc->delta_in;
+        if (r > 1 + 1e-9 || r < 1 - 1e-9) throw Error("bootstrap: one-limb input must have the canonical scale", -4);
+    }
+    // 2. ModRaise: centred lift of the q0 residues to all L limbs
+    Ciphertext raised = ct_alloc(cx, cx.L);
+    {
+        DevBuf c((size_t)2 * N, cx.stream);
+        CUDA_CHECK(cudaMemcpyAsync(c.p, a.c(0), N * 8, cudaMemcpyDeviceToDevice, cx.stream));
+        CUDA_CHECK(cudaMemcpyAsync(c.p + N, a.c(1), N * 8, cudaMemcpyDeviceToDevice, cx.stream));
+        LimbMap lm{};
+        lm.base = c.p; lm.poly_stride = N; lm.nl = 1; lm.split = 1; lm.off0 = 0; lm.off1 = 0;
+        ntt(cx, lm, 2, true, cx.stream);
+        // k_rescale_lift writes y[c][i] for i < nlm1, layout [2][nlm1][N]: lift into a temp then copy
+        DevBuf y((size_t)2 * cx.L * N, cx.stream);
+        k_rescale_lift<<<dim3(N / 256, cx.L, 2), 256, 0, cx.stream>>>(c.p, y.p, cx.L, 0, cx.logN);
+        CUDA_CHECK(cudaGetLastError());
+        cx.launches++;
+        ntt(cx, cx.qmap(y.p, cx.L, (long long)cx.L * N), 2, false, cx.stream);
+        CUDA_CHECK(cudaMemcpyAsync(raised.buf.p, y.p, (size_t)2 * cx.L * N * 8, cudaMemcpyDeviceToDevice, cx.stream));
+    }
+    raised.scale = (double)cx.mods[0];
+    if (upto == 1) { out = std::move(raised); return; }
+    // 3. CoeffToSlot
+    Ciphertext v = std::move(raised);
+    for (auto& L : bc->cts) {
+        Ciphertext t;
+        eval_level(cx, L, v, t);
+        v = std::move(t);
+    }
+    {
+        Ciphertext t;
+        mul_const_rescale(cx, v, 1.0 / (2.0 * bc->B), t, canon(cx, v.nl - 1));
+        v = std::move(t);
+    }
+    if (upto == 2) { out = std::move(v); return; }
+    // 4. EvalMod on 2 Re and 2 Im (values t/(q0 B) in [-1, 1])
+    Ciphertext re, im;
+    split_complex(cx, v, re, im, false);
+    Ciphertext parts[2] = {std::move(re), std::move(im)};
+    for (auto& x : parts) {
+        Ciphertext c;
+        cheb_eval(cx, x, bc->cheb, c);
+        for (int k = 0; k < bc->r; k++) {   // cos(2a) = 2 cos^2(a) - 1
+            Ciphertext sq;
+            mul_rescale(cx, c, c, sq);
+            mul_integer(cx, sq, 2, sq);
+            Ciphertext t;
+            ct_add_const(cx, sq, -1.0, t);
+            c = std::move(t);
+        }
+        x = std::move(c);
+    }
+    Ciphertext w;
+    merge_complex(cx, std::move(parts[0]), std::move(parts[1]), w);
+    if (upto == 3) { out = std::move(w); return; }
+    // 5. SlotToCoeff
+    if (w.nl > bc->nl_stc) align(cx, w, bc->nl_stc, 0);
+    if (w.nl != bc->nl_stc) throw Error("bootstrap: EvalMod used more levels than planned", -4);
+    if (bc->stc.empty() || std::fabs(w.scale / bc->stc_s_in - 1) > 1e-12) build_stc(cx, bc, w.scale);
+    for (auto& L : bc->stc) {
+        Ciphertext t;
+        eval_level(cx, L, w, t);
+        w = std::move(t);
+    }
+    out = std::move(w);
+}
+
+}  // namespace fhe

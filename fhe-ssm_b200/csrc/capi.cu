@@ -64,6 +64,7 @@ int fhe_ctx_create(const fhe_params* p, fhe_ctx** out) {
         q.logN = p->logN; q.L = p->L; q.K = p->K; q.alpha = p->alpha;
         q.q0bits = p->q0bits; q.qbits = p->qbits; q.pbits = p->pbits;
         q.hw = p->hw; q.sigma = p->sigma; q.device = p->device;
+        q.boot_primes = p->boot_primes; q.boot_bits = p->boot_bits > 0 ? p->boot_bits : 58;
         *out = new fhe_ctx(q);
     });
 }
@@ -339,6 +340,88 @@ int fhe_conjugate(fhe_ctx* cx, const fhe_ct* a, fhe_ct** out) {
         fhe::ct_conjugate(cx->cx, a->c, r);
         *out = wrap(cx, std::move(r));
     });
+}
+
+int fhe_mul_vec_rescale(fhe_ctx* cx, const fhe_ct* a, const double* re, const double* im, int n, fhe_ct** out) {
+    return guard([&] {
+        REQUIRE(cx && a && re && out && n > 0, "null argument");
+        bind(cx);
+        std::vector<std::complex<double>> v(n);
+        for (int i = 0; i < n; i++) v[i] = std::complex<double>(re[i], im ? im[i] : 0.0);
+        fhe::Ciphertext r;
+        fhe::mul_vec_rescale(cx->cx, a->c, v.data(), n, r, 0);
+        *out = wrap(cx, std::move(r));
+    });
+}
+int fhe_align(fhe_ctx* cx, fhe_ct* ct, int level) {
+    return guard([&] {
+        REQUIRE(cx && ct, "null argument");
+        bind(cx);
+        fhe::align(cx->cx, ct->c, nl_of(cx->cx, level), 0);
+    });
+}
+int fhe_mul_rescale(fhe_ctx* cx, const fhe_ct* a, const fhe_ct* b, fhe_ct** out) {
+    return guard([&] {
+        REQUIRE(cx && a && b && out, "null argument");
+        bind(cx);
+        fhe::Ciphertext r;
+        fhe::mul_rescale(cx->cx, a->c, b->c, r);
+        *out = wrap(cx, std::move(r));
+    });
+}
+int fhe_poly_eval(fhe_ctx* cx, const fhe_ct* x, const double* coeffs, int deg, int n, fhe_ct** out) {
+    return guard([&] {
+        REQUIRE(cx && x && coeffs && out && deg >= 1 && n > 0, "bad argument");
+        bind(cx);
+        std::vector<std::vector<std::complex<double>>> c(deg + 1, std::vector<std::complex<double>>(n));
+        for (int i = 0; i <= deg; i++)
+            for (int k = 0; k < n; k++) c[i][k] = coeffs[(size_t)i * n + k];
+        fhe::Ciphertext r;
+        fhe::poly_eval_vec(cx->cx, x->c, c, n, r);
+        *out = wrap(cx, std::move(r));
+    });
+}
+int fhe_cheb_eval(fhe_ctx* cx, const fhe_ct* x, const double* coeffs, int ncoef, fhe_ct** out) {
+    return guard([&] {
+        REQUIRE(cx && x && coeffs && out && ncoef >= 2, "bad argument");
+        bind(cx);
+        std::vector<double> c(coeffs, coeffs + ncoef);
+        fhe::Ciphertext r;
+        fhe::cheb_eval(cx->cx, x->c, c, r);
+        *out = wrap(cx, std::move(r));
+    });
+}
+int fhe_bootstrap_setup(fhe_ctx* cx, double bound, int degree) {
+    return guard([&] {
+        REQUIRE(cx && bound > 0 && degree >= 3, "bad argument");
+        bind(cx);
+        std::vector<int> rots = fhe::boot_rotations(cx->cx);
+        fhe::keygen_rotations(cx->cx, rots.data(), (int)rots.size(), true);
+        fhe::bootstrap_setup(cx->cx, bound, degree);
+    });
+}
+int fhe_bootstrap(fhe_ctx* cx, const fhe_ct* a, fhe_ct** out) {
+    return guard([&] {
+        REQUIRE(cx && a && out, "null argument");
+        bind(cx);
+        fhe::Ciphertext r;
+        fhe::bootstrap(cx->cx, a->c, r);
+        *out = wrap(cx, std::move(r));
+    });
+}
+int fhe_bootstrap_stage(fhe_ctx* cx, const fhe_ct* a, int upto, fhe_ct** out) {
+    return guard([&] {
+        REQUIRE(cx && a && out && upto >= 1 && upto <= 4, "bad argument");
+        bind(cx);
+        fhe::Ciphertext r;
+        fhe::bootstrap_upto(cx->cx, a->c, r, upto);
+        *out = wrap(cx, std::move(r));
+    });
+}
+int fhe_bootstrap_level(const fhe_ctx* cx) {
+    if (!cx) return -1;
+    const int nl = fhe::bootstrap_levels_after(cx->cx);
+    return nl ? cx->cx.L - nl : -1;
 }
 
 int fhe_ct_import(fhe_ctx* cx, const uint64_t* words, int level, double scale, fhe_ct** out) {

@@ -1,0 +1,403 @@
+// circuit.cu -- scale-managed building blocks of the encrypted model circuit.
+//
+// The reference threads a TrackedCt (ciphertext + consumed levels, gpu_real_model.cu
+// :1547-1551) through FLEXIBLEAUTO operations: EvalMult + RescaleInPlace (mulPt :2629-2632),
+// the mult-by-one level alignment (alignTo :2636-2641), EvalAdd with level reconcile
+// (addAligned :2692-2743).  Here every ciphertext carries its limb count and its exact scale
+// (a double), and these helpers keep the scale at the level's FLEXIBLEAUTO factor:
+//   * a plaintext or constant product picks its encoding scale so that the rescaled result
+//     lands exactly on scale_at[nl-1];
+//   * alignment to a lower level drops limbs for free and fixes the scale with one integer
+//     constant product + rescale (one level, whatever the gap);
+//   * constants are multiplied as exact integers; rounding is absorbed into the tracked scale.
+#include <cmath>
+
+#include "engine.h"
+
+namespace fhe {
+
+__global__ void k_mul_const(const uint64_t*, long long, uint64_t*, long long, const uint64_t*, const uint64_t*, int);
+__global__ void k_signed_to_limbs(const int64_t*, uint64_t*, LimbMap, int);
+
+static void require(bool c, const char* msg) {
+    if (!c) throw Error(msg, -4);
+}
+
+double canon(const Context& cx, int nl) { return cx.scale_at[nl]; }
+
+// integer constant M (may be negative, |M| < 2^126) as per-limb residues + shoup, on the device
+static DevBuf const_limbs(Context& cx, long double M, int nl) {
+    std::vector<uint64_t> h(2 * nl);
+    const bool neg = M < 0;
+    long double a = std::floor((neg ? -M : M) + 0.5L);
+    const unsigned __int128 u = (unsigned __int128)a;
+    for (int i = 0; i < nl; i++) {
+        const uint64_t q = cx.mods[i];
+        uint64_t r = (uint64_t)(u % q);
+        if (neg && r) r = q - r;
+        h[2 * i] = r;
+        h[2 * i + 1] = shoup_of(r, q);
+    }
+    DevBuf d(h.size(), cx.stream);
+    CUDA_CHECK(cudaMemcpyAsync(d.p, h.data(), h.size() * 8, cudaMemcpyHostToDevice, cx.stream));
+    CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+    return d;
+}
+
+// out = a * M (integer), no rescale; out may alias a
+void mul_integer(Context& cx, const Ciphertext& a, long double M, Ciphertext& out) {
+    DevBuf w = const_limbs(cx, M, a.nl);
+    Ciphertext t;
+    if (&out == &a) {
+        k_mul_const<<<dim3(cx.N / 256, a.nl, 2), 256, 0, cx.stream>>>(a.buf.p, (long long)a.stride, a.buf.p,
+                                                                       (long long)a.stride, w.p, nullptr, cx.logN);
+        CUDA_CHECK(cudaGetLastError());
+        cx.launches++;
+        return;
+    }
+    t = ct_alloc(cx, a.nl);
+    k_mul_const<<<dim3(cx.N / 256, a.nl, 2), 256, 0, cx.stream>>>(a.buf.p, (long long)a.stride, t.buf.p,
+                                                                   (long long)t.stride, w.p, nullptr, cx.logN);
+    CUDA_CHECK(cudaGetLastError());
+    cx.launches++;
+    t.scale = a.scale;
+    out = std::move(t);
+}
+
+// value * c, rescaled once; the integer factor round(c * S) is chosen so that the output
+// scale is `target` (default: the canonical factor of the output level).
+void mul_const_rescale(Context& cx, const Ciphertext& a, double c, Ciphertext& out, double target) {
+    require(a.nl >= 2, "mul_const_rescale: no level left");
+    const int nl = a.nl;
+    if (target <= 0) target = canon(cx, nl - 1);
+    const long double S = (long double)target * (long double)cx.mods[nl - 1] / (long double)a.scale;
+    const long double M = std::floor((long double)c * S + 0.5L);
+    Ciphertext t;
+    mul_integer(cx, a, M, t);
+    // the value represented is a * M / S_eff with S_eff = M / c: keep the exact scale
+    t.scale = (c != 0.0) ? a.scale * (double)(M / (long double)c) : a.scale * (double)S;
+    ct_rescale(cx, t);
+    out = std::move(t);
+}
+
+// bring a to nl_t limbs at scale `target` (default canonical).  nl_t < a.nl: one level used.
+void align(Context& cx, Ciphertext& a, int nl_t, double target) {
+    if (target <= 0) target = canon(cx, nl_t);
+    require(nl_t >= 1 && nl_t <= a.nl, "align: bad target level");
+    if (nl_t == a.nl) {
+        const double r = a.scale / target;
+        require(r > 1 - 1e-9 && r < 1 + 1e-9, "align: same level but different scale");
+        return;
+    }
+    ct_level_drop(cx, a, nl_t + 1);
+    Ciphertext t;
+    mul_const_rescale(cx, a, 1.0, t, target);
+    a = std::move(t);
+}
+
+// a and b to a common level (the lower one) with equal scales.  Equal-level operands whose
+// scales differ by an integer factor are fixed by an exact integer product.
+void match(Context& cx, Ciphertext& a, Ciphertext& b) {
+    if (a.nl > b.nl) {
+        align(cx, a, b.nl, b.scale);
+        return;
+    }
+    if (b.nl > a.nl) {
+        align(cx, b, a.nl, a.scale);
+        return;
+    }
+    const double r = a.scale / b.scale;
+    if (r > 1 - 1e-9 && r < 1 + 1e-9) return;
+    Ciphertext* lo = r > 1 ? &b : &a;
+    const double f = r > 1 ? r : 1.0 / r;
+    const double fi = std::round(f);
+    require(std::fabs(f - fi) < 1e-9 * f, "match: equal levels with a non-integer scale ratio");
+    mul_integer(cx, *lo, fi, *lo);
+    lo->scale *= fi;
+}
+
+void add_any(Context& cx, const Ciphertext& a0, const Ciphertext& b0, Ciphertext& out) {
+    Ciphertext a = ct_copy(cx, a0), b = ct_copy(cx, b0);
+    match(cx, a, b);
+    ct_add(cx, a, b, out);
+}
+void sub_any(Context& cx, const Ciphertext& a0, const Ciphertext& b0, Ciphertext& out) {
+    Ciphertext a = ct_copy(cx, a0), b = ct_copy(cx, b0);
+    match(cx, a, b);
+    ct_sub(cx, a, b, out);
+}
+
+// ct x ct at the common level, relinearised and rescaled
+void mul_rescale(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out) {
+    if (a.nl == b.nl) {
+        ct_mul_relin(cx, a, b, out);
+    } else {
+        Ciphertext x = ct_copy(cx, a.nl > b.nl ? a : b);
+        const Ciphertext& y = a.nl > b.nl ? b : a;
+        align(cx, x, y.nl, 0);
+        ct_mul_relin(cx, x, y, out);
+    }
+    ct_rescale(cx, out);
+}
+
+// per-slot product with a (complex) vector of n slots (n | N/2, repeated), then rescale; the
+// plaintext scale makes the output scale `target` (default canonical)
+void mul_vec_rescale(Context& cx, const Ciphertext& a, const std::complex<double>* v, int n, Ciphertext& out,
+                     double target) {
+    require(a.nl >= 2, "mul_vec_rescale: no level left");
+    if (target <= 0) target = canon(cx, a.nl - 1);
+    const double s = target * (double)cx.mods[a.nl - 1] / a.scale;
+    Plaintext pt = encode(cx, v, n, a.nl, s);
+    Ciphertext t;
+    ct_mul_pt(cx, a, pt, t);
+    ct_rescale(cx, t);
+    t.scale = target;   // exact by construction (a.scale * s / q)
+    out = std::move(t);
+}
+
+// + vector (n slots, repeated) at the ciphertext's scale
+void add_vec(Context& cx, const Ciphertext& a, const std::complex<double>* v, int n, Ciphertext& out) {
+    Plaintext pt = encode(cx, v, n, a.nl, a.scale);
+    ct_add_pt(cx, a, pt, out);
+}
+
+// multiply by i in every slot: the monomial X^{N/2} (exact, no level, no scale change)
+void mul_i(Context& cx, const Ciphertext& a, Ciphertext& out) {
+    if (!cx.pt_i) {
+        // coefficient form X^{N/2} -> NTT over all Q limbs
+        std::vector<int64_t> coef(cx.N, 0);
+        coef[cx.N / 2] = 1;
+        auto pt = std::make_unique<Plaintext>();
+        pt->buf = DevBuf((size_t)cx.L * cx.N, cx.stream);
+        pt->nl = cx.L;
+        pt->scale = 1.0;
+        DevBuf dc((size_t)cx.N, cx.stream);
+        CUDA_CHECK(cudaMemcpyAsync(dc.p, coef.data(), cx.N * 8, cudaMemcpyHostToDevice, cx.stream));
+        LimbMap mp = cx.qmap(pt->buf.p, cx.L, (long long)cx.L * cx.N);
+        k_signed_to_limbs<<<dim3(cx.N / 256, cx.L), 256, 0, cx.stream>>>((const int64_t*)dc.p, pt->buf.p, mp, cx.logN);
+        CUDA_CHECK(cudaGetLastError());
+        ntt(cx, mp, 1, false, cx.stream);
+        CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+        cx.pt_i = std::move(pt);
+    }
+    const double sc = a.scale;
+    Ciphertext t;
+    ct_mul_pt(cx, a, *cx.pt_i, t);
+    t.scale = sc;
+    out = std::move(t);
+}
+
+// real and imaginary parts of every slot: re = (z + conj z), im = -i (z - conj z).  With
+// halve (default) both carry twice the input scale, so they represent Re z and Im z exactly;
+// without it they keep the input scale and represent 2 Re z and 2 Im z.
+void split_complex(Context& cx, const Ciphertext& z, Ciphertext& re, Ciphertext& im, bool halve) {
+    Ciphertext c;
+    ct_conjugate(cx, z, c);
+    Ciphertext s, d;
+    ct_add(cx, z, c, s);
+    ct_sub(cx, z, c, d);
+    Ciphertext di;
+    mul_i(cx, d, di);
+    ct_mul_int(cx, di, -1, im);   // -i (z - conj z) = 2 Im(z)
+    im.scale = (halve ? 2 : 1) * z.scale;
+    re = std::move(s);
+    re.scale = (halve ? 2 : 1) * z.scale;
+}
+
+// z = re + i im  (re, im real-valued ciphertexts)
+void merge_complex(Context& cx, Ciphertext re, Ciphertext im, Ciphertext& z) {
+    match(cx, re, im);
+    Ciphertext ii;
+    mul_i(cx, im, ii);
+    ct_add(cx, re, ii, z);
+}
+
+// sum over a power-of-two window: out[i] = sum_{k < count} a[i + k*step] (log-doubling)
+void rotate_sum(Context& cx, const Ciphertext& a, int step, int count, Ciphertext& out) {
+    Ciphertext s = ct_copy(cx, a);
+    for (int k = 1; k < count; k <<= 1) {
+        Ciphertext r, t;
+        ct_rotate(cx, s, k * step, r);
+        ct_add(cx, s, r, t);
+        s = std::move(t);
+    }
+    out = std::move(s);
+}
+
+// ---------------------------------------------------------------- Chebyshev evaluation ----
+// p(x) = sum_i c_i T_i(x) on a ciphertext x with |x| <= 1, by the recursive baby-step /
+// giant-step split p = q * T_{2^m} + r (Chebyshev division, T_i T_M = (T_{i+M} + T_{|i-M|})/2).
+// Depth ceil(log2(deg+1)) + 1.  The babies T_1..T_{bs-1} are aligned to one level first.
+struct ChebEval {
+    Context& cx;
+    int bs;
+    std::vector<Ciphertext> T;         // T[i], i < bs (T[0] unused), aligned to one level
+    std::map<int, Ciphertext> giant;   // T_{2^m}, 2^m >= bs
+
+    ChebEval(Context& c, const Ciphertext& x, int degree) : cx(c) {
+        bs = 1;
+        while (bs * bs < degree + 1) bs <<= 1;   // babies up to ~sqrt(deg)
+        if (bs < 2) bs = 2;
+        T.resize(bs);
+        T[1] = ct_copy(cx, x);
+        for (int i = 2; i < bs; i++) {
+            // T_i = 2 T_a T_b - T_{a-b}, a = ceil(i/2), b = floor(i/2)
+            const int a = (i + 1) / 2, b = i / 2;
+            Ciphertext p;
+            mul_rescale(cx, T[a], T[b], p);
+            mul_integer(cx, p, 2, p);
+            if (a == b) {
+                Ciphertext one;
+                ct_add_const(cx, p, -1.0, one);
+                T[i] = std::move(one);
+            } else {
+                Ciphertext d;
+                sub_any(cx, p, T[a - b], d);
+                T[i] = std::move(d);
+            }
+        }
+        // giants T_{bs}, T_{2bs}, ...
+        int M = bs;
+        Ciphertext g;
+        {
+            const int a = bs / 2;
+            Ciphertext p;
+            mul_rescale(cx, T[a], T[a], p);
+            mul_integer(cx, p, 2, p);
+            ct_add_const(cx, p, -1.0, g);
+        }
+        giant[M] = ct_copy(cx, g);
+        while (2 * M <= degree) {
+            Ciphertext p;
+            mul_rescale(cx, giant[M], giant[M], p);
+            mul_integer(cx, p, 2, p);
+            Ciphertext n2;
+            ct_add_const(cx, p, -1.0, n2);
+            M *= 2;
+            giant[M] = std::move(n2);
+        }
+        // align babies to the lowest baby level with canonical scale
+        int lo = T[1].nl;
+        for (int i = 1; i < bs; i++) lo = std::min(lo, T[i].nl);
+        for (int i = 1; i < bs; i++) align(cx, T[i], lo, 0);
+    }
+
+    // leaf: sum_{i < bs} c_i T_i  (one level: integer products + one rescale)
+    Ciphertext leaf(const std::vector<double>& c) {
+        const int nl = T[1].nl;
+        const double target = canon(cx, nl - 1);
+        const double S = target * (double)cx.mods[nl - 1] / T[1].scale;   // all babies share T[1]'s scale
+        Ciphertext acc;
+        bool have = false;
+        for (int i = 1; i < (int)c.size() && i < bs; i++) {
+            if (c[i] == 0.0) continue;
+            Ciphertext t;
+            mul_integer(cx, T[i], std::floor((long double)c[i] * S + 0.5L), t);
+            if (!have) { acc = std::move(t); have = true; }
+            else { Ciphertext u; ct_add(cx, acc, t, u); acc = std::move(u); }
+        }
+        if (!have) {   // constant-only leaf: 0 * T_1 keeps a valid ciphertext
+            mul_integer(cx, T[1], 0, acc);
+        }
+        acc.scale = T[1].scale * S;
+        ct_rescale(cx, acc);
+        acc.scale = target;
+        if (!c.empty() && c[0] != 0.0) {
+            Ciphertext u;
+            ct_add_const(cx, acc, c[0], u);
+            acc = std::move(u);
+        }
+        return acc;
+    }
+
+    Ciphertext eval(std::vector<double> c) {
+        int deg = (int)c.size() - 1;
+        while (deg > 0 && c[deg] == 0.0) deg--;
+        c.resize(deg + 1);
+        if (deg < bs) return leaf(c);
+        int M = bs;
+        while (2 * M <= deg) M *= 2;
+        // p = q T_M + r
+        std::vector<double> q(deg - M + 1), r(c.begin(), c.begin() + M);
+        q[0] = c[M];
+        for (int i = M + 1; i <= deg; i++) {
+            q[i - M] = 2 * c[i];
+            r[2 * M - i] -= c[i];
+        }
+        Ciphertext qv = eval(q), rv = eval(r);
+        Ciphertext prod;
+        mul_rescale(cx, qv, giant[M], prod);
+        Ciphertext out;
+        add_any(cx, prod, rv, out);
+        return out;
+    }
+};
+
+void cheb_eval(Context& cx, const Ciphertext& x, const std::vector<double>& coeffs, Ciphertext& out) {
+    if (x.scale / canon(cx, x.nl) > 1 + 1e-9 || x.scale / canon(cx, x.nl) < 1 - 1e-9) {
+        Ciphertext y = ct_copy(cx, x);
+        align(cx, y, y.nl - 1, 0);
+        ChebEval ev(cx, y, (int)coeffs.size() - 1);
+        out = ev.eval(coeffs);
+        return;
+    }
+    ChebEval ev(cx, x, (int)coeffs.size() - 1);
+    out = ev.eval(coeffs);
+}
+
+// sum_i c_i (.) x^i with per-slot coefficient vectors c_i (n slots each, repeated), power
+// basis, depth ceil(log2 deg) + 1: the powers are aligned to one level, multiplied by their
+// coefficient plaintexts, summed, and c_0 is added.  (polyGate3 and the channel-mix
+// polynomials of gpu_real_model.cu:4609-4649, :5130-5163, evaluated without the
+// reference's per-term alignTo chain.)
+void poly_eval_vec(Context& cx, const Ciphertext& x, const std::vector<std::vector<std::complex<double>>>& c, int n,
+                   Ciphertext& out) {
+    const int deg = (int)c.size() - 1;
+    require(deg >= 1, "poly_eval_vec: degree must be >= 1");
+    std::vector<Ciphertext> pw(deg + 1);
+    pw[1] = ct_copy(cx, x);
+    if (pw[1].scale / canon(cx, x.nl) > 1 + 1e-9 || pw[1].scale / canon(cx, x.nl) < 1 - 1e-9)
+        align(cx, pw[1], x.nl - 1, 0);
+    for (int i = 2; i <= deg; i++) {
+        const int a = (i + 1) / 2, b = i / 2;   // x^i = x^a x^b
+        mul_rescale(cx, pw[a], pw[b], pw[i]);
+    }
+    int lo = pw[1].nl;
+    for (int i = 1; i <= deg; i++) lo = std::min(lo, pw[i].nl);
+    for (int i = 1; i <= deg; i++) align(cx, pw[i], lo, 0);
+    Ciphertext acc;
+    bool have = false;
+    for (int i = 1; i <= deg; i++) {
+        bool zero = true;
+        for (auto& v : c[i]) if (v != 0.0) { zero = false; break; }
+        if (zero) continue;
+        Ciphertext t;
+        mul_vec_rescale(cx, pw[i], c[i].data(), n, t, 0);
+        if (!have) { acc = std::move(t); have = true; }
+        else { Ciphertext u; ct_add(cx, acc, t, u); acc = std::move(u); }
+    }
+    if (!have) {
+        std::vector<std::complex<double>> z(n, 0.0);
+        mul_vec_rescale(cx, pw[1], z.data(), n, acc, 0);
+    }
+    Ciphertext r;
+    add_vec(cx, acc, c[0].data(), n, r);
+    out = std::move(r);
+}
+
+// Chebyshev interpolant of f on [a, b] of degree n (Chebyshev nodes of the first kind)
+std::vector<double> cheb_fit(double (*f)(double, const void*), const void* arg, double a, double b, int n) {
+    std::vector<double> c(n + 1, 0.0), fx(n + 1);
+    for (int k = 0; k <= n; k++) {
+        const double t = std::cos(M_PI * (k + 0.5) / (n + 1));
+        fx[k] = f(0.5 * (b - a) * t + 0.5 * (a + b), arg);
+    }
+    for (int j = 0; j <= n; j++) {
+        double s = 0;
+        for (int k = 0; k <= n; k++) s += fx[k] * std::cos(M_PI * j * (k + 0.5) / (n + 1));
+        c[j] = (j == 0 ? 1.0 : 2.0) * s / (n + 1);
+    }
+    return c;
+}
+
+}  // namespace fhe

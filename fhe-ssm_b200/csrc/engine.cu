@@ -80,10 +80,13 @@ static bool is_prime(uint64_t n) {
     return true;
 }
 
-// OpenFHE-style selection (ParameterGenerationCKKSRNS): q_{L-1} = first prime = 1 mod 2N above
-// 2^qbits, q_{L-2..1} alternating below/above it, q_0 the largest below 2^q0bits, special
-// primes descending below 2^pbits skipping the Q chain.
-static void gen_chain(int logN, int L, int q0bits, int qbits, int K, int pbits, std::vector<uint64_t>& mods) {
+// OpenFHE-style selection (ParameterGenerationCKKSRNS): the top scaling prime = first prime
+// = 1 mod 2N above 2^qbits, the ones below it alternating below/above it, q_0 the largest
+// below 2^q0bits, special primes descending below 2^pbits skipping the Q chain.  With
+// Bt > 0 the top Bt limbs (the levels a bootstrap consumes) form a second region of
+// bbits-bit primes chosen the same way; q_1..q_{L-1-Bt} are the qbits-bit user primes.
+static void gen_chain(int logN, int L, int q0bits, int qbits, int K, int pbits, int Bt, int bbits,
+                      std::vector<uint64_t>& mods) {
     const uint64_t M = 2ull << logN;
     auto first = [&](int bits) {
         uint64_t x = 1ull << bits, q = x - (x % M) + 1;
@@ -94,15 +97,20 @@ static void gen_chain(int logN, int L, int q0bits, int qbits, int K, int pbits, 
     auto prev = [&](uint64_t q) { do { q -= M; } while (!is_prime(q)); return q; };
     auto next = [&](uint64_t q) { do { q += M; } while (!is_prime(q)); return q; };
     std::vector<uint64_t> q(L), p(K);
-    if (L > 1) {
-        uint64_t qs = first(qbits), qp = qs, qn = qs;
-        q[L - 1] = qs;
+    auto region = [&](int top, int bottom, int bits) {   // fills q[bottom..top]
+        if (top < bottom) return;
+        uint64_t qs = first(bits), qp = qs, qn = qs;
+        q[top] = qs;
         int cnt = 0;
-        for (int i = L - 2; i >= 1; i--) {
+        for (int i = top - 1; i >= bottom; i--) {
             if (cnt % 2 == 0) { qp = prev(qp); q[i] = qp; }
             else { qn = next(qn); q[i] = qn; }
             cnt++;
         }
+    };
+    if (L > 1) {
+        region(L - 1 - Bt, 1, qbits);
+        region(L - 1, L - Bt, bbits);
     }
     auto in = [](uint64_t v, const std::vector<uint64_t>& a, int from, int to) {
         for (int i = from; i < to; i++) if (a[i] == v) return true;
@@ -154,13 +162,15 @@ Context::Context(const Params& p) : prm(p) {
     if (p.logN < 12 || p.logN > 16) throw Error("logN must be in [12, 16]");
     if (p.L < 1 || p.K < 1 || p.L + p.K > kMaxMod || p.alpha < 1 || p.alpha > 8 || p.K > 8)
         throw Error("bad chain shape (need 1 <= L, 1 <= K <= 8, L + K <= 64, 1 <= alpha <= 8)");
-    if (p.q0bits > 60 || p.qbits > 60 || p.pbits > 60 || p.qbits < 33)
+    if (p.q0bits > 60 || p.qbits > 60 || p.pbits > 60 || p.qbits < 33 || p.boot_bits > 60 ||
+        (p.boot_primes > 0 && p.boot_bits < 33))
         throw Error("moduli must be 33..60 bits");
+    if (p.boot_primes < 0 || p.boot_primes > p.L - 1) throw Error("boot_primes must be in [0, L-1]");
     logN = p.logN; N = 1 << logN; L = p.L; K = p.K; alpha = p.alpha; device = p.device;
     dnum_top = dnum(L);
     CUDA_CHECK(cudaSetDevice(device));
     CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
-    gen_chain(logN, L, p.q0bits, p.qbits, K, p.pbits, mods);
+    gen_chain(logN, L, p.q0bits, p.qbits, K, p.pbits, p.boot_primes, p.boot_bits, mods);
     const int nm = L + K;
     mc.resize(nm);
     psi.resize(nm);
@@ -186,10 +196,16 @@ Context::Context(const Params& p) : prm(p) {
     CUDA_CHECK(cudaMemcpyToSymbol(c_mod, mc.data(), sizeof(ModConst) * nm));
     d_tw = dev_upload(tw); d_twp = dev_upload(twp); d_itw = dev_upload(itw); d_itwp = dev_upload(itwp);
     d_ninv = dev_upload(ninv);
-    // FLEXIBLEAUTO scaling factors: scale_at[L] = q_{L-1}; scale_at[nl] = scale_at[nl+1]^2 / q_nl
+    // FLEXIBLEAUTO scaling factors: scale_at[top] = q_{top-1}; scale_at[nl] = scale_at[nl+1]^2 / q_nl,
+    // anchored separately at the top of each prime region (user region, bootstrap region)
     scale_at.assign(L + 1, 0.0);
-    scale_at[L] = (double)mods[L - 1];
-    for (int nl = L - 1; nl >= 1; nl--) scale_at[nl] = scale_at[nl + 1] * scale_at[nl + 1] / (double)mods[nl];
+    auto fill = [&](int top, int bottom) {
+        scale_at[top] = (double)mods[top - 1];
+        for (int nl = top - 1; nl >= bottom; nl--) scale_at[nl] = scale_at[nl + 1] * scale_at[nl + 1] / (double)mods[nl];
+    };
+    const int utop = L - p.boot_primes;   // limb count at the top of the user region
+    if (p.boot_primes == 0) fill(L, 1);
+    else { fill(L, utop + 1); fill(utop, 1); }
     // ModDown constants
     {
         std::vector<uint64_t> md(2 * K + (size_t)L * K * 2 + (size_t)L * 2);
@@ -232,6 +248,8 @@ Context::Context(const Params& p) : prm(p) {
 Context::~Context() {
     cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
+    boot.reset();
+    pt_i.reset();
     rlk.reset();
     rot_keys.clear();
     sk = DevBuf();

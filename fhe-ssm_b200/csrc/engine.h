@@ -63,6 +63,8 @@ struct Params {
     int hw = 192;      // secret Hamming weight (0: uniform ternary)
     double sigma = 3.19;
     int device = 0;
+    int boot_primes = 0;   // top limbs drawn as boot_bits-bit primes (the levels a bootstrap consumes)
+    int boot_bits = 58;
 };
 
 struct Context;
@@ -133,6 +135,8 @@ struct Context {
     };
     bool prof = false;
     mutable std::map<std::string, ProfEntry> prof_acc;
+    std::unique_ptr<Plaintext> pt_i;         // NTT of X^{N/2}: multiplication by i
+    std::shared_ptr<void> boot;              // bootstrapping precomputation (bootstrap.cu)
 
     explicit Context(const Params& p);
     ~Context();
@@ -205,6 +209,33 @@ void keygen_rotations(Context& cx, const int* rs, int n, bool conj);
 uint64_t rot_index(const Context& cx, int r);
 Ciphertext encrypt(Context& cx, const Plaintext& pt);
 Plaintext decrypt(Context& cx, const Ciphertext& ct);
+
+// circuit layer (circuit.cu)
+double canon(const Context& cx, int nl);
+void mul_integer(Context& cx, const Ciphertext& a, long double M, Ciphertext& out);
+void mul_const_rescale(Context& cx, const Ciphertext& a, double c, Ciphertext& out, double target = 0);
+void align(Context& cx, Ciphertext& a, int nl_t, double target = 0);
+void match(Context& cx, Ciphertext& a, Ciphertext& b);
+void add_any(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out);
+void sub_any(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out);
+void mul_rescale(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out);
+void mul_vec_rescale(Context& cx, const Ciphertext& a, const std::complex<double>* v, int n, Ciphertext& out,
+                     double target = 0);
+void add_vec(Context& cx, const Ciphertext& a, const std::complex<double>* v, int n, Ciphertext& out);
+void mul_i(Context& cx, const Ciphertext& a, Ciphertext& out);
+void split_complex(Context& cx, const Ciphertext& z, Ciphertext& re, Ciphertext& im, bool halve = true);
+void merge_complex(Context& cx, Ciphertext re, Ciphertext im, Ciphertext& z);
+void rotate_sum(Context& cx, const Ciphertext& a, int step, int count, Ciphertext& out);
+void cheb_eval(Context& cx, const Ciphertext& x, const std::vector<double>& coeffs, Ciphertext& out);
+std::vector<double> cheb_fit(double (*f)(double, const void*), const void* arg, double a, double b, int n);
+void poly_eval_vec(Context& cx, const Ciphertext& x, const std::vector<std::vector<std::complex<double>>>& c, int n,
+                   Ciphertext& out);
+// bootstrapping (bootstrap.cu)
+std::vector<int> boot_rotations(const Context& cx);
+void bootstrap_setup(Context& cx, double B, int deg);
+void bootstrap(Context& cx, const Ciphertext& in, Ciphertext& out);
+void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto);
+int bootstrap_levels_after(const Context& cx);
 
 // raw access (parity tests)
 void upload(Context& cx, uint64_t* dst, const uint64_t* src, size_t words);

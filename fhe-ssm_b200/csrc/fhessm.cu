@@ -3,4 +3,6 @@
 #include "kernels.cu"
 #include "ntt.cu"
 #include "engine.cu"
+#include "circuit.cu"
+#include "bootstrap.cu"
 #include "capi.cu"

@@ -33,7 +33,7 @@ class FheError(RuntimeError):
 class Params(C.Structure):
     _fields_ = [("logN", C.c_int), ("L", C.c_int), ("K", C.c_int), ("alpha", C.c_int),
                 ("q0bits", C.c_int), ("qbits", C.c_int), ("pbits", C.c_int), ("hw", C.c_int),
-                ("sigma", C.c_double), ("device", C.c_int)]
+                ("sigma", C.c_double), ("device", C.c_int), ("boot_primes", C.c_int), ("boot_bits", C.c_int)]
 
 
 _SIGS = {
@@ -76,6 +76,14 @@ _SIGS = {
     "fhe_rotate": (C.c_int, [_VP, _VP, C.c_int32, C.POINTER(_VP)]),
     "fhe_rotate_hoisted": (C.c_int, [_VP, _VP, C.POINTER(C.c_int32), C.c_int, C.POINTER(_VP)]),
     "fhe_conjugate": (C.c_int, [_VP, _VP, C.POINTER(_VP)]),
+    "fhe_mul_vec_rescale": (C.c_int, [_VP, _VP, _DP, _DP, C.c_int, C.POINTER(_VP)]),
+    "fhe_align": (C.c_int, [_VP, _VP, C.c_int]),
+    "fhe_mul_rescale": (C.c_int, [_VP, _VP, _VP, C.POINTER(_VP)]),
+    "fhe_poly_eval": (C.c_int, [_VP, _VP, _DP, C.c_int, C.c_int, C.POINTER(_VP)]),
+    "fhe_cheb_eval": (C.c_int, [_VP, _VP, _DP, C.c_int, C.POINTER(_VP)]),
+    "fhe_bootstrap_setup": (C.c_int, [_VP, C.c_double, C.c_int]),
+    "fhe_bootstrap": (C.c_int, [_VP, _VP, C.POINTER(_VP)]),
+    "fhe_bootstrap_level": (C.c_int, [_VP]),
     "fhe_ct_import": (C.c_int, [_VP, _U64P, C.c_int, C.c_double, C.POINTER(_VP)]),
     "fhe_ct_export": (C.c_int, [_VP, _VP, _U64P]),
     "fhe_pt_import": (C.c_int, [_VP, _U64P, C.c_int, C.c_double, C.POINTER(_VP)]),
@@ -161,8 +169,9 @@ def seed32(seed) -> bytes:
 class CryptoContext:
     """One engine context (one GPU).  Names follow the OpenFHE calls of the reference."""
 
-    def __init__(self, logN=16, L=20, K=4, alpha=4, q0bits=60, qbits=45, pbits=60, hw=192, sigma=3.19, device=0):
-        self.p = Params(logN, L, K, alpha, q0bits, qbits, pbits, hw, sigma, device)
+    def __init__(self, logN=16, L=20, K=4, alpha=4, q0bits=60, qbits=45, pbits=60, hw=192, sigma=3.19, device=0,
+                 boot_primes=0, boot_bits=58):
+        self.p = Params(logN, L, K, alpha, q0bits, qbits, pbits, hw, sigma, device, boot_primes, boot_bits)
         h = _VP()
         _check(lib().fhe_ctx_create(C.byref(self.p), C.byref(h)))
         self.h = h
@@ -323,6 +332,50 @@ class CryptoContext:
         _check(lib().fhe_ct_copy(self.h, ct.h, C.byref(h)))
         return Ciphertext(self, h)
 
+    # ---- circuit level
+    def mul_vec_rescale(self, ct, values):
+        """mulPt: ct (.) values (per slot, repeated) then RescaleInPlace, canonical scale."""
+        z = np.asarray(values, dtype=np.complex128).ravel()
+        re, im = np.ascontiguousarray(z.real), np.ascontiguousarray(z.imag)
+        h = _VP()
+        _check(lib().fhe_mul_vec_rescale(self.h, ct.h, re.ctypes.data_as(_DP), im.ctypes.data_as(_DP), len(z),
+                                         C.byref(h)))
+        return Ciphertext(self, h)
+
+    def align(self, ct, level):
+        _check(lib().fhe_align(self.h, ct.h, level))
+
+    def mul_rescale(self, a, b):
+        h = _VP()
+        _check(lib().fhe_mul_rescale(self.h, a.h, b.h, C.byref(h)))
+        return Ciphertext(self, h)
+
+    def EvalPolyVec(self, ct, coeffs):
+        """sum_i coeffs[i] (.) x^i with per-slot real coefficient vectors (power basis)."""
+        c = np.ascontiguousarray(np.asarray(coeffs, dtype=np.float64))
+        if c.ndim == 1:
+            c = c[:, None]
+        h = _VP()
+        _check(lib().fhe_poly_eval(self.h, ct.h, c.ctypes.data_as(_DP), c.shape[0] - 1, c.shape[1], C.byref(h)))
+        return Ciphertext(self, h)
+
+    def EvalChebyshevSeries(self, ct, coeffs):
+        c = np.ascontiguousarray(np.asarray(coeffs, dtype=np.float64))
+        h = _VP()
+        _check(lib().fhe_cheb_eval(self.h, ct.h, c.ctypes.data_as(_DP), len(c), C.byref(h)))
+        return Ciphertext(self, h)
+
+    def EvalBootstrapSetup(self, bound=24.0, degree=59):
+        _check(lib().fhe_bootstrap_setup(self.h, bound, degree))
+
+    def EvalBootstrap(self, ct):
+        h = _VP()
+        _check(lib().fhe_bootstrap(self.h, ct.h, C.byref(h)))
+        return Ciphertext(self, h)
+
+    def bootstrap_level(self):
+        return lib().fhe_bootstrap_level(self.h)
+
     # ---- raw words
     def ct_from_words(self, words, level, scale=1.0):
         w, p = _u64(words)
@@ -357,3 +410,17 @@ class CryptoContext:
         o1 = np.empty_like(o0)
         _check(lib().fhe_keyswitch_host(self.h, dp, level, kp, o0.ctypes.data_as(_U64P), o1.ctypes.data_as(_U64P)))
         return o0, o1
+
+
+def _register_diagnostics():
+    h = lib()
+    h.fhe_bootstrap_stage.restype = C.c_int
+    h.fhe_bootstrap_stage.argtypes = [_VP, _VP, C.c_int, C.POINTER(_VP)]
+
+
+def bootstrap_stage(ctx, ct, upto):
+    """Diagnostics: the bootstrap pipeline stopped after stage `upto` (1..4)."""
+    _register_diagnostics()
+    h = _VP()
+    _check(lib().fhe_bootstrap_stage(ctx.h, ct.h, upto, C.byref(h)))
+    return Ciphertext(ctx, h)

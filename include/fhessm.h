@@ -51,6 +51,8 @@ typedef struct {
     int hw;         /* secret Hamming weight (192); 0 = uniform ternary */
     double sigma;   /* error width (3.19) */
     int device;     /* CUDA device ordinal */
+    int boot_primes;  /* top limbs drawn as boot_bits-bit primes for the bootstrap circuit (0: none) */
+    int boot_bits;    /* size of those primes (58) */
 } fhe_params;
 
 const char* fhe_last_error(void);
@@ -132,6 +134,33 @@ int fhe_rotate(fhe_ctx* cx, const fhe_ct* a, int32_t k, fhe_ct** out);
 int fhe_rotate_hoisted(fhe_ctx* cx, const fhe_ct* a, const int32_t* ks, int n, fhe_ct** outs);
 /* EvalConj: complex conjugation of every slot (automorphism 2N-1, :1355-1369) */
 int fhe_conjugate(fhe_ctx* cx, const fhe_ct* a, fhe_ct** out);
+
+/* ---- circuit-level operations ----------------------------------------------------------
+ * mulPt (gpu_real_model.cu:2629-2632): EvalMult by a per-slot vector (re/im, n slots
+ * repeated across N/2) + RescaleInPlace; the plaintext scale is chosen so the result sits on
+ * the next level's FLEXIBLEAUTO factor */
+int fhe_mul_vec_rescale(fhe_ctx* cx, const fhe_ct* a, const double* re, const double* im, int n, fhe_ct** out);
+/* alignTo (:2636-2641): bring a ciphertext down to `level` at that level's factor (one
+ * integer product + rescale whatever the gap); in place */
+int fhe_align(fhe_ctx* cx, fhe_ct* ct, int level);
+/* EvalMult(ct, ct) + relinearise + rescale, operands aligned to the lower level first */
+int fhe_mul_rescale(fhe_ctx* cx, const fhe_ct* a, const fhe_ct* b, fhe_ct** out);
+/* polyGate3 / channel-mix polynomials (:4609-4649, :5130-5163): sum_i c_i (.) x^i, power
+ * basis, c = [deg+1][n] real per-slot coefficients (n slots, repeated) */
+int fhe_poly_eval(fhe_ctx* cx, const fhe_ct* x, const double* coeffs, int deg, int n, fhe_ct** out);
+/* sum_i c_i T_i(x) (Chebyshev basis, |x| <= 1), baby-step / giant-step, depth
+ * ceil(log2(ncoef)) + 1 */
+int fhe_cheb_eval(fhe_ctx* cx, const fhe_ct* x, const double* coeffs, int ncoef, fhe_ct** out);
+/* EvalBootstrapSetup + EvalBootstrapKeyGen (gpu_real_model.cu:1436-1444, :1293-1336):
+ * CoeffToSlot / SlotToCoeff plaintexts, the EvalMod interpolant (degree `degree` on
+ * [-bound, bound] before 3 double angles) and the rotation + conjugation keys */
+int fhe_bootstrap_setup(fhe_ctx* cx, double bound, int degree);
+/* EvalBootstrap (:2544): refresh to level fhe_bootstrap_level() */
+int fhe_bootstrap(fhe_ctx* cx, const fhe_ct* a, fhe_ct** out);
+int fhe_bootstrap_level(const fhe_ctx* cx);
+/* diagnostics: the bootstrap pipeline stopped after stage `upto` (1 ModRaise, 2 CoeffToSlot,
+ * 3 EvalMod, 4 complete) */
+int fhe_bootstrap_stage(fhe_ctx* cx, const fhe_ct* a, int upto, fhe_ct** out);
 
 /* ---- raw words (parity tests, serialisation) -------------------------------------------- */
 int fhe_ct_import(fhe_ctx* cx, const uint64_t* words, int level, double scale, fhe_ct** out);
