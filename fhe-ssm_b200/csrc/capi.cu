@@ -424,6 +424,37 @@ int fhe_bootstrap_level(const fhe_ctx* cx) {
     return nl ? cx->cx.L - nl : -1;
 }
 
+struct fhe_mvplan {
+    std::shared_ptr<fhe::MatvecPlan> p;
+};
+int fhe_matvec_plan(fhe_ctx* cx, const double* W, int rows, int cols, int D, int b1, fhe_mvplan** out) {
+    return guard([&] {
+        REQUIRE(cx && W && out && rows > 0 && cols > 0, "bad argument");
+        bind(cx);
+        *out = new fhe_mvplan{fhe::matvec_plan(cx->cx, W, rows, cols, D, b1)};
+    });
+}
+void fhe_mvplan_free(fhe_mvplan* pl) { delete pl; }
+int fhe_matvec_keygen(fhe_ctx* cx, int D, int b1) {
+    return guard([&] {
+        REQUIRE(cx && D > 0 && b1 > 0, "bad argument");
+        bind(cx);
+        std::vector<int> r = fhe::matvec_rotations(D, b1);
+        fhe::keygen_rotations(cx->cx, r.data(), (int)r.size(), false);
+    });
+}
+int fhe_matvec_bsgs(fhe_ctx* cx, const fhe_mvplan* pl, const fhe_ct* const* in, int nin, fhe_ct** out) {
+    return guard([&] {
+        REQUIRE(cx && pl && in && out && nin > 0, "null argument");
+        bind(cx);
+        std::vector<const fhe::Ciphertext*> us(nin);
+        for (int i = 0; i < nin; i++) us[i] = &in[i]->c;
+        fhe::Ciphertext r;
+        fhe::matvec(cx->cx, *pl->p, us.data(), r);
+        *out = wrap(cx, std::move(r));
+    });
+}
+
 int fhe_ct_import(fhe_ctx* cx, const uint64_t* words, int level, double scale, fhe_ct** out) {
     return guard([&] {
         REQUIRE(cx && words && out, "null argument");

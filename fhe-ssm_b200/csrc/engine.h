@@ -230,6 +230,11 @@ void cheb_eval(Context& cx, const Ciphertext& x, const std::vector<double>& coef
 std::vector<double> cheb_fit(double (*f)(double, const void*), const void* arg, double a, double b, int n);
 void poly_eval_vec(Context& cx, const Ciphertext& x, const std::vector<std::vector<std::complex<double>>>& c, int n,
                    Ciphertext& out);
+// BSGS matvec (matvec.cu)
+struct MatvecPlan;
+std::shared_ptr<MatvecPlan> matvec_plan(Context& cx, const double* W, int rows, int cols, int D, int b1);
+std::vector<int> matvec_rotations(int D, int b1);
+void matvec(Context& cx, const MatvecPlan& pl, const Ciphertext* const* us, Ciphertext& out);
 // bootstrapping (bootstrap.cu)
 std::vector<int> boot_rotations(const Context& cx);
 void bootstrap_setup(Context& cx, double B, int deg);

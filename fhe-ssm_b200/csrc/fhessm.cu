@@ -5,4 +5,5 @@
 #include "engine.cu"
 #include "circuit.cu"
 #include "bootstrap.cu"
+#include "matvec.cu"
 #include "capi.cu"

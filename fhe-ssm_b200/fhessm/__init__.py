@@ -84,6 +84,10 @@ _SIGS = {
     "fhe_bootstrap_setup": (C.c_int, [_VP, C.c_double, C.c_int]),
     "fhe_bootstrap": (C.c_int, [_VP, _VP, C.POINTER(_VP)]),
     "fhe_bootstrap_level": (C.c_int, [_VP]),
+    "fhe_matvec_plan": (C.c_int, [_VP, _DP, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(_VP)]),
+    "fhe_mvplan_free": (None, [_VP]),
+    "fhe_matvec_keygen": (C.c_int, [_VP, C.c_int, C.c_int]),
+    "fhe_matvec_bsgs": (C.c_int, [_VP, _VP, C.POINTER(_VP), C.c_int, C.POINTER(_VP)]),
     "fhe_ct_import": (C.c_int, [_VP, _U64P, C.c_int, C.c_double, C.POINTER(_VP)]),
     "fhe_ct_export": (C.c_int, [_VP, _VP, _U64P]),
     "fhe_pt_import": (C.c_int, [_VP, _U64P, C.c_int, C.c_double, C.POINTER(_VP)]),
@@ -156,6 +160,16 @@ class Ciphertext:
         out = np.empty((2, nl, self.ctx.N), dtype=np.uint64)
         _check(lib().fhe_ct_export(self.ctx.h, self.h, out.ctypes.data_as(_U64P)))
         return out
+
+
+class _MvPlan:
+    def __init__(self, h):
+        self.h = h
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().fhe_mvplan_free(self.h)
+            self.h = None
 
 
 def seed32(seed) -> bytes:
@@ -363,6 +377,23 @@ class CryptoContext:
         c = np.ascontiguousarray(np.asarray(coeffs, dtype=np.float64))
         h = _VP()
         _check(lib().fhe_cheb_eval(self.h, ct.h, c.ctypes.data_as(_DP), len(c), C.byref(h)))
+        return Ciphertext(self, h)
+
+    def matvec_plan(self, W, D, b1):
+        """Masked block-cyclic BSGS plan of W (rows <= D); column chunk s acts on input s."""
+        W = np.ascontiguousarray(np.asarray(W, dtype=np.float64))
+        h = _VP()
+        _check(lib().fhe_matvec_plan(self.h, W.ctypes.data_as(_DP), W.shape[0], W.shape[1], D, b1, C.byref(h)))
+        return _MvPlan(h)
+
+    def matvec_keygen(self, D, b1):
+        _check(lib().fhe_matvec_keygen(self.h, D, b1))
+
+    def matvec(self, plan, inputs):
+        n = len(inputs)
+        arr = (_VP * n)(*[c.h for c in inputs])
+        h = _VP()
+        _check(lib().fhe_matvec_bsgs(self.h, plan.h, arr, n, C.byref(h)))
         return Ciphertext(self, h)
 
     def EvalBootstrapSetup(self, bound=24.0, degree=59):

@@ -162,6 +162,18 @@ int fhe_bootstrap_level(const fhe_ctx* cx);
  * 3 EvalMod, 4 complete) */
 int fhe_bootstrap_stage(fhe_ctx* cx, const fhe_ct* a, int upto, fhe_ct** out);
 
+/* ---- BSGS matvec (matvecBatch / matvecBatchChunked, gpu_real_model.cu:2883-3431) ---------
+ * A plan holds the masked block-cyclic diagonals of W (rows x cols, row-major, rows <= D)
+ * for a layout of one D-channel vector per block of D slots; column chunk s of W multiplies
+ * input ciphertext s.  b1 = baby steps (D / b1 giant steps). */
+typedef struct fhe_mvplan fhe_mvplan;
+int fhe_matvec_plan(fhe_ctx* cx, const double* W, int rows, int cols, int D, int b1, fhe_mvplan** out);
+void fhe_mvplan_free(fhe_mvplan* pl);
+/* rotation keys the matvec needs: j, j - D (babies), g b1, g b1 - D (giants) */
+int fhe_matvec_keygen(fhe_ctx* cx, int D, int b1);
+/* out = W [in_0 | in_1 | ...], one level consumed, canonical scale */
+int fhe_matvec_bsgs(fhe_ctx* cx, const fhe_mvplan* pl, const fhe_ct* const* in, int nin, fhe_ct** out);
+
 /* ---- raw words (parity tests, serialisation) -------------------------------------------- */
 int fhe_ct_import(fhe_ctx* cx, const uint64_t* words, int level, double scale, fhe_ct** out);
 int fhe_ct_export(fhe_ctx* cx, const fhe_ct* ct, uint64_t* words);
