@@ -281,11 +281,14 @@ void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto
     if (!bc) throw Error("bootstrap: no bootstrap precomputation (call bootstrap_setup)", -5);
     const int N = cx.N;
     Ciphertext a = ct_copy(cx, in);
-    // 1. to one limb at the canonical scale of level L-1
+    // 1. to one limb at the canonical scale of level L-1.  A one-limb input with another scale
+    //    is relabelled (its integer message is what the pipeline refreshes) and the output
+    //    relabelled back by the same factor.
+    double relabel = 1.0;
     if (a.nl > 1) align(cx, a, 1, bc->delta_in);
     else {
-        const double r = a.scale / bc->delta_in;
-        if (r > 1 + 1e-9 || r < 1 - 1e-9) throw Error("bootstrap: one-limb input must have the canonical scale", -4);
+        relabel = a.scale / bc->delta_in;
+        a.scale = bc->delta_in;
     }
     // 2. ModRaise: centred lift of the q0 residues to all L limbs
     Ciphertext raised = ct_alloc(cx, cx.L);
@@ -348,6 +351,7 @@ void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto
         eval_level(cx, L, w, t);
         w = std::move(t);
     }
+    w.scale *= relabel;
     out = std::move(w);
 }
 

@@ -455,6 +455,88 @@ int fhe_matvec_bsgs(fhe_ctx* cx, const fhe_mvplan* pl, const fhe_ct* const* in, 
     });
 }
 
+struct fhe_model {
+    std::shared_ptr<fhe::Model> m;
+    fhe_ctx* owner;
+};
+int fhe_model_create(fhe_ctx* cx, const fhe_model_cfg* c, fhe_model** out) {
+    return guard([&] {
+        REQUIRE(cx && c && out, "null argument");
+        bind(cx);
+        fhe::ModelCfg mc;
+        mc.d = c->d; mc.dff = c->dff; mc.n_layer = c->n_layer; mc.D = c->D; mc.b1 = c->b1;
+        mc.a_min = c->a_min; mc.a_max = c->a_max; mc.alpha = c->alpha; mc.eps = c->eps;
+        mc.shift_mix = c->shift_mix != 0;
+        *out = new fhe_model{fhe::model_create(cx->cx, mc), cx};
+    });
+}
+void fhe_model_free(fhe_model* m) { delete m; }
+int fhe_model_set_layer(fhe_model* m, int layer, const double* win, const double* wout, const double* wk,
+                        const double* wr, const double* wv, const double* vecs, const double* seeds) {
+    return guard([&] {
+        REQUIRE(m && win && wout && wk && wr && wv && vecs && seeds, "null argument");
+        bind(m->owner);
+        fhe::model_set_layer(*m->m, layer, win, wout, wk, wr, wv, vecs, seeds);
+    });
+}
+int fhe_model_set_output(fhe_model* m, const double* g_out, const double* seed3) {
+    return guard([&] {
+        REQUIRE(m && g_out && seed3, "null argument");
+        m->m->g_out.assign(g_out, g_out + m->m->cfg.d);
+        m->m->out_seed = {seed3[0], seed3[1], (int)seed3[2], seed3[3], seed3[4]};
+    });
+}
+int fhe_model_keygen(fhe_model* m) {
+    return guard([&] {
+        REQUIRE(m, "null argument");
+        bind(m->owner);
+        std::vector<int> r = fhe::matvec_rotations(m->m->cfg.D, m->m->cfg.b1);
+        for (int k = 1; k < m->m->cfg.D; k <<= 1) { r.push_back(k); r.push_back(-k); }
+        fhe::keygen_rotations(m->owner->cx, r.data(), (int)r.size(), true);
+    });
+}
+int fhe_model_reset(fhe_model* m) {
+    return guard([&] {
+        REQUIRE(m, "null argument");
+        m->m->have_state = false;
+        m->m->s.clear();
+        m->m->up.clear();
+    });
+}
+int fhe_model_step(fhe_model* m, const fhe_ct* in, fhe_ct** out) {
+    return guard([&] {
+        REQUIRE(m && in && out, "null argument");
+        bind(m->owner);
+        *out = wrap(m->owner, m->m->step(in->c));
+    });
+}
+int fhe_model_stats(const fhe_model* m, long long* bootstraps, long long* steps) {
+    return guard([&] {
+        REQUIRE(m, "null argument");
+        if (bootstraps) *bootstraps = m->m->boots;
+        if (steps) *steps = m->m->steps;
+    });
+}
+int fhe_model_probe(fhe_model* m, int k) {
+    return guard([&] {
+        REQUIRE(m && k >= 0 && k <= 13, "bad argument");
+        m->m->probe = k;
+    });
+}
+int fhe_server_step(fhe_model* m, const fhe_ct* const* in, int n_in, fhe_ct** out, int* n_out, int flags) {
+    return guard([&] {
+        REQUIRE(m && in && out && n_out && n_in == 1, "one input pack per model (one ciphertext of 2N/2D lanes)");
+        bind(m->owner);
+        if (flags & 1) {
+            m->m->have_state = false;
+            m->m->s.clear();
+            m->m->up.clear();
+        }
+        out[0] = wrap(m->owner, m->m->step(in[0]->c));
+        *n_out = 1;
+    });
+}
+
 int fhe_ct_import(fhe_ctx* cx, const uint64_t* words, int level, double scale, fhe_ct** out) {
     return guard([&] {
         REQUIRE(cx && words && out, "null argument");

@@ -235,6 +235,12 @@ struct MatvecPlan;
 std::shared_ptr<MatvecPlan> matvec_plan(Context& cx, const double* W, int rows, int cols, int D, int b1);
 std::vector<int> matvec_rotations(int D, int b1);
 void matvec(Context& cx, const MatvecPlan& pl, const Ciphertext* const* us, Ciphertext& out);
+struct BabySet;
+void matvec_babies(Context& cx, const Ciphertext& u, int D, int b1, BabySet& bs);
+void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets, Ciphertext& out);
+// model (model.cu)
+struct Model;
+struct ModelCfg;
 // bootstrapping (bootstrap.cu)
 std::vector<int> boot_rotations(const Context& cx);
 void bootstrap_setup(Context& cx, double B, int deg);

@@ -6,4 +6,5 @@
 #include "circuit.cu"
 #include "bootstrap.cu"
 #include "matvec.cu"
+#include "model.cu"
 #include "capi.cu"

@@ -252,41 +252,59 @@ std::vector<int> matvec_rotations(int D, int b1) {
     return r;
 }
 
-// y = W [u_0 | u_1 | ...]: inputs (one per column chunk) at a common level and scale;
-// the output is rescaled once and lands on the canonical scale of level nl - 1
-void matvec(Context& cx, const MatvecPlan& pl, const Ciphertext* const* us, Ciphertext& out) {
-    const int N = cx.N, S = pl.nsets, b1 = pl.b1, G = pl.G, D = pl.D;
-    const int nl = us[0]->nl;
-    for (int s = 1; s < S; s++)
-        if (us[s]->nl != nl || std::fabs(us[s]->scale / us[0]->scale - 1) > 1e-9)
-            throw Error("matvec: input chunks must share level and scale", -4);
-    if (nl < 2) throw Error("matvec: no level left", -4);
-    cudaStream_t st = cx.stream;
-    // babies: rot(u, j) (j = 1..b1-1) and rot(u, j - D) (j = 0..b1-1), hoisted per input
+// the 2 b1 babies of one input: rot(u, j) (j = 0..b1-1) and rot(u, j - D) (j = 0..b1-1),
+// all with stride nl*N; one hoisted ModUp
+struct BabySet {
+    int D = 0, b1 = 0, nl = 0;
+    double scale = 0;
+    std::vector<Ciphertext> cts;   // [2 b1]: Y = 0 then Y = 1
+};
+
+void matvec_babies(Context& cx, const Ciphertext& u, int D, int b1, BabySet& bs) {
+    if (u.nl < 2) throw Error("matvec: no level left", -4);
     std::vector<int> steps;
     for (int j = 1; j < b1; j++) steps.push_back(j);
     for (int j = 0; j < b1; j++) steps.push_back(j - D);
-    std::vector<std::vector<Ciphertext>> bab(S);
-    std::vector<const uint64_t*> bptr((size_t)S * 2 * b1);
-    for (int s = 0; s < S; s++) {
-        bab[s].resize(steps.size());
-        ct_rotate_hoisted(cx, *us[s], steps.data(), (int)steps.size(), bab[s].data());
-        bptr[(size_t)s * 2 * b1 + 0] = us[s]->buf.p;
-        for (int j = 1; j < b1; j++) bptr[(size_t)s * 2 * b1 + j] = bab[s][j - 1].buf.p;
-        for (int j = 0; j < b1; j++) bptr[(size_t)s * 2 * b1 + b1 + j] = bab[s][b1 - 1 + j].buf.p;
+    std::vector<Ciphertext> r(steps.size());
+    ct_rotate_hoisted(cx, u, steps.data(), (int)steps.size(), r.data());
+    bs.D = D; bs.b1 = b1; bs.nl = u.nl; bs.scale = u.scale;
+    bs.cts.clear();
+    bs.cts.resize(2 * b1);
+    bs.cts[0] = ct_copy(cx, u);
+    for (int j = 1; j < b1; j++) bs.cts[j] = std::move(r[j - 1]);
+    for (int j = 0; j < b1; j++) bs.cts[b1 + j] = std::move(r[b1 - 1 + j]);
+}
+
+void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets, Ciphertext& out);
+
+// y = W [u_0 | u_1 | ...]: inputs (one per column chunk) at a common level and scale;
+// the output is rescaled once and lands on the canonical scale of level nl - 1
+void matvec(Context& cx, const MatvecPlan& pl, const Ciphertext* const* us, Ciphertext& out) {
+    std::vector<BabySet> bs(pl.nsets);
+    std::vector<const BabySet*> ptr(pl.nsets);
+    for (int s = 0; s < pl.nsets; s++) {
+        matvec_babies(cx, *us[s], pl.D, pl.b1, bs[s]);
+        ptr[s] = &bs[s];
     }
-    // every baby has stride nl*N (fresh allocations) except u itself: copy u if needed
-    std::vector<Ciphertext> ucopy(S);
+    matvec_apply(cx, pl, ptr.data(), out);
+}
+
+void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets, Ciphertext& out) {
+    const int N = cx.N, S = pl.nsets, b1 = pl.b1, G = pl.G, D = pl.D;
+    const int nl = sets[0]->nl;
     for (int s = 0; s < S; s++)
-        if (us[s]->stride != (size_t)nl * N) {
-            ucopy[s] = ct_copy(cx, *us[s]);
-            bptr[(size_t)s * 2 * b1] = ucopy[s].buf.p;
-        }
+        if (sets[s]->nl != nl || std::fabs(sets[s]->scale / sets[0]->scale - 1) > 1e-9 || sets[s]->D != D ||
+            sets[s]->b1 != b1)
+            throw Error("matvec: input chunks must share level, scale and baby geometry", -4);
+    cudaStream_t st = cx.stream;
+    std::vector<const uint64_t*> bptr((size_t)S * 2 * b1);
+    for (int s = 0; s < S; s++)
+        for (int k = 0; k < 2 * b1; k++) bptr[(size_t)s * 2 * b1 + k] = sets[s]->cts[k].buf.p;
     DevBuf dptr(bptr.size(), st);
     CUDA_CHECK(cudaMemcpyAsync(dptr.p, bptr.data(), bptr.size() * 8, cudaMemcpyHostToDevice, st));
     // plaintexts at this level: scale so that the rescaled output is canonical
     const double target = canon(cx, nl - 1);
-    const double spt = target * (double)cx.mods[nl - 1] / us[0]->scale;
+    const double spt = target * (double)cx.mods[nl - 1] / sets[0]->scale;
     int logD2 = 0;
     while ((1 << logD2) < 2 * D) logD2++;
     DevBuf pts((size_t)std::max(pl.P, 1) * nl * 2 * D, st);
@@ -317,9 +335,8 @@ void matvec(Context& cx, const MatvecPlan& pl, const Ciphertext* const* us, Ciph
         CUDA_CHECK(cudaGetLastError());
         cx.launches++;
     }
-    for (int s = 0; s < S; s++) bab[s].clear();
     // giants: sum_g rot(IA_g, g b1) + rot(IB_g, g b1 - D)
-    const double sc = us[0]->scale * spt;
+    const double sc = sets[0]->scale * spt;
     auto view = [&](int o) {
         Ciphertext c = ct_alloc(cx, nl);
         CUDA_CHECK(cudaMemcpyAsync(c.buf.p, inner.p + (size_t)o * 2 * nl * N, (size_t)2 * nl * N * 8,

@@ -174,6 +174,43 @@ int fhe_matvec_keygen(fhe_ctx* cx, int D, int b1);
 /* out = W [in_0 | in_1 | ...], one level consumed, canonical scale */
 int fhe_matvec_bsgs(fhe_ctx* cx, const fhe_mvplan* pl, const fhe_ct* const* in, int nin, fhe_ct** out);
 
+/* ---- the encrypted model step -------------------------------------------------------------
+ * The layer loop of gpu_real_model.cu:4744-5264 (+ carry :4688-4737, :5271-5300, output norm
+ * :5389) for the polynomial SSM of train_fhe_native_ssm.py (_fwd_np :829-890).  Lanes: one
+ * conversation per block of D slots, complex packing (lane r real part, lane r + N/2D
+ * imaginary part).  vecs: d-length decay, 1-decay, g1, mix, c, dd, p0, p1, p2, g2 then
+ * dff-length q0, q1, q2, q3, r0, r1, r2; seeds (15 values): rmsnorm Newton seeds (a, b, iters)
+ * of the time-mix and channel-mix norms (the bundle's L{i}.{tm,cm}.rsqrt,
+ * train_fhe_native_ssm.py:1121-1124), then the bootstrap gains of the refresh sites tm.x,
+ * tm.ms, u, s, g, cm.x, cm.ms, v, f (a site is refreshed at value * gain: a bootstrap's error
+ * is absolute, so small-valued sites are scaled up by relabelling the scale).
+ * fhe_model_set_output: seed3 = (a, b, iters, gain x, gain ms) of the output norm. */
+typedef struct fhe_model fhe_model;
+typedef struct {
+    int d, dff, n_layer, D, b1;
+    double a_min, a_max, alpha, eps;
+    int shift_mix;
+} fhe_model_cfg;
+int fhe_model_create(fhe_ctx* cx, const fhe_model_cfg* cfg, fhe_model** out);
+void fhe_model_free(fhe_model* m);
+int fhe_model_set_layer(fhe_model* m, int layer, const double* win, const double* wout, const double* wk,
+                        const double* wr, const double* wv, const double* vecs, const double* seeds);
+int fhe_model_set_output(fhe_model* m, const double* g_out, const double* seed3);
+/* rotation keys of the matvecs and the norm reductions (bootstrap keys: fhe_bootstrap_setup) */
+int fhe_model_keygen(fhe_model* m);
+/* drop the carried state (req.N.reset, gpu_real_model.cu:4465-4469) */
+int fhe_model_reset(fhe_model* m);
+/* one token for every lane: in = embedded rows, out = rmsnorm(h, g_out) (the client applies
+ * the tied head in plaintext, --dec-out :2444-2533) */
+int fhe_model_step(fhe_model* m, const fhe_ct* in, fhe_ct** out);
+int fhe_model_stats(const fhe_model* m, long long* bootstraps, long long* steps);
+/* diagnostics: k > 0 makes fhe_model_step return the layer-0 intermediate k (1 norm,
+ * 2 shift-mix, 3 Win x, 4 scan, 5 readout, 6 gate, 7 h+attn, 8 norm 2, 9 k_0, 10 f_0, 11 h+ffn) */
+int fhe_model_probe(fhe_model* m, int k);
+/* server step (the request/response of the serve loop :4385-4483): n_in input ciphertexts
+ * (one per pack), flags bit 0 = reset the carry first; *n_out outputs */
+int fhe_server_step(fhe_model* m, const fhe_ct* const* in, int n_in, fhe_ct** out, int* n_out, int flags);
+
 /* ---- raw words (parity tests, serialisation) -------------------------------------------- */
 int fhe_ct_import(fhe_ctx* cx, const uint64_t* words, int level, double scale, fhe_ct** out);
 int fhe_ct_export(fhe_ctx* cx, const fhe_ct* ct, uint64_t* words);
