@@ -483,7 +483,7 @@ int fhe_model_set_output(fhe_model* m, const double* g_out, const double* seed3)
     return guard([&] {
         REQUIRE(m && g_out && seed3, "null argument");
         m->m->g_out.assign(g_out, g_out + m->m->cfg.d);
-        m->m->out_seed = {seed3[0], seed3[1], (int)seed3[2], seed3[3], seed3[4]};
+        m->m->out_seed = {seed3[0], seed3[1], (int)seed3[2], seed3[3], seed3[4], seed3[5]};
     });
 }
 int fhe_model_keygen(fhe_model* m) {
@@ -519,7 +519,7 @@ int fhe_model_stats(const fhe_model* m, long long* bootstraps, long long* steps)
 }
 int fhe_model_probe(fhe_model* m, int k) {
     return guard([&] {
-        REQUIRE(m && k >= 0 && k <= 13, "bad argument");
+        REQUIRE(m && k >= 0 && k % 100 <= 13, "bad argument");
         m->m->probe = k;
     });
 }

@@ -16,7 +16,6 @@
 
 namespace fhe {
 
-__global__ void k_mul_const(const uint64_t*, long long, uint64_t*, long long, const uint64_t*, const uint64_t*, int);
 __global__ void k_signed_to_limbs(const int64_t*, uint64_t*, LimbMap, int);
 
 static void require(bool c, const char* msg) {
@@ -25,43 +24,15 @@ static void require(bool c, const char* msg) {
 
 double canon(const Context& cx, int nl) { return cx.scale_at[nl]; }
 
-// integer constant M (may be negative, |M| < 2^126) as per-limb residues + shoup, on the device
-static DevBuf const_limbs(Context& cx, long double M, int nl) {
-    std::vector<uint64_t> h(2 * nl);
-    const bool neg = M < 0;
-    long double a = std::floor((neg ? -M : M) + 0.5L);
-    const unsigned __int128 u = (unsigned __int128)a;
-    for (int i = 0; i < nl; i++) {
-        const uint64_t q = cx.mods[i];
-        uint64_t r = (uint64_t)(u % q);
-        if (neg && r) r = q - r;
-        h[2 * i] = r;
-        h[2 * i + 1] = shoup_of(r, q);
-    }
-    DevBuf d(h.size(), cx.stream);
-    CUDA_CHECK(cudaMemcpyAsync(d.p, h.data(), h.size() * 8, cudaMemcpyHostToDevice, cx.stream));
-    CUDA_CHECK(cudaStreamSynchronize(cx.stream));
-    return d;
-}
-
-// out = a * M (integer), no rescale; out may alias a
+// out = a * M (integer, |M| < 2^126), no rescale; out may alias a (scale unchanged)
 void mul_integer(Context& cx, const Ciphertext& a, long double M, Ciphertext& out) {
-    DevBuf w = const_limbs(cx, M, a.nl);
-    Ciphertext t;
-    if (&out == &a) {
-        k_mul_const<<<dim3(cx.N / 256, a.nl, 2), 256, 0, cx.stream>>>(a.buf.p, (long long)a.stride, a.buf.p,
-                                                                       (long long)a.stride, w.p, nullptr, cx.logN);
-        CUDA_CHECK(cudaGetLastError());
-        cx.launches++;
-        return;
-    }
-    t = ct_alloc(cx, a.nl);
-    k_mul_const<<<dim3(cx.N / 256, a.nl, 2), 256, 0, cx.stream>>>(a.buf.p, (long long)a.stride, t.buf.p,
-                                                                   (long long)t.stride, w.p, nullptr, cx.logN);
-    CUDA_CHECK(cudaGetLastError());
-    cx.launches++;
-    t.scale = a.scale;
-    out = std::move(t);
+    LimbConst k{};
+    k.has_w = 1;
+    limb_residues(cx, M, a.nl, k.w);
+    for (int i = 0; i < a.nl; i++) k.wp[i] = shoup_of(k.w[i], cx.mods[i]);
+    const double sc = a.scale;
+    apply_limb_const(cx, a, k, out);
+    out.scale = sc;
 }
 
 // value * c, rescaled once; the integer factor round(c * S) is chosen so that the output
@@ -147,7 +118,7 @@ void mul_vec_rescale(Context& cx, const Ciphertext& a, const std::complex<double
     require(a.nl >= 2, "mul_vec_rescale: no level left");
     if (target <= 0) target = canon(cx, a.nl - 1);
     const double s = target * (double)cx.mods[a.nl - 1] / a.scale;
-    Plaintext pt = encode(cx, v, n, a.nl, s);
+    const Plaintext& pt = encode_cached(cx, v, n, a.nl, s);
     Ciphertext t;
     ct_mul_pt(cx, a, pt, t);
     ct_rescale(cx, t);
@@ -157,7 +128,7 @@ void mul_vec_rescale(Context& cx, const Ciphertext& a, const std::complex<double
 
 // + vector (n slots, repeated) at the ciphertext's scale
 void add_vec(Context& cx, const Ciphertext& a, const std::complex<double>* v, int n, Ciphertext& out) {
-    Plaintext pt = encode(cx, v, n, a.nl, a.scale);
+    const Plaintext& pt = encode_cached(cx, v, n, a.nl, a.scale);
     ct_add_pt(cx, a, pt, out);
 }
 
@@ -276,30 +247,34 @@ struct ChebEval {
             M *= 2;
             giant[M] = std::move(n2);
         }
-        // align babies to the lowest baby level with canonical scale
+        // align babies to the lowest baby level (their scales may differ: the leaf products
+        // pick one integer factor per baby)
         int lo = T[1].nl;
         for (int i = 1; i < bs; i++) lo = std::min(lo, T[i].nl);
-        for (int i = 1; i < bs; i++) align(cx, T[i], lo, 0);
+        for (int i = 1; i < bs; i++)
+            if (T[i].nl > lo) align(cx, T[i], lo, 0);
     }
 
-    // leaf: sum_{i < bs} c_i T_i  (one level: integer products + one rescale)
+    // leaf: sum_{i < bs} c_i T_i  (one level: integer products + one rescale).  Baby i is
+    // multiplied by round(c_i * S_i), S_i = target q / scale_i, so every term carries the
+    // common scale target * q before the rescale.
     Ciphertext leaf(const std::vector<double>& c) {
         const int nl = T[1].nl;
         const double target = canon(cx, nl - 1);
-        const double S = target * (double)cx.mods[nl - 1] / T[1].scale;   // all babies share T[1]'s scale
+        const double tq = target * (double)cx.mods[nl - 1];
         Ciphertext acc;
         bool have = false;
         for (int i = 1; i < (int)c.size() && i < bs; i++) {
             if (c[i] == 0.0) continue;
             Ciphertext t;
-            mul_integer(cx, T[i], std::floor((long double)c[i] * S + 0.5L), t);
+            mul_integer(cx, T[i], std::floor((long double)c[i] * (long double)(tq / T[i].scale) + 0.5L), t);
             if (!have) { acc = std::move(t); have = true; }
-            else { Ciphertext u; ct_add(cx, acc, t, u); acc = std::move(u); }
+            else { Ciphertext u; ct_add_raw(cx, acc, t, u); acc = std::move(u); }
         }
         if (!have) {   // constant-only leaf: 0 * T_1 keeps a valid ciphertext
             mul_integer(cx, T[1], 0, acc);
         }
-        acc.scale = T[1].scale * S;
+        acc.scale = tq;
         ct_rescale(cx, acc);
         acc.scale = target;
         if (!c.empty() && c[0] != 0.0) {
@@ -362,9 +337,12 @@ void poly_eval_vec(Context& cx, const Ciphertext& x, const std::vector<std::vect
         const int a = (i + 1) / 2, b = i / 2;   // x^i = x^a x^b
         mul_rescale(cx, pw[a], pw[b], pw[i]);
     }
+    // one level for all powers; their scales may differ (each coefficient product below picks
+    // its own plaintext scale and lands on the same canonical output scale)
     int lo = pw[1].nl;
     for (int i = 1; i <= deg; i++) lo = std::min(lo, pw[i].nl);
-    for (int i = 1; i <= deg; i++) align(cx, pw[i], lo, 0);
+    for (int i = 1; i <= deg; i++)
+        if (pw[i].nl > lo) align(cx, pw[i], lo, 0);
     Ciphertext acc;
     bool have = false;
     for (int i = 1; i <= deg; i++) {

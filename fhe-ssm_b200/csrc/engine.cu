@@ -26,7 +26,6 @@ __global__ void k_moddown_final(const uint64_t*, const uint64_t*, const uint64_t
 __global__ void k_rescale_lift(const uint64_t*, uint64_t*, int, int, int);
 __global__ void k_rescale_final(uint64_t*, long long, const uint64_t*, const uint64_t*, int, int, int, int);
 __global__ void k_ewise(int, const uint64_t*, long long, const uint64_t*, long long, uint64_t*, long long, int, int);
-__global__ void k_mul_const(const uint64_t*, long long, uint64_t*, long long, const uint64_t*, const uint64_t*, int);
 __global__ void k_tensor(const uint64_t*, long long, const uint64_t*, long long, uint64_t*, long long, uint64_t*, int);
 __global__ void k_signed_to_limbs(const int64_t*, uint64_t*, LimbMap, int);
 __global__ void k_automorph(const uint64_t*, uint64_t*, uint64_t, int);
@@ -250,6 +249,7 @@ Context::~Context() {
     if (stream) cudaStreamSynchronize(stream);
     boot.reset();
     pt_i.reset();
+    ptcache.clear();
     rlk.reset();
     rot_keys.clear();
     sk = DevBuf();
@@ -415,6 +415,13 @@ void ct_add(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& o
     ewise(cx, EW_ADD, a, b.buf.p, (long long)b.stride, 0, out);
     out.scale = a.scale;
 }
+// addition of residues whose scales the caller has already made equal (no scale check)
+void ct_add_raw(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out) {
+    if (a.nl != b.nl) throw Error("add: level mismatch", -4);
+    const double sc = a.scale;
+    ewise(cx, EW_ADD, a, b.buf.p, (long long)b.stride, 0, out);
+    out.scale = sc;
+}
 void ct_sub(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out) {
     check_same(a, b, "sub");
     ewise(cx, EW_SUB, a, b.buf.p, (long long)b.stride, 0, out);
@@ -539,49 +546,54 @@ static uint64_t signed_mod(long double v, uint64_t q) {
     return neg ? (r ? q - r : 0) : r;
 }
 
-void ct_mul_const(Context& cx, const Ciphertext& a, double v, double scale, Ciphertext& out) {
-    std::vector<uint64_t> w(a.nl);
-    const long double c = (long double)v * (long double)scale;
-    for (int i = 0; i < a.nl; i++) w[i] = signed_mod(c, cx.mods[i]);
-    DevBuf d = limb_consts(cx, w, true);
-    Ciphertext t;
-    ensure_out(cx, t, a.nl);
-    k_mul_const<<<g2(cx, a.nl, 2), 256, 0, cx.stream>>>(a.buf.p, (long long)a.stride, t.buf.p, (long long)t.stride,
-                                                        d.p, nullptr, cx.logN);
+void limb_residues(const Context& cx, long double v, int nl, uint64_t* out) {
+    for (int i = 0; i < nl; i++) out[i] = signed_mod(v, cx.mods[i]);
+}
+
+void apply_limb_const(Context& cx, const Ciphertext& a, const LimbConst& k, Ciphertext& out) {
+    if (&out == &a) {
+        k_mul_const<<<g2(cx, a.nl, 2), 256, 0, cx.stream>>>(a.buf.p, (long long)a.stride, a.buf.p, (long long)a.stride,
+                                                            k, cx.logN);
+    } else {
+        Ciphertext t;
+        ensure_out(cx, t, a.nl);
+        k_mul_const<<<g2(cx, a.nl, 2), 256, 0, cx.stream>>>(a.buf.p, (long long)a.stride, t.buf.p, (long long)t.stride,
+                                                            k, cx.logN);
+        t.scale = a.scale;
+        out = std::move(t);
+    }
     CUDA_CHECK(cudaGetLastError());
     cx.launches++;
-    t.scale = a.scale * scale;
-    out = std::move(t);
+}
+
+static LimbConst mul_consts(const Context& cx, long double c, int nl) {
+    LimbConst k{};
+    k.has_w = 1;
+    limb_residues(cx, c, nl, k.w);
+    for (int i = 0; i < nl; i++) k.wp[i] = shoup_of(k.w[i], cx.mods[i]);
+    return k;
+}
+
+void ct_mul_const(Context& cx, const Ciphertext& a, double v, double scale, Ciphertext& out) {
+    const double sc = a.scale * scale;
+    apply_limb_const(cx, a, mul_consts(cx, (long double)v * (long double)scale, a.nl), out);
+    out.scale = sc;
 }
 
 void ct_mul_int(Context& cx, const Ciphertext& a, int64_t v, Ciphertext& out) {
-    std::vector<uint64_t> w(a.nl);
-    for (int i = 0; i < a.nl; i++) w[i] = signed_mod((long double)v, cx.mods[i]);
-    DevBuf d = limb_consts(cx, w, true);
-    Ciphertext t;
-    ensure_out(cx, t, a.nl);
-    k_mul_const<<<g2(cx, a.nl, 2), 256, 0, cx.stream>>>(a.buf.p, (long long)a.stride, t.buf.p, (long long)t.stride,
-                                                        d.p, nullptr, cx.logN);
-    CUDA_CHECK(cudaGetLastError());
-    cx.launches++;
-    t.scale = a.scale;
-    out = std::move(t);
+    const double sc = a.scale;
+    apply_limb_const(cx, a, mul_consts(cx, (long double)v, a.nl), out);
+    out.scale = sc;
 }
 
 // adds the constant v (every slot) at the ciphertext's scale: constant polynomial round(v*scale)
 void ct_add_const(Context& cx, const Ciphertext& a, double v, Ciphertext& out) {
-    std::vector<uint64_t> w(a.nl);
-    const long double c = (long double)v * (long double)a.scale;
-    for (int i = 0; i < a.nl; i++) w[i] = signed_mod(c, cx.mods[i]);
-    DevBuf d = limb_consts(cx, w, false);
-    Ciphertext t;
-    ensure_out(cx, t, a.nl);
-    k_mul_const<<<g2(cx, a.nl, 2), 256, 0, cx.stream>>>(a.buf.p, (long long)a.stride, t.buf.p, (long long)t.stride,
-                                                        nullptr, d.p, cx.logN);
-    CUDA_CHECK(cudaGetLastError());
-    cx.launches++;
-    t.scale = a.scale;
-    out = std::move(t);
+    LimbConst k{};
+    k.has_add = 1;
+    limb_residues(cx, (long double)v * (long double)a.scale, a.nl, k.add);
+    const double sc = a.scale;
+    apply_limb_const(cx, a, k, out);
+    out.scale = sc;
 }
 
 // ========================================================================= encoding ====

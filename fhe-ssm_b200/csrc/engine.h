@@ -136,6 +136,7 @@ struct Context {
     bool prof = false;
     mutable std::map<std::string, ProfEntry> prof_acc;
     std::unique_ptr<Plaintext> pt_i;         // NTT of X^{N/2}: multiplication by i
+    std::map<uint64_t, std::shared_ptr<Plaintext>> ptcache;   // encode_cached: (content, level, scale)
     std::shared_ptr<void> boot;              // bootstrapping precomputation (bootstrap.cu)
 
     explicit Context(const Params& p);
@@ -150,6 +151,16 @@ struct Context {
 };
 
 enum EwOp : int { EW_ADD = 0, EW_SUB = 1, EW_MULPT = 2, EW_ADDPT = 3, EW_NEG = 4 };
+
+// per-limb constants passed by value to k_mul_const (1.5 KB of kernel parameters)
+struct LimbConst {
+    uint64_t w[kMaxMod], wp[kMaxMod], add[kMaxMod];
+    int has_w, has_add;
+};
+// out = a * w (+ add on c0), limb-wise; out may alias a
+void apply_limb_const(Context& cx, const Ciphertext& a, const LimbConst& k, Ciphertext& out);
+// round(v) mod q_i for each limb (|v| < 2^126)
+void limb_residues(const Context& cx, long double v, int nl, uint64_t* out);
 
 // Brackets the launches of one kernel (or kernel pair) with CUDA events on the context's
 // stream when profiling is on; `bytes` is the algorithmic DRAM traffic of the bracket.
@@ -187,6 +198,7 @@ Ciphertext ct_alloc(Context& cx, int nl);
 Ciphertext ct_copy(Context& cx, const Ciphertext& a);
 void ct_add(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out);
 void ct_sub(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out);
+void ct_add_raw(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out);
 void ct_mul_pt(Context& cx, const Ciphertext& a, const Plaintext& pt, Ciphertext& out);
 void ct_add_pt(Context& cx, const Ciphertext& a, const Plaintext& pt, Ciphertext& out);
 void ct_mul_relin(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out);
@@ -230,6 +242,9 @@ void cheb_eval(Context& cx, const Ciphertext& x, const std::vector<double>& coef
 std::vector<double> cheb_fit(double (*f)(double, const void*), const void* arg, double a, double b, int n);
 void poly_eval_vec(Context& cx, const Ciphertext& x, const std::vector<std::vector<std::complex<double>>>& c, int n,
                    Ciphertext& out);
+// encode with a cache keyed by (content, slots, level, scale); periodic vectors (n < N/2)
+// are stored compressed (matvec.cu)
+const Plaintext& encode_cached(Context& cx, const std::complex<double>* z, int n, int nl, double scale);
 // BSGS matvec (matvec.cu)
 struct MatvecPlan;
 std::shared_ptr<MatvecPlan> matvec_plan(Context& cx, const double* W, int rows, int cols, int D, int b1);

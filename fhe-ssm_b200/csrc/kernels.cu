@@ -188,16 +188,16 @@ __global__ void k_ewise(int op, const uint64_t* a, long long sa, const uint64_t*
     o[(size_t)c * so + (size_t)i * N + x] = r;
 }
 
-// multiply every limb i by a per-limb constant w[i] (shoup pair), optionally add cst[i] to c0
-__global__ void k_mul_const(const uint64_t* a, long long sa, uint64_t* o, long long so, const uint64_t* __restrict__ w,
-                            const uint64_t* __restrict__ addc, int logN) {
+// multiply every limb i by a per-limb constant (shoup pair), optionally add a per-limb constant
+// to c0.  The constants travel in the kernel parameters (no host-to-device copy, no sync).
+__global__ void k_mul_const(const uint64_t* a, long long sa, uint64_t* o, long long so, const LimbConst k, int logN) {
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int i = blockIdx.y, c = blockIdx.z;
     const uint64_t q = c_mod[i].q;
     uint64_t v = a[(size_t)c * sa + (size_t)i * N + x];
-    if (w) v = mul_shoup(v, w[2 * i], w[2 * i + 1], q);
-    if (addc && c == 0) v = mod_add(v, addc[i], q);
+    if (k.has_w) v = mul_shoup(v, k.w[i], k.wp[i], q);
+    if (k.has_add && c == 0) v = mod_add(v, k.add[i], q);
     o[(size_t)c * so + (size_t)i * N + x] = v;
 }
 

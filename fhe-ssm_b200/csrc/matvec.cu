@@ -35,10 +35,10 @@ static void fft_special_inv_small(std::complex<double>* v, int n, int M);
 // --------------------------------------------------------------------------- kernels ----
 // coef [P][2D] fp64 -> out [P][nl][2D] words: round(c * scale) mod q_i, 2D-point NTT with the
 // first 2D entries of the ring-N root table (they are the powers of psi^(N/2D) in the same
-// bit-reversed order), then * 2^64 mod q (Montgomery form for k_bsgs_mac)
+// bit-reversed order), then (mont != 0) * 2^64 mod q (Montgomery form for k_bsgs_mac)
 __global__ void __launch_bounds__(256) k_ptgen(const double* __restrict__ coef, double scale, uint64_t* __restrict__ out,
                                                int nl, int logD2, const uint64_t* __restrict__ tw,
-                                               const uint64_t* __restrict__ twp, int N) {
+                                               const uint64_t* __restrict__ twp, int N, int mont) {
     extern __shared__ uint64_t sa[];
     const int D2 = 1 << logD2;
     const int id = blockIdx.x, i = blockIdx.y;
@@ -65,11 +65,66 @@ __global__ void __launch_bounds__(256) k_ptgen(const double* __restrict__ coef, 
         __syncthreads();
     }
     uint64_t* o = out + ((size_t)id * nl + i) * D2;
-    for (int k = threadIdx.x; k < D2; k += blockDim.x) o[k] = redc(__umul64hi(sa[k], mc.r2), sa[k] * mc.r2, mc);
+    for (int k = threadIdx.x; k < D2; k += blockDim.x)
+        o[k] = mont ? redc(__umul64hi(sa[k], mc.r2), sa[k] * mc.r2, mc) : sa[k];
 }
 
+// ------------------------------------------------------- periodic encode + plaintext cache ----
+// A slot vector of period n < N/2 encodes as the ring-2n encoding of one period at stride
+// N/2n (the identity of hpc_gpu_port/periodic_encode.hpp): a 2n-word compressed plaintext per
+// limb, read by the element-wise kernels at word x >> log2(N/2n).  Plaintexts of the model's
+// fixed vectors are cached by (content, level, scale), so a step re-encodes nothing.
+static Plaintext encode_periodic(Context& cx, const std::complex<double>* z, int n, int nl, double scale) {
+    std::vector<std::complex<double>> v(z, z + n);
+    fft_special_inv(v.data(), n, 4 * n);
+    std::vector<double> co(2 * n);
+    const double maxv = (double)((1ull << 61) - 1);
+    for (int k = 0; k < n; k++) {
+        co[k] = v[k].real();
+        co[k + n] = v[k].imag();
+        if (std::fabs(co[k] * scale) > maxv || std::fabs(co[k + n] * scale) > maxv)
+            throw Error("encode: value * scale exceeds 61 bits (refused)", -6);
+    }
+    DevBuf dc(co.size(), cx.stream);
+    CUDA_CHECK(cudaMemcpyAsync(dc.p, co.data(), co.size() * 8, cudaMemcpyHostToDevice, cx.stream));
+    int log2n = 0;
+    while ((1 << log2n) < 2 * n) log2n++;
+    Plaintext pt;
+    pt.buf = DevBuf((size_t)nl * 2 * n, cx.stream);
+    pt.nl = nl;
+    pt.scale = scale;
+    int lr = 0;
+    while ((cx.N >> lr) > 2 * n) lr++;
+    pt.log_rep = lr;
+    k_ptgen<<<dim3(1, nl), 256, 2 * n * 8, cx.stream>>>((const double*)dc.p, scale, pt.buf.p, nl, log2n, cx.d_tw,
+                                                       cx.d_twp, cx.N, 0);
+    CUDA_CHECK(cudaGetLastError());
+    cx.launches++;
+    return pt;
+}
+
+const Plaintext& encode_cached(Context& cx, const std::complex<double>* z, int n, int nl, double scale) {
+    uint64_t h = 1469598103934665603ull;   // FNV-1a over the bytes of (values, n, nl, scale)
+    auto mix = [&](const void* p, size_t bytes) {
+        const uint8_t* b = (const uint8_t*)p;
+        for (size_t i = 0; i < bytes; i++) { h ^= b[i]; h *= 1099511628211ull; }
+    };
+    mix(z, sizeof(std::complex<double>) * n);
+    mix(&n, sizeof n);
+    mix(&nl, sizeof nl);
+    mix(&scale, sizeof scale);
+    auto it = cx.ptcache.find(h);
+    if (it != cx.ptcache.end()) return *it->second;
+    if (cx.ptcache.size() > 50000) cx.ptcache.clear();
+    auto pt = std::make_shared<Plaintext>(n < cx.N / 2 && (cx.N / 2) % n == 0 && n >= 8
+                                              ? encode_periodic(cx, z, n, nl, scale)
+                                              : encode(cx, z, n, nl, scale));
+    return *cx.ptcache.emplace(h, pt).first->second;
+}
+
+constexpr int kMaxBabies = 256;   // sets * 2 * b1 (kernel-parameter array)
 struct MacArgs {
-    const uint64_t* const* babies;   // [set][2][b1] ciphertext bases (Y = 0: rot(u, j), Y = 1: rot(u, j - D))
+    const uint64_t* babies[kMaxBabies];   // [set][2][b1] ciphertext bases (Y = 0: rot(u, j), Y = 1: rot(u, j - D))
     long long bstride;               // words between c0 and c1 of a baby
     const int* ids;                  // [set][3][G][b1] plaintext id or -1 (families AA, AB, BA)
     const uint64_t* pts;             // [P][nl][2D] Montgomery words
@@ -297,11 +352,7 @@ void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets,
             sets[s]->b1 != b1)
             throw Error("matvec: input chunks must share level, scale and baby geometry", -4);
     cudaStream_t st = cx.stream;
-    std::vector<const uint64_t*> bptr((size_t)S * 2 * b1);
-    for (int s = 0; s < S; s++)
-        for (int k = 0; k < 2 * b1; k++) bptr[(size_t)s * 2 * b1 + k] = sets[s]->cts[k].buf.p;
-    DevBuf dptr(bptr.size(), st);
-    CUDA_CHECK(cudaMemcpyAsync(dptr.p, bptr.data(), bptr.size() * 8, cudaMemcpyHostToDevice, st));
+    if ((size_t)S * 2 * b1 > (size_t)kMaxBabies) throw Error("matvec: too many babies for one launch", -1);
     // plaintexts at this level: scale so that the rescaled output is canonical
     const double target = canon(cx, nl - 1);
     const double spt = target * (double)cx.mods[nl - 1] / sets[0]->scale;
@@ -311,14 +362,15 @@ void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets,
     if (pl.P > 0) {
         ProfScope ps(cx, "ptgen", 8.0 * pl.P * 2 * D * (1 + nl));
         k_ptgen<<<dim3(pl.P, nl), 256, 2 * D * 8, st>>>((const double*)pl.coef.p, spt, pts.p, nl, logD2, cx.d_tw,
-                                                        cx.d_twp, N);
+                                                        cx.d_twp, N, 1);
         CUDA_CHECK(cudaGetLastError());
         cx.launches++;
     }
     DevBuf inner((size_t)2 * G * 2 * nl * N, st);
     {
         MacArgs a;
-        a.babies = (const uint64_t* const*)dptr.p;
+        for (int s = 0; s < S; s++)
+            for (int k = 0; k < 2 * b1; k++) a.babies[(size_t)s * 2 * b1 + k] = sets[s]->cts[k].buf.p;
         a.bstride = (long long)nl * N;
         a.ids = (const int*)pl.d_ids.p;
         a.pts = pts.p;

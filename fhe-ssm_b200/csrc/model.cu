@@ -30,6 +30,7 @@ struct NormSeed {
     double a = 1.0, b = 0.0;
     int iters = 0;
     double gx = 1.0, gms = 1.0;   // bootstrap gains of the input and of mean(x^2) + eps
+    double gy = 1.0;              // bootstrap gain of the Newton iterate (~ 1/sqrt(ms))
 };
 
 struct ModelCfg {
@@ -136,33 +137,54 @@ struct Model {
             add_vec(cx, ms, ee.data(), D, e);
             ms = std::move(e);
         }
-        refresh(ms, 2 + 2 * sd.iters, sd.gms);
+        const int maxlv = bootstrap_levels_after(cx) - 1;
+        refresh(ms, std::min(2 + 2 * sd.iters, maxlv), sd.gms);
+        // the Newton chain runs on complex-packed (y, -ms/2) pairs: seed and iterations act on
+        // the real and imaginary parts separately, and a pair that runs out of levels between
+        // iterations is merged and bootstrapped once (one bootstrap serves both parts)
         Ciphertext mr, mi;
         split_complex(cx, ms, mr, mi, true);
-        Ciphertext xgr = mulv(xr, g), xgi = mulv(xi, g);
-        Ciphertext outp[2];
+        Ciphertext yp[2], mh[2];
         Ciphertext* mparts[2] = {&mr, &mi};
-        Ciphertext* xparts[2] = {&xgr, &xgi};
         for (int P = 0; P < 2; P++) {
-            const Ciphertext& mp = *mparts[P];
-            Ciphertext y, yb;
-            mul_const_rescale(cx, mp, sd.b, yb, 0);
-            ct_add_const(cx, yb, sd.a, y);
-            Ciphertext mh;
-            mul_const_rescale(cx, mp, -0.5, mh, 0);
-            for (int it = 0; it < sd.iters; it++) {
+            Ciphertext yb;
+            mul_const_rescale(cx, *mparts[P], sd.b, yb, 0);
+            ct_add_const(cx, yb, sd.a, yp[P]);
+            mul_const_rescale(cx, *mparts[P], -0.5, mh[P], 0);
+        }
+        for (int it = 0; it < sd.iters; it++) {
+            if (yp[0].nl - 1 < 2 + (it + 1 == sd.iters ? 1 : 0)) {
+                Ciphertext yc, mc;
+                merge_complex(cx, std::move(yp[0]), std::move(yp[1]), yc);
+                merge_complex(cx, std::move(mh[0]), std::move(mh[1]), mc);
+                const int rest = 2 * (sd.iters - it) + 1;
+                refresh(yc, std::min(rest, maxlv), sd.gy);
+                refresh(mc, std::min(rest, maxlv), sd.gms * 2);
+                split_complex(cx, yc, yp[0], yp[1], true);
+                split_complex(cx, mc, mh[0], mh[1], true);
+            }
+            for (int P = 0; P < 2; P++) {
                 Ciphertext y2, tt, u, y3;
-                mul_rescale(cx, y, y, y2);
-                mul_rescale(cx, mh, y, tt);
+                mul_rescale(cx, yp[P], yp[P], y2);
+                mul_rescale(cx, mh[P], yp[P], tt);
                 mul_rescale(cx, tt, y2, u);
-                mul_integer(cx, y, 3, y3);   // 1.5 y at twice the scale
-                y3.scale = y.scale * 2;
+                mul_integer(cx, yp[P], 3, y3);   // 1.5 y at twice the scale
+                y3.scale = yp[P].scale * 2;
                 Ciphertext yn;
                 add_any(cx, y3, u, yn);
-                y = std::move(yn);
+                yp[P] = std::move(yn);
             }
-            mul_rescale(cx, *xparts[P], y, outp[P]);
         }
+        if (yp[0].nl < 2) {
+            Ciphertext yc;
+            merge_complex(cx, std::move(yp[0]), std::move(yp[1]), yc);
+            refresh(yc, 1, sd.gy);
+            split_complex(cx, yc, yp[0], yp[1], true);
+        }
+        Ciphertext xgr = mulv(xr, g), xgi = mulv(xi, g);
+        Ciphertext outp[2];
+        Ciphertext* xparts[2] = {&xgr, &xgi};
+        for (int P = 0; P < 2; P++) mul_rescale(cx, *xparts[P], yp[P], outp[P]);
         Ciphertext out;
         merge_complex(cx, std::move(outp[0]), std::move(outp[1]), out);
         return out;
@@ -173,20 +195,25 @@ struct Model {
         const int nL = cfg.n_layer;
         if (!have_state) { s.clear(); up.clear(); s.resize(nL); up.resize(nL); }
         Ciphertext h = ct_copy(cx, emb);
+        // the model runs in the user region of the chain (the top limbs are the bootstrap's)
+        const int utop = cx.L - cx.prm.boot_primes;
+        if (h.nl > utop) align(cx, h, utop, 0);
         for (int l = 0; l < nL; l++) {
             LayerParams& P = L[l];
             if (!P.ready) throw Error("model: layer weights not set", -1);
             // ---- time mix
 #define FHE_PROBE(k, ct) \
-    if (probe == (k) && l == 0) return ct_copy(cx, ct);
+    if (probe % 100 == (k) && l == probe / 100) return ct_copy(cx, ct);
             Ciphertext xn = rmsnorm(h, P.g1, P.tm);
             FHE_PROBE(1, xn)
             Ciphertext u;
             if (cfg.shift_mix) {
                 std::vector<double> om(P.mix.size());
                 for (size_t i = 0; i < om.size(); i++) om[i] = 1.0 - P.mix[i];
+                refresh(xn, 1, P.g_u);
                 Ciphertext a = mulv(xn, P.mix);
                 if (have_state) {
+                    refresh(up[l], 1, P.g_u);
                     Ciphertext b = mulv(up[l], om);
                     u = addc(a, b);
                 } else {
@@ -317,8 +344,8 @@ void model_set_layer(Model& m, int l, const double* win, const double* wout, con
     for (int i = 0; i < 3; i++) P.r[i].assign(fv + (size_t)(4 + i) * dff, fv + (size_t)(5 + i) * dff);
     // seeds: tm (a, b, iters), cm (a, b, iters), then the bootstrap gains
     // tm.x, tm.ms, u, s, g, cm.x, cm.ms, v, f
-    P.tm = {seeds[0], seeds[1], (int)seeds[2], seeds[6], seeds[7]};
-    P.cm = {seeds[3], seeds[4], (int)seeds[5], seeds[11], seeds[12]};
+    P.tm = {seeds[0], seeds[1], (int)seeds[2], seeds[6], seeds[7], seeds[15]};
+    P.cm = {seeds[3], seeds[4], (int)seeds[5], seeds[11], seeds[12], seeds[16]};
     P.g_u = seeds[8]; P.g_s = seeds[9]; P.g_g = seeds[10]; P.g_v = seeds[13]; P.g_f = seeds[14];
     P.ready = true;
 }

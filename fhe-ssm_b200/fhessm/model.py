@@ -164,6 +164,7 @@ def calibrate_seeds(cfg, w, steps=2, lanes=64, seed=7, tol=1e-4):
         a, b = linear_rsqrt_seed(0.8 * m, 1.25 * M)
         seeds[tag] = (a, b, rsqrt_iters_for(a, b, m, M, tol))
         seeds["gain:" + tag + ".ms"] = boot_gain(1.25 * M)
+        seeds["gain:" + tag + ".y"] = boot_gain(1.25 / np.sqrt(0.8 * m))
     return seeds
 
 
@@ -175,12 +176,13 @@ def boot_gain(peak, target=2.0):
 
 
 def layer_seed_array(seeds, i):
-    """The 15 per-layer values of fhe_model_set_layer: Newton seeds of both norms, then the
-    bootstrap gains tm.x, tm.ms, u, s, g, cm.x, cm.ms, v, f."""
+    """The 17 per-layer values of fhe_model_set_layer: Newton seeds of both norms, then the
+    bootstrap gains tm.x, tm.ms, u, s, g, cm.x, cm.ms, v, f, tm.y, cm.y."""
     g = lambda k: seeds.get("gain:" + k, 1.0)
     return np.array(list(seeds[f"L{i}.tm"]) + list(seeds[f"L{i}.cm"]) +
                     [g(f"L{i}.tm.x"), g(f"L{i}.tm.ms"), g(f"L{i}.u"), g(f"L{i}.s"), g(f"L{i}.g"),
-                     g(f"L{i}.cm.x"), g(f"L{i}.cm.ms"), g(f"L{i}.v"), g(f"L{i}.f")], dtype=np.float64)
+                     g(f"L{i}.cm.x"), g(f"L{i}.cm.ms"), g(f"L{i}.v"), g(f"L{i}.f"),
+                     g(f"L{i}.tm.y"), g(f"L{i}.cm.y")], dtype=np.float64)
 
 
 # -------------------------------------------------------------------------- packing ----
@@ -256,7 +258,8 @@ class EncryptedModel:
             _check(h.fhe_model_set_layer(self.h, i, *[p for _, p in keep]))
         g, gp = _dp(w["g_out"])
         so, sop = _dp(np.array(list(seeds["ln_out"]) + [seeds.get("gain:ln_out.x", 1.0),
-                                                         seeds.get("gain:ln_out.ms", 1.0)], dtype=np.float64))
+                                                         seeds.get("gain:ln_out.ms", 1.0),
+                                                         seeds.get("gain:ln_out.y", 1.0)], dtype=np.float64))
         _check(h.fhe_model_set_output(self.h, gp, sop))
 
     def keygen(self):

@@ -179,12 +179,12 @@ int fhe_matvec_bsgs(fhe_ctx* cx, const fhe_mvplan* pl, const fhe_ct* const* in, 
  * :5389) for the polynomial SSM of train_fhe_native_ssm.py (_fwd_np :829-890).  Lanes: one
  * conversation per block of D slots, complex packing (lane r real part, lane r + N/2D
  * imaginary part).  vecs: d-length decay, 1-decay, g1, mix, c, dd, p0, p1, p2, g2 then
- * dff-length q0, q1, q2, q3, r0, r1, r2; seeds (15 values): rmsnorm Newton seeds (a, b, iters)
+ * dff-length q0, q1, q2, q3, r0, r1, r2; seeds (17 values): rmsnorm Newton seeds (a, b, iters)
  * of the time-mix and channel-mix norms (the bundle's L{i}.{tm,cm}.rsqrt,
  * train_fhe_native_ssm.py:1121-1124), then the bootstrap gains of the refresh sites tm.x,
- * tm.ms, u, s, g, cm.x, cm.ms, v, f (a site is refreshed at value * gain: a bootstrap's error
- * is absolute, so small-valued sites are scaled up by relabelling the scale).
- * fhe_model_set_output: seed3 = (a, b, iters, gain x, gain ms) of the output norm. */
+ * tm.ms, u, s, g, cm.x, cm.ms, v, f, tm.y, cm.y (a site is refreshed at value * gain: a
+ * bootstrap's error is absolute, so small-valued sites are scaled up by relabelling the scale).
+ * fhe_model_set_output: seed3 = (a, b, iters, gain x, gain ms, gain y) of the output norm. */
 typedef struct fhe_model fhe_model;
 typedef struct {
     int d, dff, n_layer, D, b1;
