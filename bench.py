@@ -1,18 +1,22 @@
 #!/usr/bin/env python3
 """bench.py -- device-timed throughput of the engine's hot path on 1..8 B200s.
 
-    python bench.py --gpus N --steps K --warmup W [--workload hmult] [--impl reference]
+    python bench.py --gpus N --steps K --warmup W [--workload 405m|hmult] [--impl reference]
 
-One process per GPU (torchrun for N > 1); every rank owns its own batch (conversation
-packs / ciphertext batches shard with no communication: weak scaling).  Rank 0 prints one
-JSON line.  The timed region is bracketed by a barrier and a device synchronise on both
-sides; device time comes from CUDA events recorded on the engine's own stream; the
-reported time is the maximum over ranks.
+One process per GPU (torchrun for N > 1); every rank owns its own pack of 64 conversations
+(packs shard with no communication: weak scaling).  Rank 0 prints one JSON line.  The timed
+region is bracketed by a barrier and a device synchronise on both sides; device time comes
+from CUDA events recorded on the engine's own stream; the reported time is the max over ranks.
 
-Workload "hmult" (config 2 of the baseline, its HMult row): a batch of 64 ciphertext pairs
-at N = 2^16, L = 20 (q0 60-bit + 19 x 45-bit), K = 4 x 60-bit special primes, dnum = 5;
-one step = 64 x (EvalMult ct x ct + relinearise + RescaleInPlace).  The inputs (2.7 GB)
-exceed the 126 MB L2, so no flush is needed between steps.
+Workload "405m" (default; config 4 of the baseline): one encrypted decode pass of the 405M
+polynomial SSM (24 layers, d 1024, dff 4096, 64 diagonal-decay channels per head x 16, tied
+vocabulary 50,304) advancing 64 conversations by one token, with the recurrent state carried
+encrypted and bootstrapped as needed.  Chain: N = 2^16, q0 60 bits, 13 x 45-bit user primes,
+14 x 58-bit bootstrap primes, K = 4 x 60-bit special primes (logQP 1697), HW-192 secret.
+Weights N(0, 0.02), polynomial coefficients U[-1, 1], seeded; tokens uniform, seeded.
+
+Workload "hmult" (config 2, HMult row): 64 ciphertext pairs at N = 2^16, L = 20; one step =
+64 x (EvalMult + relinearise + RescaleInPlace).
 """
 import argparse
 import json
@@ -29,9 +33,12 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "fhe-ssm_b200"))
 sys.path.insert(0, os.path.join(ROOT, "tests"))
 
-CONF = dict(logN=16, L=20, K=4, alpha=4, hw=192)
-BATCH = 64
-METRIC = "HMult+relin+rescale ciphertexts/s aggregate (N=2^16, L=20, batch 64 per GPU)"
+METRIC_405M = "encrypted tokens/s aggregate, 405M poly-SSM, 64 conv/pass, 1/2/4/8 B200"
+METRIC_HMULT = "HMult+relin+rescale ciphertexts/s aggregate (N=2^16, L=20, batch 64 per GPU)"
+MODEL_CTX = dict(logN=16, L=28, K=4, alpha=4, hw=192, boot_primes=14)
+HMULT_CTX = dict(logN=16, L=20, K=4, alpha=4, hw=192)
+LANES = 64
+CENSUS = os.path.join(ROOT, "profiles", "pass_census.json")
 
 
 def peaks():
@@ -92,7 +99,7 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def dist_setup(args):
+def dist_setup():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -102,7 +109,7 @@ def dist_setup(args):
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
     return ws, rank, local
 
@@ -128,104 +135,191 @@ def rand_ct_words(rng, moduli, nl, N):
                      for _ in range(2)])
 
 
+def roofline(prof):
+    """The dominant kernel (by device time) against the measured HBM copy bandwidth."""
+    pk = peaks()
+    if not prof:
+        return None
+    name, (n, tms, tbytes) = max(prof.items(), key=lambda kv: kv[1][1])
+    achieved = tbytes / (tms / 1000.0) / 1e9
+    peak = pk.get("hbm_gbs", 6650.0)
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tf):
+        traffic = json.load(open(tf)).get(name)
+    return {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "traffic": traffic, "launches": n, "avg_launch_us": 1000.0 * tms / n,
+            "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if "hbm_gbs" in pk else "fallback 6650 GB/s"}
+
+
+def kernel_table(prof):
+    return {k: {"launches": v[0], "ms": round(v[1], 3),
+                "GB/s": round(v[2] / (v[1] / 1000.0) / 1e9, 1) if v[1] else None} for k, v in prof.items()}
+
+
 # ------------------------------------------------------------------------ CPU oracle ----
-def oracle_hmult_rate(moduli, key, nthreads, seconds, rng):
-    """HMult+relin+rescale of the CPU oracle (single-threaded C) on `nthreads` host threads
-    (ctypes releases the GIL), ciphertexts/s over a bounded sample."""
+def oracle_keyswitch_seconds(nl_avg, nthreads, seconds):
+    """Seconds per hybrid key switch of the C oracle at N = 2^16 and the pass's average limb
+    count, on `nthreads` host threads in parallel (ctypes releases the GIL): returns
+    (seconds per key switch per thread-parallel throughput, samples)."""
     from concurrent.futures import ThreadPoolExecutor
 
-    from oracle_lib import Oracle, load
-    L, K, N = CONF["L"], CONF["K"], 1 << CONF["logN"]
-    o = Oracle(CONF["logN"], moduli[:L], moduli[L:], CONF["alpha"], load())
-    a = rand_ct_words(rng, moduli, L, N)
-    b = rand_ct_words(rng, moduli, L, N)
+    from oracle_lib import Oracle, derive_seed, gen_chain, load
+    lib = load()
+    L, K, logN = 16, 4, 16
+    q, p = gen_chain(logN, L, 60, 45, K, 60, lib)
+    o = Oracle(logN, q, p, 4, lib)
+    ms = (1).to_bytes(8, "little") + bytes(24)
+    s = o.secret(derive_seed(lib, ms, 0xFFFFFFF1), 192)
+    se = o.secret_eval(s)
+    key = o.keygen_switch(se, se, derive_seed(lib, ms, 3))
+    nl = max(2, min(L, int(round(nl_avg))))
+    rng = np.random.default_rng(5)
+    d = np.stack([rng.integers(0, int(o.mods[i]), o.N, dtype=np.uint64) for i in range(nl)])
 
     def one(_):
-        o.ct_rescale(o.ct_mul_relin(a, b, L, key), L)
+        o.keyswitch(d, nl, key)
         return 1
 
     done, t0 = 0, time.time()
     with ThreadPoolExecutor(nthreads) as ex:
         while time.time() - t0 < seconds or done == 0:
             done += sum(ex.map(one, range(nthreads)))
-    return done / (time.time() - t0), done
+    return (time.time() - t0) / done, done, nl
 
 
-# ------------------------------------------------------------------------------ main ----
-def run_reference(args):
-    ws, rank, local = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0
-    if rank != 0:
-        return 0
-    rng = np.random.default_rng(7)
-    # the chain and key words come from the same deterministic generator the engine uses;
-    # generated on the CPU by the oracle so the reference arm needs no GPU
-    from oracle_lib import Oracle, derive_seed, gen_chain, load
-    lib = load()
-    q, p = gen_chain(CONF["logN"], CONF["L"], 60, 45, CONF["K"], 60, lib)
-    moduli = np.concatenate([q, p])
-    o = Oracle(CONF["logN"], q, p, CONF["alpha"], lib)
-    ms = (1).to_bytes(8, "little") + bytes(24)
-    s = o.secret(derive_seed(lib, ms, 0xFFFFFFF1), CONF["hw"])
-    se = o.secret_eval(s)
-    s2 = np.stack([(se[m].astype(object) ** 2 % int(o.mods[m])).astype(np.uint64) for m in range(len(o.mods))])
-    key = o.keygen_switch(s2, se, derive_seed(lib, ms, 2))
-    nthreads = os.cpu_count() or 1
-    rates = []
-    for i in range(args.warmup + args.steps):
-        r, n = oracle_hmult_rate(moduli, key, nthreads, 1.0, rng)
-        if i >= args.warmup:
-            rates.append(r)
-    value = statistics.mean(rates)
-    line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "ciphertexts/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-        "ms_per_step": 1000.0 * BATCH * args.gpus / value, "dtype": "u64 (RNS residues)", "data": "synthetic",
-        "config": {"workload": "config 2: HMult+relin+rescale, N=2^16, L=20, K=4, dnum=5", "batch": BATCH},
-        "cpu_baseline": {"value": value, "unit": "ciphertexts/s", "cores": nthreads, "kind": "port",
-                         "sample": f"{nthreads} ciphertexts per step on {nthreads} threads of the C oracle "
-                                   "(OpenFHE, the reference's arithmetic library, is not installable here)"},
-        "e2e": {"value": value, "unit": "ciphertexts/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
-    return 0
+def census():
+    try:
+        return json.load(open(CENSUS))
+    except Exception:
+        return None
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
-    ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
-    ap.add_argument("--workload", default="hmult", choices=["hmult"])
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--batch", type=int, default=64, help="ciphertexts per GPU per step (smaller for ncu captures)")
-    args = ap.parse_args()
-    global BATCH
-    BATCH = args.batch
-    if args.impl == "reference":
-        return run_reference(args)
-    ws, rank, local = dist_setup(args)
+# ------------------------------------------------------------------------ workloads ----
+def run_model(args, ws, rank, local):
     import torch
 
     import fhessm
-    torch.cuda.set_device(local)
-    cx = fhessm.CryptoContext(device=local, **CONF)
+    from fhessm.model import (CONFIG_405M, EncryptedModel, calibrate_seeds, pack_lanes, plain_step, rel_err_rms,
+                              synthetic_weights)
+    cfg = CONFIG_405M
+    t_setup = time.time()
+    w = synthetic_weights(cfg, seed=1234)
+    seeds = calibrate_seeds(cfg, w, steps=6, lanes=LANES)
+    cx = fhessm.CryptoContext(device=local, **MODEL_CTX)
     cx.KeyGen(seed=1 + rank)
-    L, N = CONF["L"], 1 << CONF["logN"]
+    cx.EvalBootstrapSetup(24.0, 59)
+    m = EncryptedModel(cx, cfg, w, seeds)
+    m.keygen()
+    in_level = MODEL_CTX["boot_primes"]   # the top of the user region
     rng = np.random.default_rng(100 + rank)
-    host_a = [rand_ct_words(rng, cx.moduli, L, N) for _ in range(BATCH)]
-    host_b = [rand_ct_words(rng, cx.moduli, L, N) for _ in range(BATCH)]
-    A = [cx.ct_from_words(w, 0) for w in host_a]
-    B = [cx.ct_from_words(w, 0) for w in host_b]
+    nsteps = args.warmup + args.steps
+    toks = [rng.integers(0, cfg.vocab, LANES) for _ in range(nsteps + 1)]
+    cts = [cx.Encrypt(cx.MakeCKKSPackedPlaintext(pack_lanes(w["emb"][t], cfg.D, cx.slots), level=in_level))
+           for t in toks]
+    cx.sync()
+    setup_s = time.time() - t_setup
+    stream = torch.cuda.ExternalStream(cx.stream_ptr(), device=local)
+    outs = []
+    for i in range(args.warmup):
+        outs.append(m.step(cts[i]))
+    cx.sync()
+    barrier(ws)
+    clk = ClockSampler(local)
+    clk.start()
+    l0 = cx.launches()
+    k0 = cx.counters()
+    b0 = m.stats()["bootstraps"]
+    cx.profile(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(ws)
+    e0.record(stream)
+    for i in range(args.warmup, nsteps):
+        outs.append(m.step(cts[i]))
+    e1.record(stream)
+    cx.sync()
+    torch.cuda.synchronize()
+    barrier(ws)
+    clocks = clk.stop()
+    ms = e0.elapsed_time(e1)
+    prof = cx.profile_collect()
+    cx.profile(False)
+    launches = cx.launches() - l0
+    k1 = cx.counters()
+    boots = (m.stats()["bootstraps"] - b0) / args.steps
+    ks_per_pass = (k1[0] - k0[0]) / args.steps
+    ks_nl_avg = (k1[1] - k0[1]) / max(1, k1[0] - k0[0])
+    ms_max = max_over_ranks(ms, ws)
+    value = LANES * ws * args.steps / (ms_max / 1000.0)
+
+    # fidelity against the float64 model (exact 1/sqrt), replaying every step from a cold state
+    state, errs, top1 = None, [], []
+    for i in range(nsteps):
+        ref, state = plain_step(cfg, w, w["emb"][toks[i]], state)
+        if i >= args.warmup:
+            y = fhessm.model.unpack_lanes(cx.Decrypt(outs[i]), cfg.D, LANES, cfg.d)
+            lg, lr = y @ w["emb"].T, ref @ w["emb"].T
+            errs.append(rel_err_rms(lg, lr))
+            top1.append(float(np.mean(lg.argmax(-1) == lr.argmax(-1))))
+
+    # end to end through the public API: host words in (H2D), one pass, host words out (D2H)
+    words_in = cts[nsteps].words()
+    barrier(ws)
+    t0 = time.time()
+    ct_in = cx.ct_from_words(words_in, in_level, cts[nsteps].scale)
+    out = m.step(ct_in)
+    words_out = out.words()
+    cx.sync()
+    e2e_s = max_over_ranks(time.time() - t0, ws)
+    e2e = {"value": LANES * ws / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(words_in.nbytes),
+           "d2h_bytes_per_step": int(words_out.nbytes)}
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        t_ks, n, nl = oracle_keyswitch_seconds(ks_nl_avg, 1, 10.0)
+        cpu = {"value": LANES / (ks_per_pass * t_ks), "unit": "tokens/s", "cores": 1, "kind": "port",
+               "sample": f"{n} hybrid key switches of the C oracle at N=2^16, {nl} limbs (the pass's average), "
+                         f"single thread, scaled by the pass's {ks_per_pass:.0f} key switches (a lower bound on "
+                         f"the CPU pass time: all other work of the pass is excluded)"}
+        os.makedirs(os.path.dirname(CENSUS), exist_ok=True)
+        json.dump({"keyswitches_per_pass": ks_per_pass, "ks_avg_limbs": ks_nl_avg, "bootstraps_per_pass": boots,
+                   "kernel_launches_per_pass": launches / args.steps, "config": "405m"}, open(CENSUS, "w"), indent=1)
+    if rank == 0:
+        line = {
+            "metric": METRIC_405M, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u64 (RNS residues, CKKS)", "data": "synthetic (seeded weights and tokens)",
+            "config": {"workload": "config 4: 405M poly-SSM, one encrypted decode pass, 64 conversations per GPU",
+                       "layers": cfg.n_layer, "d_model": cfg.d, "d_ffn": cfg.dff, "vocab": cfg.vocab,
+                       "ring": "N=2^16, L=28 (60 + 13x45 + 14x58), K=4x60, HW 192", "global_batch": LANES * ws,
+                       "parallelism": f"dp{ws} (independent packs)", "l2": "working set >> L2 (keys 39 GB)"},
+            "fidelity": {"logits_relErrRms_max": max(errs), "top1_min": min(top1), "vs": "float64 model, exact 1/sqrt"},
+            "bootstraps_per_pass": boots, "keyswitches_per_pass": ks_per_pass, "setup_s": setup_s,
+            "gpu_launches": launches, "clocks": clocks, "e2e": e2e, "roofline": roofline(prof), "cpu_baseline": cpu,
+            "kernels": kernel_table(prof),
+        }
+        print(json.dumps(line), flush=True)
+
+
+def run_hmult(args, ws, rank, local):
+    import torch
+
+    import fhessm
+    cx = fhessm.CryptoContext(device=local, **HMULT_CTX)
+    cx.KeyGen(seed=1 + rank)
+    L, N = HMULT_CTX["L"], 1 << HMULT_CTX["logN"]
+    rng = np.random.default_rng(100 + rank)
+    B = args.batch
+    host_a = [rand_ct_words(rng, cx.moduli, L, N) for _ in range(B)]
+    host_b = [rand_ct_words(rng, cx.moduli, L, N) for _ in range(B)]
+    A = [cx.ct_from_words(x, 0) for x in host_a]
+    Bc = [cx.ct_from_words(x, 0) for x in host_b]
     stream = torch.cuda.ExternalStream(cx.stream_ptr(), device=local)
 
     def step():
-        outs = []
-        for a, b in zip(A, B):
+        for a, b in zip(A, Bc):
             c = cx.EvalMult(a, b)
             cx.RescaleInPlace(c)
-            outs.append(c)
-        return outs
 
     for _ in range(args.warmup):
         step()
@@ -236,7 +330,6 @@ def main():
     l0 = cx.launches()
     cx.profile(True)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    cx.sync()
     barrier(ws)
     e0.record(stream)
     for _ in range(args.steps):
@@ -251,58 +344,85 @@ def main():
     cx.profile(False)
     launches = cx.launches() - l0
     ms_max = max_over_ranks(ms, ws)
-    value = BATCH * ws * args.steps / (ms_max / 1000.0)
-
-    # ---- end to end through the C-ABI with host buffers (import -> compute -> export)
+    value = B * ws * args.steps / (ms_max / 1000.0)
     out_words = np.empty((2, L - 1, N), dtype=np.uint64)
     barrier(ws)
     t0 = time.time()
-    for _ in range(max(1, args.steps // 2)):
-        for wa, wb in zip(host_a, host_b):
-            a, b = cx.ct_from_words(wa, 0), cx.ct_from_words(wb, 0)
-            c = cx.EvalMult(a, b)
-            cx.RescaleInPlace(c)
-            out_words[...] = c.words()
+    for wa, wb in zip(host_a, host_b):
+        a, b = cx.ct_from_words(wa, 0), cx.ct_from_words(wb, 0)
+        c = cx.EvalMult(a, b)
+        cx.RescaleInPlace(c)
+        out_words[...] = c.words()
     cx.sync()
-    barrier(ws)
-    e2e_s = max_over_ranks((time.time() - t0) / max(1, args.steps // 2), ws)
-    e2e = {"value": BATCH * ws / e2e_s, "unit": "ciphertexts/s",
-           "h2d_bytes_per_step": int(2 * BATCH * host_a[0].nbytes),
-           "d2h_bytes_per_step": int(BATCH * out_words.nbytes)}
-
-    # ---- roofline of the dominant kernel (by device time)
-    pk = peaks()
-    top = max(prof.items(), key=lambda kv: kv[1][1]) if prof else None
-    roof = None
-    if top:
-        name, (nl_, tms, tbytes) = top
-        achieved = tbytes / (tms / 1000.0) / 1e9
-        peak = pk.get("hbm_gbs", 6650.0)
-        traffic = None
-        tf = os.path.join(ROOT, "profiles", "traffic.json")
-        if os.path.exists(tf):
-            traffic = json.load(open(tf)).get(name)
-        roof = {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                "frac": achieved / peak, "traffic": traffic, "launches": nl_, "avg_launch_us": 1000.0 * tms / nl_,
-                "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if "hbm_gbs" in pk else "fallback 6650"}
-    cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
-        r, n = oracle_hmult_rate(cx.moduli, cx.key_words(0), 1, 10.0, rng)
-        cpu = {"value": r, "unit": "ciphertexts/s", "cores": 1, "kind": "port",
-               "sample": f"{n} HMult+relin+rescale of the C oracle, single thread, same shape"}
+    e2e_s = max_over_ranks(time.time() - t0, ws)
+    e2e = {"value": B * ws / e2e_s, "unit": "ciphertexts/s", "h2d_bytes_per_step": int(2 * B * host_a[0].nbytes),
+           "d2h_bytes_per_step": int(B * out_words.nbytes)}
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "ciphertexts/s", "n_gpus": ws, "steps": args.steps,
+            "metric": METRIC_HMULT, "value": value, "unit": "ciphertexts/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "u64 (RNS residues)", "data": "synthetic",
-            "config": {"workload": "config 2: HMult+relin+rescale, N=2^16, L=20 (q0 60b + 19x45b), K=4x60b, dnum=5",
-                       "batch_per_gpu": BATCH, "parallelism": f"dp{ws} (independent batches)",
-                       "l2": "inputs 2.7 GB per GPU > L2, no flush"},
-            "gpu_launches": launches, "clocks": clocks, "e2e": e2e, "roofline": roof, "cpu_baseline": cpu,
-            "kernels": {k: {"launches": v[0], "ms": v[1], "GB/s": v[2] / (v[1] / 1000.0) / 1e9 if v[1] else None}
-                        for k, v in prof.items()},
+            "config": {"workload": "config 2: HMult+relin+rescale, N=2^16, L=20, K=4x60b, dnum=5",
+                       "batch_per_gpu": B, "parallelism": f"dp{ws}", "l2": "inputs 2.7 GB per GPU > L2"},
+            "gpu_launches": launches, "clocks": clocks, "e2e": e2e, "roofline": roofline(prof), "cpu_baseline": None,
+            "kernels": kernel_table(prof),
         }
         print(json.dumps(line), flush=True)
+
+
+def run_reference(args):
+    """The reference arm: the CPU path of the same workload on the host cores.  OpenFHE (the
+    reference's arithmetic library) cannot be built here, so the C oracle (a restatement of the
+    same RNS-CKKS algorithms) stands in; the pass time is the pass's key-switch census times the
+    oracle's key-switch time on all host threads (a lower bound: everything else is excluded)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    cen = census()
+    nthreads = os.cpu_count() or 1
+    if args.workload == "405m":
+        if not cen:
+            print(json.dumps({"impl": "reference", "unavailable": "no key-switch census (profiles/pass_census.json)"}))
+            return 0
+        vals = []
+        for i in range(args.warmup + args.steps):
+            t_ks, n, nl = oracle_keyswitch_seconds(cen["ks_avg_limbs"], nthreads, 2.0)
+            if i >= args.warmup:
+                vals.append(LANES / (cen["keyswitches_per_pass"] * t_ks))
+        value = statistics.mean(vals)
+        line = {"impl": "reference", "metric": METRIC_405M, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                "ms_per_step": 1000.0 * LANES / value, "dtype": "u64 (RNS residues, CKKS)", "data": "synthetic",
+                "config": {"workload": "config 4: 405M poly-SSM, one encrypted decode pass, 64 conversations"},
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": nthreads, "kind": "port",
+                                 "sample": f"C oracle key switches at {nl} limbs on {nthreads} threads, scaled by "
+                                           f"{cen['keyswitches_per_pass']:.0f} key switches per pass"},
+                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+    print(json.dumps({"impl": "reference", "unavailable": "reference arm implemented for the 405m workload only"}))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
+    ap.add_argument("--workload", default="405m", choices=["405m", "hmult"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=64, help="hmult: ciphertext pairs per GPU per step")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    ws, rank, local = dist_setup()
+    import torch
+    torch.cuda.set_device(local)
+    if args.workload == "405m":
+        run_model(args, ws, rank, local)
+    else:
+        run_hmult(args, ws, rank, local)
     if ws > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

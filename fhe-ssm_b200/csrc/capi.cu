@@ -91,6 +91,13 @@ int fhe_ctx_sync(fhe_ctx* cx) {
 }
 long long fhe_ctx_launches(const fhe_ctx* cx) { return cx ? cx->cx.launches : 0; }
 void* fhe_ctx_stream(const fhe_ctx* cx) { return cx ? (void*)cx->cx.stream : nullptr; }
+int fhe_ctx_counters(const fhe_ctx* cx, long long* keyswitches, long long* ks_limbs) {
+    return guard([&] {
+        REQUIRE(cx, "null argument");
+        if (keyswitches) *keyswitches = cx->cx.ks_count;
+        if (ks_limbs) *ks_limbs = cx->cx.ks_limbs;
+    });
+}
 int fhe_prof_enable(fhe_ctx* cx, int on) {
     return guard([&] {
         REQUIRE(cx, "null argument");

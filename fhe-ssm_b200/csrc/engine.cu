@@ -356,6 +356,8 @@ static void inner_moddown(Context& cx, const DevBuf& ext, int nl, const SwitchKe
                           const uint64_t* add1, uint64_t* out0, uint64_t* out1, uint64_t perm_k) {
     const int N = cx.N, K = cx.K, ne = nl + K, dn = cx.dnum(nl);
     cudaStream_t st = cx.stream;
+    cx.ks_count++;
+    cx.ks_limbs += nl;
     DevBuf ip((size_t)2 * ne * N, st);
     {
         ProfScope ps(cx, "key_inner", 8.0 * N * ((double)dn * ne * 3 + 2 * ne));

@@ -127,6 +127,7 @@ struct Context {
     uint8_t master[32] = {0};
     uint32_t enc_counter = 0;
     mutable long long launches = 0;  // kernel launches issued (for the launch count claim)
+    long long ks_count = 0, ks_limbs = 0;   // key switches issued and the sum of their limb counts
     // optional per-kernel CUDA-event timing (bench roofline): name -> pending event pairs
     struct ProfEntry {
         std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pending;

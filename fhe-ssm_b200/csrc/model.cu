@@ -49,7 +49,7 @@ struct LayerParams {
     // channel-mix input, channel-mix products): a bootstrap's error is absolute, so a site
     // whose values are small is refreshed at value * gain (a relabelling of the scale,
     // exact) and relabelled back
-    double g_u = 1, g_s = 1, g_g = 1, g_v = 1, g_f = 1;
+    double g_u = 1, g_s = 1, g_g = 1, g_v = 1, g_f = 1, g_z = 1;
     bool ready = false;
 };
 
@@ -240,10 +240,14 @@ struct Model {
             } else {
                 snew = std::move(bx);
             }
+            // the carried state loses a level per step: refresh it (and keep the refreshed copy
+            // as the carry) when the readout z could not cover the gate polynomial
+            refresh(snew, 5, P.g_s);
             s[l] = ct_copy(cx, snew);
             FHE_PROBE(4, snew)
             Ciphertext cs = mulv(snew, P.c), dx = mulv(x, P.dd);
             Ciphertext z = addc(cs, dx);
+            refresh(z, 4, P.g_z);
             FHE_PROBE(5, z)
             std::vector<double> zero(cfg.d, 0.0);
             Ciphertext g = poly_complex(z, {&zero, &P.p0, &P.p1, &P.p2});
@@ -347,6 +351,7 @@ void model_set_layer(Model& m, int l, const double* win, const double* wout, con
     P.tm = {seeds[0], seeds[1], (int)seeds[2], seeds[6], seeds[7], seeds[15]};
     P.cm = {seeds[3], seeds[4], (int)seeds[5], seeds[11], seeds[12], seeds[16]};
     P.g_u = seeds[8]; P.g_s = seeds[9]; P.g_g = seeds[10]; P.g_v = seeds[13]; P.g_f = seeds[14];
+    P.g_z = seeds[17];
     P.ready = true;
 }
 

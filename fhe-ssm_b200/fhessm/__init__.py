@@ -217,6 +217,15 @@ class CryptoContext:
     def rot_index(self, k):
         return lib().fhe_rot_index(self.h, k)
 
+    def counters(self):
+        """(key switches issued, sum of their limb counts) since the context was created."""
+        h = lib()
+        h.fhe_ctx_counters.restype = C.c_int
+        h.fhe_ctx_counters.argtypes = [_VP, C.POINTER(C.c_longlong), C.POINTER(C.c_longlong)]
+        k, l = C.c_longlong(), C.c_longlong()
+        _check(h.fhe_ctx_counters(self.h, C.byref(k), C.byref(l)))
+        return k.value, l.value
+
     def stream_ptr(self):
         """The engine's cudaStream_t (an int), e.g. for torch.cuda.ExternalStream."""
         return lib().fhe_ctx_stream(self.h)

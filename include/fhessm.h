@@ -69,6 +69,8 @@ double fhe_ctx_scale(const fhe_ctx* cx, int level);
 int fhe_ctx_sync(fhe_ctx* cx);
 /* kernel launches issued by this context so far */
 long long fhe_ctx_launches(const fhe_ctx* cx);
+/* key switches issued so far and the sum of their limb counts (operation census) */
+int fhe_ctx_counters(const fhe_ctx* cx, long long* keyswitches, long long* ks_limbs);
 /* the context's CUDA stream (cudaStream_t), for callers that time it with CUDA events */
 void* fhe_ctx_stream(const fhe_ctx* cx);
 /* per-kernel CUDA-event timing on the context's stream (off by default).  collect
@@ -179,10 +181,10 @@ int fhe_matvec_bsgs(fhe_ctx* cx, const fhe_mvplan* pl, const fhe_ct* const* in, 
  * :5389) for the polynomial SSM of train_fhe_native_ssm.py (_fwd_np :829-890).  Lanes: one
  * conversation per block of D slots, complex packing (lane r real part, lane r + N/2D
  * imaginary part).  vecs: d-length decay, 1-decay, g1, mix, c, dd, p0, p1, p2, g2 then
- * dff-length q0, q1, q2, q3, r0, r1, r2; seeds (17 values): rmsnorm Newton seeds (a, b, iters)
+ * dff-length q0, q1, q2, q3, r0, r1, r2; seeds (18 values): rmsnorm Newton seeds (a, b, iters)
  * of the time-mix and channel-mix norms (the bundle's L{i}.{tm,cm}.rsqrt,
  * train_fhe_native_ssm.py:1121-1124), then the bootstrap gains of the refresh sites tm.x,
- * tm.ms, u, s, g, cm.x, cm.ms, v, f, tm.y, cm.y (a site is refreshed at value * gain: a
+ * tm.ms, u, s, g, cm.x, cm.ms, v, f, tm.y, cm.y, z (a site is refreshed at value * gain: a
  * bootstrap's error is absolute, so small-valued sites are scaled up by relabelling the scale).
  * fhe_model_set_output: seed3 = (a, b, iters, gain x, gain ms, gain y) of the output norm. */
 typedef struct fhe_model fhe_model;
