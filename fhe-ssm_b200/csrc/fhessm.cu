@@ -8,3 +8,4 @@
 #include "matvec.cu"
 #include "model.cu"
 #include "capi.cu"
+#include "noalloc.cu"

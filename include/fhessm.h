@@ -226,6 +226,23 @@ int fhe_ntt_host(fhe_ctx* cx, uint64_t* words, int n, const int* mod_idx, int in
 int fhe_keyswitch_host(fhe_ctx* cx, const uint64_t* d, int level, const uint64_t* key, uint64_t* out0,
                        uint64_t* out1);
 
+/* ---- key switching without device allocation -------------------------------------------
+ * No counterpart in the reference (its key switch allocates through OpenFHE / FIDESlib).
+ * For callers that must not allocate device memory during a pass: a server that has given
+ * nearly all HBM to long-lived arenas (resident conversations' state, keys, plaintexts), or a
+ * host runtime whose own pool owns the device.  Key-switches d (device memory, limbs =
+ * L - level, eval form) with the context's resident key `which` (0 = relinearisation, else
+ * an automorphism index from fhe_rot_index) into out0, out1 (device memory, same limbs);
+ * enqueued on the context's stream (fhe_ctx_stream), results bit-identical to
+ * fhe_keyswitch_host.  Working memory is a static 64 MiB device array per GPU
+ * (FHE_NOALLOC_SCRATCH_MIB): at N = 2^16, K = 4, alpha = 4 at most 16 limbs; larger requests
+ * return FHE_ERR_ARG.  Overlapping calls on one GPU (different contexts or threads) race on
+ * that array.  The first call on a GPU does the set-up; make it before any stream capture.
+ * Per-kernel profiling must be off. */
+#define FHE_NOALLOC_SCRATCH_MIB 64
+int fhe_keyswitch_noalloc(fhe_ctx* cx, uint64_t which, const uint64_t* d, int level, uint64_t* out0,
+                          uint64_t* out1);
+
 #ifdef __cplusplus
 }
 #endif
