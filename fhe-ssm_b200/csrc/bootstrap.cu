@@ -189,8 +189,11 @@ static void eval_level(Context& cx, const BootLevel& L, const Ciphertext& v, Cip
         ct_rotate_hoisted(cx, v, steps.data(), (int)steps.size(), rs.data());
         for (size_t i = 0; i < rs.size(); i++) baby[i + 1] = std::move(rs[i]);
     }
-    Ciphertext acc;
-    bool have = false;
+    // giant g: inner_g = sum_j pt_gj . baby_j, then sum_g rot(inner_g, g b1 base) in one rotate_sum
+    std::vector<Ciphertext> inners;
+    std::vector<int> gsteps;
+    const Ciphertext* g0 = nullptr;
+    inners.reserve(L.gs.size());
     for (int g : L.gs) {
         Ciphertext inner;
         bool hi = false;
@@ -203,14 +206,17 @@ static void eval_level(Context& cx, const BootLevel& L, const Ciphertext& v, Cip
             else { Ciphertext u; ct_add(cx, inner, t, u); inner = std::move(u); }
         }
         if (!hi) continue;
-        if (g != 0) {
-            Ciphertext r;
-            ct_rotate(cx, inner, g * L.b1 * L.base, r);
-            inner = std::move(r);
-        }
-        if (!have) { acc = std::move(inner); have = true; }
-        else { Ciphertext u; ct_add(cx, acc, inner, u); acc = std::move(u); }
+        inners.push_back(std::move(inner));
+        if (g == 0) g0 = &inners.back();
+        else gsteps.push_back(g * L.b1 * L.base);
     }
+    if (inners.empty()) throw Error("bootstrap: empty linear-transform level", -1);
+    std::vector<const uint64_t*> c0s, c1s;
+    for (auto& c : inners)
+        if (&c != g0) { c0s.push_back(c.c(0)); c1s.push_back(c.c(1)); }
+    Ciphertext acc;
+    rotate_sum(cx, c0s.data(), c1s.data(), gsteps.data(), (int)gsteps.size(), v.nl, inners[0].scale,
+               g0 ? g0->c(0) : nullptr, g0 ? g0->c(1) : nullptr, acc);
     ct_rescale(cx, acc);
     acc.scale = L.s_out;
     out = std::move(acc);

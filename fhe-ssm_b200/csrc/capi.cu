@@ -2,6 +2,7 @@
 //
 // Every entry point catches the engine's exceptions and turns them into a status code plus
 // a thread-local message; no C++ exception crosses the boundary.
+#include <cmath>
 #include <cstring>
 #include <string>
 
@@ -337,6 +338,35 @@ int fhe_rotate_hoisted(fhe_ctx* cx, const fhe_ct* a, const int32_t* ks, int n, f
         std::vector<int> v(ks, ks + n);
         fhe::ct_rotate_hoisted(cx->cx, a->c, v.data(), n, r.data());
         for (int i = 0; i < n; i++) outs[i] = wrap(cx, std::move(r[i]));
+    });
+}
+int fhe_rotate_sum(fhe_ctx* cx, const fhe_ct* const* in, const int32_t* ks, int n, fhe_ct** out) {
+    return guard([&] {
+        REQUIRE(cx && in && ks && out && n > 0, "null argument");
+        bind(cx);
+        auto& c = cx->cx;
+        const int nl = in[0]->c.nl;
+        const double sc = in[0]->c.scale;
+        std::vector<const uint64_t*> c0s, c1s;
+        std::vector<int> steps;
+        const fhe::Ciphertext* extra = nullptr;
+        for (int i = 0; i < n; i++) {
+            REQUIRE(in[i], "null argument");
+            if (in[i]->c.nl != nl || std::fabs(in[i]->c.scale / sc - 1) > 1e-9)
+                throw fhe::Error("rotate_sum: inputs differ in level or scale", FHE_ERR_LEVEL);
+            if (fhe::rot_index(c, ks[i]) == 1) {
+                REQUIRE(!extra, "rotate_sum: at most one zero rotation");
+                extra = &in[i]->c;
+                continue;
+            }
+            c0s.push_back(in[i]->c.c(0));
+            c1s.push_back(in[i]->c.c(1));
+            steps.push_back(ks[i]);
+        }
+        fhe::Ciphertext r;
+        fhe::rotate_sum(c, c0s.data(), c1s.data(), steps.data(), (int)steps.size(), nl, sc,
+                        extra ? extra->c(0) : nullptr, extra ? extra->c(1) : nullptr, r);
+        *out = wrap(cx, std::move(r));
     });
 }
 int fhe_conjugate(fhe_ctx* cx, const fhe_ct* a, fhe_ct** out) {

@@ -18,9 +18,11 @@
 namespace fhe {
 
 // kernels.cu
-__global__ void k_modup_bconv(const uint64_t*, const uint64_t*, uint64_t*, const uint64_t*, int, int, int, int, int);
+__global__ void k_modup_bconv(const uint64_t*, const uint64_t*, uint64_t*, const uint64_t*, int, int, int, int, int,
+                              long long, long long, long long);
 __global__ void k_key_inner(const uint64_t*, const uint64_t*, uint64_t*, int, int, int, int, int, int);
-__global__ void k_moddown_bconv(const uint64_t*, uint64_t*, const uint64_t*, int, int, int, int, int);
+__global__ void k_moddown_bconv(const uint64_t*, uint64_t*, const uint64_t*, int, int, int, int, int, long long,
+                                long long);
 __global__ void k_moddown_final(const uint64_t*, const uint64_t*, const uint64_t*, const uint64_t*, uint64_t*,
                                 uint64_t*, const uint64_t*, int, int, int, int, int, uint64_t);
 __global__ void k_rescale_lift(const uint64_t*, uint64_t*, int, int, int);
@@ -169,6 +171,14 @@ Context::Context(const Params& p) : prm(p) {
     dnum_top = dnum(L);
     CUDA_CHECK(cudaSetDevice(device));
     CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    {
+        // keep freed transient buffers in the stream-ordered pool across synchronisations
+        // (the default threshold of 0 returns them to the driver at every sync)
+        cudaMemPool_t pool;
+        CUDA_CHECK(cudaDeviceGetDefaultMemPool(&pool, device));
+        uint64_t keep = UINT64_MAX;
+        CUDA_CHECK(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+    }
     gen_chain(logN, L, p.q0bits, p.qbits, K, p.pbits, p.boot_primes, p.boot_bits, mods);
     const int nm = L + K;
     mc.resize(nm);
@@ -319,7 +329,7 @@ static void moddown(Context& cx, uint64_t* ip, int nl, const uint64_t* add0, con
     DevBuf y((size_t)2 * nl * N, st);
     {
         ProfScope ps(cx, "moddown_bconv", 8.0 * N * (2 * K + 2 * nl));
-        k_moddown_bconv<<<g2(cx, 2), 256, 0, st>>>(ip, y.p, cx.d_md, nl, ne, L, K, cx.logN);
+        k_moddown_bconv<<<g2(cx, 2), 256, 0, st>>>(ip, y.p, cx.d_md, nl, ne, L, K, cx.logN, 0, 0);
     }
     ntt(cx, cx.qmap(y.p, nl, (long long)nl * N), 2, false, st);
     {
@@ -342,7 +352,7 @@ static DevBuf modup(Context& cx, const uint64_t* d, int nl) {
     {
         ProfScope ps(cx, "modup_bconv", 8.0 * N * (2 * nl + (double)dn * ne));
         k_modup_bconv<<<g2(cx, dn), 256, 0, st>>>(dc.p, d, ext.p, cx.modup_table(nl), nl, ne, cx.alpha, cx.L,
-                                                  cx.logN);
+                                                  cx.logN, 0, 0, 0);
     }
     LimbMap em = cx.extmap(ext.p, nl, (long long)ne * N);
     em.skip_alpha = cx.alpha;
@@ -511,19 +521,7 @@ void ct_rotate(Context& cx, const Ciphertext& a, int r, Ciphertext& out) {
 }
 void ct_conjugate(Context& cx, const Ciphertext& a, Ciphertext& out) { ct_automorph(cx, a, 2ull * cx.N - 1, out); }
 
-void ct_rotate_hoisted(Context& cx, const Ciphertext& a, const int* rs, int n, Ciphertext* outs) {
-    DevBuf ext = modup(cx, a.c(1), a.nl);
-    for (int i = 0; i < n; i++) {
-        const uint64_t k = rot_index(cx, rs[i]);
-        if (k == 1) { outs[i] = ct_copy(cx, a); continue; }
-        auto it = cx.rot_keys.find(k);
-        if (it == cx.rot_keys.end()) throw Error("rotate_hoisted: no key for step " + std::to_string(rs[i]), -5);
-        Ciphertext t = ct_alloc(cx, a.nl);
-        inner_moddown(cx, ext, a.nl, *it->second, a.c(0), nullptr, t.c(0), t.c(1), k);
-        t.scale = a.scale;
-        outs[i] = std::move(t);
-    }
-}
+// ct_rotate_hoisted: ksbatch.cu
 
 // per-limb constant (v mod q_i) with shoup, uploaded to a small device buffer
 static DevBuf limb_consts(Context& cx, const std::vector<uint64_t>& v, bool with_shoup) {

@@ -47,8 +47,9 @@ struct LimbMap {
     uint64_t* base;
     long long poly_stride;   // words between consecutive polynomials
     int nl;                  // limbs per polynomial
-    int skip_alpha;          // >0: skip limbs [poly*alpha, min(poly*alpha+alpha, skip_nq)) (ModUp own digit)
-    int skip_nq;
+    int skip_alpha;          // >0: skip limbs [dg*alpha, min(dg*alpha+alpha, skip_nq)) (ModUp own digit),
+    int skip_nq;             //     dg = poly, or poly % skip_period for a batch of ModUp outputs
+    int skip_period;
     // modulus index of limb l: l < split ? l + off0 : l - split + off1
     int split, off0, off1;
     __host__ __device__ int mod(int l) const { return l < split ? l + off0 : l - split + off1; }
@@ -101,6 +102,8 @@ struct Plaintext {
 struct SwitchKey {
     DevBuf buf;            // [dnum_top][2][L+K][N], Montgomery form
     uint64_t index = 0;    // automorphism index (0 for relinearisation)
+    DevBuf fwd;            // rotation keys: the same key with the automorphism applied (the key
+                           // of the rotate-then-switch order), built on first use by rotate_sum
 };
 
 // ---- context ----------------------------------------------------------------------------
@@ -206,6 +209,11 @@ void ct_mul_relin(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphert
 void ct_rescale(Context& cx, Ciphertext& a);
 void ct_level_drop(Context& cx, Ciphertext& a, int nl_target);   // drop limbs, no scaling
 void ct_automorph(Context& cx, const Ciphertext& a, uint64_t k, Ciphertext& out);
+// out = extra + sum_b rot((c0s[b], c1s[b]), steps[b]) for n inputs of nl limbs at `scale`
+// (no zero steps; extra0/extra1 may be null): one batched ModUp, the inner products summed
+// in QP, one ModDown (ksbatch.cu)
+void rotate_sum(Context& cx, const uint64_t* const* c0s, const uint64_t* const* c1s, const int* steps, int n,
+                int nl, double scale, const uint64_t* extra0, const uint64_t* extra1, Ciphertext& out);
 void ct_rotate(Context& cx, const Ciphertext& a, int r, Ciphertext& out);
 void ct_conjugate(Context& cx, const Ciphertext& a, Ciphertext& out);
 void ct_rotate_hoisted(Context& cx, const Ciphertext& a, const int* rs, int n, Ciphertext* outs);

@@ -3,6 +3,7 @@
 #include "kernels.cu"
 #include "ntt.cu"
 #include "engine.cu"
+#include "ksbatch.cu"
 #include "circuit.cu"
 #include "bootstrap.cu"
 #include "matvec.cu"

@@ -22,16 +22,19 @@ __device__ __forceinline__ uint32_t auto_src(uint32_t i, uint64_t k, int logN) {
 // ---------------------------------------------------------------------------- ModUp ----
 // dcoef: the nl Q-limbs in coefficient form; deval: the same limbs in eval form.
 // ext[j][e] for digit j: own limbs copied from deval, all others base-converted (coefficient
-// form, NTT'd afterwards).  tab: [dnum][alpha][2] (qhat^-1 mod q_i, shoup) then
+// form, NTT'd afterwards).  blockIdx.z indexes a batch of inputs (strides sdc, sdv, sext).  tab: [dnum][alpha][2] (qhat^-1 mod q_i, shoup) then
 // [dnum][ne][alpha][2] (qhat mod t, shoup).
 __global__ void __launch_bounds__(256) k_modup_bconv(const uint64_t* __restrict__ dcoef,
                                                      const uint64_t* __restrict__ deval, uint64_t* __restrict__ ext,
                                                      const uint64_t* __restrict__ tab, int nl, int ne, int alpha, int L,
-                                                     int logN) {
+                                                     int logN, long long sdc, long long sdv, long long sext) {
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int j = blockIdx.y;
     const int dn = gridDim.y;
+    dcoef += blockIdx.z * sdc;   // batch of inputs (blockIdx.z), same limb count
+    deval += blockIdx.z * sdv;
+    ext += blockIdx.z * sext;
     const int lo = j * alpha, sz = min(alpha, nl - lo);
     const uint64_t* qhinv = tab + (size_t)j * alpha * 2;
     const uint64_t* qh = tab + (size_t)dn * alpha * 2 + (size_t)j * ne * alpha * 2;
@@ -89,10 +92,13 @@ __global__ void k_key_inner(const uint64_t* __restrict__ ext, const uint64_t* __
 // buf: [2][ne][N], P limbs (e >= nl) already in coefficient form.  y[c][i] = BConv_{P->q_i}.
 // md: [K][2] phat^-1 mod p_k (+shoup); [L][K][2] phat_k mod q_i (+shoup); [L][2] P^-1 mod q_i.
 __global__ void k_moddown_bconv(const uint64_t* __restrict__ buf, uint64_t* __restrict__ y,
-                                const uint64_t* __restrict__ md, int nl, int ne, int L, int K, int logN) {
+                                const uint64_t* __restrict__ md, int nl, int ne, int L, int K, int logN,
+                                long long sbuf, long long sy) {
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int c = blockIdx.y;
+    buf += blockIdx.z * sbuf;   // batch of key-switch outputs (blockIdx.z)
+    y += blockIdx.z * sy;
     uint64_t t[8];
 #pragma unroll
     for (int k = 0; k < 8; k++) {

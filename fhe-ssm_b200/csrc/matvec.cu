@@ -388,23 +388,20 @@ void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets,
         cx.launches++;
     }
     // giants: sum_g rot(IA_g, g b1) + rot(IB_g, g b1 - D)
+    // (IA_0 unrotated; IB_0 is empty: rot(u, j) with j < b1 never needs the -D giant)
     const double sc = sets[0]->scale * spt;
-    auto view = [&](int o) {
-        Ciphertext c = ct_alloc(cx, nl);
-        CUDA_CHECK(cudaMemcpyAsync(c.buf.p, inner.p + (size_t)o * 2 * nl * N, (size_t)2 * nl * N * 8,
-                                   cudaMemcpyDeviceToDevice, st));
-        c.scale = sc;
-        return c;
-    };
-    Ciphertext acc = view(0);
-    for (int g = 1; g < G; g++) {
+    std::vector<const uint64_t*> c0s, c1s;
+    std::vector<int> steps;
+    for (int g = 1; g < G; g++)
         for (int X = 0; X < 2; X++) {
-            Ciphertext c = view(X * G + g), r, t;
-            ct_rotate(cx, c, X == 0 ? g * b1 : g * b1 - D, r);
-            ct_add(cx, acc, r, t);
-            acc = std::move(t);
+            const uint64_t* p = inner.p + (size_t)(X * G + g) * 2 * nl * N;
+            c0s.push_back(p);
+            c1s.push_back(p + (size_t)nl * N);
+            steps.push_back(X == 0 ? g * b1 : g * b1 - D);
         }
-    }
+    Ciphertext acc;
+    rotate_sum(cx, c0s.data(), c1s.data(), steps.data(), (int)steps.size(), nl, sc, inner.p,
+               inner.p + (size_t)nl * N, acc);
     ct_rescale(cx, acc);
     acc.scale = target;
     out = std::move(acc);

@@ -129,7 +129,7 @@ static void keyswitch_noalloc(Context& cx, const uint64_t* d, int nl, const Swit
     // ModUp (engine.cu modup): d -> coefficient form in A, base-convert each digit into B
     CUDA_CHECK(cudaMemcpyAsync(A, d, (size_t)nl * N * 8, cudaMemcpyDeviceToDevice, st));
     ntt(cx, cx.qmap(A, nl, (long long)nl * N), 1, true, st);
-    k_modup_bconv<<<g2(cx, dn), 256, 0, st>>>(A, d, B, T, nl, ne, alpha, L, cx.logN);
+    k_modup_bconv<<<g2(cx, dn), 256, 0, st>>>(A, d, B, T, nl, ne, alpha, L, cx.logN, 0, 0, 0);
     LimbMap em = cx.extmap(B, nl, (long long)ne * N);
     em.skip_alpha = alpha;
     ntt(cx, em, dn, false, st);
@@ -142,7 +142,7 @@ static void keyswitch_noalloc(Context& cx, const uint64_t* d, int nl, const Swit
     pm.base = A + (size_t)nl * N; pm.poly_stride = (long long)ne * N; pm.nl = K;
     pm.split = 0; pm.off0 = 0; pm.off1 = L;
     ntt(cx, pm, 2, true, st);
-    k_moddown_bconv<<<g2(cx, 2), 256, 0, st>>>(A, B, cx.d_md, nl, ne, L, K, cx.logN);
+    k_moddown_bconv<<<g2(cx, 2), 256, 0, st>>>(A, B, cx.d_md, nl, ne, L, K, cx.logN, 0, 0);
     ntt(cx, cx.qmap(B, nl, (long long)nl * N), 2, false, st);
     k_moddown_final<<<g2(cx, nl, 2), 256, 0, st>>>(A, B, nullptr, nullptr, out0, out1, cx.d_md, nl, ne, L, K,
                                                    cx.logN, 1);

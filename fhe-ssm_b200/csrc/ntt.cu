@@ -47,7 +47,7 @@ __device__ __forceinline__ uint64_t canon4(uint64_t v, uint64_t q) {   // [0, 4q
 
 __device__ __forceinline__ bool limb_skipped(const LimbMap& mp, int poly, int limb) {
     if (mp.skip_alpha == 0) return false;
-    const int lo = poly * mp.skip_alpha;
+    const int lo = (mp.skip_period > 0 ? poly % mp.skip_period : poly) * mp.skip_alpha;
     return limb >= lo && limb < min(lo + mp.skip_alpha, mp.skip_nq);
 }
 
@@ -262,7 +262,10 @@ void ntt(const Context& cx, const LimbMap& mp, int npoly, bool inv, cudaStream_t
     if (count == 0) return;
     int work = count;   // limb-polynomials actually transformed (ModUp skips its own digit)
     if (mp.skip_alpha)
-        for (int p = 0; p < npoly; p++) work -= std::max(0, std::min(mp.skip_alpha, mp.skip_nq - p * mp.skip_alpha));
+        for (int p = 0; p < npoly; p++) {
+            const int dg = mp.skip_period > 0 ? p % mp.skip_period : p;
+            work -= std::max(0, std::min(mp.skip_alpha, mp.skip_nq - dg * mp.skip_alpha));
+        }
     ProfScope ps(cx, inv ? "ntt_inv" : "ntt_fwd", 16.0 * cx.N * work);
     switch (cx.logN) {
         case 12: launch_ntt<12>(cx, mp, count, inv, st); break;

@@ -75,6 +75,7 @@ _SIGS = {
     "fhe_level_reduce": (C.c_int, [_VP, _VP, C.c_int]),
     "fhe_rotate": (C.c_int, [_VP, _VP, C.c_int32, C.POINTER(_VP)]),
     "fhe_rotate_hoisted": (C.c_int, [_VP, _VP, C.POINTER(C.c_int32), C.c_int, C.POINTER(_VP)]),
+    "fhe_rotate_sum": (C.c_int, [_VP, C.POINTER(_VP), C.POINTER(C.c_int32), C.c_int, C.POINTER(_VP)]),
     "fhe_conjugate": (C.c_int, [_VP, _VP, C.POINTER(_VP)]),
     "fhe_mul_vec_rescale": (C.c_int, [_VP, _VP, _DP, _DP, C.c_int, C.POINTER(_VP)]),
     "fhe_align": (C.c_int, [_VP, _VP, C.c_int]),
@@ -344,6 +345,15 @@ class CryptoContext:
         outs = (_VP * n)()
         _check(lib().fhe_rotate_hoisted(self.h, ct.h, arr, n, outs))
         return [Ciphertext(self, outs[i]) for i in range(n)]
+
+    def EvalRotateSum(self, cts, ks):
+        """sum_i EvalRotate(cts[i], ks[i]) with one batched key switch and one ModDown."""
+        n = len(cts)
+        arr = (_VP * n)(*[c.h for c in cts])
+        kk = (C.c_int32 * n)(*ks)
+        h = _VP()
+        _check(lib().fhe_rotate_sum(self.h, arr, kk, n, C.byref(h)))
+        return Ciphertext(self, h)
 
     def EvalConj(self, ct):
         h = _VP()

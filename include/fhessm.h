@@ -134,6 +134,10 @@ int fhe_level_reduce(fhe_ctx* cx, fhe_ct* ct, int levels);
 int fhe_rotate(fhe_ctx* cx, const fhe_ct* a, int32_t k, fhe_ct** out);
 /* hoisted rotations: one ModUp shared by n rotations (EvalFastRotation; used by the BSGS babies) */
 int fhe_rotate_hoisted(fhe_ctx* cx, const fhe_ct* a, const int32_t* ks, int n, fhe_ct** outs);
+/* sum_i EvalRotate(in[i], ks[i]) for inputs at one level and scale (the BSGS giant step,
+ * matvecBatch :3407): the rotations share one batched ModUp and a single ModDown of the sum
+ * (at most one ks[i] may be 0) */
+int fhe_rotate_sum(fhe_ctx* cx, const fhe_ct* const* in, const int32_t* ks, int n, fhe_ct** out);
 /* EvalConj: complex conjugation of every slot (automorphism 2N-1, :1355-1369) */
 int fhe_conjugate(fhe_ctx* cx, const fhe_ct* a, fhe_ct** out);
 

@@ -163,6 +163,25 @@ def test_rotate_convention_decrypted(pair):
         assert np.abs(cx.Decrypt(h).real - np.roll(z, -r)).max() < 1e-4, r
 
 
+def test_rotate_sum_lazy_moddown(pair):
+    """sum_i rot(ct_i, k_i) with one ModDown of the summed inner products: decrypts to the
+    rotated sum, within the rounding of the P-division of the one-at-a-time result."""
+    cx, o = pair
+    rng = np.random.default_rng(9)
+    steps = [0, 3, -5, 64, 1000]
+    cx.EvalRotateKeyGen([s for s in steps if s])
+    zs = [rng.uniform(-1, 1, o.N // 2) + 1j * rng.uniform(-1, 1, o.N // 2) for _ in steps]
+    cts = [cx.Encrypt(cx.MakeCKKSPackedPlaintext(z, 1)) for z in zs]
+    got = cx.Decrypt(cx.EvalRotateSum(cts, steps))
+    want = sum(np.roll(z, -s) for z, s in zip(zs, steps))
+    assert np.abs(got - want).max() < 1e-4
+    one = None
+    for c, s in zip(cts, steps):
+        r = cx.EvalRotate(c, s) if s else c
+        one = r if one is None else cx.EvalAdd(one, r)
+    assert np.abs(got - cx.Decrypt(one)).max() < 1e-6
+
+
 def test_production_ring_keyswitch_bit_exact():
     """N = 2^16 with the baseline's chain shape at a reduced depth: L=6, K=4, alpha=4."""
     cx, o = make_pair(16, 6, 4, 4)
