@@ -140,7 +140,10 @@ def roofline(prof):
     pk = peaks()
     if not prof:
         return None
-    name, (n, tms, tbytes) = max(prof.items(), key=lambda kv: kv[1][1])
+    kern = {k: v for k, v in prof.items() if not k.startswith("op:")}
+    if not kern:
+        return None
+    name, (n, tms, tbytes) = max(kern.items(), key=lambda kv: kv[1][1])
     achieved = tbytes / (tms / 1000.0) / 1e9
     peak = pk.get("hbm_gbs", 6650.0)
     traffic = None
@@ -153,8 +156,10 @@ def roofline(prof):
 
 
 def kernel_table(prof):
+    """Per kernel class: launches, device ms, achieved GB/s of algorithmic bytes.  Entries
+    named op:* are inclusive times of whole operations (bootstrap, matvec, ...)."""
     return {k: {"launches": v[0], "ms": round(v[1], 3),
-                "GB/s": round(v[2] / (v[1] / 1000.0) / 1e9, 1) if v[1] else None} for k, v in prof.items()}
+                "GB/s": round(v[2] / (v[1] / 1000.0) / 1e9, 1) if v[1] and v[2] else None} for k, v in prof.items()}
 
 
 # ------------------------------------------------------------------------ CPU oracle ----

@@ -24,6 +24,8 @@
 
 namespace fhe {
 
+constexpr int kDiagMax = 16;   // babies / giants of one bootstrap linear-transform level
+
 // circuit.cu
 double canon(const Context& cx, int nl);
 void align(Context& cx, Ciphertext& a, int nl_t, double target);
@@ -171,11 +173,51 @@ static BootLevel build_level(Context& cx, int lo, int hi, bool inverse, int nl_i
         const int g = (int)std::floor((double)k / L.b1), j = k - g * L.b1;
         cvec d = rotv(kv.second, -g * L.b1 * L.base);
         for (auto& x : d) x *= fold;
-        L.pts.emplace(std::make_pair(g, j), encode(cx, d.data(), n, nl_in, spt));
+        Plaintext pt = encode(cx, d.data(), n, nl_in, spt);
+        // Montgomery form: k_diag_mac accumulates 128-bit products and reduces once
+        k_mont<<<dim3(cx.N / 256, nl_in), 256, 0, cx.stream>>>(pt.buf.p, nl_in, 1, cx.logN);
+        CUDA_CHECK(cudaGetLastError());
+        L.pts.emplace(std::make_pair(g, j), std::move(pt));
         gset.insert(g);
     }
     L.gs.assign(gset.begin(), gset.end());
+    if ((int)L.gs.size() > kDiagMax || L.b1 > kDiagMax) throw Error("bootstrap: level too wide for k_diag_mac", -1);
     return L;
+}
+
+// All giants of one linear-transform level in one pass over the babies:
+// out_g[c][i][x] = sum_j pt_gj[i][x] * baby_j[c][i][x] (pt in Montgomery form, <= kDiagMax
+// products per 128-bit sum: hi < q for words < 2^60).  grid (N / 256, nl).
+struct DiagArgs {
+    const uint64_t* b0[kDiagMax];
+    const uint64_t* b1[kDiagMax];
+    const uint64_t* pt[kDiagMax][kDiagMax];   // [g][j] or null
+    uint64_t* o0[kDiagMax];
+    uint64_t* o1[kDiagMax];
+    int nb, ng;
+};
+__global__ void __launch_bounds__(256) k_diag_mac(const DiagArgs a, int logN) {
+    const int N = 1 << logN;
+    const int x = blockIdx.x * blockDim.x + threadIdx.x;
+    const int i = blockIdx.y;
+    const ModConst mc = c_mod[i];
+    const size_t w = (size_t)i * N + x;
+    uint64_t v0[kDiagMax], v1[kDiagMax];
+#pragma unroll
+    for (int j = 0; j < kDiagMax; j++)
+        if (j < a.nb) { v0[j] = a.b0[j][w]; v1[j] = a.b1[j][w]; }
+    for (int g = 0; g < a.ng; g++) {
+        u128acc s0{0, 0}, s1{0, 0};
+#pragma unroll
+        for (int j = 0; j < kDiagMax; j++) {
+            if (j >= a.nb || !a.pt[g][j]) continue;
+            const uint64_t p = a.pt[g][j][w];
+            acc_mad(s0, p, v0[j]);
+            acc_mad(s1, p, v1[j]);
+        }
+        a.o0[g][w] = redc(s0.hi, s0.lo, mc);
+        a.o1[g][w] = redc(s1.hi, s1.lo, mc);
+    }
 }
 
 static void eval_level(Context& cx, const BootLevel& L, const Ciphertext& v, Ciphertext& out) {
@@ -189,26 +231,40 @@ static void eval_level(Context& cx, const BootLevel& L, const Ciphertext& v, Cip
         ct_rotate_hoisted(cx, v, steps.data(), (int)steps.size(), rs.data());
         for (size_t i = 0; i < rs.size(); i++) baby[i + 1] = std::move(rs[i]);
     }
-    // giant g: inner_g = sum_j pt_gj . baby_j, then sum_g rot(inner_g, g b1 base) in one rotate_sum
+    // giant g: inner_g = sum_j pt_gj . baby_j (one k_diag_mac for all g), then
+    // sum_g rot(inner_g, g b1 base) in one rotate_sum
     std::vector<Ciphertext> inners;
     std::vector<int> gsteps;
     const Ciphertext* g0 = nullptr;
     inners.reserve(L.gs.size());
+    DiagArgs da{};
+    da.nb = L.b1;
+    for (int j = 0; j < L.b1; j++) { da.b0[j] = baby[j].c(0); da.b1[j] = baby[j].c(1); }
+    double spt = 0;
     for (int g : L.gs) {
-        Ciphertext inner;
-        bool hi = false;
+        const int gi = (int)inners.size();
+        bool any = false;
         for (int j = 0; j < L.b1; j++) {
             auto it = L.pts.find(std::make_pair(g, j));
             if (it == L.pts.end()) continue;
-            Ciphertext t;
-            ct_mul_pt(cx, baby[j], it->second, t);
-            if (!hi) { inner = std::move(t); hi = true; }
-            else { Ciphertext u; ct_add(cx, inner, t, u); inner = std::move(u); }
+            da.pt[gi][j] = it->second.buf.p;
+            spt = it->second.scale;
+            any = true;
         }
-        if (!hi) continue;
-        inners.push_back(std::move(inner));
+        if (!any) continue;
+        inners.push_back(ct_alloc(cx, v.nl));
+        da.o0[gi] = inners.back().c(0);
+        da.o1[gi] = inners.back().c(1);
         if (g == 0) g0 = &inners.back();
         else gsteps.push_back(g * L.b1 * L.base);
+    }
+    da.ng = (int)inners.size();
+    for (auto& c : inners) c.scale = v.scale * spt;
+    if (da.ng > 0) {
+        ProfScope ps(cx, "diag_mac", 8.0 * cx.N * v.nl * (2.0 * L.b1 + 2.0 * da.ng + (double)L.pts.size()));
+        k_diag_mac<<<dim3(cx.N / 256, v.nl), 256, 0, cx.stream>>>(da, cx.logN);
+        CUDA_CHECK(cudaGetLastError());
+        cx.launches++;
     }
     if (inners.empty()) throw Error("bootstrap: empty linear-transform level", -1);
     std::vector<const uint64_t*> c0s, c1s;
@@ -283,6 +339,7 @@ void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto
 void bootstrap(Context& cx, const Ciphertext& in, Ciphertext& out) { bootstrap_upto(cx, in, out, 4); }
 
 void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto) {
+    ProfScope op(cx, "op:bootstrap", 0);
     auto* bc = (BootCtx*)cx.boot.get();
     if (!bc) throw Error("bootstrap: no bootstrap precomputation (call bootstrap_setup)", -5);
     const int N = cx.N;
@@ -317,6 +374,7 @@ void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto
     if (upto == 1) { out = std::move(raised); return; }
     // 3. CoeffToSlot
     Ciphertext v = std::move(raised);
+    auto* ps_cts = new ProfScope(cx, "op:boot_cts", 0);
     for (auto& L : bc->cts) {
         Ciphertext t;
         eval_level(cx, L, v, t);
@@ -327,8 +385,10 @@ void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto
         mul_const_rescale(cx, v, 1.0 / (2.0 * bc->B), t, canon(cx, v.nl - 1));
         v = std::move(t);
     }
+    delete ps_cts;
     if (upto == 2) { out = std::move(v); return; }
     // 4. EvalMod on 2 Re and 2 Im (values t/(q0 B) in [-1, 1])
+    auto* ps_mod = new ProfScope(cx, "op:boot_evalmod", 0);
     Ciphertext re, im;
     split_complex(cx, v, re, im, false);
     Ciphertext parts[2] = {std::move(re), std::move(im)};
@@ -347,7 +407,9 @@ void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto
     }
     Ciphertext w;
     merge_complex(cx, std::move(parts[0]), std::move(parts[1]), w);
+    delete ps_mod;
     if (upto == 3) { out = std::move(w); return; }
+    ProfScope ps_stc(cx, "op:boot_stc", 0);
     // 5. SlotToCoeff
     if (w.nl > bc->nl_stc) align(cx, w, bc->nl_stc, 0);
     if (w.nl != bc->nl_stc) throw Error("bootstrap: EvalMod used more levels than planned", -4);

@@ -20,8 +20,18 @@
 // word i >> log2(N/2D) (the compressed store, gpu_real_model.cu:145-175).  The plan keeps
 // the 2D real small-ring coefficients of each family vector (fp64) in HBM; k_ptgen turns
 // them into residues at the level and scale of the call (scale, round, reduce, 2D-point
-// NTT, Montgomery form) and k_bsgs_mac accumulates all baby products of all giants in one
-// pass over the babies.
+// NTT, Montgomery form), for the Q limbs and the special limbs P.
+//
+// Evaluation (double hoisting, Bossuat et al., Eurocrypt 2021, section 4):
+//  * babies: one ModUp of u, then every baby rot(u, r) is left in the extended basis QP as
+//    P rot(u, r) (no ModDown): k_baby_pq computes the key inner product at the permuted
+//    slots of the shared ModUp output with the rotate-then-switch key;
+//  * k_bsgs_gemm: for every REP-group of slots (the slots that share one compressed
+//    plaintext word) the products are a dense (2G x 2b1) x (2b1 x slots) product of words
+//    mod q; the kernel stages babies and plaintext words in shared memory and accumulates
+//    128-bit;
+//  * one ModDown per giant input (2G of them, batched), then the giant rotations summed by
+//    rotate_sum (one batched ModUp, one ModDown of the sum).
 #include <cmath>
 #include <cstring>
 
@@ -33,40 +43,52 @@ namespace fhe {
 static void fft_special_inv_small(std::complex<double>* v, int n, int M);
 
 // --------------------------------------------------------------------------- kernels ----
-// coef [P][2D] fp64 -> out [P][nl][2D] words: round(c * scale) mod q_i, 2D-point NTT with the
-// first 2D entries of the ring-N root table (they are the powers of psi^(N/2D) in the same
-// bit-reversed order), then (mont != 0) * 2^64 mod q (Montgomery form for k_bsgs_mac)
+// coef [P][2D] fp64 -> out [limb][2D][P] words (word k of every plaintext of a limb is
+// contiguous, the order k_bsgs_gemm reads): round(c * scale) mod m(i), 2D-point NTT with the
+// first 2D entries of the ring-N root table (the powers of psi^(N/2D) in the same
+// bit-reversed order), then (mont != 0) * 2^64 mod q (Montgomery form for the products).
+// Limb i uses modulus i for i < nq and the special modulus L + i - nq above; IPC plaintexts
+// per CTA (their words are written together).
+template <int IPC>
 __global__ void __launch_bounds__(256) k_ptgen(const double* __restrict__ coef, double scale, uint64_t* __restrict__ out,
-                                               int nl, int logD2, const uint64_t* __restrict__ tw,
+                                               int P, int nq, int L, int logD2, const uint64_t* __restrict__ tw,
                                                const uint64_t* __restrict__ twp, int N, int mont) {
-    extern __shared__ uint64_t sa[];
+    extern __shared__ uint64_t sa[];   // [IPC][2D]
     const int D2 = 1 << logD2;
-    const int id = blockIdx.x, i = blockIdx.y;
-    const ModConst mc = c_mod[i];
-    const double* c = coef + (size_t)id * D2;
-    for (int k = threadIdx.x; k < D2; k += blockDim.x) {
-        const double v = c[k] * scale;
-        const long long r = llrint(v);
-        sa[k] = r >= 0 ? reduce64((uint64_t)r, mc) : mod_neg(reduce64((uint64_t)(-r), mc), mc.q);
+    const int id0 = blockIdx.x * IPC, i = blockIdx.y;
+    const int m = i < nq ? i : L + (i - nq);
+    const ModConst mc = c_mod[m];
+    for (int e = threadIdx.x; e < IPC * D2; e += blockDim.x) {
+        const int t = e >> logD2, k = e & (D2 - 1);
+        uint64_t r0 = 0;
+        if (id0 + t < P) {
+            const long long r = llrint(coef[(size_t)(id0 + t) * D2 + k] * scale);
+            r0 = r >= 0 ? reduce64((uint64_t)r, mc) : mod_neg(reduce64((uint64_t)(-r), mc), mc.q);
+        }
+        sa[e] = r0;
     }
     __syncthreads();
-    const uint64_t* T = tw + (size_t)i * N;
-    const uint64_t* Tp = twp + (size_t)i * N;
-    for (int m = 1, t = D2 >> 1; m < D2; m <<= 1, t >>= 1) {
-        for (int b = threadIdx.x; b < D2 / 2; b += blockDim.x) {
+    const uint64_t* T = tw + (size_t)m * N;
+    const uint64_t* Tp = twp + (size_t)m * N;
+    for (int mm = 1, t = D2 >> 1; mm < D2; mm <<= 1, t >>= 1) {
+        for (int bi = threadIdx.x; bi < IPC * (D2 / 2); bi += blockDim.x) {
+            const int v = bi / (D2 / 2), b = bi % (D2 / 2);
             const int grp = b / t, off = b % t;
             const int j1 = grp * 2 * t + off, j2 = j1 + t;
-            const uint64_t w = T[m + grp], wp = Tp[m + grp];
-            const uint64_t x = mul_shoup(sa[j2], w, wp, mc.q);
-            const uint64_t u = sa[j1];
-            sa[j1] = mod_add(u, x, mc.q);
-            sa[j2] = mod_sub(u, x, mc.q);
+            uint64_t* s2 = sa + (size_t)v * D2;
+            const uint64_t x = mul_shoup(s2[j2], T[mm + grp], Tp[mm + grp], mc.q);
+            const uint64_t u = s2[j1];
+            s2[j1] = mod_add(u, x, mc.q);
+            s2[j2] = mod_sub(u, x, mc.q);
         }
         __syncthreads();
     }
-    uint64_t* o = out + ((size_t)id * nl + i) * D2;
-    for (int k = threadIdx.x; k < D2; k += blockDim.x)
-        o[k] = mont ? redc(__umul64hi(sa[k], mc.r2), sa[k] * mc.r2, mc) : sa[k];
+    for (int e = threadIdx.x; e < IPC * D2; e += blockDim.x) {
+        const int t = e % IPC, k = e / IPC;
+        if (id0 + t >= P) continue;
+        const uint64_t v = sa[(size_t)t * D2 + k];
+        out[((size_t)i * D2 + k) * P + id0 + t] = mont ? redc(__umul64hi(v, mc.r2), v * mc.r2, mc) : v;
+    }
 }
 
 // ------------------------------------------------------- periodic encode + plaintext cache ----
@@ -96,8 +118,8 @@ static Plaintext encode_periodic(Context& cx, const std::complex<double>* z, int
     int lr = 0;
     while ((cx.N >> lr) > 2 * n) lr++;
     pt.log_rep = lr;
-    k_ptgen<<<dim3(1, nl), 256, 2 * n * 8, cx.stream>>>((const double*)dc.p, scale, pt.buf.p, nl, log2n, cx.d_tw,
-                                                       cx.d_twp, cx.N, 0);
+    k_ptgen<1><<<dim3(1, nl), 256, 2 * n * 8, cx.stream>>>((const double*)dc.p, scale, pt.buf.p, 1, nl, cx.L,
+                                                          log2n, cx.d_tw, cx.d_twp, cx.N, 0);
     CUDA_CHECK(cudaGetLastError());
     cx.launches++;
     return pt;
@@ -116,84 +138,149 @@ const Plaintext& encode_cached(Context& cx, const std::complex<double>* z, int n
     auto it = cx.ptcache.find(h);
     if (it != cx.ptcache.end()) return *it->second;
     if (cx.ptcache.size() > 50000) cx.ptcache.clear();
-    auto pt = std::make_shared<Plaintext>(n < cx.N / 2 && (cx.N / 2) % n == 0 && n >= 8
+    auto pt = std::make_shared<Plaintext>(n < cx.N / 2 && (cx.N / 2) % n == 0 && n >= 8 && n <= 4096
                                               ? encode_periodic(cx, z, n, nl, scale)
                                               : encode(cx, z, n, nl, scale));
     return *cx.ptcache.emplace(h, pt).first->second;
 }
 
-constexpr int kMaxBabies = 256;   // sets * 2 * b1 (kernel-parameter array)
-struct MacArgs {
-    const uint64_t* babies[kMaxBabies];   // [set][2][b1] ciphertext bases (Y = 0: rot(u, j), Y = 1: rot(u, j - D))
-    long long bstride;               // words between c0 and c1 of a baby
-    const int* ids;                  // [set][3][G][b1] plaintext id or -1 (families AA, AB, BA)
-    const uint64_t* pts;             // [P][nl][2D] Montgomery words
-    uint64_t* out;                   // [2G][2][nl][N] (IA_0..IA_{G-1}, IB_0..IB_{G-1})
-    int nsets, b1, G, nl, logN, lr, D2;
+constexpr int kMaxSets = 8;      // input chunks of one matvec (column blocks of D)
+constexpr int kKc = 64;          // babies per shared-memory chunk (<= 128 products per 128-bit sum)
+
+struct GemmArgs {
+    const uint64_t* babies[kMaxSets];   // per set: [2 b1][2][ne][N], QP basis (Y = 0: rot(u, j), Y = 1: rot(u, j - D))
+    const int* ids;                     // [set][3][G][b1] plaintext id or -1 (families AA, AB, BA)
+    const uint64_t* pts;                // [ne][2D][P] Montgomery words
+    uint64_t* out;                      // [2G][2][ne][N] (IA_0..IA_{G-1}, IB_0..IB_{G-1}), QP basis
+    int nsets, b1, G, nl, ne, L, logN, lr, D2, P, TW;
 };
 
-// one CTA: 64 consecutive evaluation slots of one limb, 512 threads = 64 slots x 8 output
-// groups; the babies' words for those slots are staged in shared memory per input set
-__global__ void __launch_bounds__(512) k_bsgs_mac(MacArgs a) {
-    extern __shared__ uint64_t sb[];   // [2][b1][2][64]
+// One CTA: limb e of TW consecutive slots that share one compressed plaintext word (TW <= REP),
+// both polynomials: out[o][c][x] = sum_k W[o][k] * baby[k][c][x] with W[o][k] the word of
+// family fam(o, k), giant g(o), baby j(k).  Thread (to, tn) owns outputs 2to, 2to+1 and the 4
+// columns 4tn..4tn+3 (column n = c * TW + slot).  Babies and plaintext words are staged in
+// shared memory kKc at a time; each product sum of <= kKc terms (< kKc q^2 < 2^126) is
+// Montgomery-reduced into a running sum mod q.
+__global__ void __launch_bounds__(512) k_bsgs_gemm(const GemmArgs a) {
+    extern __shared__ uint64_t sm[];
+    const int M = 2 * a.G, TW = a.TW, NC = 2 * TW;
+    uint64_t* Bs = sm;                    // [kKc][NC]
+    uint64_t* Ws = sm + (size_t)kKc * NC; // [kKc][M]
     const int N = 1 << a.logN;
-    const int i = blockIdx.y;
-    const int xs = threadIdx.x & 63, og = threadIdx.x >> 6;
-    const int x = blockIdx.x * 64 + xs;
-    const ModConst mc = c_mod[i];
-    const int nout = 2 * a.G;
-    constexpr int MAXO = 16;
-    uint64_t acc[MAXO][2];
+    const int e = blockIdx.y;
+    const int x0 = blockIdx.x * TW;
+    const int m = e < a.nl ? e : a.L + (e - a.nl);
+    const ModConst mc = c_mod[m];
+    const int nth = blockDim.x, tid = threadIdx.x;
+    const int tn = tid % (TW / 2), to = tid / (TW / 2);
+    const int o0 = 2 * to, n0 = 4 * tn;
+    const int ptw = x0 >> a.lr;
+    const int K = 2 * a.b1;
+    uint64_t sum[2][4];
 #pragma unroll
-    for (int t = 0; t < MAXO; t++) acc[t][0] = acc[t][1] = 0;
-    const int ptw = x >> a.lr;
+    for (int u = 0; u < 2; u++)
+#pragma unroll
+        for (int v = 0; v < 4; v++) sum[u][v] = 0;
     for (int s = 0; s < a.nsets; s++) {
-        __syncthreads();
-        for (int e = threadIdx.x; e < 2 * a.b1 * 2 * 64; e += blockDim.x) {
-            const int xx = e & 63, p = (e >> 6) & 1, bj = e >> 7;   // bj = Y * b1 + j
-            const uint64_t* base = a.babies[(size_t)s * 2 * a.b1 + bj];
-            sb[e] = base[(size_t)p * a.bstride + (size_t)i * N + (size_t)blockIdx.x * 64 + xx];
-        }
-        __syncthreads();
-        for (int t = 0; t < MAXO; t++) {
-            const int o = og + 8 * t;
-            if (o >= nout) break;
-            const int X = o / a.G, g = o % a.G;
-            for (int Y = 0; Y < 2; Y++) {
+        const uint64_t* bb = a.babies[s];
+        for (int k0 = 0; k0 < K; k0 += kKc) {
+            const int kc = min(kKc, K - k0);
+            __syncthreads();
+            for (int t = tid; t < kc * NC; t += nth) {
+                const int kk = t / NC, n = t % NC, c = n / TW, xs = n % TW;
+                Bs[t] = bb[(((size_t)(k0 + kk) * 2 + c) * a.ne + e) * N + x0 + xs];
+            }
+            for (int t = tid; t < kc * M; t += nth) {
+                const int kk = t / M, o = t % M;
+                const int k = k0 + kk, Y = k / a.b1, j = k % a.b1;
+                const int X = o / a.G, g = o % a.G;
                 const int fam = X == 0 ? Y : (Y == 0 ? 2 : -1);
-                if (fam < 0) continue;
-                const int* idrow = a.ids + (((size_t)s * 3 + fam) * a.G + g) * a.b1;
-                for (int j0 = 0; j0 < a.b1; j0 += 8) {
-                    u128acc p0{0, 0}, p1{0, 0};
-                    bool any = false;
+                int id = -1;
+                if (fam >= 0) id = a.ids[(((size_t)s * 3 + fam) * a.G + g) * a.b1 + j];
+                Ws[t] = id < 0 ? 0 : a.pts[((size_t)e * a.D2 + ptw) * a.P + id];
+            }
+            __syncthreads();
+            u128acc acc[2][4];
 #pragma unroll
-                    for (int jj = 0; jj < 8; jj++) {
-                        const int j = j0 + jj;
-                        if (j >= a.b1) break;
-                        const int id = idrow[j];
-                        if (id < 0) continue;
-                        any = true;
-                        const uint64_t w = a.pts[((size_t)id * a.nl + i) * a.D2 + ptw];
-                        const uint64_t* bb = sb + ((Y * a.b1 + j) * 2) * 64 + xs;
-                        acc_mad(p0, w, bb[0]);
-                        acc_mad(p1, w, bb[64]);
-                    }
-                    if (!any) continue;
-                    acc[t][0] += redc(p0.hi, p0.lo, mc);
-                    acc[t][1] += redc(p1.hi, p1.lo, mc);
-                    acc[t][0] = reduce_lazy16(acc[t][0], mc.q);
-                    acc[t][1] = reduce_lazy16(acc[t][1], mc.q);
+            for (int u = 0; u < 2; u++)
+#pragma unroll
+                for (int v = 0; v < 4; v++) acc[u][v] = u128acc{0, 0};
+            // outputs IB (o >= G) have no products with the babies rot(u, j - D) (k >= b1):
+            // those warps stop early (the split is warp-uniform)
+            const int kend = o0 >= a.G ? max(0, min(kc, a.b1 - k0)) : kc;
+            for (int kk = 0; kk < kend; kk++) {
+                const ulonglong2 wv = *reinterpret_cast<const ulonglong2*>(Ws + kk * M + o0);
+                const ulonglong2* br = reinterpret_cast<const ulonglong2*>(Bs + (size_t)kk * NC + n0);
+                const ulonglong2 b01 = br[0], b23 = br[1];
+                const uint64_t w0 = wv.x, w1 = wv.y;
+                const uint64_t bv[4] = {b01.x, b01.y, b23.x, b23.y};
+#pragma unroll
+                for (int v = 0; v < 4; v++) {
+                    acc_mad(acc[0][v], w0, bv[v]);
+                    acc_mad(acc[1][v], w1, bv[v]);
                 }
             }
+#pragma unroll
+            for (int u = 0; u < 2; u++)
+#pragma unroll
+                for (int v = 0; v < 4; v++) {
+                    // <= 64 products of words < q < 2^60: hi < 64 q^2 / 2^64 < 4q; bring it below q
+                    // (T changes by a multiple of q 2^64) before the Montgomery step
+                    uint64_t hi = acc[u][v].hi;
+                    if (hi >= 2 * mc.q) hi -= 2 * mc.q;
+                    if (hi >= mc.q) hi -= mc.q;
+                    sum[u][v] = mod_add(sum[u][v], redc(hi, acc[u][v].lo, mc), mc.q);
+                }
         }
     }
-    for (int t = 0; t < MAXO; t++) {
-        const int o = og + 8 * t;
-        if (o >= nout) break;
-        uint64_t* dst = a.out + (((size_t)o * 2) * a.nl + i) * N + x;
-        dst[0] = acc[t][0];
-        dst[(size_t)a.nl * N] = acc[t][1];
+#pragma unroll
+    for (int u = 0; u < 2; u++)
+#pragma unroll
+        for (int v = 0; v < 4; v++) {
+            const int n = n0 + v, c = n / TW, xs = n % TW;
+            a.out[(((size_t)(o0 + u) * 2 + c) * a.ne + e) * N + x0 + xs] = sum[u][v];
+        }
+}
+
+// Babies in QP: out[b] = P rot(u, r_b), i.e. c0 = tau(ip0) + P tau(u0), c1 = tau(ip1) with
+// ip = <ModUp(u1), key_b> evaluated at the permuted slots of the shared ModUp output `ext`
+// against the rotate-then-switch key (fkey[x] = key[auto_src(x)]); perm == 1: P u.
+struct BabyArgs {
+    const uint64_t* fkey[64];
+    uint64_t perm[64];
+    uint64_t pw[kMaxMod], pwp[kMaxMod];   // P mod q_i (Shoup)
+};
+__global__ void __launch_bounds__(256) k_baby_pq(const uint64_t* __restrict__ ext, const uint64_t* __restrict__ u0,
+                                                 const uint64_t* __restrict__ u1, const BabyArgs a,
+                                                 uint64_t* __restrict__ out, int nl, int ne, int dn, int L, int K,
+                                                 int logN) {
+    const int N = 1 << logN;
+    const int x = blockIdx.x * blockDim.x + threadIdx.x;
+    const int e = blockIdx.y, b = blockIdx.z;
+    const int m = e < nl ? e : L + (e - nl);
+    const ModConst mc = c_mod[m];
+    uint64_t* o = out + (size_t)b * 2 * ne * N;
+    const uint64_t k = a.perm[b];
+    uint64_t v0, v1;
+    if (k == 1) {
+        v0 = e < nl ? mul_shoup(u0[(size_t)e * N + x], a.pw[e], a.pwp[e], mc.q) : 0;
+        v1 = e < nl ? mul_shoup(u1[(size_t)e * N + x], a.pw[e], a.pwp[e], mc.q) : 0;
+    } else {
+        const uint32_t sx = auto_src((uint32_t)x, k, logN);
+        const uint64_t* key = a.fkey[b];
+        const size_t nk = (size_t)(L + K);
+        u128acc a0{0, 0}, a1{0, 0};
+        for (int d = 0; d < dn; d++) {
+            const uint64_t dv = ext[((size_t)d * ne + e) * N + sx];
+            acc_mad(a0, dv, key[(((size_t)d * 2 + 0) * nk + m) * N + x]);
+            acc_mad(a1, dv, key[(((size_t)d * 2 + 1) * nk + m) * N + x]);
+        }
+        v0 = redc(a0.hi, a0.lo, mc);
+        v1 = redc(a1.hi, a1.lo, mc);
+        if (e < nl) v0 = mod_add(v0, mul_shoup(u0[(size_t)e * N + sx], a.pw[e], a.pwp[e], mc.q), mc.q);
     }
+    o[(size_t)e * N + x] = v0;
+    o[((size_t)ne + e) * N + x] = v1;
 }
 
 // -------------------------------------------------------------------------- the plan ----
@@ -238,7 +325,7 @@ std::shared_ptr<MatvecPlan> matvec_plan(Context& cx, const double* W, int rows, 
     pl->D = D; pl->b1 = b1; pl->G = D / b1; pl->rows = rows; pl->cols = cols;
     pl->nsets = (cols + D - 1) / D;
     const int G = pl->G, S = pl->nsets;
-    if (2 * G > 8 * 16) throw Error("matvec_plan: too many giant steps (2 D / b1 must be <= 128)", -1);
+    if (2 * G > 64) throw Error("matvec_plan: too many giant steps (2 D / b1 must be <= 64)", -1);
     pl->ids.assign((size_t)S * 3 * G * b1, -1);
     // family vectors, then small-ring coefficients (in parallel)
     struct Job { int s, fam, g, j; };
@@ -307,27 +394,46 @@ std::vector<int> matvec_rotations(int D, int b1) {
     return r;
 }
 
-// the 2 b1 babies of one input: rot(u, j) (j = 0..b1-1) and rot(u, j - D) (j = 0..b1-1),
-// all with stride nl*N; one hoisted ModUp
+// the 2 b1 babies of one input in QP: P rot(u, j) (j = 0..b1-1) then P rot(u, j - D)
 struct BabySet {
     int D = 0, b1 = 0, nl = 0;
     double scale = 0;
-    std::vector<Ciphertext> cts;   // [2 b1]: Y = 0 then Y = 1
+    DevBuf pq;   // [2 b1][2][nl + K][N]
 };
 
 void matvec_babies(Context& cx, const Ciphertext& u, int D, int b1, BabySet& bs) {
+    ProfScope op(cx, "op:matvec_babies", 0);
     if (u.nl < 2) throw Error("matvec: no level left", -4);
-    std::vector<int> steps;
-    for (int j = 1; j < b1; j++) steps.push_back(j);
-    for (int j = 0; j < b1; j++) steps.push_back(j - D);
-    std::vector<Ciphertext> r(steps.size());
-    ct_rotate_hoisted(cx, u, steps.data(), (int)steps.size(), r.data());
-    bs.D = D; bs.b1 = b1; bs.nl = u.nl; bs.scale = u.scale;
-    bs.cts.clear();
-    bs.cts.resize(2 * b1);
-    bs.cts[0] = ct_copy(cx, u);
-    for (int j = 1; j < b1; j++) bs.cts[j] = std::move(r[j - 1]);
-    for (int j = 0; j < b1; j++) bs.cts[b1 + j] = std::move(r[b1 - 1 + j]);
+    const int N = cx.N, K = cx.K, L = cx.L, nl = u.nl, ne = nl + K, dn = cx.dnum(nl);
+    cudaStream_t st = cx.stream;
+    bs.D = D; bs.b1 = b1; bs.nl = nl; bs.scale = u.scale;
+    bs.pq = DevBuf((size_t)2 * b1 * 2 * ne * N, st);
+    DevBuf ext = modup(cx, u.c(1), nl);
+    BabyArgs ba{};
+    for (int i = 0; i < nl; i++) {
+        uint64_t pm = 1;
+        for (int k = 0; k < K; k++) pm = host_mulmod(pm, cx.mods[L + k] % cx.mods[i], cx.mods[i]);
+        ba.pw[i] = pm;
+        ba.pwp[i] = shoup_of(pm, cx.mods[i]);
+    }
+    const int nb = 2 * b1;
+    for (int b0 = 0; b0 < nb; b0 += 64) {
+        const int B = std::min(64, nb - b0);
+        for (int b = 0; b < B; b++) {
+            const int t = b0 + b, Y = t / b1, j = t % b1;
+            const uint64_t k = rot_index(cx, Y == 0 ? j : j - D);
+            ba.perm[b] = k;
+            ba.fkey[b] = k == 1 ? nullptr : forward_key(cx, k);
+        }
+        ProfScope ps(cx, "baby_pq", 8.0 * N * B * ((double)dn * ne * 2 + 2 * ne));
+        k_baby_pq<<<dim3(N / 256, ne, B), 256, 0, st>>>(ext.p, u.c(0), u.c(1), ba,
+                                                        bs.pq.p + (size_t)b0 * 2 * ne * N, nl, ne, dn, L, K,
+                                                        cx.logN);
+        CUDA_CHECK(cudaGetLastError());
+        cx.launches++;
+        cx.ks_count += B;
+        cx.ks_limbs += (long long)B * nl;
+    }
 }
 
 void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets, Ciphertext& out);
@@ -344,64 +450,105 @@ void matvec(Context& cx, const MatvecPlan& pl, const Ciphertext* const* us, Ciph
     matvec_apply(cx, pl, ptr.data(), out);
 }
 
+// ModDown of B polynomial pairs in QP ([B][2][nl+K][N], destroyed) into out [B][2][nl][N]
+static void moddown_many(Context& cx, uint64_t* in, int B, int nl, uint64_t* out) {
+    const int N = cx.N, K = cx.K, L = cx.L, ne = nl + K;
+    cudaStream_t st = cx.stream;
+    LimbMap pm{};
+    pm.base = in + (size_t)nl * N; pm.poly_stride = (long long)ne * N; pm.nl = K;
+    pm.split = 0; pm.off0 = 0; pm.off1 = L;
+    ntt(cx, pm, 2 * B, true, st);
+    DevBuf y((size_t)B * 2 * nl * N, st);
+    {
+        ProfScope ps(cx, "moddown_bconv", 8.0 * N * B * (2 * K + 2 * nl));
+        k_moddown_bconv<<<dim3(N / 256, 2, B), 256, 0, st>>>(in, y.p, cx.d_md, nl, ne, L, K, cx.logN,
+                                                             (long long)2 * ne * N, (long long)2 * nl * N);
+    }
+    ntt(cx, cx.qmap(y.p, nl, (long long)nl * N), 2 * B, false, st);
+    for (int b0 = 0; b0 < B; b0 += 64) {
+        const int Bc = std::min(64, B - b0);
+        FinalBatch fb{};
+        for (int b = 0; b < Bc; b++) {
+            fb.out0[b] = out + (size_t)(b0 + b) * 2 * nl * N;
+            fb.out1[b] = fb.out0[b] + (size_t)nl * N;
+            fb.perm[b] = 1;
+        }
+        ProfScope ps(cx, "moddown_final", 8.0 * N * nl * Bc * 6);
+        k_moddown_final_b<<<dim3(N / 256, nl, 2 * Bc), 256, 0, st>>>(in + (size_t)b0 * 2 * ne * N,
+                                                                     y.p + (size_t)b0 * 2 * nl * N, nullptr, fb,
+                                                                     cx.d_md, nl, ne, L, K, cx.logN);
+    }
+    CUDA_CHECK(cudaGetLastError());
+    cx.launches += 2 + (B + 63) / 64;
+}
+
 void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets, Ciphertext& out) {
-    const int N = cx.N, S = pl.nsets, b1 = pl.b1, G = pl.G, D = pl.D;
-    const int nl = sets[0]->nl;
+    ProfScope op(cx, "op:matvec_apply", 0);
+    const int N = cx.N, S = pl.nsets, b1 = pl.b1, G = pl.G, D = pl.D, K = cx.K;
+    const int nl = sets[0]->nl, ne = nl + K;
     for (int s = 0; s < S; s++)
         if (sets[s]->nl != nl || std::fabs(sets[s]->scale / sets[0]->scale - 1) > 1e-9 || sets[s]->D != D ||
             sets[s]->b1 != b1)
             throw Error("matvec: input chunks must share level, scale and baby geometry", -4);
+    if (S > kMaxSets) throw Error("matvec: too many input chunks for one launch", -1);
     cudaStream_t st = cx.stream;
-    if ((size_t)S * 2 * b1 > (size_t)kMaxBabies) throw Error("matvec: too many babies for one launch", -1);
     // plaintexts at this level: scale so that the rescaled output is canonical
     const double target = canon(cx, nl - 1);
     const double spt = target * (double)cx.mods[nl - 1] / sets[0]->scale;
     int logD2 = 0;
     while ((1 << logD2) < 2 * D) logD2++;
-    DevBuf pts((size_t)std::max(pl.P, 1) * nl * 2 * D, st);
+    int lr = 0;
+    while ((N >> lr) > 2 * D) lr++;
+    const int TW = std::min(32, 1 << lr);
+    if (TW < 8) throw Error("matvec: D too large for the ring (need N / 2D >= 8)", -1);
+    const int M = 2 * G;
+    if ((TW / 2) * (M / 2) > 512 || M % 2) throw Error("matvec: too many giant steps for one CTA", -1);
+    DevBuf pts((size_t)std::max(pl.P, 1) * ne * 2 * D, st);
     if (pl.P > 0) {
-        ProfScope ps(cx, "ptgen", 8.0 * pl.P * 2 * D * (1 + nl));
-        k_ptgen<<<dim3(pl.P, nl), 256, 2 * D * 8, st>>>((const double*)pl.coef.p, spt, pts.p, nl, logD2, cx.d_tw,
-                                                        cx.d_twp, N, 1);
+        constexpr int IPC = 4;
+        const size_t smem = (size_t)IPC * 2 * D * 8;
+        if (smem > 48 * 1024)
+            CUDA_CHECK(cudaFuncSetAttribute(k_ptgen<IPC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        ProfScope ps(cx, "ptgen", 8.0 * pl.P * 2 * D * (1 + ne));
+        k_ptgen<IPC><<<dim3((pl.P + IPC - 1) / IPC, ne), 256, smem, st>>>(
+            (const double*)pl.coef.p, spt, pts.p, pl.P, nl, cx.L, logD2, cx.d_tw, cx.d_twp, N, 1);
         CUDA_CHECK(cudaGetLastError());
         cx.launches++;
     }
-    DevBuf inner((size_t)2 * G * 2 * nl * N, st);
+    DevBuf inner((size_t)M * 2 * ne * N, st);
     {
-        MacArgs a;
-        for (int s = 0; s < S; s++)
-            for (int k = 0; k < 2 * b1; k++) a.babies[(size_t)s * 2 * b1 + k] = sets[s]->cts[k].buf.p;
-        a.bstride = (long long)nl * N;
+        GemmArgs a{};
+        for (int s = 0; s < S; s++) a.babies[s] = sets[s]->pq.p;
         a.ids = (const int*)pl.d_ids.p;
         a.pts = pts.p;
         a.out = inner.p;
-        a.nsets = S; a.b1 = b1; a.G = G; a.nl = nl; a.logN = cx.logN; a.D2 = 2 * D;
-        int lr = 0;
-        while ((N >> lr) > 2 * D) lr++;
-        a.lr = lr;
-        const size_t smem = (size_t)2 * b1 * 2 * 64 * 8;
-        ProfScope ps(cx, "bsgs_mac", 8.0 * N * nl * (2.0 * S * 2 * b1 + 2.0 * 2 * G));
+        a.nsets = S; a.b1 = b1; a.G = G; a.nl = nl; a.ne = ne; a.L = cx.L; a.logN = cx.logN; a.lr = lr;
+        a.D2 = 2 * D; a.P = std::max(pl.P, 1); a.TW = TW;
+        const size_t smem = (size_t)kKc * (2 * TW + M) * 8;
         if (smem > 48 * 1024)
-            CUDA_CHECK(cudaFuncSetAttribute(k_bsgs_mac, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        k_bsgs_mac<<<dim3(N / 64, nl), 512, smem, st>>>(a);
+            CUDA_CHECK(cudaFuncSetAttribute(k_bsgs_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        ProfScope ps(cx, "bsgs_gemm", 8.0 * N * ne * (2.0 * S * 2 * b1 + 2.0 * M) + 8.0 * pl.P * ne * 2 * D);
+        k_bsgs_gemm<<<dim3(N / TW, ne), (TW / 2) * (M / 2), smem, st>>>(a);
         CUDA_CHECK(cudaGetLastError());
         cx.launches++;
     }
-    // giants: sum_g rot(IA_g, g b1) + rot(IB_g, g b1 - D)
+    // back to Q: one ModDown per giant input, then sum_g rot(IA_g, g b1) + rot(IB_g, g b1 - D)
     // (IA_0 unrotated; IB_0 is empty: rot(u, j) with j < b1 never needs the -D giant)
+    DevBuf innq((size_t)M * 2 * nl * N, st);
+    moddown_many(cx, inner.p, M, nl, innq.p);
     const double sc = sets[0]->scale * spt;
     std::vector<const uint64_t*> c0s, c1s;
     std::vector<int> steps;
     for (int g = 1; g < G; g++)
         for (int X = 0; X < 2; X++) {
-            const uint64_t* p = inner.p + (size_t)(X * G + g) * 2 * nl * N;
+            const uint64_t* p = innq.p + (size_t)(X * G + g) * 2 * nl * N;
             c0s.push_back(p);
             c1s.push_back(p + (size_t)nl * N);
             steps.push_back(X == 0 ? g * b1 : g * b1 - D);
         }
     Ciphertext acc;
-    rotate_sum(cx, c0s.data(), c1s.data(), steps.data(), (int)steps.size(), nl, sc, inner.p,
-               inner.p + (size_t)nl * N, acc);
+    rotate_sum(cx, c0s.data(), c1s.data(), steps.data(), (int)steps.size(), nl, sc, innq.p,
+               innq.p + (size_t)nl * N, acc);
     ct_rescale(cx, acc);
     acc.scale = target;
     out = std::move(acc);

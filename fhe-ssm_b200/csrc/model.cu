@@ -78,6 +78,7 @@ struct Model {
     }
     void refresh(Ciphertext& a, int need, double gain = 1.0) {
         if (a.nl - 1 >= need) return;
+        ProfScope op(cx, "op:refresh", 0);
         Ciphertext t;
         a.scale /= gain;   // the ciphertext now represents value * gain
         bootstrap(cx, a, t);
@@ -100,6 +101,7 @@ struct Model {
 
     // polynomial with per-channel coefficient vectors on a complex-packed ciphertext
     Ciphertext poly_complex(const Ciphertext& z, const std::vector<const std::vector<double>*>& coeffs, int off = 0) {
+        ProfScope op(cx, "op:poly", 0);
         Ciphertext re, im;
         split_complex(cx, z, re, im, true);
         std::vector<std::vector<std::complex<double>>> c(coeffs.size());
@@ -114,6 +116,7 @@ struct Model {
 
     // rmsnorm: x / sqrt(mean(x^2) + eps) * g per lane (rmsnorm, gpu_real_model.cu:3451-3657)
     Ciphertext rmsnorm(const Ciphertext& x0, const std::vector<double>& g, const NormSeed& sd) {
+        ProfScope op(cx, "op:rmsnorm", 0);
         const int D = cfg.D;
         Ciphertext x = ct_copy(cx, x0);
         refresh(x, 3, sd.gx);
