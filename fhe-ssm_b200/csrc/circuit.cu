@@ -199,6 +199,31 @@ void rotate_sum(Context& cx, const Ciphertext& a, int step, int count, Ciphertex
 // p(x) = sum_i c_i T_i(x) on a ciphertext x with |x| <= 1, by the recursive baby-step /
 // giant-step split p = q * T_{2^m} + r (Chebyshev division, T_i T_M = (T_{i+M} + T_{|i-M|})/2).
 // Depth ceil(log2(deg+1)) + 1.  The babies T_1..T_{bs-1} are aligned to one level first.
+// out = sum_t w_t . in_t over nl limbs and both polynomials, w_t a per-limb integer residue
+// (Shoup): the leaf combinations of the Chebyshev evaluation in one pass.  <= kLinMax terms,
+// each lazy product < 2q, so the sum stays below 16q.
+constexpr int kLinMax = 8;
+struct LinArgs {
+    const uint64_t* in[kLinMax];
+    long long stride[kLinMax];   // words between c0 and c1 of input t
+    uint64_t w[kLinMax][kMaxMod], wp[kLinMax][kMaxMod];
+    int nt;
+};
+__global__ void __launch_bounds__(256) k_lincomb(const LinArgs a, uint64_t* out, long long ostride, int logN) {
+    const int N = 1 << logN;
+    const int x = blockIdx.x * blockDim.x + threadIdx.x;
+    const int i = blockIdx.y, c = blockIdx.z;
+    const uint64_t q = c_mod[i].q;
+    uint64_t s = 0;
+#pragma unroll
+    for (int t = 0; t < kLinMax; t++) {
+        if (t >= a.nt) break;
+        const uint64_t v = a.in[t][(size_t)c * a.stride[t] + (size_t)i * N + x];
+        s += mul_shoup_lazy(v, a.w[t][i], a.wp[t][i], q);
+    }
+    out[(size_t)c * ostride + (size_t)i * N + x] = reduce_lazy16(s, q);
+}
+
 struct ChebEval {
     Context& cx;
     int bs;
@@ -262,17 +287,27 @@ struct ChebEval {
         const int nl = T[1].nl;
         const double target = canon(cx, nl - 1);
         const double tq = target * (double)cx.mods[nl - 1];
-        Ciphertext acc;
-        bool have = false;
+        LinArgs la{};
         for (int i = 1; i < (int)c.size() && i < bs; i++) {
             if (c[i] == 0.0) continue;
-            Ciphertext t;
-            mul_integer(cx, T[i], std::floor((long double)c[i] * (long double)(tq / T[i].scale) + 0.5L), t);
-            if (!have) { acc = std::move(t); have = true; }
-            else { Ciphertext u; ct_add_raw(cx, acc, t, u); acc = std::move(u); }
+            if (la.nt == kLinMax) throw Error("chebyshev: too many baby terms in one leaf", -1);
+            const int t = la.nt++;
+            la.in[t] = T[i].c(0);
+            la.stride[t] = (long long)T[i].stride;
+            limb_residues(cx, std::floor((long double)c[i] * (long double)(tq / T[i].scale) + 0.5L), nl, la.w[t]);
+            for (int l = 0; l < nl; l++) la.wp[t][l] = shoup_of(la.w[t][l], cx.mods[l]);
         }
-        if (!have) {   // constant-only leaf: 0 * T_1 keeps a valid ciphertext
-            mul_integer(cx, T[1], 0, acc);
+        if (la.nt == 0) {   // constant-only leaf: 0 * T_1 keeps a valid ciphertext
+            la.nt = 1;
+            la.in[0] = T[1].c(0);
+            la.stride[0] = (long long)T[1].stride;
+        }
+        Ciphertext acc = ct_alloc(cx, nl);
+        {
+            ProfScope ps(cx, "lincomb", 8.0 * cx.N * nl * 2 * (la.nt + 1));
+            k_lincomb<<<dim3(cx.N / 256, nl, 2), 256, 0, cx.stream>>>(la, acc.c(0), (long long)acc.stride, cx.logN);
+            CUDA_CHECK(cudaGetLastError());
+            cx.launches++;
         }
         acc.scale = tq;
         ct_rescale(cx, acc);

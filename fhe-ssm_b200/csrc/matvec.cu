@@ -159,13 +159,26 @@ struct GemmArgs {
 // both polynomials: out[o][c][x] = sum_k W[o][k] * baby[k][c][x] with W[o][k] the word of
 // family fam(o, k), giant g(o), baby j(k).  Thread (to, tn) owns outputs 2to, 2to+1 and the 4
 // columns 4tn..4tn+3 (column n = c * TW + slot).  Babies and plaintext words are staged in
-// shared memory kKc at a time; each product sum of <= kKc terms (< kKc q^2 < 2^126) is
-// Montgomery-reduced into a running sum mod q.
+// shared memory kKc at a time, split into 30-bit halves (words < q < 2^60): a b =
+// a0 b0 + (a0 b1 + a1 b0) 2^30 + a1 b1 2^60 with every partial product a 32x32->64-bit
+// multiply-add.  The three 64-bit partial sums absorb 8 terms (< 2^64) before they are folded
+// into a 128-bit sum; each chunk sum (< kKc q^2 < 2^127) is Montgomery-reduced (W carries the
+// factor 2^64) into a running sum mod q.
+__device__ __forceinline__ void fold128(u128acc& t, uint64_t s00, uint64_t smid, uint64_t s11) {
+    // t += s00 + smid 2^30 + s11 2^60
+    uint64_t lo = s00, hi = 0;
+    const uint64_t ml = smid << 30, mh = smid >> 34;
+    const uint64_t hl = s11 << 60, hh = s11 >> 4;
+    asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(lo), "+l"(hi) : "l"(ml), "l"(mh));
+    asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(lo), "+l"(hi) : "l"(hl), "l"(hh));
+    asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(t.lo), "+l"(t.hi) : "l"(lo), "l"(hi));
+}
+
 __global__ void __launch_bounds__(512) k_bsgs_gemm(const GemmArgs a) {
-    extern __shared__ uint64_t sm[];
+    extern __shared__ uint32_t sm32[];
     const int M = 2 * a.G, TW = a.TW, NC = 2 * TW;
-    uint64_t* Bs = sm;                    // [kKc][NC]
-    uint64_t* Ws = sm + (size_t)kKc * NC; // [kKc][M]
+    uint32_t* Bs = sm32;                        // [kKc][NC][2]  (lo30, hi30)
+    uint32_t* Ws = sm32 + (size_t)kKc * NC * 2; // [kKc][M][2]
     const int N = 1 << a.logN;
     const int e = blockIdx.y;
     const int x0 = blockIdx.x * TW;
@@ -176,6 +189,7 @@ __global__ void __launch_bounds__(512) k_bsgs_gemm(const GemmArgs a) {
     const int o0 = 2 * to, n0 = 4 * tn;
     const int ptw = x0 >> a.lr;
     const int K = 2 * a.b1;
+    constexpr uint64_t M30 = (1ull << 30) - 1;
     uint64_t sum[2][4];
 #pragma unroll
     for (int u = 0; u < 2; u++)
@@ -188,7 +202,9 @@ __global__ void __launch_bounds__(512) k_bsgs_gemm(const GemmArgs a) {
             __syncthreads();
             for (int t = tid; t < kc * NC; t += nth) {
                 const int kk = t / NC, n = t % NC, c = n / TW, xs = n % TW;
-                Bs[t] = bb[(((size_t)(k0 + kk) * 2 + c) * a.ne + e) * N + x0 + xs];
+                const uint64_t v = bb[(((size_t)(k0 + kk) * 2 + c) * a.ne + e) * N + x0 + xs];
+                Bs[2 * t] = (uint32_t)(v & M30);
+                Bs[2 * t + 1] = (uint32_t)(v >> 30);
             }
             for (int t = tid; t < kc * M; t += nth) {
                 const int kk = t / M, o = t % M;
@@ -197,28 +213,46 @@ __global__ void __launch_bounds__(512) k_bsgs_gemm(const GemmArgs a) {
                 const int fam = X == 0 ? Y : (Y == 0 ? 2 : -1);
                 int id = -1;
                 if (fam >= 0) id = a.ids[(((size_t)s * 3 + fam) * a.G + g) * a.b1 + j];
-                Ws[t] = id < 0 ? 0 : a.pts[((size_t)e * a.D2 + ptw) * a.P + id];
+                const uint64_t v = id < 0 ? 0 : a.pts[((size_t)e * a.D2 + ptw) * a.P + id];
+                Ws[2 * t] = (uint32_t)(v & M30);
+                Ws[2 * t + 1] = (uint32_t)(v >> 30);
             }
             __syncthreads();
-            u128acc acc[2][4];
-#pragma unroll
-            for (int u = 0; u < 2; u++)
-#pragma unroll
-                for (int v = 0; v < 4; v++) acc[u][v] = u128acc{0, 0};
             // outputs IB (o >= G) have no products with the babies rot(u, j - D) (k >= b1):
             // those warps stop early (the split is warp-uniform)
             const int kend = o0 >= a.G ? max(0, min(kc, a.b1 - k0)) : kc;
-            for (int kk = 0; kk < kend; kk++) {
-                const ulonglong2 wv = *reinterpret_cast<const ulonglong2*>(Ws + kk * M + o0);
-                const ulonglong2* br = reinterpret_cast<const ulonglong2*>(Bs + (size_t)kk * NC + n0);
-                const ulonglong2 b01 = br[0], b23 = br[1];
-                const uint64_t w0 = wv.x, w1 = wv.y;
-                const uint64_t bv[4] = {b01.x, b01.y, b23.x, b23.y};
+            u128acc tot[2][4];
 #pragma unroll
-                for (int v = 0; v < 4; v++) {
-                    acc_mad(acc[0][v], w0, bv[v]);
-                    acc_mad(acc[1][v], w1, bv[v]);
+            for (int u = 0; u < 2; u++)
+#pragma unroll
+                for (int v = 0; v < 4; v++) tot[u][v] = u128acc{0, 0};
+            for (int kb = 0; kb < kend; kb += 8) {
+                uint64_t s00[2][4], smd[2][4], s11[2][4];
+#pragma unroll
+                for (int u = 0; u < 2; u++)
+#pragma unroll
+                    for (int v = 0; v < 4; v++) s00[u][v] = smd[u][v] = s11[u][v] = 0;
+                const int ke = min(kend, kb + 8);
+                for (int kk = kb; kk < ke; kk++) {
+                    const uint4 wv = *reinterpret_cast<const uint4*>(Ws + (size_t)(kk * M + o0) * 2);
+                    const uint4 bA = *reinterpret_cast<const uint4*>(Bs + (size_t)(kk * NC + n0) * 2);
+                    const uint4 bB = *reinterpret_cast<const uint4*>(Bs + (size_t)(kk * NC + n0) * 2 + 4);
+                    const uint32_t w0[2] = {wv.x, wv.z}, w1[2] = {wv.y, wv.w};
+                    const uint32_t b0[4] = {bA.x, bA.z, bB.x, bB.z}, b1[4] = {bA.y, bA.w, bB.y, bB.w};
+#pragma unroll
+                    for (int u = 0; u < 2; u++)
+#pragma unroll
+                        for (int v = 0; v < 4; v++) {
+                            s00[u][v] += (uint64_t)w0[u] * b0[v];
+                            smd[u][v] += (uint64_t)w0[u] * b1[v];
+                            smd[u][v] += (uint64_t)w1[u] * b0[v];
+                            s11[u][v] += (uint64_t)w1[u] * b1[v];
+                        }
                 }
+#pragma unroll
+                for (int u = 0; u < 2; u++)
+#pragma unroll
+                    for (int v = 0; v < 4; v++) fold128(tot[u][v], s00[u][v], smd[u][v], s11[u][v]);
             }
 #pragma unroll
             for (int u = 0; u < 2; u++)
@@ -226,10 +260,10 @@ __global__ void __launch_bounds__(512) k_bsgs_gemm(const GemmArgs a) {
                 for (int v = 0; v < 4; v++) {
                     // <= 64 products of words < q < 2^60: hi < 64 q^2 / 2^64 < 4q; bring it below q
                     // (T changes by a multiple of q 2^64) before the Montgomery step
-                    uint64_t hi = acc[u][v].hi;
+                    uint64_t hi = tot[u][v].hi;
                     if (hi >= 2 * mc.q) hi -= 2 * mc.q;
                     if (hi >= mc.q) hi -= mc.q;
-                    sum[u][v] = mod_add(sum[u][v], redc(hi, acc[u][v].lo, mc), mc.q);
+                    sum[u][v] = mod_add(sum[u][v], redc(hi, tot[u][v].lo, mc), mc.q);
                 }
         }
     }
