@@ -121,13 +121,26 @@ def barrier(ws):
 
 
 def max_over_ranks(v, ws):
+    """The slowest rank's time: the whole job's step time for `value`."""
     if ws == 1:
         return v
     import torch
     import torch.distributed as dist
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def pack_seeds(rank):
+    """Rank r owns its own pack of conversations: its own keys and token stream (no data
+    crosses ranks; the packs are independent units of work)."""
+    return 1 + rank, 100 + rank
+
+
+def aggregate_tokens_per_s(lanes, ws, steps, ms_max):
+    """Whole-job throughput: every rank advanced `lanes` conversations per step."""
+    return lanes * ws * steps / (ms_max / 1000.0)
 
 
 def rand_ct_words(rng, moduli, nl, N):
@@ -212,12 +225,13 @@ def run_model(args, ws, rank, local):
     w = synthetic_weights(cfg, seed=1234)
     seeds = calibrate_seeds(cfg, w, steps=6, lanes=LANES)
     cx = fhessm.CryptoContext(device=local, **MODEL_CTX)
-    cx.KeyGen(seed=1 + rank)
+    key_seed, tok_seed = pack_seeds(rank)
+    cx.KeyGen(seed=key_seed)
     cx.EvalBootstrapSetup(24.0, 59)
     m = EncryptedModel(cx, cfg, w, seeds)
     m.keygen()
     in_level = MODEL_CTX["boot_primes"]   # the top of the user region
-    rng = np.random.default_rng(100 + rank)
+    rng = np.random.default_rng(tok_seed)
     nsteps = args.warmup + args.steps
     toks = [rng.integers(0, cfg.vocab, LANES) for _ in range(nsteps + 1)]
     cts = [cx.Encrypt(cx.MakeCKKSPackedPlaintext(pack_lanes(w["emb"][t], cfg.D, cx.slots), level=in_level))
@@ -257,7 +271,7 @@ def run_model(args, ws, rank, local):
     ks_per_pass = (k1[0] - k0[0]) / args.steps
     ks_nl_avg = (k1[1] - k0[1]) / max(1, k1[0] - k0[0])
     ms_max = max_over_ranks(ms, ws)
-    value = LANES * ws * args.steps / (ms_max / 1000.0)
+    value = aggregate_tokens_per_s(LANES, ws, args.steps, ms_max)
 
     # fidelity against the float64 model (exact 1/sqrt), replaying every step from a cold state
     state, errs, top1 = None, [], []

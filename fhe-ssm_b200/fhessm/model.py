@@ -37,7 +37,7 @@ class ModelConfig:
     shift_mix: bool = True
 
 
-CONFIG_405M = ModelConfig()
+CONFIG_405M = ModelConfig(b1=64)   # double-hoisted BSGS: 127 babies, 30 giants per 1024x1024 block
 
 
 def synthetic_weights(cfg: ModelConfig, seed: int = 1234):
