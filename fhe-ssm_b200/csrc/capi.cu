@@ -88,6 +88,14 @@ int fhe_ctx_sync(fhe_ctx* cx) {
         REQUIRE(cx, "null argument");
         bind(cx);
         CUDA_CHECK(cudaStreamSynchronize(cx->cx.stream));
+        cx->cx.check_device_error();
+    });
+}
+int fhe_ctx_set_option(fhe_ctx* cx, const char* name, int value) {
+    return guard([&] {
+        REQUIRE(cx && name, "null argument");
+        if (std::strcmp(name, "matvec_tensor_cores") == 0) cx->cx.use_tc = value != 0;
+        else throw fhe::Error(std::string("unknown option ") + name, FHE_ERR_ARG);
     });
 }
 long long fhe_ctx_launches(const fhe_ctx* cx) { return cx ? cx->cx.launches : 0; }
@@ -552,6 +560,12 @@ int fhe_model_stats(const fhe_model* m, long long* bootstraps, long long* steps)
         REQUIRE(m, "null argument");
         if (bootstraps) *bootstraps = m->m->boots;
         if (steps) *steps = m->m->steps;
+    });
+}
+int fhe_model_refresh_census(const fhe_model* m, long long* counts, int n) {
+    return guard([&] {
+        REQUIRE(m && counts && n >= 0, "null argument");
+        for (int i = 0; i < n; i++) counts[i] = i < fhe::Model::kSites ? m->m->site_boots[i] : 0;
     });
 }
 int fhe_model_probe(fhe_model* m, int k) {

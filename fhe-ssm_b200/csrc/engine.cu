@@ -179,6 +179,8 @@ Context::Context(const Params& p) : prm(p) {
         uint64_t keep = UINT64_MAX;
         CUDA_CHECK(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
     }
+    CUDA_CHECK(cudaMalloc((void**)&d_err, sizeof(unsigned int)));
+    CUDA_CHECK(cudaMemset(d_err, 0, sizeof(unsigned int)));
     gen_chain(logN, L, p.q0bits, p.qbits, K, p.pbits, p.boot_primes, p.boot_bits, mods);
     const int nm = L + K;
     mc.resize(nm);
@@ -266,6 +268,7 @@ Context::~Context() {
     pk = DevBuf();
     if (stream) cudaStreamSynchronize(stream);
     for (auto* p : {d_tw, d_twp, d_itw, d_itwp, d_ninv, d_md, d_rs}) if (p) cudaFree(p);
+    if (d_err) cudaFree(d_err);
     for (auto& kv : modup_tab) cudaFree(kv.second);
     if (stream) cudaStreamDestroy(stream);
 }
@@ -892,6 +895,17 @@ void upload(Context& cx, uint64_t* dst, const uint64_t* src, size_t words) {
 void download(Context& cx, uint64_t* dst, const uint64_t* src, size_t words) {
     CUDA_CHECK(cudaMemcpyAsync(dst, src, words * 8, cudaMemcpyDeviceToHost, cx.stream));
     CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+    cx.check_device_error();
+}
+// A kernel whose bounded wait ran out left its flag: report it (the results of the work in
+// flight since the last check are not trustworthy) and clear it.
+void Context::check_device_error() {
+    unsigned int f = 0;
+    CUDA_CHECK(cudaMemcpy(&f, d_err, sizeof f, cudaMemcpyDeviceToHost));
+    if (f) {
+        CUDA_CHECK(cudaMemset(d_err, 0, sizeof f));
+        throw Error("a tensor-core wait ran out of iterations (results since the last sync are invalid)", -3);
+    }
 }
 void key_to_mont(Context& cx, uint64_t* key, bool to_mont) {
     const int nm = cx.L + cx.K;

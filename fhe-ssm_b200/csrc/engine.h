@@ -120,6 +120,8 @@ struct Context {
     // ModDown / rescale constants (level independent): see build_tables()
     uint64_t* d_md = nullptr;        // ModDown: [K] phatinv (+shoup), [L][K] phat mod q_i (+shoup), [L] Pinv (+shoup)
     uint64_t* d_rs = nullptr;        // rescale: [L][L] (ql mod qi, ql^-1 mod qi, shoup)
+    unsigned int* d_err = nullptr;   // set by a kernel whose bounded wait ran out (checked at syncs)
+    int use_tc = 1;                  // BSGS products on the tensor cores (tcgen05) where the shape allows
     std::map<int, uint64_t*> modup_tab;   // per nl: [dnum][alpha][2] qhat^-1, [dnum][ne][alpha][2] qhat mod t
     // keys
     DevBuf sk;                       // secret, eval form over all L+K moduli, [L+K][N]
@@ -138,6 +140,7 @@ struct Context {
         double ms = 0.0, bytes = 0.0;
     };
     bool prof = false;
+    void check_device_error();
     mutable std::map<std::string, ProfEntry> prof_acc;
     std::unique_ptr<Plaintext> pt_i;         // NTT of X^{N/2}: multiplication by i
     std::map<uint64_t, std::shared_ptr<Plaintext>> ptcache;   // encode_cached: (content, level, scale)

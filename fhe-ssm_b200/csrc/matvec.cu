@@ -276,6 +276,8 @@ __global__ void __launch_bounds__(512) k_bsgs_gemm(const GemmArgs a) {
         }
 }
 
+#include "tc_gemm.cuh"   // (inside namespace fhe)
+
 // Babies in QP: out[b] = P rot(u, r_b), i.e. c0 = tau(ip0) + P tau(u0), c1 = tau(ip1) with
 // ip = <ModUp(u1), key_b> evaluated at the permuted slots of the shared ModUp output `ext`
 // against the rotate-then-switch key (fkey[x] = key[auto_src(x)]); perm == 1: P u.
@@ -558,11 +560,29 @@ void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets,
         a.out = inner.p;
         a.nsets = S; a.b1 = b1; a.G = G; a.nl = nl; a.ne = ne; a.L = cx.L; a.logN = cx.logN; a.lr = lr;
         a.D2 = 2 * D; a.P = std::max(pl.P, 1); a.TW = TW;
-        const size_t smem = (size_t)kKc * (2 * TW + M) * 8;
-        if (smem > 48 * 1024)
-            CUDA_CHECK(cudaFuncSetAttribute(k_bsgs_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        ProfScope ps(cx, "bsgs_gemm", 8.0 * N * ne * (2.0 * S * 2 * b1 + 2.0 * M) + 8.0 * pl.P * ne * 2 * D);
-        k_bsgs_gemm<<<dim3(N / TW, ne), (TW / 2) * (M / 2), smem, st>>>(a);
+        const double bytes = 8.0 * N * ne * (2.0 * S * 2 * b1 + 2.0 * M) + 8.0 * pl.P * ne * 2 * D;
+        if (cx.use_tc && TW == 32 && (M == 16 || M == 32 || M == 64)) {
+            // tensor cores: 8 accumulator tiles of M columns; a 512-column tile takes all of an
+            // SM's tensor memory, so its CTAs ask for enough shared memory to run one per SM
+            const int Kp = (2 * b1 + 31) / 32 * 32;
+            const uint32_t tcols = M == 16 ? 128u : M == 32 ? 256u : 512u;
+            size_t smem = tc_smem_bytes(M, Kp);
+            if (tcols == 512) smem = std::max<size_t>(smem, 120 * 1024);
+            ProfScope ps(cx, "bsgs_tc", bytes);
+            auto launch = [&](auto kern) {
+                CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+                kern<<<dim3(N / 32, ne), kTcThreads, smem, st>>>(a, Kp, tcols, cx.d_err);
+            };
+            if (M == 16) launch(k_bsgs_tc<16>);
+            else if (M == 32) launch(k_bsgs_tc<32>);
+            else launch(k_bsgs_tc<64>);
+        } else {
+            const size_t smem = (size_t)kKc * (2 * TW + M) * 8;
+            if (smem > 48 * 1024)
+                CUDA_CHECK(cudaFuncSetAttribute(k_bsgs_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            ProfScope ps(cx, "bsgs_gemm", bytes);
+            k_bsgs_gemm<<<dim3(N / TW, ne), (TW / 2) * (M / 2), smem, st>>>(a);
+        }
         CUDA_CHECK(cudaGetLastError());
         cx.launches++;
     }

@@ -76,8 +76,12 @@ struct Model {
         for (int i = 0; i < cfg.D && off + i < (int)v.size(); i++) z[i] = v[off + i];
         return z;
     }
-    void refresh(Ciphertext& a, int need, double gain = 1.0) {
+    // refresh sites (bootstrap census, fhe_model_refresh_census)
+    enum Site { kNormX, kNormMs, kNormY, kNormM, kNormTail, kXn, kUp, kU, kSp, kSnew, kZ, kG, kV, kF, kSites };
+    long long site_boots[kSites] = {};
+    void refresh(Ciphertext& a, int need, double gain, Site site) {
         if (a.nl - 1 >= need) return;
+        site_boots[site]++;
         ProfScope op(cx, "op:refresh", 0);
         Ciphertext t;
         a.scale /= gain;   // the ciphertext now represents value * gain
@@ -119,7 +123,7 @@ struct Model {
         ProfScope op(cx, "op:rmsnorm", 0);
         const int D = cfg.D;
         Ciphertext x = ct_copy(cx, x0);
-        refresh(x, 3, sd.gx);
+        refresh(x, 3, sd.gx, kNormX);
         Ciphertext xr, xi;
         split_complex(cx, x, xr, xi, true);
         Ciphertext sr, si, sq;
@@ -141,7 +145,7 @@ struct Model {
             ms = std::move(e);
         }
         const int maxlv = bootstrap_levels_after(cx) - 1;
-        refresh(ms, std::min(2 + 2 * sd.iters, maxlv), sd.gms);
+        refresh(ms, std::min(2 + 2 * sd.iters, maxlv), sd.gms, kNormMs);
         // the Newton chain runs on complex-packed (y, -ms/2) pairs: seed and iterations act on
         // the real and imaginary parts separately, and a pair that runs out of levels between
         // iterations is merged and bootstrapped once (one bootstrap serves both parts)
@@ -161,8 +165,8 @@ struct Model {
                 merge_complex(cx, std::move(yp[0]), std::move(yp[1]), yc);
                 merge_complex(cx, std::move(mh[0]), std::move(mh[1]), mc);
                 const int rest = 2 * (sd.iters - it) + 1;
-                refresh(yc, std::min(rest, maxlv), sd.gy);
-                refresh(mc, std::min(rest, maxlv), sd.gms * 2);
+                refresh(yc, std::min(rest, maxlv), sd.gy, kNormY);
+                refresh(mc, std::min(rest, maxlv), sd.gms * 2, kNormM);
                 split_complex(cx, yc, yp[0], yp[1], true);
                 split_complex(cx, mc, mh[0], mh[1], true);
             }
@@ -181,7 +185,7 @@ struct Model {
         if (yp[0].nl < 2) {
             Ciphertext yc;
             merge_complex(cx, std::move(yp[0]), std::move(yp[1]), yc);
-            refresh(yc, 1, sd.gy);
+            refresh(yc, 1, sd.gy, kNormTail);
             split_complex(cx, yc, yp[0], yp[1], true);
         }
         Ciphertext xgr = mulv(xr, g), xgi = mulv(xi, g);
@@ -213,10 +217,10 @@ struct Model {
             if (cfg.shift_mix) {
                 std::vector<double> om(P.mix.size());
                 for (size_t i = 0; i < om.size(); i++) om[i] = 1.0 - P.mix[i];
-                refresh(xn, 1, P.g_u);
+                refresh(xn, 1, P.g_u, kXn);
                 Ciphertext a = mulv(xn, P.mix);
                 if (have_state) {
-                    refresh(up[l], 1, P.g_u);
+                    refresh(up[l], 1, P.g_u, kUp);
                     Ciphertext b = mulv(up[l], om);
                     u = addc(a, b);
                 } else {
@@ -227,7 +231,7 @@ struct Model {
                 u = std::move(xn);
             }
             FHE_PROBE(2, u)
-            refresh(u, 7, P.g_u);
+            refresh(u, 7, P.g_u, kU);
             Ciphertext x;
             {
                 const Ciphertext* in[1] = {&u};
@@ -237,7 +241,7 @@ struct Model {
             Ciphertext bx = mulv(x, P.bco), snew;
             if (have_state) {
                 Ciphertext sp = ct_copy(cx, s[l]);
-                refresh(sp, 1, P.g_s);
+                refresh(sp, 1, P.g_s, kSp);
                 Ciphertext as = mulv(sp, P.decay);
                 snew = addc(as, bx);
             } else {
@@ -245,17 +249,17 @@ struct Model {
             }
             // the carried state loses a level per step: refresh it (and keep the refreshed copy
             // as the carry) when the readout z could not cover the gate polynomial
-            refresh(snew, 5, P.g_s);
+            refresh(snew, 5, P.g_s, kSnew);
             s[l] = ct_copy(cx, snew);
             FHE_PROBE(4, snew)
             Ciphertext cs = mulv(snew, P.c), dx = mulv(x, P.dd);
             Ciphertext z = addc(cs, dx);
-            refresh(z, 4, P.g_z);
+            refresh(z, 4, P.g_z, kZ);
             FHE_PROBE(5, z)
             std::vector<double> zero(cfg.d, 0.0);
             Ciphertext g = poly_complex(z, {&zero, &P.p0, &P.p1, &P.p2});
             FHE_PROBE(6, g)
-            refresh(g, 1, P.g_g);
+            refresh(g, 1, P.g_g, kG);
             Ciphertext attn;
             {
                 const Ciphertext* in[1] = {&g};
@@ -271,7 +275,7 @@ struct Model {
             // ---- channel mix
             Ciphertext v = rmsnorm(h, P.g2, P.cm);
             FHE_PROBE(8, v)
-            refresh(v, 6, P.g_v);
+            refresh(v, 6, P.g_v, kV);
             BabySet bs;
             matvec_babies(cx, v, cfg.D, cfg.b1, bs);
             const BabySet* bsp[1] = {&bs};
@@ -298,7 +302,7 @@ struct Model {
             for (int ch = 0; ch < C; ch++)
                 if (f[ch].nl > f[lo].nl) align(cx, f[ch], f[lo].nl, f[lo].scale);
             if (f[0].nl < 2)
-                for (auto& c : f) refresh(c, 1, P.g_f);
+                for (auto& c : f) refresh(c, 1, P.g_f, kF);
             std::vector<const Ciphertext*> fin(C);
             for (int ch = 0; ch < C; ch++) fin[ch] = &f[ch];
             FHE_PROBE(12, f[C - 1])

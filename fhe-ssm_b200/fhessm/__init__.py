@@ -76,6 +76,7 @@ _SIGS = {
     "fhe_rotate": (C.c_int, [_VP, _VP, C.c_int32, C.POINTER(_VP)]),
     "fhe_rotate_hoisted": (C.c_int, [_VP, _VP, C.POINTER(C.c_int32), C.c_int, C.POINTER(_VP)]),
     "fhe_rotate_sum": (C.c_int, [_VP, C.POINTER(_VP), C.POINTER(C.c_int32), C.c_int, C.POINTER(_VP)]),
+    "fhe_ctx_set_option": (C.c_int, [_VP, C.c_char_p, C.c_int]),
     "fhe_conjugate": (C.c_int, [_VP, _VP, C.POINTER(_VP)]),
     "fhe_mul_vec_rescale": (C.c_int, [_VP, _VP, _DP, _DP, C.c_int, C.POINTER(_VP)]),
     "fhe_align": (C.c_int, [_VP, _VP, C.c_int]),
@@ -226,6 +227,10 @@ class CryptoContext:
         k, l = C.c_longlong(), C.c_longlong()
         _check(h.fhe_ctx_counters(self.h, C.byref(k), C.byref(l)))
         return k.value, l.value
+
+    def set_option(self, name, value):
+        """Engine switches: "matvec_tensor_cores" (1 = tcgen05 BSGS products, 0 = CUDA cores)."""
+        _check(lib().fhe_ctx_set_option(self.h, name.encode(), int(value)))
 
     def stream_ptr(self):
         """The engine's cudaStream_t (an int), e.g. for torch.cuda.ExternalStream."""

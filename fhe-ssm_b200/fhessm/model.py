@@ -287,6 +287,19 @@ class EncryptedModel:
         _check(lib().fhe_model_stats(self.h, C.byref(b), C.byref(s)))
         return {"bootstraps": b.value, "steps": s.value}
 
+    REFRESH_SITES = ("norm.x", "norm.ms", "norm.y", "norm.m", "norm.tail", "shift.xn", "shift.up", "u", "s.prev",
+                     "s.new", "z", "g", "v", "f")
+
+    def refresh_census(self):
+        """Bootstraps per refresh site since the model was created."""
+        n = len(self.REFRESH_SITES)
+        arr = (C.c_longlong * n)()
+        h = lib()
+        h.fhe_model_refresh_census.restype = C.c_int
+        h.fhe_model_refresh_census.argtypes = [C.c_void_p, C.POINTER(C.c_longlong), C.c_int]
+        _check(h.fhe_model_refresh_census(self.h, arr, n))
+        return dict(zip(self.REFRESH_SITES, list(arr)))
+
     def __del__(self):
         if getattr(self, "h", None):
             lib().fhe_model_free(self.h)

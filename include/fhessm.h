@@ -73,6 +73,9 @@ long long fhe_ctx_launches(const fhe_ctx* cx);
 int fhe_ctx_counters(const fhe_ctx* cx, long long* keyswitches, long long* ks_limbs);
 /* the context's CUDA stream (cudaStream_t), for callers that time it with CUDA events */
 void* fhe_ctx_stream(const fhe_ctx* cx);
+/* engine options: "matvec_tensor_cores" (default 1): BSGS products on the tcgen05 tensor cores
+ * (byte-split integer MMA); 0 selects the CUDA-core kernel (same results, bit for bit) */
+int fhe_ctx_set_option(fhe_ctx* cx, const char* name, int value);
 /* per-kernel CUDA-event timing on the context's stream (off by default).  collect
  * synchronises, writes {"kernel": [launches, total_ms, algorithmic_bytes], ...} as JSON
  * into buf (cap bytes) and resets the counters. */
@@ -210,6 +213,11 @@ int fhe_model_reset(fhe_model* m);
  * the tied head in plaintext, --dec-out :2444-2533) */
 int fhe_model_step(fhe_model* m, const fhe_ct* in, fhe_ct** out);
 int fhe_model_stats(const fhe_model* m, long long* bootstraps, long long* steps);
+/* bootstraps per refresh site since creation (the refresh rule of gpu_real_model.cu:2573-2599):
+ * 0 norm input x, 1 norm mean square, 2 norm Newton y, 3 norm Newton -ms/2, 4 norm tail y,
+ * 5 shift-mix input, 6 previous u, 7 matvec input u, 8 carried state, 9 new state, 10 readout
+ * z, 11 gate output, 12 channel-mix input v, 13 channel-mix product f */
+int fhe_model_refresh_census(const fhe_model* m, long long* counts, int n);
 /* diagnostics: k > 0 makes fhe_model_step return the layer-0 intermediate k (1 norm,
  * 2 shift-mix, 3 Win x, 4 scan, 5 readout, 6 gate, 7 h+attn, 8 norm 2, 9 k_0, 10 f_0, 11 h+ffn) */
 int fhe_model_probe(fhe_model* m, int k);

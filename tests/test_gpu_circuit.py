@@ -130,6 +130,29 @@ def test_matvec_bsgs_lanes(cx, rows, cols):
     assert np.abs(ref[0] - ref[1]).max() > 1e-2        # lanes genuinely differ (no-bleed is meaningful)
 
 
+@pytest.mark.parametrize("b1", [4, 8, 16])
+def test_matvec_tensor_core_products_bit_identical(cx, b1):
+    """The tcgen05 byte-split product kernel and the CUDA-core kernel give the same words
+    (D = 128: 2 D / b1 = 64, 32, 16 outputs per product, all three tensor-core shapes)."""
+    D = 128
+    cx.matvec_keygen(D, b1)
+    rng = np.random.default_rng(11 + b1)
+    W = rng.normal(0, 0.3, (D, 2 * D))
+    R = cx.slots // D
+    U = rng.uniform(-1, 1, (2 * R, 2 * D))
+    ins = [cx.Encrypt(cx.MakeCKKSPackedPlaintext(block_pack(U[:, s * D:(s + 1) * D], D, cx.slots), level=1))
+           for s in range(2)]
+    plan = cx.matvec_plan(W, D, b1)
+    out = {}
+    for tc in (0, 1):
+        cx.set_option("matvec_tensor_cores", tc)
+        out[tc] = cx.matvec(plan, ins).words()
+    cx.set_option("matvec_tensor_cores", 1)
+    assert (out[0] == out[1]).all()
+    got = block_unpack(cx.Decrypt(cx.matvec(plan, ins)), D, 2 * R, D)
+    assert np.abs(got - U @ W.T).max() < 1e-5
+
+
 @pytest.mark.parametrize("logN,L", [(13, 22)])
 def test_bootstrap_small_ring(logN, L):
     boot_check(logN, L, tol=5e-3)
