@@ -434,7 +434,9 @@ std::vector<int> matvec_rotations(int D, int b1) {
 struct BabySet {
     int D = 0, b1 = 0, nl = 0;
     double scale = 0;
-    DevBuf pq;   // [2 b1][2][nl + K][N]
+    DevBuf pq;              // [2 b1][2][nl + K][N]
+    mutable DevBuf split;   // tensor-core image: [nl + K][N/32][8 byte slices][64 Kp] (built on first use)
+    mutable int split_Kp = 0;
 };
 
 void matvec_babies(Context& cx, const Ciphertext& u, int D, int b1, BabySet& bs) {
@@ -562,20 +564,58 @@ void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets,
         a.D2 = 2 * D; a.P = std::max(pl.P, 1); a.TW = TW;
         const double bytes = 8.0 * N * ne * (2.0 * S * 2 * b1 + 2.0 * M) + 8.0 * pl.P * ne * 2 * D;
         if (cx.use_tc && TW == 32 && (M == 16 || M == 32 || M == 64)) {
-            // tensor cores: 8 accumulator tiles of M columns; a 512-column tile takes all of an
-            // SM's tensor memory, so its CTAs ask for enough shared memory to run one per SM
+            // tensor cores: babies split into byte slices once per baby set, plaintext words packed
+            // per call, both in the shared-memory image the product kernel bulk-copies.  8
+            // accumulator tiles of M columns; a 512-column tile takes all of an SM's tensor
+            // memory, so its CTAs ask for enough shared memory to run one per SM.
             const int Kp = (2 * b1 + 31) / 32 * 32;
+            const int R = N / 32;
             const uint32_t tcols = M == 16 ? 128u : M == 32 ? 256u : 512u;
+            Tc2Args t{};
+            for (int s = 0; s < S; s++) {
+                const BabySet& b = *sets[s];
+                if (!b.split.p || b.split_Kp != Kp) {
+                    const size_t bytes = (size_t)ne * R * 8 * 64 * Kp;
+                    b.split = DevBuf(bytes / 8, st);
+                    b.split_Kp = Kp;
+                    const size_t sm = (size_t)8 * 64 * Kp;
+                    if (sm > 48 * 1024)
+                        CUDA_CHECK(cudaFuncSetAttribute(k_tc_split_babies, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+                    ProfScope ps(cx, "tc_split", 2.0 * bytes);
+                    k_tc_split_babies<<<dim3(R, ne), 256, sm, st>>>(b.pq.p, (uint8_t*)b.split.p, 2 * b1, Kp, ne, cx.logN);
+                    CUDA_CHECK(cudaGetLastError());
+                    cx.launches++;
+                }
+                t.bsplit[s] = (const uint8_t*)b.split.p;
+            }
+            const size_t wblk = (size_t)8 * M * Kp;
+            DevBuf wpack((size_t)S * ne * 2 * D * wblk / 8, st);
+            {
+                if (wblk > 48 * 1024)
+                    CUDA_CHECK(cudaFuncSetAttribute(k_tc_pack_w, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wblk));
+                ProfScope ps(cx, "tc_pack_w", (double)S * ne * 2 * D * wblk + 8.0 * pl.P * ne * 2 * D);
+                for (int s = 0; s < S; s++) {
+                    k_tc_pack_w<<<dim3(2 * D, ne), 256, wblk, st>>>(pts.p, (const int*)pl.d_ids.p,
+                                                                  (uint8_t*)wpack.p + (size_t)s * ne * 2 * D * wblk, s, G,
+                                                                  b1, Kp, M, 2 * D, std::max(pl.P, 1));
+                    cx.launches++;
+                }
+                CUDA_CHECK(cudaGetLastError());
+            }
+            t.wpack = (const uint8_t*)wpack.p;
+            t.out = inner.p;
+            t.nsets = S; t.G = G; t.nl = nl; t.ne = ne; t.L = cx.L; t.logN = cx.logN; t.lr = lr; t.D2 = 2 * D;
+            t.Kp = Kp;
             size_t smem = tc_smem_bytes(M, Kp);
             if (tcols == 512) smem = std::max<size_t>(smem, 120 * 1024);
             ProfScope ps(cx, "bsgs_tc", bytes);
             auto launch = [&](auto kern) {
                 CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-                kern<<<dim3(N / 32, ne), kTcThreads, smem, st>>>(a, Kp, tcols, cx.d_err);
+                kern<<<dim3(R, ne), kTcThreads, smem, st>>>(t, tcols, cx.d_err);
             };
-            if (M == 16) launch(k_bsgs_tc<16>);
-            else if (M == 32) launch(k_bsgs_tc<32>);
-            else launch(k_bsgs_tc<64>);
+            if (M == 16) launch(k_bsgs_tc2<16>);
+            else if (M == 32) launch(k_bsgs_tc2<32>);
+            else launch(k_bsgs_tc2<64>);
         } else {
             const size_t smem = (size_t)kKc * (2 * TW + M) * 8;
             if (smem > 48 * 1024)

@@ -60,39 +60,134 @@ __device__ __forceinline__ void tc_ld8(uint32_t taddr, uint32_t* v) {
                  : "r"(taddr));
 }
 
-// Shared memory (dynamic, bytes): [Mside: 10 slices x 64 Kp][Nside: 8 slices x MP Kp][barrier 8]
-// [tmem address 4].  Slices 0..7 of the M side double as the epilogue exchange buffer.
+// Shared memory of k_bsgs_tc2 (dynamic, bytes): [M side: 10 slices x 64 Kp][N side: 8 slices x
+// MP Kp][2 barriers][tmem address].  Slices 0..7 of the M side double as the epilogue exchange buffer.
 __host__ __device__ inline size_t tc_smem_bytes(int Mp, int Kp) {
-    return (size_t)10 * 64 * Kp + (size_t)8 * Mp * Kp + 16;
+    return (size_t)10 * 64 * Kp + (size_t)8 * Mp * Kp + 24;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Operands packed in global memory as the exact shared-memory image of a tile, so that the
+// product kernel only issues bulk copies (cp.async.bulk, completion counted on an mbarrier).
+
+// Babies of one set -> per (limb e, group r of 32 slots) a block of byte slices 0..7, each 64
+// rows (n = c * 32 + slot) x Kp bytes (k), K-major core-matrix order.  One CTA per (r, e); the
+// block is assembled in shared memory and written with 16-byte stores.
+__global__ void __launch_bounds__(256) k_tc_split_babies(const uint64_t* __restrict__ bb, uint8_t* __restrict__ out,
+                                                         int K, int Kp, int ne, int logN) {
+    extern __shared__ __align__(16) uint8_t ss[];   // [8][64 Kp]
+    const int N = 1 << logN;
+    const int r = blockIdx.x, e = blockIdx.y, x0 = r * 32;
+    const uint32_t SB = 8u * Kp;
+    for (int t = threadIdx.x; t < 64 * (Kp / 4); t += blockDim.x) {
+        const int n = t & 63, k4 = t >> 6, c = n >> 5, xs = n & 31;
+        uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int k = 4 * k4 + u;
+            if (k < K) {
+                const uint64_t v = bb[(((size_t)k * 2 + c) * ne + e) * N + x0 + xs];
+#pragma unroll
+                for (int b = 0; b < 8; b++) w[b] |= (uint32_t)((v >> (8 * b)) & 0xFF) << (8 * u);
+            }
+        }
+        const int k = 4 * k4;
+        const size_t off = (size_t)(n >> 3) * SB + (size_t)(k >> 4) * 128 + (size_t)(n & 7) * 16 + (k & 15);
+#pragma unroll
+        for (int b = 0; b < 8; b++) *reinterpret_cast<uint32_t*>(ss + (size_t)b * 64 * Kp + off) = w[b];
+    }
+    __syncthreads();
+    uint4* dst = reinterpret_cast<uint4*>(out + ((size_t)e * (N / 32) + r) * 8 * 64 * Kp);
+    const uint4* src = reinterpret_cast<const uint4*>(ss);
+    for (int i = threadIdx.x; i < 8 * 64 * Kp / 16; i += blockDim.x) dst[i] = src[i];
+}
+
+// Plaintext words of set s of a plan -> per (limb e, compressed word w) a block of byte slices
+// 0..7, each Mp rows (outputs o) x Kp bytes (babies k): W[o][k] is the word of family
+// fam(o, k), giant g(o), baby j(k), or 0.
+__global__ void __launch_bounds__(256) k_tc_pack_w(const uint64_t* __restrict__ pts, const int* __restrict__ ids,
+                                                   uint8_t* __restrict__ out, int s, int G, int b1, int Kp, int Mp,
+                                                   int D2, int P) {
+    extern __shared__ __align__(16) uint8_t sw[];   // [8][Mp Kp]
+    const int wi = blockIdx.x, e = blockIdx.y;
+    const int M = 2 * G, K = 2 * b1;
+    const uint32_t SB = 8u * Kp;
+    const uint64_t* row = pts + ((size_t)e * D2 + wi) * P;
+    for (int t = threadIdx.x; t < Mp * (Kp / 4); t += blockDim.x) {
+        const int o = t % Mp, k4 = t / Mp;
+        uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (o < M) {
+            const int X = o / G, g = o % G;
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int k = 4 * k4 + u;
+                if (k >= K) continue;
+                const int Y = k / b1, j = k % b1;
+                const int fam = X == 0 ? Y : (Y == 0 ? 2 : -1);
+                const int id = fam >= 0 ? ids[(((size_t)s * 3 + fam) * G + g) * b1 + j] : -1;
+                if (id < 0) continue;
+                const uint64_t v = row[id];
+#pragma unroll
+                for (int b = 0; b < 8; b++) w[b] |= (uint32_t)((v >> (8 * b)) & 0xFF) << (8 * u);
+            }
+        }
+        const int k = 4 * k4;
+        const size_t off = (size_t)(o >> 3) * SB + (size_t)(k >> 4) * 128 + (size_t)(o & 7) * 16 + (k & 15);
+#pragma unroll
+        for (int b = 0; b < 8; b++) *reinterpret_cast<uint32_t*>(sw + (size_t)b * Mp * Kp + off) = w[b];
+    }
+    __syncthreads();
+    const size_t blk = (size_t)8 * Mp * Kp;
+    uint4* dst = reinterpret_cast<uint4*>(out + ((size_t)e * D2 + wi) * blk);
+    const uint4* src = reinterpret_cast<const uint4*>(sw);
+    for (int i = threadIdx.x; i < (int)(blk / 16); i += blockDim.x) dst[i] = src[i];
+}
+
+struct Tc2Args {
+    const uint8_t* bsplit[kMaxSets];   // per set: [ne][N/32][8][64 Kp]
+    const uint8_t* wpack;              // [set][ne][2D][8][Mp Kp]
+    uint64_t* out;                     // [2G][2][ne][N]
+    int nsets, G, nl, ne, L, logN, lr, D2, Kp;
+};
+
+__device__ __forceinline__ void tc_bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                     tc_smem(dst)),
+                 "l"(src), "r"(bytes), "r"(tc_smem(bar))
+                 : "memory");
+}
+
+// The product kernel on packed operands: per set, two bulk copies (babies 8 x 64 Kp bytes,
+// plaintext words 8 x Mp Kp bytes) into the slices of the shared-memory image, then the MMAs
+// and the epilogue of k_bsgs_tc.
 template <int MP>
-__global__ void __launch_bounds__(kTcThreads, 1) k_bsgs_tc(const GemmArgs a, int Kp, uint32_t tcols,
-                                                           unsigned int* err) {
+__global__ void __launch_bounds__(kTcThreads, 1) k_bsgs_tc2(const Tc2Args a, uint32_t tcols, unsigned int* err) {
     extern __shared__ __align__(1024) uint8_t tsm[];
     constexpr int Mp = MP;
+    const int Kp = a.Kp;
     uint8_t* Ms = tsm;                                        // slice s (-1..8) at (s + 1) * 64 Kp
     uint8_t* Ns = tsm + (size_t)10 * 64 * Kp;                 // slice a at a * Mp Kp
-    uint64_t* bar = (uint64_t*)(Ns + (size_t)8 * Mp * Kp);
-    uint32_t* tslot = (uint32_t*)(bar + 1);
+    uint64_t* bar = (uint64_t*)(Ns + (size_t)8 * Mp * Kp);    // [0] copies, [1] MMAs
+    uint32_t* tslot = (uint32_t*)(bar + 2);
     const int N = 1 << a.logN;
-    const int e = blockIdx.y, x0 = blockIdx.x * 32;
+    const int r = blockIdx.x, e = blockIdx.y, x0 = r * 32;
     const int m = e < a.nl ? e : a.L + (e - a.nl);
     const ModConst mc = c_mod[m];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int M = 2 * a.G, K = 2 * a.b1, ptw = x0 >> a.lr;
-    const uint32_t SB = 8u * Kp;   // bytes between 8-row groups
+    const int M = 2 * a.G, ptw = x0 >> a.lr;
+    const uint32_t SB = 8u * Kp;
+    const uint32_t bbytes = 8u * 64u * Kp, wbytes = 8u * Mp * Kp;
 
-    // zero: slices -1 and 8 (never written again), the running sums
     for (int i = tid; i < 64 * Kp / 16; i += kTcThreads) {
         reinterpret_cast<uint4*>(Ms)[i] = make_uint4(0, 0, 0, 0);
         reinterpret_cast<uint4*>(Ms + (size_t)9 * 64 * Kp)[i] = make_uint4(0, 0, 0, 0);
     }
-    uint64_t run[Mp];   // threads of rows 0..63 (h = 0): running sums mod q of column n, all outputs
+    uint64_t run[Mp];
 #pragma unroll
     for (int o = 0; o < Mp; o++) run[o] = 0;
     if (tid == 0) {
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tc_smem(bar)));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tc_smem(bar + 1)));
         asm volatile("fence.mbarrier_init.release.cluster;");
     }
     if (warp == 0) {
@@ -100,6 +195,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_bsgs_tc(const GemmArgs a, int
                      "r"(tcols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
+    asm volatile("fence.proxy.async.shared::cta;");   // zero slices, before the tensor cores read them
     asm volatile("tcgen05.fence::before_thread_sync;");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;");
@@ -108,53 +204,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_bsgs_tc(const GemmArgs a, int
     bool ok = true;
 
     for (int s = 0; s < a.nsets && ok; s++) {
-        const uint64_t* bb = a.babies[s];
-        // ---- stage B (M side): byte b of word B[k][n] -> slice b, row n, K byte k
-        for (int t = tid; t < 64 * (Kp / 4); t += kTcThreads) {
-            const int n = t & 63, k4 = t >> 6, c = n >> 5, xs = n & 31;
-            uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int k = 4 * k4 + u;
-                if (k < K) {
-                    const uint64_t v = bb[(((size_t)k * 2 + c) * a.ne + e) * N + x0 + xs];
-#pragma unroll
-                    for (int b = 0; b < 8; b++) w[b] |= (uint32_t)((v >> (8 * b)) & 0xFF) << (8 * u);
-                }
-            }
-            const int k = 4 * k4;
-            const size_t off = (size_t)(n >> 3) * SB + (size_t)(k >> 4) * 128 + (size_t)(n & 7) * 16 + (k & 15);
-#pragma unroll
-            for (int b = 0; b < 8; b++) *reinterpret_cast<uint32_t*>(Ms + (size_t)(b + 1) * 64 * Kp + off) = w[b];
+        if (tid == 0) {
+            asm volatile("fence.proxy.async.shared::cta;");   // the previous epilogue's exchange writes
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(bar)),
+                         "r"(bbytes + wbytes)
+                         : "memory");
+            tc_bulk_g2s(Ms + (size_t)64 * Kp, a.bsplit[s] + ((size_t)e * (N / 32) + r) * bbytes, bbytes, bar);
+            tc_bulk_g2s(Ns, a.wpack + (((size_t)s * a.ne + e) * a.D2 + ptw) * wbytes, wbytes, bar);
         }
-        // ---- stage W (N side): byte a of W[o][k] -> slice a, row o, K byte k (rows o >= M are zero)
-        for (int t = tid; t < Mp * (Kp / 4); t += kTcThreads) {
-            const int o = t % Mp, k4 = t / Mp;
-            uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            if (o < M) {
-                const int X = o / a.G, g = o % a.G;
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const int k = 4 * k4 + u;
-                    if (k >= K) continue;
-                    const int Y = k / a.b1, j = k % a.b1;
-                    const int fam = X == 0 ? Y : (Y == 0 ? 2 : -1);
-                    int id = -1;
-                    if (fam >= 0) id = a.ids[(((size_t)s * 3 + fam) * a.G + g) * a.b1 + j];
-                    if (id < 0) continue;
-                    const uint64_t v = a.pts[((size_t)e * a.D2 + ptw) * a.P + id];
-#pragma unroll
-                    for (int b = 0; b < 8; b++) w[b] |= (uint32_t)((v >> (8 * b)) & 0xFF) << (8 * u);
-                }
-            }
-            const int k = 4 * k4;
-            const size_t off = (size_t)(o >> 3) * SB + (size_t)(k >> 4) * 128 + (size_t)(o & 7) * 16 + (k & 15);
-#pragma unroll
-            for (int b = 0; b < 8; b++) *reinterpret_cast<uint32_t*>(Ns + (size_t)b * Mp * Kp + off) = w[b];
+        ok = __syncthreads_and(tc_wait(bar, (uint32_t)(s & 1)) ? 1 : 0) != 0;
+        if (!ok) {
+            if (tid == 0) atomicExch(err, 1u);
+            tc_wait(bar, (uint32_t)(s & 1));
+            break;
         }
-        asm volatile("fence.proxy.async.shared::cta;");
-        __syncthreads();
-        // ---- MMAs: pair p = diagonals (2p, 2p+1) into tensor-memory columns [p Mp, (p+1) Mp)
         if (tid == 0) {
             asm volatile("tcgen05.fence::after_thread_sync;");
             const uint32_t mbase = tc_smem(Ms), nbase = tc_smem(Ns);
@@ -162,7 +225,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_bsgs_tc(const GemmArgs a, int
                 const int d = 2 * p;
                 bool first = true;
                 for (int aa = max(0, d - 7); aa <= min(7, d + 1); aa++) {
-                    const uint32_t ma = mbase + (uint32_t)(d - aa + 1) * 64u * Kp;   // slice d - aa (rows 64..127: d + 1 - aa)
+                    const uint32_t ma = mbase + (uint32_t)(d - aa + 1) * 64u * Kp;
                     const uint32_t na = nbase + (uint32_t)aa * Mp * Kp;
                     for (int ks = 0; ks < Kp / 32; ks++) {
                         tc_mma(taddr + (uint32_t)(p * Mp), tc_desc(ma + ks * 256, 128, SB), tc_desc(na + ks * 256, 128, SB),
@@ -172,19 +235,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_bsgs_tc(const GemmArgs a, int
                 }
             }
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                tc_smem(bar)));
+                tc_smem(bar + 1)));
         }
-        // every thread waits; the outcome is made uniform so that no thread leaves a barrier early
-        ok = __syncthreads_and(tc_wait(bar, (uint32_t)(s & 1)) ? 1 : 0) != 0;
+        ok = __syncthreads_and(tc_wait(bar + 1, (uint32_t)(s & 1)) ? 1 : 0) != 0;
         if (!ok) {
             if (tid == 0) atomicExch(err, 1u);
-            tc_wait(bar, (uint32_t)(s & 1));   // a second bounded wait for the MMAs in flight
+            tc_wait(bar + 1, (uint32_t)(s & 1));
             break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;");
-        // ---- epilogue: warp w holds rows 32w..32w+31: n = row % 64, half h = row / 64 (d = 2p + h)
         const int row = 32 * warp + lane, n = row & 63, h = row >> 6;
-        unsigned __int128* xch = reinterpret_cast<unsigned __int128*>(Ms + (size_t)64 * Kp);   // slices 0.., [64 n][8]
+        unsigned __int128* xch = reinterpret_cast<unsigned __int128*>(Ms + (size_t)64 * Kp);
 #pragma unroll
         for (int oc = 0; oc < Mp / 8; oc++) {
             unsigned __int128 acc[8];
@@ -199,7 +260,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_bsgs_tc(const GemmArgs a, int
 #pragma unroll
                 for (int j = 0; j < 8; j++) acc[j] += (unsigned __int128)v[j] << sh;
             }
-            __syncthreads();   // previous readers of xch are done
+            __syncthreads();
             if (h == 1) {
 #pragma unroll
                 for (int j = 0; j < 8; j++) xch[n * 8 + j] = acc[j];
@@ -213,7 +274,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_bsgs_tc(const GemmArgs a, int
                     const unsigned __int128 tot = acc[j] + xch[n * 8 + j];
                     uint64_t hi = (uint64_t)(tot >> 64);
                     const uint64_t lo = (uint64_t)tot;
-                    // < 128 q^2 / 2^64 < 8q for 60-bit words
                     if (hi >= 4 * mc.q) hi -= 4 * mc.q;
                     if (hi >= 2 * mc.q) hi -= 2 * mc.q;
                     if (hi >= mc.q) hi -= mc.q;
@@ -221,10 +281,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_bsgs_tc(const GemmArgs a, int
                 }
             }
         }
+        // the next bulk copy (async proxy) overwrites the exchange buffer written here
+        asm volatile("fence.proxy.async.shared::cta;");
         asm volatile("tcgen05.fence::before_thread_sync;");
-        __syncthreads();   // tensor memory and the exchange buffer are free for the next set
+        __syncthreads();
     }
-    // ---- outputs: out[o][c][e][x0 + xs] for column n = 32 c + xs (threads of rows 0..63)
     if (ok && tid < 64) {
         const int c = tid >> 5, xs = tid & 31;
 #pragma unroll
