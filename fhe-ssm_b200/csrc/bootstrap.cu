@@ -117,9 +117,14 @@ struct BootCtx {
     double delta_in = 0, stc_s_in = 0;
 };
 
+struct CosArg {
+    double B;
+    int r;
+};
+// cos(2 pi (B x - 1/4) / 2^r): after r double angles, sin(2 pi B x)
 static double cos_target(double x, const void* arg) {
-    const double B = *(const double*)arg;
-    return std::cos(2 * M_PI * (B * x - 0.25) / 8.0);
+    const CosArg* c = (const CosArg*)arg;
+    return std::cos(2 * M_PI * (c->B * x - 0.25) / (double)(1 << c->r));
 }
 
 // rotation steps the bootstrap needs (babies j*base, giants g*b1*base)
@@ -278,10 +283,12 @@ static void eval_level(Context& cx, const BootLevel& L, const Ciphertext& v, Cip
     out = std::move(acc);
 }
 
-void bootstrap_setup(Context& cx, double B, int deg) {
+void bootstrap_setup(Context& cx, double B, int deg, int r) {
+    if (r < 1 || r > 8 || deg < 3) throw Error("bootstrap_setup: need degree >= 3 and 1..8 double angles", -1);
     auto bc = std::make_shared<BootCtx>();
     bc->B = B;
     bc->deg = deg;
+    bc->r = r;
     const int n = cx.N / 2;
     int logn = 0;
     while ((1 << logn) < n) logn++;
@@ -297,7 +304,8 @@ void bootstrap_setup(Context& cx, double B, int deg) {
     }
     nl--;   // 1/(2B) as an exact integer product, landing on the canonical scale
     const int nl_em = nl;
-    bc->cheb = cheb_fit(cos_target, &bc->B, -1.0, 1.0, deg);
+    const CosArg ca{B, r};
+    bc->cheb = cheb_fit(cos_target, &ca, -1.0, 1.0, deg);
     // EvalMod depth: Chebyshev (ceil(log2(deg+1)) + 1) + r double angles
     int cd = 0;
     while ((1 << cd) < deg + 1) cd++;

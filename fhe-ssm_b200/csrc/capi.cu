@@ -95,6 +95,7 @@ int fhe_ctx_set_option(fhe_ctx* cx, const char* name, int value) {
     return guard([&] {
         REQUIRE(cx && name, "null argument");
         if (std::strcmp(name, "matvec_tensor_cores") == 0) cx->cx.use_tc = value != 0;
+        else if (std::strcmp(name, "merged_rescale") == 0) cx->cx.merged_rescale = value != 0;
         else throw fhe::Error(std::string("unknown option ") + name, FHE_ERR_ARG);
     });
 }
@@ -443,6 +444,16 @@ int fhe_bootstrap_setup(fhe_ctx* cx, double bound, int degree) {
         std::vector<int> rots = fhe::boot_rotations(cx->cx);
         fhe::keygen_rotations(cx->cx, rots.data(), (int)rots.size(), true);
         fhe::bootstrap_setup(cx->cx, bound, degree);
+    });
+}
+
+int fhe_bootstrap_setup_r(fhe_ctx* cx, double bound, int degree, int double_angles) {
+    return guard([&] {
+        REQUIRE(cx && bound > 0 && degree >= 3, "bad argument");
+        bind(cx);
+        std::vector<int> rots = fhe::boot_rotations(cx->cx);
+        fhe::keygen_rotations(cx->cx, rots.data(), (int)rots.size(), true);
+        fhe::bootstrap_setup(cx->cx, bound, degree, double_angles);
     });
 }
 int fhe_bootstrap(fhe_ctx* cx, const fhe_ct* a, fhe_ct** out) {

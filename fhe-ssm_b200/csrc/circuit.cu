@@ -100,15 +100,22 @@ void sub_any(Context& cx, const Ciphertext& a0, const Ciphertext& b0, Ciphertext
 
 // ct x ct at the common level, relinearised and rescaled
 void mul_rescale(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out) {
+    auto prod = [&](const Ciphertext& x, const Ciphertext& y) {
+        if (cx.merged_rescale && cx.K <= 6) {   // the merged conversion sums K + 1 <= 7 lazy products
+            ct_mul_relin_rescale(cx, x, y, out);
+        } else {
+            ct_mul_relin(cx, x, y, out);
+            ct_rescale(cx, out);
+        }
+    };
     if (a.nl == b.nl) {
-        ct_mul_relin(cx, a, b, out);
+        prod(a, b);
     } else {
         Ciphertext x = ct_copy(cx, a.nl > b.nl ? a : b);
         const Ciphertext& y = a.nl > b.nl ? b : a;
         align(cx, x, y.nl, 0);
-        ct_mul_relin(cx, x, y, out);
+        prod(x, y);
     }
-    ct_rescale(cx, out);
 }
 
 // per-slot product with a (complex) vector of n slots (n | N/2, repeated), then rescale; the

@@ -26,6 +26,11 @@ __global__ void k_moddown_bconv(const uint64_t*, uint64_t*, const uint64_t*, int
 __global__ void k_moddown_final(const uint64_t*, const uint64_t*, const uint64_t*, const uint64_t*, uint64_t*,
                                 uint64_t*, const uint64_t*, int, int, int, int, int, uint64_t);
 __global__ void k_rescale_lift(const uint64_t*, uint64_t*, int, int, int);
+__global__ void k_mdr_bconv(const uint64_t*, uint64_t*, const uint64_t*, int, int, int, int);
+__global__ void k_mdr_final(const uint64_t*, long long, const uint64_t*, const uint64_t*, const uint64_t*, uint64_t*,
+                            long long, int, int, int, int);
+__global__ void k_mdr_gather(const uint64_t*, long long, const uint64_t*, const uint64_t*, uint64_t*, int, int, int,
+                             int);
 __global__ void k_rescale_final(uint64_t*, long long, const uint64_t*, const uint64_t*, int, int, int, int);
 __global__ void k_ewise(int, const uint64_t*, long long, const uint64_t*, long long, uint64_t*, long long, int, int);
 __global__ void k_tensor(const uint64_t*, long long, const uint64_t*, long long, uint64_t*, long long, uint64_t*, int);
@@ -270,6 +275,7 @@ Context::~Context() {
     for (auto* p : {d_tw, d_twp, d_itw, d_itwp, d_ninv, d_md, d_rs}) if (p) cudaFree(p);
     if (d_err) cudaFree(d_err);
     for (auto& kv : modup_tab) cudaFree(kv.second);
+    for (auto& kv : mdr_tab) cudaFree(kv.second);
     if (stream) cudaStreamDestroy(stream);
 }
 
@@ -302,6 +308,61 @@ const uint64_t* Context::modup_table(int nl) {
     }
     uint64_t* d = dev_upload(tab);
     modup_tab[nl] = d;
+    return d;
+}
+
+// ModDown and rescale in one division by M = q_l P (l = nl - 1): see k_mdr_bconv for the layout
+const uint64_t* Context::mdr_table(int nl) {
+    auto it = mdr_tab.find(nl);
+    if (it != mdr_tab.end()) return it->second;
+    const int J = K + 1, nq = nl - 1, l = nl - 1;
+    std::vector<uint64_t> m(J);
+    m[0] = mods[l];
+    for (int k = 0; k < K; k++) m[1 + k] = mods[L + k];
+    auto hat_mod = [&](int j, uint64_t t) {   // (M / m_j) mod t
+        uint64_t v = 1;
+        for (int u = 0; u < J; u++) if (u != j) v = host_mulmod(v, m[u] % t, t);
+        return v;
+    };
+    std::vector<uint64_t> tab((size_t)2 * J + (size_t)nq * J * 2 + 6 * (size_t)nq + 2 + J, 0);
+    for (int j = 0; j < J; j++) {
+        const uint64_t inv = host_invmod(hat_mod(j, m[j]), m[j]);
+        tab[2 * j] = inv;
+        tab[2 * j + 1] = shoup_of(inv, m[j]);
+    }
+    for (int i = 0; i < nq; i++) {
+        const uint64_t qi = mods[i];
+        for (int j = 0; j < J; j++) {
+            const uint64_t v = hat_mod(j, qi);
+            tab[2 * J + ((size_t)i * J + j) * 2] = v;
+            tab[2 * J + ((size_t)i * J + j) * 2 + 1] = shoup_of(v, qi);
+        }
+        uint64_t Mq = 1, Pq = 1;
+        for (int u = 0; u < J; u++) Mq = host_mulmod(Mq, m[u] % qi, qi);
+        for (int k = 0; k < K; k++) Pq = host_mulmod(Pq, mods[L + k] % qi, qi);
+        const uint64_t minv = host_invmod(Mq, qi);
+        tab[2 * J + (size_t)nq * J * 2 + 2 * i] = minv;
+        tab[2 * J + (size_t)nq * J * 2 + 2 * i + 1] = shoup_of(minv, qi);
+        tab[2 * J + (size_t)nq * J * 2 + 2 * nq + 2 * i] = Pq;
+        tab[2 * J + (size_t)nq * J * 2 + 2 * nq + 2 * i + 1] = shoup_of(Pq, qi);
+    }
+    uint64_t Pl = 1;
+    for (int k = 0; k < K; k++) Pl = host_mulmod(Pl, mods[L + k] % mods[l], mods[l]);
+    tab[2 * J + (size_t)nq * J * 2 + 4 * (size_t)nq] = Pl;
+    tab[2 * J + (size_t)nq * J * 2 + 4 * (size_t)nq + 1] = shoup_of(Pl, mods[l]);
+    const size_t mo = 2 * J + (size_t)nq * J * 2 + 4 * (size_t)nq + 2;   // M mod q_i, then 1/m_j
+    for (int i = 0; i < nq; i++) {
+        uint64_t Mq = 1;
+        for (int u = 0; u < J; u++) Mq = host_mulmod(Mq, m[u] % mods[i], mods[i]);
+        tab[mo + 2 * i] = Mq;
+        tab[mo + 2 * i + 1] = shoup_of(Mq, mods[i]);
+    }
+    for (int j = 0; j < J; j++) {
+        const double r = 1.0 / (double)m[j];
+        std::memcpy(&tab[mo + 2 * (size_t)nq + j], &r, sizeof r);
+    }
+    uint64_t* d = dev_upload(tab);
+    mdr_tab[nl] = d;
     return d;
 }
 
@@ -474,6 +535,53 @@ void ct_mul_relin(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphert
     keyswitch(cx, d2.p, nl, *cx.rlk, t.c(0), t.c(1), t.c(0), t.c(1), 1);
     t.scale = sc;
     out = std::move(t);
+}
+
+void ct_mul_relin_rescale(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out) {
+    if (a.nl != b.nl) throw Error("mul: level mismatch", -4);
+    if (a.nl < 2) throw Error("mul_rescale: no level left", -4);
+    if (!cx.rlk) throw Error("mul: no relinearisation key", -5);
+    if (cx.K > 6) throw Error("mul_relin_rescale: at most 6 special primes", -1);
+    const int N = cx.N, K = cx.K, L = cx.L, nl = a.nl, ne = nl + K, dn = cx.dnum(nl), J = K + 1;
+    cudaStream_t st = cx.stream;
+    Ciphertext d = ct_alloc(cx, nl);
+    DevBuf d2((size_t)nl * N, st);
+    {
+        ProfScope ps(cx, "tensor", 8.0 * N * nl * 7);
+        k_tensor<<<g2(cx, nl), 256, 0, st>>>(a.buf.p, (long long)a.stride, b.buf.p, (long long)b.stride, d.buf.p,
+                                             (long long)d.stride, d2.p, cx.logN);
+    }
+    DevBuf ext = modup(cx, d2.p, nl);
+    DevBuf ip((size_t)2 * ne * N, st);
+    {
+        ProfScope ps(cx, "key_inner", 8.0 * N * ((double)dn * ne * 3 + 2 * ne));
+        k_key_inner<<<g2(cx, ne), 256, 0, st>>>(ext.p, cx.rlk->buf.p, ip.p, nl, ne, dn, L, K, cx.logN);
+    }
+    cx.ks_count++;
+    cx.ks_limbs += nl;
+    const uint64_t* tab = cx.mdr_table(nl);
+    DevBuf z((size_t)2 * J * N, st);
+    k_mdr_gather<<<dim3(N / 256, J, 2), 256, 0, st>>>(d.buf.p, (long long)d.stride, ip.p, tab, z.p, nl, ne, K, cx.logN);
+    LimbMap zm{};
+    zm.base = z.p; zm.poly_stride = (long long)J * N; zm.nl = J;
+    zm.split = 1; zm.off0 = nl - 1; zm.off1 = L;
+    ntt(cx, zm, 2, true, st);
+    DevBuf y((size_t)2 * (nl - 1) * N, st);
+    {
+        ProfScope ps(cx, "moddown_bconv", 8.0 * N * (2 * J + 2 * (nl - 1)));
+        k_mdr_bconv<<<g2(cx, 2), 256, 0, st>>>(z.p, y.p, tab, nl, K, L, cx.logN);
+    }
+    ntt(cx, cx.qmap(y.p, nl - 1, (long long)(nl - 1) * N), 2, false, st);
+    Ciphertext r = ct_alloc(cx, nl - 1);
+    {
+        ProfScope ps(cx, "moddown_final", 8.0 * N * (nl - 1) * 2 * 5);
+        k_mdr_final<<<g2(cx, nl - 1, 2), 256, 0, st>>>(d.buf.p, (long long)d.stride, ip.p, y.p, tab, r.buf.p,
+                                                       (long long)r.stride, nl, ne, K, cx.logN);
+    }
+    CUDA_CHECK(cudaGetLastError());
+    cx.launches += 6;
+    r.scale = a.scale * b.scale / (double)cx.mods[nl - 1];
+    out = std::move(r);
 }
 
 void ct_rescale(Context& cx, Ciphertext& a) {

@@ -122,7 +122,9 @@ struct Context {
     uint64_t* d_rs = nullptr;        // rescale: [L][L] (ql mod qi, ql^-1 mod qi, shoup)
     unsigned int* d_err = nullptr;   // set by a kernel whose bounded wait ran out (checked at syncs)
     int use_tc = 1;                  // BSGS products on the tensor cores (tcgen05) where the shape allows
+    int merged_rescale = 1;          // circuit products: ModDown and rescale in one division by P q_l
     std::map<int, uint64_t*> modup_tab;   // per nl: [dnum][alpha][2] qhat^-1, [dnum][ne][alpha][2] qhat mod t
+    std::map<int, uint64_t*> mdr_tab;     // per nl: ModDown + rescale in one step (ct_mul_relin_rescale)
     // keys
     DevBuf sk;                       // secret, eval form over all L+K moduli, [L+K][N]
     std::vector<int8_t> sk_coeff;    // signed coefficients (client side)
@@ -153,6 +155,7 @@ struct Context {
     int dnum(int nl) const { return (nl + alpha - 1) / alpha; }
     int ext_mod(int nl, int e) const { return e < nl ? e : L + (e - nl); }
     const uint64_t* modup_table(int nl);
+    const uint64_t* mdr_table(int nl);
     LimbMap qmap(uint64_t* base, int nl, long long poly_stride) const;
     LimbMap extmap(uint64_t* base, int nl, long long poly_stride) const;   // Q_l u P
 };
@@ -209,6 +212,9 @@ void ct_add_raw(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertex
 void ct_mul_pt(Context& cx, const Ciphertext& a, const Plaintext& pt, Ciphertext& out);
 void ct_add_pt(Context& cx, const Ciphertext& a, const Plaintext& pt, Ciphertext& out);
 void ct_mul_relin(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out);
+// a * b, relinearised and rescaled with one division by P q_l (ModDown and rescale merged):
+// nl - 1 limbs out; not bit-identical to ct_mul_relin + ct_rescale (one rounding instead of two)
+void ct_mul_relin_rescale(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out);
 void ct_rescale(Context& cx, Ciphertext& a);
 void ct_level_drop(Context& cx, Ciphertext& a, int nl_target);   // drop limbs, no scaling
 void ct_automorph(Context& cx, const Ciphertext& a, uint64_t k, Ciphertext& out);
@@ -270,7 +276,7 @@ struct Model;
 struct ModelCfg;
 // bootstrapping (bootstrap.cu)
 std::vector<int> boot_rotations(const Context& cx);
-void bootstrap_setup(Context& cx, double B, int deg);
+void bootstrap_setup(Context& cx, double B, int deg, int r = 3);
 void bootstrap(Context& cx, const Ciphertext& in, Ciphertext& out);
 void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto);
 int bootstrap_levels_after(const Context& cx);

@@ -138,6 +138,84 @@ __global__ void k_moddown_final(const uint64_t* __restrict__ buf, const uint64_t
     out[(size_t)i * N + x] = v;
 }
 
+// ---------------------------------------------------------------- ModDown + rescale merged ----
+// z: [2][K+1][N] coefficient form of x on the moduli M = q_l p_0 .. p_{K-1} (x = P d + ip on q_l,
+// ip on the p_k).  y[c][i] = [x]_M mod q_i for i < nl - 1, with [x]_M the centred residue
+// (-M/2 <= [x]_M < M/2): sum_j t_j (M/m_j) - u M with t_j = x (M/m_j)^-1 mod m_j and
+// u = rint(sum_j t_j / m_j) evaluated in double precision (Halevi-Polyakov-Shoup, CT-RSA 2019).
+// The division (x - [x]_M) / M is then an exact rounding: no bias is left in the coefficients
+// (the fast conversion without u would leave floor() plus up to K+1 units on every coefficient).
+// tab: [K+1][2] (M/m_j)^-1 mod m_j (+shoup), [nl-1][K+1][2] (M/m_j) mod q_i (+shoup), then
+// [nl-1][2] M^-1 mod q_i, [nl-1][2] P mod q_i, [2] P mod q_l, [nl-1][2] M mod q_i, [K+1] 1/m_j
+// (double bit patterns).
+__global__ void __launch_bounds__(256) k_mdr_bconv(const uint64_t* __restrict__ z, uint64_t* __restrict__ y,
+                                                   const uint64_t* __restrict__ tab, int nl, int K, int L, int logN) {
+    const int N = 1 << logN;
+    const int x = blockIdx.x * blockDim.x + threadIdx.x;
+    const int c = blockIdx.y;
+    const int J = K + 1, nq = nl - 1;
+    const uint64_t* mmod = tab + 2 * J + (size_t)nq * J * 2 + 4 * (size_t)nq + 2;   // [nq][2] M mod q_i
+    const double* rinv = reinterpret_cast<const double*>(mmod + 2 * (size_t)nq);      // [J] 1 / m_j
+    uint64_t t[8];
+    double v = 0.0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        if (j < J) {
+            const uint64_t m = c_mod[j == 0 ? nl - 1 : L + j - 1].q;
+            t[j] = mul_shoup(z[((size_t)c * J + j) * N + x], tab[2 * j], tab[2 * j + 1], m);
+            v += (double)t[j] * rinv[j];
+        }
+    }
+    const uint64_t u = (uint64_t)rint(v);   // 0 <= u <= J
+    const uint64_t* hat = tab + 2 * J;
+    for (int i = 0; i < nq; i++) {
+        const uint64_t q = c_mod[i].q;
+        const uint64_t* w = hat + (size_t)i * J * 2;
+        uint64_t s = 0;
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (j < J) s += mul_shoup_lazy(t[j], w[2 * j], w[2 * j + 1], q);   // J <= 7 terms < 14q
+        s += 2 * q - mul_shoup_lazy(u, mmod[2 * i], mmod[2 * i + 1], q);       // - u M, still < 16q
+        y[((size_t)c * nq + i) * N + x] = reduce_lazy16(s, q);
+    }
+}
+// out_c[i] = (P d_c[i] + ip_c[i] - y_c[i]) * M^-1 for i < nl - 1 (eval form)
+__global__ void __launch_bounds__(256) k_mdr_final(const uint64_t* __restrict__ d, long long sd,
+                                                   const uint64_t* __restrict__ ip, const uint64_t* __restrict__ y,
+                                                   const uint64_t* __restrict__ tab, uint64_t* out, long long so,
+                                                   int nl, int ne, int K, int logN) {
+    const int N = 1 << logN;
+    const int x = blockIdx.x * blockDim.x + threadIdx.x;
+    const int i = blockIdx.y, c = blockIdx.z;
+    const int J = K + 1, nq = nl - 1;
+    const uint64_t q = c_mod[i].q;
+    const uint64_t* minv = tab + 2 * J + (size_t)nq * J * 2 + 2 * i;
+    const uint64_t* pm = tab + 2 * J + (size_t)nq * J * 2 + 2 * nq + 2 * i;
+    uint64_t v = mul_shoup(d[(size_t)c * sd + (size_t)i * N + x], pm[0], pm[1], q);
+    v = mod_add(v, ip[((size_t)c * ne + i) * N + x], q);
+    v = mod_sub(v, y[((size_t)c * nq + i) * N + x], q);
+    out[(size_t)c * so + (size_t)i * N + x] = mul_shoup(v, minv[0], minv[1], q);
+}
+// z[c][0] = P d_c[l] + ip_c[l] (the dropped limb l = nl - 1), z[c][1 + k] = ip_c[nl + k]
+__global__ void __launch_bounds__(256) k_mdr_gather(const uint64_t* __restrict__ d, long long sd,
+                                                    const uint64_t* __restrict__ ip, const uint64_t* __restrict__ tab,
+                                                    uint64_t* __restrict__ z, int nl, int ne, int K, int logN) {
+    const int N = 1 << logN;
+    const int x = blockIdx.x * blockDim.x + threadIdx.x;
+    const int j = blockIdx.y, c = blockIdx.z;
+    const int J = K + 1, l = nl - 1;
+    uint64_t v;
+    if (j == 0) {
+        const uint64_t q = c_mod[l].q;
+        // P mod q_l sits after the per-i entries: tab[2J + nq J 2 + 2 nq + 2 nq] (+shoup)
+        const uint64_t* pl = tab + 2 * J + (size_t)(nl - 1) * J * 2 + 4 * (size_t)(nl - 1);
+        v = mod_add(mul_shoup(d[(size_t)c * sd + (size_t)l * N + x], pl[0], pl[1], q), ip[((size_t)c * ne + l) * N + x], q);
+    } else {
+        v = ip[((size_t)c * ne + nl + j - 1) * N + x];
+    }
+    z[((size_t)c * J + j) * N + x] = v;
+}
+
 // ---------------------------------------------------------------------------- rescale ----
 // last: [2][N] the dropped limb (index l) in coefficient form; y[c][i] = centred lift mod q_i
 __global__ void k_rescale_lift(const uint64_t* __restrict__ last, uint64_t* __restrict__ y, int nlm1, int l,

@@ -84,6 +84,7 @@ _SIGS = {
     "fhe_poly_eval": (C.c_int, [_VP, _VP, _DP, C.c_int, C.c_int, C.POINTER(_VP)]),
     "fhe_cheb_eval": (C.c_int, [_VP, _VP, _DP, C.c_int, C.POINTER(_VP)]),
     "fhe_bootstrap_setup": (C.c_int, [_VP, C.c_double, C.c_int]),
+    "fhe_bootstrap_setup_r": (C.c_int, [_VP, C.c_double, C.c_int, C.c_int]),
     "fhe_bootstrap": (C.c_int, [_VP, _VP, C.POINTER(_VP)]),
     "fhe_bootstrap_level": (C.c_int, [_VP]),
     "fhe_matvec_plan": (C.c_int, [_VP, _DP, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(_VP)]),
@@ -420,8 +421,10 @@ class CryptoContext:
         _check(lib().fhe_matvec_bsgs(self.h, plan.h, arr, n, C.byref(h)))
         return Ciphertext(self, h)
 
-    def EvalBootstrapSetup(self, bound=24.0, degree=59):
-        _check(lib().fhe_bootstrap_setup(self.h, bound, degree))
+    def EvalBootstrapSetup(self, bound=24.0, degree=59, double_angles=3):
+        """EvalMod = Chebyshev interpolant of degree `degree` + `double_angles` double-angle
+        steps (baseline config 3: 59 and 3; degree 31 with 4 takes the same levels, fewer products)."""
+        _check(lib().fhe_bootstrap_setup_r(self.h, bound, degree, double_angles))
 
     def EvalBootstrap(self, ct):
         h = _VP()

@@ -74,7 +74,9 @@ int fhe_ctx_counters(const fhe_ctx* cx, long long* keyswitches, long long* ks_li
 /* the context's CUDA stream (cudaStream_t), for callers that time it with CUDA events */
 void* fhe_ctx_stream(const fhe_ctx* cx);
 /* engine options: "matvec_tensor_cores" (default 1): BSGS products on the tcgen05 tensor cores
- * (byte-split integer MMA); 0 selects the CUDA-core kernel (same results, bit for bit) */
+ * (byte-split integer MMA); 0 selects the CUDA-core kernel (same results, bit for bit).
+ * "merged_rescale" (default 1): circuit products divide by P q_l once (ModDown and rescale
+ * merged); 0 runs ModDown and rescale separately. */
 int fhe_ctx_set_option(fhe_ctx* cx, const char* name, int value);
 /* per-kernel CUDA-event timing on the context's stream (off by default).  collect
  * synchronises, writes {"kernel": [launches, total_ms, algorithmic_bytes], ...} as JSON
@@ -164,6 +166,9 @@ int fhe_cheb_eval(fhe_ctx* cx, const fhe_ct* x, const double* coeffs, int ncoef,
  * CoeffToSlot / SlotToCoeff plaintexts, the EvalMod interpolant (degree `degree` on
  * [-bound, bound] before 3 double angles) and the rotation + conjugation keys */
 int fhe_bootstrap_setup(fhe_ctx* cx, double bound, int degree);
+/* the same with the number of double-angle steps of EvalMod (fhe_bootstrap_setup: 3); the
+ * interpolant is of cos(2 pi (B x - 1/4) / 2^double_angles) */
+int fhe_bootstrap_setup_r(fhe_ctx* cx, double bound, int degree, int double_angles);
 /* EvalBootstrap (:2544): refresh to level fhe_bootstrap_level() */
 int fhe_bootstrap(fhe_ctx* cx, const fhe_ct* a, fhe_ct** out);
 int fhe_bootstrap_level(const fhe_ctx* cx);
