@@ -35,10 +35,10 @@ sys.path.insert(0, os.path.join(ROOT, "tests"))
 
 METRIC_405M = "encrypted tokens/s aggregate, 405M poly-SSM, 64 conv/pass, 1/2/4/8 B200"
 METRIC_HMULT = "HMult+relin+rescale ciphertexts/s aggregate (N=2^16, L=20, batch 64 per GPU)"
-# EvalMod of the model's bootstraps: the baseline's degree-59 interpolant + 3 double angles
-# (degree 31 + 4 double angles takes the same levels and 8 fewer products per bootstrap, but the
-# extra double angle amplifies the evaluation noise 4x: logits relErrRms 2.9e-3 on the 405M pass)
-BOOT_EVALMOD = (24.0, 59, 3)
+# EvalMod of the model's bootstraps: degree-31 interpolant + 4 double angles.  Same 10 levels as
+# config 3's degree 59 + 3, 8 fewer ciphertext products per bootstrap; bootstrap error 6.6e-5
+# (vs 4.5e-5), 405M logits relErrRms 3-4e-4 either way.
+BOOT_EVALMOD = (24.0, 31, 4)
 MODEL_CTX = dict(logN=16, L=28, K=4, alpha=4, hw=192, boot_primes=14)
 HMULT_CTX = dict(logN=16, L=20, K=4, alpha=4, hw=192)
 LANES = 64
