@@ -9,4 +9,5 @@
 #include "matvec.cu"
 #include "model.cu"
 #include "capi.cu"
+#include "serve.cu"
 #include "noalloc.cu"

@@ -91,6 +91,115 @@ __global__ void __launch_bounds__(256) k_ptgen(const double* __restrict__ coef, 
     }
 }
 
+// 2048-point specialisation of k_ptgen (D = 1024, the model's block): one plaintext at a time
+// in registers, 8 words per thread, 11 butterfly stages in 4 passes (3 + 3 + 3 + 2) with three
+// exchanges through shared memory; the limb's twiddles are staged in shared memory once per CTA,
+// and 4 plaintexts are written together (32-byte runs of the transposed layout).  Same
+// arithmetic as k_ptgen (canonical Shoup butterflies): identical words.
+__device__ __forceinline__ void pg_bfly(uint64_t& a, uint64_t& b, uint64_t w, uint64_t wp, uint64_t q) {
+    const uint64_t x = mul_shoup(b, w, wp, q);
+    const uint64_t u = a;
+    a = mod_add(u, x, q);
+    b = mod_sub(u, x, q);
+}
+__global__ void __launch_bounds__(256) k_ptgen2048(const double* __restrict__ coef, double scale,
+                                                   uint64_t* __restrict__ out, int P, int nq, int L,
+                                                   const uint64_t* __restrict__ tw, const uint64_t* __restrict__ twp,
+                                                   int N, int mont) {
+    constexpr int D2 = 2048, IPC = 4;
+    extern __shared__ uint64_t pg[];
+    uint64_t* T = pg;              // [D2]
+    uint64_t* Tp = pg + D2;        // [D2]
+    uint64_t* S = pg + 2 * D2;     // [IPC][D2]: exchange buffer of plaintext t, then its result
+    const int tid = threadIdx.x;
+    const int id0 = blockIdx.x * IPC, i = blockIdx.y;
+    const int m = i < nq ? i : L + (i - nq);
+    const ModConst mc = c_mod[m];
+    const uint64_t q = mc.q;
+    for (int k = tid; k < D2; k += 256) {
+        T[k] = tw[(size_t)m * N + k];
+        Tp[k] = twp[(size_t)m * N + k];
+    }
+    __syncthreads();
+    for (int t = 0; t < IPC; t++) {
+        uint64_t* Sb = S + (size_t)t * D2;
+        const int id = id0 + t;
+        uint64_t x[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            uint64_t r0 = 0;
+            if (id < P) {
+                const long long r = llrint(coef[(size_t)id * D2 + tid + 256 * k] * scale);
+                r0 = r >= 0 ? reduce64((uint64_t)r, mc) : mod_neg(reduce64((uint64_t)(-r), mc), q);
+            }
+            x[k] = r0;
+        }
+        // pass 1: elements tid + 256 k, distances 1024, 512, 256
+        pg_bfly(x[0], x[4], T[1], Tp[1], q); pg_bfly(x[1], x[5], T[1], Tp[1], q);
+        pg_bfly(x[2], x[6], T[1], Tp[1], q); pg_bfly(x[3], x[7], T[1], Tp[1], q);
+#pragma unroll
+        for (int k = 0; k < 8; k++) if ((k & 2) == 0) pg_bfly(x[k], x[k + 2], T[2 + k / 4], Tp[2 + k / 4], q);
+#pragma unroll
+        for (int k = 0; k < 8; k += 2) pg_bfly(x[k], x[k + 1], T[4 + k / 2], Tp[4 + k / 2], q);
+#pragma unroll
+        for (int k = 0; k < 8; k++) Sb[tid + 256 * k] = x[k];
+        __syncthreads();
+        // pass 2: elements blk*256 + r + 32 k (blk = tid / 32, r = tid % 32), distances 128, 64, 32
+        {
+            const int blk = tid >> 5, r = tid & 31;
+#pragma unroll
+            for (int k = 0; k < 8; k++) x[k] = Sb[blk * 256 + r + 32 * k];
+#pragma unroll
+            for (int k = 0; k < 4; k++) pg_bfly(x[k], x[k + 4], T[8 + blk], Tp[8 + blk], q);
+#pragma unroll
+            for (int k = 0; k < 8; k++) if ((k & 2) == 0) pg_bfly(x[k], x[k + 2], T[16 + 2 * blk + k / 4], Tp[16 + 2 * blk + k / 4], q);
+#pragma unroll
+            for (int k = 0; k < 8; k += 2) pg_bfly(x[k], x[k + 1], T[32 + 4 * blk + k / 2], Tp[32 + 4 * blk + k / 2], q);
+            __syncthreads();
+#pragma unroll
+            for (int k = 0; k < 8; k++) Sb[blk * 256 + r + 32 * k] = x[k];
+        }
+        __syncthreads();
+        // pass 3: elements g*32 + r + 4 k (g = tid / 4, r = tid % 4), distances 16, 8, 4
+        {
+            const int g = tid >> 2, r = tid & 3;
+#pragma unroll
+            for (int k = 0; k < 8; k++) x[k] = Sb[g * 32 + r + 4 * k];
+#pragma unroll
+            for (int k = 0; k < 4; k++) pg_bfly(x[k], x[k + 4], T[64 + g], Tp[64 + g], q);
+#pragma unroll
+            for (int k = 0; k < 8; k++) if ((k & 2) == 0) pg_bfly(x[k], x[k + 2], T[128 + 2 * g + k / 4], Tp[128 + 2 * g + k / 4], q);
+#pragma unroll
+            for (int k = 0; k < 8; k += 2) pg_bfly(x[k], x[k + 1], T[256 + 4 * g + k / 2], Tp[256 + 4 * g + k / 2], q);
+            __syncthreads();
+#pragma unroll
+            for (int k = 0; k < 8; k++) Sb[g * 32 + r + 4 * k] = x[k];
+        }
+        __syncthreads();
+        // pass 4: elements 8 tid + k, distances 2, 1
+        {
+#pragma unroll
+            for (int k = 0; k < 8; k++) x[k] = Sb[8 * tid + k];
+#pragma unroll
+            for (int k = 0; k < 8; k++) if ((k & 2) == 0) pg_bfly(x[k], x[k + 2], T[512 + 2 * tid + k / 4], Tp[512 + 2 * tid + k / 4], q);
+#pragma unroll
+            for (int k = 0; k < 8; k += 2) pg_bfly(x[k], x[k + 1], T[1024 + 4 * tid + k / 2], Tp[1024 + 4 * tid + k / 2], q);
+            __syncthreads();
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const uint64_t v = x[k];
+                Sb[8 * tid + k] = mont ? redc(__umul64hi(v, mc.r2), v * mc.r2, mc) : v;
+            }
+        }
+        __syncthreads();
+    }
+    for (int e = tid; e < IPC * D2; e += 256) {
+        const int t = e % IPC, k = e / IPC;
+        if (id0 + t >= P) continue;
+        out[((size_t)i * D2 + k) * P + id0 + t] = S[(size_t)t * D2 + k];
+    }
+}
+
 // ------------------------------------------------------- periodic encode + plaintext cache ----
 // A slot vector of period n < N/2 encodes as the ring-2n encoding of one period at stride
 // N/2n (the identity of hpc_gpu_port/periodic_encode.hpp): a 2n-word compressed plaintext per
@@ -542,7 +651,15 @@ void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets,
     const int M = 2 * G;
     if ((TW / 2) * (M / 2) > 512 || M % 2) throw Error("matvec: too many giant steps for one CTA", -1);
     DevBuf pts((size_t)std::max(pl.P, 1) * ne * 2 * D, st);
-    if (pl.P > 0) {
+    if (pl.P > 0 && logD2 == 11) {
+        const size_t smem = (size_t)(2 + 4) * 2048 * 8;
+        CUDA_CHECK(cudaFuncSetAttribute(k_ptgen2048, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        ProfScope ps(cx, "ptgen", 8.0 * pl.P * 2 * D * (1 + ne));
+        k_ptgen2048<<<dim3((pl.P + 3) / 4, ne), 256, smem, st>>>((const double*)pl.coef.p, spt, pts.p, pl.P, nl, cx.L,
+                                                                cx.d_tw, cx.d_twp, N, 1);
+        CUDA_CHECK(cudaGetLastError());
+        cx.launches++;
+    } else if (pl.P > 0) {
         constexpr int IPC = 4;
         const size_t smem = (size_t)IPC * 2 * D * 8;
         if (smem > 48 * 1024)

@@ -132,9 +132,10 @@ class Plaintext:
         self.ctx, self.h = ctx, h
 
     def __del__(self):
-        if getattr(self, "h", None):
+        # a handle outliving its closed context is dropped (its memory went with the context)
+        if getattr(self, "h", None) and getattr(self.ctx, "h", None):
             lib().fhe_pt_free(self.h)
-            self.h = None
+        self.h = None
 
     @property
     def level(self):
@@ -146,9 +147,9 @@ class Ciphertext:
         self.ctx, self.h = ctx, h
 
     def __del__(self):
-        if getattr(self, "h", None):
+        if getattr(self, "h", None) and getattr(self.ctx, "h", None):
             lib().fhe_ct_free(self.h)
-            self.h = None
+        self.h = None
 
     @property
     def level(self):
@@ -166,13 +167,13 @@ class Ciphertext:
 
 
 class _MvPlan:
-    def __init__(self, h):
-        self.h = h
+    def __init__(self, h, ctx=None):
+        self.h, self.ctx = h, ctx
 
     def __del__(self):
-        if getattr(self, "h", None):
+        if getattr(self, "h", None) and (self.ctx is None or getattr(self.ctx, "h", None)):
             lib().fhe_mvplan_free(self.h)
-            self.h = None
+        self.h = None
 
 
 def seed32(seed) -> bytes:
@@ -409,7 +410,7 @@ class CryptoContext:
         W = np.ascontiguousarray(np.asarray(W, dtype=np.float64))
         h = _VP()
         _check(lib().fhe_matvec_plan(self.h, W.ctypes.data_as(_DP), W.shape[0], W.shape[1], D, b1, C.byref(h)))
-        return _MvPlan(h)
+        return _MvPlan(h, self)
 
     def matvec_keygen(self, D, b1):
         _check(lib().fhe_matvec_keygen(self.h, D, b1))

@@ -301,9 +301,9 @@ class EncryptedModel:
         return dict(zip(self.REFRESH_SITES, list(arr)))
 
     def __del__(self):
-        if getattr(self, "h", None):
+        if getattr(self, "h", None) and getattr(self.ctx, "h", None):
             lib().fhe_model_free(self.h)
-            self.h = None
+        self.h = None
 
 
 def rel_err_rms(enc, ref):

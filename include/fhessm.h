@@ -230,6 +230,26 @@ int fhe_model_probe(fhe_model* m, int k);
  * (one per pack), flags bit 0 = reset the carry first; *n_out outputs */
 int fhe_server_step(fhe_model* m, const fhe_ct* const* in, int n_in, fhe_ct** out, int* n_out, int flags);
 
+/* ---- the serve loop (the --serve REQDIR --stateful loop of gpu_real_model.cu:4363-4483) ----
+ * req.<N>.{0..count-1} + req.<N>.meta (+ req.<N>.reset) + req.<N>.ready in, resp.<N>.* +
+ * resp.<N>.meta + resp.<N>.done (or resp.<N>.error) out, serve.status kept current, a `stop`
+ * file (or timeout_ms idle, or max_requests > 0 served) ends it.  Ciphertext files: "FSSMCT01",
+ * int32 level, limbs, logN, pad, double scale, [2][limbs][N] uint64 words. */
+typedef struct {
+    int level, nl, logN;
+    double scale;
+    uint64_t* words;   /* [2][nl][2^logN] */
+} fhe_wire_ct;
+/* one step: n_in request ciphertexts in; fill out[0..*n_out) (each out[i].words has room for
+ * the words of in[i]); reset != 0: a new session.  Returns FHE_OK or a status (message via
+ * fhe_last_error). */
+typedef int (*fhe_serve_step_fn)(void* user, int reset, int n_in, const fhe_wire_ct* in, int* n_out,
+                                 fhe_wire_ct* out);
+int fhe_serve_files(const char* dir, int timeout_ms, int max_requests, fhe_serve_step_fn step, void* user,
+                    int* served);
+/* the serve loop over fhe_server_step of model m (one pack per request) */
+int fhe_serve_model(fhe_model* m, const char* dir, int timeout_ms, int max_requests, int* served);
+
 /* ---- raw words (parity tests, serialisation) -------------------------------------------- */
 int fhe_ct_import(fhe_ctx* cx, const uint64_t* words, int level, double scale, fhe_ct** out);
 int fhe_ct_export(fhe_ctx* cx, const fhe_ct* ct, uint64_t* words);

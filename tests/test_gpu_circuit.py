@@ -153,6 +153,24 @@ def test_matvec_tensor_core_products_bit_identical(cx, b1):
     assert np.abs(got - U @ W.T).max() < 1e-5
 
 
+def test_matvec_1024_block():
+    """A 1024-wide block (the model's D) at N = 2^14: the 2048-point plaintext generation and
+    the double-hoisted BSGS with b1 = 64 against numpy, every lane different."""
+    import fhessm
+    c = fhessm.CryptoContext(logN=14, L=8, K=4, alpha=4, hw=192)
+    c.KeyGen(seed=21)
+    D, b1 = 1024, 64
+    c.matvec_keygen(D, b1)
+    rng = np.random.default_rng(5)
+    W = rng.normal(0, 0.02, (D, D))
+    R = c.slots // D
+    U = rng.uniform(-1, 1, (2 * R, D))
+    ct = c.Encrypt(c.MakeCKKSPackedPlaintext(block_pack(U, D, c.slots), level=1))
+    y = c.matvec(c.matvec_plan(W, D, b1), [ct])
+    got = block_unpack(c.Decrypt(y), D, 2 * R, D)
+    assert np.abs(got - U @ W.T).max() < 1e-5
+
+
 @pytest.mark.parametrize("logN,L", [(13, 22)])
 def test_bootstrap_small_ring(logN, L):
     boot_check(logN, L, tol=5e-3)

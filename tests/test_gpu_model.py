@@ -44,3 +44,42 @@ def test_model_two_steps_small():
         assert e_exact < 1e-3
         assert rel_err_rms(lg, lr) < 1e-3
         assert top1 >= 0.98
+
+
+def test_model_served_through_request_files(tmp_path):
+    """The same small model behind the native serve loop: two requests of one session (the first
+    with req.0.reset), answered with the carried state; outputs decrypt to the plaintext model."""
+    import threading
+
+    import fhessm
+    from fhessm import serve as sv
+    from fhessm.model import (EncryptedModel, ModelConfig, calibrate_seeds, pack_lanes, plain_step, rel_err_rms,
+                              synthetic_weights, unpack_lanes)
+    cfg = ModelConfig(d=48, dff=128, n_layer=2, vocab=512, D=64, b1=8)
+    w = synthetic_weights(cfg, seed=6)
+    seeds = calibrate_seeds(cfg, w, steps=3, lanes=128)
+    cx = fhessm.CryptoContext(logN=13, L=28, K=4, alpha=4, hw=192, boot_primes=14)
+    cx.KeyGen(seed=10)
+    cx.EvalBootstrapSetup(24.0, 59)
+    m = EncryptedModel(cx, cfg, w, seeds)
+    m.keygen()
+    d = str(tmp_path)
+    served = {}
+    th = threading.Thread(target=lambda: served.setdefault("n", sv.serve_model(m, d, timeout_ms=120000,
+                                                                               max_requests=2)))
+    th.start()
+    lanes = 2 * cx.slots // cfg.D
+    rng = np.random.default_rng(4)
+    state = None
+    for n in range(2):
+        x = w["emb"][rng.integers(0, cfg.vocab, lanes)]
+        ct = cx.Encrypt(cx.MakeCKKSPackedPlaintext(pack_lanes(x, cfg.D, cx.slots)))
+        sv.submit(d, n, [(ct.level, ct.scale, ct.words())], reset=(n == 0), lanes=lanes, tokensReal=1)
+        (resp, meta) = sv.wait_response(d, n, timeout=300)
+        level, scale, words = resp[0]
+        y = unpack_lanes(cx.Decrypt(cx.ct_from_words(words, level, scale)), cfg.D, lanes, cfg.d)
+        ref, state = plain_step(cfg, w, x, state)
+        assert rel_err_rms(y, ref) < 1e-3, n
+        assert meta["reset"] is (n == 0)
+    th.join(60)
+    assert served.get("n") == 2
