@@ -41,6 +41,8 @@ METRIC_HMULT = "HMult+relin+rescale ciphertexts/s aggregate (N=2^16, L=20, batch
 BOOT_EVALMOD = (24.0, 31, 4)
 MODEL_CTX = dict(logN=16, L=28, K=4, alpha=4, hw=192, boot_primes=14)
 HMULT_CTX = dict(logN=16, L=20, K=4, alpha=4, hw=192)
+METRIC_MATVEC = "1024x1024 encrypted BSGS matvecs/s (N=2^16, 64 conversations per ciphertext)"
+MATVEC_CTX = dict(logN=16, L=8, K=4, alpha=4, hw=192)
 LANES = 64
 CENSUS = os.path.join(ROOT, "profiles", "pass_census.json")
 
@@ -395,6 +397,59 @@ def run_hmult(args, ws, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def run_matvec(args, ws, rank, local):
+    """One 1024 x 1024 block of the 405M model's linears (double-hoisted BSGS, b1 = 64): babies,
+    tensor-core products, giants.  A step is one matvec on an input already on the device."""
+    import torch
+
+    import fhessm
+    from fhessm.model import pack_lanes
+    cx = fhessm.CryptoContext(device=local, **MATVEC_CTX)
+    cx.KeyGen(seed=1 + rank)
+    D, b1 = 1024, 64
+    cx.matvec_keygen(D, b1)
+    rng = np.random.default_rng(7 + rank)
+    plan = cx.matvec_plan(rng.normal(0, 0.02, (D, D)), D, b1)
+    U = rng.uniform(-1, 1, (LANES, D))
+    ct = cx.Encrypt(cx.MakeCKKSPackedPlaintext(pack_lanes(U, D, cx.slots), level=2))
+    stream = torch.cuda.ExternalStream(cx.stream_ptr(), device=local)
+    for _ in range(args.warmup):
+        cx.matvec(plan, [ct])
+    cx.sync()
+    barrier(ws)
+    clk = ClockSampler(local)
+    clk.start()
+    l0 = cx.launches()
+    cx.profile(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(ws)
+    e0.record(stream)
+    for _ in range(args.steps):
+        y = cx.matvec(plan, [ct])
+    e1.record(stream)
+    cx.sync()
+    barrier(ws)
+    clocks = clk.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1), ws)
+    prof = cx.profile_collect()
+    cx.profile(False)
+    value = ws * args.steps / (ms / 1000.0)
+    words = ct.words()
+    t0 = time.time()
+    out = cx.matvec(plan, [cx.ct_from_words(words, ct.level, ct.scale)]).words()
+    e2e_s = max_over_ranks(time.time() - t0, ws)
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC_MATVEC, "value": value, "unit": "matvecs/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u64 (RNS residues, CKKS)", "data": "synthetic",
+            "config": {"workload": "one 1024x1024 BSGS block of config 4 (b1 = 64, 6 limbs)", "parallelism": f"dp{ws}"},
+            "gpu_launches": cx.launches() - l0, "clocks": clocks, "roofline": roofline(prof), "cpu_baseline": None,
+            "e2e": {"value": ws / e2e_s, "unit": "matvecs/s", "h2d_bytes_per_step": int(words.nbytes),
+                    "d2h_bytes_per_step": int(out.nbytes)},
+            "kernels": kernel_table(prof)}), flush=True)
+
+
 def run_reference(args):
     """The reference arm: the CPU path of the same workload on the host cores.  OpenFHE (the
     reference's arithmetic library) cannot be built here, so the C oracle (a restatement of the
@@ -435,7 +490,7 @@ def main():
     ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
-    ap.add_argument("--workload", default="405m", choices=["405m", "hmult"])
+    ap.add_argument("--workload", default="405m", choices=["405m", "hmult", "matvec"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=64, help="hmult: ciphertext pairs per GPU per step")
     args = ap.parse_args()
@@ -446,6 +501,8 @@ def main():
     torch.cuda.set_device(local)
     if args.workload == "405m":
         run_model(args, ws, rank, local)
+    elif args.workload == "matvec":
+        run_matvec(args, ws, rank, local)
     else:
         run_hmult(args, ws, rank, local)
     if ws > 1:

@@ -25,6 +25,11 @@
 namespace fhe {
 
 constexpr int kDiagMax = 16;   // babies / giants of one bootstrap linear-transform level
+// Baby steps of a linear-transform level.  Every level is a sum of at most 63 rotated diagonals
+// (offsets -31..31 times the level's base): b1 = 16 gives 15 babies and 4 giants.  The babies
+// stay in QP (double hoisting: one ModUp, no ModDown per baby), the diagonal products run over
+// the extended basis, and only the 4 giant inputs are brought down to Q before their rotations.
+constexpr int kBootB1 = 16;
 
 // circuit.cu
 double canon(const Context& cx, int nl);
@@ -101,7 +106,8 @@ static Diags compose(const Diags& A, const Diags& B, int n) {
 }
 
 struct BootLevel {
-    int base = 1, b1 = 8;
+    int base = 1, b1 = kBootB1;
+    bool pq = true;   // plaintexts over QP (double-hoisted evaluation)
     int nl_in = 0;
     double s_in = 0, s_out = 0;
     std::map<std::pair<int, int>, Plaintext> pts;   // (g, j) -> plaintext of rot(D_k, -g b1 base)
@@ -138,8 +144,9 @@ std::vector<int> boot_rotations(const Context& cx) {
         const int lo = lv * per;
         if (lo >= logn) break;
         const int base = 1 << lo;
-        for (int j = 1; j < 8; j++) r.push_back(j * base);
-        for (int g = -4; g <= 3; g++) if (g) r.push_back(g * 8 * base);
+        for (int j = 1; j < kBootB1; j++) r.push_back(j * base);
+        for (int g = -32 / kBootB1; g < 32 / kBootB1; g++)
+            if (g && (g * kBootB1 * base) % n != 0) r.push_back(g * kBootB1 * base);   // a full turn needs no key
     }
     return r;
 }
@@ -165,7 +172,8 @@ static BootLevel build_level(Context& cx, int lo, int hi, bool inverse, int nl_i
     }
     BootLevel L;
     L.base = 1 << lo;
-    L.b1 = 8;
+    L.b1 = kBootB1;
+    L.pq = true;
     L.nl_in = nl_in;
     L.s_in = s_in;
     L.s_out = s_out;
@@ -178,9 +186,11 @@ static BootLevel build_level(Context& cx, int lo, int hi, bool inverse, int nl_i
         const int g = (int)std::floor((double)k / L.b1), j = k - g * L.b1;
         cvec d = rotv(kv.second, -g * L.b1 * L.base);
         for (auto& x : d) x *= fold;
-        Plaintext pt = encode(cx, d.data(), n, nl_in, spt);
+        Plaintext pt = L.pq ? encode_pq(cx, d.data(), n, nl_in, spt) : encode(cx, d.data(), n, nl_in, spt);
         // Montgomery form: k_diag_mac accumulates 128-bit products and reduces once
-        k_mont<<<dim3(cx.N / 256, nl_in), 256, 0, cx.stream>>>(pt.buf.p, nl_in, 1, cx.logN);
+        LimbMap mm = cx.extmap(pt.buf.p, nl_in, 0);
+        if (!L.pq) { mm.nl = nl_in; mm.split = nl_in; }
+        k_mont_map<<<dim3(cx.N / 256, mm.nl), 256, 0, cx.stream>>>(pt.buf.p, mm, cx.logN);
         CUDA_CHECK(cudaGetLastError());
         L.pts.emplace(std::make_pair(g, j), std::move(pt));
         gset.insert(g);
@@ -201,11 +211,11 @@ struct DiagArgs {
     uint64_t* o1[kDiagMax];
     int nb, ng;
 };
-__global__ void __launch_bounds__(256) k_diag_mac(const DiagArgs a, int logN) {
+__global__ void __launch_bounds__(256) k_diag_mac(const DiagArgs a, int logN, int nq, int L) {
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
-    const int i = blockIdx.y;
-    const ModConst mc = c_mod[i];
+    const int i = blockIdx.y;   // limb: Q limbs below nq, then the special limbs
+    const ModConst mc = c_mod[i < nq ? i : L + (i - nq)];
     const size_t w = (size_t)i * N + x;
     uint64_t v0[kDiagMax], v1[kDiagMax];
 #pragma unroll
@@ -225,59 +235,121 @@ __global__ void __launch_bounds__(256) k_diag_mac(const DiagArgs a, int logN) {
     }
 }
 
+// One linear-transform level: sum over the level's diagonals k of pt_k . rot(v, k base), by
+// baby steps j and giant steps g (k = g b1 + j; the plaintexts carry the -g b1 base pre-rotation).
 static void eval_level(Context& cx, const BootLevel& L, const Ciphertext& v, Ciphertext& out) {
     if (v.nl != L.nl_in) throw Error("bootstrap: level mismatch in linear transform", -4);
-    std::vector<int> steps;
-    for (int j = 1; j < L.b1; j++) steps.push_back(j * L.base);
-    std::vector<Ciphertext> baby(L.b1);
-    baby[0] = ct_copy(cx, v);
-    {
+    const int N = cx.N, K = cx.K, nl = v.nl, ne = nl + K, dn = cx.dnum(nl);
+    cudaStream_t st = cx.stream;
+    const int nb = L.b1, nw = L.pq ? ne : nl;   // limbs of babies, plaintexts and products
+    // babies: QP images P rot(v, j base) from one ModUp (L.pq), or Q rotations (hoisted)
+    DevBuf bq;
+    std::vector<Ciphertext> baby;
+    std::vector<const uint64_t*> b0(nb), b1v(nb);
+    if (L.pq) {
+        bq = DevBuf((size_t)nb * 2 * ne * N, st);
+        DevBuf ext = modup(cx, v.c(1), nl);
+        BabyArgs ba{};
+        for (int i = 0; i < nl; i++) {
+            uint64_t pm = 1;
+            for (int k = 0; k < K; k++) pm = host_mulmod(pm, cx.mods[cx.L + k] % cx.mods[i], cx.mods[i]);
+            ba.pw[i] = pm;
+            ba.pwp[i] = shoup_of(pm, cx.mods[i]);
+        }
+        for (int j = 0; j < nb; j++) {
+            const uint64_t k = j == 0 ? 1 : rot_index(cx, j * L.base);
+            ba.perm[j] = k;
+            ba.fkey[j] = k == 1 ? nullptr : forward_key(cx, k);
+        }
+        {
+            ProfScope ps(cx, "baby_pq", 8.0 * N * nb * ((double)dn * ne * 2 + 2 * ne));
+            k_baby_pq<<<dim3(N / 256, ne, nb), 256, 0, st>>>(ext.p, v.c(0), v.c(1), ba, bq.p, nl, ne, dn, cx.L, K,
+                                                            cx.logN);
+            CUDA_CHECK(cudaGetLastError());
+        }
+        cx.launches++;
+        cx.ks_count += nb - 1;
+        cx.ks_limbs += (long long)(nb - 1) * nl;
+        for (int j = 0; j < nb; j++) {
+            b0[j] = bq.p + (size_t)j * 2 * ne * N;
+            b1v[j] = b0[j] + (size_t)ne * N;
+        }
+    } else {
+        std::vector<int> steps;
+        for (int j = 1; j < nb; j++) steps.push_back(j * L.base);
+        baby.resize(nb);
+        baby[0] = ct_copy(cx, v);
         std::vector<Ciphertext> rs(steps.size());
         ct_rotate_hoisted(cx, v, steps.data(), (int)steps.size(), rs.data());
         for (size_t i = 0; i < rs.size(); i++) baby[i + 1] = std::move(rs[i]);
+        for (int j = 0; j < nb; j++) { b0[j] = baby[j].c(0); b1v[j] = baby[j].c(1); }
     }
-    // giant g: inner_g = sum_j pt_gj . baby_j (one k_diag_mac for all g), then
-    // sum_g rot(inner_g, g b1 base) in one rotate_sum
-    std::vector<Ciphertext> inners;
-    std::vector<int> gsteps;
-    const Ciphertext* g0 = nullptr;
-    inners.reserve(L.gs.size());
+    // giant g: inner_g = sum_j pt_gj . baby_j (one k_diag_mac for all g)
     DiagArgs da{};
-    da.nb = L.b1;
-    for (int j = 0; j < L.b1; j++) { da.b0[j] = baby[j].c(0); da.b1[j] = baby[j].c(1); }
+    da.nb = nb;
+    for (int j = 0; j < nb; j++) { da.b0[j] = b0[j]; da.b1[j] = b1v[j]; }
+    std::vector<int> gl;   // giants in use, in output order
     double spt = 0;
     for (int g : L.gs) {
-        const int gi = (int)inners.size();
         bool any = false;
-        for (int j = 0; j < L.b1; j++) {
+        for (int j = 0; j < nb; j++) {
             auto it = L.pts.find(std::make_pair(g, j));
             if (it == L.pts.end()) continue;
-            da.pt[gi][j] = it->second.buf.p;
+            da.pt[gl.size()][j] = it->second.buf.p;
             spt = it->second.scale;
             any = true;
         }
-        if (!any) continue;
-        inners.push_back(ct_alloc(cx, v.nl));
-        da.o0[gi] = inners.back().c(0);
-        da.o1[gi] = inners.back().c(1);
-        if (g == 0) g0 = &inners.back();
-        else gsteps.push_back(g * L.b1 * L.base);
+        if (any) gl.push_back(g);
     }
-    da.ng = (int)inners.size();
-    for (auto& c : inners) c.scale = v.scale * spt;
-    if (da.ng > 0) {
-        ProfScope ps(cx, "diag_mac", 8.0 * cx.N * v.nl * (2.0 * L.b1 + 2.0 * da.ng + (double)L.pts.size()));
-        k_diag_mac<<<dim3(cx.N / 256, v.nl), 256, 0, cx.stream>>>(da, cx.logN);
+    if (gl.empty()) throw Error("bootstrap: empty linear-transform level", -1);
+    const int G = (int)gl.size();
+    DevBuf inner((size_t)G * 2 * nw * N, st);
+    for (int gi = 0; gi < G; gi++) {
+        da.o0[gi] = inner.p + (size_t)gi * 2 * nw * N;
+        da.o1[gi] = da.o0[gi] + (size_t)nw * N;
+    }
+    da.ng = G;
+    {
+        ProfScope ps(cx, "diag_mac", 8.0 * N * nw * (2.0 * nb + 2.0 * G + (double)L.pts.size()));
+        k_diag_mac<<<dim3(N / 256, nw), 256, 0, st>>>(da, cx.logN, nl, cx.L);
         CUDA_CHECK(cudaGetLastError());
         cx.launches++;
     }
-    if (inners.empty()) throw Error("bootstrap: empty linear-transform level", -1);
-    std::vector<const uint64_t*> c0s, c1s;
-    for (auto& c : inners)
-        if (&c != g0) { c0s.push_back(c.c(0)); c1s.push_back(c.c(1)); }
+    // back to Q (QP path: one ModDown per giant input), then sum_g rot(inner_g, g b1 base)
+    DevBuf innq;
+    const uint64_t* iq = inner.p;
+    if (L.pq) {
+        innq = DevBuf((size_t)G * 2 * nl * N, st);
+        moddown_many(cx, inner.p, G, nl, innq.p);
+        iq = innq.p;
+    }
+    // giants whose rotation is the identity (g = 0, or a full turn of the slots) are summed
+    // into the unrotated term
+    std::vector<const uint64_t*> c0s, c1s, flat;
+    std::vector<int> gsteps;
+    for (int gi = 0; gi < G; gi++) {
+        const uint64_t* p = iq + (size_t)gi * 2 * nl * N;
+        const int step = gl[gi] * nb * L.base;
+        if (rot_index(cx, step) == 1) { flat.push_back(p); continue; }
+        c0s.push_back(p);
+        c1s.push_back(p + (size_t)nl * N);
+        gsteps.push_back(step);
+    }
+    DevBuf fsum;
+    const uint64_t* g0 = flat.empty() ? nullptr : flat[0];
+    if (flat.size() > 1) {
+        fsum = DevBuf((size_t)2 * nl * N, st);
+        const long long ps = (long long)nl * N;
+        k_ewise<<<dim3(N / 256, nl, 2), 256, 0, st>>>(EW_ADD, flat[0], ps, flat[1], ps, fsum.p, ps, 0, cx.logN);
+        for (size_t f = 2; f < flat.size(); f++)
+            k_ewise<<<dim3(N / 256, nl, 2), 256, 0, st>>>(EW_ADD, fsum.p, ps, flat[f], ps, fsum.p, ps, 0, cx.logN);
+        CUDA_CHECK(cudaGetLastError());
+        cx.launches += (long long)flat.size() - 1;
+        g0 = fsum.p;
+    }
     Ciphertext acc;
-    rotate_sum(cx, c0s.data(), c1s.data(), gsteps.data(), (int)gsteps.size(), v.nl, inners[0].scale,
-               g0 ? g0->c(0) : nullptr, g0 ? g0->c(1) : nullptr, acc);
+    rotate_sum(cx, c0s.data(), c1s.data(), gsteps.data(), (int)gsteps.size(), nl, v.scale * spt, g0,
+               g0 ? g0 + (size_t)nl * N : nullptr, acc);
     ct_rescale(cx, acc);
     acc.scale = L.s_out;
     out = std::move(acc);

@@ -806,6 +806,27 @@ Plaintext encode(Context& cx, const std::complex<double>* z, int nslots, int nl,
     return pt;
 }
 
+// the same plaintext over the extended basis: nl Q limbs then the K special limbs
+Plaintext encode_pq(Context& cx, const std::complex<double>* z, int nslots, int nl, double scale) {
+    if (nl < 1 || nl > cx.L) throw Error("encode: bad level", -4);
+    const int N = cx.N, ne = nl + cx.K;
+    std::vector<int64_t> coef(N);
+    encode_coeffs(cx, z, nslots, scale, coef.data());
+    DevBuf dc((size_t)N, cx.stream);
+    CUDA_CHECK(cudaMemcpyAsync(dc.p, coef.data(), N * 8, cudaMemcpyHostToDevice, cx.stream));
+    Plaintext pt;
+    pt.buf = DevBuf((size_t)ne * N, cx.stream);
+    pt.nl = ne;
+    pt.scale = scale;
+    LimbMap mp = cx.extmap(pt.buf.p, nl, (long long)ne * N);
+    k_signed_to_limbs<<<g2(cx, ne), 256, 0, cx.stream>>>((const int64_t*)dc.p, pt.buf.p, mp, cx.logN);
+    CUDA_CHECK(cudaGetLastError());
+    ntt(cx, mp, 1, false, cx.stream);
+    CUDA_CHECK(cudaStreamSynchronize(cx.stream));   // coef is a host temporary
+    cx.launches += 1;
+    return pt;
+}
+
 void decode(Context& cx, const Plaintext& pt, std::complex<double>* z) {
     const int N = cx.N, n = N / 2;
     DevBuf t((size_t)N, cx.stream);

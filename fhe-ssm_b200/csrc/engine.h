@@ -171,6 +171,7 @@ struct LimbConst {
 void apply_limb_const(Context& cx, const Ciphertext& a, const LimbConst& k, Ciphertext& out);
 // round(v) mod q_i for each limb (|v| < 2^126)
 void limb_residues(const Context& cx, long double v, int nl, uint64_t* out);
+Plaintext encode_pq(Context& cx, const std::complex<double>* z, int nslots, int nl, double scale);
 
 // Brackets the launches of one kernel (or kernel pair) with CUDA events on the context's
 // stream when profiling is on; `bytes` is the algorithmic DRAM traffic of the bracket.

@@ -5,8 +5,8 @@
 #include "engine.cu"
 #include "ksbatch.cu"
 #include "circuit.cu"
-#include "bootstrap.cu"
 #include "matvec.cu"
+#include "bootstrap.cu"
 #include "model.cu"
 #include "capi.cu"
 #include "serve.cu"

@@ -346,6 +346,16 @@ __global__ void k_mont(uint64_t* a, int nmod, int to_mont, int logN) {
     else *p = redc(0, *p, mc);
 }
 
+// every limb l of a polynomial into Montgomery form (x 2^64 mod m(l)), modulus m(l) = mp.mod(l)
+__global__ void k_mont_map(uint64_t* a, LimbMap mp, int logN) {
+    const int N = 1 << logN;
+    const int x = blockIdx.x * blockDim.x + threadIdx.x;
+    const int l = blockIdx.y;
+    const ModConst mc = c_mod[mp.mod(l)];
+    uint64_t* p = mp.base + (size_t)l * N + x;
+    *p = redc(__umul64hi(*p, mc.r2), *p * mc.r2, mc);
+}
+
 // encrypt: c0 = v*pk0 + e0 + m, c1 = v*pk1 + e1 over nl limbs; small polys in eval form
 __global__ void k_encrypt(const uint64_t* v, const uint64_t* e0, const uint64_t* e1, const uint64_t* pk, int L,
                           const uint64_t* m, uint64_t* c0, uint64_t* c1, int logN) {
