@@ -96,6 +96,7 @@ int fhe_ctx_set_option(fhe_ctx* cx, const char* name, int value) {
         REQUIRE(cx && name, "null argument");
         if (std::strcmp(name, "matvec_tensor_cores") == 0) cx->cx.use_tc = value != 0;
         else if (std::strcmp(name, "merged_rescale") == 0) cx->cx.merged_rescale = value != 0;
+        else if (std::strcmp(name, "profile_every") == 0) cx->cx.prof_every = value < 1 ? 1 : value;
         else throw fhe::Error(std::string("unknown option ") + name, FHE_ERR_ARG);
     });
 }
@@ -134,7 +135,8 @@ int fhe_prof_collect(fhe_ctx* cx, char* buf, int cap) {
             e.pending.clear();
             if (!first) js += ", ";
             first = false;
-            js += "\"" + kv.first + "\": [" + std::to_string(e.launches) + ", " + std::to_string(e.ms) + ", " +
+            const double ms = e.sampled ? e.ms * (double)e.seen / (double)e.sampled : 0.0;
+            js += "\"" + kv.first + "\": [" + std::to_string(e.seen) + ", " + std::to_string(ms) + ", " +
                   std::to_string(e.bytes) + "]";
         }
         js += "}";

@@ -136,12 +136,15 @@ struct Context {
     mutable long long launches = 0;  // kernel launches issued (for the launch count claim)
     long long ks_count = 0, ks_limbs = 0;   // key switches issued and the sum of their limb counts
     // optional per-kernel CUDA-event timing (bench roofline): name -> pending event pairs
+    // Sampled: one scope in prof_every of each name is timed; the totals are scaled by
+    // seen / sampled (the average duration of a timed scope is exact for what was timed).
     struct ProfEntry {
         std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pending;
-        long long launches = 0;
+        long long seen = 0, sampled = 0;
         double ms = 0.0, bytes = 0.0;
     };
     bool prof = false;
+    int prof_every = 1;
     void check_device_error();
     mutable std::map<std::string, ProfEntry> prof_acc;
     std::unique_ptr<Plaintext> pt_i;         // NTT of X^{N/2}: multiplication by i
@@ -180,19 +183,23 @@ struct ProfScope {
     cudaEvent_t a = nullptr, b = nullptr;
     const char* name;
     double bytes;
+    bool timed = false;
     ProfScope(const Context& c, const char* n, double by) : cx(c), name(n), bytes(by) {
         if (!cx.prof) return;
+        auto& e = cx.prof_acc[name];
+        timed = (e.seen++ % std::max(1, cx.prof_every)) == 0;
+        e.bytes += bytes;
+        if (!timed) return;
         cudaEventCreate(&a);
         cudaEventCreate(&b);
         cudaEventRecord(a, cx.stream);
     }
     ~ProfScope() {
-        if (!cx.prof) return;
+        if (!timed) return;
         cudaEventRecord(b, cx.stream);
         auto& e = cx.prof_acc[name];
         e.pending.emplace_back(a, b);
-        e.launches++;
-        e.bytes += bytes;
+        e.sampled++;
     }
 };
 

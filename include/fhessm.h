@@ -76,7 +76,9 @@ void* fhe_ctx_stream(const fhe_ctx* cx);
 /* engine options: "matvec_tensor_cores" (default 1): BSGS products on the tcgen05 tensor cores
  * (byte-split integer MMA); 0 selects the CUDA-core kernel (same results, bit for bit).
  * "merged_rescale" (default 1): circuit products divide by P q_l once (ModDown and rescale
- * merged); 0 runs ModDown and rescale separately. */
+ * merged); 0 runs ModDown and rescale separately.
+ * "profile_every" (default 1): the per-kernel timer times one scope in this many of each kind
+ * and scales the totals (keeps the timer's own cost out of a timed region). */
 int fhe_ctx_set_option(fhe_ctx* cx, const char* name, int value);
 /* per-kernel CUDA-event timing on the context's stream (off by default).  collect
  * synchronises, writes {"kernel": [launches, total_ms, algorithmic_bytes], ...} as JSON
