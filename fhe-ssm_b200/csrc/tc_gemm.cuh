@@ -177,6 +177,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_bsgs_tc2(const Tc2Args a, uin
     const int M = 2 * a.G, ptw = x0 >> a.lr;
     const uint32_t SB = 8u * Kp;
     const uint32_t bbytes = 8u * 64u * Kp, wbytes = 8u * Mp * Kp;
+    // words of this limb are < q: their bytes nbyte.. are zero, and so are the diagonals
+    // d > 2 (nbyte - 1): only those MMAs and tensor-memory columns are used (45-bit limbs:
+    // 6 bytes, 6 diagonal pairs, 84 of 144 MMAs)
+    const int nbyte = (int)((mc.k + 7) / 8);
+    const int npairs = nbyte;   // pairs p with 2p <= 2 (nbyte - 1)
 
     for (int i = tid; i < 64 * Kp / 16; i += kTcThreads) {
         reinterpret_cast<uint4*>(Ms)[i] = make_uint4(0, 0, 0, 0);
@@ -221,10 +226,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_bsgs_tc2(const Tc2Args a, uin
         if (tid == 0) {
             asm volatile("tcgen05.fence::after_thread_sync;");
             const uint32_t mbase = tc_smem(Ms), nbase = tc_smem(Ns);
-            for (int p = 0; p < 8; p++) {
+            for (int p = 0; p < npairs; p++) {
                 const int d = 2 * p;
                 bool first = true;
-                for (int aa = max(0, d - 7); aa <= min(7, d + 1); aa++) {
+                for (int aa = max(0, d - (nbyte - 1)); aa <= min(nbyte - 1, d + 1); aa++) {
                     const uint32_t ma = mbase + (uint32_t)(d - aa + 1) * 64u * Kp;
                     const uint32_t na = nbase + (uint32_t)aa * Mp * Kp;
                     for (int ks = 0; ks < Kp / 32; ks++) {
@@ -253,6 +258,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_bsgs_tc2(const Tc2Args a, uin
             for (int j = 0; j < 8; j++) acc[j] = 0;
 #pragma unroll
             for (int p = 0; p < 8; p++) {
+                if (p >= npairs) break;   // uniform: all diagonals beyond are zero
                 uint32_t v[8];
                 tc_ld8(taddr + ((uint32_t)(32 * warp) << 16) + (uint32_t)(p * Mp + oc * 8), v);
                 asm volatile("tcgen05.wait::ld.sync.aligned;");
