@@ -211,6 +211,13 @@ Context::Context(const Params& p) : prm(p) {
     }
     CUDA_CHECK(cudaMemcpyToSymbol(c_mod, mc.data(), sizeof(ModConst) * nm));
     d_tw = dev_upload(tw); d_twp = dev_upload(twp); d_itw = dev_upload(itw); d_itwp = dev_upload(itwp);
+    {
+        std::vector<uint64_t> f(2 * tw.size()), v(2 * itw.size());
+        for (size_t i = 0; i < tw.size(); i++) { f[2 * i] = tw[i]; f[2 * i + 1] = twp[i]; }
+        for (size_t i = 0; i < itw.size(); i++) { v[2 * i] = itw[i]; v[2 * i + 1] = itwp[i]; }
+        d_tw2 = dev_upload(f);
+        d_itw2 = dev_upload(v);
+    }
     d_ninv = dev_upload(ninv);
     // FLEXIBLEAUTO scaling factors: scale_at[top] = q_{top-1}; scale_at[nl] = scale_at[nl+1]^2 / q_nl,
     // anchored separately at the top of each prime region (user region, bootstrap region)
@@ -272,7 +279,7 @@ Context::~Context() {
     sk = DevBuf();
     pk = DevBuf();
     if (stream) cudaStreamSynchronize(stream);
-    for (auto* p : {d_tw, d_twp, d_itw, d_itwp, d_ninv, d_md, d_rs}) if (p) cudaFree(p);
+    for (auto* p : {d_tw, d_twp, d_itw, d_itwp, d_ninv, d_md, d_rs, d_tw2, d_itw2}) if (p) cudaFree(p);
     if (d_err) cudaFree(d_err);
     for (auto& kv : modup_tab) cudaFree(kv.second);
     for (auto& kv : mdr_tab) cudaFree(kv.second);

@@ -53,8 +53,8 @@ __device__ __forceinline__ bool limb_skipped(const LimbMap& mp, int poly, int li
 
 // ---- phase "col": stages with distance >= 256 ----------------------------------------
 template <int LOGN, bool INV>
-__global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const uint64_t* __restrict__ tw,
-                                                  const uint64_t* __restrict__ twp, const uint64_t* __restrict__ ninv) {
+__global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const ulonglong2* __restrict__ tw2,
+                                                  const uint64_t* __restrict__ ninv) {
     constexpr int N = 1 << LOGN;
     constexpr int R = N >> 8;            // rows
     constexpr int TC = 4096 / R;         // columns per tile
@@ -66,8 +66,7 @@ __global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const uint64_t* 
     const int m = mp.mod(limb);
     uint64_t* a = mp.base + (size_t)poly * mp.poly_stride + (size_t)limb * N;
     const uint64_t q = c_mod[m].q;
-    const uint64_t* T = tw + (size_t)m * N;
-    const uint64_t* Tp = twp + (size_t)m * N;
+    const ulonglong2* T2 = tw2 + (size_t)m * N;   // (twiddle, Shoup companion) pairs: one 16-byte load
     const int t = threadIdx.x;
     const int c = t % TC, g = t / TC;    // part A: column c, rows g + G*k
     const int col = blockIdx.x * TC + c;
@@ -83,7 +82,10 @@ __global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const uint64_t* 
             for (int k = 0; k < 16; k++) {
                 if (k & h) continue;
                 const int idx = (1 << s) + k / (2 * h);
-                bfly<false>(x[k], x[k + h], T[idx], Tp[idx], q);
+                {
+                    const ulonglong2 t2 = T2[idx];
+                    bfly<false>(x[k], x[k + h], t2.x, t2.y, q);
+                }
             }
         }
         if (R == 16) {
@@ -105,7 +107,10 @@ __global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const uint64_t* 
             for (int k = 0; k < 16; k++) {
                 if (k & h) continue;
                 const int idx = mrow + a2 * (8 / h) + k / (2 * h);
-                bfly<false>(x[k], x[k + h], T[idx], Tp[idx], q);
+                {
+                    const ulonglong2 t2 = T2[idx];
+                    bfly<false>(x[k], x[k + h], t2.x, t2.y, q);
+                }
             }
         }
 #pragma unroll
@@ -126,7 +131,10 @@ __global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const uint64_t* 
                 for (int k = 0; k < 16; k++) {
                     if (k & h) continue;
                     const int idx = mrow + a2 * (8 / h) + k / (2 * h);
-                    bfly<true>(x[k], x[k + h], T[idx], Tp[idx], q);
+                    {
+                    const ulonglong2 t2 = T2[idx];
+                    bfly<true>(x[k], x[k + h], t2.x, t2.y, q);
+                }
                 }
             }
 #pragma unroll
@@ -142,7 +150,10 @@ __global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const uint64_t* 
             for (int k = 0; k < 16; k++) {
                 if (k & h) continue;
                 const int idx = (1 << s) + k / (2 * h);
-                bfly<true>(x[k], x[k + h], T[idx], Tp[idx], q);
+                {
+                    const ulonglong2 t2 = T2[idx];
+                    bfly<true>(x[k], x[k + h], t2.x, t2.y, q);
+                }
             }
         }
         const uint64_t ni = ninv[2 * m], nip = ninv[2 * m + 1];
@@ -153,8 +164,7 @@ __global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const uint64_t* 
 
 // ---- phase "row": the last 8 stages, 256-word blocks ---------------------------------------
 template <int LOGN, bool INV>
-__global__ void __launch_bounds__(256, 4) k_ntt_row(LimbMap mp, const uint64_t* __restrict__ tw,
-                                                  const uint64_t* __restrict__ twp) {
+__global__ void __launch_bounds__(256, 4) k_ntt_row(LimbMap mp, const ulonglong2* __restrict__ tw2) {
     constexpr int N = 1 << LOGN;
     constexpr int S1 = LOGN - 8;
     __shared__ uint64_t sm[4096];
@@ -164,8 +174,7 @@ __global__ void __launch_bounds__(256, 4) k_ntt_row(LimbMap mp, const uint64_t* 
     const int m = mp.mod(limb);
     uint64_t* a = mp.base + (size_t)poly * mp.poly_stride + (size_t)limb * N + (size_t)blockIdx.x * 4096;
     const uint64_t q = c_mod[m].q;
-    const uint64_t* T = tw + (size_t)m * N;
-    const uint64_t* Tp = twp + (size_t)m * N;
+    const ulonglong2* T2 = tw2 + (size_t)m * N;   // (twiddle, Shoup companion) pairs: one 16-byte load
     const int t = threadIdx.x;
     const int b = t >> 4, r0 = t & 15;
     const int bg = blockIdx.x * 16 + b;  // global 256-block index
@@ -181,7 +190,10 @@ __global__ void __launch_bounds__(256, 4) k_ntt_row(LimbMap mp, const uint64_t* 
             for (int k = 0; k < 16; k++) {
                 if (k & h) continue;
                 const int idx = (1 << (S1 + s)) + (bg << s) + k / (2 * h);
-                bfly<false>(x[k], x[k + h], T[idx], Tp[idx], q);
+                {
+                    const ulonglong2 t2 = T2[idx];
+                    bfly<false>(x[k], x[k + h], t2.x, t2.y, q);
+                }
             }
         }
 #pragma unroll
@@ -197,7 +209,10 @@ __global__ void __launch_bounds__(256, 4) k_ntt_row(LimbMap mp, const uint64_t* 
             for (int k = 0; k < 16; k++) {
                 if (k & h) continue;
                 const int idx = (1 << (S1 + 4 + sp)) + (bg << (4 + sp)) + r0 * (8 / h) + k / (2 * h);
-                bfly<false>(x[k], x[k + h], T[idx], Tp[idx], q);
+                {
+                    const ulonglong2 t2 = T2[idx];
+                    bfly<false>(x[k], x[k + h], t2.x, t2.y, q);
+                }
             }
         }
         __syncthreads();
@@ -219,7 +234,10 @@ __global__ void __launch_bounds__(256, 4) k_ntt_row(LimbMap mp, const uint64_t* 
             for (int k = 0; k < 16; k++) {
                 if (k & h) continue;
                 const int idx = (1 << (S1 + 4 + sp)) + (bg << (4 + sp)) + r0 * (8 / h) + k / (2 * h);
-                bfly<true>(x[k], x[k + h], T[idx], Tp[idx], q);
+                {
+                    const ulonglong2 t2 = T2[idx];
+                    bfly<true>(x[k], x[k + h], t2.x, t2.y, q);
+                }
             }
         }
         __syncthreads();
@@ -235,7 +253,10 @@ __global__ void __launch_bounds__(256, 4) k_ntt_row(LimbMap mp, const uint64_t* 
             for (int k = 0; k < 16; k++) {
                 if (k & h) continue;
                 const int idx = (1 << (S1 + s)) + (bg << s) + k / (2 * h);
-                bfly<true>(x[k], x[k + h], T[idx], Tp[idx], q);
+                {
+                    const ulonglong2 t2 = T2[idx];
+                    bfly<true>(x[k], x[k + h], t2.x, t2.y, q);
+                }
             }
         }
 #pragma unroll
@@ -249,11 +270,11 @@ static void launch_ntt(const Context& cx, const LimbMap& mp, int count, bool inv
     constexpr int R = N >> 8;
     dim3 gcol(R / 16, count), grow(N / 4096, count);
     if (!inv) {
-        k_ntt_col<LOGN, false><<<gcol, 256, 0, st>>>(mp, cx.d_tw, cx.d_twp, cx.d_ninv);
-        k_ntt_row<LOGN, false><<<grow, 256, 0, st>>>(mp, cx.d_tw, cx.d_twp);
+        k_ntt_col<LOGN, false><<<gcol, 256, 0, st>>>(mp, (const ulonglong2*)cx.d_tw2, cx.d_ninv);
+        k_ntt_row<LOGN, false><<<grow, 256, 0, st>>>(mp, (const ulonglong2*)cx.d_tw2);
     } else {
-        k_ntt_row<LOGN, true><<<grow, 256, 0, st>>>(mp, cx.d_itw, cx.d_itwp);
-        k_ntt_col<LOGN, true><<<gcol, 256, 0, st>>>(mp, cx.d_itw, cx.d_itwp, cx.d_ninv);
+        k_ntt_row<LOGN, true><<<grow, 256, 0, st>>>(mp, (const ulonglong2*)cx.d_itw2);
+        k_ntt_col<LOGN, true><<<gcol, 256, 0, st>>>(mp, (const ulonglong2*)cx.d_itw2, cx.d_ninv);
     }
 }
 
