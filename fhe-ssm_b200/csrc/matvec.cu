@@ -116,23 +116,26 @@ __global__ void __launch_bounds__(256) k_ptgen2048(const double* __restrict__ co
     const int m = i < nq ? i : L + (i - nq);
     const ModConst mc = c_mod[m];
     const uint64_t q = mc.q;
+    // the coefficients of all IPC plaintexts are loaded up front (one latency for the CTA)
+    double cf[IPC][8];
+#pragma unroll
+    for (int t = 0; t < IPC; t++)
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+            cf[t][k] = id0 + t < P ? coef[(size_t)(id0 + t) * D2 + tid + 256 * k] : 0.0;
     for (int k = tid; k < D2; k += 256) {
         T[k] = tw[(size_t)m * N + k];
         Tp[k] = twp[(size_t)m * N + k];
     }
     __syncthreads();
+#pragma unroll
     for (int t = 0; t < IPC; t++) {
         uint64_t* Sb = S + (size_t)t * D2;
-        const int id = id0 + t;
         uint64_t x[8];
 #pragma unroll
         for (int k = 0; k < 8; k++) {
-            uint64_t r0 = 0;
-            if (id < P) {
-                const long long r = llrint(coef[(size_t)id * D2 + tid + 256 * k] * scale);
-                r0 = r >= 0 ? reduce64((uint64_t)r, mc) : mod_neg(reduce64((uint64_t)(-r), mc), q);
-            }
-            x[k] = r0;
+            const long long r = llrint(cf[t][k] * scale);
+            x[k] = r >= 0 ? reduce64((uint64_t)r, mc) : mod_neg(reduce64((uint64_t)(-r), mc), q);
         }
         // pass 1: elements tid + 256 k, distances 1024, 512, 256
         pg_bfly(x[0], x[4], T[1], Tp[1], q); pg_bfly(x[1], x[5], T[1], Tp[1], q);

@@ -22,6 +22,19 @@ namespace fhe {
 // Harvey lazy butterflies: forward inputs in [0, 4q) -> outputs in [0, 4q); inverse inputs in
 // [0, 2q) -> outputs in [0, 2q).  4q < 2^62 for the 60-bit moduli; the transforms correct to
 // [0, q) at their output.
+// Twiddle pairs are loaded with an L2 evict-last policy (a per-load cache hint): the tables are
+// re-read by every transform of the same modulus and should outlive the data streaming past them.
+__device__ __forceinline__ uint64_t tw_policy() {
+    uint64_t p;
+    asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ ulonglong2 ld_tw(const ulonglong2* a, uint64_t pol) {
+    ulonglong2 v;
+    asm("ld.global.nc.L2::cache_hint.v2.u64 {%0, %1}, [%2], %3;" : "=l"(v.x), "=l"(v.y) : "l"(a), "l"(pol));
+    return v;
+}
+
 template <bool INV>
 __device__ __forceinline__ void bfly(uint64_t& lo, uint64_t& hi, uint64_t w, uint64_t wp, uint64_t q) {
     const uint64_t q2 = q << 1;
@@ -67,6 +80,7 @@ __global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const ulonglong2
     uint64_t* a = mp.base + (size_t)poly * mp.poly_stride + (size_t)limb * N;
     const uint64_t q = c_mod[m].q;
     const ulonglong2* T2 = tw2 + (size_t)m * N;   // (twiddle, Shoup companion) pairs: one 16-byte load
+    const uint64_t pol = tw_policy();
     const int t = threadIdx.x;
     const int c = t % TC, g = t / TC;    // part A: column c, rows g + G*k
     const int col = blockIdx.x * TC + c;
@@ -83,7 +97,7 @@ __global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const ulonglong2
                 if (k & h) continue;
                 const int idx = (1 << s) + k / (2 * h);
                 {
-                    const ulonglong2 t2 = T2[idx];
+                    const ulonglong2 t2 = ld_tw(T2 + idx, pol);
                     bfly<false>(x[k], x[k + h], t2.x, t2.y, q);
                 }
             }
@@ -108,7 +122,7 @@ __global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const ulonglong2
                 if (k & h) continue;
                 const int idx = mrow + a2 * (8 / h) + k / (2 * h);
                 {
-                    const ulonglong2 t2 = T2[idx];
+                    const ulonglong2 t2 = ld_tw(T2 + idx, pol);
                     bfly<false>(x[k], x[k + h], t2.x, t2.y, q);
                 }
             }
@@ -132,7 +146,7 @@ __global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const ulonglong2
                     if (k & h) continue;
                     const int idx = mrow + a2 * (8 / h) + k / (2 * h);
                     {
-                    const ulonglong2 t2 = T2[idx];
+                    const ulonglong2 t2 = ld_tw(T2 + idx, pol);
                     bfly<true>(x[k], x[k + h], t2.x, t2.y, q);
                 }
                 }
@@ -151,7 +165,7 @@ __global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const ulonglong2
                 if (k & h) continue;
                 const int idx = (1 << s) + k / (2 * h);
                 {
-                    const ulonglong2 t2 = T2[idx];
+                    const ulonglong2 t2 = ld_tw(T2 + idx, pol);
                     bfly<true>(x[k], x[k + h], t2.x, t2.y, q);
                 }
             }
@@ -175,6 +189,7 @@ __global__ void __launch_bounds__(256, 4) k_ntt_row(LimbMap mp, const ulonglong2
     uint64_t* a = mp.base + (size_t)poly * mp.poly_stride + (size_t)limb * N + (size_t)blockIdx.x * 4096;
     const uint64_t q = c_mod[m].q;
     const ulonglong2* T2 = tw2 + (size_t)m * N;   // (twiddle, Shoup companion) pairs: one 16-byte load
+    const uint64_t pol = tw_policy();
     const int t = threadIdx.x;
     const int b = t >> 4, r0 = t & 15;
     const int bg = blockIdx.x * 16 + b;  // global 256-block index
@@ -191,7 +206,7 @@ __global__ void __launch_bounds__(256, 4) k_ntt_row(LimbMap mp, const ulonglong2
                 if (k & h) continue;
                 const int idx = (1 << (S1 + s)) + (bg << s) + k / (2 * h);
                 {
-                    const ulonglong2 t2 = T2[idx];
+                    const ulonglong2 t2 = ld_tw(T2 + idx, pol);
                     bfly<false>(x[k], x[k + h], t2.x, t2.y, q);
                 }
             }
@@ -210,7 +225,7 @@ __global__ void __launch_bounds__(256, 4) k_ntt_row(LimbMap mp, const ulonglong2
                 if (k & h) continue;
                 const int idx = (1 << (S1 + 4 + sp)) + (bg << (4 + sp)) + r0 * (8 / h) + k / (2 * h);
                 {
-                    const ulonglong2 t2 = T2[idx];
+                    const ulonglong2 t2 = ld_tw(T2 + idx, pol);
                     bfly<false>(x[k], x[k + h], t2.x, t2.y, q);
                 }
             }
@@ -235,7 +250,7 @@ __global__ void __launch_bounds__(256, 4) k_ntt_row(LimbMap mp, const ulonglong2
                 if (k & h) continue;
                 const int idx = (1 << (S1 + 4 + sp)) + (bg << (4 + sp)) + r0 * (8 / h) + k / (2 * h);
                 {
-                    const ulonglong2 t2 = T2[idx];
+                    const ulonglong2 t2 = ld_tw(T2 + idx, pol);
                     bfly<true>(x[k], x[k + h], t2.x, t2.y, q);
                 }
             }
@@ -254,7 +269,7 @@ __global__ void __launch_bounds__(256, 4) k_ntt_row(LimbMap mp, const ulonglong2
                 if (k & h) continue;
                 const int idx = (1 << (S1 + s)) + (bg << s) + k / (2 * h);
                 {
-                    const ulonglong2 t2 = T2[idx];
+                    const ulonglong2 t2 = ld_tw(T2 + idx, pol);
                     bfly<true>(x[k], x[k + h], t2.x, t2.y, q);
                 }
             }
