@@ -37,6 +37,8 @@ void align(Context& cx, Ciphertext& a, int nl_t, double target);
 void split_complex(Context& cx, const Ciphertext& z, Ciphertext& re, Ciphertext& im, bool halve);
 void merge_complex(Context& cx, Ciphertext re, Ciphertext im, Ciphertext& z);
 void cheb_eval(Context& cx, const Ciphertext& x, const std::vector<double>& coeffs, Ciphertext& out);
+void cheb_eval_n(Context& cx, const Ciphertext* const* x, int K, const std::vector<double>& coeffs, Ciphertext* out);
+void mul_rescale_n(Context& cx, const Ciphertext* const* a, const Ciphertext* const* b, int K, Ciphertext* out);
 std::vector<double> cheb_fit(double (*f)(double, const void*), const void* arg, double a, double b, int n);
 void mul_integer(Context& cx, const Ciphertext& a, long double M, Ciphertext& out);
 void mul_rescale(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out);
@@ -472,18 +474,22 @@ void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto
     Ciphertext re, im;
     split_complex(cx, v, re, im, false);
     Ciphertext parts[2] = {std::move(re), std::move(im)};
-    for (auto& x : parts) {
-        Ciphertext c;
-        cheb_eval(cx, x, bc->cheb, c);
+    {
+        // the two evaluations run side by side: every ciphertext product is one batched product
+        const Ciphertext* px[2] = {&parts[0], &parts[1]};
+        Ciphertext c[2];
+        cheb_eval_n(cx, px, 2, bc->cheb, c);
         for (int k = 0; k < bc->r; k++) {   // cos(2a) = 2 cos^2(a) - 1
-            Ciphertext sq;
-            mul_rescale(cx, c, c, sq);
-            mul_integer(cx, sq, 2, sq);
-            Ciphertext t;
-            ct_add_const(cx, sq, -1.0, t);
-            c = std::move(t);
+            const Ciphertext* pc[2] = {&c[0], &c[1]};
+            Ciphertext sq[2];
+            mul_rescale_n(cx, pc, pc, 2, sq);
+            for (int j = 0; j < 2; j++) {
+                mul_integer(cx, sq[j], 2, sq[j]);
+                ct_add_const(cx, sq[j], -1.0, c[j]);
+            }
         }
-        x = std::move(c);
+        parts[0] = std::move(c[0]);
+        parts[1] = std::move(c[1]);
     }
     Ciphertext w;
     merge_complex(cx, std::move(parts[0]), std::move(parts[1]), w);

@@ -350,6 +350,163 @@ struct ChebEval {
     }
 };
 
+// K products a[k] * b[k] relinearised and rescaled together (ct_mul_relin_rescale_n); operands
+// of unequal levels are aligned first.  Falls back to one product at a time when the batch
+// does not share a level.
+void mul_rescale_n(Context& cx, const Ciphertext* const* a, const Ciphertext* const* b, int K, Ciphertext* out) {
+    if (K == 1 || !cx.merged_rescale || cx.K > 6) {
+        for (int k = 0; k < K; k++) mul_rescale(cx, *a[k], *b[k], out[k]);
+        return;
+    }
+    std::vector<Ciphertext> tmp;
+    tmp.reserve(K);
+    std::vector<const Ciphertext*> A(K), B(K);
+    for (int k = 0; k < K; k++) {
+        if (a[k]->nl == b[k]->nl) { A[k] = a[k]; B[k] = b[k]; continue; }
+        const bool ah = a[k]->nl > b[k]->nl;
+        tmp.push_back(ct_copy(cx, ah ? *a[k] : *b[k]));
+        align(cx, tmp.back(), (ah ? b[k] : a[k])->nl, 0);
+        A[k] = ah ? &tmp.back() : a[k];
+        B[k] = ah ? b[k] : &tmp.back();
+    }
+    for (int k = 1; k < K; k++)
+        if (A[k]->nl != A[0]->nl) {
+            for (int j = 0; j < K; j++) mul_rescale(cx, *A[j], *B[j], out[j]);
+            return;
+        }
+    ct_mul_relin_rescale_n(cx, A.data(), B.data(), K, out);
+}
+
+// The Chebyshev evaluator of ChebEval over K ciphertexts at once (same level and scale, same
+// polynomial): every ciphertext product of the K evaluations is one batched product.
+struct ChebEvalN {
+    Context& cx;
+    int bs, K;
+    std::vector<std::vector<Ciphertext>> T;         // T[i][k]
+    std::map<int, std::vector<Ciphertext>> giant;   // T_{2^m}[k]
+
+    void prod(const std::vector<Ciphertext>& a, const std::vector<Ciphertext>& b, std::vector<Ciphertext>& o) {
+        std::vector<const Ciphertext*> pa(K), pb(K);
+        for (int k = 0; k < K; k++) { pa[k] = &a[k]; pb[k] = &b[k]; }
+        o.clear();
+        o.resize(K);
+        mul_rescale_n(cx, pa.data(), pb.data(), K, o.data());
+    }
+    // 2 a b - c (c = null: 2 a b - 1)
+    std::vector<Ciphertext> cheb_step(const std::vector<Ciphertext>& a, const std::vector<Ciphertext>& b,
+                                      const std::vector<Ciphertext>* c) {
+        std::vector<Ciphertext> p;
+        prod(a, b, p);
+        std::vector<Ciphertext> r(K);
+        for (int k = 0; k < K; k++) {
+            mul_integer(cx, p[k], 2, p[k]);
+            if (c) sub_any(cx, p[k], (*c)[k], r[k]);
+            else ct_add_const(cx, p[k], -1.0, r[k]);
+        }
+        return r;
+    }
+    ChebEvalN(Context& c, const Ciphertext* const* x, int K_, int degree) : cx(c), K(K_) {
+        bs = 1;
+        while (bs * bs < degree + 1) bs <<= 1;
+        if (bs < 2) bs = 2;
+        T.resize(bs);
+        T[1].resize(K);
+        for (int k = 0; k < K; k++) T[1][k] = ct_copy(cx, *x[k]);
+        for (int i = 2; i < bs; i++) {
+            const int a = (i + 1) / 2, b = i / 2;
+            T[i] = cheb_step(T[a], T[b], a == b ? nullptr : &T[a - b]);
+        }
+        int M = bs;
+        giant[M] = cheb_step(T[bs / 2], T[bs / 2], nullptr);
+        while (2 * M <= degree) {
+            giant[2 * M] = cheb_step(giant[M], giant[M], nullptr);
+            M *= 2;
+        }
+        int lo = T[1][0].nl;
+        for (int i = 1; i < bs; i++) lo = std::min(lo, T[i][0].nl);
+        for (int i = 1; i < bs; i++)
+            if (T[i][0].nl > lo)
+                for (int k = 0; k < K; k++) align(cx, T[i][k], lo, 0);
+    }
+    std::vector<Ciphertext> leaf(const std::vector<double>& c) {
+        const int nl = T[1][0].nl;
+        const double target = canon(cx, nl - 1);
+        const double tq = target * (double)cx.mods[nl - 1];
+        std::vector<Ciphertext> out(K);
+        LinArgs la{};
+        std::vector<int> terms;
+        for (int i = 1; i < (int)c.size() && i < bs; i++) {
+            if (c[i] == 0.0) continue;
+            if (la.nt == kLinMax) throw Error("chebyshev: too many baby terms in one leaf", -1);
+            const int t = la.nt++;
+            terms.push_back(i);
+            limb_residues(cx, std::floor((long double)c[i] * (long double)(tq / T[i][0].scale) + 0.5L), nl, la.w[t]);
+            for (int l = 0; l < nl; l++) la.wp[t][l] = shoup_of(la.w[t][l], cx.mods[l]);
+        }
+        if (la.nt == 0) { la.nt = 1; terms.push_back(1); }
+        for (int k = 0; k < K; k++) {
+            for (int t = 0; t < la.nt; t++) {
+                la.in[t] = T[terms[t]][k].c(0);
+                la.stride[t] = (long long)T[terms[t]][k].stride;
+            }
+            Ciphertext acc = ct_alloc(cx, nl);
+            {
+                ProfScope ps(cx, "lincomb", 8.0 * cx.N * nl * 2 * (la.nt + 1));
+                k_lincomb<<<dim3(cx.N / 256, nl, 2), 256, 0, cx.stream>>>(la, acc.c(0), (long long)acc.stride,
+                                                                          cx.logN);
+                CUDA_CHECK(cudaGetLastError());
+                cx.launches++;
+            }
+            acc.scale = tq;
+            ct_rescale(cx, acc);
+            acc.scale = target;
+            if (!c.empty() && c[0] != 0.0) {
+                Ciphertext u;
+                ct_add_const(cx, acc, c[0], u);
+                acc = std::move(u);
+            }
+            out[k] = std::move(acc);
+        }
+        return out;
+    }
+    std::vector<Ciphertext> eval(std::vector<double> c) {
+        int deg = (int)c.size() - 1;
+        while (deg > 0 && c[deg] == 0.0) deg--;
+        c.resize(deg + 1);
+        if (deg < bs) return leaf(c);
+        int M = bs;
+        while (2 * M <= deg) M *= 2;
+        std::vector<double> q(deg - M + 1), r(c.begin(), c.begin() + M);
+        q[0] = c[M];
+        for (int i = M + 1; i <= deg; i++) {
+            q[i - M] = 2 * c[i];
+            r[2 * M - i] -= c[i];
+        }
+        std::vector<Ciphertext> qv = eval(q), rv = eval(r), pr;
+        prod(qv, giant[M], pr);
+        std::vector<Ciphertext> out(K);
+        for (int k = 0; k < K; k++) add_any(cx, pr[k], rv[k], out[k]);
+        return out;
+    }
+};
+
+// cheb_eval over K ciphertexts at one level and scale, products batched
+void cheb_eval_n(Context& cx, const Ciphertext* const* x, int K, const std::vector<double>& coeffs, Ciphertext* out) {
+    std::vector<Ciphertext> y;
+    std::vector<const Ciphertext*> px(x, x + K);
+    if (x[0]->scale / canon(cx, x[0]->nl) > 1 + 1e-9 || x[0]->scale / canon(cx, x[0]->nl) < 1 - 1e-9) {
+        y.reserve(K);
+        for (int k = 0; k < K; k++) {
+            y.push_back(ct_copy(cx, *x[k]));
+            align(cx, y.back(), y.back().nl - 1, 0);
+            px[k] = &y.back();
+        }
+    }
+    ChebEvalN ev(cx, px.data(), K, (int)coeffs.size() - 1);
+    std::vector<Ciphertext> r = ev.eval(coeffs);
+    for (int k = 0; k < K; k++) out[k] = std::move(r[k]);
+}
+
 void cheb_eval(Context& cx, const Ciphertext& x, const std::vector<double>& coeffs, Ciphertext& out) {
     if (x.scale / canon(cx, x.nl) > 1 + 1e-9 || x.scale / canon(cx, x.nl) < 1 - 1e-9) {
         Ciphertext y = ct_copy(cx, x);

@@ -26,7 +26,7 @@ __global__ void k_moddown_bconv(const uint64_t*, uint64_t*, const uint64_t*, int
 __global__ void k_moddown_final(const uint64_t*, const uint64_t*, const uint64_t*, const uint64_t*, uint64_t*,
                                 uint64_t*, const uint64_t*, int, int, int, int, int, uint64_t);
 __global__ void k_rescale_lift(const uint64_t*, uint64_t*, int, int, int);
-__global__ void k_mdr_bconv(const uint64_t*, uint64_t*, const uint64_t*, int, int, int, int);
+__global__ void k_mdr_bconv(const uint64_t*, uint64_t*, const uint64_t*, int, int, int, int, long long, long long);
 __global__ void k_mdr_final(const uint64_t*, long long, const uint64_t*, const uint64_t*, const uint64_t*, uint64_t*,
                             long long, int, int, int, int);
 __global__ void k_mdr_gather(const uint64_t*, long long, const uint64_t*, const uint64_t*, uint64_t*, int, int, int,
@@ -576,7 +576,7 @@ void ct_mul_relin_rescale(Context& cx, const Ciphertext& a, const Ciphertext& b,
     DevBuf y((size_t)2 * (nl - 1) * N, st);
     {
         ProfScope ps(cx, "moddown_bconv", 8.0 * N * (2 * J + 2 * (nl - 1)));
-        k_mdr_bconv<<<g2(cx, 2), 256, 0, st>>>(z.p, y.p, tab, nl, K, L, cx.logN);
+        k_mdr_bconv<<<g2(cx, 2), 256, 0, st>>>(z.p, y.p, tab, nl, K, L, cx.logN, 0, 0);
     }
     ntt(cx, cx.qmap(y.p, nl - 1, (long long)(nl - 1) * N), 2, false, st);
     Ciphertext r = ct_alloc(cx, nl - 1);
@@ -590,6 +590,7 @@ void ct_mul_relin_rescale(Context& cx, const Ciphertext& a, const Ciphertext& b,
     r.scale = a.scale * b.scale / (double)cx.mods[nl - 1];
     out = std::move(r);
 }
+
 
 void ct_rescale(Context& cx, Ciphertext& a) {
     if (a.nl < 2) throw Error("rescale: no limb left to drop", -4);

@@ -224,6 +224,8 @@ void ct_mul_relin(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphert
 // a * b, relinearised and rescaled with one division by P q_l (ModDown and rescale merged):
 // nl - 1 limbs out; not bit-identical to ct_mul_relin + ct_rescale (one rounding instead of two)
 void ct_mul_relin_rescale(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out);
+void ct_mul_relin_rescale_n(Context& cx, const Ciphertext* const* a, const Ciphertext* const* b, int B,
+                            Ciphertext* out);
 void ct_rescale(Context& cx, Ciphertext& a);
 void ct_level_drop(Context& cx, Ciphertext& a, int nl_target);   // drop limbs, no scaling
 void ct_automorph(Context& cx, const Ciphertext& a, uint64_t k, Ciphertext& out);

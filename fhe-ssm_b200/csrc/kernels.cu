@@ -149,10 +149,13 @@ __global__ void k_moddown_final(const uint64_t* __restrict__ buf, const uint64_t
 // [nl-1][2] M^-1 mod q_i, [nl-1][2] P mod q_i, [2] P mod q_l, [nl-1][2] M mod q_i, [K+1] 1/m_j
 // (double bit patterns).
 __global__ void __launch_bounds__(256) k_mdr_bconv(const uint64_t* __restrict__ z, uint64_t* __restrict__ y,
-                                                   const uint64_t* __restrict__ tab, int nl, int K, int L, int logN) {
+                                                   const uint64_t* __restrict__ tab, int nl, int K, int L, int logN,
+                                                   long long sz, long long sy) {
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int c = blockIdx.y;
+    z += blockIdx.z * sz;   // a batch of products (blockIdx.z)
+    y += blockIdx.z * sy;
     const int J = K + 1, nq = nl - 1;
     const uint64_t* mmod = tab + 2 * J + (size_t)nq * J * 2 + 4 * (size_t)nq + 2;   // [nq][2] M mod q_i
     const double* rinv = reinterpret_cast<const double*>(mmod + 2 * (size_t)nq);      // [J] 1 / m_j

@@ -274,4 +274,84 @@ void rotate_sum(Context& cx, const uint64_t* const* c0s, const uint64_t* const* 
     out = std::move(r);
 }
 
+// B products a[k] * b[k] at one level, relinearised and rescaled together: one batched ModUp,
+// one key-inner launch, one merged ModDown + rescale (the same arithmetic as
+// ct_mul_relin_rescale, product by product)
+void ct_mul_relin_rescale_n(Context& cx, const Ciphertext* const* a, const Ciphertext* const* b, int B,
+                            Ciphertext* out) {
+    if (B < 1 || B > 64) throw Error("mul_relin_rescale_n: 1..64 products", -1);
+    const int nl = a[0]->nl;
+    for (int k = 0; k < B; k++)
+        if (a[k]->nl != nl || b[k]->nl != nl) throw Error("mul: level mismatch", -4);
+    if (nl < 2) throw Error("mul_rescale: no level left", -4);
+    if (!cx.rlk) throw Error("mul: no relinearisation key", -5);
+    if (cx.K > 6) throw Error("mul_relin_rescale: at most 6 special primes", -1);
+    const int N = cx.N, K = cx.K, L = cx.L, ne = nl + K, dn = cx.dnum(nl), J = K + 1;
+    cudaStream_t st = cx.stream;
+    DevBuf d((size_t)B * 2 * nl * N, st), d2((size_t)B * nl * N, st);
+    for (int k = 0; k < B; k++) {
+        ProfScope ps(cx, "tensor", 8.0 * N * nl * 7);
+        k_tensor<<<g2(cx, nl), 256, 0, st>>>(a[k]->buf.p, (long long)a[k]->stride, b[k]->buf.p,
+                                             (long long)b[k]->stride, d.p + (size_t)k * 2 * nl * N,
+                                             (long long)nl * N, d2.p + (size_t)k * nl * N, cx.logN);
+    }
+    // ModUp of the B d2 polynomials
+    DevBuf dc((size_t)B * nl * N, st);
+    CUDA_CHECK(cudaMemcpyAsync(dc.p, d2.p, (size_t)B * nl * N * 8, cudaMemcpyDeviceToDevice, st));
+    ntt(cx, cx.qmap(dc.p, nl, (long long)nl * N), B, true, st);
+    DevBuf ext((size_t)B * dn * ne * N, st);
+    {
+        ProfScope ps(cx, "modup_bconv", 8.0 * N * B * (2 * nl + (double)dn * ne));
+        k_modup_bconv<<<g2(cx, dn, B), 256, 0, st>>>(dc.p, d2.p, ext.p, cx.modup_table(nl), nl, ne, cx.alpha, L,
+                                                     cx.logN, (long long)nl * N, (long long)nl * N,
+                                                     (long long)dn * ne * N);
+    }
+    LimbMap em = cx.extmap(ext.p, nl, (long long)ne * N);
+    em.skip_alpha = cx.alpha;
+    em.skip_period = dn;
+    ntt(cx, em, B * dn, false, st);
+    DevBuf ip((size_t)B * 2 * ne * N, st);
+    {
+        KeyBatch kb{};
+        for (int k = 0; k < B; k++) kb.k[k] = cx.rlk->buf.p;
+        ProfScope ps(cx, "key_inner", 8.0 * N * B * ((double)dn * ne * 3 + 2 * ne));
+        k_key_inner_b<<<g2(cx, ne, B), 256, 0, st>>>(ext.p, (long long)dn * ne * N, kb, B, ip.p, nl, ne, dn, L, K,
+                                                     cx.logN, 0, 0);
+    }
+    cx.ks_count += B;
+    cx.ks_limbs += (long long)B * nl;
+    // ModDown + rescale in one division by P q_l, all products together
+    const uint64_t* tab = cx.mdr_table(nl);
+    DevBuf z((size_t)B * 2 * J * N, st);
+    for (int k = 0; k < B; k++)
+        k_mdr_gather<<<dim3(N / 256, J, 2), 256, 0, st>>>(d.p + (size_t)k * 2 * nl * N, (long long)nl * N,
+                                                          ip.p + (size_t)k * 2 * ne * N, tab,
+                                                          z.p + (size_t)k * 2 * J * N, nl, ne, K, cx.logN);
+    LimbMap zm{};
+    zm.base = z.p; zm.poly_stride = (long long)J * N; zm.nl = J;
+    zm.split = 1; zm.off0 = nl - 1; zm.off1 = L;
+    ntt(cx, zm, 2 * B, true, st);
+    DevBuf y((size_t)B * 2 * (nl - 1) * N, st);
+    {
+        ProfScope ps(cx, "moddown_bconv", 8.0 * N * B * (2 * J + 2 * (nl - 1)));
+        k_mdr_bconv<<<g2(cx, 2, B), 256, 0, st>>>(z.p, y.p, tab, nl, K, L, cx.logN, (long long)2 * J * N,
+                                                  (long long)2 * (nl - 1) * N);
+    }
+    ntt(cx, cx.qmap(y.p, nl - 1, (long long)(nl - 1) * N), 2 * B, false, st);
+    for (int k = 0; k < B; k++) {
+        Ciphertext r = ct_alloc(cx, nl - 1);
+        {
+            ProfScope ps(cx, "moddown_final", 8.0 * N * (nl - 1) * 2 * 5);
+            k_mdr_final<<<g2(cx, nl - 1, 2), 256, 0, st>>>(d.p + (size_t)k * 2 * nl * N, (long long)nl * N,
+                                                           ip.p + (size_t)k * 2 * ne * N,
+                                                           y.p + (size_t)k * 2 * (nl - 1) * N, tab, r.buf.p,
+                                                           (long long)r.stride, nl, ne, K, cx.logN);
+        }
+        r.scale = a[k]->scale * b[k]->scale / (double)cx.mods[nl - 1];
+        out[k] = std::move(r);
+    }
+    CUDA_CHECK(cudaGetLastError());
+    cx.launches += 7 + 4 * (long long)B;
+}
+
 }  // namespace fhe
