@@ -652,12 +652,18 @@ int fhe_ntt_host(fhe_ctx* cx, uint64_t* words, int n, const int* mod_idx, int in
         for (int i = 0; i < n; i++) REQUIRE(mod_idx[i] >= 0 && mod_idx[i] < c.L + c.K, "modulus index out of range");
         fhe::DevBuf d((size_t)n * c.N, c.stream);
         fhe::upload(c, d.p, words, d.words);
-        // one transform per limb (each limb names its own modulus)
-        for (int s = 0; s < n; s++) {
+        // a run of consecutive moduli, repeated back to back, is one batched transform
+        for (int s = 0; s < n;) {
+            int run = 1;
+            while (s + run < n && mod_idx[s + run] == mod_idx[s] + run) run++;
+            int reps = 1;
+            while (s + (reps + 1) * run <= n && std::equal(mod_idx + s, mod_idx + s + run, mod_idx + s + reps * run))
+                reps++;
             fhe::LimbMap mp{};
-            mp.base = d.p + (size_t)s * c.N; mp.poly_stride = 0; mp.nl = 1;
-            mp.split = 1; mp.off0 = mod_idx[s]; mp.off1 = 0;
-            fhe::ntt(c, mp, 1, inverse != 0, c.stream);
+            mp.base = d.p + (size_t)s * c.N; mp.poly_stride = (long long)run * c.N; mp.nl = run;
+            mp.split = run; mp.off0 = mod_idx[s]; mp.off1 = 0;
+            fhe::ntt(c, mp, reps, inverse != 0, c.stream);
+            s += run * reps;
         }
         fhe::download(c, words, d.p, d.words);
     });

@@ -217,6 +217,23 @@ Context::Context(const Params& p) : prm(p) {
         for (size_t i = 0; i < itw.size(); i++) { v[2 * i] = itw[i]; v[2 * i + 1] = itwp[i]; }
         d_tw2 = dev_upload(f);
         d_itw2 = dev_upload(v);
+        // the row kernel's table: block bg, slot 2^sp - 1 + j (stage sp of the last four), thread r0
+        const int nb = N >> 8, S1 = logN - 8;
+        std::vector<uint64_t> fr((size_t)nm * nb * 240 * 2), vr(fr.size());
+#pragma omp parallel for
+        for (int m = 0; m < nm; m++)
+            for (int bg = 0; bg < nb; bg++)
+                for (int sp = 0; sp < 4; sp++)
+                    for (int j = 0; j < (1 << sp); j++)
+                        for (int r0 = 0; r0 < 16; r0++) {
+                            const size_t src = (size_t)m * N + (1u << (S1 + 4 + sp)) + ((size_t)bg << (4 + sp)) +
+                                               ((size_t)r0 << sp) + j;
+                            const size_t dst = ((size_t)m * nb + bg) * 240 + (size_t)((1 << sp) - 1 + j) * 16 + r0;
+                            fr[2 * dst] = tw[src]; fr[2 * dst + 1] = twp[src];
+                            vr[2 * dst] = itw[src]; vr[2 * dst + 1] = itwp[src];
+                        }
+        d_twrow = dev_upload(fr);
+        d_itwrow = dev_upload(vr);
     }
     d_ninv = dev_upload(ninv);
     // FLEXIBLEAUTO scaling factors: scale_at[top] = q_{top-1}; scale_at[nl] = scale_at[nl+1]^2 / q_nl,
@@ -279,7 +296,7 @@ Context::~Context() {
     sk = DevBuf();
     pk = DevBuf();
     if (stream) cudaStreamSynchronize(stream);
-    for (auto* p : {d_tw, d_twp, d_itw, d_itwp, d_ninv, d_md, d_rs, d_tw2, d_itw2}) if (p) cudaFree(p);
+    for (auto* p : {d_tw, d_twp, d_itw, d_itwp, d_ninv, d_md, d_rs, d_tw2, d_itw2, d_twrow, d_itwrow}) if (p) cudaFree(p);
     if (d_err) cudaFree(d_err);
     for (auto& kv : modup_tab) cudaFree(kv.second);
     for (auto& kv : mdr_tab) cudaFree(kv.second);

@@ -19,9 +19,11 @@
 
 namespace fhe {
 
-// Harvey lazy butterflies: forward inputs in [0, 4q) -> outputs in [0, 4q); inverse inputs in
-// [0, 2q) -> outputs in [0, 2q).  4q < 2^62 for the 60-bit moduli; the transforms correct to
-// [0, q) at their output.
+// Harvey lazy butterflies.  Forward: inputs in [0, 4q + 2^32) -> outputs in [0, 4q + 2^32);
+// the conditional subtraction of 2q looks at the high words only (subtract when u >> 32 exceeds
+// 2q >> 32), which leaves u < 2q + 2^32 and saves the low-word compare.  Inverse: inputs in
+// [0, 2q) -> outputs in [0, 2q).  4q + 2^32 < 2^63 for the moduli below 2^61; the transforms
+// correct to [0, q) at their output.
 // Twiddle pairs are loaded with an L2 evict-last policy (a per-load cache hint): the tables are
 // re-read by every transform of the same modulus and should outlive the data streaming past them.
 __device__ __forceinline__ uint64_t tw_policy() {
@@ -40,7 +42,7 @@ __device__ __forceinline__ void bfly(uint64_t& lo, uint64_t& hi, uint64_t w, uin
     const uint64_t q2 = q << 1;
     if (!INV) {
         uint64_t u = lo;
-        if (u >= q2) u -= q2;
+        if ((uint32_t)(u >> 32) > (uint32_t)(q2 >> 32)) u -= q2;
         const uint64_t x = mul_shoup_lazy(hi, w, wp, q);
         lo = u + x;
         hi = u - x + q2;
@@ -52,9 +54,10 @@ __device__ __forceinline__ void bfly(uint64_t& lo, uint64_t& hi, uint64_t w, uin
         lo = u;
     }
 }
-__device__ __forceinline__ uint64_t canon4(uint64_t v, uint64_t q) {   // [0, 4q) -> [0, q)
+__device__ __forceinline__ uint64_t canon4(uint64_t v, uint64_t q) {   // [0, 4q + 2^32) -> [0, q)
     const uint64_t q2 = q << 1;
-    if (v >= q2) v -= q2;
+    if (v >= q2) v -= q2;   // < 2q + 2^32
+    if (v >= q2) v -= q2;   // < 2q
     return v >= q ? v - q : v;
 }
 
@@ -64,9 +67,29 @@ __device__ __forceinline__ bool limb_skipped(const LimbMap& mp, int poly, int li
     return limb >= lo && limb < min(lo + mp.skip_alpha, mp.skip_nq);
 }
 
+// One radix-2 stage over a thread's 16 registers at register distance H: butterfly (k, k + H)
+// for every k with k & H == 0, using twiddle number k / (2H) of the stage, tw(j).  Each of the
+// 8/H distinct twiddles is loaded once.
+template <bool INV, int H, class TW>
+__device__ __forceinline__ void stage16(uint64_t (&x)[16], uint64_t q, TW tw) {
+#pragma unroll
+    for (int j = 0; j < 8 / H; j++) {
+        const ulonglong2 t2 = tw(j);
+#pragma unroll
+        for (int kk = 0; kk < H; kk++) bfly<INV>(x[2 * H * j + kk], x[2 * H * j + kk + H], t2.x, t2.y, q);
+    }
+}
+template <bool INV, class TW>
+__device__ __forceinline__ void stage16(uint64_t (&x)[16], uint64_t q, int h, TW tw) {
+    if (h == 8) stage16<INV, 8>(x, q, tw);
+    else if (h == 4) stage16<INV, 4>(x, q, tw);
+    else if (h == 2) stage16<INV, 2>(x, q, tw);
+    else stage16<INV, 1>(x, q, tw);
+}
+
 // ---- phase "col": stages with distance >= 256 ----------------------------------------
 template <int LOGN, bool INV>
-__global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const ulonglong2* __restrict__ tw2,
+__global__ void __launch_bounds__(256, 3) k_ntt_col(LimbMap mp, const ulonglong2* __restrict__ tw2,
                                                   const uint64_t* __restrict__ ninv) {
     constexpr int N = 1 << LOGN;
     constexpr int R = N >> 8;            // rows
@@ -84,24 +107,15 @@ __global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const ulonglong2
     const int t = threadIdx.x;
     const int c = t % TC, g = t / TC;    // part A: column c, rows g + G*k
     const int col = blockIdx.x * TC + c;
+    const int a2 = t / TC;               // part B: rows 16*a2 + k
     uint64_t x[16];
     if (!INV) {
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = a[(size_t)(g + G * k) * 256 + col];
-        // part A: distances R/2 .. R/16 (register stride h = 8,4,2,1); twiddle 2^s + k/(2h)
+        // part A: distances R/2 .. R/16 (register distance h = 8,4,2,1); twiddle 2^s + k/(2h)
 #pragma unroll
-        for (int s = 0; s < 4; s++) {
-            const int h = 8 >> s;
-#pragma unroll
-            for (int k = 0; k < 16; k++) {
-                if (k & h) continue;
-                const int idx = (1 << s) + k / (2 * h);
-                {
-                    const ulonglong2 t2 = ld_tw(T2 + idx, pol);
-                    bfly<false>(x[k], x[k + h], t2.x, t2.y, q);
-                }
-            }
-        }
+        for (int s = 0; s < 4; s++)
+            stage16<false>(x, q, 8 >> s, [&](int j) { return ld_tw(T2 + (1 << s) + j, pol); });
         if (R == 16) {
 #pragma unroll
             for (int k = 0; k < 16; k++) a[(size_t)(g + G * k) * 256 + col] = x[k];
@@ -110,27 +124,15 @@ __global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const ulonglong2
 #pragma unroll
         for (int k = 0; k < 16; k++) sm[(g + G * k) * TC + c] = x[k];
         __syncthreads();
-        const int a2 = t / TC;           // part B: rows 16*a2 + k
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = sm[(16 * a2 + k) * TC + c];
         // part B: distances R/32 .. 1 (h = t_r), m_row = R/(2h), twiddle m_row + a2*(8/h) + k/(2h)
 #pragma unroll
-        for (int h = R / 32; h >= 1; h >>= 1) {
-            const int mrow = R / (2 * h);
-#pragma unroll
-            for (int k = 0; k < 16; k++) {
-                if (k & h) continue;
-                const int idx = mrow + a2 * (8 / h) + k / (2 * h);
-                {
-                    const ulonglong2 t2 = ld_tw(T2 + idx, pol);
-                    bfly<false>(x[k], x[k + h], t2.x, t2.y, q);
-                }
-            }
-        }
+        for (int h = R / 32; h >= 1; h >>= 1)
+            stage16<false>(x, q, h, [&](int j) { return ld_tw(T2 + R / (2 * h) + a2 * (8 / h) + j, pol); });
 #pragma unroll
         for (int k = 0; k < 16; k++) a[(size_t)(16 * a2 + k) * 256 + col] = x[k];
     } else {
-        const int a2 = t / TC;
         if (R == 16) {
 #pragma unroll
             for (int k = 0; k < 16; k++) x[k] = a[(size_t)(g + G * k) * 256 + col];
@@ -139,18 +141,8 @@ __global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const ulonglong2
             for (int k = 0; k < 16; k++) x[k] = a[(size_t)(16 * a2 + k) * 256 + col];
             // inverse part B first: distances 1 .. R/32
 #pragma unroll
-            for (int h = 1; h <= R / 32; h <<= 1) {
-                const int mrow = R / (2 * h);
-#pragma unroll
-                for (int k = 0; k < 16; k++) {
-                    if (k & h) continue;
-                    const int idx = mrow + a2 * (8 / h) + k / (2 * h);
-                    {
-                    const ulonglong2 t2 = ld_tw(T2 + idx, pol);
-                    bfly<true>(x[k], x[k + h], t2.x, t2.y, q);
-                }
-                }
-            }
+            for (int h = 1; h <= R / 32; h <<= 1)
+                stage16<true>(x, q, h, [&](int j) { return ld_tw(T2 + R / (2 * h) + a2 * (8 / h) + j, pol); });
 #pragma unroll
             for (int k = 0; k < 16; k++) sm[(16 * a2 + k) * TC + c] = x[k];
             __syncthreads();
@@ -158,18 +150,8 @@ __global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const ulonglong2
             for (int k = 0; k < 16; k++) x[k] = sm[(g + G * k) * TC + c];
         }
 #pragma unroll
-        for (int s = 3; s >= 0; s--) {
-            const int h = 8 >> s;
-#pragma unroll
-            for (int k = 0; k < 16; k++) {
-                if (k & h) continue;
-                const int idx = (1 << s) + k / (2 * h);
-                {
-                    const ulonglong2 t2 = ld_tw(T2 + idx, pol);
-                    bfly<true>(x[k], x[k + h], t2.x, t2.y, q);
-                }
-            }
-        }
+        for (int s = 3; s >= 0; s--)
+            stage16<true>(x, q, 8 >> s, [&](int j) { return ld_tw(T2 + (1 << s) + j, pol); });
         const uint64_t ni = ninv[2 * m], nip = ninv[2 * m + 1];
 #pragma unroll
         for (int k = 0; k < 16; k++) a[(size_t)(g + G * k) * 256 + col] = mul_shoup(x[k], ni, nip, q);
@@ -177,11 +159,21 @@ __global__ void __launch_bounds__(256, 4) k_ntt_col(LimbMap mp, const ulonglong2
 }
 
 // ---- phase "row": the last 8 stages, 256-word blocks ---------------------------------------
+// Shared memory holds each 256-word block as a 16 x 16 matrix with rows padded to 17 words:
+// both the row-wise (fixed row, column = lane) and the column-wise (fixed column, row = lane)
+// accesses of a half-warp fall on 16 distinct 8-byte bank pairs, and every access is a
+// per-thread base plus an immediate offset.
+// Part B (the last four stages) reads its twiddles from the row table `rtab`: for block bg,
+// thread r0 and stage sp (distance h = 8 >> sp), twiddle j of the 2^sp the thread needs is
+// rtab[bg][2^sp - 1 + j][r0] = Tab[2^(logN-4+sp) + bg * 2^(4+sp) + r0 * 2^sp + j], so a warp's
+// load covers consecutive pairs.
+constexpr int kRowTab = 240;   // pairs per 256-word block: 16 threads x (1 + 2 + 4 + 8)
 template <int LOGN, bool INV>
-__global__ void __launch_bounds__(256, 4) k_ntt_row(LimbMap mp, const ulonglong2* __restrict__ tw2) {
+__global__ void __launch_bounds__(256, 3) k_ntt_row(LimbMap mp, const ulonglong2* __restrict__ tw2,
+                                                  const ulonglong2* __restrict__ rtab) {
     constexpr int N = 1 << LOGN;
     constexpr int S1 = LOGN - 8;
-    __shared__ uint64_t sm[4096];
+    __shared__ uint64_t sm[16 * 272];
     const int y = blockIdx.y;
     const int poly = y / mp.nl, limb = y % mp.nl;
     if (limb_skipped(mp, poly, limb)) return;
@@ -193,87 +185,49 @@ __global__ void __launch_bounds__(256, 4) k_ntt_row(LimbMap mp, const ulonglong2
     const int t = threadIdx.x;
     const int b = t >> 4, r0 = t & 15;
     const int bg = blockIdx.x * 16 + b;  // global 256-block index
+    const ulonglong2* RB = rtab + ((size_t)m * (N >> 8) + bg) * kRowTab + r0;
+    uint64_t* sA = sm + b * 272 + r0;        // entry (k, r0) at sA[17 k]
+    uint64_t* sB = sm + b * 272 + 17 * r0;   // entry (r0, k) at sB[k]
     uint64_t x[16];
     if (!INV) {
 #pragma unroll
         for (int k = 0; k < 16; k++) x[k] = a[b * 256 + r0 + 16 * k];
         // part A: distances 128,64,32,16 (h = 8..1), twiddle 2^(S1+s) + bg*2^s + k/(2h)
 #pragma unroll
-        for (int s = 0; s < 4; s++) {
-            const int h = 8 >> s;
+        for (int s = 0; s < 4; s++)
+            stage16<false>(x, q, 8 >> s, [&](int j) { return ld_tw(T2 + (1 << (S1 + s)) + (bg << s) + j, pol); });
 #pragma unroll
-            for (int k = 0; k < 16; k++) {
-                if (k & h) continue;
-                const int idx = (1 << (S1 + s)) + (bg << s) + k / (2 * h);
-                {
-                    const ulonglong2 t2 = ld_tw(T2 + idx, pol);
-                    bfly<false>(x[k], x[k + h], t2.x, t2.y, q);
-                }
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < 16; k++) sm[b * 256 + r0 + 16 * k] = x[k];
+        for (int k = 0; k < 16; k++) sA[17 * k] = x[k];
         __syncthreads();
 #pragma unroll
-        for (int k = 0; k < 16; k++) x[k] = sm[b * 256 + 16 * r0 + k];
-        // part B: distances 8,4,2,1 (h), stage s' = 3 - log2 h: m = 2^(S1+4+s'), i = bg*2^(4+s') + r0*(8/h) + k/(2h)
+        for (int k = 0; k < 16; k++) x[k] = sB[k];
+        // part B: distances 8,4,2,1
 #pragma unroll
-        for (int sp = 0; sp < 4; sp++) {
-            const int h = 8 >> sp;
+        for (int sp = 0; sp < 4; sp++)
+            stage16<false>(x, q, 8 >> sp, [&](int j) { return ld_tw(RB + ((1 << sp) - 1 + j) * 16, pol); });
+        // each thread rewrites only the row it read: no barrier before the write
 #pragma unroll
-            for (int k = 0; k < 16; k++) {
-                if (k & h) continue;
-                const int idx = (1 << (S1 + 4 + sp)) + (bg << (4 + sp)) + r0 * (8 / h) + k / (2 * h);
-                {
-                    const ulonglong2 t2 = ld_tw(T2 + idx, pol);
-                    bfly<false>(x[k], x[k + h], t2.x, t2.y, q);
-                }
-            }
-        }
+        for (int k = 0; k < 16; k++) sB[k] = canon4(x[k], q);
         __syncthreads();
 #pragma unroll
-        for (int k = 0; k < 16; k++) sm[b * 256 + 16 * r0 + k] = canon4(x[k], q);
-        __syncthreads();
-#pragma unroll
-        for (int k = 0; k < 16; k++) a[b * 256 + r0 + 16 * k] = sm[b * 256 + r0 + 16 * k];
+        for (int k = 0; k < 16; k++) a[b * 256 + r0 + 16 * k] = sA[17 * k];
     } else {
 #pragma unroll
-        for (int k = 0; k < 16; k++) sm[b * 256 + r0 + 16 * k] = a[b * 256 + r0 + 16 * k];
+        for (int k = 0; k < 16; k++) sA[17 * k] = a[b * 256 + r0 + 16 * k];
         __syncthreads();
 #pragma unroll
-        for (int k = 0; k < 16; k++) x[k] = sm[b * 256 + 16 * r0 + k];
+        for (int k = 0; k < 16; k++) x[k] = sB[k];
 #pragma unroll
-        for (int sp = 3; sp >= 0; sp--) {
-            const int h = 8 >> sp;
+        for (int sp = 3; sp >= 0; sp--)
+            stage16<true>(x, q, 8 >> sp, [&](int j) { return ld_tw(RB + ((1 << sp) - 1 + j) * 16, pol); });
 #pragma unroll
-            for (int k = 0; k < 16; k++) {
-                if (k & h) continue;
-                const int idx = (1 << (S1 + 4 + sp)) + (bg << (4 + sp)) + r0 * (8 / h) + k / (2 * h);
-                {
-                    const ulonglong2 t2 = ld_tw(T2 + idx, pol);
-                    bfly<true>(x[k], x[k + h], t2.x, t2.y, q);
-                }
-            }
-        }
+        for (int k = 0; k < 16; k++) sB[k] = x[k];   // own row: no barrier
         __syncthreads();
 #pragma unroll
-        for (int k = 0; k < 16; k++) sm[b * 256 + 16 * r0 + k] = x[k];
-        __syncthreads();
+        for (int k = 0; k < 16; k++) x[k] = sA[17 * k];
 #pragma unroll
-        for (int k = 0; k < 16; k++) x[k] = sm[b * 256 + r0 + 16 * k];
-#pragma unroll
-        for (int s = 3; s >= 0; s--) {
-            const int h = 8 >> s;
-#pragma unroll
-            for (int k = 0; k < 16; k++) {
-                if (k & h) continue;
-                const int idx = (1 << (S1 + s)) + (bg << s) + k / (2 * h);
-                {
-                    const ulonglong2 t2 = ld_tw(T2 + idx, pol);
-                    bfly<true>(x[k], x[k + h], t2.x, t2.y, q);
-                }
-            }
-        }
+        for (int s = 3; s >= 0; s--)
+            stage16<true>(x, q, 8 >> s, [&](int j) { return ld_tw(T2 + (1 << (S1 + s)) + (bg << s) + j, pol); });
 #pragma unroll
         for (int k = 0; k < 16; k++) a[b * 256 + r0 + 16 * k] = x[k];
     }
@@ -286,9 +240,9 @@ static void launch_ntt(const Context& cx, const LimbMap& mp, int count, bool inv
     dim3 gcol(R / 16, count), grow(N / 4096, count);
     if (!inv) {
         k_ntt_col<LOGN, false><<<gcol, 256, 0, st>>>(mp, (const ulonglong2*)cx.d_tw2, cx.d_ninv);
-        k_ntt_row<LOGN, false><<<grow, 256, 0, st>>>(mp, (const ulonglong2*)cx.d_tw2);
+        k_ntt_row<LOGN, false><<<grow, 256, 0, st>>>(mp, (const ulonglong2*)cx.d_tw2, (const ulonglong2*)cx.d_twrow);
     } else {
-        k_ntt_row<LOGN, true><<<grow, 256, 0, st>>>(mp, (const ulonglong2*)cx.d_itw2);
+        k_ntt_row<LOGN, true><<<grow, 256, 0, st>>>(mp, (const ulonglong2*)cx.d_itw2, (const ulonglong2*)cx.d_itwrow);
         k_ntt_col<LOGN, true><<<gcol, 256, 0, st>>>(mp, (const ulonglong2*)cx.d_itw2, cx.d_ninv);
     }
 }

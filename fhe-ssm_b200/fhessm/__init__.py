@@ -132,10 +132,13 @@ class Plaintext:
         self.ctx, self.h = ctx, h
 
     def __del__(self):
-        # a handle outliving its closed context is dropped (its memory went with the context)
-        if getattr(self, "h", None) and getattr(self.ctx, "h", None):
-            lib().fhe_pt_free(self.h)
-        self.h = None
+        try:
+            # a handle outliving its closed context is dropped (its memory went with the context)
+            if getattr(self, "h", None) and getattr(self.ctx, "h", None):
+                lib().fhe_pt_free(self.h)
+            self.h = None
+        except (TypeError, AttributeError):   # module globals already torn down at interpreter exit
+            pass
 
     @property
     def level(self):
@@ -147,9 +150,12 @@ class Ciphertext:
         self.ctx, self.h = ctx, h
 
     def __del__(self):
-        if getattr(self, "h", None) and getattr(self.ctx, "h", None):
-            lib().fhe_ct_free(self.h)
-        self.h = None
+        try:
+            if getattr(self, "h", None) and getattr(self.ctx, "h", None):
+                lib().fhe_ct_free(self.h)
+            self.h = None
+        except (TypeError, AttributeError):   # module globals already torn down at interpreter exit
+            pass
 
     @property
     def level(self):
@@ -171,9 +177,12 @@ class _MvPlan:
         self.h, self.ctx = h, ctx
 
     def __del__(self):
-        if getattr(self, "h", None) and (self.ctx is None or getattr(self.ctx, "h", None)):
-            lib().fhe_mvplan_free(self.h)
-        self.h = None
+        try:
+            if getattr(self, "h", None) and (self.ctx is None or getattr(self.ctx, "h", None)):
+                lib().fhe_mvplan_free(self.h)
+            self.h = None
+        except (TypeError, AttributeError):   # module globals already torn down at interpreter exit
+            pass
 
 
 def seed32(seed) -> bytes:
@@ -206,7 +215,10 @@ class CryptoContext:
             self.h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except (TypeError, AttributeError):   # module globals already torn down at interpreter exit
+            pass
 
     # ---- context info
     def GetScalingFactorReal(self, level):

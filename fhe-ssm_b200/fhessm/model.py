@@ -301,9 +301,12 @@ class EncryptedModel:
         return dict(zip(self.REFRESH_SITES, list(arr)))
 
     def __del__(self):
-        if getattr(self, "h", None) and getattr(self.ctx, "h", None):
-            lib().fhe_model_free(self.h)
-        self.h = None
+        try:
+            if getattr(self, "h", None) and getattr(self.ctx, "h", None):
+                lib().fhe_model_free(self.h)
+            self.h = None
+        except (TypeError, AttributeError):   # module globals already torn down at interpreter exit
+            pass
 
 
 def rel_err_rms(enc, ref):
