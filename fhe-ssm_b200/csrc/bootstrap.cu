@@ -204,7 +204,9 @@ static BootLevel build_level(Context& cx, int lo, int hi, bool inverse, int nl_i
 
 // All giants of one linear-transform level in one pass over the babies:
 // out_g[c][i][x] = sum_j pt_gj[i][x] * baby_j[c][i][x] (pt in Montgomery form, <= kDiagMax
-// products per 128-bit sum: hi < q for words < 2^60).  grid (N / 256, nl).
+// products per 128-bit sum: hi < q for words < 2^60).  A pair of threads shares slot x: the
+// even thread takes babies 0..7, the odd one babies 8..15; the two partial sums are added with
+// one shuffle and the even thread writes c = 0, the odd one c = 1.  grid (N / 128, nl).
 struct DiagArgs {
     const uint64_t* b0[kDiagMax];
     const uint64_t* b1[kDiagMax];
@@ -213,27 +215,34 @@ struct DiagArgs {
     uint64_t* o1[kDiagMax];
     int nb, ng;
 };
-__global__ void __launch_bounds__(256) k_diag_mac(const DiagArgs a, int logN, int nq, int L) {
+__global__ void __launch_bounds__(256, 4) k_diag_mac(const DiagArgs a, int logN, int nq, int L) {
+    constexpr int H = kDiagMax / 2;
     const int N = 1 << logN;
-    const int x = blockIdx.x * blockDim.x + threadIdx.x;
+    const int x = blockIdx.x * (blockDim.x / 2) + (threadIdx.x >> 1);
+    const int half = threadIdx.x & 1;
     const int i = blockIdx.y;   // limb: Q limbs below nq, then the special limbs
     const ModConst mc = c_mod[i < nq ? i : L + (i - nq)];
     const size_t w = (size_t)i * N + x;
-    uint64_t v0[kDiagMax], v1[kDiagMax];
+    const int j0 = half * H;
+    uint64_t v0[H], v1[H];
 #pragma unroll
-    for (int j = 0; j < kDiagMax; j++)
-        if (j < a.nb) { v0[j] = a.b0[j][w]; v1[j] = a.b1[j][w]; }
+    for (int j = 0; j < H; j++)
+        if (j0 + j < a.nb) { v0[j] = a.b0[j0 + j][w]; v1[j] = a.b1[j0 + j][w]; }
     for (int g = 0; g < a.ng; g++) {
         u128acc s0{0, 0}, s1{0, 0};
 #pragma unroll
-        for (int j = 0; j < kDiagMax; j++) {
-            if (j >= a.nb || !a.pt[g][j]) continue;
-            const uint64_t p = a.pt[g][j][w];
+        for (int j = 0; j < H; j++) {
+            if (j0 + j >= a.nb || !a.pt[g][j0 + j]) continue;
+            const uint64_t p = a.pt[g][j0 + j][w];
             acc_mad(s0, p, v0[j]);
             acc_mad(s1, p, v1[j]);
         }
-        a.o0[g][w] = redc(s0.hi, s0.lo, mc);
-        a.o1[g][w] = redc(s1.hi, s1.lo, mc);
+        // the partner's sum of the output this thread writes
+        const uint64_t mlo = half ? s0.lo : s1.lo, mhi = half ? s0.hi : s1.hi;
+        const uint64_t plo = __shfl_xor_sync(0xffffffffu, mlo, 1), phi = __shfl_xor_sync(0xffffffffu, mhi, 1);
+        u128acc t = half ? s1 : s0;
+        asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(t.lo), "+l"(t.hi) : "l"(plo), "l"(phi));
+        (half ? a.o1 : a.o0)[g][w] = redc(t.hi, t.lo, mc);
     }
 }
 
@@ -313,7 +322,7 @@ static void eval_level(Context& cx, const BootLevel& L, const Ciphertext& v, Cip
     da.ng = G;
     {
         ProfScope ps(cx, "diag_mac", 8.0 * N * nw * (2.0 * nb + 2.0 * G + (double)L.pts.size()));
-        k_diag_mac<<<dim3(N / 256, nw), 256, 0, st>>>(da, cx.logN, nl, cx.L);
+        k_diag_mac<<<dim3(N / 128, nw), 256, 0, st>>>(da, cx.logN, nl, cx.L);
         CUDA_CHECK(cudaGetLastError());
         cx.launches++;
     }

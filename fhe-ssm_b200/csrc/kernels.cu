@@ -66,6 +66,45 @@ __global__ void __launch_bounds__(256) k_modup_bconv(const uint64_t* __restrict_
     }
 }
 
+// ----------------------------------------------------- digit dot products (key switching) ----
+// Switching keys are streamed once per launch and are larger than L2: their loads skip L1 and
+// carry an L2 evict-first hint, so that the ModUp outputs and the NTT tables stay resident.
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t p;
+    asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t ld_stream(const uint64_t* a, uint64_t pol) {
+    uint64_t v;
+    asm("ld.global.nc.L1::no_allocate.L2::cache_hint.u64 %0, [%1], %2;" : "=l"(v) : "l"(a), "l"(pol));
+    return v;
+}
+constexpr int kDigitBatch = 4;
+// a0 += sum_j d[j ds] k0[j ks], a1 += sum_j d[j ds] k1[j ks] over the digits j < dn (128-bit
+// sums; key words in Montgomery form).  The 3 loads of up to kDigitBatch digits are all issued
+// before the first multiply, so a thread keeps them in flight together.
+__device__ __forceinline__ void digit_dot2(const uint64_t* __restrict__ d, size_t ds, const uint64_t* __restrict__ k0,
+                                           const uint64_t* __restrict__ k1, size_t ks, int dn, u128acc& a0,
+                                           u128acc& a1) {
+    const uint64_t pol = evict_first_policy();
+    for (int j0 = 0; j0 < dn; j0 += kDigitBatch) {
+        uint64_t dv[kDigitBatch], v0[kDigitBatch], v1[kDigitBatch];
+#pragma unroll
+        for (int j = 0; j < kDigitBatch; j++)
+            if (j0 + j < dn) {
+                dv[j] = d[(size_t)(j0 + j) * ds];
+                v0[j] = ld_stream(k0 + (size_t)(j0 + j) * ks, pol);
+                v1[j] = ld_stream(k1 + (size_t)(j0 + j) * ks, pol);
+            }
+#pragma unroll
+        for (int j = 0; j < kDigitBatch; j++)
+            if (j0 + j < dn) {
+                acc_mad(a0, dv[j], v0[j]);
+                acc_mad(a1, dv[j], v1[j]);
+            }
+    }
+}
+
 // ------------------------------------------------------------------- key inner product ----
 // out[c][e] = sum_j ext[j][e] * key[j][c][m(e)]  (key in Montgomery form -> canonical result)
 __global__ void k_key_inner(const uint64_t* __restrict__ ext, const uint64_t* __restrict__ key,
@@ -77,13 +116,8 @@ __global__ void k_key_inner(const uint64_t* __restrict__ ext, const uint64_t* __
     const ModConst mc = c_mod[m];
     const size_t nk = (size_t)(L + K);
     u128acc a0{0, 0}, a1{0, 0};
-    for (int j = 0; j < dnum; j++) {
-        const uint64_t d = ext[((size_t)j * ne + e) * N + x];
-        const uint64_t kb = key[(((size_t)j * 2 + 0) * nk + m) * N + x];
-        const uint64_t ka = key[(((size_t)j * 2 + 1) * nk + m) * N + x];
-        acc_mad(a0, d, kb);
-        acc_mad(a1, d, ka);
-    }
+    digit_dot2(ext + (size_t)e * N + x, (size_t)ne * N, key + (size_t)m * N + x, key + (nk + m) * N + x, 2 * nk * N,
+               dnum, a0, a1);
     out[(size_t)e * N + x] = redc(a0.hi, a0.lo, mc);
     out[((size_t)ne + e) * N + x] = redc(a1.hi, a1.lo, mc);
 }

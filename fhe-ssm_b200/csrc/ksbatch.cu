@@ -55,11 +55,8 @@ __global__ void __launch_bounds__(256) k_key_inner_b(const uint64_t* __restrict_
         const uint64_t* eb = ext + b * ext_stride;
         const uint64_t* key = kb.k[b];
         u128acc a0{0, 0}, a1{0, 0};
-        for (int j = 0; j < dnum; j++) {
-            const uint64_t d = eb[((size_t)j * ne + e) * N + x];
-            acc_mad(a0, d, key[(((size_t)j * 2 + 0) * nk + m) * N + x]);
-            acc_mad(a1, d, key[(((size_t)j * 2 + 1) * nk + m) * N + x]);
-        }
+        digit_dot2(eb + (size_t)e * N + x, (size_t)ne * N, key + (size_t)m * N + x, key + (nk + m) * N + x,
+                   2 * nk * N, dnum, a0, a1);
         uint64_t* o = out + (size_t)b * 2 * ne * N;
         o[(size_t)e * N + x] = redc(a0.hi, a0.lo, mc);
         o[((size_t)ne + e) * N + x] = redc(a1.hi, a1.lo, mc);
@@ -74,11 +71,8 @@ __global__ void __launch_bounds__(256) k_key_inner_b(const uint64_t* __restrict_
         const uint64_t* eb = ext + b * ext_stride;
         const uint64_t* key = kb.k[b];
         u128acc a0{0, 0}, a1{0, 0};
-        for (int j = 0; j < dnum; j++) {
-            const uint64_t d = eb[((size_t)j * ne + e) * N + x];
-            acc_mad(a0, d, key[(((size_t)j * 2 + 0) * nk + m) * N + x]);
-            acc_mad(a1, d, key[(((size_t)j * 2 + 1) * nk + m) * N + x]);
-        }
+        digit_dot2(eb + (size_t)e * N + x, (size_t)ne * N, key + (size_t)m * N + x, key + (nk + m) * N + x,
+                   2 * nk * N, dnum, a0, a1);
         s0 = mod_add(s0, redc(a0.hi, a0.lo, mc), mc.q);
         s1 = mod_add(s1, redc(a1.hi, a1.lo, mc), mc.q);
     }

@@ -418,11 +418,8 @@ __global__ void __launch_bounds__(256) k_baby_pq(const uint64_t* __restrict__ ex
         const uint64_t* key = a.fkey[b];
         const size_t nk = (size_t)(L + K);
         u128acc a0{0, 0}, a1{0, 0};
-        for (int d = 0; d < dn; d++) {
-            const uint64_t dv = ext[((size_t)d * ne + e) * N + sx];
-            acc_mad(a0, dv, key[(((size_t)d * 2 + 0) * nk + m) * N + x]);
-            acc_mad(a1, dv, key[(((size_t)d * 2 + 1) * nk + m) * N + x]);
-        }
+        digit_dot2(ext + (size_t)e * N + sx, (size_t)ne * N, key + (size_t)m * N + x, key + (nk + m) * N + x,
+                   2 * nk * N, dn, a0, a1);
         v0 = redc(a0.hi, a0.lo, mc);
         v1 = redc(a1.hi, a1.lo, mc);
         if (e < nl) v0 = mod_add(v0, mul_shoup(u0[(size_t)e * N + sx], a.pw[e], a.pwp[e], mc.q), mc.q);
