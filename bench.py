@@ -248,7 +248,10 @@ def run_model(args, ws, rank, local):
     outs = []
     for i in range(args.warmup):
         outs.append(m.step(cts[i]))
-    cx.sync()
+        cx.sync()
+        mem = cx.memory()
+        print(f"warmup pass {i}: memory GiB " + ", ".join(f"{k} {v / 2**30:.1f}" for k, v in mem.items()),
+              file=sys.stderr, flush=True)
     barrier(ws)
     clk = ClockSampler(local)
     clk.start()
@@ -325,6 +328,7 @@ def run_model(args, ws, rank, local):
             "bootstraps_per_pass": boots, "keyswitches_per_pass": ks_per_pass, "setup_s": setup_s,
             "gpu_launches": launches, "clocks": clocks, "e2e": e2e, "roofline": roofline(prof), "cpu_baseline": cpu,
             "kernels": kernel_table(prof),
+            "memory_gib": {k: round(v / 2**30, 2) for k, v in cx.memory().items()},
         }
         print(json.dumps(line), flush=True)
 

@@ -97,7 +97,27 @@ int fhe_ctx_set_option(fhe_ctx* cx, const char* name, int value) {
         if (std::strcmp(name, "matvec_tensor_cores") == 0) cx->cx.use_tc = value != 0;
         else if (std::strcmp(name, "merged_rescale") == 0) cx->cx.merged_rescale = value != 0;
         else if (std::strcmp(name, "profile_every") == 0) cx->cx.prof_every = value < 1 ? 1 : value;
+        else if (std::strcmp(name, "plaintext_cache") == 0) cx->cx.pt_cache = value != 0;
+        else if (std::strcmp(name, "plaintext_cache_reserve_mib") == 0) cx->cx.pt_cache_reserve_mib = value < 0 ? 0 : value;
         else throw fhe::Error(std::string("unknown option ") + name, FHE_ERR_ARG);
+    });
+}
+int fhe_ctx_memory(fhe_ctx* cx, long long* out) {
+    return guard([&] {
+        REQUIRE(cx && out, "null argument");
+        bind(cx);
+        size_t fr = 0, tot = 0;
+        CUDA_CHECK(cudaMemGetInfo(&fr, &tot));
+        cudaMemPool_t pool;
+        CUDA_CHECK(cudaDeviceGetDefaultMemPool(&pool, cx->cx.prm.device));
+        uint64_t res = 0, used = 0;
+        CUDA_CHECK(cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReservedMemCurrent, &res));
+        CUDA_CHECK(cudaMemPoolGetAttribute(pool, cudaMemPoolAttrUsedMemCurrent, &used));
+        out[0] = (long long)fr;
+        out[1] = (long long)tot;
+        out[2] = (long long)res;
+        out[3] = (long long)used;
+        out[4] = cx->cx.pt_cache_bytes;
     });
 }
 long long fhe_ctx_launches(const fhe_ctx* cx) { return cx ? cx->cx.launches : 0; }

@@ -125,6 +125,12 @@ struct Context {
     unsigned int* d_err = nullptr;   // set by a kernel whose bounded wait ran out (checked at syncs)
     int use_tc = 1;                  // BSGS products on the tensor cores (tcgen05) where the shape allows
     int merged_rescale = 1;          // circuit products: ModDown and rescale in one division by P q_l
+    // BSGS plaintext cache (the reference's --cache-diags, gpu_real_model.cu:1647-1652, off by
+    // default as there): a plan keeps the plaintext words of its last call while at least
+    // pt_cache_reserve_mib of device memory stays free
+    int pt_cache = 0;
+    long long pt_cache_reserve_mib = 24 * 1024;
+    long long pt_cache_bytes = 0;    // held by the plans of this context
     std::map<int, uint64_t*> modup_tab;   // per nl: [dnum][alpha][2] qhat^-1, [dnum][ne][alpha][2] qhat mod t
     std::map<int, uint64_t*> mdr_tab;     // per nl: ModDown + rescale in one step (ct_mul_relin_rescale)
     // keys

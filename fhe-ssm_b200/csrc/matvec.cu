@@ -434,6 +434,16 @@ struct MatvecPlan {
     std::vector<int> ids;     // [set][3][G][b1]
     DevBuf d_ids;             // int table (packed into uint64 words)
     DevBuf coef;              // [P][2D] fp64 bit patterns
+    // plaintext words of the last call ([ne][2D][P] at level cached_nl, plaintext scale
+    // cached_spt), kept under the context's plaintext-cache budget: a recurrent model applies
+    // every matrix at the same level and scale on every step
+    mutable DevBuf cached;
+    mutable int cached_nl = 0;
+    mutable double cached_spt = 0.0;
+    Context* owner = nullptr;
+    ~MatvecPlan() {
+        if (owner && cached.p) owner->pt_cache_bytes -= (long long)(cached.words * 8);
+    }
 };
 
 static void fft_special_inv_small(std::complex<double>* v, int n, int M) {
@@ -467,6 +477,7 @@ std::shared_ptr<MatvecPlan> matvec_plan(Context& cx, const double* W, int rows, 
     if (D < 2 || (D & (D - 1)) || n % D || rows > D || b1 < 1 || D % b1)
         throw Error("matvec_plan: need D | N/2 (power of two), rows <= D, b1 | D", -1);
     auto pl = std::make_shared<MatvecPlan>();
+    pl->owner = &cx;
     pl->D = D; pl->b1 = b1; pl->G = D / b1; pl->rows = rows; pl->cols = cols;
     pl->nsets = (cols + D - 1) / D;
     const int G = pl->G, S = pl->nsets;
@@ -650,8 +661,11 @@ void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets,
     if (TW < 8) throw Error("matvec: D too large for the ring (need N / 2D >= 8)", -1);
     const int M = 2 * G;
     if ((TW / 2) * (M / 2) > 512 || M % 2) throw Error("matvec: too many giant steps for one CTA", -1);
-    DevBuf pts((size_t)std::max(pl.P, 1) * ne * 2 * D, st);
-    if (pl.P > 0 && logD2 == 11) {
+    const bool hit = pl.cached.p && pl.cached_nl == nl && pl.cached_spt == spt;
+    DevBuf pts(hit ? 0 : (size_t)std::max(pl.P, 1) * ne * 2 * D, st);
+    if (hit) {
+        // words of an earlier call at this level and scale
+    } else if (pl.P > 0 && logD2 == 11) {
         const size_t smem = (size_t)(2 + 4) * 2048 * 8;
         CUDA_CHECK(cudaFuncSetAttribute(k_ptgen2048, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         ProfScope ps(cx, "ptgen", 8.0 * pl.P * 2 * D * (1 + ne));
@@ -670,12 +684,30 @@ void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets,
         CUDA_CHECK(cudaGetLastError());
         cx.launches++;
     }
+    if (!hit && cx.pt_cache && pl.P > 0) {
+        // keep these words for the next call if the budget allows (replacing an entry of
+        // another level or scale)
+        const long long bytes = (long long)(pts.words * 8);
+        if (pl.cached.p) {
+            cx.pt_cache_bytes -= (long long)(pl.cached.words * 8);
+            pl.cached = DevBuf();
+        }
+        size_t fr = 0, tot = 0;
+        CUDA_CHECK(cudaMemGetInfo(&fr, &tot));
+        if ((long long)fr - bytes >= cx.pt_cache_reserve_mib * (1ll << 20)) {
+            pl.cached = std::move(pts);
+            pl.cached_nl = nl;
+            pl.cached_spt = spt;
+            cx.pt_cache_bytes += bytes;
+        }
+    }
+    const uint64_t* ptsrc = pts.p ? pts.p : pl.cached.p;   // this call's words, or the cached ones
     DevBuf inner((size_t)M * 2 * ne * N, st);
     {
         GemmArgs a{};
         for (int s = 0; s < S; s++) a.babies[s] = sets[s]->pq.p;
         a.ids = (const int*)pl.d_ids.p;
-        a.pts = pts.p;
+        a.pts = ptsrc;
         a.out = inner.p;
         a.nsets = S; a.b1 = b1; a.G = G; a.nl = nl; a.ne = ne; a.L = cx.L; a.logN = cx.logN; a.lr = lr;
         a.D2 = 2 * D; a.P = std::max(pl.P, 1); a.TW = TW;
@@ -712,7 +744,7 @@ void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets,
                     CUDA_CHECK(cudaFuncSetAttribute(k_tc_pack_w, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wblk));
                 ProfScope ps(cx, "tc_pack_w", (double)S * ne * 2 * D * wblk + 8.0 * pl.P * ne * 2 * D);
                 for (int s = 0; s < S; s++) {
-                    k_tc_pack_w<<<dim3(2 * D, ne), 256, wblk, st>>>(pts.p, (const int*)pl.d_ids.p,
+                    k_tc_pack_w<<<dim3(2 * D, ne), 256, wblk, st>>>(ptsrc, (const int*)pl.d_ids.p,
                                                                   (uint8_t*)wpack.p + (size_t)s * ne * 2 * D * wblk, s, G,
                                                                   b1, Kp, M, 2 * D, std::max(pl.P, 1));
                     cx.launches++;

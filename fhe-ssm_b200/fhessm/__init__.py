@@ -242,8 +242,20 @@ class CryptoContext:
         _check(h.fhe_ctx_counters(self.h, C.byref(k), C.byref(l)))
         return k.value, l.value
 
+    def memory(self):
+        """Device memory in bytes: free, total, held by the stream-ordered pool, live in the
+        pool, cached BSGS plaintexts."""
+        h = lib()
+        h.fhe_ctx_memory.restype = C.c_int
+        h.fhe_ctx_memory.argtypes = [_VP, C.POINTER(C.c_longlong)]
+        out = (C.c_longlong * 5)()
+        _check(h.fhe_ctx_memory(self.h, out))
+        return dict(zip(("free", "total", "pool_reserved", "pool_used", "pt_cache"), list(out)))
+
     def set_option(self, name, value):
-        """Engine switches: "matvec_tensor_cores" (1 = tcgen05 BSGS products, 0 = CUDA cores)."""
+        """Engine switches: "matvec_tensor_cores" (1 = tcgen05 BSGS products, 0 = CUDA cores),
+        "merged_rescale", "profile_every", "plaintext_cache" (1 = a BSGS plan keeps its plaintext
+        words for the next call at the same level and scale), "plaintext_cache_reserve_mib"."""
         _check(lib().fhe_ctx_set_option(self.h, name.encode(), int(value)))
 
     def stream_ptr(self):

@@ -67,6 +67,9 @@ int fhe_ctx_moduli(const fhe_ctx* cx, uint64_t* out);
 /* FLEXIBLEAUTO scaling factor at `level` (CryptoParametersRNS::GetScalingFactorReal) */
 double fhe_ctx_scale(const fhe_ctx* cx, int level);
 int fhe_ctx_sync(fhe_ctx* cx);
+/* device memory: out[0] free bytes, out[1] total, out[2] bytes the stream-ordered pool holds,
+ * out[3] bytes of it in live buffers, out[4] bytes of cached BSGS plaintexts */
+int fhe_ctx_memory(fhe_ctx* cx, long long* out);
 /* kernel launches issued by this context so far */
 long long fhe_ctx_launches(const fhe_ctx* cx);
 /* key switches issued so far and the sum of their limb counts (operation census) */
@@ -78,7 +81,12 @@ void* fhe_ctx_stream(const fhe_ctx* cx);
  * "merged_rescale" (default 1): circuit products divide by P q_l once (ModDown and rescale
  * merged); 0 runs ModDown and rescale separately.
  * "profile_every" (default 1): the per-kernel timer times one scope in this many of each kind
- * and scales the totals (keeps the timer's own cost out of a timed region). */
+ * and scales the totals (keeps the timer's own cost out of a timed region).
+ * "plaintext_cache" (default 0): 1 = a BSGS plan keeps the plaintext words of its last call
+ * (level and scale) resident and reuses them when the next call has the same level and scale,
+ * the reference's --cache-diags (gpu_real_model.cu:1647-1652, also off by default there).
+ * "plaintext_cache_reserve_mib" (default 24576): a plan caches only while this much device
+ * memory would stay free. */
 int fhe_ctx_set_option(fhe_ctx* cx, const char* name, int value);
 /* per-kernel CUDA-event timing on the context's stream (off by default).  collect
  * synchronises, writes {"kernel": [launches, total_ms, algorithmic_bytes], ...} as JSON

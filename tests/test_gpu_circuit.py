@@ -153,6 +153,31 @@ def test_matvec_tensor_core_products_bit_identical(cx, b1):
     assert np.abs(got - U @ W.T).max() < 1e-5
 
 
+def test_plaintext_cache_bit_identical(cx):
+    """The plan's plaintext cache (the reference's --cache-diags): a repeated call at the same
+    level and scale reuses the cached words, a call at another level regenerates them, and
+    every result equals the uncached one word for word."""
+    D, b1 = 128, 8
+    cx.matvec_keygen(D, b1)
+    rng = np.random.default_rng(31)
+    W = rng.normal(0, 0.3, (D, D))
+    R = cx.slots // D
+    U = rng.uniform(-1, 1, (2 * R, D))
+    plan = cx.matvec_plan(W, D, b1)
+    res = {}
+    for lvl in (1, 2):
+        ct = cx.Encrypt(cx.MakeCKKSPackedPlaintext(block_pack(U, D, cx.slots), level=lvl))
+        cx.set_option("plaintext_cache", 1)
+        first = cx.matvec(plan, [ct]).words()
+        again = cx.matvec(plan, [ct]).words()      # served from the cache
+        cx.set_option("plaintext_cache", 0)
+        fresh = cx.matvec(plan, [ct]).words()
+        cx.set_option("plaintext_cache", 1)
+        assert (first == again).all() and (first == fresh).all()
+        res[lvl] = first
+    assert res[1].shape != res[2].shape
+
+
 def test_matvec_1024_block():
     """A 1024-wide block (the model's D) at N = 2^14: the 2048-point plaintext generation and
     the double-hoisted BSGS with b1 = 64 against numpy, every lane different."""
