@@ -236,6 +236,14 @@ Context::Context(const Params& p) : prm(p) {
         d_itwrow = dev_upload(vr);
     }
     d_ninv = dev_upload(ninv);
+    {
+        std::vector<uint64_t> rm(2 * nm);
+        for (int m = 0; m < nm; m++) {
+            rm[2 * m] = (uint64_t)(((unsigned __int128)1 << 64) % mods[m]);
+            rm[2 * m + 1] = shoup_of(rm[2 * m], mods[m]);
+        }
+        d_rmont = dev_upload(rm);
+    }
     // FLEXIBLEAUTO scaling factors: scale_at[top] = q_{top-1}; scale_at[nl] = scale_at[nl+1]^2 / q_nl,
     // anchored separately at the top of each prime region (user region, bootstrap region)
     scale_at.assign(L + 1, 0.0);
@@ -296,7 +304,8 @@ Context::~Context() {
     sk = DevBuf();
     pk = DevBuf();
     if (stream) cudaStreamSynchronize(stream);
-    for (auto* p : {d_tw, d_twp, d_itw, d_itwp, d_ninv, d_md, d_rs, d_tw2, d_itw2, d_twrow, d_itwrow}) if (p) cudaFree(p);
+    for (auto* p : {d_tw, d_twp, d_itw, d_itwp, d_ninv, d_md, d_rs, d_tw2, d_itw2, d_twrow, d_itwrow, d_rmont})
+        if (p) cudaFree(p);
     if (d_err) cudaFree(d_err);
     for (auto& kv : modup_tab) cudaFree(kv.second);
     for (auto& kv : mdr_tab) cudaFree(kv.second);

@@ -119,6 +119,7 @@ struct Context {
     uint64_t *d_tw = nullptr, *d_twp = nullptr, *d_itw = nullptr, *d_itwp = nullptr, *d_ninv = nullptr;
     uint64_t *d_tw2 = nullptr, *d_itw2 = nullptr;   // the same tables as (twiddle, Shoup) pairs for the NTT kernels
     uint64_t *d_twrow = nullptr, *d_itwrow = nullptr;   // last-four-stage twiddles in the row kernel's access order
+    uint64_t* d_rmont = nullptr;     // [L+K][2]: 2^64 mod q (+ Shoup), the factor into Montgomery form
     // ModDown / rescale constants (level independent): see build_tables()
     uint64_t* d_md = nullptr;        // ModDown: [K] phatinv (+shoup), [L][K] phat mod q_i (+shoup), [L] Pinv (+shoup)
     uint64_t* d_rs = nullptr;        // rescale: [L][L] (ql mod qi, ql^-1 mod qi, shoup)

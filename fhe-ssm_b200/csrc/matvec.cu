@@ -94,22 +94,20 @@ __global__ void __launch_bounds__(256) k_ptgen(const double* __restrict__ coef, 
 // 2048-point specialisation of k_ptgen (D = 1024, the model's block): one plaintext at a time
 // in registers, 8 words per thread, 11 butterfly stages in 4 passes (3 + 3 + 3 + 2) with three
 // exchanges through shared memory; the limb's twiddles are staged in shared memory once per CTA,
-// and 4 plaintexts are written together (32-byte runs of the transposed layout).  Same
-// arithmetic as k_ptgen (canonical Shoup butterflies): identical words.
-__device__ __forceinline__ void pg_bfly(uint64_t& a, uint64_t& b, uint64_t w, uint64_t wp, uint64_t q) {
-    const uint64_t x = mul_shoup(b, w, wp, q);
-    const uint64_t u = a;
-    a = mod_add(u, x, q);
-    b = mod_sub(u, x, q);
+// and 4 plaintexts are written together (32-byte runs of the transposed layout).  The
+// butterflies are the lazy ones of the ring NTT (values in [0, 4q + 2^32), twiddle and Shoup
+// companion read as one 16-byte pair); the output is made canonical, or taken to Montgomery
+// form by a Shoup product with 2^64 mod q: the same words as k_ptgen.
+__device__ __forceinline__ void pgl(uint64_t& a, uint64_t& b, const ulonglong2 t, uint64_t q) {
+    bfly<false>(a, b, t.x, t.y, q);
 }
 __global__ void __launch_bounds__(256) k_ptgen2048(const double* __restrict__ coef, double scale,
                                                    uint64_t* __restrict__ out, int P, int nq, int L,
-                                                   const uint64_t* __restrict__ tw, const uint64_t* __restrict__ twp,
-                                                   int N, int mont) {
+                                                   const ulonglong2* __restrict__ tw2,
+                                                   const uint64_t* __restrict__ rmont, int N, int mont) {
     constexpr int D2 = 2048, IPC = 4;
     extern __shared__ uint64_t pg[];
-    uint64_t* T = pg;              // [D2]
-    uint64_t* Tp = pg + D2;        // [D2]
+    ulonglong2* T = reinterpret_cast<ulonglong2*>(pg);   // [D2] (twiddle, Shoup companion) pairs
     uint64_t* S = pg + 2 * D2;     // [IPC][D2]: exchange buffer of plaintext t, then its result
     const int tid = threadIdx.x;
     const int id0 = blockIdx.x * IPC, i = blockIdx.y;
@@ -123,10 +121,8 @@ __global__ void __launch_bounds__(256) k_ptgen2048(const double* __restrict__ co
 #pragma unroll
         for (int k = 0; k < 8; k++)
             cf[t][k] = id0 + t < P ? coef[(size_t)(id0 + t) * D2 + tid + 256 * k] : 0.0;
-    for (int k = tid; k < D2; k += 256) {
-        T[k] = tw[(size_t)m * N + k];
-        Tp[k] = twp[(size_t)m * N + k];
-    }
+    for (int k = tid; k < D2; k += 256) T[k] = tw2[(size_t)m * N + k];
+    const uint64_t rq = rmont[2 * m], rqp = rmont[2 * m + 1];   // 2^64 mod q (+ Shoup): Montgomery form
     __syncthreads();
 #pragma unroll
     for (int t = 0; t < IPC; t++) {
@@ -138,12 +134,12 @@ __global__ void __launch_bounds__(256) k_ptgen2048(const double* __restrict__ co
             x[k] = r >= 0 ? reduce64((uint64_t)r, mc) : mod_neg(reduce64((uint64_t)(-r), mc), q);
         }
         // pass 1: elements tid + 256 k, distances 1024, 512, 256
-        pg_bfly(x[0], x[4], T[1], Tp[1], q); pg_bfly(x[1], x[5], T[1], Tp[1], q);
-        pg_bfly(x[2], x[6], T[1], Tp[1], q); pg_bfly(x[3], x[7], T[1], Tp[1], q);
+        pgl(x[0], x[4], T[1], q); pgl(x[1], x[5], T[1], q);
+        pgl(x[2], x[6], T[1], q); pgl(x[3], x[7], T[1], q);
 #pragma unroll
-        for (int k = 0; k < 8; k++) if ((k & 2) == 0) pg_bfly(x[k], x[k + 2], T[2 + k / 4], Tp[2 + k / 4], q);
+        for (int k = 0; k < 8; k++) if ((k & 2) == 0) pgl(x[k], x[k + 2], T[2 + k / 4], q);
 #pragma unroll
-        for (int k = 0; k < 8; k += 2) pg_bfly(x[k], x[k + 1], T[4 + k / 2], Tp[4 + k / 2], q);
+        for (int k = 0; k < 8; k += 2) pgl(x[k], x[k + 1], T[4 + k / 2], q);
 #pragma unroll
         for (int k = 0; k < 8; k++) Sb[tid + 256 * k] = x[k];
         __syncthreads();
@@ -153,11 +149,11 @@ __global__ void __launch_bounds__(256) k_ptgen2048(const double* __restrict__ co
 #pragma unroll
             for (int k = 0; k < 8; k++) x[k] = Sb[blk * 256 + r + 32 * k];
 #pragma unroll
-            for (int k = 0; k < 4; k++) pg_bfly(x[k], x[k + 4], T[8 + blk], Tp[8 + blk], q);
+            for (int k = 0; k < 4; k++) pgl(x[k], x[k + 4], T[8 + blk], q);
 #pragma unroll
-            for (int k = 0; k < 8; k++) if ((k & 2) == 0) pg_bfly(x[k], x[k + 2], T[16 + 2 * blk + k / 4], Tp[16 + 2 * blk + k / 4], q);
+            for (int k = 0; k < 8; k++) if ((k & 2) == 0) pgl(x[k], x[k + 2], T[16 + 2 * blk + k / 4], q);
 #pragma unroll
-            for (int k = 0; k < 8; k += 2) pg_bfly(x[k], x[k + 1], T[32 + 4 * blk + k / 2], Tp[32 + 4 * blk + k / 2], q);
+            for (int k = 0; k < 8; k += 2) pgl(x[k], x[k + 1], T[32 + 4 * blk + k / 2], q);
             __syncthreads();
 #pragma unroll
             for (int k = 0; k < 8; k++) Sb[blk * 256 + r + 32 * k] = x[k];
@@ -169,11 +165,11 @@ __global__ void __launch_bounds__(256) k_ptgen2048(const double* __restrict__ co
 #pragma unroll
             for (int k = 0; k < 8; k++) x[k] = Sb[g * 32 + r + 4 * k];
 #pragma unroll
-            for (int k = 0; k < 4; k++) pg_bfly(x[k], x[k + 4], T[64 + g], Tp[64 + g], q);
+            for (int k = 0; k < 4; k++) pgl(x[k], x[k + 4], T[64 + g], q);
 #pragma unroll
-            for (int k = 0; k < 8; k++) if ((k & 2) == 0) pg_bfly(x[k], x[k + 2], T[128 + 2 * g + k / 4], Tp[128 + 2 * g + k / 4], q);
+            for (int k = 0; k < 8; k++) if ((k & 2) == 0) pgl(x[k], x[k + 2], T[128 + 2 * g + k / 4], q);
 #pragma unroll
-            for (int k = 0; k < 8; k += 2) pg_bfly(x[k], x[k + 1], T[256 + 4 * g + k / 2], Tp[256 + 4 * g + k / 2], q);
+            for (int k = 0; k < 8; k += 2) pgl(x[k], x[k + 1], T[256 + 4 * g + k / 2], q);
             __syncthreads();
 #pragma unroll
             for (int k = 0; k < 8; k++) Sb[g * 32 + r + 4 * k] = x[k];
@@ -184,14 +180,14 @@ __global__ void __launch_bounds__(256) k_ptgen2048(const double* __restrict__ co
 #pragma unroll
             for (int k = 0; k < 8; k++) x[k] = Sb[8 * tid + k];
 #pragma unroll
-            for (int k = 0; k < 8; k++) if ((k & 2) == 0) pg_bfly(x[k], x[k + 2], T[512 + 2 * tid + k / 4], Tp[512 + 2 * tid + k / 4], q);
+            for (int k = 0; k < 8; k++) if ((k & 2) == 0) pgl(x[k], x[k + 2], T[512 + 2 * tid + k / 4], q);
 #pragma unroll
-            for (int k = 0; k < 8; k += 2) pg_bfly(x[k], x[k + 1], T[1024 + 4 * tid + k / 2], Tp[1024 + 4 * tid + k / 2], q);
+            for (int k = 0; k < 8; k += 2) pgl(x[k], x[k + 1], T[1024 + 4 * tid + k / 2], q);
             __syncthreads();
 #pragma unroll
             for (int k = 0; k < 8; k++) {
                 const uint64_t v = x[k];
-                Sb[8 * tid + k] = mont ? redc(__umul64hi(v, mc.r2), v * mc.r2, mc) : v;
+                Sb[8 * tid + k] = mont ? mul_shoup(v, rq, rqp, q) : canon4(v, q);
             }
         }
         __syncthreads();
@@ -670,7 +666,7 @@ void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets,
         CUDA_CHECK(cudaFuncSetAttribute(k_ptgen2048, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         ProfScope ps(cx, "ptgen", 8.0 * pl.P * 2 * D * (1 + ne));
         k_ptgen2048<<<dim3((pl.P + 3) / 4, ne), 256, smem, st>>>((const double*)pl.coef.p, spt, pts.p, pl.P, nl, cx.L,
-                                                                cx.d_tw, cx.d_twp, N, 1);
+                                                                (const ulonglong2*)cx.d_tw2, cx.d_rmont, N, 1);
         CUDA_CHECK(cudaGetLastError());
         cx.launches++;
     } else if (pl.P > 0) {
