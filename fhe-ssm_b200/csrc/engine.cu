@@ -335,7 +335,7 @@ const uint64_t* Context::modup_table(int nl) {
                 for (int b = 0; b < sz; b++) if (b != a) v = host_mulmod(v, mods[lo + b] % t, t);
                 const size_t o = (size_t)dn * alpha * 2 + (((size_t)j * ne + e) * alpha + a) * 2;
                 tab[o] = v;
-                tab[o + 1] = shoup_of(v, t);
+                tab[o + 1] = mont_of(v, t);
             }
         }
     }

@@ -23,7 +23,8 @@ __device__ __forceinline__ uint32_t auto_src(uint32_t i, uint64_t k, int logN) {
 // dcoef: the nl Q-limbs in coefficient form; deval: the same limbs in eval form.
 // ext[j][e] for digit j: own limbs copied from deval, all others base-converted (coefficient
 // form, NTT'd afterwards).  blockIdx.z indexes a batch of inputs (strides sdc, sdv, sext).  tab: [dnum][alpha][2] (qhat^-1 mod q_i, shoup) then
-// [dnum][ne][alpha][2] (qhat mod t, shoup).
+// [dnum][ne][alpha][2] (qhat mod t, qhat 2^64 mod t): each output is one 128-bit sum of
+// products with the Montgomery-form constants and one Montgomery reduction.
 __global__ void __launch_bounds__(256) k_modup_bconv(const uint64_t* __restrict__ dcoef,
                                                      const uint64_t* __restrict__ deval, uint64_t* __restrict__ ext,
                                                      const uint64_t* __restrict__ tab, int nl, int ne, int alpha, int L,
@@ -55,14 +56,13 @@ __global__ void __launch_bounds__(256) k_modup_bconv(const uint64_t* __restrict_
             out[(size_t)e * N + x] = deval[(size_t)e * N + x];
             continue;
         }
-        const int m = e < nl ? e : L + (e - nl);
-        const uint64_t q = c_mod[m].q;
+        const ModConst mt = c_mod[e < nl ? e : L + (e - nl)];
         const uint64_t* w = sw + e * alpha * 2;
-        uint64_t s = 0;
+        u128acc s{0, 0};
 #pragma unroll
-        for (int a = 0; a < 8; a++)
-            if (a < sz) s += mul_shoup_lazy(t[a], w[2 * a], w[2 * a + 1], q);   // < 2q each: s < 16q < 2^64
-        out[(size_t)e * N + x] = reduce_lazy16(s, q);
+        for (int a = 0; a < 8; a++)   // constants in Montgomery form: sum < 8 2^60 t < t 2^64
+            if (a < sz) acc_mad(s, t[a], w[2 * a + 1]);
+        out[(size_t)e * N + x] = redc(s.hi, s.lo, mt);
     }
 }
 

@@ -110,3 +110,4 @@ inline uint64_t host_powmod(uint64_t a, uint64_t e, uint64_t q) {
 }
 inline uint64_t host_invmod(uint64_t a, uint64_t q) { return host_powmod(a, q - 2, q); }
 inline uint64_t shoup_of(uint64_t w, uint64_t q) { return (uint64_t)(((unsigned __int128)w << 64) / q); }
+inline uint64_t mont_of(uint64_t w, uint64_t q) { return (uint64_t)(((unsigned __int128)w << 64) % q); }   // w 2^64 mod q

@@ -97,8 +97,8 @@ static void keyswitch_noalloc(Context& cx, const uint64_t* d, int nl, const Swit
     uint64_t* B = A + (size_t)std::max(nl, 2 * ne) * N;
     uint64_t* T = B + (size_t)std::max(dn * ne, 2 * nl) * N;
 
-    // ModUp table: [dn][alpha] (Q_j/q_a)^-1 mod q_a, then [dn][ne][alpha] (Q_j/q_a) mod m(e),
-    // each with its Shoup companion
+    // ModUp table (the layout of Context::modup_table): [dn][alpha] (Q_j/q_a)^-1 mod q_a with its
+    // Shoup companion, then [dn][ne][alpha] (Q_j/q_a) mod m(e) with its Montgomery form
     NoAllocTab tab;
     const int tw = noalloc_tab_words(cx, nl);
     for (int i = 0; i < tw; i++) tab.w[i] = 0;
@@ -120,7 +120,7 @@ static void keyswitch_noalloc(Context& cx, const uint64_t* d, int nl, const Swit
                 for (int b = 0; b < sz; b++) if (b != a) v = host_mulmod(v, cx.mods[lo + b] % t, t);
                 const int o = dn * alpha * 2 + ((j * ne + e) * alpha + a) * 2;
                 tab.w[o] = v;
-                tab.w[o + 1] = shoup_of(v, t);
+                tab.w[o + 1] = mont_of(v, t);
             }
         }
     }
