@@ -38,6 +38,7 @@ void split_complex(Context& cx, const Ciphertext& z, Ciphertext& re, Ciphertext&
 void merge_complex(Context& cx, Ciphertext re, Ciphertext im, Ciphertext& z);
 void cheb_eval(Context& cx, const Ciphertext& x, const std::vector<double>& coeffs, Ciphertext& out);
 void cheb_eval_n(Context& cx, const Ciphertext* const* x, int K, const std::vector<double>& coeffs, Ciphertext* out);
+int cheb_depth(const std::vector<double>& coeffs);
 void mul_rescale_n(Context& cx, const Ciphertext* const* a, const Ciphertext* const* b, int K, Ciphertext* out);
 std::vector<double> cheb_fit(double (*f)(double, const void*), const void* arg, double a, double b, int n);
 void mul_integer(Context& cx, const Ciphertext& a, long double M, Ciphertext& out);
@@ -389,10 +390,9 @@ void bootstrap_setup(Context& cx, double B, int deg, int r) {
     const int nl_em = nl;
     const CosArg ca{B, r};
     bc->cheb = cheb_fit(cos_target, &ca, -1.0, 1.0, deg);
-    // EvalMod depth: Chebyshev (ceil(log2(deg+1)) + 1) + r double angles
-    int cd = 0;
-    while ((1 << cd) < deg + 1) cd++;
-    nl = nl_em - (cd + 1) - bc->r;
+    // EvalMod depth: the levels the Chebyshev evaluation of these coefficients takes (its
+    // baby / giant / leaf tree, cheb_depth) + r double angles
+    nl = nl_em - cheb_depth(bc->cheb) - bc->r;
     // SlotToCoeff is built on the first bootstrap, when the (data-independent) scale of the
     // EvalMod output is known; its first level absorbs that scale and q0 / (2 pi Delta_in)
     bc->delta_in = canon(cx, 1);

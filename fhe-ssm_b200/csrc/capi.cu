@@ -459,6 +459,24 @@ int fhe_cheb_eval(fhe_ctx* cx, const fhe_ct* x, const double* coeffs, int ncoef,
         *out = wrap(cx, std::move(r));
     });
 }
+int fhe_cheb_eval_n(fhe_ctx* cx, const fhe_ct* const* xs, int count, const double* coeffs, int ncoef,
+                    fhe_ct** outs) {
+    return guard([&] {
+        REQUIRE(cx && xs && coeffs && outs && ncoef >= 2 && count >= 1 && count <= 64, "bad argument");
+        bind(cx);
+        std::vector<const fhe::Ciphertext*> in(count);
+        for (int k = 0; k < count; k++) {
+            REQUIRE(xs[k], "null ciphertext");
+            REQUIRE(xs[k]->c.nl == xs[0]->c.nl && xs[k]->c.scale == xs[0]->c.scale,
+                    "batched Chebyshev series: the inputs must share level and scale");
+            in[k] = &xs[k]->c;
+        }
+        std::vector<double> c(coeffs, coeffs + ncoef);
+        std::vector<fhe::Ciphertext> r(count);
+        fhe::cheb_eval_n(cx->cx, in.data(), count, c, r.data());
+        for (int k = 0; k < count; k++) outs[k] = wrap(cx, std::move(r[k]));
+    });
+}
 int fhe_bootstrap_setup(fhe_ctx* cx, double bound, int degree) {
     return guard([&] {
         REQUIRE(cx && bound > 0 && degree >= 3, "bad argument");

@@ -490,6 +490,44 @@ struct ChebEvalN {
     }
 };
 
+// Levels consumed by ChebEval / ChebEvalN on a canonical-scale input: the same tree on depths
+// (a product is one level below its deeper operand; babies are aligned to the deepest baby;
+// a leaf is one level below the babies).
+static int cheb_depth_rec(std::vector<double> c, int bs, int lo, const std::map<int, int>& gd) {
+    int deg = (int)c.size() - 1;
+    while (deg > 0 && c[deg] == 0.0) deg--;
+    c.resize(deg + 1);
+    if (deg < bs) return lo + 1;
+    int M = bs;
+    while (2 * M <= deg) M *= 2;
+    std::vector<double> q(deg - M + 1), r(c.begin(), c.begin() + M);
+    q[0] = c[M];
+    for (int i = M + 1; i <= deg; i++) {
+        q[i - M] = 2 * c[i];
+        r[2 * M - i] -= c[i];
+    }
+    const int dq = cheb_depth_rec(q, bs, lo, gd), dr = cheb_depth_rec(r, bs, lo, gd);
+    return std::max(std::max(dq, gd.at(M)) + 1, dr);
+}
+int cheb_depth(const std::vector<double>& coeffs) {
+    const int degree = (int)coeffs.size() - 1;
+    int bs = 1;
+    while (bs * bs < degree + 1) bs <<= 1;
+    if (bs < 2) bs = 2;
+    std::vector<int> d(bs, 0);
+    for (int i = 2; i < bs; i++) d[i] = std::max(d[(i + 1) / 2], d[i / 2]) + 1;
+    int lo = 0;
+    for (int i = 1; i < bs; i++) lo = std::max(lo, d[i]);
+    std::map<int, int> gd;
+    int M = bs;
+    gd[M] = d[bs / 2] + 1;
+    while (2 * M <= degree) {
+        gd[2 * M] = gd[M] + 1;
+        M *= 2;
+    }
+    return cheb_depth_rec(coeffs, bs, lo, gd);
+}
+
 // cheb_eval over K ciphertexts at one level and scale, products batched
 void cheb_eval_n(Context& cx, const Ciphertext* const* x, int K, const std::vector<double>& coeffs, Ciphertext* out) {
     std::vector<Ciphertext> y;

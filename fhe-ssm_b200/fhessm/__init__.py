@@ -83,6 +83,7 @@ _SIGS = {
     "fhe_mul_rescale": (C.c_int, [_VP, _VP, _VP, C.POINTER(_VP)]),
     "fhe_poly_eval": (C.c_int, [_VP, _VP, _DP, C.c_int, C.c_int, C.POINTER(_VP)]),
     "fhe_cheb_eval": (C.c_int, [_VP, _VP, _DP, C.c_int, C.POINTER(_VP)]),
+    "fhe_cheb_eval_n": (C.c_int, [_VP, C.POINTER(_VP), C.c_int, _DP, C.c_int, C.POINTER(_VP)]),
     "fhe_bootstrap_setup": (C.c_int, [_VP, C.c_double, C.c_int]),
     "fhe_bootstrap_setup_r": (C.c_int, [_VP, C.c_double, C.c_int, C.c_int]),
     "fhe_bootstrap": (C.c_int, [_VP, _VP, C.POINTER(_VP)]),
@@ -428,6 +429,14 @@ class CryptoContext:
         h = _VP()
         _check(lib().fhe_cheb_eval(self.h, ct.h, c.ctypes.data_as(_DP), len(c), C.byref(h)))
         return Ciphertext(self, h)
+
+    def EvalChebyshevSeriesBatch(self, cts, coeffs):
+        """EvalChebyshevSeries on ciphertexts of one level and scale with batched products."""
+        c = np.ascontiguousarray(np.asarray(coeffs, dtype=np.float64))
+        ins = (_VP * len(cts))(*[x.h for x in cts])
+        outs = (_VP * len(cts))()
+        _check(lib().fhe_cheb_eval_n(self.h, ins, len(cts), c.ctypes.data_as(_DP), len(c), outs))
+        return [Ciphertext(self, outs[k]) for k in range(len(cts))]
 
     def matvec_plan(self, W, D, b1):
         """Masked block-cyclic BSGS plan of W (rows <= D); column chunk s acts on input s."""

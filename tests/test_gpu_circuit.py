@@ -65,6 +65,22 @@ def test_chebyshev_series(cx):
     assert np.abs(cx.Decrypt(y).real - ref).max() < 1e-6
 
 
+@pytest.mark.parametrize("ncoef", [12, 16, 24, 32])
+def test_chebyshev_series_batched_matches_single(cx, ncoef):
+    """The batched evaluator (two ciphertexts, products batched, as in the bootstrap's EvalMod)
+    gives the single evaluator's words, for leaf-times-giant and product-times-giant trees."""
+    rng = np.random.default_rng(40 + ncoef)
+    c = rng.uniform(-1, 1, ncoef) / np.arange(1, ncoef + 1)
+    xs = [rng.uniform(-1, 1, cx.slots) for _ in range(2)]
+    cts = [cx.Encrypt(cx.MakeCKKSPackedPlaintext(x)) for x in xs]
+    got = cx.EvalChebyshevSeriesBatch(cts, c)
+    for k in range(2):
+        single = cx.EvalChebyshevSeries(cts[k], c)
+        assert (got[k].words() == single.words()).all()
+        ref = np.polynomial.chebyshev.chebval(xs[k], c)
+        assert np.abs(cx.Decrypt(got[k]).real - ref).max() < 1e-6
+
+
 def test_lemma2_scan(cx):
     """s_t = a (.) s_{t-1} + b (.) x_t over 8 steps (cpu_real_model.cpp:580-603)."""
     rng = np.random.default_rng(3)
