@@ -168,7 +168,11 @@ def roofline(prof):
     traffic = None
     tf = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tf):
-        traffic = json.load(open(tf)).get(name)
+        # DRAM bytes per limb-transform from an ncu capture, scaled to this run's average launch by its
+        # limbs per launch (algorithmic bytes per launch / algorithmic bytes per limb)
+        t = json.load(open(tf)).get(name)
+        if isinstance(t, dict) and n:
+            traffic = t["dram_bytes_per_limb"] * (tbytes / n) / t["algorithmic_bytes_per_limb"]
     return {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
             "traffic": traffic, "launches": n, "avg_launch_us": 1000.0 * tms / n,
             "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if "hbm_gbs" in pk else "fallback 6650 GB/s"}
