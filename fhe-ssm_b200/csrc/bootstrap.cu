@@ -351,6 +351,7 @@ static void eval_level(Context& cx, const BootLevel& L, const Ciphertext& v, Cip
     const uint64_t* g0 = flat.empty() ? nullptr : flat[0];
     if (flat.size() > 1) {
         fsum = DevBuf((size_t)2 * nl * N, st);
+        ProfScope pe(cx, "ewise", 8.0 * N * nl * 2 * 3 * (double)(flat.size() - 1));
         const long long ps = (long long)nl * N;
         k_ewise<<<dim3(N / 256, nl, 2), 256, 0, st>>>(EW_ADD, flat[0], ps, flat[1], ps, fsum.p, ps, 0, cx.logN);
         for (size_t f = 2; f < flat.size(); f++)

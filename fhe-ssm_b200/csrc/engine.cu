@@ -513,6 +513,7 @@ static void check_same(const Ciphertext& a, const Ciphertext& b, const char* op)
 static void ewise(Context& cx, int op, const Ciphertext& a, const uint64_t* b, long long sb, int log_rep,
                   Ciphertext& out) {
     ensure_out(cx, out, a.nl);
+    ProfScope ps(cx, "ewise", 8.0 * cx.N * a.nl * 2 * 3);
     k_ewise<<<g2(cx, a.nl, 2), 256, 0, cx.stream>>>(op, a.buf.p, (long long)a.stride, b, sb, out.buf.p,
                                                     (long long)out.stride, log_rep, cx.logN);
     CUDA_CHECK(cudaGetLastError());
@@ -594,7 +595,11 @@ void ct_mul_relin_rescale(Context& cx, const Ciphertext& a, const Ciphertext& b,
     cx.ks_limbs += nl;
     const uint64_t* tab = cx.mdr_table(nl);
     DevBuf z((size_t)2 * J * N, st);
-    k_mdr_gather<<<dim3(N / 256, J, 2), 256, 0, st>>>(d.buf.p, (long long)d.stride, ip.p, tab, z.p, nl, ne, K, cx.logN);
+    {
+        ProfScope ps(cx, "mdr_gather", 8.0 * N * 2 * (1 + 2 * J));
+        k_mdr_gather<<<dim3(N / 256, J, 2), 256, 0, st>>>(d.buf.p, (long long)d.stride, ip.p, tab, z.p, nl, ne, K,
+                                                          cx.logN);
+    }
     LimbMap zm{};
     zm.base = z.p; zm.poly_stride = (long long)J * N; zm.nl = J;
     zm.split = 1; zm.off0 = nl - 1; zm.off1 = L;
@@ -629,9 +634,16 @@ void ct_rescale(Context& cx, Ciphertext& a) {
     lm.base = last.p; lm.poly_stride = N; lm.nl = 1; lm.split = 1; lm.off0 = l; lm.off1 = 0;
     ntt(cx, lm, 2, true, st);
     DevBuf y((size_t)2 * l * N, st);
-    k_rescale_lift<<<g2(cx, l, 2), 256, 0, st>>>(last.p, y.p, l, l, cx.logN);
+    {
+        ProfScope ps(cx, "rescale_lift", 8.0 * N * 2 * (1 + l));
+        k_rescale_lift<<<g2(cx, l, 2), 256, 0, st>>>(last.p, y.p, l, l, cx.logN);
+    }
     ntt(cx, cx.qmap(y.p, l, (long long)l * N), 2, false, st);
-    k_rescale_final<<<g2(cx, l, 2), 256, 0, st>>>(a.buf.p, (long long)a.stride, y.p, cx.d_rs, l, l, cx.L, cx.logN);
+    {
+        ProfScope ps(cx, "rescale_final", 8.0 * N * 2 * l * 3);
+        k_rescale_final<<<g2(cx, l, 2), 256, 0, st>>>(a.buf.p, (long long)a.stride, y.p, cx.d_rs, l, l, cx.L,
+                                                      cx.logN);
+    }
     CUDA_CHECK(cudaGetLastError());
     cx.launches += 2;
     a.scale /= (double)cx.mods[l];
@@ -696,6 +708,7 @@ void limb_residues(const Context& cx, long double v, int nl, uint64_t* out) {
 }
 
 void apply_limb_const(Context& cx, const Ciphertext& a, const LimbConst& k, Ciphertext& out) {
+    ProfScope ps(cx, "mul_const", 8.0 * cx.N * a.nl * 2 * 2);
     if (&out == &a) {
         k_mul_const<<<g2(cx, a.nl, 2), 256, 0, cx.stream>>>(a.buf.p, (long long)a.stride, a.buf.p, (long long)a.stride,
                                                             k, cx.logN);

@@ -317,10 +317,13 @@ void ct_mul_relin_rescale_n(Context& cx, const Ciphertext* const* a, const Ciphe
     // ModDown + rescale in one division by P q_l, all products together
     const uint64_t* tab = cx.mdr_table(nl);
     DevBuf z((size_t)B * 2 * J * N, st);
-    for (int k = 0; k < B; k++)
-        k_mdr_gather<<<dim3(N / 256, J, 2), 256, 0, st>>>(d.p + (size_t)k * 2 * nl * N, (long long)nl * N,
-                                                          ip.p + (size_t)k * 2 * ne * N, tab,
-                                                          z.p + (size_t)k * 2 * J * N, nl, ne, K, cx.logN);
+    {
+        ProfScope ps(cx, "mdr_gather", 8.0 * N * B * 2 * (1 + 2 * J));
+        for (int k = 0; k < B; k++)
+            k_mdr_gather<<<dim3(N / 256, J, 2), 256, 0, st>>>(d.p + (size_t)k * 2 * nl * N, (long long)nl * N,
+                                                              ip.p + (size_t)k * 2 * ne * N, tab,
+                                                              z.p + (size_t)k * 2 * J * N, nl, ne, K, cx.logN);
+    }
     LimbMap zm{};
     zm.base = z.p; zm.poly_stride = (long long)J * N; zm.nl = J;
     zm.split = 1; zm.off0 = nl - 1; zm.off1 = L;
