@@ -122,6 +122,7 @@ struct BootCtx {
     int r = 3, deg = 59;
     std::vector<double> cheb;
     std::vector<BootLevel> cts, stc;
+    int nl_top = 0;   // limbs of the ModRaise output
     int nl_stc = 0, nl_out = 0;
     double delta_in = 0, stc_s_in = 0;
 };
@@ -378,16 +379,22 @@ void bootstrap_setup(Context& cx, double B, int deg, int r) {
     int logn = 0;
     while ((1 << logn) < n) logn++;
     const int per = (logn + 2) / 3;
-    const int Lt = cx.L;
+    // ModRaise lifts to all limbs but the top one: CoeffToSlot takes three levels and carries
+    // the EvalMod argument's 1/(2B) in its last level, so the chain's top prime is not needed
+    const int Lt = cx.L - 1;
+    bc->nl_top = Lt;
     const double q0 = (double)cx.mods[0];
-    // CoeffToSlot at scale q0 throughout (each level's plaintext scale is its own prime)
+    // CoeffToSlot at scale q0 (each level's plaintext scale is its own prime); the last level
+    // also carries the factor 1/(2B) of the EvalMod argument and lands on the canonical scale,
+    // so no level is spent on that constant
     int nl = Lt;
     for (int lv = 0; lv < 3; lv++) {
         const int hi = logn - lv * per, lo = std::max(0, hi - per);
-        bc->cts.push_back(build_level(cx, lo, hi, true, nl, q0, q0, 1.0));
+        const bool last = lv == 2;
+        bc->cts.push_back(build_level(cx, lo, hi, true, nl, q0, last ? canon(cx, nl - 1) : q0,
+                                      last ? 1.0 / (2.0 * B) : 1.0));
         nl--;
     }
-    nl--;   // 1/(2B) as an exact integer product, landing on the canonical scale
     const int nl_em = nl;
     const CosArg ca{B, r};
     bc->cheb = cheb_fit(cos_target, &ca, -1.0, 1.0, deg);
@@ -445,8 +452,9 @@ void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto
         relabel = a.scale / bc->delta_in;
         a.scale = bc->delta_in;
     }
-    // 2. ModRaise: centred lift of the q0 residues to all L limbs
-    Ciphertext raised = ct_alloc(cx, cx.L);
+    // 2. ModRaise: centred lift of the q0 residues to the bootstrap's top limbs
+    const int Lt = bc->nl_top;
+    Ciphertext raised = ct_alloc(cx, Lt);
     {
         DevBuf c((size_t)2 * N, cx.stream);
         CUDA_CHECK(cudaMemcpyAsync(c.p, a.c(0), N * 8, cudaMemcpyDeviceToDevice, cx.stream));
@@ -455,12 +463,12 @@ void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto
         lm.base = c.p; lm.poly_stride = N; lm.nl = 1; lm.split = 1; lm.off0 = 0; lm.off1 = 0;
         ntt(cx, lm, 2, true, cx.stream);
         // k_rescale_lift writes y[c][i] for i < nlm1, layout [2][nlm1][N]: lift into a temp then copy
-        DevBuf y((size_t)2 * cx.L * N, cx.stream);
-        k_rescale_lift<<<dim3(N / 256, cx.L, 2), 256, 0, cx.stream>>>(c.p, y.p, cx.L, 0, cx.logN);
+        DevBuf y((size_t)2 * Lt * N, cx.stream);
+        k_rescale_lift<<<dim3(N / 256, Lt, 2), 256, 0, cx.stream>>>(c.p, y.p, Lt, 0, cx.logN);
         CUDA_CHECK(cudaGetLastError());
         cx.launches++;
-        ntt(cx, cx.qmap(y.p, cx.L, (long long)cx.L * N), 2, false, cx.stream);
-        CUDA_CHECK(cudaMemcpyAsync(raised.buf.p, y.p, (size_t)2 * cx.L * N * 8, cudaMemcpyDeviceToDevice, cx.stream));
+        ntt(cx, cx.qmap(y.p, Lt, (long long)Lt * N), 2, false, cx.stream);
+        CUDA_CHECK(cudaMemcpyAsync(raised.buf.p, y.p, (size_t)2 * Lt * N * 8, cudaMemcpyDeviceToDevice, cx.stream));
     }
     raised.scale = (double)cx.mods[0];
     if (upto == 1) { out = std::move(raised); return; }
@@ -470,11 +478,6 @@ void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto
     for (auto& L : bc->cts) {
         Ciphertext t;
         eval_level(cx, L, v, t);
-        v = std::move(t);
-    }
-    {
-        Ciphertext t;
-        mul_const_rescale(cx, v, 1.0 / (2.0 * bc->B), t, canon(cx, v.nl - 1));
         v = std::move(t);
     }
     delete ps_cts;
