@@ -42,6 +42,7 @@ int cheb_depth(const std::vector<double>& coeffs);
 void mul_rescale_n(Context& cx, const Ciphertext* const* a, const Ciphertext* const* b, int K, Ciphertext* out);
 std::vector<double> cheb_fit(double (*f)(double, const void*), const void* arg, double a, double b, int n);
 void mul_integer(Context& cx, const Ciphertext& a, long double M, Ciphertext& out);
+void mul_integer_add_const(Context& cx, const Ciphertext& a, long double M, double v, Ciphertext& out);
 void mul_rescale(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out);
 __global__ void k_rescale_lift(const uint64_t*, uint64_t*, int, int, int);
 
@@ -496,10 +497,7 @@ void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto
             const Ciphertext* pc[2] = {&c[0], &c[1]};
             Ciphertext sq[2];
             mul_rescale_n(cx, pc, pc, 2, sq);
-            for (int j = 0; j < 2; j++) {
-                mul_integer(cx, sq[j], 2, sq[j]);
-                ct_add_const(cx, sq[j], -1.0, c[j]);
-            }
+            for (int j = 0; j < 2; j++) mul_integer_add_const(cx, sq[j], 2, -1.0, c[j]);
         }
         parts[0] = std::move(c[0]);
         parts[1] = std::move(c[1]);

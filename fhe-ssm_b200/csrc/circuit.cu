@@ -35,6 +35,20 @@ void mul_integer(Context& cx, const Ciphertext& a, long double M, Ciphertext& ou
     out.scale = sc;
 }
 
+// out = a * M + v (v at a's scale) in one pass over the limbs: the same words as mul_integer
+// followed by ct_add_const (the Chebyshev doubling 2 T^2 - 1 and the double angles)
+void mul_integer_add_const(Context& cx, const Ciphertext& a, long double M, double v, Ciphertext& out) {
+    LimbConst k{};
+    k.has_w = 1;
+    limb_residues(cx, M, a.nl, k.w);
+    for (int i = 0; i < a.nl; i++) k.wp[i] = shoup_of(k.w[i], cx.mods[i]);
+    k.has_add = 1;
+    limb_residues(cx, (long double)v * (long double)a.scale, a.nl, k.add);
+    const double sc = a.scale;
+    apply_limb_const(cx, a, k, out);
+    out.scale = sc;
+}
+
 // value * c, rescaled once; the integer factor round(c * S) is chosen so that the output
 // scale is `target` (default: the canonical factor of the output level).
 void mul_const_rescale(Context& cx, const Ciphertext& a, double c, Ciphertext& out, double target) {
@@ -248,12 +262,12 @@ struct ChebEval {
             const int a = (i + 1) / 2, b = i / 2;
             Ciphertext p;
             mul_rescale(cx, T[a], T[b], p);
-            mul_integer(cx, p, 2, p);
             if (a == b) {
                 Ciphertext one;
-                ct_add_const(cx, p, -1.0, one);
+                mul_integer_add_const(cx, p, 2, -1.0, one);
                 T[i] = std::move(one);
             } else {
+                mul_integer(cx, p, 2, p);
                 Ciphertext d;
                 sub_any(cx, p, T[a - b], d);
                 T[i] = std::move(d);
@@ -266,16 +280,14 @@ struct ChebEval {
             const int a = bs / 2;
             Ciphertext p;
             mul_rescale(cx, T[a], T[a], p);
-            mul_integer(cx, p, 2, p);
-            ct_add_const(cx, p, -1.0, g);
+            mul_integer_add_const(cx, p, 2, -1.0, g);
         }
         giant[M] = ct_copy(cx, g);
         while (2 * M <= degree) {
             Ciphertext p;
             mul_rescale(cx, giant[M], giant[M], p);
-            mul_integer(cx, p, 2, p);
             Ciphertext n2;
-            ct_add_const(cx, p, -1.0, n2);
+            mul_integer_add_const(cx, p, 2, -1.0, n2);
             M *= 2;
             giant[M] = std::move(n2);
         }
@@ -399,9 +411,12 @@ struct ChebEvalN {
         prod(a, b, p);
         std::vector<Ciphertext> r(K);
         for (int k = 0; k < K; k++) {
-            mul_integer(cx, p[k], 2, p[k]);
-            if (c) sub_any(cx, p[k], (*c)[k], r[k]);
-            else ct_add_const(cx, p[k], -1.0, r[k]);
+            if (c) {
+                mul_integer(cx, p[k], 2, p[k]);
+                sub_any(cx, p[k], (*c)[k], r[k]);
+            } else {
+                mul_integer_add_const(cx, p[k], 2, -1.0, r[k]);
+            }
         }
         return r;
     }

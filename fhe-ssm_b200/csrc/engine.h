@@ -262,6 +262,7 @@ Plaintext decrypt(Context& cx, const Ciphertext& ct);
 // circuit layer (circuit.cu)
 double canon(const Context& cx, int nl);
 void mul_integer(Context& cx, const Ciphertext& a, long double M, Ciphertext& out);
+void mul_integer_add_const(Context& cx, const Ciphertext& a, long double M, double v, Ciphertext& out);
 void mul_const_rescale(Context& cx, const Ciphertext& a, double c, Ciphertext& out, double target = 0);
 void align(Context& cx, Ciphertext& a, int nl_t, double target = 0);
 void match(Context& cx, Ciphertext& a, Ciphertext& b);

@@ -727,7 +727,8 @@ void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets,
                     if (sm > 48 * 1024)
                         CUDA_CHECK(cudaFuncSetAttribute(k_tc_split_babies, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
                     ProfScope ps(cx, "tc_split", 2.0 * bytes);
-                    k_tc_split_babies<<<dim3(R, ne), 256, sm, st>>>(b.pq.p, (uint8_t*)b.split.p, 2 * b1, Kp, ne, cx.logN);
+                    k_tc_split_babies<<<dim3(R, ne), 256, sm, st>>>(b.pq.p, (uint8_t*)b.split.p, 2 * b1, Kp, ne, nl,
+                                                                    cx.L, cx.logN);
                     CUDA_CHECK(cudaGetLastError());
                     cx.launches++;
                 }
@@ -742,7 +743,7 @@ void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets,
                 for (int s = 0; s < S; s++) {
                     k_tc_pack_w<<<dim3(2 * D, ne), 256, wblk, st>>>(ptsrc, (const int*)pl.d_ids.p,
                                                                   (uint8_t*)wpack.p + (size_t)s * ne * 2 * D * wblk, s, G,
-                                                                  b1, Kp, M, 2 * D, std::max(pl.P, 1));
+                                                                  b1, Kp, M, 2 * D, std::max(pl.P, 1), nl, cx.L);
                     cx.launches++;
                 }
                 CUDA_CHECK(cudaGetLastError());

@@ -74,10 +74,13 @@ __host__ __device__ inline size_t tc_smem_bytes(int Mp, int Kp) {
 // rows (n = c * 32 + slot) x Kp bytes (k), K-major core-matrix order.  One CTA per (r, e); the
 // block is assembled in shared memory and written with 16-byte stores.
 __global__ void __launch_bounds__(256) k_tc_split_babies(const uint64_t* __restrict__ bb, uint8_t* __restrict__ out,
-                                                         int K, int Kp, int ne, int logN) {
+                                                         int K, int Kp, int ne, int nl, int L, int logN) {
     extern __shared__ __align__(16) uint8_t ss[];   // [8][64 Kp]
     const int N = 1 << logN;
     const int r = blockIdx.x, e = blockIdx.y, x0 = r * 32;
+    // words of this limb are < q: only byte slices 0..nbyte-1 are written (the product kernel
+    // reads no others)
+    const int nbyte = (int)((c_mod[e < nl ? e : L + (e - nl)].k + 7) / 8);
     const uint32_t SB = 8u * Kp;
     for (int t = threadIdx.x; t < 64 * (Kp / 4); t += blockDim.x) {
         const int n = t & 63, k4 = t >> 6, c = n >> 5, xs = n & 31;
@@ -94,12 +97,13 @@ __global__ void __launch_bounds__(256) k_tc_split_babies(const uint64_t* __restr
         const int k = 4 * k4;
         const size_t off = (size_t)(n >> 3) * SB + (size_t)(k >> 4) * 128 + (size_t)(n & 7) * 16 + (k & 15);
 #pragma unroll
-        for (int b = 0; b < 8; b++) *reinterpret_cast<uint32_t*>(ss + (size_t)b * 64 * Kp + off) = w[b];
+        for (int b = 0; b < 8; b++)
+            if (b < nbyte) *reinterpret_cast<uint32_t*>(ss + (size_t)b * 64 * Kp + off) = w[b];
     }
     __syncthreads();
     uint4* dst = reinterpret_cast<uint4*>(out + ((size_t)e * (N / 32) + r) * 8 * 64 * Kp);
     const uint4* src = reinterpret_cast<const uint4*>(ss);
-    for (int i = threadIdx.x; i < 8 * 64 * Kp / 16; i += blockDim.x) dst[i] = src[i];
+    for (int i = threadIdx.x; i < nbyte * 64 * Kp / 16; i += blockDim.x) dst[i] = src[i];
 }
 
 // Plaintext words of set s of a plan -> per (limb e, compressed word w) a block of byte slices
@@ -107,9 +111,10 @@ __global__ void __launch_bounds__(256) k_tc_split_babies(const uint64_t* __restr
 // fam(o, k), giant g(o), baby j(k), or 0.
 __global__ void __launch_bounds__(256) k_tc_pack_w(const uint64_t* __restrict__ pts, const int* __restrict__ ids,
                                                    uint8_t* __restrict__ out, int s, int G, int b1, int Kp, int Mp,
-                                                   int D2, int P) {
+                                                   int D2, int P, int nl, int L) {
     extern __shared__ __align__(16) uint8_t sw[];   // [8][Mp Kp]
     const int wi = blockIdx.x, e = blockIdx.y;
+    const int nbyte = (int)((c_mod[e < nl ? e : L + (e - nl)].k + 7) / 8);   // slices the product reads
     const int M = 2 * G, K = 2 * b1;
     const uint32_t SB = 8u * Kp;
     const uint64_t* row = pts + ((size_t)e * D2 + wi) * P;
@@ -134,13 +139,14 @@ __global__ void __launch_bounds__(256) k_tc_pack_w(const uint64_t* __restrict__ 
         const int k = 4 * k4;
         const size_t off = (size_t)(o >> 3) * SB + (size_t)(k >> 4) * 128 + (size_t)(o & 7) * 16 + (k & 15);
 #pragma unroll
-        for (int b = 0; b < 8; b++) *reinterpret_cast<uint32_t*>(sw + (size_t)b * Mp * Kp + off) = w[b];
+        for (int b = 0; b < 8; b++)
+            if (b < nbyte) *reinterpret_cast<uint32_t*>(sw + (size_t)b * Mp * Kp + off) = w[b];
     }
     __syncthreads();
     const size_t blk = (size_t)8 * Mp * Kp;
     uint4* dst = reinterpret_cast<uint4*>(out + ((size_t)e * D2 + wi) * blk);
     const uint4* src = reinterpret_cast<const uint4*>(sw);
-    for (int i = threadIdx.x; i < (int)(blk / 16); i += blockDim.x) dst[i] = src[i];
+    for (int i = threadIdx.x; i < (int)((size_t)nbyte * Mp * Kp / 16); i += blockDim.x) dst[i] = src[i];
 }
 
 struct Tc2Args {
@@ -176,16 +182,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_bsgs_tc2(const Tc2Args a, uin
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int M = 2 * a.G, ptw = x0 >> a.lr;
     const uint32_t SB = 8u * Kp;
-    const uint32_t bbytes = 8u * 64u * Kp, wbytes = 8u * Mp * Kp;
     // words of this limb are < q: their bytes nbyte.. are zero, and so are the diagonals
     // d > 2 (nbyte - 1): only those MMAs and tensor-memory columns are used (45-bit limbs:
-    // 6 bytes, 6 diagonal pairs, 84 of 144 MMAs)
+    // 6 bytes, 6 diagonal pairs, 84 of 144 MMAs), and only byte slices 0..nbyte-1 are copied
     const int nbyte = (int)((mc.k + 7) / 8);
     const int npairs = nbyte;   // pairs p with 2p <= 2 (nbyte - 1)
+    const uint32_t bbytes = (uint32_t)nbyte * 64u * Kp, wbytes = (uint32_t)nbyte * Mp * Kp;
 
+    // zero M-side slots: slot 0 (slice -1) and slots nbyte+1..9 (slices nbyte..8, read by the
+    // stacked second diagonal of the top pairs and never copied)
     for (int i = tid; i < 64 * Kp / 16; i += kTcThreads) {
         reinterpret_cast<uint4*>(Ms)[i] = make_uint4(0, 0, 0, 0);
-        reinterpret_cast<uint4*>(Ms + (size_t)9 * 64 * Kp)[i] = make_uint4(0, 0, 0, 0);
+        for (int sl = nbyte + 1; sl <= 9; sl++)
+            reinterpret_cast<uint4*>(Ms + (size_t)sl * 64 * Kp)[i] = make_uint4(0, 0, 0, 0);
     }
     uint64_t run[Mp];
 #pragma unroll
@@ -214,8 +223,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_bsgs_tc2(const Tc2Args a, uin
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(bar)),
                          "r"(bbytes + wbytes)
                          : "memory");
-            tc_bulk_g2s(Ms + (size_t)64 * Kp, a.bsplit[s] + ((size_t)e * (N / 32) + r) * bbytes, bbytes, bar);
-            tc_bulk_g2s(Ns, a.wpack + (((size_t)s * a.ne + e) * a.D2 + ptw) * wbytes, wbytes, bar);
+            tc_bulk_g2s(Ms + (size_t)64 * Kp, a.bsplit[s] + ((size_t)e * (N / 32) + r) * 8 * 64 * Kp, bbytes, bar);
+            tc_bulk_g2s(Ns, a.wpack + (((size_t)s * a.ne + e) * a.D2 + ptw) * 8 * Mp * Kp, wbytes, bar);
         }
         ok = __syncthreads_and(tc_wait(bar, (uint32_t)(s & 1)) ? 1 : 0) != 0;
         if (!ok) {
