@@ -265,15 +265,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_bsgs_tc2(const Tc2Args a, uin
             unsigned __int128 acc[8];
 #pragma unroll
             for (int j = 0; j < 8; j++) acc[j] = 0;
+            // the accumulators of PB diagonal pairs are loaded together before one wait (one
+            // tensor-memory round trip per group instead of one per pair)
+            constexpr int PB = MP >= 64 ? 4 : 8;
 #pragma unroll
-            for (int p = 0; p < 8; p++) {
-                if (p >= npairs) break;   // uniform: all diagonals beyond are zero
-                uint32_t v[8];
-                tc_ld8(taddr + ((uint32_t)(32 * warp) << 16) + (uint32_t)(p * Mp + oc * 8), v);
+            for (int p0 = 0; p0 < 8; p0 += PB) {
+                if (p0 >= npairs) break;   // uniform: all diagonals beyond are zero
+                uint32_t v[PB][8];
+#pragma unroll
+                for (int p = 0; p < PB; p++)   // columns of all 8 pairs are allocated (tcols = 8 Mp)
+                    tc_ld8(taddr + ((uint32_t)(32 * warp) << 16) + (uint32_t)((p0 + p) * Mp + oc * 8), v[p]);
                 asm volatile("tcgen05.wait::ld.sync.aligned;");
-                const int sh = 8 * (2 * p + h);
 #pragma unroll
-                for (int j = 0; j < 8; j++) acc[j] += (unsigned __int128)v[j] << sh;
+                for (int p = 0; p < PB; p++) {
+                    if (p0 + p >= npairs) break;
+                    const int sh = 8 * (2 * (p0 + p) + h);
+#pragma unroll
+                    for (int j = 0; j < 8; j++) acc[j] += (unsigned __int128)v[p][j] << sh;
+                }
             }
             __syncthreads();
             if (h == 1) {
