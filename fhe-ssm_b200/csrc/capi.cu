@@ -459,6 +459,12 @@ int fhe_cheb_eval(fhe_ctx* cx, const fhe_ct* x, const double* coeffs, int ncoef,
         *out = wrap(cx, std::move(r));
     });
 }
+int fhe_cheb_depth(const double* coeffs, int ncoef, int* depth) {
+    return guard([&] {
+        REQUIRE(coeffs && depth && ncoef >= 2, "bad argument");
+        *depth = fhe::cheb_depth(std::vector<double>(coeffs, coeffs + ncoef));
+    });
+}
 int fhe_cheb_eval_n(fhe_ctx* cx, const fhe_ct* const* xs, int count, const double* coeffs, int ncoef,
                     fhe_ct** outs) {
     return guard([&] {

@@ -84,6 +84,7 @@ _SIGS = {
     "fhe_poly_eval": (C.c_int, [_VP, _VP, _DP, C.c_int, C.c_int, C.POINTER(_VP)]),
     "fhe_cheb_eval": (C.c_int, [_VP, _VP, _DP, C.c_int, C.POINTER(_VP)]),
     "fhe_cheb_eval_n": (C.c_int, [_VP, C.POINTER(_VP), C.c_int, _DP, C.c_int, C.POINTER(_VP)]),
+    "fhe_cheb_depth": (C.c_int, [_DP, C.c_int, C.POINTER(C.c_int)]),
     "fhe_bootstrap_setup": (C.c_int, [_VP, C.c_double, C.c_int]),
     "fhe_bootstrap_setup_r": (C.c_int, [_VP, C.c_double, C.c_int, C.c_int]),
     "fhe_bootstrap": (C.c_int, [_VP, _VP, C.POINTER(_VP)]),
@@ -508,6 +509,14 @@ def _register_diagnostics():
     h = lib()
     h.fhe_bootstrap_stage.restype = C.c_int
     h.fhe_bootstrap_stage.argtypes = [_VP, _VP, C.c_int, C.POINTER(_VP)]
+
+
+def cheb_depth(coeffs):
+    """Levels EvalChebyshevSeries consumes for these coefficients (host computation, no GPU)."""
+    c = np.ascontiguousarray(np.asarray(coeffs, dtype=np.float64))
+    d = C.c_int()
+    _check(lib().fhe_cheb_depth(c.ctypes.data_as(_DP), len(c), C.byref(d)))
+    return d.value
 
 
 def bootstrap_stage(ctx, ct, upto):

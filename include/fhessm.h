@@ -172,6 +172,9 @@ int fhe_poly_eval(fhe_ctx* cx, const fhe_ct* x, const double* coeffs, int deg, i
 /* sum_i c_i T_i(x) (Chebyshev basis, |x| <= 1), baby-step / giant-step, depth
  * ceil(log2(ncoef)) + 1 */
 int fhe_cheb_eval(fhe_ctx* cx, const fhe_ct* x, const double* coeffs, int ncoef, fhe_ct** out);
+/* levels fhe_cheb_eval consumes on a canonical-scale input for these coefficients (host only:
+ * the bootstrap plans SlotToCoeff's level with it) */
+int fhe_cheb_depth(const double* coeffs, int ncoef, int* depth);
 /* the same series on `count` ciphertexts of one level and scale, every ciphertext product of
  * the evaluations batched (the bootstrap's EvalMod runs its real and imaginary parts this way) */
 int fhe_cheb_eval_n(fhe_ctx* cx, const fhe_ct* const* xs, int count, const double* coeffs, int ncoef,

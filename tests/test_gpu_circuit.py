@@ -81,6 +81,17 @@ def test_chebyshev_series_batched_matches_single(cx, ncoef):
         assert np.abs(cx.Decrypt(got[k]).real - ref).max() < 1e-6
 
 
+@pytest.mark.parametrize("ncoef", [8, 16, 24, 32])
+def test_chebyshev_series_consumes_the_planned_depth(cx, ncoef):
+    """The evaluator uses exactly the levels fhe_cheb_depth plans (the bootstrap relies on it)."""
+    import fhessm
+    rng = np.random.default_rng(60 + ncoef)
+    c = rng.uniform(0.5, 1.0, ncoef)
+    ct = cx.Encrypt(cx.MakeCKKSPackedPlaintext(rng.uniform(-1, 1, cx.slots)))
+    y = cx.EvalChebyshevSeries(ct, c)
+    assert y.level - ct.level == fhessm.cheb_depth(c)
+
+
 def test_lemma2_scan(cx):
     """s_t = a (.) s_{t-1} + b (.) x_t over 8 steps (cpu_real_model.cpp:580-603)."""
     rng = np.random.default_rng(3)
