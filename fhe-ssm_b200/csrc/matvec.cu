@@ -9,10 +9,14 @@
 //   rho_k(u) = M_k . rot(u, k) + (1 - M_k) . rot(u, k - D),   M_k[c] = [c + k < D].
 // With k = g b1 + j the baby masks (M_j) and the giant masks (pushed through the giant
 // rotation) are folded into three families of D-periodic plaintexts (AA, AB, BA; BB is
-// empty), so the matvec is
-//   y = sum_g rot(IA_g, g b1) + rot(IB_g, g b1 - D),
-//   IA_g = sum_j AA_gj . rot(u, j) + AB_gj . rot(u, j - D),  IB_g = sum_j BA_gj . rot(u, j)
-// i.e. 2 b1 - 1 hoisted baby rotations and 2 (D/b1 - 1) giant rotations.
+// empty): y = sum_g rot(IA_g, g b1) + rot(IB_g, g b1 - D) with
+//   IA_g = sum_j AA_gj . rot(u, j) + AB_gj . rot(u, j - D),  IB_g = sum_j BA_gj . rot(u, j).
+// A D-periodic plaintext is invariant under rot(., -D), so rot(BA . rot(u, j), g b1 - D) =
+// rot(BA . rot(u, j - D), g b1): the BA family joins AB on the baby rot(u, j - D) under the
+// same giant, and
+//   y = sum_g rot(I_g, g b1),  I_g = sum_j AA_gj . rot(u, j) + (AB_gj + BA_gj) . rot(u, j - D),
+// i.e. 2 b1 - 1 hoisted baby rotations and D/b1 - 1 giant rotations (the masks of AB and BA
+// are disjoint, so the merged family is one plaintext per (g, j)).
 //
 // Plaintexts.  Every family vector is D-periodic, so its ring-N encoding is the ring-2D
 // encoding of one period embedded at stride N/(2D) (hpc_gpu_port/periodic_encode.hpp:1-40
@@ -257,10 +261,11 @@ constexpr int kKc = 64;          // babies per shared-memory chunk (<= 128 produ
 
 struct GemmArgs {
     const uint64_t* babies[kMaxSets];   // per set: [2 b1][2][ne][N], QP basis (Y = 0: rot(u, j), Y = 1: rot(u, j - D))
-    const int* ids;                     // [set][3][G][b1] plaintext id or -1 (families AA, AB, BA)
+    const int* ids;                     // [set][3][G][b1] plaintext id or -1 (families AA, AB+BA; the
+                                        // third, BA alone, is empty in merged plans)
     const uint64_t* pts;                // [ne][2D][P] Montgomery words
-    uint64_t* out;                      // [2G][2][ne][N] (IA_0..IA_{G-1}, IB_0..IB_{G-1}), QP basis
-    int nsets, b1, G, nl, ne, L, logN, lr, D2, P, TW;
+    uint64_t* out;                      // [M][2][ne][N] (I_0..I_{G-1}, then zero outputs up to M), QP
+    int nsets, b1, G, M, nl, ne, L, logN, lr, D2, P, TW;
 };
 
 // One CTA: limb e of TW consecutive slots that share one compressed plaintext word (TW <= REP),
@@ -284,7 +289,7 @@ __device__ __forceinline__ void fold128(u128acc& t, uint64_t s00, uint64_t smid,
 
 __global__ void __launch_bounds__(512) k_bsgs_gemm(const GemmArgs a) {
     extern __shared__ uint32_t sm32[];
-    const int M = 2 * a.G, TW = a.TW, NC = 2 * TW;
+    const int M = a.M, TW = a.TW, NC = 2 * TW;
     uint32_t* Bs = sm32;                        // [kKc][NC][2]  (lo30, hi30)
     uint32_t* Ws = sm32 + (size_t)kKc * NC * 2; // [kKc][M][2]
     const int N = 1 << a.logN;
@@ -326,8 +331,8 @@ __global__ void __launch_bounds__(512) k_bsgs_gemm(const GemmArgs a) {
                 Ws[2 * t + 1] = (uint32_t)(v >> 30);
             }
             __syncthreads();
-            // outputs IB (o >= G) have no products with the babies rot(u, j - D) (k >= b1):
-            // those warps stop early (the split is warp-uniform)
+            // outputs o >= G (the zero second output when G = 1) have no products with the
+            // babies rot(u, j - D) (k >= b1): those warps stop early (the split is warp-uniform)
             const int kend = o0 >= a.G ? max(0, min(kc, a.b1 - k0)) : kc;
             u128acc tot[2][4];
 #pragma unroll
@@ -485,10 +490,7 @@ std::shared_ptr<MatvecPlan> matvec_plan(Context& cx, const double* W, int rows, 
     for (int s = 0; s < S; s++)
         for (int g = 0; g < G; g++)
             for (int j = 0; j < b1; j++)
-                for (int fam = 0; fam < 3; fam++) {
-                    if (fam == 2 && g == 0) continue;   // giant-B mask [p < 0] is empty
-                    jobs.push_back({s, fam, g, j});
-                }
+                for (int fam = 0; fam < 2; fam++) jobs.push_back({s, fam, g, j});   // AA, AB + BA
     std::vector<std::vector<double>> co(jobs.size());
     std::vector<char> nz(jobs.size(), 0);
 #pragma omp parallel for schedule(dynamic, 16)
@@ -500,7 +502,8 @@ std::shared_ptr<MatvecPlan> matvec_plan(Context& cx, const double* W, int rows, 
         for (int p = 0; p < D; p++) {
             const bool ga = p >= J.g * b1;                 // giant A keeps inner slots p >= g b1
             const bool mj = p + J.j < D;                   // baby A (rot(u, j)) is valid where p + j < D
-            const bool use = J.fam == 0 ? (ga && mj) : J.fam == 1 ? (ga && !mj) : (!ga && mj);
+            // family 0: AA (ga, mj); family 1: AB (ga, !mj) + BA (!ga, mj) on the baby rot(u, j - D)
+            const bool use = J.fam == 0 ? (ga && mj) : (ga != mj);
             double w = 0.0;
             if (use) {
                 const int c = ((p - J.g * b1) % D + D) % D;     // output channel of this inner slot
@@ -542,7 +545,7 @@ std::vector<int> matvec_rotations(int D, int b1) {
     std::vector<int> r;
     for (int j = 1; j < b1; j++) r.push_back(j);
     for (int j = 0; j < b1; j++) r.push_back(j - D);
-    for (int g = 1; g < D / b1; g++) { r.push_back(g * b1); r.push_back(g * b1 - D); }
+    for (int g = 1; g < D / b1; g++) r.push_back(g * b1);
     return r;
 }
 
@@ -655,7 +658,7 @@ void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets,
     while ((N >> lr) > 2 * D) lr++;
     const int TW = std::min(32, 1 << lr);
     if (TW < 8) throw Error("matvec: D too large for the ring (need N / 2D >= 8)", -1);
-    const int M = 2 * G;
+    const int M = std::max(2, G);   // outputs I_g (a second, zero output when G = 1: the kernels pair outputs)
     if ((TW / 2) * (M / 2) > 512 || M % 2) throw Error("matvec: too many giant steps for one CTA", -1);
     const bool hit = pl.cached.p && pl.cached_nl == nl && pl.cached_spt == spt;
     DevBuf pts(hit ? 0 : (size_t)std::max(pl.P, 1) * ne * 2 * D, st);
@@ -705,7 +708,7 @@ void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets,
         a.ids = (const int*)pl.d_ids.p;
         a.pts = ptsrc;
         a.out = inner.p;
-        a.nsets = S; a.b1 = b1; a.G = G; a.nl = nl; a.ne = ne; a.L = cx.L; a.logN = cx.logN; a.lr = lr;
+        a.nsets = S; a.b1 = b1; a.G = G; a.M = M; a.nl = nl; a.ne = ne; a.L = cx.L; a.logN = cx.logN; a.lr = lr;
         a.D2 = 2 * D; a.P = std::max(pl.P, 1); a.TW = TW;
         const double bytes = 8.0 * N * ne * (2.0 * S * 2 * b1 + 2.0 * M) + 8.0 * pl.P * ne * 2 * D;
         if (cx.use_tc && TW == 32 && (M == 16 || M == 32 || M == 64)) {
@@ -750,7 +753,8 @@ void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets,
             }
             t.wpack = (const uint8_t*)wpack.p;
             t.out = inner.p;
-            t.nsets = S; t.G = G; t.nl = nl; t.ne = ne; t.L = cx.L; t.logN = cx.logN; t.lr = lr; t.D2 = 2 * D;
+            t.nsets = S; t.G = G; t.M = M; t.nl = nl; t.ne = ne; t.L = cx.L; t.logN = cx.logN; t.lr = lr;
+            t.D2 = 2 * D;
             t.Kp = Kp;
             size_t smem = tc_smem_bytes(M, Kp);
             if (tcols == 512) smem = std::max<size_t>(smem, 120 * 1024);
@@ -772,20 +776,18 @@ void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets,
         CUDA_CHECK(cudaGetLastError());
         cx.launches++;
     }
-    // back to Q: one ModDown per giant input, then sum_g rot(IA_g, g b1) + rot(IB_g, g b1 - D)
-    // (IA_0 unrotated; IB_0 is empty: rot(u, j) with j < b1 never needs the -D giant)
-    DevBuf innq((size_t)M * 2 * nl * N, st);
-    moddown_many(cx, inner.p, M, nl, innq.p);
+    // back to Q: one ModDown per giant input, then sum_g rot(I_g, g b1) (I_0 unrotated)
+    DevBuf innq((size_t)G * 2 * nl * N, st);
+    moddown_many(cx, inner.p, G, nl, innq.p);
     const double sc = sets[0]->scale * spt;
     std::vector<const uint64_t*> c0s, c1s;
     std::vector<int> steps;
-    for (int g = 1; g < G; g++)
-        for (int X = 0; X < 2; X++) {
-            const uint64_t* p = innq.p + (size_t)(X * G + g) * 2 * nl * N;
-            c0s.push_back(p);
-            c1s.push_back(p + (size_t)nl * N);
-            steps.push_back(X == 0 ? g * b1 : g * b1 - D);
-        }
+    for (int g = 1; g < G; g++) {
+        const uint64_t* p = innq.p + (size_t)g * 2 * nl * N;
+        c0s.push_back(p);
+        c1s.push_back(p + (size_t)nl * N);
+        steps.push_back(g * b1);
+    }
     Ciphertext acc;
     rotate_sum(cx, c0s.data(), c1s.data(), steps.data(), (int)steps.size(), nl, sc, innq.p,
                innq.p + (size_t)nl * N, acc);

@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(256) k_tc_pack_w(const uint64_t* __restrict__ 
     extern __shared__ __align__(16) uint8_t sw[];   // [8][Mp Kp]
     const int wi = blockIdx.x, e = blockIdx.y;
     const int nbyte = (int)((c_mod[e < nl ? e : L + (e - nl)].k + 7) / 8);   // slices the product reads
-    const int M = 2 * G, K = 2 * b1;
+    const int M = Mp, K = 2 * b1;   // outputs o: giant g = o % G of family X = o / G (X = 1: none)
     const uint32_t SB = 8u * Kp;
     const uint64_t* row = pts + ((size_t)e * D2 + wi) * P;
     for (int t = threadIdx.x; t < Mp * (Kp / 4); t += blockDim.x) {
@@ -152,8 +152,8 @@ __global__ void __launch_bounds__(256) k_tc_pack_w(const uint64_t* __restrict__ 
 struct Tc2Args {
     const uint8_t* bsplit[kMaxSets];   // per set: [ne][N/32][8][64 Kp]
     const uint8_t* wpack;              // [set][ne][2D][8][Mp Kp]
-    uint64_t* out;                     // [2G][2][ne][N]
-    int nsets, G, nl, ne, L, logN, lr, D2, Kp;
+    uint64_t* out;                     // [M][2][ne][N]
+    int nsets, G, M, nl, ne, L, logN, lr, D2, Kp;
 };
 
 __device__ __forceinline__ void tc_bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_bsgs_tc2(const Tc2Args a, uin
     const int m = e < a.nl ? e : a.L + (e - a.nl);
     const ModConst mc = c_mod[m];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int M = 2 * a.G, ptw = x0 >> a.lr;
+    const int M = a.M, ptw = x0 >> a.lr;
     const uint32_t SB = 8u * Kp;
     // words of this limb are < q: their bytes nbyte.. are zero, and so are the diagonals
     // d > 2 (nbyte - 1): only those MMAs and tensor-memory columns are used (45-bit limbs:
