@@ -406,6 +406,36 @@ def run_hmult(args, ws, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def run_ntt(args, ws, rank, local):
+    """Auxiliary kernel benchmark (not a bench line of the headline metric): batched forward and
+    inverse NTTs over `--limbs` limb-polynomials of the 405M chain at N = 2^16 through the C-ABI
+    (fhe_ntt_host: one batched transform per direction), timed by the per-kernel CUDA-event timer
+    (device time of the transforms only, the host copies around them excluded)."""
+    import fhessm
+    cx = fhessm.CryptoContext(device=local, **MODEL_CTX)
+    rng = np.random.default_rng(rank)
+    n = args.limbs
+    w = rng.integers(0, 1 << 44, (n, cx.N), dtype=np.uint64)   # below every modulus of the chain
+    mi = [i % (cx.L + cx.K) for i in range(n)]
+    for _ in range(args.warmup):
+        cx.ntt(cx.ntt(w, mi), mi, inverse=True)
+    cx.profile(True)
+    for _ in range(args.steps):
+        f = cx.ntt(w, mi)
+        b = cx.ntt(f, mi, inverse=True)
+    prof = cx.profile_collect()
+    cx.profile(False)
+    if not (b == w).all():
+        raise RuntimeError("ntt workload: inverse(forward(x)) != x")
+    if rank == 0:
+        us = {k: 1000.0 * prof[name][1] / (prof[name][0] * n) for k, name in (("fwd", "ntt_fwd"), ("inv", "ntt_inv"))}
+        print(json.dumps({"metric": "NTT limb-transforms/s (N=2^16, forward)", "value": 1e6 / us["fwd"],
+                          "unit": "limbs/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+                          "higher_is_better": True, "dtype": "u64", "data": "synthetic",
+                          "config": {"workload": f"{n} limb-polynomials, moduli of the 405M chain"},
+                          "us_per_limb": us, "kernels": kernel_table(prof)}), flush=True)
+
+
 def run_matvec(args, ws, rank, local):
     """One 1024 x 1024 block of the 405M model's linears (double-hoisted BSGS, b1 = 64): babies,
     tensor-core products, giants.  A step is one matvec on an input already on the device."""
@@ -499,9 +529,10 @@ def main():
     ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
-    ap.add_argument("--workload", default="405m", choices=["405m", "hmult", "matvec"])
+    ap.add_argument("--workload", default="405m", choices=["405m", "hmult", "matvec", "ntt"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=64, help="hmult: ciphertext pairs per GPU per step")
+    ap.add_argument("--limbs", type=int, default=1024, help="ntt: limb-polynomials per transform")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -512,6 +543,8 @@ def main():
         run_model(args, ws, rank, local)
     elif args.workload == "matvec":
         run_matvec(args, ws, rank, local)
+    elif args.workload == "ntt":
+        run_ntt(args, ws, rank, local)
     else:
         run_hmult(args, ws, rank, local)
     if ws > 1:
