@@ -105,6 +105,16 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def host_threads():
+    """torchrun sets OMP_NUM_THREADS=1 for every rank, which leaves the engine's host-side set-up
+    (key, plan and table construction, OpenMP loops) on one core per rank.  Give each rank its
+    share of the host's cores instead; must run before torch or the engine library is loaded.
+    Set-up only: nothing in the timed region runs on these threads."""
+    lws = int(os.environ.get("LOCAL_WORLD_SIZE", "1"))
+    if lws > 1 and os.environ.get("OMP_NUM_THREADS") == "1":
+        os.environ["OMP_NUM_THREADS"] = str(max(1, (os.cpu_count() or 1) // lws))
+
+
 def dist_setup():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -536,6 +546,7 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    host_threads()
     ws, rank, local = dist_setup()
     import torch
     torch.cuda.set_device(local)
