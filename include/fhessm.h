@@ -200,7 +200,8 @@ int fhe_bootstrap_stage(fhe_ctx* cx, const fhe_ct* a, int upto, fhe_ct** out);
 typedef struct fhe_mvplan fhe_mvplan;
 int fhe_matvec_plan(fhe_ctx* cx, const double* W, int rows, int cols, int D, int b1, fhe_mvplan** out);
 void fhe_mvplan_free(fhe_mvplan* pl);
-/* rotation keys the matvec needs: j, j - D (babies), g b1, g b1 - D (giants) */
+/* rotation keys the matvec needs: j, j - D (babies), g b1 (giants; one giant family: the
+ * plan's D-periodic diagonals let every family share the g b1 rotation) */
 int fhe_matvec_keygen(fhe_ctx* cx, int D, int b1);
 /* out = W [in_0 | in_1 | ...], one level consumed, canonical scale */
 int fhe_matvec_bsgs(fhe_ctx* cx, const fhe_mvplan* pl, const fhe_ct* const* in, int nin, fhe_ct** out);
