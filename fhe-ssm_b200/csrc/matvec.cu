@@ -31,10 +31,10 @@
 //    P rot(u, r) (no ModDown): k_baby_pq computes the key inner product at the permuted
 //    slots of the shared ModUp output with the rotate-then-switch key;
 //  * k_bsgs_gemm: for every REP-group of slots (the slots that share one compressed
-//    plaintext word) the products are a dense (2G x 2b1) x (2b1 x slots) product of words
+//    plaintext word) the products are a dense (G x 2b1) x (2b1 x slots) product of words
 //    mod q; the kernel stages babies and plaintext words in shared memory and accumulates
 //    128-bit;
-//  * one ModDown per giant input (2G of them, batched), then the giant rotations summed by
+//  * one ModDown per giant input (G of them, batched), then the giant rotations summed by
 //    rotate_sum (one batched ModUp, one ModDown of the sum).
 #include <cmath>
 #include <cstring>
