@@ -482,7 +482,8 @@ std::shared_ptr<MatvecPlan> matvec_plan(Context& cx, const double* W, int rows, 
     pl->D = D; pl->b1 = b1; pl->G = D / b1; pl->rows = rows; pl->cols = cols;
     pl->nsets = (cols + D - 1) / D;
     const int G = pl->G, S = pl->nsets;
-    if (2 * G > 64) throw Error("matvec_plan: too many giant steps (2 D / b1 must be <= 64)", -1);
+    // matvec_apply's product tile pairs the M = max(2, G) outputs of one giant family: G <= 64
+    if (G > 64) throw Error("matvec_plan: too many giant steps (D / b1 must be <= 64)", -1);
     pl->ids.assign((size_t)S * 3 * G * b1, -1);
     // family vectors, then small-ring coefficients (in parallel)
     struct Job { int s, fam, g, j; };

@@ -23,7 +23,8 @@
 //    that overlap in time (different contexts' streams, or different host threads) race on
 //    it.  Calls through one context are ordered by that context's stream and do not.
 //  * the first call on a device does the set-up (cudaGetSymbolAddress, which may load the
-//    module on that device); make it before any stream capture on that device.
+//    module on that device); make it before any stream capture on that device.  A set-up
+//    that fails is reported and retried by the next call; it does not disable the entry point.
 //  * per-kernel profiling (fhe_prof_enable) creates CUDA events, so it must be off.
 //  * no word of the scratch is read before this call writes it (the table is copied in
 //    first, ModUp writes every extended limb, the inner product and ModDown write every word
@@ -49,23 +50,26 @@ __global__ void k_noalloc_tab(const NoAllocTab t, uint64_t* __restrict__ dst, in
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) dst[i] = t.w[i];
 }
 
-static std::once_flag g_noalloc_once[kNoAllocMaxDevices];
+static std::mutex g_noalloc_mu;
 static uint64_t* g_noalloc_ptr[kNoAllocMaxDevices];
-static cudaError_t g_noalloc_err[kNoAllocMaxDevices];
 
-// Device address of the scratch on `dev`, which the caller has made current.  Looked up once
-// per device; a failed lookup is remembered and reported on every later call.
+// Device address of the scratch on `dev`, which the caller has made current.  Looked up on the
+// first call that succeeds on a device and kept; a failed lookup (for example one made during a
+// stream capture) is not remembered: its error is cleared from the runtime's sticky last-error
+// slot and reported, and the next call tries again.
 static uint64_t* noalloc_scratch(int dev) {
     if (dev < 0 || dev >= kNoAllocMaxDevices) throw Error("fhe_keyswitch_noalloc: device index out of range", -1);
-    std::call_once(g_noalloc_once[dev], [dev] {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
         void* p = nullptr;
-        g_noalloc_err[dev] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            throw Error(std::string("fhe_keyswitch_noalloc: cudaGetSymbolAddress failed: ") + cudaGetErrorString(e),
+                        -3);
+        }
         g_noalloc_ptr[dev] = static_cast<uint64_t*>(p);
-    });
-    if (g_noalloc_err[dev] != cudaSuccess)
-        throw Error(std::string("fhe_keyswitch_noalloc: cudaGetSymbolAddress failed: ") +
-                        cudaGetErrorString(g_noalloc_err[dev]),
-                    -3);
+    }
     return g_noalloc_ptr[dev];
 }
 

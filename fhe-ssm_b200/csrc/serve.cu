@@ -3,7 +3,9 @@
 //
 // Protocol, all inside one request directory:
 //   client: writes req.<N>.0 .. req.<N>.<count-1> (ciphertexts) and req.<N>.meta (JSON with
-//           at least "count"; "lanes", "tokensReal", ... are echoed), optionally req.<N>.reset
+//           at least "count"; the reference's other fields are checked when present -- ringDim
+//           and level against the ciphertexts, interleave 0, packTokens <= 1 -- and lanes,
+//           tokensReal, dpad, packTokens are echoed in resp.<N>.meta), optionally req.<N>.reset
 //           (drop the carried state first: a new session), then creates req.<N>.ready.
 //   server: runs one step per request in order N = 0, 1, ..., writes resp.<N>.<i>,
 //           resp.<N>.meta, then resp.<N>.done -- or resp.<N>.error with the message -- and
@@ -132,9 +134,15 @@ int fhe_serve_files(const char* dir, int timeout_ms, int max_requests, fhe_serve
                 N++;
             };
             std::string meta;
-            long long count = -1;
+            long long count = -1, mv = 0;
             if (!read_text(req + ".meta", meta) || !json_int(meta, "count", count) || count < 1 || count > 1024) {
                 fail("bad or missing request meta");
+                continue;
+            }
+            // the reference's packing fields (gpu_real_model.cu:2333-2340): this engine serves the
+            // block layout with one token per lane, so an interleaved or multi-token pack is refused
+            if ((json_int(meta, "interleave", mv) && mv != 0) || (json_int(meta, "packTokens", mv) && mv > 1)) {
+                fail("request meta asks for an interleaved or multi-token pack; this server runs the block layout");
                 continue;
             }
             const bool reset = file_exists(req + ".reset");
@@ -143,6 +151,14 @@ int fhe_serve_files(const char* dir, int timeout_ms, int max_requests, fhe_serve
             for (long long i = 0; i < count && ok; i++) ok = read_ct(req + "." + std::to_string(i), ins[i]);
             if (!ok) {
                 fail("unreadable request ciphertext");
+                continue;
+            }
+            long long ring = 0, lvl = 0;
+            for (long long i = 0; i < count && ok; i++)
+                ok = (!json_int(meta, "ringDim", ring) || ring == (1LL << ins[i].logN)) &&
+                     (!json_int(meta, "level", lvl) || lvl == ins[i].level);
+            if (!ok) {
+                fail("request meta (ringDim / level) does not match its ciphertexts");
                 continue;
             }
             std::vector<fhe_wire_ct> win((size_t)count), wout((size_t)count);
@@ -158,12 +174,25 @@ int fhe_serve_files(const char* dir, int timeout_ms, int max_requests, fhe_serve
                 fail(rc != 0 ? std::string("step failed: ") + fhe_last_error() : "step returned no output");
                 continue;
             }
+            // an output must fit the buffer of its input: same ring, 1..in.nl limbs
+            for (int i = 0; i < n_out && ok; i++)
+                ok = wout[i].nl >= 1 && wout[i].nl <= ins[i].nl && wout[i].logN == ins[i].logN;
+            if (!ok) {
+                fail("step returned an output larger than its input or of another ring");
+                continue;
+            }
             for (int i = 0; i < n_out; i++) write_ct(resp + "." + std::to_string(i), wout[i]);
-            long long lanes = 0, toks = 0;
-            std::string rm = "{\"count\":" + std::to_string(n_out) + ",\"level\":" + std::to_string(wout[0].level);
-            if (json_int(meta, "lanes", lanes)) rm += ",\"lanes\":" + std::to_string(lanes);
-            if (json_int(meta, "tokensReal", toks)) rm += ",\"tokensReal\":" + std::to_string(toks);
-            rm += ",\"ringDim\":" + std::to_string(1LL << wout[0].logN) + ",\"reset\":" + (reset ? "true" : "false") + "}\n";
+            // the reference's response meta fields, in its order (writeCtMeta, gpu_real_model.cu:2333-2340)
+            long long lanes = 1, toks = 0, pack = 1, dpad = 0;
+            json_int(meta, "lanes", lanes);
+            json_int(meta, "tokensReal", toks);
+            json_int(meta, "packTokens", pack);
+            json_int(meta, "dpad", dpad);
+            std::string rm = "{\"count\":" + std::to_string(n_out) + ",\"packTokens\":" + std::to_string(pack) +
+                             ",\"tokensReal\":" + std::to_string(toks) + ",\"dpad\":" + std::to_string(dpad) +
+                             ",\"interleave\":0,\"lanes\":" + std::to_string(lanes) +
+                             ",\"ringDim\":" + std::to_string(1LL << wout[0].logN) +
+                             ",\"level\":" + std::to_string(wout[0].level) + ",\"reset\":" + (reset ? "true" : "false") + "}\n";
             write_text_atomic(resp + ".meta", rm);
             write_text_atomic(resp + ".done", "ok\n");
             for (long long i = 0; i < count; i++) std::remove((req + "." + std::to_string(i)).c_str());

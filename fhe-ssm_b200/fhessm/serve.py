@@ -83,8 +83,15 @@ def serve_files(reqdir, step, timeout_ms=60000, max_requests=0):
                 a = np.ctypeslib.as_array(w.words, shape=(2 * w.nl << w.logN,)).reshape(2, w.nl, 1 << w.logN).copy()
                 cts.append((w.level, w.scale, a))
             res = step(bool(reset), cts)
+            # out[i].words has room for the words of input i only: check every result first
+            if not 1 <= len(res) <= n_in:
+                return -7
+            res = [(lv, sc, np.ascontiguousarray(wd, dtype=np.uint64)) for lv, sc, wd in res]
+            for i, (_, _, words) in enumerate(res):
+                if (words.ndim != 3 or words.shape[0] != 2 or words.shape[2] != 1 << inp[i].logN
+                        or not 1 <= words.shape[1] <= inp[i].nl):
+                    return -7
             for i, (level, scale, words) in enumerate(res):
-                words = np.ascontiguousarray(words, dtype=np.uint64)
                 out[i].level, out[i].nl, out[i].scale = level, words.shape[1], scale
                 C.memmove(out[i].words, words.ctypes.data, words.nbytes)
             n_out[0] = len(res)

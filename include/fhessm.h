@@ -258,9 +258,12 @@ typedef struct {
     double scale;
     uint64_t* words;   /* [2][nl][2^logN] */
 } fhe_wire_ct;
-/* one step: n_in request ciphertexts in; fill out[0..*n_out) (each out[i].words has room for
- * the words of in[i]); reset != 0: a new session.  Returns FHE_OK or a status (message via
- * fhe_last_error). */
+/* one step: n_in request ciphertexts in; fill out[0..*n_out) with 1 <= *n_out <= n_in.  out[i].words
+ * has room for the words of in[i] only, so output i must keep in[i].logN and at most in[i].nl limbs;
+ * the loop answers a request whose outputs break this with resp.<N>.error (the callback itself must
+ * not write past that room).  reset != 0: a new session.  Returns FHE_OK or a status (message via
+ * fhe_last_error).  Request meta fields of the reference (ringDim, level, interleave, packTokens) are
+ * checked when present; lanes, tokensReal, dpad and packTokens are echoed in resp.<N>.meta. */
 typedef int (*fhe_serve_step_fn)(void* user, int reset, int n_in, const fhe_wire_ct* in, int* n_out,
                                  fhe_wire_ct* out);
 int fhe_serve_files(const char* dir, int timeout_ms, int max_requests, fhe_serve_step_fn step, void* user,
@@ -292,7 +295,8 @@ int fhe_keyswitch_host(fhe_ctx* cx, const uint64_t* d, int level, const uint64_t
  * fhe_keyswitch_host.  Working memory is a static 64 MiB device array per GPU
  * (FHE_NOALLOC_SCRATCH_MIB): at N = 2^16, K = 4, alpha = 4 at most 16 limbs; larger requests
  * return FHE_ERR_ARG.  Overlapping calls on one GPU (different contexts or threads) race on
- * that array.  The first call on a GPU does the set-up; make it before any stream capture.
+ * that array.  The first call on a GPU does the set-up; make it before any stream capture (a
+ * failed set-up returns an error and is retried by the next call).
  * Per-kernel profiling must be off. */
 #define FHE_NOALLOC_SCRATCH_MIB 64
 int fhe_keyswitch_noalloc(fhe_ctx* cx, uint64_t which, const uint64_t* d, int level, uint64_t* out0,

@@ -74,6 +74,46 @@ def test_noalloc_matches_allocating_keyswitch_on_consecutive_calls(env):
     assert (from_dev(c0) == e0).all() and (from_dev(c1) == e1).all()
 
 
+def _pool_high_water(reset):
+    """Used-memory high-water mark of device 0's default memory pool (the pool the engine's
+    stream-ordered allocations come from), through the driver API; reset=True restarts it."""
+    cu = C.CDLL("libcuda.so.1")
+    pool = C.c_void_p()
+    assert cu.cuDeviceGetDefaultMemPool(C.byref(pool), 0) == 0
+    used_high = 8   # CU_MEMPOOL_ATTR_USED_MEM_HIGH (value type cuuint64_t)
+    v = C.c_uint64(0)
+    if reset:
+        assert cu.cuMemPoolSetAttribute(pool, used_high, C.byref(v)) == 0
+    assert cu.cuMemPoolGetAttribute(pool, used_high, C.byref(v)) == 0
+    return v.value
+
+
+def test_noalloc_allocates_nothing(env):
+    """The property the entry point exists for: across calls (after the first, which sets up the
+    per-GPU scratch address), neither the pool's high-water mark nor the device's free memory
+    moves."""
+    cx, h, torch = env
+    rng = np.random.default_rng(5)
+    lv = 6
+    d = to_dev(torch, rand_limbs(cx, cx.L - lv, rng))
+    o0 = torch.empty((cx.L - lv, cx.N), dtype=torch.int64, device="cuda:0")
+    o1 = torch.empty_like(o0)
+    k = cx.rot_index(1)
+    assert h.fhe_keyswitch_noalloc(cx.h, 0, d.data_ptr(), lv, o0.data_ptr(), o1.data_ptr()) == 0
+    cx.sync()
+    torch.cuda.synchronize()
+    mem0 = cx.memory()
+    free0 = torch.cuda.mem_get_info(0)[0]
+    hw0 = _pool_high_water(reset=True)
+    for which in (0, k, 0):
+        assert h.fhe_keyswitch_noalloc(cx.h, which, d.data_ptr(), lv, o0.data_ptr(), o1.data_ptr()) == 0
+    cx.sync()
+    mem1 = cx.memory()
+    assert _pool_high_water(reset=False) <= hw0, "the pool's high-water mark grew during no-alloc calls"
+    assert (mem1["pool_used"], mem1["pool_reserved"]) == (mem0["pool_used"], mem0["pool_reserved"])
+    assert torch.cuda.mem_get_info(0)[0] == free0
+
+
 def test_noalloc_refuses_oversize_and_host_memory(env):
     cx, h, torch = env
     d = torch.zeros((cx.L, cx.N), dtype=torch.int64, device="cuda:0")
