@@ -246,6 +246,18 @@ int fhe_encode(fhe_ctx* cx, const double* re, const double* im, int n, int level
         *out = new fhe_pt{fhe::encode(c, z.data(), n, nl, sc), cx};
     });
 }
+int fhe_encode_periodic(fhe_ctx* cx, const double* re, const double* im, int period, int count, int level,
+                        double scale, uint64_t* words) {
+    return guard([&] {
+        REQUIRE(cx && re && words && period > 0 && count > 0, "bad argument");
+        bind(cx);
+        auto& c = cx->cx;
+        const int nl = nl_of(c, level);
+        std::vector<std::complex<double>> z((size_t)period * count);
+        for (size_t i = 0; i < z.size(); i++) z[i] = std::complex<double>(re[i], im ? im[i] : 0.0);
+        fhe::encode_periodic_words(c, z.data(), period, count, nl, scale > 0 ? scale : c.scale_at[nl], words);
+    });
+}
 int fhe_decode(fhe_ctx* cx, const fhe_pt* pt, double* re, double* im) {
     return guard([&] {
         REQUIRE(cx && pt && re, "null argument");

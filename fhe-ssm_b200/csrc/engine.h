@@ -287,6 +287,8 @@ const Plaintext& encode_cached(Context& cx, const std::complex<double>* z, int n
 struct MatvecPlan;
 std::shared_ptr<MatvecPlan> matvec_plan(Context& cx, const double* W, int rows, int cols, int D, int b1);
 std::vector<int> matvec_rotations(int D, int b1);
+void encode_periodic_words(Context& cx, const std::complex<double>* z, int period, int count, int nl, double scale,
+                           uint64_t* host_out);
 void matvec(Context& cx, const MatvecPlan& pl, const Ciphertext* const* us, Ciphertext& out);
 struct BabySet;
 void matvec_babies(Context& cx, const Ciphertext& u, int D, int b1, BabySet& bs);

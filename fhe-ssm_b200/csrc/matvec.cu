@@ -542,6 +542,60 @@ std::shared_ptr<MatvecPlan> matvec_plan(Context& cx, const double* W, int rows, 
     return pl;
 }
 
+// The compressed store entries of `count` period-`period` slot vectors (the reference's
+// periodicEncodeComp, hpc_gpu_port/periodic_encode.hpp:263-276): the plan's small-ring inverse
+// FFT on the host, then the plan's device generator (k_ptgen2048 at period 1024, else k_ptgen)
+// in canonical form.  host_out: [count][nl][2 period]; word j2 of limb l is word
+// j2 << log2(N / (2 period)) of the dense encoding of the tiled vector.
+void encode_periodic_words(Context& cx, const std::complex<double>* z, int period, int count, int nl, double scale,
+                           uint64_t* host_out) {
+    const int D = period, D2 = 2 * period;
+    if (D < 4 || (D & (D - 1)) || (cx.N / 2) % D || D > 2048 || count < 1 || nl < 1 || nl > cx.L)
+        throw Error("encode_periodic: period must be a power of two in [4, 2048] dividing N/2; 1 <= limbs <= L", -1);
+    std::vector<double> flat((size_t)count * D2);
+    const double maxv = (double)((1ull << 61) - 1);
+#pragma omp parallel for schedule(dynamic, 4)
+    for (int t = 0; t < count; t++) {
+        std::vector<std::complex<double>> v(z + (size_t)t * D, z + (size_t)(t + 1) * D);
+        fft_special_inv_small(v.data(), D, 4 * D);
+        for (int k = 0; k < D; k++) {
+            flat[(size_t)t * D2 + k] = v[k].real();
+            flat[(size_t)t * D2 + k + D] = v[k].imag();
+        }
+    }
+    for (double c : flat)
+        if (std::fabs(c * scale) > maxv) throw Error("encode: value * scale exceeds 61 bits (refused)", -6);
+    DevBuf dc(flat.size(), cx.stream), out((size_t)nl * D2 * count, cx.stream);
+    CUDA_CHECK(cudaMemcpyAsync(dc.p, flat.data(), flat.size() * 8, cudaMemcpyHostToDevice, cx.stream));
+    if (D2 == 2048) {
+        const size_t smem = (size_t)(2 + 4) * 2048 * 8;
+        CUDA_CHECK(cudaFuncSetAttribute(k_ptgen2048, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        k_ptgen2048<<<dim3((count + 3) / 4, nl), 256, smem, cx.stream>>>((const double*)dc.p, scale, out.p, count, nl,
+                                                                        cx.L, (const ulonglong2*)cx.d_tw2, cx.d_rmont,
+                                                                        cx.N, 0);
+    } else {
+        constexpr int IPC = 4;
+        int logD2 = 0;
+        while ((1 << logD2) < D2) logD2++;
+        const size_t smem = (size_t)IPC * D2 * 8;
+        if (smem > 48 * 1024)
+            CUDA_CHECK(cudaFuncSetAttribute(k_ptgen<IPC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        k_ptgen<IPC><<<dim3((count + IPC - 1) / IPC, nl), 256, smem, cx.stream>>>((const double*)dc.p, scale, out.p,
+                                                                                count, nl, cx.L, logD2, cx.d_tw,
+                                                                                cx.d_twp, cx.N, 0);
+    }
+    CUDA_CHECK(cudaGetLastError());
+    cx.launches++;
+    // [limb][2D][count] on the device -> [count][limb][2D] for the caller
+    std::vector<uint64_t> tr(out.words);
+    CUDA_CHECK(cudaMemcpyAsync(tr.data(), out.p, tr.size() * 8, cudaMemcpyDeviceToHost, cx.stream));
+    CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+    for (int l = 0; l < nl; l++)
+        for (int k = 0; k < D2; k++)
+            for (int t = 0; t < count; t++)
+                host_out[((size_t)t * nl + l) * D2 + k] = tr[((size_t)l * D2 + k) * count + t];
+}
+
 std::vector<int> matvec_rotations(int D, int b1) {
     std::vector<int> r;
     for (int j = 1; j < b1; j++) r.push_back(j);

@@ -56,6 +56,7 @@ _SIGS = {
     "fhe_rot_index": (C.c_uint64, [_VP, C.c_int32]),
     "fhe_encode": (C.c_int, [_VP, _DP, _DP, C.c_int, C.c_int, C.c_double, C.POINTER(_VP)]),
     "fhe_decode": (C.c_int, [_VP, _VP, _DP, _DP]),
+    "fhe_encode_periodic": (C.c_int, [_VP, _DP, _DP, C.c_int, C.c_int, C.c_int, C.c_double, _U64P]),
     "fhe_pt_free": (None, [_VP]),
     "fhe_pt_level": (C.c_int, [_VP]),
     "fhe_encrypt": (C.c_int, [_VP, _VP, C.POINTER(_VP)]),
@@ -310,6 +311,22 @@ class CryptoContext:
         _check(lib().fhe_encode(self.h, re.ctypes.data_as(_DP), im.ctypes.data_as(_DP), len(z), level, scale,
                                 C.byref(h)))
         return Plaintext(self, h)
+
+    def periodic_encode_comp(self, periods, level=0, scale=0.0):
+        """Compressed store entries of period vectors (the reference's periodicEncodeComp,
+        periodic_encode.hpp:263-276): periods (count, period) complex -> words
+        [count][L - level][2 period]; word j2 of a limb equals word j2 << log2(N / (2 period)) of
+        the dense encoding of the tiled vector."""
+        z = np.asarray(periods, dtype=np.complex128)
+        if z.ndim == 1:
+            z = z[None]
+        count, period = z.shape
+        re = np.ascontiguousarray(z.real)
+        im = np.ascontiguousarray(z.imag)
+        out = np.empty((count, self.L - level, 2 * period), dtype=np.uint64)
+        _check(lib().fhe_encode_periodic(self.h, re.ctypes.data_as(_DP), im.ctypes.data_as(_DP), period, count, level,
+                                         scale, out.ctypes.data_as(_U64P)))
+        return out
 
     def Decode(self, pt):
         re = np.empty(self.slots)

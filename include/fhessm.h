@@ -115,6 +115,15 @@ uint64_t fhe_rot_index(const fhe_ctx* cx, int32_t step);
 int fhe_encode(fhe_ctx* cx, const double* re, const double* im, int n, int level, double scale, fhe_pt** out);
 /* replaces Plaintext::GetRealPackedValue / GetCKKSPackedValue (:2211): N/2 slots */
 int fhe_decode(fhe_ctx* cx, const fhe_pt* pt, double* re, double* im);
+/* The compressed store entry of a periodic slot vector (replaces periodicEncodeComp,
+ * hpc_gpu_port/periodic_encode.hpp:263-276, the store entry of buildComp, gpu_real_model.cu:
+ * 2888-2925): count vectors of `period` complex slots (re, im: [count][period]; im may be NULL),
+ * each tiled N/(2 period) times across the slots, encoded at `level` and `scale` (<= 0: the
+ * level's scale) into words [count][L - level][2 period], canonical.  Word j2 of limb l equals
+ * word j2 << log2(N / (2 period)) of fhe_encode of the tiled vector.  period: a power of two in
+ * [4, 2048] dividing N/2.  The words come from the device generator the matvec plans use. */
+int fhe_encode_periodic(fhe_ctx* cx, const double* re, const double* im, int period, int count, int level,
+                        double scale, uint64_t* words);
 void fhe_pt_free(fhe_pt* pt);
 int fhe_pt_level(const fhe_pt* pt);
 

@@ -183,10 +183,7 @@ uint64_t oc_root(const oc_ctx* c, int m) { return c->psi[m]; }
 
 /* ================================ NTT ============================================== */
 /* Cooley-Tukey, natural in -> bit-reversed out (periodic_encode.hpp:241-260 loop shape). */
-void oc_ntt(const oc_ctx* c, uint64_t* a, int m) {
-    const uint64_t q = c->mod[m];
-    const uint64_t* tab = c->tab[m];
-    const int n = c->N;
+static void ntt_ct(uint64_t q, const uint64_t* tab, int n, uint64_t* a) {
     for (int mm = 1, t = n >> 1; mm < n; mm <<= 1, t >>= 1) {
         for (int i = 0; i < mm; i++) {
             const int j1 = i * 2 * t;
@@ -199,6 +196,21 @@ void oc_ntt(const oc_ctx* c, uint64_t* a, int m) {
             }
         }
     }
+}
+void oc_ntt(const oc_ctx* c, uint64_t* a, int m) { ntt_ct(c->mod[m], c->tab[m], c->N, a); }
+/* The same transform at ring 2^logN with an explicit primitive 2^(logN+1)-th root psi: the
+ * table Tab[brev(i)] = psi^i is built as the context builds its own (the periodic encoder's
+ * small-ring transform, periodic_encode.hpp:150-160, takes psi' = psi^REP). */
+void oc_ntt_root(int logN, uint64_t q, uint64_t psi, uint64_t* a) {
+    const int n = 1 << logN;
+    uint64_t* tab = (uint64_t*)malloc(sizeof(uint64_t) * n);
+    uint64_t x = 1;
+    for (int i = 0; i < n; i++) {
+        tab[brev((uint32_t)i, logN)] = x;
+        x = oc_mulmod(x, psi, q);
+    }
+    ntt_ct(q, tab, n, a);
+    free(tab);
 }
 /* Gentleman-Sande, bit-reversed in -> natural out, then * N^-1. */
 void oc_intt(const oc_ctx* c, uint64_t* a, int m) {

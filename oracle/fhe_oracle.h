@@ -45,6 +45,8 @@ uint64_t oc_root(const oc_ctx* c, int m);
 
 /* ---- NTT (periodic_encode.hpp:241-260 ordering: natural in, bit-reversed out) ----- */
 void oc_ntt(const oc_ctx* c, uint64_t* a, int m);
+/* the same transform at ring 2^logN with an explicit primitive 2^(logN+1)-th root psi */
+void oc_ntt_root(int logN, uint64_t q, uint64_t psi, uint64_t* a);
 void oc_intt(const oc_ctx* c, uint64_t* a, int m);
 /* eval-form automorphism X -> X^k (k odd): out[i] = in[j], 2brev(j)+1 = k(2brev(i)+1) mod 2N */
 void oc_automorph_eval(const oc_ctx* c, const uint64_t* in, uint64_t* out, uint64_t k);

@@ -38,6 +38,7 @@ def load():
         "oc_root": (C.c_uint64, [C.c_void_p, C.c_int]),
         "oc_ntt": (None, [C.c_void_p, U64P, C.c_int]),
         "oc_intt": (None, [C.c_void_p, U64P, C.c_int]),
+        "oc_ntt_root": (None, [C.c_int, C.c_uint64, C.c_uint64, U64P]),
         "oc_automorph_eval": (None, [C.c_void_p, U64P, U64P, C.c_uint64]),
         "oc_automorph_coeff": (None, [C.c_void_p, U64P, U64P, C.c_uint64, C.c_int]),
         "oc_rot_index": (C.c_uint64, [C.c_int, C.c_int64]),
