@@ -172,7 +172,8 @@ def roofline(prof):
     kern = {k: v for k, v in prof.items() if not k.startswith("op:")}
     if not kern:
         return None
-    name, (n, tms, tbytes) = max(kern.items(), key=lambda kv: kv[1][1])
+    name, v = max(kern.items(), key=lambda kv: kv[1][1])
+    n, tms, tbytes = v[:3]
     achieved = tbytes / (tms / 1000.0) / 1e9
     peak = pk.get("hbm_gbs", 6650.0)
     traffic = None
@@ -188,11 +189,37 @@ def roofline(prof):
             "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if "hbm_gbs" in pk else "fallback 6650 GB/s"}
 
 
+def tensor_pipe(prof):
+    """The tcgen05 BSGS product against the dense int8 tensor peak: int8 multiply-accumulates the
+    kernel issues (counted by the engine per launch) per second of its device time.  The int8 peak
+    is taken as twice the measured bf16 rate (the nominal dense int8 : bf16 ratio), i.e. the
+    measured bf16 TFLOP/s figure read as tera-MAC/s."""
+    v = (prof or {}).get("bsgs_tc")
+    if not v or len(v) < 4 or not v[1] or not v[3]:
+        return None
+    pk = peaks()
+    peak = pk.get("bf16_tflops", 1590.0)
+    achieved = v[3] / (v[1] / 1000.0) / 1e12
+    return {"kernel": "k_bsgs_tc2", "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "int8 TMAC/s",
+            "frac": achieved / peak, "launches": v[0], "ms": v[1],
+            "peak_source": ("MEASURED_PEAKS.json bf16_tflops x 2 (int8 ops), as MAC/s (of measured)"
+                            if "bf16_tflops" in pk else "fallback 1.59 PFLOP/s bf16 x 2 (of fallback)")}
+
+
 def kernel_table(prof):
     """Per kernel class: launches, device ms, achieved GB/s of algorithmic bytes.  Entries
     named op:* are inclusive times of whole operations (bootstrap, matvec, ...)."""
     return {k: {"launches": v[0], "ms": round(v[1], 3),
                 "GB/s": round(v[2] / (v[1] / 1000.0) / 1e9, 1) if v[1] and v[2] else None} for k, v in prof.items()}
+
+
+def census():
+    """The 405M pass's key-switch census, committed by hand from a bench line's "census" (the
+    reference arm scales its timed key switches by it)."""
+    try:
+        return json.load(open(CENSUS))
+    except Exception:
+        return None
 
 
 # ------------------------------------------------------------------------ CPU oracle ----
@@ -226,14 +253,39 @@ def oracle_keyswitch_seconds(nl_avg, nthreads, seconds):
     return (time.time() - t0) / done, done, nl
 
 
-def census():
-    try:
-        return json.load(open(CENSUS))
-    except Exception:
-        return None
-
-
 # ------------------------------------------------------------------------ workloads ----
+def oracle_hmult_setup(L=20, K=4, logN=16):
+    """Config 2's HMult on the C oracle: a relinearisation key and one ciphertext pair at N = 2^16,
+    L limbs (45-bit primes over a 60-bit q0, K x 60-bit special primes, dnum = ceil(L/4))."""
+    from oracle_lib import Oracle, derive_seed, gen_chain, load
+    lib = load()
+    q, p = gen_chain(logN, L, 60, 45, K, 60, lib)
+    o = Oracle(logN, q, p, 4, lib)
+    ms = (1).to_bytes(8, "little") + bytes(24)
+    se = o.secret_eval(o.secret(derive_seed(lib, ms, 0xFFFFFFF1), 192))
+    # a switching key of the relinearisation key's shape (its words do not change the work)
+    rlk = o.keygen_switch(se, se, derive_seed(lib, ms, 2))
+    rng = np.random.default_rng(9)
+    a = rand_ct_words(rng, o.mods, L, o.N)
+    b = rand_ct_words(rng, o.mods, L, o.N)
+    return o, rlk, a, b
+
+
+def oracle_hmult_batch(o, rlk, a, b, L, nthreads):
+    """nthreads HMult + relinearise + rescale of the oracle run concurrently (ctypes releases the
+    GIL); returns the wall seconds of the batch."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    def one(_):
+        o.ct_rescale(o.ct_mul_relin(a, b, L, rlk), L)
+        return 1
+
+    t0 = time.time()
+    with ThreadPoolExecutor(nthreads) as ex:
+        assert sum(ex.map(one, range(nthreads))) == nthreads
+    return time.time() - t0
+
+
 def run_model(args, ws, rank, local):
     import torch
 
@@ -272,8 +324,6 @@ def run_model(args, ws, rank, local):
     l0 = cx.launches()
     k0 = cx.counters()
     b0 = m.stats()["bootstraps"]
-    cx.set_option("profile_every", 8)   # time one kernel call in 8 of each kind: the timer stays out of the way
-    cx.profile(True)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(ws)
     torch.cuda.nvtx.range_push("timed")   # ncu --nvtx --nvtx-include "timed/" selects these launches
@@ -287,8 +337,6 @@ def run_model(args, ws, rank, local):
     barrier(ws)
     clocks = clk.stop()
     ms = e0.elapsed_time(e1)
-    prof = cx.profile_collect()
-    cx.profile(False)
     launches = cx.launches() - l0
     k1 = cx.counters()
     boots = (m.stats()["bootstraps"] - b0) / args.steps
@@ -296,6 +344,14 @@ def run_model(args, ws, rank, local):
     ks_nl_avg = (k1[1] - k0[1]) / max(1, k1[0] - k0[0])
     ms_max = max_over_ranks(ms, ws)
     value = aggregate_tokens_per_s(LANES, ws, args.steps, ms_max)
+
+    # the per-kernel table and the roofline come from one more pass, outside the timed region, with
+    # every kernel call bracketed by CUDA events on the engine's stream
+    cx.set_option("profile_every", 1)
+    cx.profile(True)
+    m.step(cts[nsteps - 1])
+    prof = cx.profile_collect()
+    cx.profile(False)
 
     # fidelity against the float64 model (exact 1/sqrt), replaying every step from a cold state
     state, errs, top1 = None, [], []
@@ -319,16 +375,18 @@ def run_model(args, ws, rank, local):
     e2e = {"value": LANES * ws / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(words_in.nbytes),
            "d2h_bytes_per_step": int(words_out.nbytes)}
 
+    fidelity = {"logits_relErrRms_max": max(errs), "top1_min": min(top1), "vs": "float64 model, exact 1/sqrt",
+                "bar": "relErrRms <= 1e-3 and top-1 >= 0.98"}
+    fidelity["ok"] = bool(fidelity["logits_relErrRms_max"] <= 1e-3 and fidelity["top1_min"] >= 0.98)
+
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         t_ks, n, nl = oracle_keyswitch_seconds(ks_nl_avg, 1, 10.0)
         cpu = {"value": LANES / (ks_per_pass * t_ks), "unit": "tokens/s", "cores": 1, "kind": "port",
+               "method": "estimate: timed key switches x the pass's key-switch census",
                "sample": f"{n} hybrid key switches of the C oracle at N=2^16, {nl} limbs (the pass's average), "
-                         f"single thread, scaled by the pass's {ks_per_pass:.0f} key switches (a lower bound on "
-                         f"the CPU pass time: all other work of the pass is excluded)"}
-        os.makedirs(os.path.dirname(CENSUS), exist_ok=True)
-        json.dump({"keyswitches_per_pass": ks_per_pass, "ks_avg_limbs": ks_nl_avg, "bootstraps_per_pass": boots,
-                   "kernel_launches_per_pass": launches / args.steps, "config": "405m"}, open(CENSUS, "w"), indent=1)
+                         f"single thread, timed, then scaled by the pass's {ks_per_pass:.0f} key switches (a lower "
+                         f"bound on the CPU pass time: all other work of the pass is excluded)"}
     if rank == 0:
         line = {
             "metric": METRIC_405M, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
@@ -338,13 +396,19 @@ def run_model(args, ws, rank, local):
                        "layers": cfg.n_layer, "d_model": cfg.d, "d_ffn": cfg.dff, "vocab": cfg.vocab,
                        "ring": "N=2^16, L=28 (60 + 13x45 + 14x58), K=4x60, HW 192", "global_batch": LANES * ws,
                        "parallelism": f"dp{ws} (independent packs)", "l2": "working set >> L2 (keys 39 GB)"},
-            "fidelity": {"logits_relErrRms_max": max(errs), "top1_min": min(top1), "vs": "float64 model, exact 1/sqrt"},
-            "bootstraps_per_pass": boots, "keyswitches_per_pass": ks_per_pass, "setup_s": setup_s,
-            "gpu_launches": launches, "clocks": clocks, "e2e": e2e, "roofline": roofline(prof), "cpu_baseline": cpu,
             "kernels": kernel_table(prof),
             "memory_gib": {k: round(v / 2**30, 2) for k, v in cx.memory().items()},
+            "census": {"keyswitches_per_pass": ks_per_pass, "ks_avg_limbs": ks_nl_avg, "bootstraps_per_pass": boots,
+                       "kernel_launches_per_pass": launches / args.steps},
+            "setup_s": setup_s, "gpu_launches": launches, "clocks": clocks, "e2e": e2e, "cpu_baseline": cpu,
+            "tensor_pipe": tensor_pipe(prof), "roofline": roofline(prof),
+            "fidelity": fidelity,
         }
         print(json.dumps(line), flush=True)
+        print(f"fidelity: logits relErrRms max {fidelity['logits_relErrRms_max']:.3e}, top-1 min "
+              f"{fidelity['top1_min']:.4f} ({'ok' if fidelity['ok'] else 'FAILED'})", file=sys.stderr, flush=True)
+    if not fidelity["ok"]:
+        raise SystemExit(f"fidelity below the bar on rank {rank}: {fidelity}")
 
 
 def run_hmult(args, ws, rank, local):
@@ -374,7 +438,6 @@ def run_hmult(args, ws, rank, local):
     clk = ClockSampler(local)
     clk.start()
     l0 = cx.launches()
-    cx.profile(True)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(ws)
     e0.record(stream)
@@ -386,11 +449,13 @@ def run_hmult(args, ws, rank, local):
     barrier(ws)
     clocks = clk.stop()
     ms = e0.elapsed_time(e1)
-    prof = cx.profile_collect()
-    cx.profile(False)
     launches = cx.launches() - l0
     ms_max = max_over_ranks(ms, ws)
     value = B * ws * args.steps / (ms_max / 1000.0)
+    cx.profile(True)   # the kernel table: one more step, outside the timed region
+    step()
+    prof = cx.profile_collect()
+    cx.profile(False)
     out_words = np.empty((2, L - 1, N), dtype=np.uint64)
     barrier(ws)
     t0 = time.time()
@@ -403,6 +468,17 @@ def run_hmult(args, ws, rank, local):
     e2e_s = max_over_ranks(time.time() - t0, ws)
     e2e = {"value": B * ws / e2e_s, "unit": "ciphertexts/s", "h2d_bytes_per_step": int(2 * B * host_a[0].nbytes),
            "d2h_bytes_per_step": int(B * out_words.nbytes)}
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        # the same operation on the C oracle, timed on this host: one thread, then every host thread
+        o, rlk, ha, hb = oracle_hmult_setup(L)
+        nth = os.cpu_count() or 1
+        t1 = oracle_hmult_batch(o, rlk, ha, hb, L, 1)
+        tn = min(oracle_hmult_batch(o, rlk, ha, hb, L, nth) for _ in range(2))
+        cpu = {"value": nth / tn, "unit": "ciphertexts/s", "cores": nth, "kind": "port",
+               "single_thread": 1.0 / t1,
+               "sample": f"C oracle HMult+relin+rescale at N=2^16, L={L}, dnum=5: 1 on one thread ({t1:.2f} s), "
+                         f"then {nth} at once on {nth} threads (best of 2 batches, {tn:.2f} s)"}
     if rank == 0:
         line = {
             "metric": METRIC_HMULT, "value": value, "unit": "ciphertexts/s", "n_gpus": ws, "steps": args.steps,
@@ -410,7 +486,7 @@ def run_hmult(args, ws, rank, local):
             "vs_baseline": None, "dtype": "u64 (RNS residues)", "data": "synthetic",
             "config": {"workload": "config 2: HMult+relin+rescale, N=2^16, L=20, K=4x60b, dnum=5",
                        "batch_per_gpu": B, "parallelism": f"dp{ws}", "l2": "inputs 2.7 GB per GPU > L2"},
-            "gpu_launches": launches, "clocks": clocks, "e2e": e2e, "roofline": roofline(prof), "cpu_baseline": None,
+            "gpu_launches": launches, "clocks": clocks, "e2e": e2e, "roofline": roofline(prof), "cpu_baseline": cpu,
             "kernels": kernel_table(prof),
         }
         print(json.dumps(line), flush=True)
@@ -502,34 +578,74 @@ def run_matvec(args, ws, rank, local):
 def run_reference(args):
     """The reference arm: the CPU path of the same workload on the host cores.  OpenFHE (the
     reference's arithmetic library) cannot be built here, so the C oracle (a restatement of the
-    same RNS-CKKS algorithms) stands in; the pass time is the pass's key-switch census times the
-    oracle's key-switch time on all host threads (a lower bound: everything else is excluded)."""
+    same RNS-CKKS algorithms, pinned to the reference's own expander and NTT) stands in.  Every step
+    is a real, bounded sample timed on the host: one batch of oracle operations on all host
+    threads.  hmult: the sample is config 2's operation itself, so `value` is measured directly.
+    405m: the sample is a batch of key switches at the pass's average limb count, and `value`
+    scales it by the pass's key-switch census (an estimate and a lower bound on the CPU pass: all
+    other work of the pass is left out); ms_per_step is the sample's own time."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    cen = census()
     nthreads = os.cpu_count() or 1
-    if args.workload == "405m":
-        if not cen:
-            print(json.dumps({"impl": "reference", "unavailable": "no key-switch census (profiles/pass_census.json)"}))
-            return 0
-        vals = []
+    base = {"impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "data": "synthetic"}
+    if args.workload == "hmult":
+        L = HMULT_CTX["L"]
+        o, rlk, ha, hb = oracle_hmult_setup(L)
+        times = []
         for i in range(args.warmup + args.steps):
-            t_ks, n, nl = oracle_keyswitch_seconds(cen["ks_avg_limbs"], nthreads, 2.0)
+            t = oracle_hmult_batch(o, rlk, ha, hb, L, nthreads)
             if i >= args.warmup:
-                vals.append(LANES / (cen["keyswitches_per_pass"] * t_ks))
-        value = statistics.mean(vals)
-        line = {"impl": "reference", "metric": METRIC_405M, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-                "ms_per_step": 1000.0 * LANES / value, "dtype": "u64 (RNS residues, CKKS)", "data": "synthetic",
-                "config": {"workload": "config 4: 405M poly-SSM, one encrypted decode pass, 64 conversations"},
-                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": nthreads, "kind": "port",
-                                 "sample": f"C oracle key switches at {nl} limbs on {nthreads} threads, scaled by "
-                                           f"{cen['keyswitches_per_pass']:.0f} key switches per pass"},
-                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+                times.append(t)
+        value = nthreads * len(times) / sum(times)
+        line = dict(base, metric=METRIC_HMULT, value=value, unit="ciphertexts/s",
+                    ms_per_step=1000.0 * statistics.mean(times), dtype="u64 (RNS residues)",
+                    config={"workload": "config 2: HMult+relin+rescale, N=2^16, L=20, K=4x60b, dnum=5"},
+                    cpu_baseline={"value": value, "unit": "ciphertexts/s", "cores": nthreads, "kind": "port",
+                                  "sample": f"per step {nthreads} C-oracle HMult+relin+rescale, one per thread"},
+                    e2e={"value": value, "unit": "ciphertexts/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
         print(json.dumps(line), flush=True)
         return 0
-    print(json.dumps({"impl": "reference", "unavailable": "reference arm implemented for the 405m workload only"}))
+    if args.workload != "405m":
+        print(json.dumps({"impl": "reference", "unavailable": "reference arm implemented for the 405m and hmult "
+                                                              "workloads"}))
+        return 0
+    cen = census()
+    if not cen:
+        print(json.dumps({"impl": "reference", "unavailable": "no key-switch census (profiles/pass_census.json)"}))
+        return 0
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle_lib import Oracle, derive_seed, gen_chain, load
+    lib = load()
+    q, p = gen_chain(16, 16, 60, 45, 4, 60, lib)
+    o = Oracle(16, q, p, 4, lib)
+    ms = (1).to_bytes(8, "little") + bytes(24)
+    se = o.secret_eval(o.secret(derive_seed(lib, ms, 0xFFFFFFF1), 192))
+    key = o.keygen_switch(se, se, derive_seed(lib, ms, 3))
+    nl = max(2, min(16, int(round(cen["ks_avg_limbs"]))))
+    rng = np.random.default_rng(5)
+    d = np.stack([rng.integers(0, int(o.mods[i]), o.N, dtype=np.uint64) for i in range(nl)])
+    times = []
+    with ThreadPoolExecutor(nthreads) as ex:
+        for i in range(args.warmup + args.steps):
+            t0 = time.time()
+            list(ex.map(lambda _: o.keyswitch(d, nl, key), range(nthreads)))
+            if i >= args.warmup:
+                times.append(time.time() - t0)
+    t_ks = sum(times) / (nthreads * len(times))          # seconds per key switch at full concurrency
+    value = LANES / (cen["keyswitches_per_pass"] * t_ks)
+    line = dict(base, metric=METRIC_405M, value=value, unit="tokens/s", ms_per_step=1000.0 * statistics.mean(times),
+                dtype="u64 (RNS residues, CKKS)",
+                config={"workload": "config 4: 405M poly-SSM, one encrypted decode pass, 64 conversations"},
+                cpu_baseline={"value": value, "unit": "tokens/s", "cores": nthreads, "kind": "port",
+                              "method": "estimate: timed key switches x the pass's key-switch census",
+                              "sample": f"per step {nthreads} C-oracle key switches at N=2^16, {nl} limbs, one per "
+                                        f"thread (timed; ms_per_step is this sample), scaled by "
+                                        f"{cen['keyswitches_per_pass']:.0f} key switches per pass"},
+                e2e={"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
+    print(json.dumps(line), flush=True)
     return 0
 
 

@@ -157,7 +157,7 @@ int fhe_prof_collect(fhe_ctx* cx, char* buf, int cap) {
             first = false;
             const double ms = e.sampled ? e.ms * (double)e.seen / (double)e.sampled : 0.0;
             js += "\"" + kv.first + "\": [" + std::to_string(e.seen) + ", " + std::to_string(ms) + ", " +
-                  std::to_string(e.bytes) + "]";
+                  std::to_string(e.bytes) + ", " + std::to_string(e.ops) + "]";
         }
         js += "}";
         c.prof_acc.clear();

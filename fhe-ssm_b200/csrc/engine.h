@@ -151,6 +151,7 @@ struct Context {
         std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pending;
         long long seen = 0, sampled = 0;
         double ms = 0.0, bytes = 0.0;
+        double ops = 0.0;   // tensor-core kernels: int8 multiply-accumulates issued (0 for the others)
     };
     bool prof = false;
     int prof_every = 1;
@@ -193,11 +194,12 @@ struct ProfScope {
     const char* name;
     double bytes;
     bool timed = false;
-    ProfScope(const Context& c, const char* n, double by) : cx(c), name(n), bytes(by) {
+    ProfScope(const Context& c, const char* n, double by, double ops = 0.0) : cx(c), name(n), bytes(by) {
         if (!cx.prof) return;
         auto& e = cx.prof_acc[name];
         timed = (e.seen++ % std::max(1, cx.prof_every)) == 0;
         e.bytes += bytes;
+        e.ops += ops;
         if (!timed) return;
         cudaEventCreate(&a);
         cudaEventCreate(&b);

@@ -813,7 +813,18 @@ void matvec_apply(Context& cx, const MatvecPlan& pl, const BabySet* const* sets,
             t.Kp = Kp;
             size_t smem = tc_smem_bytes(M, Kp);
             if (tcols == 512) smem = std::max<size_t>(smem, 120 * 1024);
-            ProfScope ps(cx, "bsgs_tc", bytes);
+            // int8 MACs the tensor cores are given: per CTA and input set, for each diagonal pair p of
+            // the limb's byte width, one 128 x M x 32 MMA per (byte slice, 32-deep K chunk)
+            double macs = 0.0;
+            for (int e = 0; e < ne; e++) {
+                uint64_t q = cx.mods[cx.ext_mod(nl, e)];
+                int nbyte = 0;
+                while (q) { nbyte++; q >>= 8; }
+                for (int p = 0; p < nbyte; p++)
+                    macs += (double)(std::min(nbyte - 1, 2 * p + 1) - std::max(0, 2 * p - (nbyte - 1)) + 1) * (Kp / 32);
+            }
+            macs *= (double)R * S * 128.0 * M * 32.0;
+            ProfScope ps(cx, "bsgs_tc", bytes, macs);
             auto launch = [&](auto kern) {
                 CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
                 kern<<<dim3(R, ne), kTcThreads, smem, st>>>(t, tcols, cx.d_err);

@@ -269,7 +269,8 @@ class CryptoContext:
         _check(lib().fhe_prof_enable(self.h, 1 if on else 0))
 
     def profile_collect(self):
-        """{kernel: (launches, total_ms, algorithmic_bytes)} since the last collect."""
+        """{kernel: (launches, total_ms, algorithmic_bytes, int8_macs)} since the last collect
+        (int8_macs: multiply-accumulates given to the tensor cores, 0 for the other kernels)."""
         import json
         buf = C.create_string_buffer(1 << 16)
         _check(lib().fhe_prof_collect(self.h, buf, len(buf)))
