@@ -523,6 +523,16 @@ int fhe_bootstrap(fhe_ctx* cx, const fhe_ct* a, fhe_ct** out) {
         *out = wrap(cx, std::move(r));
     });
 }
+int fhe_bootstrap_n(fhe_ctx* cx, const fhe_ct* const* in, int n, fhe_ct** out) {
+    return guard([&] {
+        REQUIRE(cx && in && out && n > 0, "null argument");
+        for (int i = 0; i < n; i++) REQUIRE(in[i], "null ciphertext");
+        bind(cx);
+        std::vector<fhe::Ciphertext> r((size_t)n);
+        for (int i = 0; i < n; i++) fhe::bootstrap(cx->cx, in[i]->c, r[i]);
+        for (int i = 0; i < n; i++) out[i] = wrap(cx, std::move(r[i]));
+    });
+}
 int fhe_bootstrap_stage(fhe_ctx* cx, const fhe_ct* a, int upto, fhe_ct** out) {
     return guard([&] {
         REQUIRE(cx && a && out && upto >= 1 && upto <= 4, "bad argument");

@@ -484,6 +484,16 @@ class CryptoContext:
         _check(lib().fhe_bootstrap(self.h, ct.h, C.byref(h)))
         return Ciphertext(self, h)
 
+    def EvalBootstrapBatch(self, cts):
+        """fhe_bootstrap_n: every ciphertext of the list, refreshed, in order."""
+        h = lib()
+        h.fhe_bootstrap_n.restype = C.c_int
+        h.fhe_bootstrap_n.argtypes = [_VP, C.POINTER(_VP), C.c_int, C.POINTER(_VP)]
+        ins = (_VP * len(cts))(*[c.h for c in cts])
+        outs = (_VP * len(cts))()
+        _check(h.fhe_bootstrap_n(self.h, ins, len(cts), outs))
+        return [Ciphertext(self, outs[i]) for i in range(len(cts))]
+
     def bootstrap_level(self):
         return lib().fhe_bootstrap_level(self.h)
 

@@ -86,11 +86,12 @@ def _rms(x, g, eps, seed=None, cap=None, tag=None):
     return x * y * g
 
 
-def plain_step(cfg: ModelConfig, w, h, state, seeds=None, cap=None):
+def plain_step(cfg: ModelConfig, w, h, state, seeds=None, cap=None, hidden=False):
     """One recurrent step for a batch of lanes: h (lanes, d) embedded tokens; state is a
     list per layer of (s_prev, u_prev) or None (cold start).  Returns (y, new_state) with
-    y = rmsnorm(h_final, g_out).  seeds: None = exact 1/sqrt (the _fwd_np reference), else
-    the circuit's Newton rsqrt with the per-site seeds."""
+    y = rmsnorm(h_final, g_out) (hidden=True: h_final itself, before the output norm).
+    seeds: None = exact 1/sqrt (the _fwd_np reference), else the circuit's Newton rsqrt with
+    the per-site seeds."""
     new_state = []
     H = h.astype(np.float64)
     for i, L in enumerate(w["layers"]):
@@ -120,6 +121,8 @@ def plain_step(cfg: ModelConfig, w, h, state, seeds=None, cap=None):
         _peak(cap, f"L{i}.f", act * gate)
         H = H + (act * gate) @ L["wv"].T
         new_state.append((s, un))
+    if hidden:
+        return H, new_state
     sd = seeds["ln_out"] if seeds else None
     return _rms(H, w["g_out"], cfg.eps, sd, cap, "ln_out"), new_state
 
@@ -148,16 +151,17 @@ def rsqrt_iters_for(a, b, lo, hi, tol=1e-4, cap=14):
     raise ValueError("Newton rsqrt did not converge")
 
 
-def calibrate_seeds(cfg, w, steps=2, lanes=64, seed=7, tol=1e-4, margin=2.0):
+def calibrate_seeds(cfg, w, steps=2, lanes=64, seed=7, tol=1e-4, margin=2.0, inputs=None):
     """Per-site (a, b, iters) from the ranges of mean(x^2)+eps over a calibration run: the
     linear seed is fitted on [m / margin, M * margin] and the iteration count verified there
     (the reference uses [0.8 m, 1.25 M]; a wider window keeps conversations whose state drifts
-    past the calibration tokens inside the Newton basin, at the cost of about one iteration)."""
+    past the calibration tokens inside the Newton basin, at the cost of about one iteration).
+    The run feeds embeddings of random tokens, or the given input batches (lanes, d) in turn."""
     rng = np.random.default_rng(seed)
     cap, state = {}, None
-    for _ in range(steps):
-        ids = rng.integers(0, cfg.vocab, lanes)
-        _, state = plain_step(cfg, w, w["emb"][ids], state, None, cap)
+    batches = inputs if inputs is not None else [w["emb"][rng.integers(0, cfg.vocab, lanes)] for _ in range(steps)]
+    for x in batches:
+        _, state = plain_step(cfg, w, x, state, None, cap)
     seeds = {}
     for tag, rows in cap.items():
         if tag.startswith("peak:"):

@@ -197,6 +197,9 @@ int fhe_bootstrap_setup(fhe_ctx* cx, double bound, int degree);
 int fhe_bootstrap_setup_r(fhe_ctx* cx, double bound, int degree, int double_angles);
 /* EvalBootstrap (:2544): refresh to level fhe_bootstrap_level() */
 int fhe_bootstrap(fhe_ctx* cx, const fhe_ct* a, fhe_ct** out);
+/* a batch of n ciphertexts, one after another on the context's stream (the batched
+ * EvalBootstrap of baseline config 3, 32 ciphertexts per call); out[i] refreshes in[i] */
+int fhe_bootstrap_n(fhe_ctx* cx, const fhe_ct* const* in, int n, fhe_ct** out);
 int fhe_bootstrap_level(const fhe_ctx* cx);
 /* diagnostics: the bootstrap pipeline stopped after stage `upto` (1 ModRaise, 2 CoeffToSlot,
  * 3 EvalMod, 4 complete) */
