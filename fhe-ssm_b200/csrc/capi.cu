@@ -181,6 +181,13 @@ int fhe_keygen_rotations(fhe_ctx* cx, const int32_t* steps, int n, int conj) {
         fhe::keygen_rotations(cx->cx, v.data(), n, conj != 0);
     });
 }
+int fhe_keygen_auto(fhe_ctx* cx, const uint64_t* idx, int n) {
+    return guard([&] {
+        REQUIRE(cx && (idx || n == 0), "null argument");
+        bind(cx);
+        fhe::keygen_auto(cx->cx, idx, n);
+    });
+}
 static fhe::SwitchKey* find_key(fhe::Context& c, uint64_t which) {
     if (which == 0) {
         if (!c.rlk) throw fhe::Error("no relinearisation key", FHE_ERR_KEY);
@@ -614,8 +621,7 @@ int fhe_model_keygen(fhe_model* m) {
     return guard([&] {
         REQUIRE(m, "null argument");
         bind(m->owner);
-        std::vector<int> r = fhe::matvec_rotations(m->m->cfg.D, m->m->cfg.b1);
-        for (int k = 1; k < m->m->cfg.D; k <<= 1) { r.push_back(k); r.push_back(-k); }
+        std::vector<int> r = fhe::model_rotation_steps(m->m->cfg);
         fhe::keygen_rotations(m->owner->cx, r.data(), (int)r.size(), true);
     });
 }

@@ -928,34 +928,36 @@ static std::unique_ptr<SwitchKey> gen_switch_key(Context& cx, const uint64_t* s_
         pm[i] = v;
     }
     DevBuf dpm = limb_consts(cx, pm, false);
-    std::vector<uint64_t> a((size_t)nm * N);
-    std::vector<int64_t> e(N);
-    DevBuf de((size_t)nm * N, cx.stream);
+    std::memcpy(key->seed, key_seed, 32);
+    key->seeded = true;
+    // every digit's a-half on the device, straight from the seed (the seeded expander, tag SKEY)
+    expand_uniform_dev(cx, key_seed, 0, cx.dnum_top, 0, nm, kTagSKEY, key->buf.p + (size_t)nm * N,
+                       (long long)2 * nm * N);
+    // the digits' Gaussian errors (host), uploaded together
+    std::vector<int64_t> e((size_t)cx.dnum_top * N);
+    for (int j = 0; j < cx.dnum_top; j++)
+        sample_gauss(key_seed, (uint32_t)j, 0, cx.prm.sigma, e.data() + (size_t)j * N, N);
+    DevBuf de((size_t)nm * N, cx.stream), d((size_t)cx.dnum_top * N, cx.stream);
+    CUDA_CHECK(cudaMemcpyAsync(d.p, e.data(), e.size() * 8, cudaMemcpyHostToDevice, cx.stream));
     for (int j = 0; j < cx.dnum_top; j++) {
-#pragma omp parallel for schedule(dynamic)
-        for (int m = 0; m < nm; m++)
-            sample_uniform(key_seed, (uint32_t)j, (uint32_t)m, kTagSKEY, cx.mods[m], a.data() + (size_t)m * N, N);
-        sample_gauss(key_seed, (uint32_t)j, 0, cx.prm.sigma, e.data(), N);
         uint64_t* kb = key->buf.p + ((size_t)j * 2 + 0) * nm * N;
         uint64_t* ka = key->buf.p + ((size_t)j * 2 + 1) * nm * N;
-        CUDA_CHECK(cudaMemcpyAsync(ka, a.data(), a.size() * 8, cudaMemcpyHostToDevice, cx.stream));
         // e in eval form over every modulus: broadcast the single polynomial to all limbs
         LimbMap mp = fullmap(cx, de.p);
         mp.poly_stride = 0;
-        {
-            DevBuf d((size_t)N, cx.stream);
-            CUDA_CHECK(cudaMemcpyAsync(d.p, e.data(), (size_t)N * 8, cudaMemcpyHostToDevice, cx.stream));
-            k_signed_to_limbs<<<dim3(N / 256, nm), 256, 0, cx.stream>>>((const int64_t*)d.p, de.p, mp, cx.logN);
-            CUDA_CHECK(cudaGetLastError());
-            ntt(cx, fullmap(cx, de.p), 1, false, cx.stream);
-            const int lo = j * cx.alpha, hi = std::min(lo + cx.alpha, cx.L);
-            k_keyb<<<dim3(N / 256, nm), 256, 0, cx.stream>>>(ka, de.p, s_key, s_src, dpm.p, kb, lo, hi, cx.logN);
-            CUDA_CHECK(cudaGetLastError());
-            CUDA_CHECK(cudaStreamSynchronize(cx.stream));   // a, e are reused host buffers
-        }
+        k_signed_to_limbs<<<dim3(N / 256, nm), 256, 0, cx.stream>>>((const int64_t*)d.p + (size_t)j * N, de.p, mp,
+                                                                    cx.logN);
+        CUDA_CHECK(cudaGetLastError());
+        ntt(cx, fullmap(cx, de.p), 1, false, cx.stream);
+        const int lo = j * cx.alpha, hi = std::min(lo + cx.alpha, cx.L);
+        k_keyb<<<dim3(N / 256, nm), 256, 0, cx.stream>>>(ka, de.p, s_key, s_src, dpm.p, kb, lo, hi, cx.logN);
+        CUDA_CHECK(cudaGetLastError());
+        cx.launches += 2;
     }
     k_mont<<<dim3(N / 256, cx.dnum_top * 2 * nm), 256, 0, cx.stream>>>(key->buf.p, nm, 1, cx.logN);
     CUDA_CHECK(cudaGetLastError());
+    CUDA_CHECK(cudaStreamSynchronize(cx.stream));   // e is a host temporary
+    cx.launches++;
     return key;
 }
 
@@ -976,12 +978,7 @@ void keygen(Context& cx, const uint8_t seed[32]) {
     // public key over the L Q-limbs
     cx.pk = DevBuf((size_t)2 * cx.L * N, cx.stream);
     {
-        std::vector<uint64_t> a((size_t)cx.L * N);
-#pragma omp parallel for
-        for (int m = 0; m < cx.L; m++)
-            sample_uniform(p_seed, 0, (uint32_t)m, kTagPKEY, cx.mods[m], a.data() + (size_t)m * N, N);
-        CUDA_CHECK(cudaMemcpyAsync(cx.pk.p + (size_t)cx.L * N, a.data(), a.size() * 8, cudaMemcpyHostToDevice,
-                                   cx.stream));
+        expand_uniform_dev(cx, p_seed, 0, 1, 0, cx.L, kTagPKEY, cx.pk.p + (size_t)cx.L * N, 0);
         std::vector<int64_t> e(N);
         sample_gauss(p_seed, 0xFFFFFFFFu, 0, cx.prm.sigma, e.data(), N);
         DevBuf de((size_t)cx.L * N, cx.stream);
@@ -1020,13 +1017,26 @@ static void gen_auto_key(Context& cx, uint64_t k) {
     CUDA_CHECK(cudaStreamSynchronize(cx.stream));
 }
 
-void keygen_rotations(Context& cx, const int* rs, int n, bool conj) {
-    if (!cx.sk.p) throw Error("keygen_rotations: no secret key", -5);
+void keygen_auto(Context& cx, const uint64_t* ks, int n) {
     for (int i = 0; i < n; i++) {
-        const uint64_t k = rot_index(cx, rs[i]);
-        if (k != 1) gen_auto_key(cx, k);
+        const uint64_t k = ks[i];
+        if (!(k & 1) || k >= 2ull * cx.N) throw Error("keygen_auto: automorphism index must be odd and below 2N", -1);
+        if (k == 1 || cx.rot_keys.count(k)) continue;
+        if (!cx.sk.p) throw Error("keygen_auto: no secret key", -5);
+        gen_auto_key(cx, k);
     }
-    if (conj) gen_auto_key(cx, 2ull * cx.N - 1);
+}
+
+void keygen_rotations(Context& cx, const int* rs, int n, bool conj) {
+    // keys already held (generated earlier, or loaded from part files) are kept; only a missing
+    // key needs the secret
+    auto need = [&](uint64_t k) {
+        if (k == 1 || cx.rot_keys.count(k)) return;
+        if (!cx.sk.p) throw Error("keygen_rotations: no key for automorphism " + std::to_string(k) + " and no secret", -5);
+        gen_auto_key(cx, k);
+    };
+    for (int i = 0; i < n; i++) need(rot_index(cx, rs[i]));
+    if (conj) need(2ull * cx.N - 1);
 }
 
 Ciphertext encrypt(Context& cx, const Plaintext& pt) {

@@ -102,6 +102,8 @@ struct Plaintext {
 struct SwitchKey {
     DevBuf buf;            // [dnum_top][2][L+K][N], Montgomery form
     uint64_t index = 0;    // automorphism index (0 for relinearisation)
+    uint8_t seed[32] = {0};   // the a-halves' expander seed (seeded keys: part files carry it)
+    bool seeded = false;
     DevBuf fwd;            // rotation keys: the same key with the automorphism applied (the key
                            // of the rotate-then-switch order), built on first use by rotate_sum
 };
@@ -214,7 +216,9 @@ struct ProfScope {
     }
 };
 
-// ---- low-level launches (ntt.cu, kernels.cu) ---------------------------------------------
+// ---- low-level launches (ntt.cu, kernels.cu, keys.cu) --------------------------------------
+void expand_uniform_dev(Context& cx, const uint8_t seed[32], int digit0, int ndigit, int limb0, int nlimb,
+                        uint32_t tag, uint64_t* out, long long digit_stride);
 void ntt(const Context& cx, const LimbMap& mp, int npoly, bool inv, cudaStream_t st);
 
 // ---- operations (engine.cu) ---------------------------------------------------------------
@@ -257,6 +261,7 @@ void decode(Context& cx, const Plaintext& pt, std::complex<double>* z);
 // client-side crypto (keys held by the context)
 void keygen(Context& cx, const uint8_t seed[32]);
 void keygen_rotations(Context& cx, const int* rs, int n, bool conj);
+void keygen_auto(Context& cx, const uint64_t* ks, int n);   // keys for automorphism indices
 uint64_t rot_index(const Context& cx, int r);
 Ciphertext encrypt(Context& cx, const Plaintext& pt);
 Plaintext decrypt(Context& cx, const Ciphertext& ct);

@@ -319,6 +319,14 @@ struct Model {
     }
 };
 
+// the rotation amounts of a step: the BSGS matvec's babies and giants and the rmsnorm's block
+// sums (+2^k up, -2^k back down); the conjugation (complex split) comes on top
+std::vector<int> model_rotation_steps(const ModelCfg& cfg) {
+    std::vector<int> r = matvec_rotations(cfg.D, cfg.b1);
+    for (int k = 1; k < cfg.D; k <<= 1) { r.push_back(k); r.push_back(-k); }
+    return r;
+}
+
 // ------------------------------------------------------------------ construction API ----
 std::shared_ptr<Model> model_create(Context& cx, const ModelCfg& cfg) {
     if (cfg.d < 1 || cfg.D < cfg.d || (cfg.D & (cfg.D - 1)) || (cx.N / 2) % cfg.D)

@@ -196,6 +196,44 @@ def seed32(seed) -> bytes:
     return int(seed).to_bytes(8, "little") + bytes(24)
 
 
+class PartLayout(C.Structure):
+    """fhe_part_layout: the header fields of a seeded key part file (FSSMSKY1)."""
+    _fields_ = [(k, C.c_uint32) for k in ("version", "expander", "N", "sizeQ", "sizeP", "numPartQ", "numPerPartQ",
+                                          "count")]
+
+
+def part_header(path):
+    """Header of a seeded key part file (no GPU needed): (layout dict, moduli, key tag)."""
+    h = lib()
+    h.fhe_part_header.restype = C.c_int
+    h.fhe_part_header.argtypes = [C.c_char_p, C.POINTER(PartLayout), _U64P, C.c_int, C.c_char_p, C.c_int]
+    lay = PartLayout()
+    mods = np.zeros(256, dtype=np.uint64)
+    tag = C.create_string_buffer(4097)
+    _check(h.fhe_part_header(path.encode(), C.byref(lay), mods.ctypes.data_as(_U64P), 256, tag, len(tag)))
+    d = {k: getattr(lay, k) for k, _ in PartLayout._fields_}
+    return d, mods[:d["sizeQ"] + d["sizeP"]].copy(), tag.value.decode()
+
+
+def write_part_words(path, layout, moduli, tag, indices, seeds, b):
+    """A seeded key part file from caller-held words (no GPU needed): layout dict (N, sizeQ, sizeP,
+    numPartQ, numPerPartQ), indices (count,), seeds (count, 32) uint8, b (count, numPartQ,
+    sizeQ + sizeP, N) uint64."""
+    h = lib()
+    h.fhe_part_write_words.restype = C.c_int
+    h.fhe_part_write_words.argtypes = [C.c_char_p, C.POINTER(PartLayout), _U64P, C.c_char_p,
+                                       C.POINTER(C.c_uint32), C.POINTER(C.c_uint8), _U64P]
+    idx = np.ascontiguousarray(indices, dtype=np.uint32)
+    sd = np.ascontiguousarray(seeds, dtype=np.uint8)
+    bw = np.ascontiguousarray(b, dtype=np.uint64)
+    mods = np.ascontiguousarray(moduli, dtype=np.uint64)
+    lay = PartLayout(1, 1, layout["N"], layout["sizeQ"], layout["sizeP"], layout["numPartQ"], layout["numPerPartQ"],
+                     len(idx))
+    _check(h.fhe_part_write_words(path.encode(), C.byref(lay), mods.ctypes.data_as(_U64P), tag.encode(),
+                                  idx.ctypes.data_as(C.POINTER(C.c_uint32)), sd.ctypes.data_as(C.POINTER(C.c_uint8)),
+                                  bw.ctypes.data_as(_U64P)))
+
+
 class CryptoContext:
     """One engine context (one GPU).  Names follow the OpenFHE calls of the reference."""
 
@@ -283,6 +321,14 @@ class CryptoContext:
     def EvalRotateKeyGen(self, steps, conj=False):
         arr = (C.c_int32 * len(steps))(*steps)
         _check(lib().fhe_keygen_rotations(self.h, arr, len(steps), 1 if conj else 0))
+
+    def keygen_auto(self, indices):
+        """Keys for automorphism indices (the autoIndices of a rotation-index contract)."""
+        h = lib()
+        h.fhe_keygen_auto.restype = C.c_int
+        h.fhe_keygen_auto.argtypes = [_VP, _U64P, C.c_int]
+        w = np.ascontiguousarray(indices, dtype=np.uint64)
+        _check(h.fhe_keygen_auto(self.h, w.ctypes.data_as(_U64P), len(w)))
 
     def key_words(self, which=0):
         out = np.empty((self.dnum, 2, self.L + self.K, self.N), dtype=np.uint64)
@@ -503,6 +549,25 @@ class CryptoContext:
         h = _VP()
         _check(lib().fhe_ct_import(self.h, p, level, scale, C.byref(h)))
         return Ciphertext(self, h)
+
+    def save_keys_part(self, path, which, tag="fhe-ssm"):
+        """Seeded part file (FSSMSKY1) of the keys `which` (0 = relinearisation, else automorphism
+        indices), as the reference's writeSeededPart writes it."""
+        h = lib()
+        h.fhe_keys_save_part.restype = C.c_int
+        h.fhe_keys_save_part.argtypes = [_VP, C.c_char_p, _U64P, C.c_int, C.c_char_p]
+        w = np.ascontiguousarray(which, dtype=np.uint64)
+        _check(h.fhe_keys_save_part(self.h, path.encode(), w.ctypes.data_as(_U64P), len(w), tag.encode()))
+
+    def load_keys_part(self, path):
+        """Keys of a seeded part file (b from the file, a expanded from the seeds on the device);
+        returns how many were added."""
+        h = lib()
+        h.fhe_keys_load_part.restype = C.c_int
+        h.fhe_keys_load_part.argtypes = [_VP, C.c_char_p, C.POINTER(C.c_int)]
+        n = C.c_int()
+        _check(h.fhe_keys_load_part(self.h, path.encode(), C.byref(n)))
+        return n.value
 
     def pt_from_words(self, words, level, scale=1.0):
         w, p = _u64(words)

@@ -291,6 +291,16 @@ class EncryptedModel:
         _check(lib().fhe_model_stats(self.h, C.byref(b), C.byref(s)))
         return {"bootstraps": b.value, "steps": s.value}
 
+    def rot_contract(self):
+        """The rotation-index contract ("fhe-ssm-rot-indices-v1") a client keygen must satisfy."""
+        import json
+        h = lib()
+        h.fhe_model_rot_contract.restype = C.c_int
+        h.fhe_model_rot_contract.argtypes = [_VP, C.c_char_p, C.c_int]
+        buf = C.create_string_buffer(1 << 16)
+        _check(h.fhe_model_rot_contract(self.h, buf, len(buf)))
+        return json.loads(buf.value.decode())
+
     REFRESH_SITES = ("norm.x", "norm.ms", "norm.y", "norm.m", "norm.tail", "shift.xn", "shift.up", "u", "s.prev",
                      "s.new", "z", "g", "v", "f")
 

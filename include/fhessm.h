@@ -100,6 +100,9 @@ int fhe_prof_collect(fhe_ctx* cx, char* buf, int cap);
 int fhe_keygen(fhe_ctx* cx, const uint8_t seed[32]);
 /* replaces EvalRotateKeyGen(rots) (:1299-1336); conj != 0 adds the conjugation key */
 int fhe_keygen_rotations(fhe_ctx* cx, const int32_t* steps, int n, int conj);
+/* switching keys for the automorphism indices idx[0..n) (odd, < 2N; 1 is skipped): the client
+ * minting the index list of a rotation-index contract (fhe_model_rot_contract's autoIndices) */
+int fhe_keygen_auto(fhe_ctx* cx, const uint64_t* idx, int n);
 /* raw key material (canonical residues), for parity checks and key files:
  * which = 0: relinearisation key; otherwise the automorphism index (5^r mod 2N, or 2N-1). */
 int fhe_key_export(fhe_ctx* cx, uint64_t which, uint64_t* words);
@@ -282,6 +285,34 @@ int fhe_serve_files(const char* dir, int timeout_ms, int max_requests, fhe_serve
                     int* served);
 /* the serve loop over fhe_server_step of model m (one pack per request) */
 int fhe_serve_model(fhe_model* m, const char* dir, int timeout_ms, int max_requests, int* served);
+
+/* ---- key material: seeded part files and the rotation-index contract --------------------
+ * Part files follow the reference's FSSMSKY1 format (hpc_gpu_port/seeded_keys.hpp:44-52; written
+ * by writeSeededPart :327-349, read by readSeededPartHeader :354-370 and expandSeededKeys
+ * :382-420): a header with the ring, chain and digit layout, then per key its automorphism index,
+ * the 32-byte seed of its a-halves and its b-halves [numPartQ][sizeQ + sizeP][N] in evaluation
+ * form.  Index 0 carries the relinearisation key (this engine's extension).  The a-halves are
+ * re-expanded from the seeds on the device when a file is loaded. */
+typedef struct {
+    uint32_t version, expander, N, sizeQ, sizeP, numPartQ, numPerPartQ, count;
+} fhe_part_layout;
+/* header of a part file (no GPU needed): moduli[sizeQ + sizeP] and the key tag when non-NULL */
+int fhe_part_header(const char* path, fhe_part_layout* lay, uint64_t* moduli, int moduli_cap, char* tag, int tag_cap);
+/* write a part file from caller-held words (no GPU needed): lay->count records of indices[k],
+ * seeds[k][32], b[k][numPartQ][sizeQ + sizeP][N] */
+int fhe_part_write_words(const char* path, const fhe_part_layout* lay, const uint64_t* moduli, const char* tag,
+                         const uint32_t* indices, const uint8_t* seeds, const uint64_t* b);
+/* write the context's keys `which[0..n)` (0 = relinearisation, else automorphism indices); every one
+ * must have been generated from a seed in this context (replaces writeSeededPart) */
+int fhe_keys_save_part(fhe_ctx* cx, const char* path, const uint64_t* which, int n, const char* tag);
+/* load a part file minted for this context's chain (else FHE_ERR_ARG, as the reference's loader
+ * refuses): b words from the file, a-halves expanded from the seeds on the device; keys the context
+ * already holds are kept; *inserted = keys added (replaces expandSeededKeys + LoadContext) */
+int fhe_keys_load_part(fhe_ctx* cx, const char* path, int* inserted);
+/* the rotation-index contract of a model ("fhe-ssm-rot-indices-v1", the --dump-rot-indices JSON of
+ * gpu_real_model.cu:1337-1394): rotationAmounts, bootstrapSteps, and autoIndices = every
+ * automorphism index the server will look up (5^s mod 2N, and 2N - 1) */
+int fhe_model_rot_contract(const fhe_model* m, char* buf, int cap);
 
 /* ---- raw words (parity tests, serialisation) -------------------------------------------- */
 int fhe_ct_import(fhe_ctx* cx, const uint64_t* words, int level, double scale, fhe_ct** out);
