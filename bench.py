@@ -575,6 +575,93 @@ def run_matvec(args, ws, rank, local):
             "kernels": kernel_table(prof)}), flush=True)
 
 
+METRIC_KSDIST = "hybrid key switches/s of one ciphertext, limb-partitioned over N B200 (N=2^16, L=20)"
+
+
+def run_ksdist(args, ws, rank, local):
+    """Single-pack latency (config 5's multi-GPU case): one ciphertext's hybrid key switch at
+    N = 2^16, L = 20 (dnum 5), its limbs split over the ranks (fhe_keyswitch_dist: NCCL all-gathers
+    of d's coefficient limbs before ModUp and of the special limbs before ModDown).  Strong scaling:
+    the same key switch on every N; a step is one key switch; the device time is the slowest rank's."""
+    import torch
+
+    import fhessm
+    from fhessm import dist as fd
+    import torch.distributed as tdist
+    cx = fhessm.CryptoContext(device=local, logN=16, L=20, K=4, alpha=4, hw=192)
+    cx.KeyGen(seed=1)                                   # the same keys on every rank
+    if ws > 1:
+        obj = [fd.unique_id() if rank == 0 else None]
+        tdist.broadcast_object_list(obj, src=0)
+        uid = obj[0]
+    else:
+        uid = fd.unique_id()
+    fd.init(cx, ws, rank, uid)
+    level, nl = 0, 20
+    rng = np.random.default_rng(5)
+    d = np.stack([rng.integers(0, int(cx.moduli[i]), cx.N, dtype=np.uint64) for i in range(nl)])
+    lo, cnt, _ = fd.limb_block(nl, ws, rank)
+    dev = torch.from_numpy(np.ascontiguousarray(d[lo:lo + cnt]).view(np.int64)).to(f"cuda:{local}")
+    o0 = torch.zeros((max(cnt, 1), cx.N), dtype=torch.int64, device=f"cuda:{local}")
+    o1 = torch.zeros_like(o0)
+    stream = torch.cuda.ExternalStream(cx.stream_ptr(), device=local)
+
+    def step():
+        fd.keyswitch(cx, 0, dev.data_ptr(), level, o0.data_ptr(), o1.data_ptr())
+
+    for _ in range(args.warmup):
+        step()
+    cx.sync()
+    barrier(ws)
+    clk = ClockSampler(local)
+    clk.start()
+    l0 = cx.launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(ws)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    cx.sync()
+    torch.cuda.synchronize()
+    barrier(ws)
+    clocks = clk.stop()
+    ms_max = max_over_ranks(e0.elapsed_time(e1), ws)
+    value = args.steps / (ms_max / 1000.0)
+    launches = cx.launches() - l0
+    # correctness of the timed output against the single-GPU key switch of the whole ciphertext
+    e_0, _ = cx.keyswitch_raw(d, level, cx.key_words(0))
+    ok = bool((o0.cpu().numpy().view(np.uint64)[:cnt] == e_0[lo:lo + cnt]).all())
+    # end to end: the rank's limbs from pinned host memory, the key switch, its result limbs back
+    host_in = torch.from_numpy(np.ascontiguousarray(d[lo:lo + cnt]).view(np.int64)).pin_memory()
+    host_out = torch.empty((2, max(cnt, 1), cx.N), dtype=torch.int64).pin_memory()
+    barrier(ws)
+    t0 = time.time()
+    for _ in range(args.steps):
+        dev.copy_(host_in, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        step()
+        cx.sync()
+        host_out[0].copy_(o0)
+        host_out[1].copy_(o1)
+    e2e_s = max_over_ranks(time.time() - t0, ws)
+    if not ok:
+        raise SystemExit(f"ksdist: rank {rank}'s limbs differ from the single-GPU key switch")
+    if rank == 0:
+        bytes_ks = 8.0 * cx.N * (2 * nl + 5 * 2 * (nl + 4) + 3 * 5 * (nl + 4) + 2 * nl)
+        print(json.dumps({
+            "metric": METRIC_KSDIST, "value": value, "unit": "key switches/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "u64 (RNS residues)", "data": "synthetic",
+            "config": {"workload": "one ciphertext's hybrid key switch (relinearisation key), N=2^16, L=20, K=4, "
+                                   "dnum=5, limbs split over the ranks", "parallelism": f"limb-partitioned x{ws}",
+                       "l2": "key 120 MiB per rank > L2 share"},
+            "gpu_launches": launches, "clocks": clocks, "bit_exact_vs_single_gpu": ok,
+            "e2e": {"value": args.steps / e2e_s, "unit": "key switches/s",
+                    "h2d_bytes_per_step": int(host_in.numel() * 8), "d2h_bytes_per_step": int(2 * cnt * cx.N * 8)},
+            "algorithmic_bytes_per_ks": bytes_ks, "roofline": None, "cpu_baseline": None}), flush=True)
+
+
 def run_reference(args):
     """The reference arm: the CPU path of the same workload on the host cores.  OpenFHE (the
     reference's arithmetic library) cannot be built here, so the C oracle (a restatement of the
@@ -655,7 +742,7 @@ def main():
     ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
-    ap.add_argument("--workload", default="405m", choices=["405m", "hmult", "matvec", "ntt"])
+    ap.add_argument("--workload", default="405m", choices=["405m", "hmult", "matvec", "ntt", "ksdist"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=64, help="hmult: ciphertext pairs per GPU per step")
     ap.add_argument("--limbs", type=int, default=1024, help="ntt: limb-polynomials per transform")
@@ -672,6 +759,8 @@ def main():
         run_matvec(args, ws, rank, local)
     elif args.workload == "ntt":
         run_ntt(args, ws, rank, local)
+    elif args.workload == "ksdist":
+        run_ksdist(args, ws, rank, local)
     else:
         run_hmult(args, ws, rank, local)
     if ws > 1:

@@ -162,6 +162,7 @@ struct Context {
     std::unique_ptr<Plaintext> pt_i;         // NTT of X^{N/2}: multiplication by i
     std::map<uint64_t, std::shared_ptr<Plaintext>> ptcache;   // encode_cached: (content, level, scale)
     std::shared_ptr<void> boot;              // bootstrapping precomputation (bootstrap.cu)
+    std::shared_ptr<void> dist;              // limb-partitioned group: NCCL communicator and stream (dist.cu)
 
     explicit Context(const Params& p);
     ~Context();

@@ -327,6 +327,27 @@ int fhe_ntt_host(fhe_ctx* cx, uint64_t* words, int n, const int* mod_idx, int in
 int fhe_keyswitch_host(fhe_ctx* cx, const uint64_t* d, int level, const uint64_t* key, uint64_t* out0,
                        uint64_t* out1);
 
+/* ---- limb-partitioned key switching over several GPUs (single-pack latency) -------------
+ * Replaces the reference's multi-device context (gpu_real_model.cu:847-884 --devices; FIDESlib's
+ * limb placement :995-997 and SetDevices :1158-1161).  Rank g of `world` owns a block of the Q
+ * limbs and of the K special limbs of every polynomial: per = ceil(n / world) limbs, rank g the
+ * limbs [g per, (g + 1) per) that exist (fhe_dist_limbs gives its Q block).  A key switch
+ * all-gathers the ranks' Q limbs of d in coefficient form before ModUp and their special limbs of
+ * the inner products before ModDown (NCCL, on the context's own communication stream); all other
+ * work stays on the rank's limbs, and every rank's limbs equal the single-GPU key switch's. */
+/* an NCCL unique id (128 bytes): rank 0 makes it and shares it with the other ranks */
+int fhe_dist_unique_id(uint8_t* out);
+/* join a group of `world` ranks (one context per GPU, same chain and keys) */
+int fhe_dist_init(fhe_ctx* cx, int world, int rank, const uint8_t* id);
+/* this rank's block of the L - level Q limbs: *first, *count (count may be 0) */
+int fhe_dist_limbs(const fhe_ctx* cx, int level, int* first, int* count);
+/* key switch with the resident key `which` (0 = relinearisation, else an automorphism index):
+ * d_own = the rank's Q limbs of d (eval form, device memory, [count][N]) -> out0, out1, the rank's
+ * limbs of the result (device memory).  Every rank of the group must call it (a collective),
+ * enqueued on the context's stream. */
+int fhe_keyswitch_dist(fhe_ctx* cx, uint64_t which, const uint64_t* d_own, int level, uint64_t* out0,
+                       uint64_t* out1);
+
 /* ---- key switching without device allocation -------------------------------------------
  * No counterpart in the reference (its key switch allocates through OpenFHE / FIDESlib).
  * For callers that must not allocate device memory during a pass: a server that has given

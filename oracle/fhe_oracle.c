@@ -401,6 +401,109 @@ void oc_keyswitch(const oc_ctx* c, const uint64_t* d, int nl, const uint64_t* ke
     free(ext); free(i0); free(i1);
 }
 
+/* ====================== limb-partitioned key switching (one rank's share) ============ */
+/* A rank owns Q limbs [qlo, qlo + nqo) and P limbs [plo, plo + npo); its "own ext limbs" are those
+ * Q limbs then those P limbs.  After the first exchange every rank holds all nl limbs of d in
+ * coefficient form (dcoef); after the second, the np P limbs of the inner product (both
+ * polynomials) in coefficient form.  These three pieces are the rank-local arithmetic. */
+static int own_ext_mod(const oc_ctx* c, int nl, int qlo, int nqo, int plo, int o) {
+    return o < nqo ? qlo + o : ext_mod(c, nl, nl + plo + (o - nqo));
+}
+static int own_ext_index(int nl, int qlo, int nqo, int plo, int o) { return o < nqo ? qlo + o : nl + plo + (o - nqo); }
+
+void oc_ks_part_ext(const oc_ctx* c, const uint64_t* dcoef, int nl, int qlo, int nqo, int plo, int npo,
+                    uint64_t* ext_own) {
+    const int N = c->N, alpha = c->alpha, dnum = ceil_div(nl, alpha), no = nqo + npo;
+    for (int j = 0; j < dnum; j++) {
+        const int lo = j * alpha, hi = (lo + alpha < nl) ? lo + alpha : nl, sz = hi - lo;
+        for (int o = 0; o < no; o++) {
+            const int e = own_ext_index(nl, qlo, nqo, plo, o), m = own_ext_mod(c, nl, qlo, nqo, plo, o);
+            const uint64_t pm = c->mod[m];
+            uint64_t* dst = ext_own + ((size_t)j * no + o) * N;
+            if (e >= lo && e < hi) {   /* the digit's own limb: d itself, back in eval form */
+                memcpy(dst, dcoef + (size_t)e * N, sizeof(uint64_t) * N);
+                oc_ntt(c, dst, m);
+                continue;
+            }
+            uint64_t qhinv[64], qh[64];
+            for (int a = 0; a < sz; a++) {
+                const uint64_t qi = c->mod[lo + a];
+                uint64_t v = 1, w = 1;
+                for (int b = 0; b < sz; b++)
+                    if (b != a) {
+                        v = oc_mulmod(v, c->mod[lo + b] % qi, qi);
+                        w = oc_mulmod(w, c->mod[lo + b] % pm, pm);
+                    }
+                qhinv[a] = oc_invmod(v, qi);
+                qh[a] = w;
+            }
+            for (int k = 0; k < N; k++) {
+                u128 acc = 0;
+                for (int a = 0; a < sz; a++)
+                    acc += (u128)oc_mulmod(dcoef[(size_t)(lo + a) * N + k], qhinv[a], c->mod[lo + a]) * qh[a];
+                dst[k] = (uint64_t)(acc % pm);
+            }
+            oc_ntt(c, dst, m);
+        }
+    }
+}
+
+void oc_ks_part_inner(const oc_ctx* c, const uint64_t* ext_own, int nl, const uint64_t* key, int qlo, int nqo,
+                      int plo, int npo, uint64_t* out0, uint64_t* out1) {
+    const int N = c->N, nk = c->nq + c->np, dnum = ceil_div(nl, c->alpha), no = nqo + npo;
+    for (int o = 0; o < no; o++) {
+        const int m = own_ext_mod(c, nl, qlo, nqo, plo, o);
+        const uint64_t q = c->mod[m];
+        for (int x = 0; x < N; x++) {
+            u128 a0 = 0, a1 = 0;
+            for (int j = 0; j < dnum; j++) {
+                const uint64_t d = ext_own[((size_t)j * no + o) * N + x];
+                a0 = (a0 + (u128)d * key[(((size_t)j * 2 + 0) * nk + m) * N + x]) % q;
+                a1 = (a1 + (u128)d * key[(((size_t)j * 2 + 1) * nk + m) * N + x]) % q;
+            }
+            out0[(size_t)o * N + x] = (uint64_t)a0;
+            out1[(size_t)o * N + x] = (uint64_t)a1;
+        }
+    }
+}
+
+/* own Q limbs of one inner-product polynomial (eval) and all its np P limbs (coefficient form,
+ * NOT yet multiplied by phat^-1) -> own Q limbs of the key-switch output */
+void oc_ks_part_moddown(const oc_ctx* c, const uint64_t* in_own, const uint64_t* pcoef, int nl, int qlo, int nqo,
+                        uint64_t* out_own) {
+    const int N = c->N, np = c->np;
+    uint64_t* t = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)np * N);
+    uint64_t* tmp = (uint64_t*)malloc(sizeof(uint64_t) * N);
+    for (int k = 0; k < np; k++) {
+        const uint64_t pk = c->mod[c->nq + k];
+        uint64_t phat = 1;
+        for (int b = 0; b < np; b++) if (b != k) phat = oc_mulmod(phat, c->mod[c->nq + b] % pk, pk);
+        const uint64_t phinv = oc_invmod(phat, pk);
+        for (int x = 0; x < N; x++) t[(size_t)k * N + x] = oc_mulmod(pcoef[(size_t)k * N + x], phinv, pk);
+    }
+    for (int o = 0; o < nqo; o++) {
+        const int i = qlo + o;
+        const uint64_t qi = c->mod[i];
+        uint64_t ph[64], P = 1;
+        for (int k = 0; k < np; k++) {
+            uint64_t v = 1;
+            for (int b = 0; b < np; b++) if (b != k) v = oc_mulmod(v, c->mod[c->nq + b] % qi, qi);
+            ph[k] = v;
+            P = oc_mulmod(P, c->mod[c->nq + k] % qi, qi);
+        }
+        const uint64_t Pinv = oc_invmod(P, qi);
+        for (int x = 0; x < N; x++) {
+            u128 acc = 0;
+            for (int k = 0; k < np; k++) acc += (u128)t[(size_t)k * N + x] * ph[k];
+            tmp[x] = (uint64_t)(acc % qi);
+        }
+        oc_ntt(c, tmp, i);
+        for (int x = 0; x < N; x++)
+            out_own[(size_t)o * N + x] = oc_mulmod(subm(in_own[(size_t)o * N + x], tmp[x], qi), Pinv, qi);
+    }
+    free(t); free(tmp);
+}
+
 /* ================================ ciphertext ops =================================== */
 void oc_ct_add(const oc_ctx* c, const uint64_t* a, const uint64_t* b, int nl, uint64_t* out) {
     const int N = c->N;

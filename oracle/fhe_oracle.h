@@ -66,6 +66,19 @@ void oc_key_inner(const oc_ctx* c, const uint64_t* ext, int nl, const uint64_t* 
 /* full key switch of d (nl limbs, eval) -> (out0, out1) (nl limbs each) */
 void oc_keyswitch(const oc_ctx* c, const uint64_t* d, int nl, const uint64_t* key, uint64_t* out0, uint64_t* out1);
 
+/* ---- limb-partitioned key switching: one rank's share ------------------------------
+ * The rank owns Q limbs [qlo, qlo+nqo) and P limbs [plo, plo+npo) ("own ext limbs": those Q limbs
+ * then those P limbs).  ext: dcoef = all nl Q limbs of d in coefficient form (after the first
+ * all-gather) -> ext_own [dnum][nqo+npo][N] eval.  inner: -> out0/out1 [nqo+npo][N].  moddown:
+ * in_own = own Q limbs of one inner-product polynomial (eval), pcoef = its np P limbs in
+ * coefficient form (after the second all-gather) -> out_own [nqo][N]. */
+void oc_ks_part_ext(const oc_ctx* c, const uint64_t* dcoef, int nl, int qlo, int nqo, int plo, int npo,
+                    uint64_t* ext_own);
+void oc_ks_part_inner(const oc_ctx* c, const uint64_t* ext_own, int nl, const uint64_t* key, int qlo, int nqo,
+                      int plo, int npo, uint64_t* out0, uint64_t* out1);
+void oc_ks_part_moddown(const oc_ctx* c, const uint64_t* in_own, const uint64_t* pcoef, int nl, int qlo, int nqo,
+                        uint64_t* out_own);
+
 /* ---- ciphertext ops; a ct with nl limbs is [2][nl][N] ---------------------------- */
 void oc_ct_add(const oc_ctx* c, const uint64_t* a, const uint64_t* b, int nl, uint64_t* out);
 void oc_ct_mul_pt(const oc_ctx* c, const uint64_t* a, const uint64_t* pt, int nl, uint64_t* out);

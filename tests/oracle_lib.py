@@ -47,6 +47,9 @@ def load():
         "oc_moddown": (None, [C.c_void_p, U64P, C.c_int, U64P]),
         "oc_key_inner": (None, [C.c_void_p, U64P, C.c_int, U64P, U64P, U64P]),
         "oc_keyswitch": (None, [C.c_void_p, U64P, C.c_int, U64P, U64P, U64P]),
+        "oc_ks_part_ext": (None, [C.c_void_p, U64P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, U64P]),
+        "oc_ks_part_inner": (None, [C.c_void_p, U64P, C.c_int, U64P, C.c_int, C.c_int, C.c_int, C.c_int, U64P, U64P]),
+        "oc_ks_part_moddown": (None, [C.c_void_p, U64P, U64P, C.c_int, C.c_int, C.c_int, U64P]),
         "oc_ct_add": (None, [C.c_void_p, U64P, U64P, C.c_int, U64P]),
         "oc_ct_mul_pt": (None, [C.c_void_p, U64P, U64P, C.c_int, U64P]),
         "oc_ct_mul_relin": (None, [C.c_void_p, U64P, U64P, C.c_int, U64P, U64P]),
