@@ -345,25 +345,8 @@ def run_model(args, ws, rank, local):
     ms_max = max_over_ranks(ms, ws)
     value = aggregate_tokens_per_s(LANES, ws, args.steps, ms_max)
 
-    # the per-kernel table and the roofline come from one more pass, outside the timed region, with
-    # every kernel call bracketed by CUDA events on the engine's stream
-    cx.set_option("profile_every", 1)
-    cx.profile(True)
-    m.step(cts[nsteps - 1])
-    prof = cx.profile_collect()
-    cx.profile(False)
-
-    # fidelity against the float64 model (exact 1/sqrt), replaying every step from a cold state
-    state, errs, top1 = None, [], []
-    for i in range(nsteps):
-        ref, state = plain_step(cfg, w, w["emb"][toks[i]], state)
-        if i >= args.warmup:
-            y = fhessm.model.unpack_lanes(cx.Decrypt(outs[i]), cfg.D, LANES, cfg.d)
-            lg, lr = y @ w["emb"].T, ref @ w["emb"].T
-            errs.append(rel_err_rms(lg, lr))
-            top1.append(float(np.mean(lg.argmax(-1) == lr.argmax(-1))))
-
-    # end to end through the public API: host words in (H2D), one pass, host words out (D2H)
+    # end to end through the public API, right after the timed passes (the GPU still warm): host
+    # words in (H2D), one pass, host words out (D2H)
     words_in = cts[nsteps].words()
     barrier(ws)
     t0 = time.time()
@@ -375,6 +358,50 @@ def run_model(args, ws, rank, local):
     e2e = {"value": LANES * ws / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(words_in.nbytes),
            "d2h_bytes_per_step": int(words_out.nbytes)}
 
+    # the per-kernel table and the roofline come from two more passes, outside the timed region:
+    # one call in 4 of every kernel kind bracketed by CUDA events on the engine's stream
+    cx.set_option("profile_every", 4)
+    cx.profile(True)
+    for i in range(2):
+        m.step(cts[i])
+    prof = cx.profile_collect()
+    cx.profile(False)
+    prof = {k: (v[0] / 2, v[1] / 2, v[2] / 2, v[3] / 2) for k, v in prof.items()}   # per pass
+    census = m.refresh_census()
+
+    # fidelity against the float64 model (exact 1/sqrt), replaying every step from a cold state
+    state, errs, top1 = None, [], []
+    for i in range(nsteps):
+        ref, state = plain_step(cfg, w, w["emb"][toks[i]], state)
+        if i >= args.warmup:
+            y = fhessm.model.unpack_lanes(cx.Decrypt(outs[i]), cfg.D, LANES, cfg.d)
+            lg, lr = y @ w["emb"].T, ref @ w["emb"].T
+            errs.append(rel_err_rms(lg, lr))
+            top1.append(float(np.mean(lg.argmax(-1) == lr.argmax(-1))))
+
+    # end to end through the public API, right after the timed passes (the GPU still warm): host
+    # words in (H2D), one pass, host words out (D2H)
+    words_in = cts[nsteps].words()
+    barrier(ws)
+    t0 = time.time()
+    ct_in = cx.ct_from_words(words_in, in_level, cts[nsteps].scale)
+    out = m.step(ct_in)
+    words_out = out.words()
+    cx.sync()
+    e2e_s = max_over_ranks(time.time() - t0, ws)
+    e2e = {"value": LANES * ws / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(words_in.nbytes),
+           "d2h_bytes_per_step": int(words_out.nbytes)}
+
+    # the per-kernel table and the roofline come from two more passes, outside the timed region:
+    # one call in 4 of every kernel kind bracketed by CUDA events on the engine's stream
+    cx.set_option("profile_every", 4)
+    cx.profile(True)
+    for i in range(2):
+        m.step(cts[i])
+    prof = cx.profile_collect()
+    cx.profile(False)
+    prof = {k: (v[0] / 2, v[1] / 2, v[2] / 2, v[3] / 2) for k, v in prof.items()}   # per pass
+    census = m.refresh_census()
     fidelity = {"logits_relErrRms_max": max(errs), "top1_min": min(top1), "vs": "float64 model, exact 1/sqrt",
                 "bar": "relErrRms <= 1e-3 and top-1 >= 0.98"}
     fidelity["ok"] = bool(fidelity["logits_relErrRms_max"] <= 1e-3 and fidelity["top1_min"] >= 0.98)
@@ -399,7 +426,8 @@ def run_model(args, ws, rank, local):
             "kernels": kernel_table(prof),
             "memory_gib": {k: round(v / 2**30, 2) for k, v in cx.memory().items()},
             "census": {"keyswitches_per_pass": ks_per_pass, "ks_avg_limbs": ks_nl_avg, "bootstraps_per_pass": boots,
-                       "kernel_launches_per_pass": launches / args.steps},
+                       "kernel_launches_per_pass": launches / args.steps,
+                       "bootstraps_by_site_all_passes": census},
             "setup_s": setup_s, "gpu_launches": launches, "clocks": clocks, "e2e": e2e, "cpu_baseline": cpu,
             "tensor_pipe": tensor_pipe(prof), "roofline": roofline(prof),
             "fidelity": fidelity,

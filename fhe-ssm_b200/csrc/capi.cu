@@ -47,7 +47,10 @@ static int nl_of(const fhe::Context& cx, int level) {
     if (level < 0 || level >= cx.L) throw fhe::Error("level out of range", FHE_ERR_ARG);
     return cx.L - level;
 }
-static void bind(fhe_ctx* c) { CUDA_CHECK(cudaSetDevice(c->cx.device)); }
+static void bind(fhe_ctx* c) {
+    CUDA_CHECK(cudaSetDevice(c->cx.device));
+    c->cx.activate();
+}
 
 static fhe_ct* wrap(fhe_ctx* c, fhe::Ciphertext&& x) {
     auto* r = new fhe_ct{std::move(x), c};

@@ -8,6 +8,8 @@
 // index 5^r mod 2N, conjugation 2N-1 (:1355-1369).
 #include <omp.h>
 
+#include <mutex>
+
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -209,7 +211,7 @@ Context::Context(const Params& p) : prm(p) {
         const uint64_t ni = host_invmod((uint64_t)N % q, q);
         ninv[2 * m] = ni; ninv[2 * m + 1] = shoup_of(ni, q);
     }
-    CUDA_CHECK(cudaMemcpyToSymbol(c_mod, mc.data(), sizeof(ModConst) * nm));
+    activate();
     d_tw = dev_upload(tw); d_twp = dev_upload(twp); d_itw = dev_upload(itw); d_itwp = dev_upload(itwp);
     {
         std::vector<uint64_t> f(2 * tw.size()), v(2 * itw.size());
@@ -1085,6 +1087,21 @@ void download(Context& cx, uint64_t* dst, const uint64_t* src, size_t words) {
 }
 // A kernel whose bounded wait ran out left its flag: report it (the results of the work in
 // flight since the last check are not trustworthy) and clear it.
+// the moduli table each device's c_mod holds now (what the last activate() on it wrote)
+static std::mutex g_cmod_mu;
+static std::vector<ModConst> g_cmod_loaded[kMaxDevices];
+
+void Context::activate() {
+    if (device < 0 || device >= kMaxDevices) throw Error("device index out of range", -1);
+    std::lock_guard<std::mutex> lk(g_cmod_mu);
+    auto& cur = g_cmod_loaded[device];
+    if (cur.size() == mc.size() && std::memcmp(cur.data(), mc.data(), mc.size() * sizeof(ModConst)) == 0) return;
+    // another chain's constants are in the table: let the kernels that read them finish first
+    if (!cur.empty()) CUDA_CHECK(cudaDeviceSynchronize());
+    CUDA_CHECK(cudaMemcpyToSymbol(c_mod, mc.data(), sizeof(ModConst) * mc.size()));
+    cur = mc;
+}
+
 void Context::check_device_error() {
     unsigned int f = 0;
     CUDA_CHECK(cudaMemcpy(&f, d_err, sizeof f, cudaMemcpyDeviceToHost));

@@ -37,6 +37,7 @@ struct Error : std::runtime_error {
     } while (0)
 
 constexpr int kMaxMod = 64;
+constexpr int kMaxDevices = 64;
 
 // constant-memory copy of every modulus' constants (index: Q chain then P chain)
 // defined once: the library is one translation unit (fhessm.cu)
@@ -158,6 +159,10 @@ struct Context {
     bool prof = false;
     int prof_every = 1;
     void check_device_error();
+    // Makes this context's moduli the ones in the device's constant table c_mod (one table per
+    // device, shared by every context on it): when another context with a different chain wrote
+    // it last, the device is synchronised and the table rewritten.  Every C-ABI entry calls it.
+    void activate();
     mutable std::map<std::string, ProfEntry> prof_acc;
     std::unique_ptr<Plaintext> pt_i;         // NTT of X^{N/2}: multiplication by i
     std::map<uint64_t, std::shared_ptr<Plaintext>> ptcache;   // encode_cached: (content, level, scale)

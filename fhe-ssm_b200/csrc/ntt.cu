@@ -256,6 +256,10 @@ void ntt(const Context& cx, const LimbMap& mp, int npoly, bool inv, cudaStream_t
             const int dg = mp.skip_period > 0 ? p % mp.skip_period : p;
             work -= std::max(0, std::min(mp.skip_alpha, mp.skip_nq - dg * mp.skip_alpha));
         }
+    // the launch's batch size class as an inclusive "op:" entry (where the transforms' time goes)
+    static const char* kCls[2][3] = {{"op:ntt_fwd_le16", "op:ntt_fwd_le64", "op:ntt_fwd_gt64"},
+                                     {"op:ntt_inv_le16", "op:ntt_inv_le64", "op:ntt_inv_gt64"}};
+    ProfScope pc(cx, kCls[inv ? 1 : 0][work <= 16 ? 0 : work <= 64 ? 1 : 2], 16.0 * cx.N * work);
     ProfScope ps(cx, inv ? "ntt_inv" : "ntt_fwd", 16.0 * cx.N * work);
     switch (cx.logN) {
         case 12: launch_ntt<12>(cx, mp, count, inv, st); break;
