@@ -66,7 +66,7 @@ __global__ void __launch_bounds__(256) k_ptgen(const double* __restrict__ coef, 
         const int t = e >> logD2, k = e & (D2 - 1);
         uint64_t r0 = 0;
         if (id0 + t < P) {
-            const long long r = llrint(coef[(size_t)(id0 + t) * D2 + k] * scale);
+            const long long r = llround(coef[(size_t)(id0 + t) * D2 + k] * scale);   // ties away from zero, as llround in encode
             r0 = r >= 0 ? reduce64((uint64_t)r, mc) : mod_neg(reduce64((uint64_t)(-r), mc), mc.q);
         }
         sa[e] = r0;
@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(256) k_ptgen2048(const double* __restrict__ co
         uint64_t x[8];
 #pragma unroll
         for (int k = 0; k < 8; k++) {
-            const long long r = llrint(cf[t][k] * scale);
+            const long long r = llround(cf[t][k] * scale);   // ties away from zero, as llround in encode
             x[k] = r >= 0 ? reduce64((uint64_t)r, mc) : mod_neg(reduce64((uint64_t)(-r), mc), q);
         }
         // pass 1: elements tid + 256 k, distances 1024, 512, 256

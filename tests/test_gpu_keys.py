@@ -17,9 +17,11 @@ CTX = dict(logN=13, L=28, K=4, alpha=4, hw=192, boot_primes=14)
 
 def test_part_file_round_trip_and_refusal(tmp_path):
     import fhessm
-    a = fhessm.CryptoContext(logN=13, L=8, K=2, alpha=3, hw=64)
-    b = fhessm.CryptoContext(logN=13, L=8, K=2, alpha=3, hw=64)
-    other = fhessm.CryptoContext(logN=13, L=7, K=2, alpha=3, hw=64)
+    # K = 3 special primes (180 bits) above a digit of alpha = 3 45-bit limbs: the switching noise
+    # stays small; `other` has another chain on the same GPU
+    a = fhessm.CryptoContext(logN=13, L=8, K=3, alpha=3, hw=64)
+    b = fhessm.CryptoContext(logN=13, L=8, K=3, alpha=3, hw=64)
+    other = fhessm.CryptoContext(logN=13, L=7, K=3, alpha=3, hw=64)
     try:
         a.KeyGen(seed=21)
         a.EvalRotateKeyGen([1, -2, 7], conj=True)
@@ -38,6 +40,7 @@ def test_part_file_round_trip_and_refusal(tmp_path):
         z = np.random.default_rng(1).uniform(-1, 1, a.slots)
         ct = a.Encrypt(a.MakeCKKSPackedPlaintext(z, 1))
         rb = b.EvalRotate(b.ct_from_words(ct.words(), ct.level, ct.scale), 7)
+        assert (rb.words() == a.EvalRotate(ct, 7).words()).all()   # loaded keys act as the minted ones
         back = a.ct_from_words(rb.words(), rb.level, rb.scale)
         assert np.abs(a.Decrypt(back).real - np.roll(z, -7)).max() < 1e-4
     finally:
