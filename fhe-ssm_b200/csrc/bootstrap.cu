@@ -355,9 +355,9 @@ static void eval_level(Context& cx, const BootLevel& L, const Ciphertext& v, Cip
         fsum = DevBuf((size_t)2 * nl * N, st);
         ProfScope pe(cx, "ewise", 8.0 * N * nl * 2 * 3 * (double)(flat.size() - 1));
         const long long ps = (long long)nl * N;
-        k_ewise<<<dim3(N / 256, nl, 2), 256, 0, st>>>(EW_ADD, flat[0], ps, flat[1], ps, fsum.p, ps, 0, cx.logN);
+        launch_pdl(cx, k_ewise, dim3(N / 256, nl, 2), dim3(256), 0, st, EW_ADD, flat[0], ps, flat[1], ps, fsum.p, ps, 0, cx.logN);
         for (size_t f = 2; f < flat.size(); f++)
-            k_ewise<<<dim3(N / 256, nl, 2), 256, 0, st>>>(EW_ADD, fsum.p, ps, flat[f], ps, fsum.p, ps, 0, cx.logN);
+            launch_pdl(cx, k_ewise, dim3(N / 256, nl, 2), dim3(256), 0, st, EW_ADD, fsum.p, ps, flat[f], ps, fsum.p, ps, 0, cx.logN);
         CUDA_CHECK(cudaGetLastError());
         cx.launches += (long long)flat.size() - 1;
         g0 = fsum.p;
@@ -465,7 +465,7 @@ void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto
         ntt(cx, lm, 2, true, cx.stream);
         // k_rescale_lift writes y[c][i] for i < nlm1, layout [2][nlm1][N]: lift into a temp then copy
         DevBuf y((size_t)2 * Lt * N, cx.stream);
-        k_rescale_lift<<<dim3(N / 256, Lt, 2), 256, 0, cx.stream>>>(c.p, y.p, Lt, 0, cx.logN);
+        launch_pdl(cx, k_rescale_lift, dim3(N / 256, Lt, 2), dim3(256), 0, cx.stream, c.p, y.p, Lt, 0, cx.logN);
         CUDA_CHECK(cudaGetLastError());
         cx.launches++;
         ntt(cx, cx.qmap(y.p, Lt, (long long)Lt * N), 2, false, cx.stream);

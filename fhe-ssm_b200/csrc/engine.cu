@@ -428,12 +428,12 @@ static void moddown(Context& cx, uint64_t* ip, int nl, const uint64_t* add0, con
     DevBuf y((size_t)2 * nl * N, st);
     {
         ProfScope ps(cx, "moddown_bconv", 8.0 * N * (2 * K + 2 * nl));
-        k_moddown_bconv<<<g2(cx, 2), 256, 0, st>>>(ip, y.p, cx.d_md, nl, ne, L, K, cx.logN, 0, 0);
+        launch_pdl(cx, k_moddown_bconv, g2(cx, 2), dim3(256), 0, st, ip, y.p, cx.d_md, nl, ne, L, K, cx.logN, 0, 0);
     }
     ntt(cx, cx.qmap(y.p, nl, (long long)nl * N), 2, false, st);
     {
         ProfScope ps(cx, "moddown_final", 8.0 * N * nl * (6 + (add0 ? 1 : 0) + (add1 ? 1 : 0)));
-        k_moddown_final<<<g2(cx, nl, 2), 256, 0, st>>>(ip, y.p, add0, add1, out0, out1, cx.d_md, nl, ne, L, K,
+        launch_pdl(cx, k_moddown_final, g2(cx, nl, 2), dim3(256), 0, st, ip, y.p, add0, add1, out0, out1, cx.d_md, nl, ne, L, K,
                                                        cx.logN, perm_k);
     }
     CUDA_CHECK(cudaGetLastError());
@@ -450,7 +450,7 @@ static DevBuf modup(Context& cx, const uint64_t* d, int nl) {
     DevBuf ext((size_t)dn * ne * N, st);
     {
         ProfScope ps(cx, "modup_bconv", 8.0 * N * (2 * nl + (double)dn * ne));
-        k_modup_bconv<<<g2(cx, dn), 256, 0, st>>>(dc.p, d, ext.p, cx.modup_table(nl), nl, ne, cx.alpha, cx.L,
+        launch_pdl(cx, k_modup_bconv, g2(cx, dn), dim3(256), 0, st, dc.p, d, ext.p, cx.modup_table(nl), nl, ne, cx.alpha, cx.L,
                                                   cx.logN, 0, 0, 0);
     }
     LimbMap em = cx.extmap(ext.p, nl, (long long)ne * N);
@@ -470,7 +470,7 @@ static void inner_moddown(Context& cx, const DevBuf& ext, int nl, const SwitchKe
     DevBuf ip((size_t)2 * ne * N, st);
     {
         ProfScope ps(cx, "key_inner", 8.0 * N * ((double)dn * ne * 3 + 2 * ne));
-        k_key_inner<<<g2(cx, ne), 256, 0, st>>>(ext.p, key.buf.p, ip.p, nl, ne, dn, cx.L, K, cx.logN);
+        launch_pdl(cx, k_key_inner, g2(cx, ne), dim3(256), 0, st, ext.p, key.buf.p, ip.p, nl, ne, dn, cx.L, K, cx.logN);
     }
     cx.launches += 1;
     moddown(cx, ip.p, nl, add0, add1, out0, out1, perm_k);
@@ -516,7 +516,7 @@ static void ewise(Context& cx, int op, const Ciphertext& a, const uint64_t* b, l
                   Ciphertext& out) {
     ensure_out(cx, out, a.nl);
     ProfScope ps(cx, "ewise", 8.0 * cx.N * a.nl * 2 * 3);
-    k_ewise<<<g2(cx, a.nl, 2), 256, 0, cx.stream>>>(op, a.buf.p, (long long)a.stride, b, sb, out.buf.p,
+    launch_pdl(cx, k_ewise, g2(cx, a.nl, 2), dim3(256), 0, cx.stream, op, a.buf.p, (long long)a.stride, b, sb, out.buf.p,
                                                     (long long)out.stride, log_rep, cx.logN);
     CUDA_CHECK(cudaGetLastError());
     cx.launches++;
@@ -563,7 +563,7 @@ void ct_mul_relin(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphert
     DevBuf d2((size_t)nl * cx.N, cx.stream);
     {
         ProfScope ps(cx, "tensor", 8.0 * cx.N * nl * 7);
-        k_tensor<<<g2(cx, nl), 256, 0, cx.stream>>>(a.buf.p, (long long)a.stride, b.buf.p, (long long)b.stride,
+        launch_pdl(cx, k_tensor, g2(cx, nl), dim3(256), 0, cx.stream, a.buf.p, (long long)a.stride, b.buf.p, (long long)b.stride,
                                                     t.buf.p, (long long)t.stride, d2.p, cx.logN);
     }
     CUDA_CHECK(cudaGetLastError());
@@ -584,14 +584,14 @@ void ct_mul_relin_rescale(Context& cx, const Ciphertext& a, const Ciphertext& b,
     DevBuf d2((size_t)nl * N, st);
     {
         ProfScope ps(cx, "tensor", 8.0 * N * nl * 7);
-        k_tensor<<<g2(cx, nl), 256, 0, st>>>(a.buf.p, (long long)a.stride, b.buf.p, (long long)b.stride, d.buf.p,
+        launch_pdl(cx, k_tensor, g2(cx, nl), dim3(256), 0, st, a.buf.p, (long long)a.stride, b.buf.p, (long long)b.stride, d.buf.p,
                                              (long long)d.stride, d2.p, cx.logN);
     }
     DevBuf ext = modup(cx, d2.p, nl);
     DevBuf ip((size_t)2 * ne * N, st);
     {
         ProfScope ps(cx, "key_inner", 8.0 * N * ((double)dn * ne * 3 + 2 * ne));
-        k_key_inner<<<g2(cx, ne), 256, 0, st>>>(ext.p, cx.rlk->buf.p, ip.p, nl, ne, dn, L, K, cx.logN);
+        launch_pdl(cx, k_key_inner, g2(cx, ne), dim3(256), 0, st, ext.p, cx.rlk->buf.p, ip.p, nl, ne, dn, L, K, cx.logN);
     }
     cx.ks_count++;
     cx.ks_limbs += nl;
@@ -599,7 +599,7 @@ void ct_mul_relin_rescale(Context& cx, const Ciphertext& a, const Ciphertext& b,
     DevBuf z((size_t)2 * J * N, st);
     {
         ProfScope ps(cx, "mdr_gather", 8.0 * N * 2 * (1 + 2 * J));
-        k_mdr_gather<<<dim3(N / 256, J, 2), 256, 0, st>>>(d.buf.p, (long long)d.stride, ip.p, tab, z.p, nl, ne, K,
+        launch_pdl(cx, k_mdr_gather, dim3(N / 256, J, 2), dim3(256), 0, st, d.buf.p, (long long)d.stride, ip.p, tab, z.p, nl, ne, K,
                                                           cx.logN);
     }
     LimbMap zm{};
@@ -609,13 +609,13 @@ void ct_mul_relin_rescale(Context& cx, const Ciphertext& a, const Ciphertext& b,
     DevBuf y((size_t)2 * (nl - 1) * N, st);
     {
         ProfScope ps(cx, "moddown_bconv", 8.0 * N * (2 * J + 2 * (nl - 1)));
-        k_mdr_bconv<<<g2(cx, 2), 256, 0, st>>>(z.p, y.p, tab, nl, K, L, cx.logN, 0, 0);
+        launch_pdl(cx, k_mdr_bconv, g2(cx, 2), dim3(256), 0, st, z.p, y.p, tab, nl, K, L, cx.logN, 0, 0);
     }
     ntt(cx, cx.qmap(y.p, nl - 1, (long long)(nl - 1) * N), 2, false, st);
     Ciphertext r = ct_alloc(cx, nl - 1);
     {
         ProfScope ps(cx, "moddown_final", 8.0 * N * (nl - 1) * 2 * 5);
-        k_mdr_final<<<g2(cx, nl - 1, 2), 256, 0, st>>>(d.buf.p, (long long)d.stride, ip.p, y.p, tab, r.buf.p,
+        launch_pdl(cx, k_mdr_final, g2(cx, nl - 1, 2), dim3(256), 0, st, d.buf.p, (long long)d.stride, ip.p, y.p, tab, r.buf.p,
                                                        (long long)r.stride, nl, ne, K, cx.logN);
     }
     CUDA_CHECK(cudaGetLastError());
@@ -638,12 +638,12 @@ void ct_rescale(Context& cx, Ciphertext& a) {
     DevBuf y((size_t)2 * l * N, st);
     {
         ProfScope ps(cx, "rescale_lift", 8.0 * N * 2 * (1 + l));
-        k_rescale_lift<<<g2(cx, l, 2), 256, 0, st>>>(last.p, y.p, l, l, cx.logN);
+        launch_pdl(cx, k_rescale_lift, g2(cx, l, 2), dim3(256), 0, st, last.p, y.p, l, l, cx.logN);
     }
     ntt(cx, cx.qmap(y.p, l, (long long)l * N), 2, false, st);
     {
         ProfScope ps(cx, "rescale_final", 8.0 * N * 2 * l * 3);
-        k_rescale_final<<<g2(cx, l, 2), 256, 0, st>>>(a.buf.p, (long long)a.stride, y.p, cx.d_rs, l, l, cx.L,
+        launch_pdl(cx, k_rescale_final, g2(cx, l, 2), dim3(256), 0, st, a.buf.p, (long long)a.stride, y.p, cx.d_rs, l, l, cx.L,
                                                       cx.logN);
     }
     CUDA_CHECK(cudaGetLastError());
@@ -712,12 +712,12 @@ void limb_residues(const Context& cx, long double v, int nl, uint64_t* out) {
 void apply_limb_const(Context& cx, const Ciphertext& a, const LimbConst& k, Ciphertext& out) {
     ProfScope ps(cx, "mul_const", 8.0 * cx.N * a.nl * 2 * 2);
     if (&out == &a) {
-        k_mul_const<<<g2(cx, a.nl, 2), 256, 0, cx.stream>>>(a.buf.p, (long long)a.stride, a.buf.p, (long long)a.stride,
+        launch_pdl(cx, k_mul_const, g2(cx, a.nl, 2), dim3(256), 0, cx.stream, a.buf.p, (long long)a.stride, a.buf.p, (long long)a.stride,
                                                             k, cx.logN);
     } else {
         Ciphertext t;
         ensure_out(cx, t, a.nl);
-        k_mul_const<<<g2(cx, a.nl, 2), 256, 0, cx.stream>>>(a.buf.p, (long long)a.stride, t.buf.p, (long long)t.stride,
+        launch_pdl(cx, k_mul_const, g2(cx, a.nl, 2), dim3(256), 0, cx.stream, a.buf.p, (long long)a.stride, t.buf.p, (long long)t.stride,
                                                             k, cx.logN);
         t.scale = a.scale;
         out = std::move(t);

@@ -128,6 +128,7 @@ struct Context {
     uint64_t* d_rs = nullptr;        // rescale: [L][L] (ql mod qi, ql^-1 mod qi, shoup)
     unsigned int* d_err = nullptr;   // set by a kernel whose bounded wait ran out (checked at syncs)
     int use_tc = 1;                  // BSGS products on the tensor cores (tcgen05) where the shape allows
+    int use_pdl = 1;                 // programmatic dependent launch for the hot kernels (launch_pdl)
     int merged_rescale = 1;          // circuit products: ModDown and rescale in one division by P q_l
     // BSGS plaintext cache (the reference's --cache-diags, gpu_real_model.cu:1647-1652, off by
     // default as there): a plan keeps the plaintext words of its last call while at least
@@ -222,6 +223,21 @@ struct ProfScope {
     }
 };
 
+// ---- programmatic dependent launch ------------------------------------------------------
+// A kernel launched by launch_pdl may be scheduled while the previous kernel on the stream is
+// still running: its CTAs start, run pdl_wait() -- which returns once the previous grid has
+// completed and its writes are visible -- and only then touch memory.  Every kernel launched this
+// way calls pdl_wait() before its first global load or store; pdl_trigger() lets the next grid be
+// scheduled as soon as all of this grid's CTAs have started.  For a kernel launched the ordinary
+// way both are no-ops.  What is gained is the gap between dependent kernels (scheduling the next
+// grid, its CTAs' start-up), which dominates the short launches of small batches.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+template <typename... P, typename... A>
+inline void launch_pdl(const Context& cx, void (*k)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       A&&... args);
+
 // ---- low-level launches (ntt.cu, kernels.cu, keys.cu) --------------------------------------
 void expand_uniform_dev(Context& cx, const uint8_t seed[32], int digit0, int ndigit, int limb0, int nlimb,
                         uint32_t tag, uint64_t* out, long long digit_stride);
@@ -315,6 +331,22 @@ void bootstrap_setup(Context& cx, double B, int deg, int r = 3);
 void bootstrap(Context& cx, const Ciphertext& in, Ciphertext& out);
 void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto);
 int bootstrap_levels_after(const Context& cx);
+
+template <typename... P, typename... A>
+inline void launch_pdl(const Context& cx, void (*k)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       A&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = cx.use_pdl ? 1 : 0;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    CUDA_CHECK(cudaLaunchKernelEx(&cfg, k, std::forward<A>(args)...));
+}
 
 // raw access (parity tests)
 void upload(Context& cx, uint64_t* dst, const uint64_t* src, size_t words);

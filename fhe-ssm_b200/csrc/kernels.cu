@@ -29,6 +29,8 @@ __global__ void __launch_bounds__(256) k_modup_bconv(const uint64_t* __restrict_
                                                      const uint64_t* __restrict__ deval, uint64_t* __restrict__ ext,
                                                      const uint64_t* __restrict__ tab, int nl, int ne, int alpha, int L,
                                                      int logN, long long sdc, long long sdv, long long sext) {
+    pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
+    pdl_trigger();
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int j = blockIdx.y;
@@ -109,6 +111,8 @@ __device__ __forceinline__ void digit_dot2(const uint64_t* __restrict__ d, size_
 // out[c][e] = sum_j ext[j][e] * key[j][c][m(e)]  (key in Montgomery form -> canonical result)
 __global__ void k_key_inner(const uint64_t* __restrict__ ext, const uint64_t* __restrict__ key,
                             uint64_t* __restrict__ out, int nl, int ne, int dnum, int L, int K, int logN) {
+    pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
+    pdl_trigger();
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int e = blockIdx.y;
@@ -128,6 +132,8 @@ __global__ void k_key_inner(const uint64_t* __restrict__ ext, const uint64_t* __
 __global__ void k_moddown_bconv(const uint64_t* __restrict__ buf, uint64_t* __restrict__ y,
                                 const uint64_t* __restrict__ md, int nl, int ne, int L, int K, int logN,
                                 long long sbuf, long long sy) {
+    pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
+    pdl_trigger();
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int c = blockIdx.y;
@@ -158,6 +164,8 @@ __global__ void k_moddown_final(const uint64_t* __restrict__ buf, const uint64_t
                                 const uint64_t* add0, const uint64_t* add1, uint64_t* out0, uint64_t* out1,
                                 const uint64_t* __restrict__ md, int nl, int ne, int L, int K, int logN,
                                 uint64_t perm_k) {
+    pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
+    pdl_trigger();
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int i = blockIdx.y, c = blockIdx.z;
@@ -185,6 +193,8 @@ __global__ void k_moddown_final(const uint64_t* __restrict__ buf, const uint64_t
 __global__ void __launch_bounds__(256) k_mdr_bconv(const uint64_t* __restrict__ z, uint64_t* __restrict__ y,
                                                    const uint64_t* __restrict__ tab, int nl, int K, int L, int logN,
                                                    long long sz, long long sy) {
+    pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
+    pdl_trigger();
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int c = blockIdx.y;
@@ -221,6 +231,8 @@ __global__ void __launch_bounds__(256) k_mdr_final(const uint64_t* __restrict__ 
                                                    const uint64_t* __restrict__ ip, const uint64_t* __restrict__ y,
                                                    const uint64_t* __restrict__ tab, uint64_t* out, long long so,
                                                    int nl, int ne, int K, int logN) {
+    pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
+    pdl_trigger();
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int i = blockIdx.y, c = blockIdx.z;
@@ -237,6 +249,8 @@ __global__ void __launch_bounds__(256) k_mdr_final(const uint64_t* __restrict__ 
 __global__ void __launch_bounds__(256) k_mdr_gather(const uint64_t* __restrict__ d, long long sd,
                                                     const uint64_t* __restrict__ ip, const uint64_t* __restrict__ tab,
                                                     uint64_t* __restrict__ z, int nl, int ne, int K, int logN) {
+    pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
+    pdl_trigger();
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int j = blockIdx.y, c = blockIdx.z;
@@ -257,6 +271,8 @@ __global__ void __launch_bounds__(256) k_mdr_gather(const uint64_t* __restrict__
 // last: [2][N] the dropped limb (index l) in coefficient form; y[c][i] = centred lift mod q_i
 __global__ void k_rescale_lift(const uint64_t* __restrict__ last, uint64_t* __restrict__ y, int nlm1, int l,
                                int logN) {
+    pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
+    pdl_trigger();
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int i = blockIdx.y, c = blockIdx.z;
@@ -271,6 +287,8 @@ __global__ void k_rescale_lift(const uint64_t* __restrict__ last, uint64_t* __re
 // a_c[i] = (a_c[i] - y[c][i]) * q_l^-1   (rs: [l][i][2] = (q_l^-1 mod q_i, shoup))
 __global__ void k_rescale_final(uint64_t* a, long long stride, const uint64_t* __restrict__ y,
                                 const uint64_t* __restrict__ rs, int nlm1, int l, int L, int logN) {
+    pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
+    pdl_trigger();
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int i = blockIdx.y, c = blockIdx.z;
@@ -285,6 +303,8 @@ __global__ void k_rescale_final(uint64_t* a, long long stride, const uint64_t* _
 // ct op ct / ct op pt.  pt has log_rep: word x of limb i = pt[i][x >> log_rep] (x in eval order).
 __global__ void k_ewise(int op, const uint64_t* a, long long sa, const uint64_t* b, long long sb, uint64_t* o,
                         long long so, int log_rep, int logN) {
+    pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
+    pdl_trigger();
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int i = blockIdx.y, c = blockIdx.z;
@@ -312,6 +332,8 @@ __global__ void k_ewise(int op, const uint64_t* a, long long sa, const uint64_t*
 // multiply every limb i by a per-limb constant (shoup pair), optionally add a per-limb constant
 // to c0.  The constants travel in the kernel parameters (no host-to-device copy, no sync).
 __global__ void k_mul_const(const uint64_t* a, long long sa, uint64_t* o, long long so, const LimbConst k, int logN) {
+    pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
+    pdl_trigger();
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int i = blockIdx.y, c = blockIdx.z;
@@ -325,6 +347,8 @@ __global__ void k_mul_const(const uint64_t* a, long long sa, uint64_t* o, long l
 // tensor: d0 = a0 b0, d1 = a0 b1 + a1 b0 (into o), d2 = a1 b1 (into d2)
 __global__ void k_tensor(const uint64_t* a, long long sa, const uint64_t* b, long long sb, uint64_t* o, long long so,
                          uint64_t* d2, int logN) {
+    pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
+    pdl_trigger();
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int i = blockIdx.y;

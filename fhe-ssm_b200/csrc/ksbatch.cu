@@ -44,6 +44,8 @@ __global__ void __launch_bounds__(256) k_key_inner_b(const uint64_t* __restrict_
                                                      const KeyBatch kb, int B, uint64_t* __restrict__ out, int nl,
                                                      int ne, int dnum, int L, int K, int logN, int sum,
                                                      int accumulate) {
+    pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
+    pdl_trigger();
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int e = blockIdx.y;
@@ -86,6 +88,8 @@ __global__ void __launch_bounds__(256) k_moddown_final_b(const uint64_t* __restr
                                                          const uint64_t* __restrict__ y, const uint64_t* add0,
                                                          const FinalBatch fb, const uint64_t* __restrict__ md,
                                                          int nl, int ne, int L, int K, int logN) {
+    pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
+    pdl_trigger();
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int i = blockIdx.y, c = blockIdx.z & 1, b = blockIdx.z >> 1;
@@ -107,6 +111,8 @@ __global__ void __launch_bounds__(256) k_moddown_final_b(const uint64_t* __restr
 __global__ void __launch_bounds__(256) k_gather_rot(const RotBatch rb, int B, uint64_t* __restrict__ dev,
                                                     uint64_t* __restrict__ dc, uint64_t* __restrict__ cs0,
                                                     const uint64_t* init0, int nl, int logN, int accumulate) {
+    pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
+    pdl_trigger();
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
     const int i = blockIdx.y;
@@ -184,7 +190,7 @@ void ct_rotate_hoisted(Context& cx, const Ciphertext& a, const int* rs, int n, C
         DevBuf ip((size_t)B * 2 * ne * N, st);
         {
             ProfScope ps(cx, "key_inner", 8.0 * N * B * ((double)dn * ne * 2 + 2 * ne) + 8.0 * N * dn * ne);
-            k_key_inner_b<<<gb(cx, ne, B), 256, 0, st>>>(ext.p, 0, kb, B, ip.p, nl, ne, dn, L, K, cx.logN, 0, 0);
+            launch_pdl(cx, k_key_inner_b, gb(cx, ne, B), dim3(256), 0, st, ext.p, 0, kb, B, ip.p, nl, ne, dn, L, K, cx.logN, 0, 0);
         }
         LimbMap pm{};
         pm.base = ip.p + (size_t)nl * N; pm.poly_stride = (long long)ne * N; pm.nl = K;
@@ -193,13 +199,13 @@ void ct_rotate_hoisted(Context& cx, const Ciphertext& a, const int* rs, int n, C
         DevBuf y((size_t)B * 2 * nl * N, st);
         {
             ProfScope ps(cx, "moddown_bconv", 8.0 * N * B * (2 * K + 2 * nl));
-            k_moddown_bconv<<<gb(cx, 2, B), 256, 0, st>>>(ip.p, y.p, cx.d_md, nl, ne, L, K, cx.logN,
+            launch_pdl(cx, k_moddown_bconv, gb(cx, 2, B), dim3(256), 0, st, ip.p, y.p, cx.d_md, nl, ne, L, K, cx.logN,
                                                           (long long)2 * ne * N, (long long)2 * nl * N);
         }
         ntt(cx, cx.qmap(y.p, nl, (long long)nl * N), 2 * B, false, st);
         {
             ProfScope ps(cx, "moddown_final", 8.0 * N * nl * B * 7);
-            k_moddown_final_b<<<gb(cx, nl, 2 * B), 256, 0, st>>>(ip.p, y.p, a.c(0), fb, cx.d_md, nl, ne, L, K,
+            launch_pdl(cx, k_moddown_final_b, gb(cx, nl, 2 * B), dim3(256), 0, st, ip.p, y.p, a.c(0), fb, cx.d_md, nl, ne, L, K,
                                                                  cx.logN);
         }
         CUDA_CHECK(cudaGetLastError());
@@ -240,13 +246,13 @@ void rotate_sum(Context& cx, const uint64_t* const* c0s, const uint64_t* const* 
         DevBuf dev((size_t)B * nl * N, st), dc((size_t)B * nl * N, st);
         {
             ProfScope ps(cx, "gather_rot", 8.0 * N * nl * (3.0 * B + 2));
-            k_gather_rot<<<gb(cx, nl), 256, 0, st>>>(rb, B, dev.p, dc.p, cs0.p, extra0, nl, cx.logN, c0 > 0);
+            launch_pdl(cx, k_gather_rot, gb(cx, nl), dim3(256), 0, st, rb, B, dev.p, dc.p, cs0.p, extra0, nl, cx.logN, c0 > 0);
         }
         ntt(cx, cx.qmap(dc.p, nl, (long long)nl * N), B, true, st);
         DevBuf ext((size_t)B * dn * ne * N, st);
         {
             ProfScope ps(cx, "modup_bconv", 8.0 * N * B * (2 * nl + (double)dn * ne));
-            k_modup_bconv<<<gb(cx, dn, B), 256, 0, st>>>(dc.p, dev.p, ext.p, tab, nl, ne, cx.alpha, L, cx.logN,
+            launch_pdl(cx, k_modup_bconv, gb(cx, dn, B), dim3(256), 0, st, dc.p, dev.p, ext.p, tab, nl, ne, cx.alpha, L, cx.logN,
                                                          (long long)nl * N, (long long)nl * N,
                                                          (long long)dn * ne * N);
         }
@@ -256,7 +262,7 @@ void rotate_sum(Context& cx, const uint64_t* const* c0s, const uint64_t* const* 
         ntt(cx, em, B * dn, false, st);
         {
             ProfScope ps(cx, "key_inner", 8.0 * N * ((double)B * dn * ne * 3 + 2 * ne));
-            k_key_inner_b<<<gb(cx, ne), 256, 0, st>>>(ext.p, (long long)dn * ne * N, kb, B, acc.p, nl, ne, dn, L, K,
+            launch_pdl(cx, k_key_inner_b, gb(cx, ne), dim3(256), 0, st, ext.p, (long long)dn * ne * N, kb, B, acc.p, nl, ne, dn, L, K,
                                                       cx.logN, 1, c0 > 0);
         }
         CUDA_CHECK(cudaGetLastError());
@@ -285,7 +291,7 @@ void ct_mul_relin_rescale_n(Context& cx, const Ciphertext* const* a, const Ciphe
     DevBuf d((size_t)B * 2 * nl * N, st), d2((size_t)B * nl * N, st);
     for (int k = 0; k < B; k++) {
         ProfScope ps(cx, "tensor", 8.0 * N * nl * 7);
-        k_tensor<<<g2(cx, nl), 256, 0, st>>>(a[k]->buf.p, (long long)a[k]->stride, b[k]->buf.p,
+        launch_pdl(cx, k_tensor, g2(cx, nl), dim3(256), 0, st, a[k]->buf.p, (long long)a[k]->stride, b[k]->buf.p,
                                              (long long)b[k]->stride, d.p + (size_t)k * 2 * nl * N,
                                              (long long)nl * N, d2.p + (size_t)k * nl * N, cx.logN);
     }
@@ -296,7 +302,7 @@ void ct_mul_relin_rescale_n(Context& cx, const Ciphertext* const* a, const Ciphe
     DevBuf ext((size_t)B * dn * ne * N, st);
     {
         ProfScope ps(cx, "modup_bconv", 8.0 * N * B * (2 * nl + (double)dn * ne));
-        k_modup_bconv<<<g2(cx, dn, B), 256, 0, st>>>(dc.p, d2.p, ext.p, cx.modup_table(nl), nl, ne, cx.alpha, L,
+        launch_pdl(cx, k_modup_bconv, g2(cx, dn, B), dim3(256), 0, st, dc.p, d2.p, ext.p, cx.modup_table(nl), nl, ne, cx.alpha, L,
                                                      cx.logN, (long long)nl * N, (long long)nl * N,
                                                      (long long)dn * ne * N);
     }
@@ -309,7 +315,7 @@ void ct_mul_relin_rescale_n(Context& cx, const Ciphertext* const* a, const Ciphe
         KeyBatch kb{};
         for (int k = 0; k < B; k++) kb.k[k] = cx.rlk->buf.p;
         ProfScope ps(cx, "key_inner", 8.0 * N * B * ((double)dn * ne * 3 + 2 * ne));
-        k_key_inner_b<<<g2(cx, ne, B), 256, 0, st>>>(ext.p, (long long)dn * ne * N, kb, B, ip.p, nl, ne, dn, L, K,
+        launch_pdl(cx, k_key_inner_b, g2(cx, ne, B), dim3(256), 0, st, ext.p, (long long)dn * ne * N, kb, B, ip.p, nl, ne, dn, L, K,
                                                      cx.logN, 0, 0);
     }
     cx.ks_count += B;
@@ -320,7 +326,7 @@ void ct_mul_relin_rescale_n(Context& cx, const Ciphertext* const* a, const Ciphe
     {
         ProfScope ps(cx, "mdr_gather", 8.0 * N * B * 2 * (1 + 2 * J));
         for (int k = 0; k < B; k++)
-            k_mdr_gather<<<dim3(N / 256, J, 2), 256, 0, st>>>(d.p + (size_t)k * 2 * nl * N, (long long)nl * N,
+            launch_pdl(cx, k_mdr_gather, dim3(N / 256, J, 2), dim3(256), 0, st, d.p + (size_t)k * 2 * nl * N, (long long)nl * N,
                                                               ip.p + (size_t)k * 2 * ne * N, tab,
                                                               z.p + (size_t)k * 2 * J * N, nl, ne, K, cx.logN);
     }
@@ -331,7 +337,7 @@ void ct_mul_relin_rescale_n(Context& cx, const Ciphertext* const* a, const Ciphe
     DevBuf y((size_t)B * 2 * (nl - 1) * N, st);
     {
         ProfScope ps(cx, "moddown_bconv", 8.0 * N * B * (2 * J + 2 * (nl - 1)));
-        k_mdr_bconv<<<g2(cx, 2, B), 256, 0, st>>>(z.p, y.p, tab, nl, K, L, cx.logN, (long long)2 * J * N,
+        launch_pdl(cx, k_mdr_bconv, g2(cx, 2, B), dim3(256), 0, st, z.p, y.p, tab, nl, K, L, cx.logN, (long long)2 * J * N,
                                                   (long long)2 * (nl - 1) * N);
     }
     ntt(cx, cx.qmap(y.p, nl - 1, (long long)(nl - 1) * N), 2 * B, false, st);
@@ -339,7 +345,7 @@ void ct_mul_relin_rescale_n(Context& cx, const Ciphertext* const* a, const Ciphe
         Ciphertext r = ct_alloc(cx, nl - 1);
         {
             ProfScope ps(cx, "moddown_final", 8.0 * N * (nl - 1) * 2 * 5);
-            k_mdr_final<<<g2(cx, nl - 1, 2), 256, 0, st>>>(d.p + (size_t)k * 2 * nl * N, (long long)nl * N,
+            launch_pdl(cx, k_mdr_final, g2(cx, nl - 1, 2), dim3(256), 0, st, d.p + (size_t)k * 2 * nl * N, (long long)nl * N,
                                                            ip.p + (size_t)k * 2 * ne * N,
                                                            y.p + (size_t)k * 2 * (nl - 1) * N, tab, r.buf.p,
                                                            (long long)r.stride, nl, ne, K, cx.logN);

@@ -673,7 +673,7 @@ static void moddown_many(Context& cx, uint64_t* in, int B, int nl, uint64_t* out
     DevBuf y((size_t)B * 2 * nl * N, st);
     {
         ProfScope ps(cx, "moddown_bconv", 8.0 * N * B * (2 * K + 2 * nl));
-        k_moddown_bconv<<<dim3(N / 256, 2, B), 256, 0, st>>>(in, y.p, cx.d_md, nl, ne, L, K, cx.logN,
+        launch_pdl(cx, k_moddown_bconv, dim3(N / 256, 2, B), dim3(256), 0, st, in, y.p, cx.d_md, nl, ne, L, K, cx.logN,
                                                              (long long)2 * ne * N, (long long)2 * nl * N);
     }
     ntt(cx, cx.qmap(y.p, nl, (long long)nl * N), 2 * B, false, st);
@@ -686,7 +686,7 @@ static void moddown_many(Context& cx, uint64_t* in, int B, int nl, uint64_t* out
             fb.perm[b] = 1;
         }
         ProfScope ps(cx, "moddown_final", 8.0 * N * nl * Bc * 6);
-        k_moddown_final_b<<<dim3(N / 256, nl, 2 * Bc), 256, 0, st>>>(in + (size_t)b0 * 2 * ne * N,
+        launch_pdl(cx, k_moddown_final_b, dim3(N / 256, nl, 2 * Bc), dim3(256), 0, st, in + (size_t)b0 * 2 * ne * N,
                                                                      y.p + (size_t)b0 * 2 * nl * N, nullptr, fb,
                                                                      cx.d_md, nl, ne, L, K, cx.logN);
     }

@@ -91,6 +91,8 @@ __device__ __forceinline__ void stage16(uint64_t (&x)[16], uint64_t q, int h, TW
 template <int LOGN, bool INV>
 __global__ void __launch_bounds__(256, 3) k_ntt_col(LimbMap mp, const ulonglong2* __restrict__ tw2,
                                                   const uint64_t* __restrict__ ninv) {
+    pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
+    pdl_trigger();
     constexpr int N = 1 << LOGN;
     constexpr int R = N >> 8;            // rows
     constexpr int TC = 4096 / R;         // columns per tile
@@ -171,6 +173,8 @@ constexpr int kRowTab = 240;   // pairs per 256-word block: 16 threads x (1 + 2 
 template <int LOGN, bool INV>
 __global__ void __launch_bounds__(256, 3) k_ntt_row(LimbMap mp, const ulonglong2* __restrict__ tw2,
                                                   const ulonglong2* __restrict__ rtab) {
+    pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
+    pdl_trigger();
     constexpr int N = 1 << LOGN;
     constexpr int S1 = LOGN - 8;
     __shared__ uint64_t sm[16 * 272];
@@ -239,11 +243,11 @@ static void launch_ntt(const Context& cx, const LimbMap& mp, int count, bool inv
     constexpr int R = N >> 8;
     dim3 gcol(R / 16, count), grow(N / 4096, count);
     if (!inv) {
-        k_ntt_col<LOGN, false><<<gcol, 256, 0, st>>>(mp, (const ulonglong2*)cx.d_tw2, cx.d_ninv);
-        k_ntt_row<LOGN, false><<<grow, 256, 0, st>>>(mp, (const ulonglong2*)cx.d_tw2, (const ulonglong2*)cx.d_twrow);
+        launch_pdl(cx, k_ntt_col<LOGN, false>, gcol, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_tw2, cx.d_ninv);
+        launch_pdl(cx, k_ntt_row<LOGN, false>, grow, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_tw2, (const ulonglong2*)cx.d_twrow);
     } else {
-        k_ntt_row<LOGN, true><<<grow, 256, 0, st>>>(mp, (const ulonglong2*)cx.d_itw2, (const ulonglong2*)cx.d_itwrow);
-        k_ntt_col<LOGN, true><<<gcol, 256, 0, st>>>(mp, (const ulonglong2*)cx.d_itw2, cx.d_ninv);
+        launch_pdl(cx, k_ntt_row<LOGN, true>, grow, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_itw2, (const ulonglong2*)cx.d_itwrow);
+        launch_pdl(cx, k_ntt_col<LOGN, true>, gcol, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_itw2, cx.d_ninv);
     }
 }
 
