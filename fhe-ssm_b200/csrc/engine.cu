@@ -629,6 +629,22 @@ void ct_rescale(Context& cx, Ciphertext& a) {
     if (a.nl < 2) throw Error("rescale: no limb left to drop", -4);
     const int N = cx.N, l = a.nl - 1;
     cudaStream_t st = cx.stream;
+    if (cx.logN >= 13) {
+        // the dropped limb of both polynomials to coefficient form in place, then one fused
+        // forward transform: lift on load, (a_i - y) q_l^-1 on store (ntt.cu, ntt_rescale)
+        LimbMap lm{};
+        lm.base = a.c(0) + (size_t)l * N; lm.poly_stride = (long long)a.stride; lm.nl = 1;
+        lm.split = 1; lm.off0 = l; lm.off1 = 0;
+        ntt(cx, lm, 2, true, st);
+        DevBuf y((size_t)2 * l * N, st);
+        {
+            ProfScope ps(cx, "rescale_ntt", 8.0 * N * (4.0 * l + 2));
+            ntt_rescale(cx, a.buf.p, (long long)a.stride, l, y.p, st);
+        }
+        a.scale /= (double)cx.mods[l];
+        a.nl = l;
+        return;
+    }
     DevBuf last((size_t)2 * N, st);
     CUDA_CHECK(cudaMemcpyAsync(last.p, a.c(0) + (size_t)l * N, N * 8, cudaMemcpyDeviceToDevice, st));
     CUDA_CHECK(cudaMemcpyAsync(last.p + N, a.c(1) + (size_t)l * N, N * 8, cudaMemcpyDeviceToDevice, st));

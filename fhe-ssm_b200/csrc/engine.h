@@ -242,6 +242,8 @@ inline void launch_pdl(const Context& cx, void (*k)(P...), dim3 grid, dim3 block
 void expand_uniform_dev(Context& cx, const uint8_t seed[32], int digit0, int ndigit, int limb0, int nlimb,
                         uint32_t tag, uint64_t* out, long long digit_stride);
 void ntt(const Context& cx, const LimbMap& mp, int npoly, bool inv, cudaStream_t st);
+// rescale by the last of l + 1 limbs, the dropped limbs already inverse-transformed in place (ntt.cu)
+void ntt_rescale(const Context& cx, uint64_t* a, long long stride, int l, uint64_t* y, cudaStream_t st);
 
 // ---- operations (engine.cu) ---------------------------------------------------------------
 // key switching of d (nl limbs, eval) -> (out0, out1) added into add0/add1 (may be null),

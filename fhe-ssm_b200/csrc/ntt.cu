@@ -87,10 +87,25 @@ __device__ __forceinline__ void stage16(uint64_t (&x)[16], uint64_t q, int h, TW
     else stage16<INV, 1>(x, q, tw);
 }
 
+// A forward transform with a fused prologue and epilogue (FUSE = true): the rescale of a
+// ciphertext.  The column pass reads, in place of its input limb i, the centred lift of the
+// dropped limb (coefficient form, src + poly * src_stride) modulo q_i; the row pass writes, in
+// place of the transformed lift y, the rescaled limb dst_i = (dst_i - y) * q_l^-1 (rs: [l][i][2],
+// q_l^-1 mod q_i with its Shoup companion).  The words equal k_rescale_lift -> NTT ->
+// k_rescale_final.
+struct NttFuse {
+    const uint64_t* src;
+    long long src_stride;
+    uint64_t* dst;
+    long long dst_stride;
+    const uint64_t* rs;
+    int l, L;
+};
+
 // ---- phase "col": stages with distance >= 256 ----------------------------------------
-template <int LOGN, bool INV>
+template <int LOGN, bool INV, bool FUSE = false>
 __global__ void __launch_bounds__(256, 3) k_ntt_col(LimbMap mp, const ulonglong2* __restrict__ tw2,
-                                                  const uint64_t* __restrict__ ninv) {
+                                                  const uint64_t* __restrict__ ninv, NttFuse fz) {
     pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
     pdl_trigger();
     constexpr int N = 1 << LOGN;
@@ -112,8 +127,19 @@ __global__ void __launch_bounds__(256, 3) k_ntt_col(LimbMap mp, const ulonglong2
     const int a2 = t / TC;               // part B: rows 16*a2 + k
     uint64_t x[16];
     if (!INV) {
+        if (FUSE) {   // centred lift of the dropped limb: v > q_l / 2 stands for v - q_l
+            const uint64_t* src = fz.src + (size_t)poly * fz.src_stride;
+            const ModConst mi = c_mod[m];
+            const uint64_t ql = c_mod[fz.l].q, qlm = reduce64(ql, mi);
 #pragma unroll
-        for (int k = 0; k < 16; k++) x[k] = a[(size_t)(g + G * k) * 256 + col];
+            for (int k = 0; k < 16; k++) {
+                const uint64_t v = src[(size_t)(g + G * k) * 256 + col];
+                x[k] = v > (ql >> 1) ? mod_sub(reduce64(v, mi), qlm, q) : reduce64(v, mi);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 16; k++) x[k] = a[(size_t)(g + G * k) * 256 + col];
+        }
         // part A: distances R/2 .. R/16 (register distance h = 8,4,2,1); twiddle 2^s + k/(2h)
 #pragma unroll
         for (int s = 0; s < 4; s++)
@@ -170,9 +196,9 @@ __global__ void __launch_bounds__(256, 3) k_ntt_col(LimbMap mp, const ulonglong2
 // rtab[bg][2^sp - 1 + j][r0] = Tab[2^(logN-4+sp) + bg * 2^(4+sp) + r0 * 2^sp + j], so a warp's
 // load covers consecutive pairs.
 constexpr int kRowTab = 240;   // pairs per 256-word block: 16 threads x (1 + 2 + 4 + 8)
-template <int LOGN, bool INV>
+template <int LOGN, bool INV, bool FUSE = false>
 __global__ void __launch_bounds__(256, 3) k_ntt_row(LimbMap mp, const ulonglong2* __restrict__ tw2,
-                                                  const ulonglong2* __restrict__ rtab) {
+                                                  const ulonglong2* __restrict__ rtab, NttFuse fz) {
     pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
     pdl_trigger();
     constexpr int N = 1 << LOGN;
@@ -213,8 +239,19 @@ __global__ void __launch_bounds__(256, 3) k_ntt_row(LimbMap mp, const ulonglong2
 #pragma unroll
         for (int k = 0; k < 16; k++) sB[k] = canon4(x[k], q);
         __syncthreads();
+        if (FUSE) {   // the rescaled limb in place of the transformed lift
+            uint64_t* d = fz.dst + (size_t)poly * fz.dst_stride + (size_t)limb * N + (size_t)blockIdx.x * 4096;
+            const uint64_t* w = fz.rs + ((size_t)fz.l * fz.L + m) * 2;
+            const uint64_t w0 = w[0], w1 = w[1];
 #pragma unroll
-        for (int k = 0; k < 16; k++) a[b * 256 + r0 + 16 * k] = sA[17 * k];
+            for (int k = 0; k < 16; k++) {
+                uint64_t* p = d + b * 256 + r0 + 16 * k;
+                *p = mul_shoup(mod_sub(*p, sA[17 * k], q), w0, w1, q);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 16; k++) a[b * 256 + r0 + 16 * k] = sA[17 * k];
+        }
     } else {
 #pragma unroll
         for (int k = 0; k < 16; k++) sA[17 * k] = a[b * 256 + r0 + 16 * k];
@@ -243,11 +280,15 @@ static void launch_ntt(const Context& cx, const LimbMap& mp, int count, bool inv
     constexpr int R = N >> 8;
     dim3 gcol(R / 16, count), grow(N / 4096, count);
     if (!inv) {
-        launch_pdl(cx, k_ntt_col<LOGN, false>, gcol, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_tw2, cx.d_ninv);
-        launch_pdl(cx, k_ntt_row<LOGN, false>, grow, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_tw2, (const ulonglong2*)cx.d_twrow);
+        launch_pdl(cx, k_ntt_col<LOGN, false>, gcol, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_tw2, cx.d_ninv,
+                   NttFuse{});
+        launch_pdl(cx, k_ntt_row<LOGN, false>, grow, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_tw2,
+                   (const ulonglong2*)cx.d_twrow, NttFuse{});
     } else {
-        launch_pdl(cx, k_ntt_row<LOGN, true>, grow, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_itw2, (const ulonglong2*)cx.d_itwrow);
-        launch_pdl(cx, k_ntt_col<LOGN, true>, gcol, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_itw2, cx.d_ninv);
+        launch_pdl(cx, k_ntt_row<LOGN, true>, grow, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_itw2,
+                   (const ulonglong2*)cx.d_itwrow, NttFuse{});
+        launch_pdl(cx, k_ntt_col<LOGN, true>, gcol, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_itw2, cx.d_ninv,
+                   NttFuse{});
     }
 }
 
@@ -272,6 +313,34 @@ void ntt(const Context& cx, const LimbMap& mp, int npoly, bool inv, cudaStream_t
         case 15: launch_ntt<15>(cx, mp, count, inv, st); break;
         case 16: launch_ntt<16>(cx, mp, count, inv, st); break;
         default: throw Error("ntt: logN must be in [12, 16]");
+    }
+    CUDA_CHECK(cudaGetLastError());
+    cx.launches += 2;
+}
+
+template <int LOGN>
+static void launch_ntt_rescale(const Context& cx, const LimbMap& mp, int count, const NttFuse& fz, cudaStream_t st) {
+    constexpr int N = 1 << LOGN;
+    constexpr int R = N >> 8;
+    launch_pdl(cx, k_ntt_col<LOGN, false, true>, dim3(R / 16, count), dim3(256), 0, st, mp,
+               (const ulonglong2*)cx.d_tw2, cx.d_ninv, fz);
+    launch_pdl(cx, k_ntt_row<LOGN, false, true>, dim3(N / 4096, count), dim3(256), 0, st, mp,
+               (const ulonglong2*)cx.d_tw2, (const ulonglong2*)cx.d_twrow, fz);
+}
+
+// The rescale of a ciphertext with nl = l + 1 limbs, past the inverse transform of its dropped
+// limb (in place, coefficient form): its limbs 0..l-1 become (a_i - lift_i(a_l)) q_l^-1, the lift's
+// transform held in y ([2][l][N] scratch).  Two launches instead of lift, transform and final.
+void ntt_rescale(const Context& cx, uint64_t* a, long long stride, int l, uint64_t* y, cudaStream_t st) {
+    if (cx.logN < 13) throw Error("ntt_rescale: logN must be >= 13", -1);
+    LimbMap mp = cx.qmap(y, l, (long long)l * cx.N);
+    NttFuse fz{a + (size_t)l * cx.N, stride, a, stride, cx.d_rs, l, cx.L};
+    switch (cx.logN) {
+        case 13: launch_ntt_rescale<13>(cx, mp, 2 * l, fz, st); break;
+        case 14: launch_ntt_rescale<14>(cx, mp, 2 * l, fz, st); break;
+        case 15: launch_ntt_rescale<15>(cx, mp, 2 * l, fz, st); break;
+        case 16: launch_ntt_rescale<16>(cx, mp, 2 * l, fz, st); break;
+        default: throw Error("ntt_rescale: logN must be in [13, 16]");
     }
     CUDA_CHECK(cudaGetLastError());
     cx.launches += 2;
