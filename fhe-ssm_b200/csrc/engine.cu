@@ -11,6 +11,7 @@
 #include <mutex>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <cstring>
 
@@ -212,6 +213,8 @@ Context::Context(const Params& p) : prm(p) {
         ninv[2 * m] = ni; ninv[2 * m + 1] = shoup_of(ni, q);
     }
     activate();
+    // FHESSM_NTT_CLUSTER=0/1 overrides the default transform path at N = 2^16 (tuning and A/B runs)
+    if (const char* e = std::getenv("FHESSM_NTT_CLUSTER")) ntt_cluster = std::atoi(e) != 0;
     d_tw = dev_upload(tw); d_twp = dev_upload(twp); d_itw = dev_upload(itw); d_itwp = dev_upload(itwp);
     {
         std::vector<uint64_t> f(2 * tw.size()), v(2 * itw.size());

@@ -129,6 +129,7 @@ struct Context {
     unsigned int* d_err = nullptr;   // set by a kernel whose bounded wait ran out (checked at syncs)
     int use_tc = 1;                  // BSGS products on the tensor cores (tcgen05) where the shape allows
     int use_pdl = 1;                 // programmatic dependent launch for the hot kernels (launch_pdl)
+    int ntt_cluster = 0;             // N = 2^16: one cluster launch per transform (ntt.cu, k_ntt_cluster)
     int merged_rescale = 1;          // circuit products: ModDown and rescale in one division by P q_l
     // BSGS plaintext cache (the reference's --cache-diags, gpu_real_model.cu:1647-1652, off by
     // default as there): a plan keeps the plaintext words of its last call while at least

@@ -274,6 +274,159 @@ __global__ void __launch_bounds__(256, 3) k_ntt_row(LimbMap mp, const ulonglong2
     }
 }
 
+// ---- one launch per transform at N = 2^16: a cluster of 8 CTAs per limb ------------------
+// The limb is a 256 x 256 row-major matrix.  CTA k of the cluster (512 threads, 16 words each)
+// owns columns [32k, 32k + 32) for the 8 stages with distance >= 256 (column transforms) and rows
+// [32k, 32k + 32) for the last 8 (row transforms); between the two the CTAs read each other's
+// blocks from shared memory across the cluster (distributed shared memory), so the limb crosses
+// HBM once in each direction and the transform is one launch.  Butterflies, twiddle indices and
+// value ranges are those of k_ntt_col / k_ntt_row (the words are identical).
+//   forward: load columns (layout A: rows g + 16m) -> stages 0-3 -> smem -> layout B (rows
+//            16 a2 + k) -> stages 4-7 -> own smem; cluster barrier; read rows from the 8 CTAs
+//            (layout C: columns u + 16m) -> cluster barrier -> stages 8-11 -> smem (swizzled) ->
+//            layout D (columns 16 j + e) -> stages 12-15 -> smem -> layout C -> store rows.
+//   inverse: the same steps in reverse order with the inverse tables, then * N^-1.
+// Shared memory: one 80 KB buffer: [256][40] words for the column phase (row stride 40 = 8 mod 16:
+// the two rows a warp touches in a cross-CTA read fall on different banks), [32][264] for the row
+// phase with the word of column c at c ^ ((c >> 4) & 15) (conflict-free for both layouts).
+constexpr int kClC = 8, kClT = 512, kClP1 = 40, kClP2 = 264;
+constexpr size_t kClSmem = (size_t)256 * kClP1 * 8;   // >= 32 * kClP2 * 8
+
+__device__ __forceinline__ void cl_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint64_t cl_ld(uint32_t laddr, uint32_t rank) {
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(laddr), "r"(rank));
+    uint64_t v;
+    asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(ra) : "memory");
+    return v;
+}
+__device__ __forceinline__ int cl_swz(int c) { return c ^ ((c >> 4) & 15); }
+
+template <bool INV>
+__global__ void __cluster_dims__(kClC, 1, 1) __launch_bounds__(kClT, 1)
+    k_ntt_cluster(LimbMap mp, const ulonglong2* __restrict__ tw2, const ulonglong2* __restrict__ rtab,
+                  const uint64_t* __restrict__ ninv) {
+    pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
+    pdl_trigger();
+    constexpr int N = 1 << 16;
+    extern __shared__ __align__(16) uint64_t cs[];
+    const int y = blockIdx.y;
+    const int poly = y / mp.nl, limb = y % mp.nl;
+    if (limb_skipped(mp, poly, limb)) return;   // uniform over the cluster: no barrier is reached
+    const int m = mp.mod(limb);
+    uint64_t* a = mp.base + (size_t)poly * mp.poly_stride + (size_t)limb * N;
+    const uint64_t q = c_mod[m].q;
+    const ulonglong2* T2 = tw2 + (size_t)m * N;
+    const uint64_t pol = tw_policy();
+    const int k = blockIdx.x;                    // rank in the cluster
+    const int t = threadIdx.x;
+    const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(cs);
+    // layout A / B (column phase): column 32k + cc
+    const int cc = t & 31, g = t >> 5;           // A: rows g + 16 mm; B: rows 16 g + kk
+    // layout C / D (row phase): row 32k + rr
+    const int rr = t >> 4, u = t & 15;           // C: columns u + 16 mm; D: columns 16 u + e
+    const int r = 32 * k + rr;
+    const ulonglong2* RB = rtab + ((size_t)m * (N >> 8) + r) * kRowTab + u;
+    uint64_t x[16];
+    if (!INV) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) x[i] = a[(size_t)(g + 16 * i) * 256 + 32 * k + cc];
+#pragma unroll
+        for (int s = 0; s < 4; s++)
+            stage16<false>(x, q, 8 >> s, [&](int j) { return ld_tw(T2 + (1 << s) + j, pol); });
+#pragma unroll
+        for (int i = 0; i < 16; i++) cs[(g + 16 * i) * kClP1 + cc] = x[i];
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 16; i++) x[i] = cs[(16 * g + i) * kClP1 + cc];
+#pragma unroll
+        for (int h = 8, s = 4; h >= 1; h >>= 1, s++)
+            stage16<false>(x, q, h, [&](int j) { return ld_tw(T2 + (1 << s) + g * (8 / h) + j, pol); });
+#pragma unroll
+        for (int i = 0; i < 16; i++) cs[(16 * g + i) * kClP1 + cc] = x[i];   // own rows only: no barrier
+        cl_sync();
+        // row r, columns u + 16 i: CTA i >> 1 holds them at [r][u + 16 (i & 1)]
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+            x[i] = cl_ld(sbase + (uint32_t)((r * kClP1 + u + 16 * (i & 1)) * 8), (uint32_t)(i >> 1));
+        cl_sync();   // every CTA has read what it needs: the buffer is free
+#pragma unroll
+        for (int s = 0; s < 4; s++)
+            stage16<false>(x, q, 8 >> s, [&](int j) { return ld_tw(T2 + (1 << (8 + s)) + (r << s) + j, pol); });
+#pragma unroll
+        for (int i = 0; i < 16; i++) cs[rr * kClP2 + cl_swz(u + 16 * i)] = x[i];
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 16; i++) x[i] = cs[rr * kClP2 + cl_swz(16 * u + i)];
+#pragma unroll
+        for (int sp = 0; sp < 4; sp++)
+            stage16<false>(x, q, 8 >> sp, [&](int j) { return ld_tw(RB + ((1 << sp) - 1 + j) * 16, pol); });
+#pragma unroll
+        for (int i = 0; i < 16; i++) cs[rr * kClP2 + cl_swz(16 * u + i)] = canon4(x[i], q);   // own words
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 16; i++) a[(size_t)r * 256 + u + 16 * i] = cs[rr * kClP2 + cl_swz(u + 16 * i)];
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; i++) cs[rr * kClP2 + cl_swz(u + 16 * i)] = a[(size_t)r * 256 + u + 16 * i];
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 16; i++) x[i] = cs[rr * kClP2 + cl_swz(16 * u + i)];
+#pragma unroll
+        for (int sp = 3; sp >= 0; sp--)
+            stage16<true>(x, q, 8 >> sp, [&](int j) { return ld_tw(RB + ((1 << sp) - 1 + j) * 16, pol); });
+#pragma unroll
+        for (int i = 0; i < 16; i++) cs[rr * kClP2 + cl_swz(16 * u + i)] = x[i];   // own words
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 16; i++) x[i] = cs[rr * kClP2 + cl_swz(u + 16 * i)];
+#pragma unroll
+        for (int s = 3; s >= 0; s--)
+            stage16<true>(x, q, 8 >> s, [&](int j) { return ld_tw(T2 + (1 << (8 + s)) + (r << s) + j, pol); });
+        // the row block as [32][264] (unswizzled) for the other CTAs' column reads
+        __syncthreads();   // every thread is done reading the swizzled block
+#pragma unroll
+        for (int i = 0; i < 16; i++) cs[rr * kClP2 + u + 16 * i] = x[i];
+        cl_sync();
+        // column 32k + cc, rows 16 g + i: CTA g >> 1 holds them at [(16 g + i) & 31][32k + cc]
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+            x[i] = cl_ld(sbase + (uint32_t)((((16 * g + i) & 31) * kClP2 + 32 * k + cc) * 8), (uint32_t)(g >> 1));
+        cl_sync();
+#pragma unroll
+        for (int h = 1, s = 7; h <= 8; h <<= 1, s--)
+            stage16<true>(x, q, h, [&](int j) { return ld_tw(T2 + (1 << s) + g * (8 / h) + j, pol); });
+#pragma unroll
+        for (int i = 0; i < 16; i++) cs[(16 * g + i) * kClP1 + cc] = x[i];
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 16; i++) x[i] = cs[(g + 16 * i) * kClP1 + cc];
+#pragma unroll
+        for (int s = 3; s >= 0; s--)
+            stage16<true>(x, q, 8 >> s, [&](int j) { return ld_tw(T2 + (1 << s) + j, pol); });
+        const uint64_t ni = ninv[2 * m], nip = ninv[2 * m + 1];
+#pragma unroll
+        for (int i = 0; i < 16; i++) a[(size_t)(g + 16 * i) * 256 + 32 * k + cc] = mul_shoup(x[i], ni, nip, q);
+    }
+}
+
+static void launch_ntt_cluster(const Context& cx, const LimbMap& mp, int count, bool inv, cudaStream_t st) {
+    auto kern = inv ? k_ntt_cluster<true> : k_ntt_cluster<false>;
+    static bool attr_set[2] = {false, false};
+    if (!attr_set[inv ? 1 : 0]) {
+        CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kClSmem));
+        attr_set[inv ? 1 : 0] = true;
+    }
+    if (inv)
+        launch_pdl(cx, k_ntt_cluster<true>, dim3(kClC, count), dim3(kClT), kClSmem, st, mp,
+                   (const ulonglong2*)cx.d_itw2, (const ulonglong2*)cx.d_itwrow, cx.d_ninv);
+    else
+        launch_pdl(cx, k_ntt_cluster<false>, dim3(kClC, count), dim3(kClT), kClSmem, st, mp,
+                   (const ulonglong2*)cx.d_tw2, (const ulonglong2*)cx.d_twrow, cx.d_ninv);
+}
+
 template <int LOGN>
 static void launch_ntt(const Context& cx, const LimbMap& mp, int count, bool inv, cudaStream_t st) {
     constexpr int N = 1 << LOGN;
@@ -311,7 +464,15 @@ void ntt(const Context& cx, const LimbMap& mp, int npoly, bool inv, cudaStream_t
         case 13: launch_ntt<13>(cx, mp, count, inv, st); break;
         case 14: launch_ntt<14>(cx, mp, count, inv, st); break;
         case 15: launch_ntt<15>(cx, mp, count, inv, st); break;
-        case 16: launch_ntt<16>(cx, mp, count, inv, st); break;
+        case 16:
+            if (cx.ntt_cluster) {
+                launch_ntt_cluster(cx, mp, count, inv, st);
+                CUDA_CHECK(cudaGetLastError());
+                cx.launches += 1;
+                return;
+            }
+            launch_ntt<16>(cx, mp, count, inv, st);
+            break;
         default: throw Error("ntt: logN must be in [12, 16]");
     }
     CUDA_CHECK(cudaGetLastError());
