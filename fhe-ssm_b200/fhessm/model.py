@@ -151,11 +151,17 @@ def rsqrt_iters_for(a, b, lo, hi, tol=1e-4, cap=14):
     raise ValueError("Newton rsqrt did not converge")
 
 
-def calibrate_seeds(cfg, w, steps=2, lanes=64, seed=7, tol=1e-4, margin=2.0, inputs=None):
+def calibrate_seeds(cfg, w, steps=2, lanes=64, seed=7, tol=1e-4, margin=2.0, inputs=None, ms_margin=None):
     """Per-site (a, b, iters) from the ranges of mean(x^2)+eps over a calibration run: the
-    linear seed is fitted on [m / margin, M * margin] and the iteration count verified there
-    (the reference uses [0.8 m, 1.25 M]; a wider window keeps conversations whose state drifts
-    past the calibration tokens inside the Newton basin, at the cost of about one iteration).
+    linear seed is fitted on [m / lo, M * hi] with (lo, hi) = ms_margin (default (margin,
+    margin)) and the iteration count verified there (the reference uses [0.8 m, 1.25 M]; a
+    wider window keeps conversations whose state drifts past the calibration tokens inside the
+    Newton basin, at the cost of about one iteration).  The tails are one-sided: conversations
+    outside the calibration range reach mean squares several times the calibrated maximum
+    but stay within about 10 % of the minimum, so ms_margin = (1.25, 4) covers them for a few
+    iterations more per pass than a symmetric window would.  A lane outside the basin is
+    not refreshed by the Newton steps and its output is lost.  The bootstrap gains use
+    [m / margin, M * margin] in either case.
     The run feeds embeddings of random tokens, or the given input batches (lanes, d) in turn."""
     rng = np.random.default_rng(seed)
     cap, state = {}, None
@@ -169,11 +175,12 @@ def calibrate_seeds(cfg, w, steps=2, lanes=64, seed=7, tol=1e-4, margin=2.0, inp
             continue
         arr = np.array(rows)
         m, M = float(arr[:, 0].min()), float(arr[:, 1].max())
-        lo, hi = m / margin, M * margin
+        mlo, mhi = ms_margin if ms_margin is not None else (margin, margin)
+        lo, hi = m / mlo, M * mhi
         a, b = linear_rsqrt_seed(lo, hi)
         seeds[tag] = (a, b, rsqrt_iters_for(a, b, lo, hi, tol))
-        seeds["gain:" + tag + ".ms"] = boot_gain(hi)
-        seeds["gain:" + tag + ".y"] = boot_gain(1.0 / np.sqrt(lo))
+        seeds["gain:" + tag + ".ms"] = boot_gain(M * margin)
+        seeds["gain:" + tag + ".y"] = boot_gain(1.0 / np.sqrt(m / margin))
     return seeds
 
 
