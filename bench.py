@@ -297,8 +297,11 @@ def run_model(args, ws, rank, local):
     t_setup = time.time()
     w = synthetic_weights(cfg, seed=1234)
     # Newton seeds and bootstrap gains from 6 steps of 512 calibration conversations (not the
-    # timed ones), with the Newton window stretched 4x above the largest mean square seen
-    seeds = calibrate_seeds(cfg, w, steps=6, lanes=CAL_LANES, ms_margin=(1.25, 4.0))
+    # timed ones).  The Newton window reaches 3x above the largest mean square seen and 1.25x
+    # below the smallest, at a tolerance of 3e-4: over 32 held-out packs of 64 conversations
+    # (12 steps each) the worst Newton error is 9e-5, at two more iterations per pass than a
+    # 64-conversation calibration whose window misses some of them
+    seeds = calibrate_seeds(cfg, w, steps=6, lanes=CAL_LANES, tol=3e-4, ms_margin=(1.25, 3.0))
     cx = fhessm.CryptoContext(device=local, **MODEL_CTX)
     key_seed, tok_seed = pack_seeds(rank)
     cx.KeyGen(seed=key_seed)

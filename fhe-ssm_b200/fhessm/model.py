@@ -157,10 +157,11 @@ def calibrate_seeds(cfg, w, steps=2, lanes=64, seed=7, tol=1e-4, margin=2.0, inp
     margin)) and the iteration count verified there (the reference uses [0.8 m, 1.25 M]; a
     wider window keeps conversations whose state drifts past the calibration tokens inside the
     Newton basin, at the cost of about one iteration).  The tails are one-sided: conversations
-    outside the calibration range reach mean squares several times the calibrated maximum
-    but stay within about 10 % of the minimum, so ms_margin = (1.25, 4) covers them for a few
-    iterations more per pass than a symmetric window would.  A lane outside the basin is
-    not refreshed by the Newton steps and its output is lost.  The bootstrap gains use
+    outside the calibration range reach mean squares a few times the calibrated maximum but
+    stay within about 10 % of the minimum, so an asymmetric ms_margin such as (1.25, 3) covers
+    them at about the iteration count of the symmetric (2, 2).  Beyond the window's top the
+    linear seed falls towards zero and Newton's iteration, which multiplies a small relative
+    seed by only about 1.5 per step there, leaves that lane's norm wrong.  The bootstrap gains use
     [m / margin, M * margin] in either case.
     The run feeds embeddings of random tokens, or the given input batches (lanes, d) in turn."""
     rng = np.random.default_rng(seed)
