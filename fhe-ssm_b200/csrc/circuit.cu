@@ -11,6 +11,7 @@
 //     constant product + rescale (one level, whatever the gap);
 //   * constants are multiplied as exact integers; rounding is absorbed into the tracked scale.
 #include <cmath>
+#include <tuple>
 
 #include "engine.h"
 
@@ -245,123 +246,6 @@ __global__ void __launch_bounds__(256) k_lincomb(const LinArgs a, uint64_t* out,
     out[(size_t)c * ostride + (size_t)i * N + x] = reduce_lazy16(s, q);
 }
 
-struct ChebEval {
-    Context& cx;
-    int bs;
-    std::vector<Ciphertext> T;         // T[i], i < bs (T[0] unused), aligned to one level
-    std::map<int, Ciphertext> giant;   // T_{2^m}, 2^m >= bs
-
-    ChebEval(Context& c, const Ciphertext& x, int degree) : cx(c) {
-        bs = 1;
-        while (bs * bs < degree + 1) bs <<= 1;   // babies up to ~sqrt(deg)
-        if (bs < 2) bs = 2;
-        T.resize(bs);
-        T[1] = ct_copy(cx, x);
-        for (int i = 2; i < bs; i++) {
-            // T_i = 2 T_a T_b - T_{a-b}, a = ceil(i/2), b = floor(i/2)
-            const int a = (i + 1) / 2, b = i / 2;
-            Ciphertext p;
-            mul_rescale(cx, T[a], T[b], p);
-            if (a == b) {
-                Ciphertext one;
-                mul_integer_add_const(cx, p, 2, -1.0, one);
-                T[i] = std::move(one);
-            } else {
-                mul_integer(cx, p, 2, p);
-                Ciphertext d;
-                sub_any(cx, p, T[a - b], d);
-                T[i] = std::move(d);
-            }
-        }
-        // giants T_{bs}, T_{2bs}, ...
-        int M = bs;
-        Ciphertext g;
-        {
-            const int a = bs / 2;
-            Ciphertext p;
-            mul_rescale(cx, T[a], T[a], p);
-            mul_integer_add_const(cx, p, 2, -1.0, g);
-        }
-        giant[M] = ct_copy(cx, g);
-        while (2 * M <= degree) {
-            Ciphertext p;
-            mul_rescale(cx, giant[M], giant[M], p);
-            Ciphertext n2;
-            mul_integer_add_const(cx, p, 2, -1.0, n2);
-            M *= 2;
-            giant[M] = std::move(n2);
-        }
-        // align babies to the lowest baby level (their scales may differ: the leaf products
-        // pick one integer factor per baby)
-        int lo = T[1].nl;
-        for (int i = 1; i < bs; i++) lo = std::min(lo, T[i].nl);
-        for (int i = 1; i < bs; i++)
-            if (T[i].nl > lo) align(cx, T[i], lo, 0);
-    }
-
-    // leaf: sum_{i < bs} c_i T_i  (one level: integer products + one rescale).  Baby i is
-    // multiplied by round(c_i * S_i), S_i = target q / scale_i, so every term carries the
-    // common scale target * q before the rescale.
-    Ciphertext leaf(const std::vector<double>& c) {
-        const int nl = T[1].nl;
-        const double target = canon(cx, nl - 1);
-        const double tq = target * (double)cx.mods[nl - 1];
-        LinArgs la{};
-        for (int i = 1; i < (int)c.size() && i < bs; i++) {
-            if (c[i] == 0.0) continue;
-            if (la.nt == kLinMax) throw Error("chebyshev: too many baby terms in one leaf", -1);
-            const int t = la.nt++;
-            la.in[t] = T[i].c(0);
-            la.stride[t] = (long long)T[i].stride;
-            limb_residues(cx, std::floor((long double)c[i] * (long double)(tq / T[i].scale) + 0.5L), nl, la.w[t]);
-            for (int l = 0; l < nl; l++) la.wp[t][l] = shoup_of(la.w[t][l], cx.mods[l]);
-        }
-        if (la.nt == 0) {   // constant-only leaf: 0 * T_1 keeps a valid ciphertext
-            la.nt = 1;
-            la.in[0] = T[1].c(0);
-            la.stride[0] = (long long)T[1].stride;
-        }
-        Ciphertext acc = ct_alloc(cx, nl);
-        {
-            ProfScope ps(cx, "lincomb", 8.0 * cx.N * nl * 2 * (la.nt + 1));
-            k_lincomb<<<dim3(cx.N / 256, nl, 2), 256, 0, cx.stream>>>(la, acc.c(0), (long long)acc.stride, cx.logN);
-            CUDA_CHECK(cudaGetLastError());
-            cx.launches++;
-        }
-        acc.scale = tq;
-        ct_rescale(cx, acc);
-        acc.scale = target;
-        if (!c.empty() && c[0] != 0.0) {
-            Ciphertext u;
-            ct_add_const(cx, acc, c[0], u);
-            acc = std::move(u);
-        }
-        return acc;
-    }
-
-    Ciphertext eval(std::vector<double> c) {
-        int deg = (int)c.size() - 1;
-        while (deg > 0 && c[deg] == 0.0) deg--;
-        c.resize(deg + 1);
-        if (deg < bs) return leaf(c);
-        int M = bs;
-        while (2 * M <= deg) M *= 2;
-        // p = q T_M + r
-        std::vector<double> q(deg - M + 1), r(c.begin(), c.begin() + M);
-        q[0] = c[M];
-        for (int i = M + 1; i <= deg; i++) {
-            q[i - M] = 2 * c[i];
-            r[2 * M - i] -= c[i];
-        }
-        Ciphertext qv = eval(q), rv = eval(r);
-        Ciphertext prod;
-        mul_rescale(cx, qv, giant[M], prod);
-        Ciphertext out;
-        add_any(cx, prod, rv, out);
-        return out;
-    }
-};
-
 // K products a[k] * b[k] relinearised and rescaled together (ct_mul_relin_rescale_n); operands
 // of unequal levels are aligned first.  Falls back to one product at a time when the batch
 // does not share a level.
@@ -389,14 +273,40 @@ void mul_rescale_n(Context& cx, const Ciphertext* const* a, const Ciphertext* co
     ct_mul_relin_rescale_n(cx, A.data(), B.data(), K, out);
 }
 
-// The Chebyshev evaluator of ChebEval over K ciphertexts at once (same level and scale, same
+// Chebyshev series sum_i c_i T_i(x) over K ciphertexts at once (same level and scale, same
 // polynomial): every ciphertext product of the K evaluations is one batched product.
+// Babies T_1 .. T_{bs-1} by T_i = 2 T_a T_b - T_{a-b} (a = ceil(i/2), b = floor(i/2)), giants
+// T_{bs}, T_{2bs}, ... by doubling, and the series split recursively as p = q T_M + r down to
+// leaves of degree < bs.
+//   * A product or a difference of operands at two levels reads the higher one brought down to
+//     the lower level (align: one constant product and rescale).  Such an aligned copy of a baby
+//     or a giant is made once per level and kept (T_1 serves T_3, T_5 and T_7, a giant both
+//     halves of the series below it).
+//   * A leaf is one integer-weighted sum and one rescale.  Its babies are not aligned: baby i
+//     enters through its first nl limbs (dropping limbs is free) with the integer weight
+//     round(c_i tq / scale_i), so every term carries the common scale tq before the rescale.
 struct ChebEvalN {
     Context& cx;
-    int bs, K;
+    int bs, K, lo = 0;
     std::vector<std::vector<Ciphertext>> T;         // T[i][k]
     std::map<int, std::vector<Ciphertext>> giant;   // T_{2^m}[k]
+    std::map<std::tuple<const void*, int, double>, std::vector<Ciphertext>> memo;   // aligned copies
 
+    // src (a baby or a giant of this evaluator) at nl limbs and scale `target`: src itself, or
+    // its aligned copy, made on first use
+    const std::vector<Ciphertext>& at(const std::vector<Ciphertext>& src, int nl, double target) {
+        const double r = src[0].scale / target;
+        if (src[0].nl == nl && r > 1 - 1e-9 && r < 1 + 1e-9) return src;
+        const auto key = std::make_tuple((const void*)&src, nl, target);
+        auto it = memo.find(key);
+        if (it != memo.end()) return it->second;
+        std::vector<Ciphertext> v(K);
+        for (int k = 0; k < K; k++) {
+            v[k] = ct_copy(cx, src[k]);
+            align(cx, v[k], nl, target);
+        }
+        return memo.emplace(key, std::move(v)).first->second;
+    }
     void prod(const std::vector<Ciphertext>& a, const std::vector<Ciphertext>& b, std::vector<Ciphertext>& o) {
         std::vector<const Ciphertext*> pa(K), pb(K);
         for (int k = 0; k < K; k++) { pa[k] = &a[k]; pb[k] = &b[k]; }
@@ -404,25 +314,32 @@ struct ChebEvalN {
         o.resize(K);
         mul_rescale_n(cx, pa.data(), pb.data(), K, o.data());
     }
+    // a * b for two persistent operands (babies, giants), the higher one read at the lower level
+    void prod_at(const std::vector<Ciphertext>& a, const std::vector<Ciphertext>& b, std::vector<Ciphertext>& o) {
+        if (a[0].nl == b[0].nl) prod(a, b, o);
+        else if (a[0].nl > b[0].nl) prod(at(a, b[0].nl, canon(cx, b[0].nl)), b, o);
+        else prod(a, at(b, a[0].nl, canon(cx, a[0].nl)), o);
+    }
     // 2 a b - c (c = null: 2 a b - 1)
     std::vector<Ciphertext> cheb_step(const std::vector<Ciphertext>& a, const std::vector<Ciphertext>& b,
                                       const std::vector<Ciphertext>* c) {
         std::vector<Ciphertext> p;
-        prod(a, b, p);
+        prod_at(a, b, p);
         std::vector<Ciphertext> r(K);
+        if (!c) {
+            for (int k = 0; k < K; k++) mul_integer_add_const(cx, p[k], 2, -1.0, r[k]);
+            return r;
+        }
+        const std::vector<Ciphertext>& ca = at(*c, p[0].nl, p[0].scale);
         for (int k = 0; k < K; k++) {
-            if (c) {
-                mul_integer(cx, p[k], 2, p[k]);
-                sub_any(cx, p[k], (*c)[k], r[k]);
-            } else {
-                mul_integer_add_const(cx, p[k], 2, -1.0, r[k]);
-            }
+            mul_integer(cx, p[k], 2, p[k]);
+            ct_sub(cx, p[k], ca[k], r[k]);
         }
         return r;
     }
     ChebEvalN(Context& c, const Ciphertext* const* x, int K_, int degree) : cx(c), K(K_) {
         bs = 1;
-        while (bs * bs < degree + 1) bs <<= 1;
+        while (bs * bs < degree + 1) bs <<= 1;   // babies up to ~sqrt(deg)
         if (bs < 2) bs = 2;
         T.resize(bs);
         T[1].resize(K);
@@ -437,14 +354,11 @@ struct ChebEvalN {
             giant[2 * M] = cheb_step(giant[M], giant[M], nullptr);
             M *= 2;
         }
-        int lo = T[1][0].nl;
+        lo = T[1][0].nl;
         for (int i = 1; i < bs; i++) lo = std::min(lo, T[i][0].nl);
-        for (int i = 1; i < bs; i++)
-            if (T[i][0].nl > lo)
-                for (int k = 0; k < K; k++) align(cx, T[i][k], lo, 0);
     }
     std::vector<Ciphertext> leaf(const std::vector<double>& c) {
-        const int nl = T[1][0].nl;
+        const int nl = lo;
         const double target = canon(cx, nl - 1);
         const double tq = target * (double)cx.mods[nl - 1];
         std::vector<Ciphertext> out(K);
@@ -458,7 +372,7 @@ struct ChebEvalN {
             limb_residues(cx, std::floor((long double)c[i] * (long double)(tq / T[i][0].scale) + 0.5L), nl, la.w[t]);
             for (int l = 0; l < nl; l++) la.wp[t][l] = shoup_of(la.w[t][l], cx.mods[l]);
         }
-        if (la.nt == 0) { la.nt = 1; terms.push_back(1); }
+        if (la.nt == 0) { la.nt = 1; terms.push_back(1); }   // constant-only leaf: 0 * T_1
         for (int k = 0; k < K; k++) {
             for (int t = 0; t < la.nt; t++) {
                 la.in[t] = T[terms[t]][k].c(0);
@@ -491,6 +405,7 @@ struct ChebEvalN {
         if (deg < bs) return leaf(c);
         int M = bs;
         while (2 * M <= deg) M *= 2;
+        // p = q T_M + r
         std::vector<double> q(deg - M + 1), r(c.begin(), c.begin() + M);
         q[0] = c[M];
         for (int i = M + 1; i <= deg; i++) {
@@ -498,16 +413,24 @@ struct ChebEvalN {
             r[2 * M - i] -= c[i];
         }
         std::vector<Ciphertext> qv = eval(q), rv = eval(r), pr;
-        prod(qv, giant[M], pr);
+        if (qv[0].nl <= giant[M][0].nl) {
+            prod(qv, at(giant[M], qv[0].nl, qv[0].scale), pr);
+        } else {   // never for the trees of cheb_depth (a leaf sits below every giant it meets)
+            for (int k = 0; k < K; k++) align(cx, qv[k], giant[M][0].nl, giant[M][0].scale);
+            prod(qv, giant[M], pr);
+        }
         std::vector<Ciphertext> out(K);
-        for (int k = 0; k < K; k++) add_any(cx, pr[k], rv[k], out[k]);
+        for (int k = 0; k < K; k++) {
+            if (rv[k].nl > pr[k].nl) align(cx, rv[k], pr[k].nl, pr[k].scale);
+            if (rv[k].nl == pr[k].nl) ct_add(cx, pr[k], rv[k], out[k]);
+            else add_any(cx, pr[k], rv[k], out[k]);
+        }
         return out;
     }
 };
 
-// Levels consumed by ChebEval / ChebEvalN on a canonical-scale input: the same tree on depths
-// (a product is one level below its deeper operand; babies are aligned to the deepest baby;
-// a leaf is one level below the babies).
+// Levels consumed by ChebEvalN on a canonical-scale input: the same tree on depths (a product
+// is one level below its deeper operand; a leaf is one level below the deepest baby).
 static int cheb_depth_rec(std::vector<double> c, int bs, int lo, const std::map<int, int>& gd) {
     int deg = (int)c.size() - 1;
     while (deg > 0 && c[deg] == 0.0) deg--;
@@ -561,15 +484,8 @@ void cheb_eval_n(Context& cx, const Ciphertext* const* x, int K, const std::vect
 }
 
 void cheb_eval(Context& cx, const Ciphertext& x, const std::vector<double>& coeffs, Ciphertext& out) {
-    if (x.scale / canon(cx, x.nl) > 1 + 1e-9 || x.scale / canon(cx, x.nl) < 1 - 1e-9) {
-        Ciphertext y = ct_copy(cx, x);
-        align(cx, y, y.nl - 1, 0);
-        ChebEval ev(cx, y, (int)coeffs.size() - 1);
-        out = ev.eval(coeffs);
-        return;
-    }
-    ChebEval ev(cx, x, (int)coeffs.size() - 1);
-    out = ev.eval(coeffs);
+    const Ciphertext* px[1] = {&x};
+    cheb_eval_n(cx, px, 1, coeffs, &out);
 }
 
 // sum_i c_i (.) x^i with per-slot coefficient vectors c_i (n slots each, repeated), power
