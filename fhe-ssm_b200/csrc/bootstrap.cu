@@ -404,7 +404,13 @@ void bootstrap_setup(Context& cx, double B, int deg, int r) {
     nl = nl_em - cheb_depth(bc->cheb) - bc->r;
     // SlotToCoeff is built on the first bootstrap, when the (data-independent) scale of the
     // EvalMod output is known; its first level absorbs that scale and q0 / (2 pi Delta_in)
-    bc->delta_in = canon(cx, 1);
+    {
+        int q0bits = 0;
+        while (q0bits < 64 && (cx.mods[0] >> q0bits)) q0bits++;
+        bc->delta_in = cx.boot_delta_log2 > 0    ? std::ldexp(1.0, cx.boot_delta_log2)
+                       : cx.boot_delta_log2 < 0 ? canon(cx, 1)
+                                                : std::ldexp(1.0, q0bits - 11);
+    }
     bc->nl_stc = nl;
     bc->nl_out = nl - 3;
     cx.boot = bc;

@@ -101,6 +101,11 @@ int fhe_ctx_set_option(fhe_ctx* cx, const char* name, int value) {
         else if (std::strcmp(name, "merged_rescale") == 0) cx->cx.merged_rescale = value != 0;
         else if (std::strcmp(name, "pdl") == 0) cx->cx.use_pdl = value != 0;
         else if (std::strcmp(name, "ntt_cluster") == 0) cx->cx.ntt_cluster = value != 0;
+        else if (std::strcmp(name, "boot_delta_log2") == 0) {
+            if (value != 0 && value != -1 && (value < 30 || value > 56))
+                throw fhe::Error("boot_delta_log2: 0 (auto), -1 (canonical) or 30..56", -1);
+            cx->cx.boot_delta_log2 = value;
+        }
         else if (std::strcmp(name, "profile_every") == 0) cx->cx.prof_every = value < 1 ? 1 : value;
         else if (std::strcmp(name, "plaintext_cache") == 0) cx->cx.pt_cache = value != 0;
         else if (std::strcmp(name, "plaintext_cache_reserve_mib") == 0) cx->cx.pt_cache_reserve_mib = value < 0 ? 0 : value;

@@ -489,46 +489,67 @@ void cheb_eval(Context& cx, const Ciphertext& x, const std::vector<double>& coef
 }
 
 // sum_i c_i (.) x^i with per-slot coefficient vectors c_i (n slots each, repeated), power
-// basis, depth ceil(log2 deg) + 1: the powers are aligned to one level, multiplied by their
-// coefficient plaintexts, summed, and c_0 is added.  (polyGate3 and the channel-mix
-// polynomials of gpu_real_model.cu:4609-4649, :5130-5163, evaluated without the
-// reference's per-term alignTo chain.)
+// basis, depth ceil(log2 deg) + 1, for K inputs at once (each with its own coefficients; the
+// power products of the K evaluations are batched products).  The powers are not aligned to one
+// level: each is level-dropped (free) to the lowest power's level, multiplied by its coefficient
+// plaintext, whose encoding scale lands the product on the canonical scale of the level below,
+// and the terms are summed; c_0 is added last.  (polyGate3 and the channel-mix polynomials of
+// gpu_real_model.cu:4609-4649, :5130-5163, evaluated without the reference's per-term alignTo
+// chain.)
+void poly_eval_vec_n(Context& cx, const Ciphertext* const* xs, int K,
+                     const std::vector<std::vector<std::complex<double>>>* const* cs, int n, Ciphertext* outs) {
+    std::vector<std::vector<Ciphertext>> pw(K);
+    int maxdeg = 0;
+    for (int k = 0; k < K; k++) {
+        const int deg = (int)cs[k]->size() - 1;
+        require(deg >= 1, "poly_eval_vec: degree must be >= 1");
+        maxdeg = std::max(maxdeg, deg);
+        pw[k].resize(deg + 1);
+        pw[k][1] = ct_copy(cx, *xs[k]);
+        const double r = pw[k][1].scale / canon(cx, xs[k]->nl);
+        if (r > 1 + 1e-9 || r < 1 - 1e-9) align(cx, pw[k][1], xs[k]->nl - 1, 0);
+    }
+    for (int i = 2; i <= maxdeg; i++) {   // x^i = x^a x^b for every input of degree >= i
+        const int a = (i + 1) / 2, b = i / 2;
+        std::vector<const Ciphertext*> pa, pb;
+        std::vector<int> who;
+        for (int k = 0; k < K; k++)
+            if ((int)pw[k].size() > i) { pa.push_back(&pw[k][a]); pb.push_back(&pw[k][b]); who.push_back(k); }
+        std::vector<Ciphertext> o(who.size());
+        mul_rescale_n(cx, pa.data(), pb.data(), (int)who.size(), o.data());
+        for (size_t j = 0; j < who.size(); j++) pw[who[j]][i] = std::move(o[j]);
+    }
+    for (int k = 0; k < K; k++) {
+        const auto& c = *cs[k];
+        const int deg = (int)c.size() - 1;
+        int lo = pw[k][1].nl;
+        for (int i = 1; i <= deg; i++) lo = std::min(lo, pw[k][i].nl);
+        Ciphertext acc;
+        bool have = false;
+        for (int i = 1; i <= deg; i++) {
+            bool zero = true;
+            for (auto& v : c[i]) if (v != 0.0) { zero = false; break; }
+            if (zero) continue;
+            ct_level_drop(cx, pw[k][i], lo);
+            Ciphertext t;
+            mul_vec_rescale(cx, pw[k][i], c[i].data(), n, t, 0);
+            if (!have) { acc = std::move(t); have = true; }
+            else { Ciphertext u; ct_add(cx, acc, t, u); acc = std::move(u); }
+        }
+        if (!have) {
+            std::vector<std::complex<double>> z(n, 0.0);
+            ct_level_drop(cx, pw[k][1], lo);
+            mul_vec_rescale(cx, pw[k][1], z.data(), n, acc, 0);
+        }
+        add_vec(cx, acc, c[0].data(), n, outs[k]);
+    }
+}
+
 void poly_eval_vec(Context& cx, const Ciphertext& x, const std::vector<std::vector<std::complex<double>>>& c, int n,
                    Ciphertext& out) {
-    const int deg = (int)c.size() - 1;
-    require(deg >= 1, "poly_eval_vec: degree must be >= 1");
-    std::vector<Ciphertext> pw(deg + 1);
-    pw[1] = ct_copy(cx, x);
-    if (pw[1].scale / canon(cx, x.nl) > 1 + 1e-9 || pw[1].scale / canon(cx, x.nl) < 1 - 1e-9)
-        align(cx, pw[1], x.nl - 1, 0);
-    for (int i = 2; i <= deg; i++) {
-        const int a = (i + 1) / 2, b = i / 2;   // x^i = x^a x^b
-        mul_rescale(cx, pw[a], pw[b], pw[i]);
-    }
-    // one level for all powers; their scales may differ (each coefficient product below picks
-    // its own plaintext scale and lands on the same canonical output scale)
-    int lo = pw[1].nl;
-    for (int i = 1; i <= deg; i++) lo = std::min(lo, pw[i].nl);
-    for (int i = 1; i <= deg; i++)
-        if (pw[i].nl > lo) align(cx, pw[i], lo, 0);
-    Ciphertext acc;
-    bool have = false;
-    for (int i = 1; i <= deg; i++) {
-        bool zero = true;
-        for (auto& v : c[i]) if (v != 0.0) { zero = false; break; }
-        if (zero) continue;
-        Ciphertext t;
-        mul_vec_rescale(cx, pw[i], c[i].data(), n, t, 0);
-        if (!have) { acc = std::move(t); have = true; }
-        else { Ciphertext u; ct_add(cx, acc, t, u); acc = std::move(u); }
-    }
-    if (!have) {
-        std::vector<std::complex<double>> z(n, 0.0);
-        mul_vec_rescale(cx, pw[1], z.data(), n, acc, 0);
-    }
-    Ciphertext r;
-    add_vec(cx, acc, c[0].data(), n, r);
-    out = std::move(r);
+    const Ciphertext* px[1] = {&x};
+    const std::vector<std::vector<std::complex<double>>>* pc[1] = {&c};
+    poly_eval_vec_n(cx, px, 1, pc, n, &out);
 }
 
 // Chebyshev interpolant of f on [a, b] of degree n (Chebyshev nodes of the first kind)

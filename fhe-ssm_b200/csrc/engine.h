@@ -131,6 +131,14 @@ struct Context {
     int use_pdl = 1;                 // programmatic dependent launch for the hot kernels (launch_pdl)
     int ntt_cluster = 0;             // N = 2^16: one cluster launch per transform (ntt.cu, k_ntt_cluster)
     int merged_rescale = 1;          // circuit products: ModDown and rescale in one division by P q_l
+    // bootstrap input scale: the message is brought to one limb (q0) at scale 2^boot_delta_log2.
+    // q0 / scale is the factor by which SlotToCoeff amplifies the error of EvalMod's output, and
+    // 2 pi |m| scale / q0 the argument whose sine EvalMod returns in place of it (relative error
+    // (2 pi |m| scale / q0)^2 / 6 on the largest coefficients).  0 (default): scale = 2^(bits(q0)
+    // - 11), 2^49 for a 60-bit q0 (17.7 bits on U[-1, 1] slots at N = 2^16 against 13.8 at the
+    // canonical scale; 1.5e-5 on constant slots of magnitude 2); -1: the chain's canonical
+    // level-1 scale; read by bootstrap_setup
+    int boot_delta_log2 = 0;
     // BSGS plaintext cache (the reference's --cache-diags, gpu_real_model.cu:1647-1652, off by
     // default as there): a plan keeps the plaintext words of its last call while at least
     // pt_cache_reserve_mib of device memory stays free
@@ -312,6 +320,9 @@ void cheb_eval(Context& cx, const Ciphertext& x, const std::vector<double>& coef
 std::vector<double> cheb_fit(double (*f)(double, const void*), const void* arg, double a, double b, int n);
 void poly_eval_vec(Context& cx, const Ciphertext& x, const std::vector<std::vector<std::complex<double>>>& c, int n,
                    Ciphertext& out);
+void poly_eval_vec_n(Context& cx, const Ciphertext* const* xs, int K,
+                     const std::vector<std::vector<std::complex<double>>>* const* cs, int n, Ciphertext* outs);
+void mul_rescale_n(Context& cx, const Ciphertext* const* a, const Ciphertext* const* b, int K, Ciphertext* out);
 // encode with a cache keyed by (content, slots, level, scale); periodic vectors (n < N/2)
 // are stored compressed (matvec.cu)
 const Plaintext& encode_cached(Context& cx, const std::complex<double>* z, int n, int nl, double scale);

@@ -103,19 +103,40 @@ struct Model {
         return o;
     }
 
-    // polynomial with per-channel coefficient vectors on a complex-packed ciphertext
-    Ciphertext poly_complex(const Ciphertext& z, const std::vector<const std::vector<double>*>& coeffs, int off = 0) {
+    // polynomials with per-channel coefficient vectors on complex-packed ciphertexts: zs[j]
+    // with coefficients cs[j] (channels from offs[j]); out[2 j] and out[2 j + 1] are the real
+    // and imaginary parts of the result.  The power products of all 2 J parts run batched.
+    void poly_parts(const std::vector<const Ciphertext*>& zs,
+                    const std::vector<std::vector<const std::vector<double>*>>& cs, const std::vector<int>& offs,
+                    std::vector<Ciphertext>& out) {
         ProfScope op(cx, "op:poly", 0);
-        Ciphertext re, im;
-        split_complex(cx, z, re, im, true);
-        std::vector<std::vector<std::complex<double>>> c(coeffs.size());
-        for (size_t i = 0; i < coeffs.size(); i++) c[i] = slots(*coeffs[i], off);
-        Ciphertext pr, pi;
-        poly_eval_vec(cx, re, c, cfg.D, pr);
-        poly_eval_vec(cx, im, c, cfg.D, pi);
+        const int J = (int)zs.size();
+        std::vector<Ciphertext> parts(2 * J);
+        std::vector<std::vector<std::vector<std::complex<double>>>> c(J);
+        for (int j = 0; j < J; j++) {
+            split_complex(cx, *zs[j], parts[2 * j], parts[2 * j + 1], true);
+            for (auto* v : cs[j]) c[j].push_back(slots(*v, offs[j]));
+        }
+        std::vector<const Ciphertext*> px(2 * J);
+        std::vector<const std::vector<std::vector<std::complex<double>>>*> pc(2 * J);
+        for (int k = 0; k < 2 * J; k++) { px[k] = &parts[k]; pc[k] = &c[k / 2]; }
+        out.clear();
+        out.resize(2 * J);
+        poly_eval_vec_n(cx, px.data(), 2 * J, pc.data(), cfg.D, out.data());
+    }
+    Ciphertext poly_complex(const Ciphertext& z, const std::vector<const std::vector<double>*>& coeffs, int off = 0) {
+        std::vector<Ciphertext> p;
+        poly_parts({&z}, {coeffs}, {off}, p);
         Ciphertext o;
-        merge_complex(cx, std::move(pr), std::move(pi), o);
+        merge_complex(cx, std::move(p[0]), std::move(p[1]), o);
         return o;
+    }
+    // K products a[k] * b[k], relinearised and rescaled as one batch
+    void mul_n(const std::vector<const Ciphertext*>& a, const std::vector<const Ciphertext*>& b,
+               std::vector<Ciphertext>& out) {
+        out.clear();
+        out.resize(a.size());
+        mul_rescale_n(cx, a.data(), b.data(), (int)a.size(), out.data());
     }
 
     // rmsnorm: x / sqrt(mean(x^2) + eps) * g per lane (rmsnorm, gpu_real_model.cu:3451-3657)
@@ -126,10 +147,12 @@ struct Model {
         refresh(x, 3, sd.gx, kNormX);
         Ciphertext xr, xi;
         split_complex(cx, x, xr, xi, true);
-        Ciphertext sr, si, sq;
-        mul_rescale(cx, xr, xr, sr);
-        mul_rescale(cx, xi, xi, si);
-        merge_complex(cx, std::move(sr), std::move(si), sq);
+        Ciphertext sq;
+        {
+            std::vector<Ciphertext> s2;
+            mul_n({&xr, &xi}, {&xr, &xi}, s2);
+            merge_complex(cx, std::move(s2[0]), std::move(s2[1]), sq);
+        }
         // block sums land on channel 0 of every block, then are broadcast back
         Ciphertext t;
         rotate_sum(cx, sq, 1, D, t);
@@ -170,15 +193,17 @@ struct Model {
                 split_complex(cx, yc, yp[0], yp[1], true);
                 split_complex(cx, mc, mh[0], mh[1], true);
             }
+            // y <- 1.5 y + (-ms/2) y^3 on both parts: {y^2, (-ms/2) y} of both parts as one batch
+            // of four products, then their product as one batch of two
+            std::vector<Ciphertext> sq2, u;
+            mul_n({&yp[0], &mh[0], &yp[1], &mh[1]}, {&yp[0], &yp[0], &yp[1], &yp[1]}, sq2);
+            mul_n({&sq2[1], &sq2[3]}, {&sq2[0], &sq2[2]}, u);
             for (int P = 0; P < 2; P++) {
-                Ciphertext y2, tt, u, y3;
-                mul_rescale(cx, yp[P], yp[P], y2);
-                mul_rescale(cx, mh[P], yp[P], tt);
-                mul_rescale(cx, tt, y2, u);
+                Ciphertext y3;
                 mul_integer(cx, yp[P], 3, y3);   // 1.5 y at twice the scale
                 y3.scale = yp[P].scale * 2;
                 Ciphertext yn;
-                add_any(cx, y3, u, yn);
+                add_any(cx, y3, u[P], yn);
                 yp[P] = std::move(yn);
             }
         }
@@ -188,10 +213,12 @@ struct Model {
             refresh(yc, 1, sd.gy, kNormTail);
             split_complex(cx, yc, yp[0], yp[1], true);
         }
+        // x g at the level of y: the parts of x are level-dropped (free) to one limb above y,
+        // so that the gain product lands on y's level and scale without an alignment
+        if (xr.nl > yp[0].nl + 1) { ct_level_drop(cx, xr, yp[0].nl + 1); ct_level_drop(cx, xi, yp[0].nl + 1); }
         Ciphertext xgr = mulv(xr, g), xgi = mulv(xi, g);
-        Ciphertext outp[2];
-        Ciphertext* xparts[2] = {&xgr, &xgi};
-        for (int P = 0; P < 2; P++) mul_rescale(cx, *xparts[P], yp[P], outp[P]);
+        std::vector<Ciphertext> outp;
+        mul_n({&xgr, &xgi}, {&yp[0], &yp[1]}, outp);
         Ciphertext out;
         merge_complex(cx, std::move(outp[0]), std::move(outp[1]), out);
         return out;
@@ -279,23 +306,36 @@ struct Model {
             BabySet bs;
             matvec_babies(cx, v, cfg.D, cfg.b1, bs);
             const BabySet* bsp[1] = {&bs};
-            std::vector<Ciphertext> f(C);
+            // k_j = Wk_j v and r_j = Wr_j v for every chunk, then the activation and gate
+            // polynomials of all chunks on their real and imaginary parts (power products
+            // batched over the 4 C parts), then act * gate part by part (one batch of 2 C
+            // products), merged per chunk
+            std::vector<Ciphertext> kr(2 * C);
             for (int ch = 0; ch < C; ch++) {
-                Ciphertext k, r;
-                matvec_apply(cx, *P.wk[ch], bsp, k);
-                matvec_apply(cx, *P.wr[ch], bsp, r);
-                if (ch == 0) FHE_PROBE(9, k)
-                Ciphertext act = poly_complex(k, {&P.q[0], &P.q[1], &P.q[2], &P.q[3]}, ch * cfg.D);
-                Ciphertext gate = poly_complex(r, {&P.r[0], &P.r[1], &P.r[2]}, ch * cfg.D);
-                Ciphertext ar, ai, gr, gi;
-                split_complex(cx, act, ar, ai, true);
-                split_complex(cx, gate, gr, gi, true);
-                Ciphertext fr, fi;
-                mul_rescale(cx, ar, gr, fr);
-                mul_rescale(cx, ai, gi, fi);
-                merge_complex(cx, std::move(fr), std::move(fi), f[ch]);
-                if (ch == 0) FHE_PROBE(10, f[0])
+                matvec_apply(cx, *P.wk[ch], bsp, kr[2 * ch]);
+                matvec_apply(cx, *P.wr[ch], bsp, kr[2 * ch + 1]);
+                if (ch == 0) FHE_PROBE(9, kr[0])
             }
+            std::vector<const Ciphertext*> zs(2 * C);
+            std::vector<std::vector<const std::vector<double>*>> pcs(2 * C);
+            std::vector<int> offs(2 * C);
+            for (int ch = 0; ch < C; ch++) {
+                zs[2 * ch] = &kr[2 * ch];
+                pcs[2 * ch] = {&P.q[0], &P.q[1], &P.q[2], &P.q[3]};
+                zs[2 * ch + 1] = &kr[2 * ch + 1];
+                pcs[2 * ch + 1] = {&P.r[0], &P.r[1], &P.r[2]};
+                offs[2 * ch] = offs[2 * ch + 1] = ch * cfg.D;
+            }
+            std::vector<Ciphertext> pp;   // [chunk][act / gate][re / im]
+            poly_parts(zs, pcs, offs, pp);
+            std::vector<const Ciphertext*> pa, pg;
+            for (int ch = 0; ch < C; ch++)
+                for (int q = 0; q < 2; q++) { pa.push_back(&pp[4 * ch + q]); pg.push_back(&pp[4 * ch + 2 + q]); }
+            std::vector<Ciphertext> fp;
+            mul_n(pa, pg, fp);
+            std::vector<Ciphertext> f(C);
+            for (int ch = 0; ch < C; ch++) merge_complex(cx, std::move(fp[2 * ch]), std::move(fp[2 * ch + 1]), f[ch]);
+            FHE_PROBE(10, f[0])
             // the chunks ran identical pipelines: bring any stragglers to the lowest one
             int lo = 0;
             for (int ch = 1; ch < C; ch++) if (f[ch].nl < f[lo].nl) lo = ch;

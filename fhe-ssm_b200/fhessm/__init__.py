@@ -296,7 +296,10 @@ class CryptoContext:
     def set_option(self, name, value):
         """Engine switches: "matvec_tensor_cores" (1 = tcgen05 BSGS products, 0 = CUDA cores),
         "merged_rescale", "profile_every", "plaintext_cache" (1 = a BSGS plan keeps its plaintext
-        words for the next call at the same level and scale), "plaintext_cache_reserve_mib"."""
+        words for the next call at the same level and scale), "plaintext_cache_reserve_mib",
+        "pdl", "ntt_cluster", "boot_delta_log2" (the bootstrap input scale, read by
+        EvalBootstrapSetup: 0 = 2^(bits(q0) - 11), -1 = the canonical level-1 scale, else
+        2^value)."""
         _check(lib().fhe_ctx_set_option(self.h, name.encode(), int(value)))
 
     def stream_ptr(self):
