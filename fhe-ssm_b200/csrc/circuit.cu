@@ -66,6 +66,25 @@ void mul_const_rescale(Context& cx, const Ciphertext& a, double c, Ciphertext& o
     out = std::move(t);
 }
 
+// K constant products a[k] * c[k] (one limb count), rescaled as one batch (mul_const_rescale each)
+void mul_const_rescale_n(Context& cx, const Ciphertext* const* a, const double* c, int K, Ciphertext* out,
+                         double target) {
+    const int nl = a[0]->nl;
+    require(nl >= 2, "mul_const_rescale: no level left");
+    if (target <= 0) target = canon(cx, nl - 1);
+    std::vector<Ciphertext*> t(K);
+    for (int k = 0; k < K; k++) {
+        require(a[k]->nl == nl, "mul_const_rescale_n: the ciphertexts differ in limb count");
+        const long double S = (long double)target * (long double)cx.mods[nl - 1] / (long double)a[k]->scale;
+        const long double M = std::floor((long double)c[k] * S + 0.5L);
+        const double sc = a[k]->scale;
+        mul_integer(cx, *a[k], M, out[k]);
+        out[k].scale = (c[k] != 0.0) ? sc * (double)(M / (long double)c[k]) : sc * (double)S;
+        t[k] = &out[k];
+    }
+    ct_rescale_n(cx, t.data(), K);
+}
+
 // bring a to nl_t limbs at scale `target` (default canonical).  nl_t < a.nl: one level used.
 void align(Context& cx, Ciphertext& a, int nl_t, double target) {
     if (target <= 0) target = canon(cx, nl_t);
@@ -146,6 +165,48 @@ void mul_vec_rescale(Context& cx, const Ciphertext& a, const std::complex<double
     ct_rescale(cx, t);
     t.scale = target;   // exact by construction (a.scale * s / q)
     out = std::move(t);
+}
+
+// K per-slot products a[k] * v[k] (n slots each), one level of limbs for all, rescaled as one
+// batch; each output lands on `target` (default: the canonical scale of the level below)
+void mul_vec_rescale_n(Context& cx, const Ciphertext* const* a, const std::complex<double>* const* v, int n, int K,
+                       Ciphertext* out, double target) {
+    if (K == 1) { mul_vec_rescale(cx, *a[0], v[0], n, out[0], target); return; }
+    const int nl = a[0]->nl;
+    require(nl >= 2, "mul_vec_rescale: no level left");
+    if (target <= 0) target = canon(cx, nl - 1);
+    std::vector<Ciphertext*> t(K);
+    for (int k = 0; k < K; k++) {
+        require(a[k]->nl == nl, "mul_vec_rescale_n: the ciphertexts differ in limb count");
+        const double s = target * (double)cx.mods[nl - 1] / a[k]->scale;
+        const Plaintext& pt = encode_cached(cx, v[k], n, nl, s);
+        ct_mul_pt(cx, *a[k], pt, out[k]);
+        t[k] = &out[k];
+    }
+    ct_rescale_n(cx, t.data(), K);
+    for (int k = 0; k < K; k++) out[k].scale = target;   // exact by construction
+}
+
+// align() of K ciphertexts to nl_t limbs and scale `target` (default canonical), the rescales batched
+void align_n(Context& cx, Ciphertext* const* a, int K, int nl_t, double target) {
+    if (target <= 0) target = canon(cx, nl_t);
+    std::vector<Ciphertext*> todo;
+    for (int k = 0; k < K; k++) {
+        require(nl_t >= 1 && nl_t <= a[k]->nl, "align: bad target level");
+        if (a[k]->nl == nl_t) {
+            const double r = a[k]->scale / target;
+            require(r > 1 - 1e-9 && r < 1 + 1e-9, "align: same level but different scale");
+            continue;
+        }
+        ct_level_drop(cx, *a[k], nl_t + 1);
+        const long double S = (long double)target * (long double)cx.mods[nl_t] / (long double)a[k]->scale;
+        const long double M = std::floor(S + 0.5L);
+        const double sc = a[k]->scale;
+        mul_integer(cx, *a[k], M, *a[k]);
+        a[k]->scale = sc * (double)M;
+        todo.push_back(a[k]);
+    }
+    ct_rescale_n(cx, todo.data(), (int)todo.size());
 }
 
 // + vector (n slots, repeated) at the ciphertext's scale
@@ -301,10 +362,12 @@ struct ChebEvalN {
         auto it = memo.find(key);
         if (it != memo.end()) return it->second;
         std::vector<Ciphertext> v(K);
+        std::vector<Ciphertext*> pv(K);
         for (int k = 0; k < K; k++) {
             v[k] = ct_copy(cx, src[k]);
-            align(cx, v[k], nl, target);
+            pv[k] = &v[k];
         }
+        align_n(cx, pv.data(), K, nl, target);
         return memo.emplace(key, std::move(v)).first->second;
     }
     void prod(const std::vector<Ciphertext>& a, const std::vector<Ciphertext>& b, std::vector<Ciphertext>& o) {
@@ -373,28 +436,31 @@ struct ChebEvalN {
             for (int l = 0; l < nl; l++) la.wp[t][l] = shoup_of(la.w[t][l], cx.mods[l]);
         }
         if (la.nt == 0) { la.nt = 1; terms.push_back(1); }   // constant-only leaf: 0 * T_1
+        std::vector<Ciphertext*> pacc(K);
         for (int k = 0; k < K; k++) {
             for (int t = 0; t < la.nt; t++) {
                 la.in[t] = T[terms[t]][k].c(0);
                 la.stride[t] = (long long)T[terms[t]][k].stride;
             }
-            Ciphertext acc = ct_alloc(cx, nl);
+            out[k] = ct_alloc(cx, nl);
             {
                 ProfScope ps(cx, "lincomb", 8.0 * cx.N * nl * 2 * (la.nt + 1));
-                k_lincomb<<<dim3(cx.N / 256, nl, 2), 256, 0, cx.stream>>>(la, acc.c(0), (long long)acc.stride,
+                k_lincomb<<<dim3(cx.N / 256, nl, 2), 256, 0, cx.stream>>>(la, out[k].c(0), (long long)out[k].stride,
                                                                           cx.logN);
                 CUDA_CHECK(cudaGetLastError());
                 cx.launches++;
             }
-            acc.scale = tq;
-            ct_rescale(cx, acc);
-            acc.scale = target;
+            out[k].scale = tq;
+            pacc[k] = &out[k];
+        }
+        ct_rescale_n(cx, pacc.data(), K);
+        for (int k = 0; k < K; k++) {
+            out[k].scale = target;
             if (!c.empty() && c[0] != 0.0) {
                 Ciphertext u;
-                ct_add_const(cx, acc, c[0], u);
-                acc = std::move(u);
+                ct_add_const(cx, out[k], c[0], u);
+                out[k] = std::move(u);
             }
-            out[k] = std::move(acc);
         }
         return out;
     }
@@ -420,8 +486,12 @@ struct ChebEvalN {
             prod(qv, giant[M], pr);
         }
         std::vector<Ciphertext> out(K);
+        if (rv[0].nl > pr[0].nl) {
+            std::vector<Ciphertext*> prv(K);
+            for (int k = 0; k < K; k++) prv[k] = &rv[k];
+            align_n(cx, prv.data(), K, pr[0].nl, pr[0].scale);
+        }
         for (int k = 0; k < K; k++) {
-            if (rv[k].nl > pr[k].nl) align(cx, rv[k], pr[k].nl, pr[k].scale);
             if (rv[k].nl == pr[k].nl) ct_add(cx, pr[k], rv[k], out[k]);
             else add_any(cx, pr[k], rv[k], out[k]);
         }
@@ -519,30 +589,46 @@ void poly_eval_vec_n(Context& cx, const Ciphertext* const* xs, int K,
         mul_rescale_n(cx, pa.data(), pb.data(), (int)who.size(), o.data());
         for (size_t j = 0; j < who.size(); j++) pw[who[j]][i] = std::move(o[j]);
     }
+    // the coefficient products of every input, one batch per limb count
+    std::vector<std::complex<double>> zero(n, 0.0);
+    struct Term { int k, i; const std::complex<double>* v; };
+    std::map<int, std::vector<Term>> by_nl;
     for (int k = 0; k < K; k++) {
         const auto& c = *cs[k];
         const int deg = (int)c.size() - 1;
         int lo = pw[k][1].nl;
         for (int i = 1; i <= deg; i++) lo = std::min(lo, pw[k][i].nl);
-        Ciphertext acc;
         bool have = false;
         for (int i = 1; i <= deg; i++) {
-            bool zero = true;
-            for (auto& v : c[i]) if (v != 0.0) { zero = false; break; }
-            if (zero) continue;
+            bool nz = false;
+            for (auto& v : c[i]) if (v != 0.0) { nz = true; break; }
+            if (!nz) continue;
             ct_level_drop(cx, pw[k][i], lo);
-            Ciphertext t;
-            mul_vec_rescale(cx, pw[k][i], c[i].data(), n, t, 0);
-            if (!have) { acc = std::move(t); have = true; }
-            else { Ciphertext u; ct_add(cx, acc, t, u); acc = std::move(u); }
+            by_nl[lo].push_back({k, i, c[i].data()});
+            have = true;
         }
-        if (!have) {
-            std::vector<std::complex<double>> z(n, 0.0);
+        if (!have) {   // all-zero polynomial: 0 * x keeps a valid ciphertext
             ct_level_drop(cx, pw[k][1], lo);
-            mul_vec_rescale(cx, pw[k][1], z.data(), n, acc, 0);
+            by_nl[lo].push_back({k, 1, zero.data()});
         }
-        add_vec(cx, acc, c[0].data(), n, outs[k]);
     }
+    std::vector<Ciphertext> acc(K);
+    std::vector<char> have(K, 0);
+    for (auto& g : by_nl) {
+        const auto& terms = g.second;
+        const int B = (int)terms.size();
+        std::vector<const Ciphertext*> in(B);
+        std::vector<const std::complex<double>*> vs(B);
+        for (int j = 0; j < B; j++) { in[j] = &pw[terms[j].k][terms[j].i]; vs[j] = terms[j].v; }
+        std::vector<Ciphertext> prod(B);
+        mul_vec_rescale_n(cx, in.data(), vs.data(), n, B, prod.data(), 0);
+        for (int j = 0; j < B; j++) {
+            const int k = terms[j].k;
+            if (!have[k]) { acc[k] = std::move(prod[j]); have[k] = 1; }
+            else { Ciphertext u; ct_add(cx, acc[k], prod[j], u); acc[k] = std::move(u); }
+        }
+    }
+    for (int k = 0; k < K; k++) add_vec(cx, acc[k], (*cs[k])[0].data(), n, outs[k]);
 }
 
 void poly_eval_vec(Context& cx, const Ciphertext& x, const std::vector<std::vector<std::complex<double>>>& c, int n,

@@ -628,6 +628,63 @@ void ct_mul_relin_rescale(Context& cx, const Ciphertext& a, const Ciphertext& b,
 }
 
 
+// dst[p] = src[p] (one limb of N words each), p < npoly = gridDim.y
+struct LimbPtrs {
+    const uint64_t* src[kFuseMax];
+};
+__global__ void __launch_bounds__(256) k_gather_limbs(const LimbPtrs g, uint64_t* __restrict__ dst, int logN) {
+    pdl_wait();
+    pdl_trigger();
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, p = blockIdx.y;
+    dst[((size_t)p << logN) + x] = g.src[p][x];
+}
+
+// The rescale of K ciphertexts of one limb count as one batch: their dropped limbs gathered into
+// one buffer and inverse-transformed by one launch pair, then one fused forward transform for
+// all of them (ntt_rescale_n), kFuseMax / 2 ciphertexts at a time.  The words equal K calls of
+// ct_rescale.
+void ct_rescale_n(Context& cx, Ciphertext* const* a, int K) {
+    if (K < 1) return;
+    if (K == 1 || cx.logN < 13) {
+        for (int k = 0; k < K; k++) ct_rescale(cx, *a[k]);
+        return;
+    }
+    const int nl = a[0]->nl;
+    for (int k = 0; k < K; k++)
+        if (a[k]->nl != nl) throw Error("rescale_n: the ciphertexts differ in limb count", -4);
+    if (nl < 2) throw Error("rescale: no limb left to drop", -4);
+    const int N = cx.N, l = nl - 1;
+    cudaStream_t st = cx.stream;
+    for (int k0 = 0; k0 < K; k0 += kFuseMax / 2) {
+        const int B = std::min(kFuseMax / 2, K - k0);
+        LimbPtrs g{};
+        uint64_t* dst[kFuseMax];
+        for (int b = 0; b < B; b++) {
+            Ciphertext& c = *a[k0 + b];
+            g.src[2 * b] = c.c(0) + (size_t)l * N;
+            g.src[2 * b + 1] = c.c(1) + (size_t)l * N;
+            dst[2 * b] = c.c(0);
+            dst[2 * b + 1] = c.c(1);
+        }
+        DevBuf t((size_t)2 * B * N, st);
+        launch_pdl(cx, k_gather_limbs, dim3(N / 256, 2 * B), dim3(256), 0, st, g, t.p, cx.logN);
+        CUDA_CHECK(cudaGetLastError());
+        cx.launches++;
+        LimbMap lm{};
+        lm.base = t.p; lm.poly_stride = N; lm.nl = 1; lm.split = 1; lm.off0 = l; lm.off1 = 0;
+        ntt(cx, lm, 2 * B, true, st);
+        DevBuf y((size_t)2 * B * l * N, st);
+        {
+            ProfScope ps(cx, "rescale_ntt", 8.0 * N * B * (4.0 * l + 2));
+            ntt_rescale_n(cx, t.p, N, dst, 2 * B, l, y.p, st);
+        }
+        for (int b = 0; b < B; b++) {
+            a[k0 + b]->scale /= (double)cx.mods[l];
+            a[k0 + b]->nl = l;
+        }
+    }
+}
+
 void ct_rescale(Context& cx, Ciphertext& a) {
     if (a.nl < 2) throw Error("rescale: no limb left to drop", -4);
     const int N = cx.N, l = a.nl - 1;

@@ -253,6 +253,9 @@ void expand_uniform_dev(Context& cx, const uint8_t seed[32], int digit0, int ndi
 void ntt(const Context& cx, const LimbMap& mp, int npoly, bool inv, cudaStream_t st);
 // rescale by the last of l + 1 limbs, the dropped limbs already inverse-transformed in place (ntt.cu)
 void ntt_rescale(const Context& cx, uint64_t* a, long long stride, int l, uint64_t* y, cudaStream_t st);
+constexpr int kFuseMax = 16;   // polynomials of one fused rescale transform (ntt_rescale_n)
+void ntt_rescale_n(const Context& cx, const uint64_t* src, long long src_stride, uint64_t* const* dst, int npoly,
+                   int l, uint64_t* y, cudaStream_t st);
 
 // ---- operations (engine.cu) ---------------------------------------------------------------
 // key switching of d (nl limbs, eval) -> (out0, out1) added into add0/add1 (may be null),
@@ -274,6 +277,7 @@ void ct_mul_relin_rescale(Context& cx, const Ciphertext& a, const Ciphertext& b,
 void ct_mul_relin_rescale_n(Context& cx, const Ciphertext* const* a, const Ciphertext* const* b, int B,
                             Ciphertext* out);
 void ct_rescale(Context& cx, Ciphertext& a);
+void ct_rescale_n(Context& cx, Ciphertext* const* a, int K);   // K rescales of one limb count, batched
 void ct_level_drop(Context& cx, Ciphertext& a, int nl_target);   // drop limbs, no scaling
 void ct_automorph(Context& cx, const Ciphertext& a, uint64_t k, Ciphertext& out);
 // out = extra + sum_b rot((c0s[b], c1s[b]), steps[b]) for n inputs of nl limbs at `scale`
@@ -305,6 +309,11 @@ void mul_integer(Context& cx, const Ciphertext& a, long double M, Ciphertext& ou
 void mul_integer_add_const(Context& cx, const Ciphertext& a, long double M, double v, Ciphertext& out);
 void mul_const_rescale(Context& cx, const Ciphertext& a, double c, Ciphertext& out, double target = 0);
 void align(Context& cx, Ciphertext& a, int nl_t, double target = 0);
+void align_n(Context& cx, Ciphertext* const* a, int K, int nl_t, double target = 0);
+void mul_const_rescale_n(Context& cx, const Ciphertext* const* a, const double* c, int K, Ciphertext* out,
+                         double target = 0);
+void mul_vec_rescale_n(Context& cx, const Ciphertext* const* a, const std::complex<double>* const* v, int n, int K,
+                       Ciphertext* out, double target = 0);
 void match(Context& cx, Ciphertext& a, Ciphertext& b);
 void add_any(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out);
 void sub_any(Context& cx, const Ciphertext& a, const Ciphertext& b, Ciphertext& out);

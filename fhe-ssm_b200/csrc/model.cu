@@ -97,6 +97,27 @@ struct Model {
         mul_vec_rescale(cx, a, z.data(), cfg.D, o, 0);
         return o;
     }
+    // a * va + b * vb (per-channel vectors): both inputs read at the lower of their levels (a
+    // limb drop, free) so that the two products are one batch and land on one level and scale
+    Ciphertext mulv_sum(const Ciphertext& a, const std::vector<double>& va, const Ciphertext& b,
+                        const std::vector<double>& vb) {
+        const int lo = std::min(a.nl, b.nl);
+        Ciphertext& ma = const_cast<Ciphertext&>(a);
+        Ciphertext& mb = const_cast<Ciphertext&>(b);
+        const int na = a.nl, nb = b.nl;
+        ma.nl = lo;
+        mb.nl = lo;
+        auto za = slots(va), zb = slots(vb);
+        const Ciphertext* in[2] = {&a, &b};
+        const std::complex<double>* vs[2] = {za.data(), zb.data()};
+        Ciphertext o[2];
+        mul_vec_rescale_n(cx, in, vs, cfg.D, 2, o, 0);
+        ma.nl = na;
+        mb.nl = nb;
+        Ciphertext r;
+        ct_add(cx, o[0], o[1], r);
+        return r;
+    }
     Ciphertext addc(const Ciphertext& a, const Ciphertext& b) {
         Ciphertext o;
         add_any(cx, a, b, o);
@@ -176,11 +197,15 @@ struct Model {
         split_complex(cx, ms, mr, mi, true);
         Ciphertext yp[2], mh[2];
         Ciphertext* mparts[2] = {&mr, &mi};
-        for (int P = 0; P < 2; P++) {
-            Ciphertext yb;
-            mul_const_rescale(cx, *mparts[P], sd.b, yb, 0);
-            ct_add_const(cx, yb, sd.a, yp[P]);
-            mul_const_rescale(cx, *mparts[P], -0.5, mh[P], 0);
+        {   // seed a + b ms and -ms/2 of both parts: four constant products, one batched rescale
+            const Ciphertext* in[4] = {mparts[0], mparts[0], mparts[1], mparts[1]};
+            const double cs4[4] = {sd.b, -0.5, sd.b, -0.5};
+            Ciphertext o[4];
+            mul_const_rescale_n(cx, in, cs4, 4, o, 0);
+            for (int P = 0; P < 2; P++) {
+                ct_add_const(cx, o[2 * P], sd.a, yp[P]);
+                mh[P] = std::move(o[2 * P + 1]);
+            }
         }
         for (int it = 0; it < sd.iters; it++) {
             if (yp[0].nl - 1 < 2 + (it + 1 == sd.iters ? 1 : 0)) {
@@ -245,13 +270,11 @@ struct Model {
                 std::vector<double> om(P.mix.size());
                 for (size_t i = 0; i < om.size(); i++) om[i] = 1.0 - P.mix[i];
                 refresh(xn, 1, P.g_u, kXn);
-                Ciphertext a = mulv(xn, P.mix);
                 if (have_state) {
                     refresh(up[l], 1, P.g_u, kUp);
-                    Ciphertext b = mulv(up[l], om);
-                    u = addc(a, b);
+                    u = mulv_sum(xn, P.mix, up[l], om);
                 } else {
-                    u = std::move(a);
+                    u = mulv(xn, P.mix);
                 }
                 up[l] = ct_copy(cx, xn);
             } else {
@@ -265,22 +288,20 @@ struct Model {
                 matvec(cx, *P.win, in, x);
             }
             FHE_PROBE(3, x)
-            Ciphertext bx = mulv(x, P.bco), snew;
+            Ciphertext snew;
             if (have_state) {
                 Ciphertext sp = ct_copy(cx, s[l]);
                 refresh(sp, 1, P.g_s, kSp);
-                Ciphertext as = mulv(sp, P.decay);
-                snew = addc(as, bx);
+                snew = mulv_sum(sp, P.decay, x, P.bco);
             } else {
-                snew = std::move(bx);
+                snew = mulv(x, P.bco);
             }
             // the carried state loses a level per step: refresh it (and keep the refreshed copy
             // as the carry) when the readout z could not cover the gate polynomial
             refresh(snew, 5, P.g_s, kSnew);
             s[l] = ct_copy(cx, snew);
             FHE_PROBE(4, snew)
-            Ciphertext cs = mulv(snew, P.c), dx = mulv(x, P.dd);
-            Ciphertext z = addc(cs, dx);
+            Ciphertext z = mulv_sum(snew, P.c, x, P.dd);
             refresh(z, 4, P.g_z, kZ);
             FHE_PROBE(5, z)
             std::vector<double> zero(cfg.d, 0.0);

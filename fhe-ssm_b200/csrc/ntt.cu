@@ -87,17 +87,16 @@ __device__ __forceinline__ void stage16(uint64_t (&x)[16], uint64_t q, int h, TW
     else stage16<INV, 1>(x, q, tw);
 }
 
-// A forward transform with a fused prologue and epilogue (FUSE = true): the rescale of a
-// ciphertext.  The column pass reads, in place of its input limb i, the centred lift of the
-// dropped limb (coefficient form, src + poly * src_stride) modulo q_i; the row pass writes, in
-// place of the transformed lift y, the rescaled limb dst_i = (dst_i - y) * q_l^-1 (rs: [l][i][2],
-// q_l^-1 mod q_i with its Shoup companion).  The words equal k_rescale_lift -> NTT ->
-// k_rescale_final.
+// A forward transform with a fused prologue and epilogue (FUSE = true): the rescale of up to
+// kFuseMax / 2 ciphertexts.  The column pass reads, in place of its input limb i, the centred
+// lift of the dropped limb (coefficient form, src + poly * src_stride) modulo q_i; the row pass
+// writes, in place of the transformed lift y, the rescaled limb dst[poly]_i = (dst[poly]_i - y)
+// * q_l^-1 (rs: [l][i][2], q_l^-1 mod q_i with its Shoup companion).  The words equal
+// k_rescale_lift -> NTT -> k_rescale_final.
 struct NttFuse {
     const uint64_t* src;
     long long src_stride;
-    uint64_t* dst;
-    long long dst_stride;
+    uint64_t* dst[kFuseMax];   // polynomial p's limbs 0..l-1 at dst[p] (limb stride N)
     const uint64_t* rs;
     int l, L;
 };
@@ -240,7 +239,7 @@ __global__ void __launch_bounds__(256, 3) k_ntt_row(LimbMap mp, const ulonglong2
         for (int k = 0; k < 16; k++) sB[k] = canon4(x[k], q);
         __syncthreads();
         if (FUSE) {   // the rescaled limb in place of the transformed lift
-            uint64_t* d = fz.dst + (size_t)poly * fz.dst_stride + (size_t)limb * N + (size_t)blockIdx.x * 4096;
+            uint64_t* d = fz.dst[poly] + (size_t)limb * N + (size_t)blockIdx.x * 4096;
             const uint64_t* w = fz.rs + ((size_t)fz.l * fz.L + m) * 2;
             const uint64_t w0 = w[0], w1 = w[1];
 #pragma unroll
@@ -489,22 +488,36 @@ static void launch_ntt_rescale(const Context& cx, const LimbMap& mp, int count, 
                (const ulonglong2*)cx.d_tw2, (const ulonglong2*)cx.d_twrow, fz);
 }
 
-// The rescale of a ciphertext with nl = l + 1 limbs, past the inverse transform of its dropped
-// limb (in place, coefficient form): its limbs 0..l-1 become (a_i - lift_i(a_l)) q_l^-1, the lift's
-// transform held in y ([2][l][N] scratch).  Two launches instead of lift, transform and final.
-void ntt_rescale(const Context& cx, uint64_t* a, long long stride, int l, uint64_t* y, cudaStream_t st) {
+// The rescale of npoly polynomials with l + 1 limbs each (npoly <= kFuseMax), past the inverse
+// transform of their dropped limbs (coefficient form, polynomial p's at src + p * src_stride):
+// the limbs 0..l-1 at dst[p] become (a_i - lift_i(a_l)) q_l^-1, the lifts' transforms held in y
+// ([npoly][l][N] scratch).  Two launches instead of lift, transform and final.
+void ntt_rescale_n(const Context& cx, const uint64_t* src, long long src_stride, uint64_t* const* dst, int npoly,
+                   int l, uint64_t* y, cudaStream_t st) {
     if (cx.logN < 13) throw Error("ntt_rescale: logN must be >= 13", -1);
+    if (npoly < 1 || npoly > kFuseMax) throw Error("ntt_rescale: 1 to 16 polynomials", -1);
     LimbMap mp = cx.qmap(y, l, (long long)l * cx.N);
-    NttFuse fz{a + (size_t)l * cx.N, stride, a, stride, cx.d_rs, l, cx.L};
+    NttFuse fz{};
+    fz.src = src;
+    fz.src_stride = src_stride;
+    for (int p = 0; p < npoly; p++) fz.dst[p] = dst[p];
+    fz.rs = cx.d_rs;
+    fz.l = l;
+    fz.L = cx.L;
     switch (cx.logN) {
-        case 13: launch_ntt_rescale<13>(cx, mp, 2 * l, fz, st); break;
-        case 14: launch_ntt_rescale<14>(cx, mp, 2 * l, fz, st); break;
-        case 15: launch_ntt_rescale<15>(cx, mp, 2 * l, fz, st); break;
-        case 16: launch_ntt_rescale<16>(cx, mp, 2 * l, fz, st); break;
+        case 13: launch_ntt_rescale<13>(cx, mp, npoly * l, fz, st); break;
+        case 14: launch_ntt_rescale<14>(cx, mp, npoly * l, fz, st); break;
+        case 15: launch_ntt_rescale<15>(cx, mp, npoly * l, fz, st); break;
+        case 16: launch_ntt_rescale<16>(cx, mp, npoly * l, fz, st); break;
         default: throw Error("ntt_rescale: logN must be in [13, 16]");
     }
     CUDA_CHECK(cudaGetLastError());
     cx.launches += 2;
+}
+// one ciphertext: the dropped limb transformed in place (a + l N, poly stride `stride`)
+void ntt_rescale(const Context& cx, uint64_t* a, long long stride, int l, uint64_t* y, cudaStream_t st) {
+    uint64_t* dst[2] = {a, a + stride};
+    ntt_rescale_n(cx, a + (size_t)l * cx.N, stride, dst, 2, l, y, st);
 }
 
 }  // namespace fhe
