@@ -37,8 +37,37 @@ __device__ __forceinline__ ulonglong2 ld_tw(const ulonglong2* a, uint64_t pol) {
     return v;
 }
 
-template <bool INV>
+// Shoup product with a cheaper quotient (AR = 1 butterflies): the high 64 bits of x * wp without
+// the x_lo * wp_lo term and the carries out of the cross terms' low halves.  The estimate is 0 to
+// 2 below floor(x wp / 2^64), so x * w - est * q lies in [0, 4q) (Shoup's exact quotient: [0, 2q)).
+__device__ __forceinline__ uint64_t mul_shoup_q4(uint64_t x, uint64_t w, uint64_t wp, uint64_t q) {
+    const uint32_t x0 = (uint32_t)x, x1 = (uint32_t)(x >> 32), p0 = (uint32_t)wp, p1 = (uint32_t)(wp >> 32);
+    const uint64_t est = (uint64_t)x1 * p1 + __umulhi(x0, p1) + __umulhi(x1, p0);
+    return x * w - est * q;
+}
+
+// AR = 0: the Harvey butterflies above.  AR = 1: the same with mul_shoup_q4; forward values in
+// [0, 8q + 2^32) (u is brought below 4q + 2^32 by the high-word test against 4q), inverse values
+// in [0, 4q).  8q + 2^33 < 2^64 for the moduli below 2^61.
+template <bool INV, int AR = 0>
 __device__ __forceinline__ void bfly(uint64_t& lo, uint64_t& hi, uint64_t w, uint64_t wp, uint64_t q) {
+    if (AR == 1) {
+        const uint64_t q4 = q << 2;
+        if (!INV) {
+            uint64_t u = lo;
+            if ((uint32_t)(u >> 32) > (uint32_t)(q4 >> 32)) u -= q4;
+            const uint64_t x = mul_shoup_q4(hi, w, wp, q);
+            lo = u + x;
+            hi = u - x + q4;
+        } else {
+            uint64_t u = lo + hi;
+            if (u >= q4) u -= q4;
+            const uint64_t t = lo - hi + q4;
+            hi = mul_shoup_q4(t, w, wp, q);
+            lo = u;
+        }
+        return;
+    }
     const uint64_t q2 = q << 1;
     if (!INV) {
         uint64_t u = lo;
@@ -60,6 +89,16 @@ __device__ __forceinline__ uint64_t canon4(uint64_t v, uint64_t q) {   // [0, 4q
     if (v >= q2) v -= q2;   // < 2q
     return v >= q ? v - q : v;
 }
+// the forward transform's output range of butterflies AR -> [0, q)  (2^32 < q)
+template <int AR>
+__device__ __forceinline__ uint64_t canon_out(uint64_t v, uint64_t q) {
+    if (AR == 0) return canon4(v, q);
+    const uint64_t q4 = q << 2, q2 = q << 1;
+    if (v >= q4) v -= q4;   // [0, 8q + 2^32) -> [0, 4q + 2^32) < 5q
+    if (v >= q2) v -= q2;   // < 3q
+    if (v >= q) v -= q;     // < 2q
+    return v >= q ? v - q : v;
+}
 
 __device__ __forceinline__ bool limb_skipped(const LimbMap& mp, int poly, int limb) {
     if (mp.skip_alpha == 0) return false;
@@ -70,21 +109,21 @@ __device__ __forceinline__ bool limb_skipped(const LimbMap& mp, int poly, int li
 // One radix-2 stage over a thread's 16 registers at register distance H: butterfly (k, k + H)
 // for every k with k & H == 0, using twiddle number k / (2H) of the stage, tw(j).  Each of the
 // 8/H distinct twiddles is loaded once.
-template <bool INV, int H, class TW>
-__device__ __forceinline__ void stage16(uint64_t (&x)[16], uint64_t q, TW tw) {
+template <bool INV, int H, int AR, class TW>
+__device__ __forceinline__ void stage16h(uint64_t (&x)[16], uint64_t q, TW tw) {
 #pragma unroll
     for (int j = 0; j < 8 / H; j++) {
         const ulonglong2 t2 = tw(j);
 #pragma unroll
-        for (int kk = 0; kk < H; kk++) bfly<INV>(x[2 * H * j + kk], x[2 * H * j + kk + H], t2.x, t2.y, q);
+        for (int kk = 0; kk < H; kk++) bfly<INV, AR>(x[2 * H * j + kk], x[2 * H * j + kk + H], t2.x, t2.y, q);
     }
 }
-template <bool INV, class TW>
+template <bool INV, int AR = 0, class TW>
 __device__ __forceinline__ void stage16(uint64_t (&x)[16], uint64_t q, int h, TW tw) {
-    if (h == 8) stage16<INV, 8>(x, q, tw);
-    else if (h == 4) stage16<INV, 4>(x, q, tw);
-    else if (h == 2) stage16<INV, 2>(x, q, tw);
-    else stage16<INV, 1>(x, q, tw);
+    if (h == 8) stage16h<INV, 8, AR>(x, q, tw);
+    else if (h == 4) stage16h<INV, 4, AR>(x, q, tw);
+    else if (h == 2) stage16h<INV, 2, AR>(x, q, tw);
+    else stage16h<INV, 1, AR>(x, q, tw);
 }
 
 // A forward transform with a fused prologue and epilogue (FUSE = true): the rescale of up to
@@ -102,7 +141,7 @@ struct NttFuse {
 };
 
 // ---- phase "col": stages with distance >= 256 ----------------------------------------
-template <int LOGN, bool INV, bool FUSE = false>
+template <int LOGN, bool INV, bool FUSE = false, int AR = 0>
 __global__ void __launch_bounds__(256, 3) k_ntt_col(LimbMap mp, const ulonglong2* __restrict__ tw2,
                                                   const uint64_t* __restrict__ ninv, NttFuse fz) {
     pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
@@ -142,7 +181,7 @@ __global__ void __launch_bounds__(256, 3) k_ntt_col(LimbMap mp, const ulonglong2
         // part A: distances R/2 .. R/16 (register distance h = 8,4,2,1); twiddle 2^s + k/(2h)
 #pragma unroll
         for (int s = 0; s < 4; s++)
-            stage16<false>(x, q, 8 >> s, [&](int j) { return ld_tw(T2 + (1 << s) + j, pol); });
+            stage16<false, AR>(x, q, 8 >> s, [&](int j) { return ld_tw(T2 + (1 << s) + j, pol); });
         if (R == 16) {
 #pragma unroll
             for (int k = 0; k < 16; k++) a[(size_t)(g + G * k) * 256 + col] = x[k];
@@ -156,7 +195,7 @@ __global__ void __launch_bounds__(256, 3) k_ntt_col(LimbMap mp, const ulonglong2
         // part B: distances R/32 .. 1 (h = t_r), m_row = R/(2h), twiddle m_row + a2*(8/h) + k/(2h)
 #pragma unroll
         for (int h = R / 32; h >= 1; h >>= 1)
-            stage16<false>(x, q, h, [&](int j) { return ld_tw(T2 + R / (2 * h) + a2 * (8 / h) + j, pol); });
+            stage16<false, AR>(x, q, h, [&](int j) { return ld_tw(T2 + R / (2 * h) + a2 * (8 / h) + j, pol); });
 #pragma unroll
         for (int k = 0; k < 16; k++) a[(size_t)(16 * a2 + k) * 256 + col] = x[k];
     } else {
@@ -169,7 +208,7 @@ __global__ void __launch_bounds__(256, 3) k_ntt_col(LimbMap mp, const ulonglong2
             // inverse part B first: distances 1 .. R/32
 #pragma unroll
             for (int h = 1; h <= R / 32; h <<= 1)
-                stage16<true>(x, q, h, [&](int j) { return ld_tw(T2 + R / (2 * h) + a2 * (8 / h) + j, pol); });
+                stage16<true, AR>(x, q, h, [&](int j) { return ld_tw(T2 + R / (2 * h) + a2 * (8 / h) + j, pol); });
 #pragma unroll
             for (int k = 0; k < 16; k++) sm[(16 * a2 + k) * TC + c] = x[k];
             __syncthreads();
@@ -178,7 +217,7 @@ __global__ void __launch_bounds__(256, 3) k_ntt_col(LimbMap mp, const ulonglong2
         }
 #pragma unroll
         for (int s = 3; s >= 0; s--)
-            stage16<true>(x, q, 8 >> s, [&](int j) { return ld_tw(T2 + (1 << s) + j, pol); });
+            stage16<true, AR>(x, q, 8 >> s, [&](int j) { return ld_tw(T2 + (1 << s) + j, pol); });
         const uint64_t ni = ninv[2 * m], nip = ninv[2 * m + 1];
 #pragma unroll
         for (int k = 0; k < 16; k++) a[(size_t)(g + G * k) * 256 + col] = mul_shoup(x[k], ni, nip, q);
@@ -195,7 +234,7 @@ __global__ void __launch_bounds__(256, 3) k_ntt_col(LimbMap mp, const ulonglong2
 // rtab[bg][2^sp - 1 + j][r0] = Tab[2^(logN-4+sp) + bg * 2^(4+sp) + r0 * 2^sp + j], so a warp's
 // load covers consecutive pairs.
 constexpr int kRowTab = 240;   // pairs per 256-word block: 16 threads x (1 + 2 + 4 + 8)
-template <int LOGN, bool INV, bool FUSE = false>
+template <int LOGN, bool INV, bool FUSE = false, int AR = 0>
 __global__ void __launch_bounds__(256, 3) k_ntt_row(LimbMap mp, const ulonglong2* __restrict__ tw2,
                                                   const ulonglong2* __restrict__ rtab, NttFuse fz) {
     pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
@@ -224,7 +263,7 @@ __global__ void __launch_bounds__(256, 3) k_ntt_row(LimbMap mp, const ulonglong2
         // part A: distances 128,64,32,16 (h = 8..1), twiddle 2^(S1+s) + bg*2^s + k/(2h)
 #pragma unroll
         for (int s = 0; s < 4; s++)
-            stage16<false>(x, q, 8 >> s, [&](int j) { return ld_tw(T2 + (1 << (S1 + s)) + (bg << s) + j, pol); });
+            stage16<false, AR>(x, q, 8 >> s, [&](int j) { return ld_tw(T2 + (1 << (S1 + s)) + (bg << s) + j, pol); });
 #pragma unroll
         for (int k = 0; k < 16; k++) sA[17 * k] = x[k];
         __syncthreads();
@@ -233,10 +272,10 @@ __global__ void __launch_bounds__(256, 3) k_ntt_row(LimbMap mp, const ulonglong2
         // part B: distances 8,4,2,1
 #pragma unroll
         for (int sp = 0; sp < 4; sp++)
-            stage16<false>(x, q, 8 >> sp, [&](int j) { return ld_tw(RB + ((1 << sp) - 1 + j) * 16, pol); });
+            stage16<false, AR>(x, q, 8 >> sp, [&](int j) { return ld_tw(RB + ((1 << sp) - 1 + j) * 16, pol); });
         // each thread rewrites only the row it read: no barrier before the write
 #pragma unroll
-        for (int k = 0; k < 16; k++) sB[k] = canon4(x[k], q);
+        for (int k = 0; k < 16; k++) sB[k] = canon_out<AR>(x[k], q);
         __syncthreads();
         if (FUSE) {   // the rescaled limb in place of the transformed lift
             uint64_t* d = fz.dst[poly] + (size_t)limb * N + (size_t)blockIdx.x * 4096;
@@ -259,7 +298,7 @@ __global__ void __launch_bounds__(256, 3) k_ntt_row(LimbMap mp, const ulonglong2
         for (int k = 0; k < 16; k++) x[k] = sB[k];
 #pragma unroll
         for (int sp = 3; sp >= 0; sp--)
-            stage16<true>(x, q, 8 >> sp, [&](int j) { return ld_tw(RB + ((1 << sp) - 1 + j) * 16, pol); });
+            stage16<true, AR>(x, q, 8 >> sp, [&](int j) { return ld_tw(RB + ((1 << sp) - 1 + j) * 16, pol); });
 #pragma unroll
         for (int k = 0; k < 16; k++) sB[k] = x[k];   // own row: no barrier
         __syncthreads();
@@ -267,7 +306,7 @@ __global__ void __launch_bounds__(256, 3) k_ntt_row(LimbMap mp, const ulonglong2
         for (int k = 0; k < 16; k++) x[k] = sA[17 * k];
 #pragma unroll
         for (int s = 3; s >= 0; s--)
-            stage16<true>(x, q, 8 >> s, [&](int j) { return ld_tw(T2 + (1 << (S1 + s)) + (bg << s) + j, pol); });
+            stage16<true, AR>(x, q, 8 >> s, [&](int j) { return ld_tw(T2 + (1 << (S1 + s)) + (bg << s) + j, pol); });
 #pragma unroll
         for (int k = 0; k < 16; k++) a[b * 256 + r0 + 16 * k] = x[k];
     }
@@ -426,22 +465,27 @@ static void launch_ntt_cluster(const Context& cx, const LimbMap& mp, int count, 
                    (const ulonglong2*)cx.d_tw2, (const ulonglong2*)cx.d_twrow, cx.d_ninv);
 }
 
-template <int LOGN>
-static void launch_ntt(const Context& cx, const LimbMap& mp, int count, bool inv, cudaStream_t st) {
+template <int LOGN, int AR>
+static void launch_ntt_ar(const Context& cx, const LimbMap& mp, int count, bool inv, cudaStream_t st) {
     constexpr int N = 1 << LOGN;
     constexpr int R = N >> 8;
     dim3 gcol(R / 16, count), grow(N / 4096, count);
     if (!inv) {
-        launch_pdl(cx, k_ntt_col<LOGN, false>, gcol, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_tw2, cx.d_ninv,
-                   NttFuse{});
-        launch_pdl(cx, k_ntt_row<LOGN, false>, grow, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_tw2,
+        launch_pdl(cx, k_ntt_col<LOGN, false, false, AR>, gcol, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_tw2,
+                   cx.d_ninv, NttFuse{});
+        launch_pdl(cx, k_ntt_row<LOGN, false, false, AR>, grow, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_tw2,
                    (const ulonglong2*)cx.d_twrow, NttFuse{});
     } else {
-        launch_pdl(cx, k_ntt_row<LOGN, true>, grow, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_itw2,
+        launch_pdl(cx, k_ntt_row<LOGN, true, false, AR>, grow, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_itw2,
                    (const ulonglong2*)cx.d_itwrow, NttFuse{});
-        launch_pdl(cx, k_ntt_col<LOGN, true>, gcol, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_itw2, cx.d_ninv,
-                   NttFuse{});
+        launch_pdl(cx, k_ntt_col<LOGN, true, false, AR>, gcol, dim3(256), 0, st, mp, (const ulonglong2*)cx.d_itw2,
+                   cx.d_ninv, NttFuse{});
     }
+}
+template <int LOGN>
+static void launch_ntt(const Context& cx, const LimbMap& mp, int count, bool inv, cudaStream_t st) {
+    if (cx.ntt_arith == 1) launch_ntt_ar<LOGN, 1>(cx, mp, count, inv, st);
+    else launch_ntt_ar<LOGN, 0>(cx, mp, count, inv, st);
 }
 
 void ntt(const Context& cx, const LimbMap& mp, int npoly, bool inv, cudaStream_t st) {
@@ -478,14 +522,20 @@ void ntt(const Context& cx, const LimbMap& mp, int npoly, bool inv, cudaStream_t
     cx.launches += 2;
 }
 
-template <int LOGN>
-static void launch_ntt_rescale(const Context& cx, const LimbMap& mp, int count, const NttFuse& fz, cudaStream_t st) {
+template <int LOGN, int AR>
+static void launch_ntt_rescale_ar(const Context& cx, const LimbMap& mp, int count, const NttFuse& fz,
+                                  cudaStream_t st) {
     constexpr int N = 1 << LOGN;
     constexpr int R = N >> 8;
-    launch_pdl(cx, k_ntt_col<LOGN, false, true>, dim3(R / 16, count), dim3(256), 0, st, mp,
+    launch_pdl(cx, k_ntt_col<LOGN, false, true, AR>, dim3(R / 16, count), dim3(256), 0, st, mp,
                (const ulonglong2*)cx.d_tw2, cx.d_ninv, fz);
-    launch_pdl(cx, k_ntt_row<LOGN, false, true>, dim3(N / 4096, count), dim3(256), 0, st, mp,
+    launch_pdl(cx, k_ntt_row<LOGN, false, true, AR>, dim3(N / 4096, count), dim3(256), 0, st, mp,
                (const ulonglong2*)cx.d_tw2, (const ulonglong2*)cx.d_twrow, fz);
+}
+template <int LOGN>
+static void launch_ntt_rescale(const Context& cx, const LimbMap& mp, int count, const NttFuse& fz, cudaStream_t st) {
+    if (cx.ntt_arith == 1) launch_ntt_rescale_ar<LOGN, 1>(cx, mp, count, fz, st);
+    else launch_ntt_rescale_ar<LOGN, 0>(cx, mp, count, fz, st);
 }
 
 // The rescale of npoly polynomials with l + 1 limbs each (npoly <= kFuseMax), past the inverse
