@@ -632,7 +632,8 @@ void ct_mul_relin_rescale(Context& cx, const Ciphertext& a, const Ciphertext& b,
 struct LimbPtrs {
     const uint64_t* src[kFuseMax];
 };
-__global__ void __launch_bounds__(256) k_gather_limbs(const LimbPtrs g, uint64_t* __restrict__ dst, int logN) {
+__global__ void __launch_bounds__(256) k_gather_limbs(const __grid_constant__ LimbPtrs g, uint64_t* __restrict__ dst,
+                                                      int logN) {
     pdl_wait();
     pdl_trigger();
     const int x = blockIdx.x * blockDim.x + threadIdx.x, p = blockIdx.y;

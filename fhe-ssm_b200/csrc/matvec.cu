@@ -399,34 +399,48 @@ struct BabyArgs {
     uint64_t perm[64];
     uint64_t pw[kMaxMod], pwp[kMaxMod];   // P mod q_i (Shoup)
 };
+// Each thread owns one slot x of one baby and walks `per` consecutive limbs e (Context::
+// baby_limbs): the permuted source slot, the baby's key pointer and its index are computed once
+// per thread, not once per limb.
 __global__ void __launch_bounds__(256) k_baby_pq(const uint64_t* __restrict__ ext, const uint64_t* __restrict__ u0,
-                                                 const uint64_t* __restrict__ u1, const BabyArgs a,
+                                                 const uint64_t* __restrict__ u1, const __grid_constant__ BabyArgs a,
                                                  uint64_t* __restrict__ out, int nl, int ne, int dn, int L, int K,
-                                                 int logN) {
+                                                 int logN, int per) {
     const int N = 1 << logN;
     const int x = blockIdx.x * blockDim.x + threadIdx.x;
-    const int e = blockIdx.y, b = blockIdx.z;
-    const int m = e < nl ? e : L + (e - nl);
-    const ModConst mc = c_mod[m];
+    const int b = blockIdx.z;
+    const int e0 = blockIdx.y * per, e1 = min(ne, e0 + per);
     uint64_t* o = out + (size_t)b * 2 * ne * N;
     const uint64_t k = a.perm[b];
-    uint64_t v0, v1;
     if (k == 1) {
-        v0 = e < nl ? mul_shoup(u0[(size_t)e * N + x], a.pw[e], a.pwp[e], mc.q) : 0;
-        v1 = e < nl ? mul_shoup(u1[(size_t)e * N + x], a.pw[e], a.pwp[e], mc.q) : 0;
-    } else {
-        const uint32_t sx = auto_src((uint32_t)x, k, logN);
-        const uint64_t* key = a.fkey[b];
-        const size_t nk = (size_t)(L + K);
+        for (int e = e0; e < e1; e++) {
+            const uint64_t q = c_mod[e < nl ? e : L + (e - nl)].q;
+            uint64_t v0 = 0, v1 = 0;
+            if (e < nl) {
+                v0 = mul_shoup(u0[(size_t)e * N + x], a.pw[e], a.pwp[e], q);
+                v1 = mul_shoup(u1[(size_t)e * N + x], a.pw[e], a.pwp[e], q);
+            }
+            o[(size_t)e * N + x] = v0;
+            o[((size_t)ne + e) * N + x] = v1;
+        }
+        return;
+    }
+    const uint32_t sx = auto_src((uint32_t)x, k, logN);
+    const uint64_t* key = a.fkey[b];
+    const size_t nk = (size_t)(L + K);
+#pragma unroll 1
+    for (int e = e0; e < e1; e++) {
+        const int m = e < nl ? e : L + (e - nl);
+        const ModConst mc = c_mod[m];
         u128acc a0{0, 0}, a1{0, 0};
         digit_dot2(ext + (size_t)e * N + sx, (size_t)ne * N, key + (size_t)m * N + x, key + (nk + m) * N + x,
                    2 * nk * N, dn, a0, a1);
-        v0 = redc(a0.hi, a0.lo, mc);
-        v1 = redc(a1.hi, a1.lo, mc);
+        uint64_t v0 = redc(a0.hi, a0.lo, mc);
+        const uint64_t v1 = redc(a1.hi, a1.lo, mc);
         if (e < nl) v0 = mod_add(v0, mul_shoup(u0[(size_t)e * N + sx], a.pw[e], a.pwp[e], mc.q), mc.q);
+        o[(size_t)e * N + x] = v0;
+        o[((size_t)ne + e) * N + x] = v1;
     }
-    o[(size_t)e * N + x] = v0;
-    o[((size_t)ne + e) * N + x] = v1;
 }
 
 // -------------------------------------------------------------------------- the plan ----
@@ -638,9 +652,10 @@ void matvec_babies(Context& cx, const Ciphertext& u, int D, int b1, BabySet& bs)
             ba.fkey[b] = k == 1 ? nullptr : forward_key(cx, k);
         }
         ProfScope ps(cx, "baby_pq", 8.0 * N * B * ((double)dn * ne * 2 + 2 * ne));
-        k_baby_pq<<<dim3(N / 256, ne, B), 256, 0, st>>>(ext.p, u.c(0), u.c(1), ba,
-                                                        bs.pq.p + (size_t)b0 * 2 * ne * N, nl, ne, dn, L, K,
-                                                        cx.logN);
+        const int per = std::max(1, cx.baby_limbs);
+        k_baby_pq<<<dim3(N / 256, (ne + per - 1) / per, B), 256, 0, st>>>(ext.p, u.c(0), u.c(1), ba,
+                                                                          bs.pq.p + (size_t)b0 * 2 * ne * N, nl, ne,
+                                                                          dn, L, K, cx.logN, per);
         CUDA_CHECK(cudaGetLastError());
         cx.launches++;
         cx.ks_count += B;

@@ -143,7 +143,8 @@ struct NttFuse {
 // ---- phase "col": stages with distance >= 256 ----------------------------------------
 template <int LOGN, bool INV, bool FUSE = false, int AR = 0>
 __global__ void __launch_bounds__(256, 3) k_ntt_col(LimbMap mp, const ulonglong2* __restrict__ tw2,
-                                                  const uint64_t* __restrict__ ninv, NttFuse fz) {
+                                                  const uint64_t* __restrict__ ninv,
+                                                  const __grid_constant__ NttFuse fz) {
     pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
     pdl_trigger();
     constexpr int N = 1 << LOGN;
@@ -236,7 +237,8 @@ __global__ void __launch_bounds__(256, 3) k_ntt_col(LimbMap mp, const ulonglong2
 constexpr int kRowTab = 240;   // pairs per 256-word block: 16 threads x (1 + 2 + 4 + 8)
 template <int LOGN, bool INV, bool FUSE = false, int AR = 0>
 __global__ void __launch_bounds__(256, 3) k_ntt_row(LimbMap mp, const ulonglong2* __restrict__ tw2,
-                                                  const ulonglong2* __restrict__ rtab, NttFuse fz) {
+                                                  const ulonglong2* __restrict__ rtab,
+                                                  const __grid_constant__ NttFuse fz) {
     pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
     pdl_trigger();
     constexpr int N = 1 << LOGN;
