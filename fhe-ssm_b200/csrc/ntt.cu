@@ -46,24 +46,58 @@ __device__ __forceinline__ uint64_t mul_shoup_q4(uint64_t x, uint64_t w, uint64_
     return x * w - est * q;
 }
 
+// mul_shoup_q4 in explicit 32-bit steps (AR = 2 butterflies), the same words: the quotient
+// estimate from three 32 x 32 products, then x w - est q modulo 2^64 as x w + est (2^64 - q)
+// with the subtraction folded into the multiply-adds (nq = 2^64 - q): six multiply-adds, of
+// which the products landing at and above bit 64 are never formed.
+__device__ __forceinline__ uint64_t mul_shoup_q4_ptx(uint64_t x, uint64_t w, uint64_t wp, uint64_t nq) {
+    uint64_t r;
+    asm("{\n\t"
+        ".reg .u32 x0, x1, w0, w1, p0, p1, n0, n1, h0, h1, e0, e1, r0, r1;\n\t"
+        ".reg .u64 e, t;\n\t"
+        "mov.b64 {x0, x1}, %1;\n\t"
+        "mov.b64 {w0, w1}, %2;\n\t"
+        "mov.b64 {p0, p1}, %3;\n\t"
+        "mov.b64 {n0, n1}, %4;\n\t"
+        "mul.hi.u32 h0, x0, p1;\n\t"
+        "mul.hi.u32 h1, x1, p0;\n\t"
+        "cvt.u64.u32 t, h0;\n\t"
+        "mad.wide.u32 e, x1, p1, t;\n\t"       // est = x1 p1 + hi(x0 p1)
+        "cvt.u64.u32 t, h1;\n\t"
+        "add.u64 e, e, t;\n\t"                  //     + hi(x1 p0)
+        "mov.b64 {e0, e1}, e;\n\t"
+        "mul.wide.u32 t, x0, w0;\n\t"
+        "mad.wide.u32 t, e0, n0, t;\n\t"        // low words: x0 w0 + e0 n0
+        "mov.b64 {r0, r1}, t;\n\t"
+        "mad.lo.u32 r1, x0, w1, r1;\n\t"
+        "mad.lo.u32 r1, x1, w0, r1;\n\t"
+        "mad.lo.u32 r1, e0, n1, r1;\n\t"
+        "mad.lo.u32 r1, e1, n0, r1;\n\t"
+        "mov.b64 %0, {r0, r1};\n\t"
+        "}"
+        : "=l"(r)
+        : "l"(x), "l"(w), "l"(wp), "l"(nq));
+    return r;
+}
+
 // AR = 0: the Harvey butterflies above.  AR = 1: the same with mul_shoup_q4; forward values in
 // [0, 8q + 2^32) (u is brought below 4q + 2^32 by the high-word test against 4q), inverse values
 // in [0, 4q).  8q + 2^33 < 2^64 for the moduli below 2^61.
 template <bool INV, int AR = 0>
 __device__ __forceinline__ void bfly(uint64_t& lo, uint64_t& hi, uint64_t w, uint64_t wp, uint64_t q) {
-    if (AR == 1) {
+    if (AR >= 1) {
         const uint64_t q4 = q << 2;
         if (!INV) {
             uint64_t u = lo;
             if ((uint32_t)(u >> 32) > (uint32_t)(q4 >> 32)) u -= q4;
-            const uint64_t x = mul_shoup_q4(hi, w, wp, q);
+            const uint64_t x = AR == 2 ? mul_shoup_q4_ptx(hi, w, wp, 0 - q) : mul_shoup_q4(hi, w, wp, q);
             lo = u + x;
             hi = u - x + q4;
         } else {
             uint64_t u = lo + hi;
             if (u >= q4) u -= q4;
             const uint64_t t = lo - hi + q4;
-            hi = mul_shoup_q4(t, w, wp, q);
+            hi = AR == 2 ? mul_shoup_q4_ptx(t, w, wp, 0 - q) : mul_shoup_q4(t, w, wp, q);
             lo = u;
         }
         return;
@@ -92,7 +126,7 @@ __device__ __forceinline__ uint64_t canon4(uint64_t v, uint64_t q) {   // [0, 4q
 // the forward transform's output range of butterflies AR -> [0, q)  (2^32 < q)
 template <int AR>
 __device__ __forceinline__ uint64_t canon_out(uint64_t v, uint64_t q) {
-    if (AR == 0) return canon4(v, q);
+    if (AR == 0) return canon4(v, q);   // AR 1 and 2: the same ranges
     const uint64_t q4 = q << 2, q2 = q << 1;
     if (v >= q4) v -= q4;   // [0, 8q + 2^32) -> [0, 4q + 2^32) < 5q
     if (v >= q2) v -= q2;   // < 3q
@@ -486,7 +520,8 @@ static void launch_ntt_ar(const Context& cx, const LimbMap& mp, int count, bool 
 }
 template <int LOGN>
 static void launch_ntt(const Context& cx, const LimbMap& mp, int count, bool inv, cudaStream_t st) {
-    if (cx.ntt_arith == 1) launch_ntt_ar<LOGN, 1>(cx, mp, count, inv, st);
+    if (cx.ntt_arith == 2) launch_ntt_ar<LOGN, 2>(cx, mp, count, inv, st);
+    else if (cx.ntt_arith == 1) launch_ntt_ar<LOGN, 1>(cx, mp, count, inv, st);
     else launch_ntt_ar<LOGN, 0>(cx, mp, count, inv, st);
 }
 
@@ -536,7 +571,8 @@ static void launch_ntt_rescale_ar(const Context& cx, const LimbMap& mp, int coun
 }
 template <int LOGN>
 static void launch_ntt_rescale(const Context& cx, const LimbMap& mp, int count, const NttFuse& fz, cudaStream_t st) {
-    if (cx.ntt_arith == 1) launch_ntt_rescale_ar<LOGN, 1>(cx, mp, count, fz, st);
+    if (cx.ntt_arith == 2) launch_ntt_rescale_ar<LOGN, 2>(cx, mp, count, fz, st);
+    else if (cx.ntt_arith == 1) launch_ntt_rescale_ar<LOGN, 1>(cx, mp, count, fz, st);
     else launch_ntt_rescale_ar<LOGN, 0>(cx, mp, count, fz, st);
 }
 
