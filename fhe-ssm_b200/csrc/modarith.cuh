@@ -64,9 +64,39 @@ __device__ __forceinline__ uint64_t mul_barrett(uint64_t a, uint64_t b, const Mo
 struct u128acc {
     uint64_t lo, hi;
 };
+// acc += a * b (128-bit), column by column in 32-bit words with three carry chains: the
+// products a0 b0 and a1 b1 land in their own columns in one chain, the two cross products in one
+// chain each (ten multiply-adds and carry adds; the accumulator never overflows 128 bits here)
+#ifndef FHESSM_ACC_PTX
+#define FHESSM_ACC_PTX 1
+#endif
 __device__ __forceinline__ void acc_mad(u128acc& acc, uint64_t a, uint64_t b) {
+#if !FHESSM_ACC_PTX
     const uint64_t pl = a * b, ph = __umul64hi(a, b);
     asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(acc.lo), "+l"(acc.hi) : "l"(pl), "l"(ph));
+    return;
+#endif
+    asm("{\n\t"
+        ".reg .u32 a0, a1, b0, b1, s0, s1, s2, s3;\n\t"
+        "mov.b64 {a0, a1}, %2;\n\t"
+        "mov.b64 {b0, b1}, %3;\n\t"
+        "mov.b64 {s0, s1}, %0;\n\t"
+        "mov.b64 {s2, s3}, %1;\n\t"
+        "mad.lo.cc.u32 s0, a0, b0, s0;\n\t"
+        "madc.hi.cc.u32 s1, a0, b0, s1;\n\t"
+        "madc.lo.cc.u32 s2, a1, b1, s2;\n\t"
+        "madc.hi.u32 s3, a1, b1, s3;\n\t"
+        "mad.lo.cc.u32 s1, a0, b1, s1;\n\t"
+        "madc.hi.cc.u32 s2, a0, b1, s2;\n\t"
+        "addc.u32 s3, s3, 0;\n\t"
+        "mad.lo.cc.u32 s1, a1, b0, s1;\n\t"
+        "madc.hi.cc.u32 s2, a1, b0, s2;\n\t"
+        "addc.u32 s3, s3, 0;\n\t"
+        "mov.b64 %0, {s0, s1};\n\t"
+        "mov.b64 %1, {s2, s3};\n\t"
+        "}"
+        : "+l"(acc.lo), "+l"(acc.hi)
+        : "l"(a), "l"(b));
 }
 // Montgomery: returns T * 2^-64 mod q for T = hi:lo < q * 2^64, canonical.
 __device__ __forceinline__ uint64_t redc(uint64_t hi, uint64_t lo, const ModConst& m) {

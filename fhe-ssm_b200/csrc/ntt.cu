@@ -37,20 +37,13 @@ __device__ __forceinline__ ulonglong2 ld_tw(const ulonglong2* a, uint64_t pol) {
     return v;
 }
 
-// Shoup product with a cheaper quotient (AR = 1 butterflies): the high 64 bits of x * wp without
-// the x_lo * wp_lo term and the carries out of the cross terms' low halves.  The estimate is 0 to
-// 2 below floor(x wp / 2^64), so x * w - est * q lies in [0, 4q) (Shoup's exact quotient: [0, 2q)).
-__device__ __forceinline__ uint64_t mul_shoup_q4(uint64_t x, uint64_t w, uint64_t wp, uint64_t q) {
-    const uint32_t x0 = (uint32_t)x, x1 = (uint32_t)(x >> 32), p0 = (uint32_t)wp, p1 = (uint32_t)(wp >> 32);
-    const uint64_t est = (uint64_t)x1 * p1 + __umulhi(x0, p1) + __umulhi(x1, p0);
-    return x * w - est * q;
-}
-
-// mul_shoup_q4 in explicit 32-bit steps (AR = 2 butterflies), the same words: the quotient
-// estimate from three 32 x 32 products, then x w - est q modulo 2^64 as x w + est (2^64 - q)
-// with the subtraction folded into the multiply-adds (nq = 2^64 - q): six multiply-adds, of
-// which the products landing at and above bit 64 are never formed.
-__device__ __forceinline__ uint64_t mul_shoup_q4_ptx(uint64_t x, uint64_t w, uint64_t wp, uint64_t nq) {
+// Shoup product with a cheaper quotient (AR = 1 butterflies), written as explicit 32-bit steps.
+// est = x1 p1 + hi(x0 p1) + hi(x1 p0) is the high 64 bits of x * wp without the x0 * p0 term and
+// the carries out of the cross terms' low halves (x = x1:x0, wp = p1:p0 in 32-bit words): 0 to 2
+// below floor(x wp / 2^64), so x w - est q lies in [0, 4q) (Shoup's exact quotient: [0, 2q)).
+// x w - est q is formed modulo 2^64 as x w + est (2^64 - q) (nq = 2^64 - q), the subtraction
+// folded into the multiply-adds: nine 32-bit multiplies in all, no product at or above bit 64.
+__device__ __forceinline__ uint64_t mul_shoup_q4(uint64_t x, uint64_t w, uint64_t wp, uint64_t nq) {
     uint64_t r;
     asm("{\n\t"
         ".reg .u32 x0, x1, w0, w1, p0, p1, n0, n1, h0, h1, e0, e1, r0, r1;\n\t"
@@ -82,22 +75,22 @@ __device__ __forceinline__ uint64_t mul_shoup_q4_ptx(uint64_t x, uint64_t w, uin
 
 // AR = 0: the Harvey butterflies above.  AR = 1: the same with mul_shoup_q4; forward values in
 // [0, 8q + 2^32) (u is brought below 4q + 2^32 by the high-word test against 4q), inverse values
-// in [0, 4q).  8q + 2^33 < 2^64 for the moduli below 2^61.
+// in [0, 4q).  8q + 2^33 < 2^64 for the moduli below 2^61.  The output words are the same.
 template <bool INV, int AR = 0>
 __device__ __forceinline__ void bfly(uint64_t& lo, uint64_t& hi, uint64_t w, uint64_t wp, uint64_t q) {
-    if (AR >= 1) {
+    if (AR == 1) {
         const uint64_t q4 = q << 2;
         if (!INV) {
             uint64_t u = lo;
             if ((uint32_t)(u >> 32) > (uint32_t)(q4 >> 32)) u -= q4;
-            const uint64_t x = AR == 2 ? mul_shoup_q4_ptx(hi, w, wp, 0 - q) : mul_shoup_q4(hi, w, wp, q);
+            const uint64_t x = mul_shoup_q4(hi, w, wp, 0 - q);
             lo = u + x;
             hi = u - x + q4;
         } else {
             uint64_t u = lo + hi;
             if (u >= q4) u -= q4;
             const uint64_t t = lo - hi + q4;
-            hi = AR == 2 ? mul_shoup_q4_ptx(t, w, wp, 0 - q) : mul_shoup_q4(t, w, wp, q);
+            hi = mul_shoup_q4(t, w, wp, 0 - q);
             lo = u;
         }
         return;
@@ -126,7 +119,7 @@ __device__ __forceinline__ uint64_t canon4(uint64_t v, uint64_t q) {   // [0, 4q
 // the forward transform's output range of butterflies AR -> [0, q)  (2^32 < q)
 template <int AR>
 __device__ __forceinline__ uint64_t canon_out(uint64_t v, uint64_t q) {
-    if (AR == 0) return canon4(v, q);   // AR 1 and 2: the same ranges
+    if (AR == 0) return canon4(v, q);
     const uint64_t q4 = q << 2, q2 = q << 1;
     if (v >= q4) v -= q4;   // [0, 8q + 2^32) -> [0, 4q + 2^32) < 5q
     if (v >= q2) v -= q2;   // < 3q
@@ -520,8 +513,7 @@ static void launch_ntt_ar(const Context& cx, const LimbMap& mp, int count, bool 
 }
 template <int LOGN>
 static void launch_ntt(const Context& cx, const LimbMap& mp, int count, bool inv, cudaStream_t st) {
-    if (cx.ntt_arith == 2) launch_ntt_ar<LOGN, 2>(cx, mp, count, inv, st);
-    else if (cx.ntt_arith == 1) launch_ntt_ar<LOGN, 1>(cx, mp, count, inv, st);
+    if (cx.ntt_arith == 1) launch_ntt_ar<LOGN, 1>(cx, mp, count, inv, st);
     else launch_ntt_ar<LOGN, 0>(cx, mp, count, inv, st);
 }
 
@@ -571,8 +563,7 @@ static void launch_ntt_rescale_ar(const Context& cx, const LimbMap& mp, int coun
 }
 template <int LOGN>
 static void launch_ntt_rescale(const Context& cx, const LimbMap& mp, int count, const NttFuse& fz, cudaStream_t st) {
-    if (cx.ntt_arith == 2) launch_ntt_rescale_ar<LOGN, 2>(cx, mp, count, fz, st);
-    else if (cx.ntt_arith == 1) launch_ntt_rescale_ar<LOGN, 1>(cx, mp, count, fz, st);
+    if (cx.ntt_arith == 1) launch_ntt_rescale_ar<LOGN, 1>(cx, mp, count, fz, st);
     else launch_ntt_rescale_ar<LOGN, 0>(cx, mp, count, fz, st);
 }
 
