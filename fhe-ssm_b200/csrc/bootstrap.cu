@@ -237,8 +237,8 @@ __global__ void __launch_bounds__(256, 4) k_diag_mac(const DiagArgs a, int logN,
         for (int j = 0; j < H; j++) {
             if (j0 + j >= a.nb || !a.pt[g][j0 + j]) continue;
             const uint64_t p = a.pt[g][j0 + j][w];
-            acc_mad(s0, p, v0[j]);
-            acc_mad(s1, p, v1[j]);
+            acc_mad32(s0, p, v0[j]);
+            acc_mad32(s1, p, v1[j]);
         }
         // the partner's sum of the output this thread writes
         const uint64_t mlo = half ? s0.lo : s1.lo, mhi = half ? s0.hi : s1.hi;

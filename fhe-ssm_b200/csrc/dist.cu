@@ -110,7 +110,7 @@ __global__ void __launch_bounds__(256) k_dist_modup(const uint64_t* __restrict__
     for (int a = 0; a < 8; a++)
         if (a < sz) {
             const uint64_t t = mul_shoup(dcoef[(size_t)(lo + a) * N + x], qhinv[2 * a], qhinv[2 * a + 1], c_mod[lo + a].q);
-            acc_mad(s, t, w[2 * a + 1]);
+            acc_mad32(s, t, w[2 * a + 1]);
         }
     *out = redc(s.hi, s.lo, mt);
 }

@@ -63,7 +63,7 @@ __global__ void __launch_bounds__(256) k_modup_bconv(const uint64_t* __restrict_
         u128acc s{0, 0};
 #pragma unroll
         for (int a = 0; a < 8; a++)   // constants in Montgomery form: sum < 8 2^60 t < t 2^64
-            if (a < sz) acc_mad(s, t[a], w[2 * a + 1]);
+            if (a < sz) acc_mad32(s, t[a], w[2 * a + 1]);
         out[(size_t)e * N + x] = redc(s.hi, s.lo, mt);
     }
 }

@@ -82,6 +82,54 @@ __global__ void __launch_bounds__(256) k_key_inner_b(const uint64_t* __restrict_
     out[((size_t)ne + e) * N + x] = s1;
 }
 
+// Key inner products of B ModUp outputs against one shared key (the relinearisation key of a
+// batch of products): out[b][c][e] = sum_j ext_b[j][e] * key[j][c][m(e)].  A thread serves
+// kKeyShare outputs of one slot, so each key word is read once per kKeyShare products.
+constexpr int kKeyShare = 4;
+__global__ void __launch_bounds__(256) k_key_inner_shared(const uint64_t* __restrict__ ext, long long ext_stride,
+                                                          const uint64_t* __restrict__ key, int B,
+                                                          uint64_t* __restrict__ out, int nl, int ne, int dnum, int L,
+                                                          int K, int logN) {
+    pdl_wait();   // launched by launch_pdl: the previous kernel's writes first
+    pdl_trigger();
+    const int N = 1 << logN;
+    const int x = blockIdx.x * blockDim.x + threadIdx.x;
+    const int e = blockIdx.y;
+    const int b0 = blockIdx.z * kKeyShare, nb = min(kKeyShare, B - b0);
+    const int m = e < nl ? e : L + (e - nl);
+    const ModConst mc = c_mod[m];
+    const size_t nk = (size_t)(L + K);
+    const uint64_t pol = evict_first_policy();
+    const uint64_t* k0 = key + (size_t)m * N + x;
+    const uint64_t* k1 = key + (nk + m) * N + x;
+    const uint64_t* eb = ext + (size_t)b0 * ext_stride + (size_t)e * N + x;
+    u128acc a0[kKeyShare], a1[kKeyShare];
+#pragma unroll
+    for (int i = 0; i < kKeyShare; i++) a0[i] = a1[i] = u128acc{0, 0};
+#pragma unroll 2
+    for (int j = 0; j < dnum; j++) {
+        const uint64_t v0 = ld_stream(k0 + (size_t)j * 2 * nk * N, pol);
+        const uint64_t v1 = ld_stream(k1 + (size_t)j * 2 * nk * N, pol);
+        uint64_t dv[kKeyShare];
+#pragma unroll
+        for (int i = 0; i < kKeyShare; i++)
+            if (i < nb) dv[i] = eb[(size_t)i * ext_stride + (size_t)j * ne * N];
+#pragma unroll
+        for (int i = 0; i < kKeyShare; i++)
+            if (i < nb) {
+                acc_mad(a0[i], dv[i], v0);
+                acc_mad(a1[i], dv[i], v1);
+            }
+    }
+#pragma unroll
+    for (int i = 0; i < kKeyShare; i++)
+        if (i < nb) {
+            uint64_t* o = out + (size_t)(b0 + i) * 2 * ne * N;
+            o[(size_t)e * N + x] = redc(a0[i].hi, a0[i].lo, mc);
+            o[((size_t)ne + e) * N + x] = redc(a1[i].hi, a1[i].lo, mc);
+        }
+}
+
 // Batched ModDown epilogue: out_c(b)[i][x] = add_c[i][s] + (buf_b[c][i][s] - y_b[c][i][s]) P^-1
 // with s = auto_src(x, perm_b); add_0 = add0 (shared), add_1 = none.  grid z = 2 * batch.
 __global__ void __launch_bounds__(256) k_moddown_final_b(const uint64_t* __restrict__ buf,
@@ -312,11 +360,11 @@ void ct_mul_relin_rescale_n(Context& cx, const Ciphertext* const* a, const Ciphe
     ntt(cx, em, B * dn, false, st);
     DevBuf ip((size_t)B * 2 * ne * N, st);
     {
-        KeyBatch kb{};
-        for (int k = 0; k < B; k++) kb.k[k] = cx.rlk->buf.p;
-        ProfScope ps(cx, "key_inner", 8.0 * N * B * ((double)dn * ne * 3 + 2 * ne));
-        launch_pdl(cx, k_key_inner_b, g2(cx, ne, B), dim3(256), 0, st, ext.p, (long long)dn * ne * N, kb, B, ip.p, nl, ne, dn, L, K,
-                                                     cx.logN, 0, 0);
+        // the relinearisation key is read once per kKeyShare products
+        const int nz = (B + kKeyShare - 1) / kKeyShare;
+        ProfScope ps(cx, "key_inner", 8.0 * N * ((double)dn * ne * (B + 2.0 * nz) + 2.0 * B * ne));
+        launch_pdl(cx, k_key_inner_shared, g2(cx, ne, nz), dim3(256), 0, st, ext.p, (long long)dn * ne * N,
+                   (const uint64_t*)cx.rlk->buf.p, B, ip.p, nl, ne, dn, L, K, cx.logN);
     }
     cx.ks_count += B;
     cx.ks_limbs += (long long)B * nl;

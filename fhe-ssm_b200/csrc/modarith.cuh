@@ -64,18 +64,16 @@ __device__ __forceinline__ uint64_t mul_barrett(uint64_t a, uint64_t b, const Mo
 struct u128acc {
     uint64_t lo, hi;
 };
-// acc += a * b (128-bit), column by column in 32-bit words with three carry chains: the
-// products a0 b0 and a1 b1 land in their own columns in one chain, the two cross products in one
-// chain each (ten multiply-adds and carry adds; the accumulator never overflows 128 bits here)
-#ifndef FHESSM_ACC_PTX
-#define FHESSM_ACC_PTX 1
-#endif
 __device__ __forceinline__ void acc_mad(u128acc& acc, uint64_t a, uint64_t b) {
-#if !FHESSM_ACC_PTX
     const uint64_t pl = a * b, ph = __umul64hi(a, b);
     asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(acc.lo), "+l"(acc.hi) : "l"(pl), "l"(ph));
-    return;
-#endif
+}
+// The same sum, column by column in 32-bit words with three carry chains: the products a0 b0 and
+// a1 b1 land in their own columns in one chain, the two cross products in one chain each (ten
+// multiply-adds and carry adds).  Fewer instructions than acc_mad, but it keeps more registers
+// live: it pays in the kernels with few loads in flight (the base conversion, the bootstrap's
+// diagonal sums) and costs occupancy in the key inner products, which keep acc_mad.
+__device__ __forceinline__ void acc_mad32(u128acc& acc, uint64_t a, uint64_t b) {
     asm("{\n\t"
         ".reg .u32 a0, a1, b0, b1, s0, s1, s2, s3;\n\t"
         "mov.b64 {a0, a1}, %2;\n\t"
