@@ -278,8 +278,7 @@ static void eval_level(Context& cx, const BootLevel& L, const Ciphertext& v, Cip
         {
             ProfScope ps(cx, "baby_pq", 8.0 * N * nb * ((double)dn * ne * 2 + 2 * ne));
             const int per = std::max(1, cx.baby_limbs);
-            auto kern = cx.baby_async ? k_baby_pq_async : k_baby_pq;
-            kern<<<dim3(N / 256, (ne + per - 1) / per, nb), 256, 0, st>>>(ext.p, v.c(0), v.c(1), ba, bq.p, nl, ne,
+            k_baby_pq<<<dim3(N / 256, (ne + per - 1) / per, nb), 256, 0, st>>>(ext.p, v.c(0), v.c(1), ba, bq.p, nl, ne,
                                                                            dn, cx.L, K, cx.logN, per);
             CUDA_CHECK(cudaGetLastError());
         }

@@ -443,96 +443,6 @@ __global__ void __launch_bounds__(256) k_baby_pq(const uint64_t* __restrict__ ex
     }
 }
 
-// k_baby_pq with the key and source words streamed through a per-thread ring of kBabyStages
-// shared-memory slots by asynchronous copies (cp.async): the loads of the next kBabyStages - 1
-// (limb, digit) steps are in flight while a step is multiplied, and no register holds a word
-// that is still on its way.  Each thread reads only its own slots, so no barrier is needed;
-// cp.async.wait_group is the only wait.  The same words as k_baby_pq.
-constexpr int kBabyStages = 4;
-__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async8_hint(uint32_t dst, const void* src, uint64_t pol) {
-    asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "l"(pol)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int W>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(W) : "memory");
-}
-__global__ void __launch_bounds__(256) k_baby_pq_async(const uint64_t* __restrict__ ext,
-                                                       const uint64_t* __restrict__ u0,
-                                                       const uint64_t* __restrict__ u1,
-                                                       const __grid_constant__ BabyArgs a, uint64_t* __restrict__ out,
-                                                       int nl, int ne, int dn, int L, int K, int logN, int per) {
-    __shared__ uint64_t sbuf[kBabyStages][3][256];
-    const int N = 1 << logN;
-    const int tid = threadIdx.x;
-    const int x = blockIdx.x * blockDim.x + tid;
-    const int b = blockIdx.z;
-    const int e0 = blockIdx.y * per, e1 = min(ne, e0 + per);
-    uint64_t* o = out + (size_t)b * 2 * ne * N;
-    const uint64_t k = a.perm[b];
-    if (k == 1) {
-        for (int e = e0; e < e1; e++) {
-            const uint64_t q = c_mod[e < nl ? e : L + (e - nl)].q;
-            uint64_t v0 = 0, v1 = 0;
-            if (e < nl) {
-                v0 = mul_shoup(u0[(size_t)e * N + x], a.pw[e], a.pwp[e], q);
-                v1 = mul_shoup(u1[(size_t)e * N + x], a.pw[e], a.pwp[e], q);
-            }
-            o[(size_t)e * N + x] = v0;
-            o[((size_t)ne + e) * N + x] = v1;
-        }
-        return;
-    }
-    const uint32_t sx = auto_src((uint32_t)x, k, logN);
-    const uint64_t* key = a.fkey[b];
-    const size_t nk = (size_t)(L + K);
-    const int T = (e1 - e0) * dn;   // (limb, digit) steps of this thread
-    const uint64_t pol = evict_first_policy();
-    const uint32_t s0 = (uint32_t)__cvta_generic_to_shared(&sbuf[0][0][tid]);
-    auto issue = [&](int t) {
-        const int e = e0 + t / dn, j = t - (t / dn) * dn;
-        const int m = e < nl ? e : L + (e - nl);
-        const uint32_t d = s0 + (uint32_t)((t % kBabyStages) * 3 * 256 * 8);
-        const uint64_t* kj = key + (size_t)j * 2 * nk * N;
-        cp_async8_hint(d, kj + (size_t)m * N + x, pol);
-        cp_async8_hint(d + 256 * 8, kj + (nk + m) * N + x, pol);
-        cp_async8(d + 2 * 256 * 8, ext + ((size_t)j * ne + e) * N + sx);
-    };
-#pragma unroll
-    for (int t = 0; t < kBabyStages - 1; t++) {
-        if (t < T) issue(t);
-        cp_async_commit();
-    }
-    u128acc a0{0, 0}, a1{0, 0};
-    int e = e0, j = 0;
-    for (int t = 0; t < T; t++) {
-        if (t + kBabyStages - 1 < T) issue(t + kBabyStages - 1);
-        cp_async_commit();
-        cp_async_wait<kBabyStages - 1>();   // this step's group has landed
-        const int sl = t % kBabyStages;
-        const uint64_t d = sbuf[sl][2][tid];
-        acc_mad(a0, d, sbuf[sl][0][tid]);
-        acc_mad(a1, d, sbuf[sl][1][tid]);
-        if (++j == dn) {
-            const int m = e < nl ? e : L + (e - nl);
-            const ModConst mc = c_mod[m];
-            uint64_t v0 = redc(a0.hi, a0.lo, mc);
-            const uint64_t v1 = redc(a1.hi, a1.lo, mc);
-            if (e < nl) v0 = mod_add(v0, mul_shoup(u0[(size_t)e * N + sx], a.pw[e], a.pwp[e], mc.q), mc.q);
-            o[(size_t)e * N + x] = v0;
-            o[((size_t)ne + e) * N + x] = v1;
-            a0 = u128acc{0, 0};
-            a1 = u128acc{0, 0};
-            j = 0;
-            e++;
-        }
-    }
-}
-
 // -------------------------------------------------------------------------- the plan ----
 struct MatvecPlan {
     int D = 0, b1 = 0, G = 0, nsets = 0, P = 0, rows = 0, cols = 0;
@@ -743,8 +653,7 @@ void matvec_babies(Context& cx, const Ciphertext& u, int D, int b1, BabySet& bs)
         }
         ProfScope ps(cx, "baby_pq", 8.0 * N * B * ((double)dn * ne * 2 + 2 * ne));
         const int per = std::max(1, cx.baby_limbs);
-        auto kern = cx.baby_async ? k_baby_pq_async : k_baby_pq;
-        kern<<<dim3(N / 256, (ne + per - 1) / per, B), 256, 0, st>>>(ext.p, u.c(0), u.c(1), ba,
+        k_baby_pq<<<dim3(N / 256, (ne + per - 1) / per, B), 256, 0, st>>>(ext.p, u.c(0), u.c(1), ba,
                                                                      bs.pq.p + (size_t)b0 * 2 * ne * N, nl, ne, dn, L,
                                                                      K, cx.logN, per);
         CUDA_CHECK(cudaGetLastError());
