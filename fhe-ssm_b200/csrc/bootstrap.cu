@@ -112,6 +112,7 @@ static Diags compose(const Diags& A, const Diags& B, int n) {
 struct BootLevel {
     int base = 1, b1 = kBootB1;
     bool pq = true;   // plaintexts over QP (double-hoisted evaluation)
+    int log_rep = 0;  // > 0: every plaintext is REP-compressed (its diagonals are slot-periodic)
     int nl_in = 0;
     double s_in = 0, s_out = 0;
     std::map<std::pair<int, int>, Plaintext> pts;   // (g, j) -> plaintext of rot(D_k, -g b1 base)
@@ -156,6 +157,19 @@ std::vector<int> boot_rotations(const Context& cx) {
     return r;
 }
 
+// the smallest power-of-two period of a slot vector (exact comparison: the entries of a
+// periodic diagonal are computed by the same operations in every period)
+static int slot_period(const cvec& d) {
+    const int n = (int)d.size();
+    int p = 1;
+    for (;; p <<= 1) {
+        if (p >= n) return n;
+        bool ok = true;
+        for (int i = p; i < n && ok; i++) ok = d[i] == d[i % p];
+        if (ok) return p;
+    }
+}
+
 // build one merged level (stages with lenh = 2^lo .. 2^hi-1) as BSGS plaintexts
 static BootLevel build_level(Context& cx, int lo, int hi, bool inverse, int nl_in, double s_in, double s_out,
                              std::complex<double> fold) {
@@ -183,6 +197,12 @@ static BootLevel build_level(Context& cx, int lo, int hi, bool inverse, int nl_i
     L.s_in = s_in;
     L.s_out = s_out;
     const double spt = s_out * (double)cx.mods[nl_in - 1] / s_in;
+    // The diagonals of stages with lenh < 2^hi repeat every 2^hi slots (a stage's entries depend
+    // on the slot's position in its block of 2 lenh).  Below the full slot count such a level's
+    // plaintexts are stored compressed: 2P words per limb for period P, read at x >> log_rep.
+    int period = 1;
+    for (auto& kv : D) period = std::max(period, slot_period(kv.second));
+    const bool comp = cx.boot_compress && period < n && period <= 4096 && period >= 8;
     std::set<int> gset;
     for (auto& kv : D) {
         const int o = kv.first;
@@ -191,12 +211,18 @@ static BootLevel build_level(Context& cx, int lo, int hi, bool inverse, int nl_i
         const int g = (int)std::floor((double)k / L.b1), j = k - g * L.b1;
         cvec d = rotv(kv.second, -g * L.b1 * L.base);
         for (auto& x : d) x *= fold;
-        Plaintext pt = L.pq ? encode_pq(cx, d.data(), n, nl_in, spt) : encode(cx, d.data(), n, nl_in, spt);
-        // Montgomery form: k_diag_mac accumulates 128-bit products and reduces once
-        LimbMap mm = cx.extmap(pt.buf.p, nl_in, 0);
-        if (!L.pq) { mm.nl = nl_in; mm.split = nl_in; }
-        k_mont_map<<<dim3(cx.N / 256, mm.nl), 256, 0, cx.stream>>>(pt.buf.p, mm, cx.logN);
-        CUDA_CHECK(cudaGetLastError());
+        Plaintext pt;
+        if (comp) {
+            // Montgomery form, over QP or Q (k_diag_mac accumulates 128-bit products, reduces once)
+            pt = encode_periodic_ext(cx, d.data(), period, nl_in, spt, L.pq, true);
+            L.log_rep = pt.log_rep;
+        } else {
+            pt = L.pq ? encode_pq(cx, d.data(), n, nl_in, spt) : encode(cx, d.data(), n, nl_in, spt);
+            LimbMap mm = cx.extmap(pt.buf.p, nl_in, 0);
+            if (!L.pq) { mm.nl = nl_in; mm.split = nl_in; }
+            k_mont_map<<<dim3(cx.N / 256, mm.nl), 256, 0, cx.stream>>>(pt.buf.p, mm, cx.logN);
+            CUDA_CHECK(cudaGetLastError());
+        }
         L.pts.emplace(std::make_pair(g, j), std::move(pt));
         gset.insert(g);
     }
@@ -213,10 +239,10 @@ static BootLevel build_level(Context& cx, int lo, int hi, bool inverse, int nl_i
 struct DiagArgs {
     const uint64_t* b0[kDiagMax];
     const uint64_t* b1[kDiagMax];
-    const uint64_t* pt[kDiagMax][kDiagMax];   // [g][j] or null
+    const uint64_t* pt[kDiagMax][kDiagMax];   // [g][j] or null; word x of limb i at [i][x >> lr]
     uint64_t* o0[kDiagMax];
     uint64_t* o1[kDiagMax];
-    int nb, ng;
+    int nb, ng, lr;
 };
 __global__ void __launch_bounds__(256, 4) k_diag_mac(const DiagArgs a, int logN, int nq, int L) {
     constexpr int H = kDiagMax / 2;
@@ -226,6 +252,7 @@ __global__ void __launch_bounds__(256, 4) k_diag_mac(const DiagArgs a, int logN,
     const int i = blockIdx.y;   // limb: Q limbs below nq, then the special limbs
     const ModConst mc = c_mod[i < nq ? i : L + (i - nq)];
     const size_t w = (size_t)i * N + x;
+    const size_t wp = ((size_t)i << (logN - a.lr)) + (x >> a.lr);   // the plaintext word of slot x
     const int j0 = half * H;
     uint64_t v0[H], v1[H];
 #pragma unroll
@@ -236,7 +263,7 @@ __global__ void __launch_bounds__(256, 4) k_diag_mac(const DiagArgs a, int logN,
 #pragma unroll
         for (int j = 0; j < H; j++) {
             if (j0 + j >= a.nb || !a.pt[g][j0 + j]) continue;
-            const uint64_t p = a.pt[g][j0 + j][w];
+            const uint64_t p = a.pt[g][j0 + j][wp];
             acc_mad32(s0, p, v0[j]);
             acc_mad32(s1, p, v1[j]);
         }
@@ -302,6 +329,7 @@ static void eval_level(Context& cx, const BootLevel& L, const Ciphertext& v, Cip
     // giant g: inner_g = sum_j pt_gj . baby_j (one k_diag_mac for all g)
     DiagArgs da{};
     da.nb = nb;
+    da.lr = L.log_rep;
     for (int j = 0; j < nb; j++) { da.b0[j] = b0[j]; da.b1[j] = b1v[j]; }
     std::vector<int> gl;   // giants in use, in output order
     double spt = 0;
@@ -325,7 +353,7 @@ static void eval_level(Context& cx, const BootLevel& L, const Ciphertext& v, Cip
     }
     da.ng = G;
     {
-        ProfScope ps(cx, "diag_mac", 8.0 * N * nw * (2.0 * nb + 2.0 * G + (double)L.pts.size()));
+        ProfScope ps(cx, "diag_mac", 8.0 * N * nw * (2.0 * nb + 2.0 * G + (double)L.pts.size() / (1 << L.log_rep)));
         k_diag_mac<<<dim3(N / 128, nw), 256, 0, st>>>(da, cx.logN, nl, cx.L);
         CUDA_CHECK(cudaGetLastError());
         cx.launches++;

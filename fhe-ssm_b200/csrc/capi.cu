@@ -103,6 +103,7 @@ int fhe_ctx_set_option(fhe_ctx* cx, const char* name, int value) {
         else if (std::strcmp(name, "ntt_cluster") == 0) cx->cx.ntt_cluster = value != 0;
         else if (std::strcmp(name, "ntt_arith") == 0) cx->cx.ntt_arith = value == 1 ? 1 : 0;
         else if (std::strcmp(name, "baby_limbs") == 0) cx->cx.baby_limbs = value < 1 ? 1 : value > 64 ? 64 : value;
+        else if (std::strcmp(name, "boot_compress") == 0) cx->cx.boot_compress = value != 0;
         else if (std::strcmp(name, "boot_delta_log2") == 0) {
             if (value != 0 && value != -1 && (value < 30 || value > 56))
                 throw fhe::Error("boot_delta_log2: 0 (auto), -1 (canonical) or 30..56", -1);

@@ -131,6 +131,7 @@ struct Context {
     int use_pdl = 1;                 // programmatic dependent launch for the hot kernels (launch_pdl)
     int ntt_cluster = 0;             // N = 2^16: one cluster launch per transform (ntt.cu, k_ntt_cluster)
     int baby_limbs = 8;              // k_baby_pq: limbs walked by one thread
+    int boot_compress = 1;           // bootstrap_setup: slot-periodic level plaintexts stored compressed
     int ntt_arith = 1;               // NTT butterflies: 1 cheaper Shoup quotient in 32-bit steps (ntt.cu, mul_shoup_q4), 0 exact
     int merged_rescale = 1;          // circuit products: ModDown and rescale in one division by P q_l
     // bootstrap input scale: the message is brought to one limb (q0) at scale 2^boot_delta_log2.

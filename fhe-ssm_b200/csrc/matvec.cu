@@ -208,7 +208,11 @@ __global__ void __launch_bounds__(256) k_ptgen2048(const double* __restrict__ co
 // N/2n (the identity of hpc_gpu_port/periodic_encode.hpp): a 2n-word compressed plaintext per
 // limb, read by the element-wise kernels at word x >> log2(N/2n).  Plaintexts of the model's
 // fixed vectors are cached by (content, level, scale), so a step re-encodes nothing.
-static Plaintext encode_periodic(Context& cx, const std::complex<double>* z, int n, int nl, double scale) {
+// A slot vector of period n (n | N/2, n <= 4096) as a REP-compressed plaintext (word x of a
+// limb = comp[x >> log_rep], 2n words per limb): nl Q limbs, then (pq) the K special limbs, in
+// Montgomery form when `mont` is set.
+Plaintext encode_periodic_ext(Context& cx, const std::complex<double>* z, int n, int nl, double scale, bool pq,
+                              bool mont) {
     std::vector<std::complex<double>> v(z, z + n);
     fft_special_inv(v.data(), n, 4 * n);
     std::vector<double> co(2 * n);
@@ -223,18 +227,24 @@ static Plaintext encode_periodic(Context& cx, const std::complex<double>* z, int
     CUDA_CHECK(cudaMemcpyAsync(dc.p, co.data(), co.size() * 8, cudaMemcpyHostToDevice, cx.stream));
     int log2n = 0;
     while ((1 << log2n) < 2 * n) log2n++;
+    const int nlimb = nl + (pq ? cx.K : 0);
     Plaintext pt;
-    pt.buf = DevBuf((size_t)nl * 2 * n, cx.stream);
-    pt.nl = nl;
+    pt.buf = DevBuf((size_t)nlimb * 2 * n, cx.stream);
+    pt.nl = nlimb;
     pt.scale = scale;
     int lr = 0;
     while ((cx.N >> lr) > 2 * n) lr++;
     pt.log_rep = lr;
-    k_ptgen<1><<<dim3(1, nl), 256, 2 * n * 8, cx.stream>>>((const double*)dc.p, scale, pt.buf.p, 1, nl, cx.L,
-                                                          log2n, cx.d_tw, cx.d_twp, cx.N, 0);
+    if (2 * n * 8 > 48 * 1024)
+        CUDA_CHECK(cudaFuncSetAttribute(k_ptgen<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * n * 8));
+    k_ptgen<1><<<dim3(1, nlimb), 256, 2 * n * 8, cx.stream>>>((const double*)dc.p, scale, pt.buf.p, 1, nl, cx.L,
+                                                             log2n, cx.d_tw, cx.d_twp, cx.N, mont ? 1 : 0);
     CUDA_CHECK(cudaGetLastError());
     cx.launches++;
     return pt;
+}
+static Plaintext encode_periodic(Context& cx, const std::complex<double>* z, int n, int nl, double scale) {
+    return encode_periodic_ext(cx, z, n, nl, scale, false, false);
 }
 
 const Plaintext& encode_cached(Context& cx, const std::complex<double>* z, int n, int nl, double scale) {
