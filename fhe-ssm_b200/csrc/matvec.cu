@@ -99,11 +99,12 @@ __global__ void __launch_bounds__(256) k_ptgen(const double* __restrict__ coef, 
 // in registers, 8 words per thread, 11 butterfly stages in 4 passes (3 + 3 + 3 + 2) with three
 // exchanges through shared memory; the limb's twiddles are staged in shared memory once per CTA,
 // and 4 plaintexts are written together (32-byte runs of the transposed layout).  The
-// butterflies are the lazy ones of the ring NTT (values in [0, 4q + 2^32), twiddle and Shoup
-// companion read as one 16-byte pair); the output is made canonical, or taken to Montgomery
-// form by a Shoup product with 2^64 mod q: the same words as k_ptgen.
+// butterflies are the lazy ones of the ring NTT with the cheaper quotient (values in
+// [0, 8q + 2^32), twiddle and Shoup companion read as one 16-byte pair); the output is made
+// canonical, or taken to Montgomery form by a Shoup product with 2^64 mod q: the same words as
+// k_ptgen.
 __device__ __forceinline__ void pgl(uint64_t& a, uint64_t& b, const ulonglong2 t, uint64_t q) {
-    bfly<false>(a, b, t.x, t.y, q);
+    bfly<false, 1>(a, b, t.x, t.y, q);
 }
 __global__ void __launch_bounds__(256) k_ptgen2048(const double* __restrict__ coef, double scale,
                                                    uint64_t* __restrict__ out, int P, int nq, int L,
@@ -191,7 +192,7 @@ __global__ void __launch_bounds__(256) k_ptgen2048(const double* __restrict__ co
 #pragma unroll
             for (int k = 0; k < 8; k++) {
                 const uint64_t v = x[k];
-                Sb[8 * tid + k] = mont ? mul_shoup(v, rq, rqp, q) : canon4(v, q);
+                Sb[8 * tid + k] = mont ? mul_shoup(v, rq, rqp, q) : canon_out<1>(v, q);
             }
         }
         __syncthreads();
