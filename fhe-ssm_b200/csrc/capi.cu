@@ -142,6 +142,19 @@ int fhe_ctx_counters(const fhe_ctx* cx, long long* keyswitches, long long* ks_li
         if (ks_limbs) *ks_limbs = cx->cx.ks_limbs;
     });
 }
+int fhe_ctx_stat(const fhe_ctx* cx, const char* name, long long* value) {
+    return guard([&] {
+        REQUIRE(cx && name && value, "null argument");
+        const fhe::Context& c = cx->cx;
+        if (std::strcmp(name, "launches") == 0) *value = c.launches;
+        else if (std::strcmp(name, "keyswitches") == 0) *value = c.ks_count;
+        else if (std::strcmp(name, "ks_limbs") == 0) *value = c.ks_limbs;
+        else if (std::strcmp(name, "pt_encodes") == 0) *value = c.pt_encodes;
+        else if (std::strcmp(name, "pt_cached") == 0) *value = (long long)c.ptcache.size();
+        else if (std::strcmp(name, "host_waits") == 0) *value = c.host_waits;
+        else throw fhe::Error(std::string("unknown statistic: ") + name, -1);
+    });
+}
 int fhe_prof_enable(fhe_ctx* cx, int on) {
     return guard([&] {
         REQUIRE(cx, "null argument");

@@ -312,6 +312,9 @@ Context::~Context() {
     for (auto* p : {d_tw, d_twp, d_itw, d_itwp, d_ninv, d_md, d_rs, d_tw2, d_itw2, d_twrow, d_itwrow, d_rmont})
         if (p) cudaFree(p);
     if (d_err) cudaFree(d_err);
+    for (auto& e : stage_ev)
+        if (e) cudaEventDestroy(e);
+    if (stage) cudaFreeHost(stage);
     for (auto& kv : modup_tab) cudaFree(kv.second);
     for (auto& kv : mdr_tab) cudaFree(kv.second);
     if (stream) cudaStreamDestroy(stream);
@@ -912,13 +915,36 @@ static void encode_coeffs(Context& cx, const std::complex<double>* z, int nslots
     }
 }
 
+void upload_async(Context& cx, void* dev, const void* host, size_t bytes) {
+    if (bytes > Context::kStageBytes) {   // larger than a slot: a plain copy, then wait for it
+        CUDA_CHECK(cudaMemcpyAsync(dev, host, bytes, cudaMemcpyHostToDevice, cx.stream));
+        CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+        return;
+    }
+    if (!cx.stage) {
+        CUDA_CHECK(cudaHostAlloc((void**)&cx.stage, Context::kStageSlots * Context::kStageBytes,
+                                 cudaHostAllocDefault));
+        for (auto& e : cx.stage_ev) CUDA_CHECK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    }
+    const int i = cx.stage_next;
+    cx.stage_next = (i + 1) % Context::kStageSlots;
+    if (cudaEventQuery(cx.stage_ev[i]) == cudaErrorNotReady) {   // the slot's last copy is still queued
+        cx.host_waits++;
+        CUDA_CHECK(cudaEventSynchronize(cx.stage_ev[i]));
+    }
+    uint8_t* slot = cx.stage + (size_t)i * Context::kStageBytes;
+    std::memcpy(slot, host, bytes);
+    CUDA_CHECK(cudaMemcpyAsync(dev, slot, bytes, cudaMemcpyHostToDevice, cx.stream));
+    CUDA_CHECK(cudaEventRecord(cx.stage_ev[i], cx.stream));
+}
+
 Plaintext encode(Context& cx, const std::complex<double>* z, int nslots, int nl, double scale) {
     if (nl < 1 || nl > cx.L) throw Error("encode: bad level", -4);
     const int N = cx.N;
     std::vector<int64_t> coef(N);
     encode_coeffs(cx, z, nslots, scale, coef.data());
     DevBuf dc((size_t)N, cx.stream);
-    CUDA_CHECK(cudaMemcpyAsync(dc.p, coef.data(), N * 8, cudaMemcpyHostToDevice, cx.stream));
+    upload_async(cx, dc.p, coef.data(), (size_t)N * 8);
     Plaintext pt;
     pt.buf = DevBuf((size_t)nl * N, cx.stream);
     pt.nl = nl;
@@ -927,8 +953,8 @@ Plaintext encode(Context& cx, const std::complex<double>* z, int nslots, int nl,
     k_signed_to_limbs<<<g2(cx, nl), 256, 0, cx.stream>>>((const int64_t*)dc.p, pt.buf.p, mp, cx.logN);
     CUDA_CHECK(cudaGetLastError());
     ntt(cx, mp, 1, false, cx.stream);
-    CUDA_CHECK(cudaStreamSynchronize(cx.stream));   // coef is a host temporary
     cx.launches += 1;
+    cx.pt_encodes++;
     return pt;
 }
 
@@ -939,7 +965,7 @@ Plaintext encode_pq(Context& cx, const std::complex<double>* z, int nslots, int 
     std::vector<int64_t> coef(N);
     encode_coeffs(cx, z, nslots, scale, coef.data());
     DevBuf dc((size_t)N, cx.stream);
-    CUDA_CHECK(cudaMemcpyAsync(dc.p, coef.data(), N * 8, cudaMemcpyHostToDevice, cx.stream));
+    upload_async(cx, dc.p, coef.data(), (size_t)N * 8);
     Plaintext pt;
     pt.buf = DevBuf((size_t)ne * N, cx.stream);
     pt.nl = ne;
@@ -948,8 +974,8 @@ Plaintext encode_pq(Context& cx, const std::complex<double>* z, int nslots, int 
     k_signed_to_limbs<<<g2(cx, ne), 256, 0, cx.stream>>>((const int64_t*)dc.p, pt.buf.p, mp, cx.logN);
     CUDA_CHECK(cudaGetLastError());
     ntt(cx, mp, 1, false, cx.stream);
-    CUDA_CHECK(cudaStreamSynchronize(cx.stream));   // coef is a host temporary
     cx.launches += 1;
+    cx.pt_encodes++;
     return pt;
 }
 

@@ -160,6 +160,16 @@ struct Context {
     uint32_t enc_counter = 0;
     mutable long long launches = 0;  // kernel launches issued (for the launch count claim)
     long long ks_count = 0, ks_limbs = 0;   // key switches issued and the sum of their limb counts
+    long long pt_encodes = 0;        // plaintexts encoded on an encode-cache miss
+    long long host_waits = 0;        // uploads that waited for a staging slot still in flight
+    // Pinned host staging for uploads on the hot path (upload_async): kStageSlots slots of
+    // kStageBytes, used round robin; slot i is reused once the event recorded after its copy
+    // has completed, so an upload never waits for the stream's other work.
+    static constexpr int kStageSlots = 8;
+    static constexpr size_t kStageBytes = (size_t)1 << 20;
+    uint8_t* stage = nullptr;
+    cudaEvent_t stage_ev[kStageSlots] = {};
+    int stage_next = 0;
     // optional per-kernel CUDA-event timing (bench roofline): name -> pending event pairs
     // Sampled: one scope in prof_every of each name is timed; the totals are scaled by
     // seen / sampled (the average duration of a timed scope is exact for what was timed).
@@ -206,6 +216,10 @@ void apply_limb_const(Context& cx, const Ciphertext& a, const LimbConst& k, Ciph
 // round(v) mod q_i for each limb (|v| < 2^126)
 void limb_residues(const Context& cx, long double v, int nl, uint64_t* out);
 Plaintext encode_pq(Context& cx, const std::complex<double>* z, int nslots, int nl, double scale);
+// host -> device copy of `bytes` (<= Context::kStageBytes) through a pinned staging slot, ordered
+// on the context's stream: the host buffer may be reused as soon as the call returns, and the
+// stream is not drained (a pageable-memory copy would wait for all earlier work first)
+void upload_async(Context& cx, void* dev, const void* host, size_t bytes);
 
 // Brackets the launches of one kernel (or kernel pair) with CUDA events on the context's
 // stream when profiling is on; `bytes` is the algorithmic DRAM traffic of the bracket.

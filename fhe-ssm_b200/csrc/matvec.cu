@@ -225,7 +225,8 @@ Plaintext encode_periodic_ext(Context& cx, const std::complex<double>* z, int n,
             throw Error("encode: value * scale exceeds 61 bits (refused)", -6);
     }
     DevBuf dc(co.size(), cx.stream);
-    CUDA_CHECK(cudaMemcpyAsync(dc.p, co.data(), co.size() * 8, cudaMemcpyHostToDevice, cx.stream));
+    upload_async(cx, dc.p, co.data(), co.size() * 8);
+    cx.pt_encodes++;
     int log2n = 0;
     while ((1 << log2n) < 2 * n) log2n++;
     const int nlimb = nl + (pq ? cx.K : 0);

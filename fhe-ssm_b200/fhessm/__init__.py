@@ -274,6 +274,16 @@ class CryptoContext:
     def rot_index(self, k):
         return lib().fhe_rot_index(self.h, k)
 
+    def stat(self, name):
+        """A named engine statistic (fhe_ctx_stat): "launches", "keyswitches", "ks_limbs",
+        "pt_encodes", "pt_cached", "host_waits"."""
+        h = lib()
+        h.fhe_ctx_stat.restype = C.c_int
+        h.fhe_ctx_stat.argtypes = [_VP, C.c_char_p, C.POINTER(C.c_longlong)]
+        v = C.c_longlong()
+        _check(h.fhe_ctx_stat(self.h, name.encode(), C.byref(v)))
+        return v.value
+
     def counters(self):
         """(key switches issued, sum of their limb counts) since the context was created."""
         h = lib()

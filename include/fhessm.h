@@ -74,6 +74,10 @@ int fhe_ctx_memory(fhe_ctx* cx, long long* out);
 long long fhe_ctx_launches(const fhe_ctx* cx);
 /* key switches issued so far and the sum of their limb counts (operation census) */
 int fhe_ctx_counters(const fhe_ctx* cx, long long* keyswitches, long long* ks_limbs);
+/* a named statistic of the context: "launches", "keyswitches", "ks_limbs", "pt_encodes" (plaintexts
+ * encoded on a cache miss), "pt_cached" (plaintexts held by the encode cache), "host_waits" (times a
+ * host-to-device upload had to wait for an earlier one's staging buffer).  Unknown name: error. */
+int fhe_ctx_stat(const fhe_ctx* cx, const char* name, long long* value);
 /* the context's CUDA stream (cudaStream_t), for callers that time it with CUDA events */
 void* fhe_ctx_stream(const fhe_ctx* cx);
 /* engine options: "matvec_tensor_cores" (default 1): BSGS products on the tcgen05 tensor cores
