@@ -90,7 +90,16 @@ void* fhe_ctx_stream(const fhe_ctx* cx);
  * (level and scale) resident and reuses them when the next call has the same level and scale,
  * the reference's --cache-diags (gpu_real_model.cu:1647-1652, also off by default there).
  * "plaintext_cache_reserve_mib" (default 24576): a plan caches only while this much device
- * memory would stay free. */
+ * memory would stay free.
+ * "pdl" (default 1): programmatic dependent launch of the hot kernels.
+ * "ntt_cluster" (default 0): N = 2^16 transforms as one 8-CTA cluster launch per limb.
+ * "ntt_arith" (default 1): NTT butterflies with the cheaper Shoup quotient; 0: exact quotient
+ * (the same words either way).
+ * "baby_limbs" (default 8): limbs walked by one thread of the baby key inner products.
+ * "boot_compress" (default 1): bootstrap levels with slot-periodic diagonals keep their
+ * plaintexts compressed (read by the next fhe_bootstrap_setup; the same words).
+ * "boot_delta_log2" (default 0 = 2^(bits(q0) - 11)): the bootstrap input scale, read by the
+ * next fhe_bootstrap_setup; -1 = the chain's canonical level-1 scale, 30..56 = 2^value. */
 int fhe_ctx_set_option(fhe_ctx* cx, const char* name, int value);
 /* per-kernel CUDA-event timing on the context's stream (off by default).  collect
  * synchronises, writes {"kernel": [launches, total_ms, algorithmic_bytes], ...} as JSON
