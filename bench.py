@@ -138,6 +138,16 @@ def barrier(ws):
         dist.barrier()
 
 
+def broadcast_object(obj, ws):
+    """rank 0's obj on every rank"""
+    if ws == 1:
+        return obj
+    import torch.distributed as dist
+    box = [obj]
+    dist.broadcast_object_list(box, src=0)
+    return box[0]
+
+
 def max_over_ranks(v, ws):
     """The slowest rank's time: the whole job's step time for `value`."""
     if ws == 1:
@@ -302,7 +312,11 @@ def run_model(args, ws, rank, local):
     # below the smallest, at a tolerance of 3e-4: over 32 held-out packs of 64 conversations
     # (12 steps each) the worst Newton error is 9e-5, at two more iterations per pass than a
     # 64-conversation calibration whose window misses some of them
-    seeds = calibrate_seeds(cfg, w, steps=6, lanes=CAL_LANES, tol=3e-4, ms_margin=(1.25, 3.0))
+    # (rank 0 calibrates and sends the result: one host's cores are shared by all ranks)
+    seeds = None
+    if rank == 0:
+        seeds = calibrate_seeds(cfg, w, steps=6, lanes=CAL_LANES, tol=3e-4, ms_margin=(1.25, 3.0))
+    seeds = broadcast_object(seeds, ws)
     cx = fhessm.CryptoContext(device=local, **MODEL_CTX)
     key_seed, tok_seed = pack_seeds(rank)
     cx.KeyGen(seed=key_seed)

@@ -1,6 +1,7 @@
 """The N > 1 path of bench.py on CPU: world_size-2 gloo ranks (no GPU).  Each rank owns an
-independent pack (its own keys and tokens); the only collectives are the barrier and the
-max-over-ranks reduction of the timed region, and rank 0 reports the aggregate."""
+independent pack (its own keys and tokens); the only collectives are the set-up broadcast of
+rank 0's calibration, the barrier and the max-over-ranks reduction of the timed region, and
+rank 0 reports the aggregate."""
 import os
 import socket
 import sys
@@ -28,7 +29,9 @@ def _rank(rank, ws, port, q):
         bench.barrier(ws)
         ms = 1000.0 + 250.0 * rank            # rank 1 is the slow one
         ms_max = bench.max_over_ranks(ms, ws)
-        q.put((rank, ms_max, bench.pack_seeds(rank), bench.aggregate_tokens_per_s(64, ws, 2, ms_max)))
+        # calibration results travel from rank 0 (the other ranks pass None)
+        seeds = bench.broadcast_object({"L0.tm": (1.5, -0.25, 3), "gain:L0.u": 0.5} if rank == 0 else None, ws)
+        q.put((rank, ms_max, bench.pack_seeds(rank), bench.aggregate_tokens_per_s(64, ws, 2, ms_max), seeds))
         bench.barrier(ws)
     finally:
         dist.destroy_process_group()
@@ -48,3 +51,4 @@ def test_two_rank_gloo_reduction_and_packs():
     assert [g[1] for g in got] == [1250.0, 1250.0]          # every rank sees the slowest time
     assert got[0][2] != got[1][2]                            # distinct packs
     assert abs(got[0][3] - 64 * 2 * 2 / 1.25) < 1e-9         # 64 conversations x 2 ranks x 2 steps / 1.25 s
+    assert got[0][4] == got[1][4] == {"L0.tm": (1.5, -0.25, 3), "gain:L0.u": 0.5}   # rank 0's seeds everywhere
