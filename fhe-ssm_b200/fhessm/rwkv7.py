@@ -1,0 +1,362 @@
+"""fhessm.rwkv7 -- the RWKV-7 (x070) polynomial model of config 5, in recurrent form.
+
+The reference holds this model only as a plaintext PyTorch harness
+(results/vector-d-20261104/harness/rwkv7_model.py, the x070 forward with every non-polynomial
+operation routed through one site hook); its encrypted port is not in the reference tree.  This
+module restates that forward one token at a time for a batch of conversations, in float64:
+
+  * ``RWKV7Shape`` and ``synthetic_weights``: the parameter set under the reference's
+    state-dict names (rwkv7_model.py:234-306), seeded;
+  * ``step``: one token through every block and the output norm, with the sites evaluated
+    exactly or as the circuit evaluates them (``Sites``: Chebyshev polynomials on fitted
+    intervals, Newton inverse square roots from a linear seed), carrying the per-layer state
+    (the two time-shift inputs and the per-head wkv matrix);
+  * ``fit_sites``: the polynomial of every site from a calibration run.
+
+Per layer (rwkv7_model.py:329-392): x0 = ln1(x); time shift xx = prev - x0; six mixes
+x_* = x0 + xx m_*; r, k, v linear; decay w = exp(-e^{-1/2} sigmoid(w0 + tanh(x_w W1) W2));
+value residual v += (v_first - v) sigmoid(v0 + (x_v V1) V2) from layer 1 on; in-context rate
+a = sigmoid(a0 + (x_a A1) A2); gate g = sigmoid(x_g G1) G2; kk = normalize(k k_k) per head;
+k <- k (1 + (a - 1) k_a); the state S <- S diag(w) + (S (-kk)) (kk a)^T + v k^T, y = S r
+(wkv7_recurrence, :277-298); GroupNorm per head, the bonus ((r k r_k) summed per head) v, the
+output projection of y g; then the channel mix relu(x_k Wk)^2 Wv on ln2 with its own time shift.
+"""
+from dataclasses import dataclass
+
+import numpy as np
+
+EXP_M05 = float(np.exp(-0.5))
+
+
+@dataclass
+class RWKV7Shape:
+    n_layer: int = 24
+    n_embd: int = 1024
+    head_size: int = 64
+    d_decay: int = 64
+    d_aaa: int = 64
+    d_mv: int = 32
+    d_gate: int = 128
+    dim_ffn: int = 4096
+    vocab_size: int = 65536
+
+    @property
+    def n_head(self):
+        return self.n_embd // self.head_size
+
+
+RWKV7_04B = RWKV7Shape()   # config 5: 24 layers, d = 1024, head size 64, V = 65,536
+
+
+def synthetic_weights(sh: RWKV7Shape, seed: int = 7):
+    """Seeded parameters under the reference's state-dict names: norm gains near 1, mixes in
+    [0, 1), matrices N(0, 1/fan_in), decay bias around -1 (rwkv7_model.py:234-306)."""
+    rng = np.random.default_rng(seed)
+    C, H, N, F = sh.n_embd, sh.n_head, sh.head_size, sh.dim_ffn
+    mat = lambda o, i: rng.normal(0.0, 1.0 / np.sqrt(i), (o, i))      # a Linear's (out, in) weight
+    lora = lambda i, o, s=1.0: rng.normal(0.0, s / np.sqrt(i), (i, o))   # x @ W with W (in, out)
+    w = {"emb.weight": rng.normal(0.0, 0.5, (sh.vocab_size, C)),
+         "ln_out.weight": 1.0 + 0.1 * rng.normal(size=C), "ln_out.bias": 0.1 * rng.normal(size=C),
+         "head.weight": mat(sh.vocab_size, C)}
+    for i in range(sh.n_layer):
+        p = f"blocks.{i}."
+        if i == 0:
+            w[p + "ln0.weight"] = 1.0 + 0.1 * rng.normal(size=C)
+            w[p + "ln0.bias"] = 0.1 * rng.normal(size=C)
+        for ln in ("ln1", "ln2"):
+            w[p + ln + ".weight"] = 1.0 + 0.1 * rng.normal(size=C)
+            w[p + ln + ".bias"] = 0.1 * rng.normal(size=C)
+        a = p + "att."
+        for m in ("x_r", "x_w", "x_k", "x_v", "x_a", "x_g"):
+            w[a + m] = rng.uniform(0.0, 1.0, C)
+        w[a + "w0"] = -1.0 + 0.5 * rng.normal(size=C)
+        w[a + "w1"], w[a + "w2"] = lora(C, sh.d_decay), lora(sh.d_decay, C, 0.5)
+        w[a + "a0"] = 0.5 * rng.normal(size=C)
+        w[a + "a1"], w[a + "a2"] = lora(C, sh.d_aaa), lora(sh.d_aaa, C, 0.5)
+        if i > 0:
+            w[a + "v0"] = 0.5 * rng.normal(size=C)
+            w[a + "v1"], w[a + "v2"] = lora(C, sh.d_mv), lora(sh.d_mv, C, 0.5)
+        w[a + "g1"], w[a + "g2"] = lora(C, sh.d_gate), lora(sh.d_gate, C, 0.5)
+        w[a + "k_k"] = 0.8 + 0.2 * rng.uniform(size=C)
+        w[a + "k_a"] = rng.uniform(size=C)
+        w[a + "r_k"] = 0.5 * rng.normal(size=(H, N))
+        for lin in ("receptance", "key", "value", "output"):
+            w[a + lin + ".weight"] = mat(C, C)
+        w[a + "ln_x.weight"] = 1.0 + 0.1 * rng.normal(size=C)
+        w[a + "ln_x.bias"] = 0.1 * rng.normal(size=C)
+        f = p + "ffn."
+        w[f + "x_k"] = rng.uniform(0.0, 1.0, C)
+        w[f + "key.weight"] = mat(F, C)
+        w[f + "value.weight"] = mat(C, F) * 0.5
+    return w
+
+
+# -------------------------------------------------------------------------------- sites ----
+SITE_FUNCS = {   # rwkv7_model.py:46-56
+    "w_tanh": np.tanh,
+    "decay": lambda x: np.exp(-EXP_M05 / (1.0 + np.exp(-x))),
+    "v_sigmoid": lambda x: 1.0 / (1.0 + np.exp(-x)),
+    "a_sigmoid": lambda x: 1.0 / (1.0 + np.exp(-x)),
+    "g_sigmoid": lambda x: 1.0 / (1.0 + np.exp(-x)),
+    "relu2": lambda x: np.maximum(x, 0.0) ** 2,
+}
+RSQRT_EPS = {"ln": 1e-5, "gn": 64e-5, "kk": 0.0}
+
+
+def cheb_fit(f, lo, hi, degree):
+    """Chebyshev interpolant of f on [lo, hi] (Chebyshev nodes of the first kind), coefficients
+    in the variable t = (2x - lo - hi) / (hi - lo) (rwkv7_model.py:113-127 evaluates the same
+    series by Clenshaw)."""
+    n = degree + 1
+    t = np.cos(np.pi * (np.arange(n) + 0.5) / n)
+    fx = f(0.5 * (hi - lo) * t + 0.5 * (hi + lo))
+    c = np.array([2.0 / n * np.sum(fx * np.cos(np.pi * j * (np.arange(n) + 0.5) / n)) for j in range(n)])
+    c[0] /= 2.0
+    return c
+
+
+def cheb_val(x, c, lo, hi):
+    t = (2.0 * x - (lo + hi)) / (hi - lo)
+    return np.polynomial.chebyshev.chebval(t, c)
+
+
+class Sites:
+    """Exact site functions (fits None), or the circuit's: a Chebyshev series per site kind and
+    block on its interval, and Newton 1/sqrt from a linear seed per norm site.  record=True keeps
+    the input range of every site (calibration)."""
+
+    def __init__(self, fits=None, record=False):
+        self.fits = fits
+        self.record = record
+        self.ranges = {}
+
+    def _rec(self, name, x):
+        if self.record:
+            lo, hi = self.ranges.get(name, (np.inf, -np.inf))
+            self.ranges[name] = (min(lo, float(np.min(x))), max(hi, float(np.max(x))))
+
+    def poly(self, name, kind, x):
+        self._rec(name, x)
+        if self.fits is None or name not in self.fits:
+            return SITE_FUNCS[kind](x)
+        lo, hi, c = self.fits[name]
+        return cheb_val(x, c, lo, hi)
+
+    def rsqrt(self, name, kind, x):
+        """1/sqrt(x + eps) (kk: 1/max(sqrt(x), 1e-12))"""
+        v = x + RSQRT_EPS[kind]
+        self._rec(name, v)
+        if self.fits is None or name not in self.fits:
+            return 1.0 / np.maximum(np.sqrt(np.maximum(v, 0.0)), 1e-12) if kind == "kk" else 1.0 / np.sqrt(v)
+        a, b, iters = self.fits[name]
+        y = a + b * v
+        for _ in range(int(iters)):
+            y = 1.5 * y - 0.5 * v * y ** 3
+        return y
+
+
+def _ln(sites, name, x, wgt, bias):
+    mu = x.mean(-1, keepdims=True)
+    xc = x - mu
+    var = (xc * xc).mean(-1, keepdims=True)
+    return xc * sites.rsqrt(name, "ln", var) * wgt + bias
+
+
+def new_state(sh: RWKV7Shape, lanes: int):
+    C, H, N = sh.n_embd, sh.n_head, sh.head_size
+    return [{"att": np.zeros((lanes, C)), "ffn": np.zeros((lanes, C)), "S": np.zeros((lanes, H, N, N))}
+            for _ in range(sh.n_layer)]
+
+
+def block_step(sh: RWKV7Shape, w, i, x, st, v_first, sites):
+    """One block for one token: x (lanes, C) -> (x', v_first); st (the block's state) is updated."""
+    B, C = x.shape
+    H, N = sh.n_head, sh.head_size
+    p = f"blocks.{i}."
+    a_ = p + "att."
+    if i == 0:
+        x = _ln(sites, p + "ln0", x, w[p + "ln0.weight"], w[p + "ln0.bias"])
+    x0 = _ln(sites, p + "ln1", x, w[p + "ln1.weight"], w[p + "ln1.bias"])
+    xx = st["att"] - x0
+    st["att"] = x0
+    xr, xw, xk, xv, xa, xg = (x0 + xx * w[a_ + m] for m in ("x_r", "x_w", "x_k", "x_v", "x_a", "x_g"))
+    r = xr @ w[a_ + "receptance.weight"].T
+    z = w[a_ + "w0"] + sites.poly(a_ + "w_tanh", "w_tanh", xw @ w[a_ + "w1"]) @ w[a_ + "w2"]
+    dec = sites.poly(a_ + "decay", "decay", z)
+    k = xk @ w[a_ + "key.weight"].T
+    v = xv @ w[a_ + "value.weight"].T
+    if i == 0:
+        v_first = v
+    else:
+        v = v + (v_first - v) * sites.poly(a_ + "v_sigmoid", "v_sigmoid", w[a_ + "v0"] + (xv @ w[a_ + "v1"]) @ w[a_ + "v2"])
+    a = sites.poly(a_ + "a_sigmoid", "a_sigmoid", w[a_ + "a0"] + (xa @ w[a_ + "a1"]) @ w[a_ + "a2"])
+    g = sites.poly(a_ + "g_sigmoid", "g_sigmoid", xg @ w[a_ + "g1"]) @ w[a_ + "g2"]
+    kk = (k * w[a_ + "k_k"]).reshape(B, H, N)
+    kk = (kk * sites.rsqrt(a_ + "kk_rsqrt", "kk", (kk * kk).sum(-1, keepdims=True))).reshape(B, C)
+    k = k * (1.0 + (a - 1.0) * w[a_ + "k_a"])
+    # wkv7 state update, one step (rwkv7_model.py:290-296): S <- S diag(w) + (S (-kk)) (kk a)^T + v k^T
+    S = st["S"]
+    dh, kh, vh, rh = (t.reshape(B, H, N) for t in (dec, k, v, r))
+    ah, bh = -kk.reshape(B, H, N), (kk * a).reshape(B, H, N)
+    Sa = np.einsum("bhij,bhj->bhi", S, ah)
+    S = S * dh[:, :, None, :] + Sa[..., :, None] * bh[:, :, None, :] + vh[..., :, None] * kh[:, :, None, :]
+    st["S"] = S
+    y = np.einsum("bhij,bhj->bhi", S, rh)
+    yc = y - y.mean(-1, keepdims=True)
+    var = (yc * yc).mean(-1, keepdims=True)
+    y = (yc * sites.rsqrt(a_ + "gn_rsqrt", "gn", var)).reshape(B, C) * w[a_ + "ln_x.weight"] + w[a_ + "ln_x.bias"]
+    y = y + ((rh * kh * w[a_ + "r_k"]).sum(-1, keepdims=True) * vh).reshape(B, C)
+    x = x + (y * g) @ w[a_ + "output.weight"].T
+    f = p + "ffn."
+    xf = _ln(sites, p + "ln2", x, w[p + "ln2.weight"], w[p + "ln2.bias"])
+    xx = st["ffn"] - xf
+    st["ffn"] = xf
+    kf = (xf + xx * w[f + "x_k"]) @ w[f + "key.weight"].T
+    x = x + sites.poly(f + "relu2", "relu2", kf) @ w[f + "value.weight"].T
+    return x, v_first
+
+
+def step(sh: RWKV7Shape, w, tokens, state, sites=None, hidden=None):
+    """One token per conversation through every block: tokens (lanes,) -> logits (lanes, V).
+    state is new_state(...) and is updated in place; hidden (a list) collects each block's output."""
+    sites = sites or Sites()
+    x = w["emb.weight"][np.asarray(tokens)].astype(np.float64)
+    v_first = None
+    for i in range(sh.n_layer):
+        x, v_first = block_step(sh, w, i, x, state[i], v_first, sites)
+        if hidden is not None:
+            hidden.append(x.copy())
+    x = _ln(sites, "ln_out", x, w["ln_out.weight"], w["ln_out.bias"])
+    return x @ w["head.weight"].T
+
+
+def fit_sites(sh: RWKV7Shape, w, token_batches, degree=15, margin=0.1, tol=1e-4, seed_margin=(1.25, 2.0)):
+    """Polynomial sites from a calibration run: every Chebyshev site on its observed interval
+    widened by `margin` of its width (the harness's fit.py does the same per site), every norm
+    site a linear seed with the Newton iterations that reach `tol` on [m / lo, M * hi]."""
+    from .model import linear_rsqrt_seed, rsqrt_iters_for
+    rec = Sites(record=True)
+    st = new_state(sh, len(token_batches[0]))
+    for t in token_batches:
+        step(sh, w, t, st, rec)
+    fits = {}
+    for name, (lo, hi) in rec.ranges.items():
+        kind = name.split(".")[-1]
+        if name.endswith(("ln0", "ln1", "ln2", "ln_out", "gn_rsqrt", "kk_rsqrt")):
+            m0, m1 = max(lo, 1e-12) / seed_margin[0], hi * seed_margin[1]
+            a, b = linear_rsqrt_seed(m0, m1)
+            # the wkv readout's variance spans decades on a cold state: Newton from a linear seed
+            # then runs in its slow (x1.5 per step) phase for many steps
+            fits[name] = (a, b, rsqrt_iters_for(a, b, m0, m1, tol, cap=60))
+            continue
+        pad = margin * (hi - lo) + 1e-6
+        fits[name] = (lo - pad, hi + pad, cheb_fit(SITE_FUNCS[kind], lo - pad, hi + pad, degree))
+    return fits
+
+
+# ----------------------------------------------------------------- the encrypted wkv state ----
+class EncryptedWkv:
+    """The x070 state update of one head on the engine, for the conversations packed in one
+    ciphertext (slots / N^2 of them).  Layouts inside conversation c's block of N^2 slots:
+
+      * state        S[i][j] at c N^2 + i N + j;
+      * channel      a vector v[j] at c N^2 + j (row 0), zeros elsewhere;
+      * column       v[i] at c N^2 + i N + j for every j (the value side of v k^T).
+
+    Moves between them are rotations and one mask, never a general permutation:
+      * replicate a channel vector down the rows: N -> N rows by log2 N doublings (rotations
+        by -N 2^t);
+      * row sums: log2 N rotations by +2^t leave sum_j M[i][j] at (i, 0); a mask keeps only
+        that column (one level) and log2 N rotations by -2^t spread it along the row;
+      * the value projection v = W x lands in the column layout directly: the replicated x
+        times the plaintext W[i][c] at (i, c), row-summed and spread.
+
+    One step (wkv7_recurrence, rwkv7_model.py:290-296, with a = -kk and b = kk a):
+        S <- S (.) w_rep + spread(rowsum(S (.) a_rep)) (.) b_rep + v_col (.) k_rep,
+        y[i] = rowsum(S (.) r_rep) at (i, 0).
+    Every product is a relinearised, rescaled ciphertext product (mul_rescale), every mask a
+    plaintext product; levels are matched by align before additions."""
+
+    def __init__(self, cx, N=64):
+        self.cx, self.N = cx, N
+        self.B = N * N
+        self.lanes = cx.slots // self.B
+        if self.lanes < 1 or cx.slots % self.B:
+            raise ValueError("a conversation's N^2 state must divide the slots")
+        self.lg = int(np.log2(N))
+        m = np.zeros(self.B)
+        m[::N] = 1.0
+        self.mask_j0 = m
+
+    @staticmethod
+    def rotations(N=64):
+        r = []
+        for t in range(int(np.log2(N))):
+            r += [1 << t, -(1 << t), N << t, -(N << t)]
+        return r
+
+    # layout helpers --------------------------------------------------------------------------
+    def pack_state(self, S):
+        """S (lanes, N, N) -> slot vector"""
+        z = np.zeros(self.cx.slots)
+        z[: self.lanes * self.B] = np.asarray(S).reshape(self.lanes, -1).ravel()
+        return z
+
+    def pack_channel(self, v):
+        z = np.zeros(self.cx.slots)
+        for c in range(self.lanes):
+            z[c * self.B: c * self.B + self.N] = v[c]
+        return z
+
+    def unpack_state(self, z):
+        return np.asarray(z[: self.lanes * self.B]).real.reshape(self.lanes, self.N, self.N)
+
+    def unpack_col0(self, z):
+        """the values at (i, 0) of every conversation: (lanes, N)"""
+        return self.unpack_state(z)[:, :, 0]
+
+    def _add(self, a, b):
+        cx = self.cx
+        a, b = cx.Copy(a), cx.Copy(b)
+        if a.level < b.level:
+            cx.align(a, b.level)
+        elif b.level < a.level:
+            cx.align(b, a.level)
+        return cx.EvalAdd(a, b)
+
+    def _doubling(self, ct, step):
+        cx = self.cx
+        for t in range(self.lg):
+            ct = cx.EvalAdd(ct, cx.EvalRotate(ct, step << t))
+        return ct
+
+    def rep_rows(self, ct):
+        return self._doubling(ct, -self.N)
+
+    def spread_rowsum(self, ct):
+        """M -> (sum_j M[i][j]) at every (i, j): row sums, the column-0 mask, the spread"""
+        s = self._doubling(ct, 1)
+        s = self.cx.mul_vec_rescale(s, self.mask_j0)
+        return self._doubling(s, -1)
+
+    def rowsum_col0(self, ct):
+        """M -> sum_j M[i][j] at (i, 0), masked (zeros elsewhere)"""
+        return self.cx.mul_vec_rescale(self._doubling(ct, 1), self.mask_j0)
+
+    def value_column(self, x_ct, Wv):
+        """v = Wv x in the column layout from x in the channel layout (Wv: (N, N), v[i] =
+        sum_c Wv[i][c] x[c])"""
+        xr = self.rep_rows(x_ct)
+        return self.spread_rowsum(self.cx.mul_vec_rescale(xr, np.asarray(Wv, dtype=np.float64).ravel()))
+
+    def step(self, S_ct, w_ct, a_ct, b_ct, k_ct, r_ct, v_col):
+        """(S', y): the channel-layout inputs w, a, b, k, r; the column-layout value v_col"""
+        cx = self.cx
+        wr, ar, br, kr, rr = (self.rep_rows(c) for c in (w_ct, a_ct, b_ct, k_ct, r_ct))
+        sw = cx.mul_rescale(S_ct, wr)
+        sa = self.spread_rowsum(cx.mul_rescale(S_ct, ar))
+        sab = cx.mul_rescale(sa, br)
+        vk = cx.mul_rescale(v_col, kr)
+        S2 = self._add(self._add(sw, sab), vk)
+        y = self.rowsum_col0(cx.mul_rescale(S2, rr))
+        return S2, y
