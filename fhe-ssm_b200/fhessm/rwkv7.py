@@ -168,13 +168,15 @@ def new_state(sh: RWKV7Shape, lanes: int):
             for _ in range(sh.n_layer)]
 
 
-def block_step(sh: RWKV7Shape, w, i, x, st, v_first, sites):
-    """One block for one token: x (lanes, C) -> (x', v_first); st (the block's state) is updated."""
+def block_step(sh: RWKV7Shape, w, i, x, st, v_first, sites, ln0=True):
+    """One block for one token: x (lanes, C) -> (x', v_first); st (the block's state) is updated.
+    ln0=False: x is already through block 0's input norm (the client applies it before encrypting,
+    the reference folds it into the embedding table)."""
     B, C = x.shape
     H, N = sh.n_head, sh.head_size
     p = f"blocks.{i}."
     a_ = p + "att."
-    if i == 0:
+    if i == 0 and ln0:
         x = _ln(sites, p + "ln0", x, w[p + "ln0.weight"], w[p + "ln0.bias"])
     x0 = _ln(sites, p + "ln1", x, w[p + "ln1.weight"], w[p + "ln1.bias"])
     xx = st["att"] - x0
@@ -360,3 +362,230 @@ class EncryptedWkv:
         S2 = self._add(self._add(sw, sab), vk)
         y = self.rowsum_col0(cx.mul_rescale(S2, rr))
         return S2, y
+
+
+# ------------------------------------------------------------------ the encrypted RWKV-7 block ----
+class EncryptedRWKV7Block:
+    """One RWKV-7 block (time mix with the wkv state, channel mix) on the engine for one head
+    (C = N = 64), with the circuit's sites (``fits``: Chebyshev series, Newton 1/sqrt), against
+    which ``block_step(..., Sites(fits))`` is the float64 mirror.  Conversations sit one per N^2
+    slots (EncryptedWkv's layouts).  Linear layers in the channel layout run on the engine's BSGS
+    matvec (D = N, each N-slot block an independent vector); the value projection lands in the
+    column layout and the readout y in column 0 (EncryptedWkv); the output projection takes y from
+    column 0 back to the channel layout by a spread along the rows, a plaintext product with
+    Wo^T and column sums.  A ciphertext is bootstrapped when it has fewer levels left than the
+    next operation needs."""
+
+    def __init__(self, cx, sh: RWKV7Shape, w, layer, fits, b1=8):
+        if sh.n_embd != sh.head_size:
+            raise ValueError("one head: n_embd must equal head_size")
+        self.cx, self.sh, self.w, self.layer, self.fits = cx, sh, w, layer, fits
+        self.N = N = sh.head_size
+        self.wkv = EncryptedWkv(cx, N)
+        self.lanes = self.wkv.lanes
+        p = f"blocks.{layer}."
+        self.p, self.a_ = p, p + "att."
+        pad = lambda M: np.pad(M, ((0, N - M.shape[0]), (0, N - M.shape[1])))
+        a_ = self.a_
+        self.plans = {
+            "r": cx.matvec_plan(w[a_ + "receptance.weight"], N, b1),
+            "k": cx.matvec_plan(w[a_ + "key.weight"], N, b1),
+            "w1": cx.matvec_plan(pad(w[a_ + "w1"].T), N, b1), "w2": cx.matvec_plan(pad(w[a_ + "w2"].T), N, b1),
+            "a1": cx.matvec_plan(pad(w[a_ + "a1"].T), N, b1), "a2": cx.matvec_plan(pad(w[a_ + "a2"].T), N, b1),
+            "g1": cx.matvec_plan(pad(w[a_ + "g1"].T), N, b1),
+        }
+        if layer > 0:
+            self.plans["v1"] = cx.matvec_plan(pad(w[a_ + "v1"].T), N, b1)
+            self.plans["v2"] = cx.matvec_plan(pad(w[a_ + "v2"].T), N, b1)
+        F = sh.dim_ffn
+        kf, vf = w[p + "ffn.key.weight"], w[p + "ffn.value.weight"]
+        self.ffn_k = [cx.matvec_plan(kf[c * N:(c + 1) * N], N, b1) for c in range(F // N)]
+        self.ffn_v = cx.matvec_plan(vf, N, b1)   # (N, F): column chunk s acts on input s
+        self.g2 = pad(w[a_ + "g2"])               # (d_gate, C) -> the col-0 projection below
+        self.state = None                         # (prev_att, prev_ffn, S) ciphertexts
+
+    @staticmethod
+    def rotations(N=64):
+        return EncryptedWkv.rotations(N)
+
+    # level management ---------------------------------------------------------------------------
+    def left(self, ct):
+        return self.cx.L - ct.level - 1
+
+    def ensure(self, ct, k):
+        if self.left(ct) < k:
+            return self.cx.EvalBootstrap(ct)
+        return ct
+
+    def add(self, a, b):
+        return self.wkv._add(a, b)
+
+    def sub(self, a, b):
+        cx = self.cx
+        a, b = cx.Copy(a), cx.Copy(b)
+        if a.level < b.level:
+            cx.align(a, b.level)
+        elif b.level < a.level:
+            cx.align(b, a.level)
+        return cx.EvalSub(a, b)
+
+    def chan(self, v):
+        """a per-channel constant vector in the channel layout (one N^2 period)"""
+        z = np.zeros(self.N * self.N)
+        z[: self.N] = v
+        return z
+
+    def mulv(self, ct, v):
+        return self.cx.mul_vec_rescale(ct, self.chan(v))
+
+    def addv(self, ct, v):
+        """ct + v (channel layout) at ct's level and scale"""
+        cx = self.cx
+        pt = cx.MakeCKKSPackedPlaintext(np.tile(self.chan(v), cx.slots // (self.N * self.N)), level=ct.level,
+                                        scale=ct.scale)
+        return cx.EvalAdd(ct, pt)
+
+    def mulmul(self, a, b):
+        return self.cx.mul_rescale(a, b)
+
+    # circuit pieces ---------------------------------------------------------------------------------
+    def cheb(self, name, x):
+        """the site polynomial of `name` on x in the channel layout: [lo, hi] mapped to [-1, 1],
+        the series, and the row-0 mask (the series' constant term lands in every slot, and the
+        layouts' rotations need zeros outside the vector)"""
+        cx = self.cx
+        lo, hi, c = self.fits[name]
+        depth = 3 + int(np.ceil(np.log2(len(c))))
+        x = self.ensure(x, depth)
+        t = cx.EvalMultConst(x, 2.0 / (hi - lo))
+        t = cx.EvalAddConst(t, -(lo + hi) / (hi - lo))
+        return self.mulv(cx.EvalChebyshevSeries(t, c), np.ones(self.N))
+
+    def newton(self, name, v):
+        """the site's 1/sqrt(v) by its linear seed and Newton steps (v: eps already added)"""
+        cx = self.cx
+        a, b, iters = self.fits[name]
+        v = self.ensure(v, 4)
+        y = cx.EvalAddConst(cx.EvalMultConst(v, b), a)
+        mh = cx.EvalMultConst(v, -0.5)
+        for _ in range(int(iters)):
+            if self.left(y) < 3:
+                y = cx.EvalBootstrap(y)
+            if self.left(mh) < 3:
+                mh = cx.EvalBootstrap(mh)
+            y2 = self.mulmul(y, y)
+            t = self.mulmul(mh, y)
+            u = self.mulmul(t, y2)
+            y = self.add(cx.EvalMultConst(y, 1.5), u)
+        return y
+
+    def spread_mean(self, x, scale):
+        """scale * sum_j x[j] in every channel slot (channel layout in, channel layout out)"""
+        wkv = self.wkv
+        s = wkv._doubling(x, 1)
+        s = self.cx.mul_vec_rescale(s, self.chan(np.r_[scale, np.zeros(self.N - 1)]))
+        return wkv._doubling(s, -1)
+
+    def layer_norm(self, name, x, wgt, bias):
+        cx = self.cx
+        x = self.ensure(x, 4)
+        xc = self.sub(x, self.spread_mean(x, 1.0 / self.N))
+        var = self.spread_mean(self.mulmul(xc, xc), 1.0 / self.N)
+        y = self.newton(name, cx.EvalAddConst(var, RSQRT_EPS["ln"]))
+        xc = self.ensure(xc, 2)
+        return self.addv(self.mulv(self.mulmul(xc, y), wgt), bias)
+
+    def col0_to_channel(self, z_col0, Wt):
+        """z[i] at (i, 0) (zeros elsewhere) -> (Wt z)[j] in the channel layout: spread along the rows,
+        times Wt[j][i] at (i, j), column sums (rotations by +N 2^t), row 0 kept"""
+        cx, wkv, N = self.cx, self.wkv, self.N
+        zs = wkv._doubling(z_col0, -1)
+        prod = cx.mul_vec_rescale(zs, np.asarray(Wt, dtype=np.float64).T.ravel())
+        cs = wkv._doubling(prod, N)
+        row0 = np.zeros(N * N)
+        row0[:N] = 1.0
+        return cx.mul_vec_rescale(cs, row0)
+
+    def channel_to_col0(self, x, M):
+        """x[c] in the channel layout -> (M^T x)[i] = sum_c M[c][i] x[c] at (i, 0)"""
+        wkv = self.wkv
+        xr = wkv.rep_rows(x)
+        return wkv.rowsum_col0(self.cx.mul_vec_rescale(xr, np.asarray(M, dtype=np.float64).T.ravel()))
+
+    def head_sum_col0(self, z_col0):
+        """sum_i z[i] at every (i, 0): column sums, the (0, 0) mask, a spread down column 0"""
+        cx, wkv, N = self.cx, self.wkv, self.N
+        s = wkv._doubling(z_col0, N)
+        m = np.zeros(N * N)
+        m[0] = 1.0
+        s = cx.mul_vec_rescale(s, m)
+        return wkv._doubling(s, -N)
+
+    # the block ------------------------------------------------------------------------------------
+    def step(self, x):
+        """x (channel layout, the block's input) -> the block's output (channel layout)"""
+        cx, w, a_, p, N, wkv = self.cx, self.w, self.a_, self.p, self.N, self.wkv
+        if self.state is None:
+            zero = cx.Encrypt(cx.MakeCKKSPackedPlaintext(np.zeros(cx.slots)))
+            self.state = [zero, cx.Copy(zero), cx.Copy(zero)]
+        prev_att, prev_ffn, S = self.state
+        # ---- time mix
+        x0 = self.ensure(self.layer_norm(p + "ln1", x, w[p + "ln1.weight"], w[p + "ln1.bias"]), 6)
+        xx = self.sub(prev_att, x0)
+        mix = {m: self.add(x0, self.mulv(xx, w[a_ + m])) for m in ("x_r", "x_w", "x_k", "x_v", "x_a", "x_g")}
+        mix = {m: self.ensure(c, 6) for m, c in mix.items()}
+        r = cx.matvec(self.plans["r"], [mix["x_r"]])
+        k = cx.matvec(self.plans["k"], [mix["x_k"]])
+        v_col = wkv.value_column(mix["x_v"], w[a_ + "value.weight"])
+        z = self.addv(cx.matvec(self.plans["w2"], [self.ensure(self.cheb(a_ + "w_tanh",
+                                cx.matvec(self.plans["w1"], [mix["x_w"]])), 2)]), w[a_ + "w0"])
+        dec = self.cheb(a_ + "decay", z)
+        av = self.addv(cx.matvec(self.plans["a2"], [cx.matvec(self.plans["a1"], [mix["x_a"]])]), w[a_ + "a0"])
+        a = self.cheb(a_ + "a_sigmoid", av)
+        gs = self.cheb(a_ + "g_sigmoid", cx.matvec(self.plans["g1"], [mix["x_g"]]))
+        g_col0 = self.channel_to_col0(self.ensure(gs, 4), self.g2)
+        kk = self.mulv(k, w[a_ + "k_k"])
+        kn = self.newton(a_ + "kk_rsqrt", self.spread_mean(self.mulmul(kk, kk), 1.0))
+        kk = self.mulmul(self.ensure(kk, 2), kn)
+        a = self.ensure(a, 4)
+        kmod = self.mulmul(k, self.addv(self.mulv(self.addv(a, -np.ones(N)), w[a_ + "k_a"]), np.ones(N)))
+        b = self.mulmul(kk, a)
+        na = cx.EvalMultConst(kk, -1.0)
+        ins = [self.ensure(c, 8) for c in (dec, na, b, kmod, r, v_col)]
+        S = self.ensure(S, 8)
+        S, y = wkv.step(S, ins[0], ins[1], ins[2], ins[3], ins[4], ins[5])
+        # GroupNorm over the head (y[i] at (i, 0))
+        y = self.ensure(y, 6)
+        yc = self.sub(y, self.cx.EvalMultConst(self.head_sum_col0(y), 1.0 / N))
+        var = self.cx.EvalMultConst(self.head_sum_col0(self.mulmul(yc, yc)), 1.0 / N)
+        gn = self.newton(a_ + "gn_rsqrt", cx.EvalAddConst(var, RSQRT_EPS["gn"]))
+        yc = self.ensure(yc, 3)
+        col0 = lambda v: np.concatenate([[v[i]] + [0.0] * (N - 1) for i in range(N)])
+        y = self.mulmul(yc, gn)
+        y = cx.mul_vec_rescale(y, col0(w[a_ + "ln_x.weight"]))
+        ypt = cx.MakeCKKSPackedPlaintext(np.tile(col0(w[a_ + "ln_x.bias"]), cx.slots // (N * N)), level=y.level,
+                                         scale=y.scale)
+        y = cx.EvalAdd(y, ypt)
+        # bonus ((r k r_k) summed over the head) v, in column 0
+        rk = self.mulv(self.mulmul(self.ensure(r, 3), self.ensure(kmod, 3)), w[a_ + "r_k"].ravel())
+        s = wkv.rowsum_col0(wkv.rep_rows(rk))   # sum_j rk[j] at every (i, 0)
+        vc0 = cx.mul_vec_rescale(self.ensure(v_col, 3), wkv.mask_j0)
+        y = self.add(y, self.mulmul(self.ensure(s, 2), vc0))
+        y = self.ensure(y, 4)
+        yg = self.mulmul(y, self.ensure(g_col0, 2))
+        att = self.col0_to_channel(self.ensure(yg, 3), w[a_ + "output.weight"])
+        x1 = self.add(x, att)
+        # ---- channel mix
+        f = p + "ffn."
+        xf = self.ensure(self.layer_norm(p + "ln2", x1, w[p + "ln2.weight"], w[p + "ln2.bias"]), 4)
+        xxf = self.sub(prev_ffn, xf)
+        kf_in = self.ensure(self.add(xf, self.mulv(xxf, w[f + "x_k"])), 3)
+        hs = [self.ensure(self.cheb(f + "relu2", cx.matvec(pl, [kf_in])), 2) for pl in self.ffn_k]
+        lv = max(h.level for h in hs)   # the matvec's inputs share one level and scale
+        for h in hs:
+            if h.level < lv:
+                cx.align(h, lv)
+        out = cx.matvec(self.ffn_v, hs)
+        x2 = self.add(x1, out)
+        self.state = [x0, xf, S]
+        return x2

@@ -54,3 +54,40 @@ def test_wkv_state_update_matches_float64():
             assert es < 1e-4 and ey < 1e-4
     finally:
         cx.close()
+
+
+def test_rwkv7_block_matches_polynomial_model():
+    """One RWKV-7 block (layer 0: time mix with the wkv state, channel mix) on the engine for one
+    head of 64 channels, two tokens, against the float64 block with the same polynomial sites and
+    Newton seeds.  N = 2^13 with the bootstrapping chain (q0 60 bits, 19 x 45-bit user primes,
+    14 x 58-bit bootstrap primes, K = 4): a correctness test of the circuit, not a secure
+    parameter set at this ring size."""
+    import fhessm
+    from fhessm.rwkv7 import (EncryptedRWKV7Block, RWKV7Shape, Sites, _ln, block_step, fit_sites, new_state,
+                              synthetic_weights)
+    sh = RWKV7Shape(n_layer=1, n_embd=64, head_size=64, d_decay=16, d_aaa=16, d_mv=8, d_gate=32, dim_ffn=256,
+                    vocab_size=256)
+    w = synthetic_weights(sh, seed=9)
+    fits = fit_sites(sh, w, [np.random.default_rng(12).integers(0, sh.vocab_size, 32) for _ in range(4)], degree=15)
+    sites = Sites(fits)
+    cx = fhessm.CryptoContext(logN=13, L=34, K=4, alpha=4, hw=64, boot_primes=14)
+    try:
+        cx.KeyGen(seed=23)
+        cx.EvalRotateKeyGen(EncryptedRWKV7Block.rotations(64))
+        cx.matvec_keygen(64, 8)
+        cx.EvalBootstrapSetup(24.0, 31, 4)
+        blk = EncryptedRWKV7Block(cx, sh, w, 0, fits)
+        st = new_state(sh, 1)
+        toks = np.random.default_rng(13).integers(0, sh.vocab_size, 2)
+        for t, tok in enumerate(toks):
+            x = _ln(sites, "blocks.0.ln0", w["emb.weight"][[tok]], w["blocks.0.ln0.weight"], w["blocks.0.ln0.bias"])
+            ref, _ = block_step(sh, w, 0, x.copy(), st[0], None, sites, ln0=False)
+            z = np.zeros(cx.slots)
+            z[:64] = x[0]
+            out = blk.step(cx.Encrypt(cx.MakeCKKSPackedPlaintext(z)))
+            got = np.asarray(cx.Decrypt(out)).real[:64]
+            err = np.abs(got - ref[0]).max() / np.abs(ref[0]).max()
+            print(f"token {t}: block output rel err {err:.2e} (level {out.level})")
+            assert err < 1e-3
+    finally:
+        cx.close()
