@@ -448,6 +448,10 @@ class EncryptedRWKV7Block:
     def mulmul(self, a, b):
         return self.cx.mul_rescale(a, b)
 
+    def mulc(self, ct, c):
+        """ct * c, rescaled onto the next level's canonical scale (a constant slot vector)"""
+        return self.cx.mul_vec_rescale(ct, np.full(8, float(c)))
+
     # circuit pieces ---------------------------------------------------------------------------------
     def cheb(self, name, x):
         """the site polynomial of `name` on x in the channel layout: [lo, hi] mapped to [-1, 1],
@@ -457,7 +461,7 @@ class EncryptedRWKV7Block:
         lo, hi, c = self.fits[name]
         depth = 3 + int(np.ceil(np.log2(len(c))))
         x = self.ensure(x, depth)
-        t = cx.EvalMultConst(x, 2.0 / (hi - lo))
+        t = self.mulc(x, 2.0 / (hi - lo))
         t = cx.EvalAddConst(t, -(lo + hi) / (hi - lo))
         return self.mulv(cx.EvalChebyshevSeries(t, c), np.ones(self.N))
 
@@ -466,8 +470,8 @@ class EncryptedRWKV7Block:
         cx = self.cx
         a, b, iters = self.fits[name]
         v = self.ensure(v, 4)
-        y = cx.EvalAddConst(cx.EvalMultConst(v, b), a)
-        mh = cx.EvalMultConst(v, -0.5)
+        y = cx.EvalAddConst(self.mulc(v, b), a)
+        mh = self.mulc(v, -0.5)
         for _ in range(int(iters)):
             if self.left(y) < 3:
                 y = cx.EvalBootstrap(y)
@@ -476,7 +480,7 @@ class EncryptedRWKV7Block:
             y2 = self.mulmul(y, y)
             t = self.mulmul(mh, y)
             u = self.mulmul(t, y2)
-            y = self.add(cx.EvalMultConst(y, 1.5), u)
+            y = self.add(self.mulc(y, 1.5), u)
         return y
 
     def spread_mean(self, x, scale):
@@ -550,14 +554,14 @@ class EncryptedRWKV7Block:
         a = self.ensure(a, 4)
         kmod = self.mulmul(k, self.addv(self.mulv(self.addv(a, -np.ones(N)), w[a_ + "k_a"]), np.ones(N)))
         b = self.mulmul(kk, a)
-        na = cx.EvalMultConst(kk, -1.0)
+        na = self.mulc(kk, -1.0)
         ins = [self.ensure(c, 8) for c in (dec, na, b, kmod, r, v_col)]
         S = self.ensure(S, 8)
         S, y = wkv.step(S, ins[0], ins[1], ins[2], ins[3], ins[4], ins[5])
         # GroupNorm over the head (y[i] at (i, 0))
         y = self.ensure(y, 6)
-        yc = self.sub(y, self.cx.EvalMultConst(self.head_sum_col0(y), 1.0 / N))
-        var = self.cx.EvalMultConst(self.head_sum_col0(self.mulmul(yc, yc)), 1.0 / N)
+        yc = self.sub(y, self.mulc(self.head_sum_col0(y), 1.0 / N))
+        var = self.mulc(self.head_sum_col0(self.mulmul(yc, yc)), 1.0 / N)
         gn = self.newton(a_ + "gn_rsqrt", cx.EvalAddConst(var, RSQRT_EPS["gn"]))
         yc = self.ensure(yc, 3)
         col0 = lambda v: np.concatenate([[v[i]] + [0.0] * (N - 1) for i in range(N)])
