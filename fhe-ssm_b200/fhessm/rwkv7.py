@@ -527,10 +527,13 @@ class EncryptedRWKV7Block:
 
     # the block ------------------------------------------------------------------------------------
     def step(self, x):
-        """x (channel layout, the block's input) -> the block's output (channel layout)"""
+        """x (channel layout, the block's input) -> the block's output (channel layout).  x comes
+        at most at the top of the chain's user region (with a bootstrapping chain the scales of
+        the two regions are anchored separately, and products must not cross from one to the
+        other)."""
         cx, w, a_, p, N, wkv = self.cx, self.w, self.a_, self.p, self.N, self.wkv
-        if self.state is None:
-            zero = cx.Encrypt(cx.MakeCKKSPackedPlaintext(np.zeros(cx.slots)))
+        if self.state is None:   # the cold state, at the input's level
+            zero = cx.Encrypt(cx.MakeCKKSPackedPlaintext(np.zeros(cx.slots), level=x.level))
             self.state = [zero, cx.Copy(zero), cx.Copy(zero)]
         prev_att, prev_ffn, S = self.state
         # ---- time mix
