@@ -436,7 +436,7 @@ class EncryptedRWKV7Block:
         return z
 
     def mulv(self, ct, v):
-        return self.cx.mul_vec_rescale(ct, self.chan(v))
+        return self.cx.mul_vec_rescale(self.ensure(ct, 1), self.chan(v))
 
     def addv(self, ct, v):
         """ct + v (channel layout) at ct's level and scale"""
@@ -446,11 +446,12 @@ class EncryptedRWKV7Block:
         return cx.EvalAdd(ct, pt)
 
     def mulmul(self, a, b):
-        return self.cx.mul_rescale(a, b)
+        """a * b, relinearised and rescaled; an operand without a level left is bootstrapped"""
+        return self.cx.mul_rescale(self.ensure(a, 1), self.ensure(b, 1))
 
     def mulc(self, ct, c):
         """ct * c, rescaled onto the next level's canonical scale (a constant slot vector)"""
-        return self.cx.mul_vec_rescale(ct, np.full(8, float(c)))
+        return self.cx.mul_vec_rescale(self.ensure(ct, 1), np.full(8, float(c)))
 
     # circuit pieces ---------------------------------------------------------------------------------
     def cheb(self, name, x):
