@@ -527,8 +527,14 @@ class EncryptedRWKV7Block:
         return wkv._doubling(s, -N)
 
     # the block ------------------------------------------------------------------------------------
-    def step(self, x):
-        """x (channel layout, the block's input) -> the block's output (channel layout).  x comes
+    def to_column(self, x):
+        """a channel-layout vector x[i] -> the column layout (x[i] at (i, j)): the identity
+        projection into column 0, then a spread along the rows"""
+        return self.wkv._doubling(self.channel_to_col0(x, np.eye(self.N)), -1)
+
+    def step(self, x, v_first=None):
+        """(x, v_first) -> (the block's output, v_first): x in the channel layout, v_first the
+        first block's value in the column layout (None for block 0, which makes it).  x comes
         at most at the top of the chain's user region (with a bootstrapping chain the scales of
         the two regions are anchored separately, and products must not cross from one to the
         other)."""
@@ -545,6 +551,12 @@ class EncryptedRWKV7Block:
         r = cx.matvec(self.plans["r"], [mix["x_r"]])
         k = cx.matvec(self.plans["k"], [mix["x_k"]])
         v_col = wkv.value_column(mix["x_v"], w[a_ + "value.weight"])
+        if self.layer == 0:
+            v_first = v_col
+        else:   # v += (v_first - v) sigmoid(v0 + (x_v V1) V2), the gate brought to the column layout
+            vg = self.addv(cx.matvec(self.plans["v2"], [cx.matvec(self.plans["v1"], [mix["x_v"]])]), w[a_ + "v0"])
+            gate = self.to_column(self.ensure(self.cheb(a_ + "v_sigmoid", vg), 4))
+            v_col = self.add(v_col, self.mulmul(self.sub(v_first, v_col), gate))
         z = self.addv(cx.matvec(self.plans["w2"], [self.ensure(self.cheb(a_ + "w_tanh",
                                 cx.matvec(self.plans["w1"], [mix["x_w"]])), 2)]), w[a_ + "w0"])
         dec = self.cheb(a_ + "decay", z)
@@ -596,4 +608,34 @@ class EncryptedRWKV7Block:
         out = cx.matvec(self.ffn_v, hs)
         x2 = self.add(x1, out)
         self.state = [x0, xf, S]
-        return x2
+        return x2, v_first
+
+
+class EncryptedRWKV7:
+    """Every block of a one-head RWKV-7 on the engine (EncryptedRWKV7Block each), the value of
+    block 0 carried to the others.  The client applies block 0's input norm before encrypting
+    (the reference folds ln0 into the embedding table) and the output norm and head after
+    decrypting (``client_logits``), as the reference's server does not evaluate them."""
+
+    def __init__(self, cx, sh: RWKV7Shape, w, fits, b1=8):
+        self.cx, self.sh, self.w, self.fits = cx, sh, w, fits
+        self.blocks = [EncryptedRWKV7Block(cx, sh, w, i, fits, b1) for i in range(sh.n_layer)]
+
+    def step(self, x_ct):
+        v_first = None
+        for b in self.blocks:
+            x_ct, v_first = b.step(x_ct, v_first)
+        return x_ct
+
+    def client_input(self, tokens, sites=None, lanes_per_ct=1):
+        """the embedding rows through block 0's input norm, in the channel layout"""
+        sites = sites or Sites(self.fits)
+        w = self.w
+        x = _ln(sites, "blocks.0.ln0", w["emb.weight"][np.asarray(tokens)], w["blocks.0.ln0.weight"],
+                w["blocks.0.ln0.bias"])
+        return x
+
+    def client_logits(self, hidden, sites=None):
+        sites = sites or Sites(self.fits)
+        w = self.w
+        return _ln(sites, "ln_out", hidden, w["ln_out.weight"], w["ln_out.bias"]) @ w["head.weight"].T

@@ -84,10 +84,42 @@ def test_rwkv7_block_matches_polynomial_model():
             ref, _ = block_step(sh, w, 0, x.copy(), st[0], None, sites, ln0=False)
             z = np.zeros(cx.slots)
             z[:64] = x[0]
-            out = blk.step(cx.Encrypt(cx.MakeCKKSPackedPlaintext(z, level=14)))   # the user region's top
+            out, _ = blk.step(cx.Encrypt(cx.MakeCKKSPackedPlaintext(z, level=14)))   # the user region's top
             got = np.asarray(cx.Decrypt(out)).real[:64]
             err = np.abs(got - ref[0]).max() / np.abs(ref[0]).max()
             print(f"token {t}: block output rel err {err:.2e} (level {out.level})")
             assert err < 1e-3
+    finally:
+        cx.close()
+
+
+def test_rwkv7_two_layers_logits_match_polynomial_model():
+    """Two blocks (the value residual of block 1 on block 0's value), three tokens, logits after the
+    client's output norm and head against the float64 model with the same sites."""
+    import fhessm
+    from fhessm.rwkv7 import EncryptedRWKV7, RWKV7Shape, Sites, fit_sites, new_state, step, synthetic_weights
+    sh = RWKV7Shape(n_layer=2, n_embd=64, head_size=64, d_decay=16, d_aaa=16, d_mv=8, d_gate=32, dim_ffn=256,
+                    vocab_size=256)
+    w = synthetic_weights(sh, seed=10)
+    fits = fit_sites(sh, w, [np.random.default_rng(14).integers(0, sh.vocab_size, 32) for _ in range(4)], degree=15)
+    sites = Sites(fits)
+    cx = fhessm.CryptoContext(logN=13, L=34, K=4, alpha=4, hw=64, boot_primes=14)
+    try:
+        cx.KeyGen(seed=24)
+        cx.EvalRotateKeyGen(fhessm.rwkv7.EncryptedRWKV7Block.rotations(64))
+        cx.matvec_keygen(64, 8)
+        cx.EvalBootstrapSetup(24.0, 31, 4)
+        model = EncryptedRWKV7(cx, sh, w, fits)
+        st = new_state(sh, 1)
+        for t, tok in enumerate(np.random.default_rng(15).integers(0, sh.vocab_size, 3)):
+            ref = step(sh, w, [tok], st, sites)
+            z = np.zeros(cx.slots)
+            z[:64] = model.client_input([tok])[0]
+            out = model.step(cx.Encrypt(cx.MakeCKKSPackedPlaintext(z, level=14)))
+            hid = np.asarray(cx.Decrypt(out)).real[:64][None]
+            lg = model.client_logits(hid)
+            err = np.abs(lg - ref).max() / np.abs(ref).max()
+            print(f"token {t}: logits rel err {err:.2e}, top-1 {lg.argmax() == ref.argmax()}")
+            assert err < 1e-3 and lg.argmax() == ref.argmax()
     finally:
         cx.close()
