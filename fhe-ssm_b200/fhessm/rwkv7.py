@@ -466,13 +466,17 @@ class EncryptedRWKV7Block:
         t = cx.EvalAddConst(t, -(lo + hi) / (hi - lo))
         return self.mulv(cx.EvalChebyshevSeries(t, c), np.ones(self.N))
 
-    def newton(self, name, v):
-        """the site's 1/sqrt(v) by its linear seed and Newton steps (v: eps already added)"""
+    def newton(self, name, v, mask):
+        """the site's 1/sqrt(v) by its linear seed and Newton steps (v: eps already added) in the
+        slots where ``mask`` (one N^2 period) is 1.  The other slots hold eps alone, where Newton
+        would climb towards 1/sqrt(eps) (40 for GroupNorm's) and a bootstrap of that range loses
+        precision in every slot: the 1.5 y term carries the mask, which sends them to zero."""
         cx = self.cx
         a, b, iters = self.fits[name]
         v = self.ensure(v, 4)
         y = cx.EvalAddConst(self.mulc(v, b), a)
         mh = self.mulc(v, -0.5)
+        m15 = 1.5 * np.asarray(mask, dtype=np.float64)
         for _ in range(int(iters)):
             if self.left(y) < 3:
                 y = cx.EvalBootstrap(y)
@@ -481,7 +485,7 @@ class EncryptedRWKV7Block:
             y2 = self.mulmul(y, y)
             t = self.mulmul(mh, y)
             u = self.mulmul(t, y2)
-            y = self.add(self.mulc(y, 1.5), u)
+            y = self.add(cx.mul_vec_rescale(y, m15), u)
         return y
 
     def spread_mean(self, x, scale):
@@ -496,7 +500,7 @@ class EncryptedRWKV7Block:
         x = self.ensure(x, 4)
         xc = self.sub(x, self.spread_mean(x, 1.0 / self.N))
         var = self.spread_mean(self.mulmul(xc, xc), 1.0 / self.N)
-        y = self.newton(name, cx.EvalAddConst(var, RSQRT_EPS["ln"]))
+        y = self.newton(name, cx.EvalAddConst(var, RSQRT_EPS["ln"]), self.chan(np.ones(self.N)))
         xc = self.ensure(xc, 2)
         return self.addv(self.mulv(self.mulmul(xc, y), wgt), bias)
 
@@ -565,7 +569,7 @@ class EncryptedRWKV7Block:
         gs = self.cheb(a_ + "g_sigmoid", cx.matvec(self.plans["g1"], [mix["x_g"]]))
         g_col0 = self.channel_to_col0(self.ensure(gs, 4), self.g2)
         kk = self.mulv(k, w[a_ + "k_k"])
-        kn = self.newton(a_ + "kk_rsqrt", self.spread_mean(self.mulmul(kk, kk), 1.0))
+        kn = self.newton(a_ + "kk_rsqrt", self.spread_mean(self.mulmul(kk, kk), 1.0), self.chan(np.ones(N)))
         kk = self.mulmul(self.ensure(kk, 2), kn)
         a = self.ensure(a, 4)
         kmod = self.mulmul(k, self.addv(self.mulv(self.addv(a, -np.ones(N)), w[a_ + "k_a"]), np.ones(N)))
@@ -578,7 +582,7 @@ class EncryptedRWKV7Block:
         y = self.ensure(y, 6)
         yc = self.sub(y, self.mulc(self.head_sum_col0(y), 1.0 / N))
         var = self.mulc(self.head_sum_col0(self.mulmul(yc, yc)), 1.0 / N)
-        gn = self.newton(a_ + "gn_rsqrt", cx.EvalAddConst(var, RSQRT_EPS["gn"]))
+        gn = self.newton(a_ + "gn_rsqrt", cx.EvalAddConst(var, RSQRT_EPS["gn"]), wkv.mask_j0)
         yc = self.ensure(yc, 3)
         col0 = lambda v: np.concatenate([[v[i]] + [0.0] * (N - 1) for i in range(N)])
         y = self.mulmul(yc, gn)

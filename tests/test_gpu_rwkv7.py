@@ -94,7 +94,7 @@ def test_rwkv7_block_matches_polynomial_model():
 
 
 def test_rwkv7_two_layers_logits_match_polynomial_model():
-    """Two blocks (the value residual of block 1 on block 0's value), three tokens, logits after the
+    """Two blocks (the value residual of block 1 on block 0's value), four tokens, logits after the
     client's output norm and head against the float64 model with the same sites."""
     import fhessm
     from fhessm.rwkv7 import EncryptedRWKV7, RWKV7Shape, Sites, fit_sites, new_state, step, synthetic_weights
@@ -111,7 +111,7 @@ def test_rwkv7_two_layers_logits_match_polynomial_model():
         cx.EvalBootstrapSetup(24.0, 31, 4)
         model = EncryptedRWKV7(cx, sh, w, fits)
         st = new_state(sh, 1)
-        for t, tok in enumerate(np.random.default_rng(15).integers(0, sh.vocab_size, 3)):
+        for t, tok in enumerate(np.random.default_rng(15).integers(0, sh.vocab_size, 4)):
             ref = step(sh, w, [tok], st, sites)
             z = np.zeros(cx.slots)
             z[:64] = model.client_input([tok])[0]
