@@ -139,22 +139,28 @@ static double cos_target(double x, const void* arg) {
     return std::cos(2 * M_PI * (c->B * x - 0.25) / (double)(1 << c->r));
 }
 
-// rotation steps the bootstrap needs (babies j*base, giants g*b1*base)
+// rotation steps the bootstrap needs (babies j*base, giants g*b1*base).  SlotToCoeff's levels
+// start at stage 0, 1 per, 2 per; CoeffToSlot's are cut from the top (logn - per, logn - 2 per,
+// 0), which is the same split only when per divides logn (n = 2^12, 2^15): both sets of bases.
 std::vector<int> boot_rotations(const Context& cx) {
     const int n = cx.N / 2;
     int logn = 0;
     while ((1 << logn) < n) logn++;
-    std::vector<int> r;
+    std::set<int> r;
     const int per = (logn + 2) / 3;   // stages per level (5 at n = 2^15)
+    std::set<int> los;
     for (int lv = 0; lv < 3; lv++) {
-        const int lo = lv * per;
-        if (lo >= logn) break;
-        const int base = 1 << lo;
-        for (int j = 1; j < kBootB1; j++) r.push_back(j * base);
-        for (int g = -32 / kBootB1; g < 32 / kBootB1; g++)
-            if (g && (g * kBootB1 * base) % n != 0) r.push_back(g * kBootB1 * base);   // a full turn needs no key
+        if (lv * per < logn) los.insert(lv * per);                         // SlotToCoeff
+        los.insert(std::max(0, logn - (lv + 1) * per));                    // CoeffToSlot
     }
-    return r;
+    for (int lo : los) {
+        const int base = 1 << lo;
+        for (int j = 1; j < kBootB1; j++)
+            if ((j * base) % n != 0) r.insert(j * base);
+        for (int g = -32 / kBootB1; g < 32 / kBootB1; g++)
+            if (g && (g * kBootB1 * base) % n != 0) r.insert(g * kBootB1 * base);   // a full turn needs no key
+    }
+    return std::vector<int>(r.begin(), r.end());
 }
 
 // the smallest power-of-two period of a slot vector (exact comparison: the entries of a

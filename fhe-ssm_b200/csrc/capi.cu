@@ -342,8 +342,8 @@ int fhe_ct_copy(fhe_ctx* cx, const fhe_ct* a, fhe_ct** out) {
             *out = wrap(cx, std::move(r));                                  \
         });                                                                 \
     }
-BINOP(fhe_add, fhe::ct_add)
-BINOP(fhe_sub, fhe::ct_sub)
+BINOP(fhe_add, fhe::add_any)
+BINOP(fhe_sub, fhe::sub_any)
 BINOP(fhe_mul_ct_ct_relin, fhe::ct_mul_relin)
 
 int fhe_mul_ct_pt(fhe_ctx* cx, const fhe_ct* a, const fhe_pt* pt, fhe_ct** out) {

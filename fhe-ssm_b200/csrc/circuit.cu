@@ -101,7 +101,9 @@ void align(Context& cx, Ciphertext& a, int nl_t, double target) {
 }
 
 // a and b to a common level (the lower one) with equal scales.  Equal-level operands whose
-// scales differ by an integer factor are fixed by an exact integer product.
+// scales differ by an integer factor are fixed by an exact integer product; any other ratio (a
+// bootstrap's output against a product of canonical operands, say) by aligning both one level
+// down onto the canonical scale there.
 void match(Context& cx, Ciphertext& a, Ciphertext& b) {
     if (a.nl > b.nl) {
         align(cx, a, b.nl, b.scale);
@@ -116,17 +118,35 @@ void match(Context& cx, Ciphertext& a, Ciphertext& b) {
     Ciphertext* lo = r > 1 ? &b : &a;
     const double f = r > 1 ? r : 1.0 / r;
     const double fi = std::round(f);
-    require(std::fabs(f - fi) < 1e-9 * f, "match: equal levels with a non-integer scale ratio");
-    mul_integer(cx, *lo, fi, *lo);
-    lo->scale *= fi;
+    if (std::fabs(f - fi) < 1e-9 * f) {
+        mul_integer(cx, *lo, fi, *lo);
+        lo->scale *= fi;
+        return;
+    }
+    require(a.nl >= 2, "match: equal levels with a non-integer scale ratio and no level left");
+    align(cx, a, a.nl - 1, 0);
+    align(cx, b, b.nl - 1, 0);
+}
+
+static bool same_level_scale(const Ciphertext& a, const Ciphertext& b) {
+    const double r = a.scale / b.scale;
+    return a.nl == b.nl && r > 1 - 1e-9 && r < 1 + 1e-9;
 }
 
 void add_any(Context& cx, const Ciphertext& a0, const Ciphertext& b0, Ciphertext& out) {
+    if (same_level_scale(a0, b0)) {
+        ct_add(cx, a0, b0, out);
+        return;
+    }
     Ciphertext a = ct_copy(cx, a0), b = ct_copy(cx, b0);
     match(cx, a, b);
     ct_add(cx, a, b, out);
 }
 void sub_any(Context& cx, const Ciphertext& a0, const Ciphertext& b0, Ciphertext& out) {
+    if (same_level_scale(a0, b0)) {
+        ct_sub(cx, a0, b0, out);
+        return;
+    }
     Ciphertext a = ct_copy(cx, a0), b = ct_copy(cx, b0);
     match(cx, a, b);
     ct_sub(cx, a, b, out);

@@ -318,13 +318,8 @@ class EncryptedWkv:
         return self.unpack_state(z)[:, :, 0]
 
     def _add(self, a, b):
-        cx = self.cx
-        a, b = cx.Copy(a), cx.Copy(b)
-        if a.level < b.level:
-            cx.align(a, b.level)
-        elif b.level < a.level:
-            cx.align(b, a.level)
-        return cx.EvalAdd(a, b)
+        """a + b; the engine's EvalAdd reconciles levels and scales"""
+        return self.cx.EvalAdd(a, b)
 
     def _doubling(self, ct, step):
         cx = self.cx
@@ -366,49 +361,105 @@ class EncryptedWkv:
 
 # ------------------------------------------------------------------ the encrypted RWKV-7 block ----
 class EncryptedRWKV7Block:
-    """One RWKV-7 block (time mix with the wkv state, channel mix) on the engine for one head
-    (C = N = 64), with the circuit's sites (``fits``: Chebyshev series, Newton 1/sqrt), against
-    which ``block_step(..., Sites(fits))`` is the float64 mirror.  Conversations sit one per N^2
-    slots (EncryptedWkv's layouts).  Linear layers in the channel layout run on the engine's BSGS
-    matvec (D = N, each N-slot block an independent vector); the value projection lands in the
-    column layout and the readout y in column 0 (EncryptedWkv); the output projection takes y from
-    column 0 back to the channel layout by a spread along the rows, a plaintext product with
-    Wo^T and column sums.  A ciphertext is bootstrapped when it has fewer levels left than the
-    next operation needs."""
+    """One RWKV-7 block (time mix with the wkv state, channel mix) on the engine for ``convs``
+    conversations of C = H N channels (H heads of N), with the circuit's sites (``fits``:
+    Chebyshev series, Newton 1/sqrt), against which ``block_step(..., Sites(fits))`` is the
+    float64 mirror.  Two layouts:
 
-    def __init__(self, cx, sh: RWKV7Shape, w, layer, fits, b1=8):
-        if sh.n_embd != sh.head_size:
-            raise ValueError("one head: n_embd must equal head_size")
+      * contiguous: conversation l's channel c at slot l C + c.  This is the engine's matvec
+        layout with D = C, so every linear layer is one BSGS matvec (LoRA matrices padded to
+        C x C); a per-head sum (kk normalisation, GroupNorm, the bonus) is log2 N doublings by
+        +1, a mask at the head's first slot and log2 N doublings by -1, a per-conversation sum
+        (LayerNorm) the same over C;
+      * the wkv state: head block b = l H + h; B = slots / N^2 blocks per state ciphertext, block
+        u of state ciphertext t holds head block t B + u in EncryptedWkv's layouts.
+
+    Into the state blocks (``to_rows``): a rotation by t B N brings blocks t B .. t B + B - 1 to
+    slots u N + j, a mask keeps them, and log2 B bit steps move the blocks whose index has bit
+    b set by 2^b (N^2 - N) (high bit first), one mask level each.  Back (``from_col0``): the
+    readout y[i] at (i, 0) of each block is transposed to row 0 inside the block (spread along
+    the row, the diagonal mask, column sums, the row-0 mask), the bit steps run in reverse and a
+    rotation by -t B N puts the blocks in place.  A ciphertext is bootstrapped when it has fewer
+    levels left than the next operation needs."""
+
+    def __init__(self, cx, sh: RWKV7Shape, w, layer, fits, convs=1, b1=8):
+        C, N = sh.n_embd, sh.head_size
+        if cx.slots % C or convs * C > cx.slots:
+            raise ValueError("the contiguous layout needs C | slots and convs * C <= slots")
         self.cx, self.sh, self.w, self.layer, self.fits = cx, sh, w, layer, fits
-        self.N = N = sh.head_size
+        self.C, self.N, self.H, self.convs = C, N, sh.n_head, convs
         self.wkv = EncryptedWkv(cx, N)
-        self.lanes = self.wkv.lanes
+        self.B = self.wkv.lanes                       # head blocks per state ciphertext
+        self.nb = convs * self.H                      # head blocks in use
+        self.n_state = -(-self.nb // self.B)
+        self.lgB = int(np.log2(self.B))
+        self.keys = set(self.rotations(sh, cx.slots))
+        self.lane_mask = np.zeros(cx.slots)
+        self.lane_mask[: convs * C] = 1.0
         p = f"blocks.{layer}."
         self.p, self.a_ = p, p + "att."
-        pad = lambda M: np.pad(M, ((0, N - M.shape[0]), (0, N - M.shape[1])))
         a_ = self.a_
+        pad = lambda M: np.pad(M, ((0, C - M.shape[0]), (0, C - M.shape[1])))
+        plan = lambda M: cx.matvec_plan(M, C, b1)
         self.plans = {
-            "r": cx.matvec_plan(w[a_ + "receptance.weight"], N, b1),
-            "k": cx.matvec_plan(w[a_ + "key.weight"], N, b1),
-            "w1": cx.matvec_plan(pad(w[a_ + "w1"].T), N, b1), "w2": cx.matvec_plan(pad(w[a_ + "w2"].T), N, b1),
-            "a1": cx.matvec_plan(pad(w[a_ + "a1"].T), N, b1), "a2": cx.matvec_plan(pad(w[a_ + "a2"].T), N, b1),
-            "g1": cx.matvec_plan(pad(w[a_ + "g1"].T), N, b1),
+            "r": plan(w[a_ + "receptance.weight"]), "k": plan(w[a_ + "key.weight"]),
+            "v": plan(w[a_ + "value.weight"]), "o": plan(w[a_ + "output.weight"]),
+            "w1": plan(pad(w[a_ + "w1"].T)), "w2": plan(pad(w[a_ + "w2"].T)),
+            "a1": plan(pad(w[a_ + "a1"].T)), "a2": plan(pad(w[a_ + "a2"].T)),
+            "g1": plan(pad(w[a_ + "g1"].T)), "g2": plan(pad(w[a_ + "g2"].T)),
         }
+        self.mid = {"w1": sh.d_decay, "a1": sh.d_aaa, "g1": sh.d_gate}
         if layer > 0:
-            self.plans["v1"] = cx.matvec_plan(pad(w[a_ + "v1"].T), N, b1)
-            self.plans["v2"] = cx.matvec_plan(pad(w[a_ + "v2"].T), N, b1)
+            self.plans["v1"] = plan(pad(w[a_ + "v1"].T))
+            self.plans["v2"] = plan(pad(w[a_ + "v2"].T))
+            self.mid["v1"] = sh.d_mv
         F = sh.dim_ffn
+        if F % C:
+            raise ValueError("dim_ffn must be a multiple of n_embd")
         kf, vf = w[p + "ffn.key.weight"], w[p + "ffn.value.weight"]
-        self.ffn_k = [cx.matvec_plan(kf[c * N:(c + 1) * N], N, b1) for c in range(F // N)]
-        self.ffn_v = cx.matvec_plan(vf, N, b1)   # (N, F): column chunk s acts on input s
-        self.g2 = pad(w[a_ + "g2"])               # (d_gate, C) -> the col-0 projection below
-        self.state = None                         # (prev_att, prev_ffn, S) ciphertexts
+        self.ffn_k = [plan(kf[c * C:(c + 1) * C]) for c in range(F // C)]
+        self.ffn_v = plan(vf)                          # (C, F): column chunk s acts on input s
+        self.state = None                              # (prev_att, prev_ffn, [S_t]) ciphertexts
 
     @staticmethod
-    def rotations(N=64):
-        return EncryptedWkv.rotations(N)
+    def rotations(sh: RWKV7Shape, slots):
+        """the rotation steps the block uses at this slot count"""
+        N, C = sh.head_size, sh.n_embd
+        r = set(EncryptedWkv.rotations(N))
+        for t in range(int(np.log2(C))):
+            r |= {1 << t, -(1 << t)}
+        for k in range(int(np.log2(slots)) - 1):
+            r |= {1 << k, -(1 << k)}
+        r.add(slots // 2)
+        for b in range(int(np.log2(slots // (N * N)))):
+            d = (1 << b) * (N * N - N)
+            r |= {d, -d}
+        return sorted(r)
 
-    # level management ---------------------------------------------------------------------------
+    # packing -------------------------------------------------------------------------------------
+    def pack(self, x):
+        """x (convs, C) -> the contiguous slot vector"""
+        z = np.zeros(self.cx.slots)
+        z[: self.convs * self.C] = np.asarray(x, dtype=np.float64).ravel()
+        return z
+
+    def unpack(self, z):
+        return np.asarray(z).real[: self.convs * self.C].reshape(self.convs, self.C)
+
+    def tile(self, v):
+        """a per-channel vector on every conversation in use, zeros elsewhere"""
+        z = np.zeros(self.cx.slots)
+        z[: self.convs * self.C] = np.tile(np.asarray(v, dtype=np.float64).ravel(), self.convs)
+        return z
+
+    def every(self, period, scale, first=1):
+        """scale at the first ``first`` slots of every block of ``period`` slots in use"""
+        z = np.zeros(self.cx.slots)
+        for s in range(0, self.convs * self.C, period):
+            z[s:s + first] = scale
+        return z
+
+    # level management and arithmetic --------------------------------------------------------------
     def left(self, ct):
         return self.cx.L - ct.level - 1
 
@@ -421,29 +472,32 @@ class EncryptedRWKV7Block:
         return self.wkv._add(a, b)
 
     def sub(self, a, b):
-        cx = self.cx
-        a, b = cx.Copy(a), cx.Copy(b)
-        if a.level < b.level:
-            cx.align(a, b.level)
-        elif b.level < a.level:
-            cx.align(b, a.level)
-        return cx.EvalSub(a, b)
+        return self.cx.EvalSub(a, b)
 
-    def chan(self, v):
-        """a per-channel constant vector in the channel layout (one N^2 period)"""
-        z = np.zeros(self.N * self.N)
-        z[: self.N] = v
-        return z
+    def rot(self, ct, k):
+        """left rotation by k (slot s receives slot s + k), one keyed step or its binary digits"""
+        slots = self.cx.slots
+        k %= slots
+        if k == 0:
+            return ct
+        for kk in (k, k - slots):
+            if kk in self.keys:
+                return self.cx.EvalRotate(ct, kk)
+        for b in range(int(np.log2(slots))):
+            if k >> b & 1:
+                ct = self.cx.EvalRotate(ct, 1 << b)
+        return ct
 
     def mulv(self, ct, v):
-        return self.cx.mul_vec_rescale(self.ensure(ct, 1), self.chan(v))
+        return self.cx.mul_vec_rescale(self.ensure(ct, 1), self.tile(v))
+
+    def mask(self, ct, m):
+        return self.cx.mul_vec_rescale(self.ensure(ct, 1), m)
 
     def addv(self, ct, v):
-        """ct + v (channel layout) at ct's level and scale"""
+        """ct + v (per channel) at ct's level and scale"""
         cx = self.cx
-        pt = cx.MakeCKKSPackedPlaintext(np.tile(self.chan(v), cx.slots // (self.N * self.N)), level=ct.level,
-                                        scale=ct.scale)
-        return cx.EvalAdd(ct, pt)
+        return cx.EvalAdd(ct, cx.MakeCKKSPackedPlaintext(self.tile(v), level=ct.level, scale=ct.scale))
 
     def mulmul(self, a, b):
         """a * b, relinearised and rescaled; an operand without a level left is bootstrapped"""
@@ -453,30 +507,33 @@ class EncryptedRWKV7Block:
         """ct * c, rescaled onto the next level's canonical scale (a constant slot vector)"""
         return self.cx.mul_vec_rescale(self.ensure(ct, 1), np.full(8, float(c)))
 
-    # circuit pieces ---------------------------------------------------------------------------------
-    def cheb(self, name, x):
-        """the site polynomial of `name` on x in the channel layout: [lo, hi] mapped to [-1, 1],
-        the series, and the row-0 mask (the series' constant term lands in every slot, and the
-        layouts' rotations need zeros outside the vector)"""
+    def mv(self, name, ct):
+        return self.cx.matvec(self.plans[name], [self.ensure(ct, 2)])
+
+    # circuit pieces -----------------------------------------------------------------------------
+    def cheb(self, name, x, mask=None):
+        """the site polynomial of `name` on x: [lo, hi] mapped to [-1, 1], the series, and a mask
+        (the series' constant term lands in every slot; slots outside the conversations in use,
+        or past a LoRA width, must stay zero for the sums and bootstraps that follow)"""
         cx = self.cx
         lo, hi, c = self.fits[name]
         depth = 3 + int(np.ceil(np.log2(len(c))))
         x = self.ensure(x, depth)
         t = self.mulc(x, 2.0 / (hi - lo))
         t = cx.EvalAddConst(t, -(lo + hi) / (hi - lo))
-        return self.mulv(cx.EvalChebyshevSeries(t, c), np.ones(self.N))
+        return self.mask(cx.EvalChebyshevSeries(t, c), self.lane_mask if mask is None else mask)
 
-    def newton(self, name, v, mask):
-        """the site's 1/sqrt(v) by its linear seed and Newton steps (v: eps already added) in the
-        slots where ``mask`` (one N^2 period) is 1.  The other slots hold eps alone, where Newton
-        would climb towards 1/sqrt(eps) (40 for GroupNorm's) and a bootstrap of that range loses
-        precision in every slot: the 1.5 y term carries the mask, which sends them to zero."""
+    def newton(self, name, v):
+        """the site's 1/sqrt(v) by its linear seed and Newton steps (v: eps already added).  Slots
+        outside the conversations hold eps alone, where Newton would climb towards 1/sqrt(eps)
+        (40 for GroupNorm's) and a bootstrap of that range loses precision in every slot: the
+        1.5 y term carries the lane mask, which sends them to zero."""
         cx = self.cx
         a, b, iters = self.fits[name]
         v = self.ensure(v, 4)
         y = cx.EvalAddConst(self.mulc(v, b), a)
         mh = self.mulc(v, -0.5)
-        m15 = 1.5 * np.asarray(mask, dtype=np.float64)
+        m15 = 1.5 * self.lane_mask
         for _ in range(int(iters)):
             if self.left(y) < 3:
                 y = cx.EvalBootstrap(y)
@@ -488,116 +545,141 @@ class EncryptedRWKV7Block:
             y = self.add(cx.mul_vec_rescale(y, m15), u)
         return y
 
-    def spread_mean(self, x, scale):
-        """scale * sum_j x[j] in every channel slot (channel layout in, channel layout out)"""
-        wkv = self.wkv
-        s = wkv._doubling(x, 1)
-        s = self.cx.mul_vec_rescale(s, self.chan(np.r_[scale, np.zeros(self.N - 1)]))
-        return wkv._doubling(s, -1)
+    def group_sum(self, x, width, scale):
+        """scale * (the sum over each block of `width` slots) in every slot of the block"""
+        cx = self.cx
+        s = self.ensure(x, 1)
+        for t in range(int(np.log2(width))):
+            s = cx.EvalAdd(s, cx.EvalRotate(s, 1 << t))
+        s = cx.mul_vec_rescale(s, self.every(width, scale))
+        for t in range(int(np.log2(width))):
+            s = cx.EvalAdd(s, cx.EvalRotate(s, -(1 << t)))
+        return s
 
     def layer_norm(self, name, x, wgt, bias):
-        cx = self.cx
+        cx, C = self.cx, self.C
         x = self.ensure(x, 4)
-        xc = self.sub(x, self.spread_mean(x, 1.0 / self.N))
-        var = self.spread_mean(self.mulmul(xc, xc), 1.0 / self.N)
-        y = self.newton(name, cx.EvalAddConst(var, RSQRT_EPS["ln"]), self.chan(np.ones(self.N)))
+        xc = self.sub(x, self.group_sum(x, C, 1.0 / C))
+        var = self.group_sum(self.mulmul(xc, xc), C, 1.0 / C)
+        y = self.newton(name, cx.EvalAddConst(var, RSQRT_EPS["ln"]))
         xc = self.ensure(xc, 2)
         return self.addv(self.mulv(self.mulmul(xc, y), wgt), bias)
 
-    def col0_to_channel(self, z_col0, Wt):
-        """z[i] at (i, 0) (zeros elsewhere) -> (Wt z)[j] in the channel layout: spread along the rows,
-        times Wt[j][i] at (i, j), column sums (rotations by +N 2^t), row 0 kept"""
-        cx, wkv, N = self.cx, self.wkv, self.N
-        zs = wkv._doubling(z_col0, -1)
-        prod = cx.mul_vec_rescale(zs, np.asarray(Wt, dtype=np.float64).T.ravel())
-        cs = wkv._doubling(prod, N)
-        row0 = np.zeros(N * N)
-        row0[:N] = 1.0
-        return cx.mul_vec_rescale(cs, row0)
+    # between the contiguous layout and the state blocks -----------------------------------------
+    def _blocks_in(self, t):
+        return min(self.B, self.nb - t * self.B)
 
-    def channel_to_col0(self, x, M):
-        """x[c] in the channel layout -> (M^T x)[i] = sum_c M[c][i] x[c] at (i, 0)"""
-        wkv = self.wkv
-        xr = wkv.rep_rows(x)
-        return wkv.rowsum_col0(self.cx.mul_vec_rescale(xr, np.asarray(M, dtype=np.float64).T.ravel()))
+    def _bit_mask(self, t, b, packed_below):
+        """slots of the elements (u, j) of state ciphertext t whose block index u has bit b set,
+        at their position while the bits of u below `packed_below` are packed (u N) and the
+        others spread (u N^2)"""
+        N, z = self.N, np.zeros(self.cx.slots)
+        for u in range(self._blocks_in(t)):
+            if u >> b & 1:
+                lo = u & ((1 << packed_below) - 1)
+                base = (u - lo) * N * N + lo * N
+                z[base:base + N] = 1.0
+        return z
 
-    def head_sum_col0(self, z_col0):
-        """sum_i z[i] at every (i, 0): column sums, the (0, 0) mask, a spread down column 0"""
-        cx, wkv, N = self.cx, self.wkv, self.N
-        s = wkv._doubling(z_col0, N)
-        m = np.zeros(N * N)
-        m[0] = 1.0
-        s = cx.mul_vec_rescale(s, m)
-        return wkv._doubling(s, -N)
+    def to_rows(self, X, t):
+        """contiguous X -> row 0 of the blocks of state ciphertext t (head block t B + u's
+        channels at u N^2 + j)"""
+        cx, N, nbt = self.cx, self.N, self._blocks_in(t)
+        Y = self.rot(X, t * self.B * N)
+        m = np.zeros(cx.slots)
+        m[: nbt * N] = 1.0
+        Y = self.mask(Y, m)
+        for b in reversed(range(self.lgB)):
+            mb = self._bit_mask(t, b, b + 1)
+            mv = cx.mul_vec_rescale(Y, mb)
+            keep = cx.mul_vec_rescale(Y, 1.0 - mb)
+            Y = cx.EvalAdd(keep, cx.EvalRotate(mv, -(1 << b) * (N * N - N)))
+        return Y
+
+    def from_col0(self, y, t):
+        """y[i] at (i, 0) of the blocks of state ciphertext t -> the contiguous layout"""
+        cx, N, wkv, nbt = self.cx, self.N, self.wkv, self._blocks_in(t)
+        z = wkv._doubling(self.ensure(y, 2 + self.lgB), -1)          # (i, j) = y[i]
+        diag = np.zeros(cx.slots)
+        for u in range(nbt):
+            diag[u * N * N + np.arange(N) * (N + 1)] = 1.0
+        z = wkv._doubling(cx.mul_vec_rescale(z, diag), N)              # (0, j) = y[j]
+        row0 = np.zeros(cx.slots)
+        for u in range(nbt):
+            row0[u * N * N: u * N * N + N] = 1.0
+        z = cx.mul_vec_rescale(z, row0)
+        for b in range(self.lgB):
+            mb = self._bit_mask(t, b, b)
+            mv = cx.mul_vec_rescale(z, mb)
+            keep = cx.mul_vec_rescale(z, 1.0 - mb)
+            z = cx.EvalAdd(keep, cx.EvalRotate(mv, (1 << b) * (N * N - N)))
+        return self.rot(z, -t * self.B * N)
+
+    def to_column(self, x_rows):
+        """row 0 (x[j] at (0, j)) -> the column layout (x[i] at (i, j) for every j)"""
+        wkv, N = self.wkv, self.N
+        xr = wkv.rep_rows(x_rows)
+        eye = np.eye(N).ravel()
+        return wkv._doubling(wkv.rowsum_col0(self.cx.mul_vec_rescale(xr, eye)), -1)
 
     # the block ------------------------------------------------------------------------------------
-    def to_column(self, x):
-        """a channel-layout vector x[i] -> the column layout (x[i] at (i, j)): the identity
-        projection into column 0, then a spread along the rows"""
-        return self.wkv._doubling(self.channel_to_col0(x, np.eye(self.N)), -1)
-
     def step(self, x, v_first=None):
-        """(x, v_first) -> (the block's output, v_first): x in the channel layout, v_first the
-        first block's value in the column layout (None for block 0, which makes it).  x comes
-        at most at the top of the chain's user region (with a bootstrapping chain the scales of
-        the two regions are anchored separately, and products must not cross from one to the
-        other)."""
-        cx, w, a_, p, N, wkv = self.cx, self.w, self.a_, self.p, self.N, self.wkv
+        """(x, v_first) -> (the block's output, v_first), both contiguous; v_first is None for
+        block 0, which makes it.  x comes at most at the top of the chain's user region (with a
+        bootstrapping chain the scales of the two regions are anchored separately, and products
+        must not cross from one to the other)."""
+        cx, w, a_, p, N, C, wkv = self.cx, self.w, self.a_, self.p, self.N, self.C, self.wkv
         if self.state is None:   # the cold state, at the input's level
             zero = cx.Encrypt(cx.MakeCKKSPackedPlaintext(np.zeros(cx.slots), level=x.level))
-            self.state = [zero, cx.Copy(zero), cx.Copy(zero)]
+            self.state = [zero, cx.Copy(zero), [cx.Copy(zero) for _ in range(self.n_state)]]
         prev_att, prev_ffn, S = self.state
+        mid = lambda name: self.every(C, 1.0, self.mid[name])
         # ---- time mix
         x0 = self.ensure(self.layer_norm(p + "ln1", x, w[p + "ln1.weight"], w[p + "ln1.bias"]), 6)
         xx = self.sub(prev_att, x0)
-        mix = {m: self.add(x0, self.mulv(xx, w[a_ + m])) for m in ("x_r", "x_w", "x_k", "x_v", "x_a", "x_g")}
-        mix = {m: self.ensure(c, 6) for m, c in mix.items()}
-        r = cx.matvec(self.plans["r"], [mix["x_r"]])
-        k = cx.matvec(self.plans["k"], [mix["x_k"]])
-        v_col = wkv.value_column(mix["x_v"], w[a_ + "value.weight"])
+        mix = {m: self.ensure(self.add(x0, self.mulv(xx, w[a_ + m])), 6) for m in ("x_r", "x_w", "x_k", "x_v", "x_a", "x_g")}
+        r = self.mv("r", mix["x_r"])
+        k = self.mv("k", mix["x_k"])
+        v = self.mv("v", mix["x_v"])
         if self.layer == 0:
-            v_first = v_col
-        else:   # v += (v_first - v) sigmoid(v0 + (x_v V1) V2), the gate brought to the column layout
-            vg = self.addv(cx.matvec(self.plans["v2"], [cx.matvec(self.plans["v1"], [mix["x_v"]])]), w[a_ + "v0"])
-            gate = self.to_column(self.ensure(self.cheb(a_ + "v_sigmoid", vg), 4))
-            v_col = self.add(v_col, self.mulmul(self.sub(v_first, v_col), gate))
-        z = self.addv(cx.matvec(self.plans["w2"], [self.ensure(self.cheb(a_ + "w_tanh",
-                                cx.matvec(self.plans["w1"], [mix["x_w"]])), 2)]), w[a_ + "w0"])
-        dec = self.cheb(a_ + "decay", z)
-        av = self.addv(cx.matvec(self.plans["a2"], [cx.matvec(self.plans["a1"], [mix["x_a"]])]), w[a_ + "a0"])
-        a = self.cheb(a_ + "a_sigmoid", av)
-        gs = self.cheb(a_ + "g_sigmoid", cx.matvec(self.plans["g1"], [mix["x_g"]]))
-        g_col0 = self.channel_to_col0(self.ensure(gs, 4), self.g2)
-        kk = self.mulv(k, w[a_ + "k_k"])
-        kn = self.newton(a_ + "kk_rsqrt", self.spread_mean(self.mulmul(kk, kk), 1.0), self.chan(np.ones(N)))
+            v_first = v
+        else:   # v += (v_first - v) sigmoid(v0 + (x_v V1) V2)
+            vm = self.cheb(a_ + "v_sigmoid", self.addv(self.mv("v2", self.mv("v1", mix["x_v"])), w[a_ + "v0"]))
+            v = self.add(v, self.mulmul(self.sub(v_first, v), vm))
+        wt = self.cheb(a_ + "w_tanh", self.mv("w1", mix["x_w"]), mid("w1"))
+        dec = self.cheb(a_ + "decay", self.addv(self.mv("w2", wt), w[a_ + "w0"]))
+        a = self.cheb(a_ + "a_sigmoid", self.addv(self.mv("a2", self.mv("a1", mix["x_a"])), w[a_ + "a0"]))
+        gs = self.cheb(a_ + "g_sigmoid", self.mv("g1", mix["x_g"]), mid("g1"))
+        g = self.mv("g2", gs)
+        kk = self.mulv(k, w[a_ + "k_k"].ravel())
+        kn = self.newton(a_ + "kk_rsqrt", self.group_sum(self.mulmul(kk, kk), N, 1.0))
         kk = self.mulmul(self.ensure(kk, 2), kn)
         a = self.ensure(a, 4)
-        kmod = self.mulmul(k, self.addv(self.mulv(self.addv(a, -np.ones(N)), w[a_ + "k_a"]), np.ones(N)))
+        kmod = self.mulmul(k, self.addv(self.mulv(self.addv(a, -np.ones(C)), w[a_ + "k_a"].ravel()), np.ones(C)))
         b = self.mulmul(kk, a)
         na = self.mulc(kk, -1.0)
-        ins = [self.ensure(c, 8) for c in (dec, na, b, kmod, r, v_col)]
-        S = self.ensure(S, 8)
-        S, y = wkv.step(S, ins[0], ins[1], ins[2], ins[3], ins[4], ins[5])
-        # GroupNorm over the head (y[i] at (i, 0))
+        # ---- the wkv state, block by block
+        ins = [self.ensure(c, 9 + self.lgB) for c in (dec, na, b, kmod, r)]
+        vin = self.ensure(v, 11 + self.lgB)
+        S_new, y = [], None
+        for t in range(self.n_state):
+            rows = [self.to_rows(c, t) for c in ins]
+            vcol = self.to_column(self.to_rows(vin, t))
+            St, yt = wkv.step(self.ensure(S[t], 8), *rows, vcol)
+            S_new.append(St)
+            yt = self.from_col0(yt, t)
+            y = yt if y is None else self.add(y, yt)
+        # GroupNorm per head
         y = self.ensure(y, 6)
-        yc = self.sub(y, self.mulc(self.head_sum_col0(y), 1.0 / N))
-        var = self.mulc(self.head_sum_col0(self.mulmul(yc, yc)), 1.0 / N)
-        gn = self.newton(a_ + "gn_rsqrt", cx.EvalAddConst(var, RSQRT_EPS["gn"]), wkv.mask_j0)
+        yc = self.sub(y, self.group_sum(y, N, 1.0 / N))
+        var = self.group_sum(self.mulmul(yc, yc), N, 1.0 / N)
+        gn = self.newton(a_ + "gn_rsqrt", cx.EvalAddConst(var, RSQRT_EPS["gn"]))
         yc = self.ensure(yc, 3)
-        col0 = lambda v: np.concatenate([[v[i]] + [0.0] * (N - 1) for i in range(N)])
-        y = self.mulmul(yc, gn)
-        y = cx.mul_vec_rescale(y, col0(w[a_ + "ln_x.weight"]))
-        ypt = cx.MakeCKKSPackedPlaintext(np.tile(col0(w[a_ + "ln_x.bias"]), cx.slots // (N * N)), level=y.level,
-                                         scale=y.scale)
-        y = cx.EvalAdd(y, ypt)
-        # bonus ((r k r_k) summed over the head) v, in column 0
+        y = self.addv(self.mulv(self.mulmul(yc, gn), w[a_ + "ln_x.weight"]), w[a_ + "ln_x.bias"])
+        # bonus ((r k r_k) summed over the head) v
         rk = self.mulv(self.mulmul(self.ensure(r, 3), self.ensure(kmod, 3)), w[a_ + "r_k"].ravel())
-        s = wkv.rowsum_col0(wkv.rep_rows(rk))   # sum_j rk[j] at every (i, 0)
-        vc0 = cx.mul_vec_rescale(self.ensure(v_col, 3), wkv.mask_j0)
-        y = self.add(y, self.mulmul(self.ensure(s, 2), vc0))
-        y = self.ensure(y, 4)
-        yg = self.mulmul(y, self.ensure(g_col0, 2))
-        att = self.col0_to_channel(self.ensure(yg, 3), w[a_ + "output.weight"])
+        y = self.add(y, self.mulmul(self.ensure(self.group_sum(rk, N, 1.0), 2), self.ensure(v, 2)))
+        att = self.mv("o", self.mulmul(self.ensure(y, 3), self.ensure(g, 2)))
         x1 = self.add(x, att)
         # ---- channel mix
         f = p + "ffn."
@@ -609,21 +691,33 @@ class EncryptedRWKV7Block:
         for h in hs:
             if h.level < lv:
                 cx.align(h, lv)
-        out = cx.matvec(self.ffn_v, hs)
-        x2 = self.add(x1, out)
-        self.state = [x0, xf, S]
+        x2 = self.add(x1, cx.matvec(self.ffn_v, hs))
+        self.state = [x0, xf, S_new]
         return x2, v_first
 
 
 class EncryptedRWKV7:
-    """Every block of a one-head RWKV-7 on the engine (EncryptedRWKV7Block each), the value of
-    block 0 carried to the others.  The client applies block 0's input norm before encrypting
-    (the reference folds ln0 into the embedding table) and the output norm and head after
-    decrypting (``client_logits``), as the reference's server does not evaluate them."""
+    """Every block of an RWKV-7 on the engine (EncryptedRWKV7Block each) for ``convs``
+    conversations in the contiguous layout, the value of block 0 carried to the others.  The
+    client applies block 0's input norm before encrypting (the reference folds ln0 into the
+    embedding table) and the output norm and head after decrypting (``client_logits``), as the
+    reference's server does not evaluate them."""
 
-    def __init__(self, cx, sh: RWKV7Shape, w, fits, b1=8):
+    def __init__(self, cx, sh: RWKV7Shape, w, fits, convs=1, b1=8):
         self.cx, self.sh, self.w, self.fits = cx, sh, w, fits
-        self.blocks = [EncryptedRWKV7Block(cx, sh, w, i, fits, b1) for i in range(sh.n_layer)]
+        self.blocks = [EncryptedRWKV7Block(cx, sh, w, i, fits, convs, b1) for i in range(sh.n_layer)]
+
+    @staticmethod
+    def keygen(cx, sh: RWKV7Shape, b1=8):
+        """the rotation and matvec keys the blocks use"""
+        cx.EvalRotateKeyGen(EncryptedRWKV7Block.rotations(sh, cx.slots))
+        cx.matvec_keygen(sh.n_embd, b1)
+
+    def pack(self, x):
+        return self.blocks[0].pack(x)
+
+    def unpack(self, z):
+        return self.blocks[0].unpack(z)
 
     def step(self, x_ct):
         v_first = None
@@ -631,13 +725,12 @@ class EncryptedRWKV7:
             x_ct, v_first = b.step(x_ct, v_first)
         return x_ct
 
-    def client_input(self, tokens, sites=None, lanes_per_ct=1):
-        """the embedding rows through block 0's input norm, in the channel layout"""
+    def client_input(self, tokens, sites=None):
+        """the embedding rows through block 0's input norm, (convs, C)"""
         sites = sites or Sites(self.fits)
         w = self.w
-        x = _ln(sites, "blocks.0.ln0", w["emb.weight"][np.asarray(tokens)], w["blocks.0.ln0.weight"],
-                w["blocks.0.ln0.bias"])
-        return x
+        return _ln(sites, "blocks.0.ln0", w["emb.weight"][np.asarray(tokens)], w["blocks.0.ln0.weight"],
+                   w["blocks.0.ln0.bias"])
 
     def client_logits(self, hidden, sites=None):
         sites = sites or Sites(self.fits)

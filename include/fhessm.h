@@ -157,7 +157,11 @@ int fhe_ct_copy(fhe_ctx* cx, const fhe_ct* a, fhe_ct** out);
 int fhe_mul_ct_pt(fhe_ctx* cx, const fhe_ct* a, const fhe_pt* pt, fhe_ct** out);
 /* EvalMult(ct, ct) with relinearisation, no rescale (rmsnorm x^2 :3520, polyGate3 :4627) */
 int fhe_mul_ct_ct_relin(fhe_ctx* cx, const fhe_ct* a, const fhe_ct* b, fhe_ct** out);
-/* EvalAdd / EvalSub at equal level and scale (addAligned :2692-2743 aligns first) */
+/* EvalAdd / EvalSub with the levels and scales reconciled, as OpenFHE's FLEXIBLEAUTO EvalAdd
+   does for addAligned (:2692-2743, the add at :2743): the operand with more limbs is aligned down
+   to the other's level and scale; at equal levels an integer scale ratio is fixed by an exact
+   integer product and any other ratio by aligning both one level down.  Operands already at one
+   level and scale are added as they are. */
 int fhe_add(fhe_ctx* cx, const fhe_ct* a, const fhe_ct* b, fhe_ct** out);
 int fhe_sub(fhe_ctx* cx, const fhe_ct* a, const fhe_ct* b, fhe_ct** out);
 /* EvalAdd(ct, pt) (addPtV :2756-2759) */

@@ -58,13 +58,13 @@ def test_wkv_state_update_matches_float64():
 
 def test_rwkv7_block_matches_polynomial_model():
     """One RWKV-7 block (layer 0: time mix with the wkv state, channel mix) on the engine for one
-    head of 64 channels, two tokens, against the float64 block with the same polynomial sites and
+    head of 64 channels (contiguous layout, one state ciphertext), two tokens, against the float64 block with the same polynomial sites and
     Newton seeds.  N = 2^13 with the bootstrapping chain (q0 60 bits, 19 x 45-bit user primes,
     14 x 58-bit bootstrap primes, K = 4): a correctness test of the circuit, not a secure
     parameter set at this ring size."""
     import fhessm
-    from fhessm.rwkv7 import (EncryptedRWKV7Block, RWKV7Shape, Sites, _ln, block_step, fit_sites, new_state,
-                              synthetic_weights)
+    from fhessm.rwkv7 import (EncryptedRWKV7, EncryptedRWKV7Block, RWKV7Shape, Sites, _ln, block_step, fit_sites,
+                              new_state, synthetic_weights)
     sh = RWKV7Shape(n_layer=1, n_embd=64, head_size=64, d_decay=16, d_aaa=16, d_mv=8, d_gate=32, dim_ffn=256,
                     vocab_size=256)
     w = synthetic_weights(sh, seed=9)
@@ -73,8 +73,7 @@ def test_rwkv7_block_matches_polynomial_model():
     cx = fhessm.CryptoContext(logN=13, L=34, K=4, alpha=4, hw=64, boot_primes=14)
     try:
         cx.KeyGen(seed=23)
-        cx.EvalRotateKeyGen(EncryptedRWKV7Block.rotations(64))
-        cx.matvec_keygen(64, 8)
+        EncryptedRWKV7.keygen(cx, sh)
         cx.EvalBootstrapSetup(24.0, 31, 4)
         blk = EncryptedRWKV7Block(cx, sh, w, 0, fits)
         st = new_state(sh, 1)
@@ -106,8 +105,7 @@ def test_rwkv7_two_layers_logits_match_polynomial_model():
     cx = fhessm.CryptoContext(logN=13, L=34, K=4, alpha=4, hw=64, boot_primes=14)
     try:
         cx.KeyGen(seed=24)
-        cx.EvalRotateKeyGen(fhessm.rwkv7.EncryptedRWKV7Block.rotations(64))
-        cx.matvec_keygen(64, 8)
+        EncryptedRWKV7.keygen(cx, sh)
         cx.EvalBootstrapSetup(24.0, 31, 4)
         model = EncryptedRWKV7(cx, sh, w, fits)
         st = new_state(sh, 1)
@@ -121,5 +119,39 @@ def test_rwkv7_two_layers_logits_match_polynomial_model():
             err = np.abs(lg - ref).max() / np.abs(ref).max()
             print(f"token {t}: logits rel err {err:.2e}, top-1 {lg.argmax() == ref.argmax()}")
             assert err < 1e-3 and lg.argmax() == ref.argmax()
+    finally:
+        cx.close()
+
+
+def test_rwkv7_multi_head_conversations_logits():
+    """Two heads of 64 (C = 128), two blocks, two conversations at N = 2^14: two head blocks per
+    state ciphertext (the bit-step moves between the contiguous layout and the state blocks run),
+    two state ciphertexts per layer; logits of both conversations over three tokens."""
+    import fhessm
+    from fhessm.rwkv7 import EncryptedRWKV7, RWKV7Shape, Sites, fit_sites, new_state, step, synthetic_weights
+    sh = RWKV7Shape(n_layer=2, n_embd=128, head_size=64, d_decay=16, d_aaa=16, d_mv=8, d_gate=32, dim_ffn=256,
+                    vocab_size=256)
+    w = synthetic_weights(sh, seed=11)
+    rng = np.random.default_rng(16)
+    seqs = [rng.integers(0, sh.vocab_size, 2) for _ in range(3)]
+    cal = [np.concatenate([s, rng.integers(0, sh.vocab_size, 30)]) for s in seqs]
+    fits = fit_sites(sh, w, cal, degree=15)
+    sites = Sites(fits)
+    cx = fhessm.CryptoContext(logN=14, L=34, K=4, alpha=4, hw=64, boot_primes=14)
+    try:
+        cx.KeyGen(seed=25)
+        EncryptedRWKV7.keygen(cx, sh)
+        cx.EvalBootstrapSetup(24.0, 31, 4)
+        model = EncryptedRWKV7(cx, sh, w, fits, convs=2)
+        assert model.blocks[0].B == 2 and model.blocks[0].n_state == 2
+        st = new_state(sh, 2)
+        for t, toks in enumerate(seqs):
+            ref = step(sh, w, toks, st, sites)
+            out = model.step(cx.Encrypt(cx.MakeCKKSPackedPlaintext(model.pack(model.client_input(toks)), level=14)))
+            lg = model.client_logits(model.unpack(cx.Decrypt(out)))
+            err = np.abs(lg - ref).max() / np.abs(ref).max()
+            top1 = (lg.argmax(-1) == ref.argmax(-1)).all()
+            print(f"token {t}: logits rel err {err:.2e}, top-1 {top1}")
+            assert err < 1e-3 and top1
     finally:
         cx.close()

@@ -1,0 +1,63 @@
+"""The encrypted RWKV-7 circuit (fhessm.rwkv7.EncryptedRWKV7) on the plaintext slot simulator
+(CPU): several heads, several conversations and several head blocks per state ciphertext, so
+that every move between the contiguous channel layout and the wkv state blocks (the rotation,
+the bit steps, the per-block transpose of the readout) and the level bookkeeping run.  With
+exact slot arithmetic the circuit must reproduce the float64 model with the same polynomial
+sites to round-off."""
+import numpy as np
+import pytest
+
+from sim_engine import SimContext
+
+
+def run(shape, slots, convs, tokens, seed=3):
+    from fhessm.rwkv7 import EncryptedRWKV7, RWKV7Shape, Sites, fit_sites, new_state, step, synthetic_weights
+    sh = RWKV7Shape(**shape)
+    w = synthetic_weights(sh, seed=seed)
+    rng = np.random.default_rng(seed + 1)
+    seqs = [rng.integers(0, sh.vocab_size, convs) for _ in range(tokens)]
+    fits = fit_sites(sh, w, seqs, degree=7)   # sites fitted on the run itself: every input inside
+    cx = SimContext(slots)
+    EncryptedRWKV7.keygen(cx, sh)
+    model = EncryptedRWKV7(cx, sh, w, fits, convs=convs)
+    st = new_state(sh, convs)
+    sites = Sites(fits)
+    errs = []
+    for toks in seqs:
+        ref = step(sh, w, toks, st, sites)
+        x = model.client_input(toks)
+        out = model.step(cx.Encrypt(cx.MakeCKKSPackedPlaintext(model.pack(x), level=14)))
+        lg = model.client_logits(model.unpack(cx.Decrypt(out)))
+        errs.append(np.abs(lg - ref).max() / np.abs(ref).max())
+        # nothing outside the conversations in use
+        assert np.abs(cx.Decrypt(out)[convs * sh.n_embd:]).max() < 1e-9
+    return errs, model, cx
+
+
+@pytest.mark.parametrize("convs", [1, 3])
+def test_multi_head_blocks_per_state_ciphertext(convs):
+    """head size 16 (N^2 = 256), 4 heads, 1024 slots: 4 head blocks per state ciphertext"""
+    shape = dict(n_layer=2, n_embd=64, head_size=16, d_decay=8, d_aaa=8, d_mv=4, d_gate=16, dim_ffn=128,
+                 vocab_size=64)
+    errs, model, cx = run(shape, 1024, convs, 3)
+    blk = model.blocks[0]
+    assert blk.B == 4 and blk.n_state == -(-convs * 4 // 4)
+    assert max(errs) < 1e-9, errs
+
+
+def test_one_block_per_state_ciphertext():
+    """head size 16 at 256 slots: one head block per state ciphertext, 2 heads x 2 conversations"""
+    shape = dict(n_layer=1, n_embd=32, head_size=16, d_decay=8, d_aaa=8, d_mv=4, d_gate=16, dim_ffn=64,
+                 vocab_size=64)
+    errs, model, cx = run(shape, 256, 2, 2)
+    assert model.blocks[0].B == 1 and model.blocks[0].n_state == 4
+    assert max(errs) < 1e-9, errs
+
+
+def test_partial_last_state_ciphertext():
+    """2 heads x 3 conversations at 4 blocks per state ciphertext: the second one half used"""
+    shape = dict(n_layer=1, n_embd=32, head_size=16, d_decay=8, d_aaa=8, d_mv=4, d_gate=16, dim_ffn=64,
+                 vocab_size=64)
+    errs, model, cx = run(shape, 1024, 3, 2)
+    assert model.blocks[0].B == 4 and model.blocks[0].n_state == 2
+    assert max(errs) < 1e-9, errs
