@@ -258,105 +258,102 @@ def fit_sites(sh: RWKV7Shape, w, token_batches, degree=15, margin=0.1, tol=1e-4,
 
 # ----------------------------------------------------------------- the encrypted wkv state ----
 class EncryptedWkv:
-    """The x070 state update of one head on the engine, for the conversations packed in one
-    ciphertext (slots / N^2 of them).  Layouts inside conversation c's block of N^2 slots:
+    """The x070 state update on the engine for ``blocks`` head blocks (conversation l, head h:
+    block b = l H + h), every vector in the contiguous channel layout (block b's channel j at
+    slot b N + j).  The state is N ciphertexts, one per row index: row ciphertext i holds row i of
+    every block's N x N matrix, S_b[i][j] at slot b N + j, so that the state update needs no
+    change of layout:
 
-      * state        S[i][j] at c N^2 + i N + j;
-      * channel      a vector v[j] at c N^2 + j (row 0), zeros elsewhere;
-      * column       v[i] at c N^2 + i N + j for every j (the value side of v k^T).
-
-    Moves between them are rotations and one mask, never a general permutation:
-      * replicate a channel vector down the rows: N -> N rows by log2 N doublings (rotations
-        by -N 2^t);
-      * row sums: log2 N rotations by +2^t leave sum_j M[i][j] at (i, 0); a mask keeps only
-        that column (one level) and log2 N rotations by -2^t spread it along the row;
-      * the value projection v = W x lands in the column layout directly: the replicated x
-        times the plaintext W[i][c] at (i, c), row-summed and spread.
+      * S diag(w): a slot product of every row ciphertext with w;
+      * (S a) b^T: row i's per-block sum of S_i (.) a (log2 N doublings by +1, a mask at the
+        block's first slot, log2 N doublings by -1 spread it over the block) times b;
+      * v k^T: v[i] of every block over the block (v rotated by i, all i from one hoisted
+        rotation, the first-slot mask, the spread) times k;
+      * the readout y[i] = sum_j S_i[j] r[j]: row i's per-block sum at the block's first slot,
+        moved to slot i of the block; the N moves are one batched rotate-and-sum.
 
     One step (wkv7_recurrence, rwkv7_model.py:290-296, with a = -kk and b = kk a):
-        S <- S (.) w_rep + spread(rowsum(S (.) a_rep)) (.) b_rep + v_col (.) k_rep,
-        y[i] = rowsum(S (.) r_rep) at (i, 0).
+        S_i <- S_i (.) w + spread(sum(S_i (.) a)) (.) b + bcast_i(v) (.) k,   y = sum_i move_i(sum(S_i (.) r)).
     Every product is a relinearised, rescaled ciphertext product (mul_rescale), every mask a
-    plaintext product; levels are matched by align before additions."""
+    plaintext product; the engine's EvalAdd reconciles levels and scales."""
 
-    def __init__(self, cx, N=64):
-        self.cx, self.N = cx, N
-        self.B = N * N
-        self.lanes = cx.slots // self.B
-        if self.lanes < 1 or cx.slots % self.B:
-            raise ValueError("a conversation's N^2 state must divide the slots")
+    def __init__(self, cx, N=64, blocks=1):
+        if cx.slots % N or blocks * N > cx.slots:
+            raise ValueError("the contiguous layout needs N | slots and blocks * N <= slots")
+        self.cx, self.N, self.blocks = cx, N, blocks
         self.lg = int(np.log2(N))
-        m = np.zeros(self.B)
-        m[::N] = 1.0
-        self.mask_j0 = m
+        first = np.zeros(cx.slots)
+        first[: blocks * N: N] = 1.0
+        self.first = first          # the first slot of every block in use
 
     @staticmethod
     def rotations(N=64):
-        r = []
+        r = set()
         for t in range(int(np.log2(N))):
-            r += [1 << t, -(1 << t), N << t, -(N << t)]
-        return r
+            r |= {1 << t, -(1 << t)}
+        for i in range(1, N):
+            r |= {i, -i}
+        return sorted(r)
 
     # layout helpers --------------------------------------------------------------------------
     def pack_state(self, S):
-        """S (lanes, N, N) -> slot vector"""
-        z = np.zeros(self.cx.slots)
-        z[: self.lanes * self.B] = np.asarray(S).reshape(self.lanes, -1).ravel()
-        return z
+        """S (blocks, N, N) -> N slot vectors (row i of every block)"""
+        S = np.asarray(S, dtype=np.float64)
+        out = []
+        for i in range(self.N):
+            z = np.zeros(self.cx.slots)
+            z[: self.blocks * self.N] = S[:, i, :].ravel()
+            out.append(z)
+        return out
 
     def pack_channel(self, v):
+        """v (blocks, N) -> slot vector"""
         z = np.zeros(self.cx.slots)
-        for c in range(self.lanes):
-            z[c * self.B: c * self.B + self.N] = v[c]
+        z[: self.blocks * self.N] = np.asarray(v, dtype=np.float64).ravel()
         return z
 
-    def unpack_state(self, z):
-        return np.asarray(z[: self.lanes * self.B]).real.reshape(self.lanes, self.N, self.N)
+    def unpack_channel(self, z):
+        return np.asarray(z).real[: self.blocks * self.N].reshape(self.blocks, self.N)
 
-    def unpack_col0(self, z):
-        """the values at (i, 0) of every conversation: (lanes, N)"""
-        return self.unpack_state(z)[:, :, 0]
+    def unpack_state(self, rows):
+        """N decrypted row vectors -> (blocks, N, N)"""
+        return np.stack([self.unpack_channel(z) for z in rows], axis=1)
 
-    def _add(self, a, b):
-        """a + b; the engine's EvalAdd reconciles levels and scales"""
-        return self.cx.EvalAdd(a, b)
-
+    # moves -------------------------------------------------------------------------------------
     def _doubling(self, ct, step):
         cx = self.cx
         for t in range(self.lg):
             ct = cx.EvalAdd(ct, cx.EvalRotate(ct, step << t))
         return ct
 
-    def rep_rows(self, ct):
-        return self._doubling(ct, -self.N)
-
-    def spread_rowsum(self, ct):
-        """M -> (sum_j M[i][j]) at every (i, j): row sums, the column-0 mask, the spread"""
-        s = self._doubling(ct, 1)
-        s = self.cx.mul_vec_rescale(s, self.mask_j0)
+    def block_sum(self, ct, scale=1.0):
+        """scale * sum_j ct[b N + j] in every slot of block b (one level)"""
+        s = self.cx.mul_vec_rescale(self._doubling(ct, 1), scale * self.first)
         return self._doubling(s, -1)
 
-    def rowsum_col0(self, ct):
-        """M -> sum_j M[i][j] at (i, 0), masked (zeros elsewhere)"""
-        return self.cx.mul_vec_rescale(self._doubling(ct, 1), self.mask_j0)
+    def bcast(self, v_rot_i):
+        """v[i] of every block over the block, from v rotated left by i (one level)"""
+        return self._doubling(self.cx.mul_vec_rescale(v_rot_i, self.first), -1)
 
-    def value_column(self, x_ct, Wv):
-        """v = Wv x in the column layout from x in the channel layout (Wv: (N, N), v[i] =
-        sum_c Wv[i][c] x[c])"""
-        xr = self.rep_rows(x_ct)
-        return self.spread_rowsum(self.cx.mul_vec_rescale(xr, np.asarray(Wv, dtype=np.float64).ravel()))
-
-    def step(self, S_ct, w_ct, a_ct, b_ct, k_ct, r_ct, v_col):
-        """(S', y): the channel-layout inputs w, a, b, k, r; the column-layout value v_col"""
-        cx = self.cx
-        wr, ar, br, kr, rr = (self.rep_rows(c) for c in (w_ct, a_ct, b_ct, k_ct, r_ct))
-        sw = cx.mul_rescale(S_ct, wr)
-        sa = self.spread_rowsum(cx.mul_rescale(S_ct, ar))
-        sab = cx.mul_rescale(sa, br)
-        vk = cx.mul_rescale(v_col, kr)
-        S2 = self._add(self._add(sw, sab), vk)
-        y = self.rowsum_col0(cx.mul_rescale(S2, rr))
-        return S2, y
+    def step(self, S, w, a, b, k, r, v):
+        """(S', y) for the row ciphertexts S and the channel-layout inputs (y in the channel
+        layout)"""
+        cx, N = self.cx, self.N
+        vrot = [v] + cx.EvalFastRotation(v, list(range(1, N)))
+        S2, heads = [], []
+        for i in range(N):
+            sw = cx.mul_rescale(S[i], w)
+            sab = cx.mul_rescale(self.block_sum(cx.mul_rescale(S[i], a)), b)
+            vk = cx.mul_rescale(self.bcast(vrot[i]), k)
+            Si = cx.EvalAdd(cx.EvalAdd(sw, sab), vk)
+            S2.append(Si)
+            heads.append(cx.mul_vec_rescale(self._doubling(cx.mul_rescale(Si, r), 1), self.first))
+        lv = max(h.level for h in heads)   # the rotate-and-sum's inputs share one level and scale
+        for h in heads:
+            if h.level < lv:
+                cx.align(h, lv)
+        y = cx.EvalRotateSum(heads[1:], [-i for i in range(1, N)])
+        return S2, cx.EvalAdd(y, heads[0])
 
 
 # ------------------------------------------------------------------ the encrypted RWKV-7 block ----
@@ -364,23 +361,14 @@ class EncryptedRWKV7Block:
     """One RWKV-7 block (time mix with the wkv state, channel mix) on the engine for ``convs``
     conversations of C = H N channels (H heads of N), with the circuit's sites (``fits``:
     Chebyshev series, Newton 1/sqrt), against which ``block_step(..., Sites(fits))`` is the
-    float64 mirror.  Two layouts:
-
-      * contiguous: conversation l's channel c at slot l C + c.  This is the engine's matvec
-        layout with D = C, so every linear layer is one BSGS matvec (LoRA matrices padded to
-        C x C); a per-head sum (kk normalisation, GroupNorm, the bonus) is log2 N doublings by
-        +1, a mask at the head's first slot and log2 N doublings by -1, a per-conversation sum
-        (LayerNorm) the same over C;
-      * the wkv state: head block b = l H + h; B = slots / N^2 blocks per state ciphertext, block
-        u of state ciphertext t holds head block t B + u in EncryptedWkv's layouts.
-
-    Into the state blocks (``to_rows``): a rotation by t B N brings blocks t B .. t B + B - 1 to
-    slots u N + j, a mask keeps them, and log2 B bit steps move the blocks whose index has bit
-    b set by 2^b (N^2 - N) (high bit first), one mask level each.  Back (``from_col0``): the
-    readout y[i] at (i, 0) of each block is transposed to row 0 inside the block (spread along
-    the row, the diagonal mask, column sums, the row-0 mask), the bit steps run in reverse and a
-    rotation by -t B N puts the blocks in place.  A ciphertext is bootstrapped when it has fewer
-    levels left than the next operation needs."""
+    float64 mirror.  Every vector is in the contiguous layout: conversation l's channel c at slot
+    l C + c (head block b = l H + h at slots b N .. b N + N - 1).  This is the engine's matvec
+    layout with D = C, so every linear layer is one BSGS matvec (LoRA matrices padded to C x C);
+    a per-head sum (kk normalisation, GroupNorm, the bonus) is log2 N doublings by +1, a mask at
+    the head's first slot and log2 N doublings by -1, a per-conversation sum (LayerNorm) the same
+    over C.  The wkv state is EncryptedWkv's N row ciphertexts in the same layout, so nothing
+    changes layout inside the block.  A ciphertext is bootstrapped when it has fewer levels left
+    than the next operation needs (the state rows together, in one batched bootstrap)."""
 
     def __init__(self, cx, sh: RWKV7Shape, w, layer, fits, convs=1, b1=8):
         C, N = sh.n_embd, sh.head_size
@@ -388,12 +376,7 @@ class EncryptedRWKV7Block:
             raise ValueError("the contiguous layout needs C | slots and convs * C <= slots")
         self.cx, self.sh, self.w, self.layer, self.fits = cx, sh, w, layer, fits
         self.C, self.N, self.H, self.convs = C, N, sh.n_head, convs
-        self.wkv = EncryptedWkv(cx, N)
-        self.B = self.wkv.lanes                       # head blocks per state ciphertext
-        self.nb = convs * self.H                      # head blocks in use
-        self.n_state = -(-self.nb // self.B)
-        self.lgB = int(np.log2(self.B))
-        self.keys = set(self.rotations(sh, cx.slots))
+        self.wkv = EncryptedWkv(cx, N, convs * self.H)
         self.lane_mask = np.zeros(cx.slots)
         self.lane_mask[: convs * C] = 1.0
         p = f"blocks.{layer}."
@@ -419,21 +402,14 @@ class EncryptedRWKV7Block:
         kf, vf = w[p + "ffn.key.weight"], w[p + "ffn.value.weight"]
         self.ffn_k = [plan(kf[c * C:(c + 1) * C]) for c in range(F // C)]
         self.ffn_v = plan(vf)                          # (C, F): column chunk s acts on input s
-        self.state = None                              # (prev_att, prev_ffn, [S_t]) ciphertexts
+        self.state = None                              # (prev_att, prev_ffn, [state rows]) ciphertexts
 
     @staticmethod
-    def rotations(sh: RWKV7Shape, slots):
-        """the rotation steps the block uses at this slot count"""
-        N, C = sh.head_size, sh.n_embd
-        r = set(EncryptedWkv.rotations(N))
-        for t in range(int(np.log2(C))):
+    def rotations(sh: RWKV7Shape, slots=None):
+        """the rotation steps the block uses"""
+        r = set(EncryptedWkv.rotations(sh.head_size))
+        for t in range(int(np.log2(sh.n_embd))):
             r |= {1 << t, -(1 << t)}
-        for k in range(int(np.log2(slots)) - 1):
-            r |= {1 << k, -(1 << k)}
-        r.add(slots // 2)
-        for b in range(int(np.log2(slots // (N * N)))):
-            d = (1 << b) * (N * N - N)
-            r |= {d, -d}
         return sorted(r)
 
     # packing -------------------------------------------------------------------------------------
@@ -469,24 +445,10 @@ class EncryptedRWKV7Block:
         return ct
 
     def add(self, a, b):
-        return self.wkv._add(a, b)
+        return self.cx.EvalAdd(a, b)
 
     def sub(self, a, b):
         return self.cx.EvalSub(a, b)
-
-    def rot(self, ct, k):
-        """left rotation by k (slot s receives slot s + k), one keyed step or its binary digits"""
-        slots = self.cx.slots
-        k %= slots
-        if k == 0:
-            return ct
-        for kk in (k, k - slots):
-            if kk in self.keys:
-                return self.cx.EvalRotate(ct, kk)
-        for b in range(int(np.log2(slots))):
-            if k >> b & 1:
-                ct = self.cx.EvalRotate(ct, 1 << b)
-        return ct
 
     def mulv(self, ct, v):
         return self.cx.mul_vec_rescale(self.ensure(ct, 1), self.tile(v))
@@ -565,62 +527,15 @@ class EncryptedRWKV7Block:
         xc = self.ensure(xc, 2)
         return self.addv(self.mulv(self.mulmul(xc, y), wgt), bias)
 
-    # between the contiguous layout and the state blocks -----------------------------------------
-    def _blocks_in(self, t):
-        return min(self.B, self.nb - t * self.B)
-
-    def _bit_mask(self, t, b, packed_below):
-        """slots of the elements (u, j) of state ciphertext t whose block index u has bit b set,
-        at their position while the bits of u below `packed_below` are packed (u N) and the
-        others spread (u N^2)"""
-        N, z = self.N, np.zeros(self.cx.slots)
-        for u in range(self._blocks_in(t)):
-            if u >> b & 1:
-                lo = u & ((1 << packed_below) - 1)
-                base = (u - lo) * N * N + lo * N
-                z[base:base + N] = 1.0
-        return z
-
-    def to_rows(self, X, t):
-        """contiguous X -> row 0 of the blocks of state ciphertext t (head block t B + u's
-        channels at u N^2 + j)"""
-        cx, N, nbt = self.cx, self.N, self._blocks_in(t)
-        Y = self.rot(X, t * self.B * N)
-        m = np.zeros(cx.slots)
-        m[: nbt * N] = 1.0
-        Y = self.mask(Y, m)
-        for b in reversed(range(self.lgB)):
-            mb = self._bit_mask(t, b, b + 1)
-            mv = cx.mul_vec_rescale(Y, mb)
-            keep = cx.mul_vec_rescale(Y, 1.0 - mb)
-            Y = cx.EvalAdd(keep, cx.EvalRotate(mv, -(1 << b) * (N * N - N)))
-        return Y
-
-    def from_col0(self, y, t):
-        """y[i] at (i, 0) of the blocks of state ciphertext t -> the contiguous layout"""
-        cx, N, wkv, nbt = self.cx, self.N, self.wkv, self._blocks_in(t)
-        z = wkv._doubling(self.ensure(y, 2 + self.lgB), -1)          # (i, j) = y[i]
-        diag = np.zeros(cx.slots)
-        for u in range(nbt):
-            diag[u * N * N + np.arange(N) * (N + 1)] = 1.0
-        z = wkv._doubling(cx.mul_vec_rescale(z, diag), N)              # (0, j) = y[j]
-        row0 = np.zeros(cx.slots)
-        for u in range(nbt):
-            row0[u * N * N: u * N * N + N] = 1.0
-        z = cx.mul_vec_rescale(z, row0)
-        for b in range(self.lgB):
-            mb = self._bit_mask(t, b, b)
-            mv = cx.mul_vec_rescale(z, mb)
-            keep = cx.mul_vec_rescale(z, 1.0 - mb)
-            z = cx.EvalAdd(keep, cx.EvalRotate(mv, (1 << b) * (N * N - N)))
-        return self.rot(z, -t * self.B * N)
-
-    def to_column(self, x_rows):
-        """row 0 (x[j] at (0, j)) -> the column layout (x[i] at (i, j) for every j)"""
-        wkv, N = self.wkv, self.N
-        xr = wkv.rep_rows(x_rows)
-        eye = np.eye(N).ravel()
-        return wkv._doubling(wkv.rowsum_col0(self.cx.mul_vec_rescale(xr, eye)), -1)
+    def refresh(self, cts, k):
+        """the ciphertexts with fewer than k levels left bootstrapped, in one batch"""
+        low = [i for i, c in enumerate(cts) if self.left(c) < k]
+        if not low:
+            return list(cts)
+        out = list(cts)
+        for i, c in zip(low, self.cx.EvalBootstrapBatch([cts[i] for i in low])):
+            out[i] = c
+        return out
 
     # the block ------------------------------------------------------------------------------------
     def step(self, x, v_first=None):
@@ -631,7 +546,7 @@ class EncryptedRWKV7Block:
         cx, w, a_, p, N, C, wkv = self.cx, self.w, self.a_, self.p, self.N, self.C, self.wkv
         if self.state is None:   # the cold state, at the input's level
             zero = cx.Encrypt(cx.MakeCKKSPackedPlaintext(np.zeros(cx.slots), level=x.level))
-            self.state = [zero, cx.Copy(zero), [cx.Copy(zero) for _ in range(self.n_state)]]
+            self.state = [zero, cx.Copy(zero), [cx.Copy(zero) for _ in range(N)]]
         prev_att, prev_ffn, S = self.state
         mid = lambda name: self.every(C, 1.0, self.mid[name])
         # ---- time mix
@@ -658,17 +573,9 @@ class EncryptedRWKV7Block:
         kmod = self.mulmul(k, self.addv(self.mulv(self.addv(a, -np.ones(C)), w[a_ + "k_a"].ravel()), np.ones(C)))
         b = self.mulmul(kk, a)
         na = self.mulc(kk, -1.0)
-        # ---- the wkv state, block by block
-        ins = [self.ensure(c, 9 + self.lgB) for c in (dec, na, b, kmod, r)]
-        vin = self.ensure(v, 11 + self.lgB)
-        S_new, y = [], None
-        for t in range(self.n_state):
-            rows = [self.to_rows(c, t) for c in ins]
-            vcol = self.to_column(self.to_rows(vin, t))
-            St, yt = wkv.step(self.ensure(S[t], 8), *rows, vcol)
-            S_new.append(St)
-            yt = self.from_col0(yt, t)
-            y = yt if y is None else self.add(y, yt)
+        # ---- the wkv state
+        ins = [self.ensure(c, 6) for c in (dec, na, b, kmod, r, v)]
+        S, y = wkv.step(self.refresh(S, 5), *ins)
         # GroupNorm per head
         y = self.ensure(y, 6)
         yc = self.sub(y, self.group_sum(y, N, 1.0 / N))
@@ -692,7 +599,7 @@ class EncryptedRWKV7Block:
             if h.level < lv:
                 cx.align(h, lv)
         x2 = self.add(x1, cx.matvec(self.ffn_v, hs))
-        self.state = [x0, xf, S_new]
+        self.state = [x0, xf, S]
         return x2, v_first
 
 

@@ -93,6 +93,17 @@ class SimContext:
         self.rotations += 1
         return SimCt(np.roll(ct.z, -int(k)), ct.level)   # slot s receives slot s + k
 
+    def EvalFastRotation(self, ct, ks):
+        return [self.EvalRotate(ct, k) for k in ks]
+
+    def EvalRotateSum(self, cts, ks):
+        if len({c.level for c in cts}) != 1:
+            raise RuntimeError("rotate_sum: inputs at different levels")
+        out = self.EvalRotate(cts[0], ks[0])
+        for c, k in zip(cts[1:], ks[1:]):
+            out = SimCt(out.z + self.EvalRotate(c, k).z, out.level)
+        return out
+
     def align(self, ct, level):
         if level < ct.level:
             raise RuntimeError("align: only downwards")
@@ -116,6 +127,9 @@ class SimContext:
     def EvalBootstrap(self, ct):
         self.bootstraps += 1
         return SimCt(ct.z.copy(), self.boot_level)
+
+    def EvalBootstrapBatch(self, cts):
+        return [self.EvalBootstrap(c) for c in cts]
 
     # the BSGS matvec on D-slot lanes ------------------------------------------------------------
     def matvec_plan(self, W, D, b1):

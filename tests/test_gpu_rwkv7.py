@@ -1,10 +1,7 @@
-"""The RWKV-7 wkv state update (config 5's time-mix core) on the engine, against the float64
-recurrence of fhessm.rwkv7 (itself pinned to the reference harness, tests/test_rwkv7_reference.py).
-
-Two conversations of one head (N = 64: a 64 x 64 state each, one ciphertext at N = 2^14), two
-steps of S <- S diag(w) + (S a) b^T + v k^T and y = S r with a = -kk, b = kk * a (kk a unit vector
-per conversation), the value projected from x inside the circuit straight into the layout the
-outer product needs.  Decrypted state and readout must match to 1e-4 of their largest entry."""
+"""RWKV-7 (config 5's model) on the engine against the float64 recurrence of fhessm.rwkv7
+(itself pinned to the reference harness, tests/test_rwkv7_reference.py): the wkv state update
+alone, one block, and whole models of several blocks, heads and conversations, with the same
+polynomial sites and Newton seeds on both sides."""
 import numpy as np
 import pytest
 
@@ -12,44 +9,43 @@ pytestmark = pytest.mark.gpu
 
 
 def test_wkv_state_update_matches_float64():
+    """Four head blocks (two conversations of two heads, N = 64) in the row-stacked layout: the
+    state as 64 row ciphertexts at N = 2^14, two steps of S <- S diag(w) + (S a) b^T + v k^T and
+    y = S r with a = -kk, b = kk * a (kk a unit vector per head).  Decrypted state and readout
+    must match to 1e-4 of their largest entry."""
     import fhessm
     from fhessm.rwkv7 import EncryptedWkv
-    N = 64
+    N, blocks = 64, 4
     cx = fhessm.CryptoContext(logN=14, L=18, K=3, alpha=3, hw=64)
     try:
         cx.KeyGen(seed=21)
         cx.EvalRotateKeyGen(EncryptedWkv.rotations(N))
-        wkv = EncryptedWkv(cx, N)
-        B = wkv.lanes
-        assert B == 2
+        wkv = EncryptedWkv(cx, N, blocks)
         rng = np.random.default_rng(4)
-        S = 0.3 * rng.normal(size=(B, N, N))
-        Wv = rng.normal(0.0, 1.0 / 8.0, (N, N))
+        S = 0.3 * rng.normal(size=(blocks, N, N))
         enc = lambda z: cx.Encrypt(cx.MakeCKKSPackedPlaintext(z))
-        S_ct = enc(wkv.pack_state(S))
+        S_ct = [enc(z) for z in wkv.pack_state(S)]
         for step in range(2):
-            w = rng.uniform(0.5, 1.0, (B, N))
-            kk = rng.normal(size=(B, N))
+            w = rng.uniform(0.5, 1.0, (blocks, N))
+            kk = rng.normal(size=(blocks, N))
             kk /= np.linalg.norm(kk, axis=1, keepdims=True)
-            a_rate = rng.uniform(0.0, 1.0, (B, N))
+            a_rate = rng.uniform(0.0, 1.0, (blocks, N))
             a, b = -kk, kk * a_rate
-            k = rng.normal(0.0, 0.3, (B, N))
-            r = rng.normal(0.0, 0.3, (B, N))
-            x = rng.normal(size=(B, N))
-            v = x @ Wv.T
+            k = rng.normal(0.0, 0.3, (blocks, N))
+            r = rng.normal(0.0, 0.3, (blocks, N))
+            v = rng.normal(size=(blocks, N))
             # float64 reference (rwkv7_model.py:290-296)
             Sa = np.einsum("bij,bj->bi", S, a)
             S = S * w[:, None, :] + Sa[:, :, None] * b[:, None, :] + v[:, :, None] * k[:, None, :]
             y = np.einsum("bij,bj->bi", S, r)
             # encrypted
-            cts = [enc(wkv.pack_channel(t)) for t in (w, a, b, k, r, x)]
-            v_col = wkv.value_column(cts[5], Wv)
-            S_ct, y_ct = wkv.step(S_ct, cts[0], cts[1], cts[2], cts[3], cts[4], v_col)
-            S_dec = wkv.unpack_state(cx.Decrypt(S_ct))
-            y_dec = wkv.unpack_col0(cx.Decrypt(y_ct))
+            cts = [enc(wkv.pack_channel(t)) for t in (w, a, b, k, r, v)]
+            S_ct, y_ct = wkv.step(S_ct, *cts)
+            S_dec = wkv.unpack_state([cx.Decrypt(c) for c in S_ct])
+            y_dec = wkv.unpack_channel(cx.Decrypt(y_ct))
             es = np.abs(S_dec - S).max() / np.abs(S).max()
             ey = np.abs(y_dec - y).max() / np.abs(y).max()
-            print(f"step {step}: state err {es:.2e}, readout err {ey:.2e}, state level {S_ct.level}, "
+            print(f"step {step}: state err {es:.2e}, readout err {ey:.2e}, state level {S_ct[0].level}, "
                   f"readout level {y_ct.level}")
             assert es < 1e-4 and ey < 1e-4
     finally:
@@ -58,7 +54,7 @@ def test_wkv_state_update_matches_float64():
 
 def test_rwkv7_block_matches_polynomial_model():
     """One RWKV-7 block (layer 0: time mix with the wkv state, channel mix) on the engine for one
-    head of 64 channels (contiguous layout, one state ciphertext), two tokens, against the float64 block with the same polynomial sites and
+    head of 64 channels, two tokens, against the float64 block with the same polynomial sites and
     Newton seeds.  N = 2^13 with the bootstrapping chain (q0 60 bits, 19 x 45-bit user primes,
     14 x 58-bit bootstrap primes, K = 4): a correctness test of the circuit, not a secure
     parameter set at this ring size."""
@@ -124,9 +120,8 @@ def test_rwkv7_two_layers_logits_match_polynomial_model():
 
 
 def test_rwkv7_multi_head_conversations_logits():
-    """Two heads of 64 (C = 128), two blocks, two conversations at N = 2^14: two head blocks per
-    state ciphertext (the bit-step moves between the contiguous layout and the state blocks run),
-    two state ciphertexts per layer; logits of both conversations over three tokens."""
+    """Two heads of 64 (C = 128), two blocks, two conversations at N = 2^14 (four head blocks in
+    every state row ciphertext); logits of both conversations over three tokens."""
     import fhessm
     from fhessm.rwkv7 import EncryptedRWKV7, RWKV7Shape, Sites, fit_sites, new_state, step, synthetic_weights
     sh = RWKV7Shape(n_layer=2, n_embd=128, head_size=64, d_decay=16, d_aaa=16, d_mv=8, d_gate=32, dim_ffn=256,
@@ -143,7 +138,6 @@ def test_rwkv7_multi_head_conversations_logits():
         EncryptedRWKV7.keygen(cx, sh)
         cx.EvalBootstrapSetup(24.0, 31, 4)
         model = EncryptedRWKV7(cx, sh, w, fits, convs=2)
-        assert model.blocks[0].B == 2 and model.blocks[0].n_state == 2
         st = new_state(sh, 2)
         for t, toks in enumerate(seqs):
             ref = step(sh, w, toks, st, sites)

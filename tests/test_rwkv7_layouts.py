@@ -30,34 +30,23 @@ def run(shape, slots, convs, tokens, seed=3):
         lg = model.client_logits(model.unpack(cx.Decrypt(out)))
         errs.append(np.abs(lg - ref).max() / np.abs(ref).max())
         # nothing outside the conversations in use
-        assert np.abs(cx.Decrypt(out)[convs * sh.n_embd:]).max() < 1e-9
+        assert np.abs(cx.Decrypt(out)[convs * sh.n_embd:]).max() < 1e-9 if convs * sh.n_embd < slots else True
     return errs, model, cx
 
 
 @pytest.mark.parametrize("convs", [1, 3])
-def test_multi_head_blocks_per_state_ciphertext(convs):
-    """head size 16 (N^2 = 256), 4 heads, 1024 slots: 4 head blocks per state ciphertext"""
+def test_heads_and_conversations(convs):
+    """head size 16, 4 heads, 1024 slots: 4 or 12 head blocks in every state row ciphertext"""
     shape = dict(n_layer=2, n_embd=64, head_size=16, d_decay=8, d_aaa=8, d_mv=4, d_gate=16, dim_ffn=128,
                  vocab_size=64)
     errs, model, cx = run(shape, 1024, convs, 3)
-    blk = model.blocks[0]
-    assert blk.B == 4 and blk.n_state == -(-convs * 4 // 4)
+    assert model.blocks[0].wkv.blocks == 4 * convs
     assert max(errs) < 1e-9, errs
 
 
-def test_one_block_per_state_ciphertext():
-    """head size 16 at 256 slots: one head block per state ciphertext, 2 heads x 2 conversations"""
+def test_full_slots():
+    """every slot in use: 2 heads x 4 conversations of 32 channels at 256 slots"""
     shape = dict(n_layer=1, n_embd=32, head_size=16, d_decay=8, d_aaa=8, d_mv=4, d_gate=16, dim_ffn=64,
                  vocab_size=64)
-    errs, model, cx = run(shape, 256, 2, 2)
-    assert model.blocks[0].B == 1 and model.blocks[0].n_state == 4
-    assert max(errs) < 1e-9, errs
-
-
-def test_partial_last_state_ciphertext():
-    """2 heads x 3 conversations at 4 blocks per state ciphertext: the second one half used"""
-    shape = dict(n_layer=1, n_embd=32, head_size=16, d_decay=8, d_aaa=8, d_mv=4, d_gate=16, dim_ffn=64,
-                 vocab_size=64)
-    errs, model, cx = run(shape, 1024, 3, 2)
-    assert model.blocks[0].B == 4 and model.blocks[0].n_state == 2
+    errs, model, cx = run(shape, 256, 8, 2)
     assert max(errs) < 1e-9, errs
