@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """bench.py -- device-timed throughput of the engine's hot path on 1..8 B200s.
 
-    python bench.py --gpus N --steps K --warmup W [--workload 405m|hmult] [--impl reference]
+    python bench.py --gpus N --steps K --warmup W [--workload 405m|hmult|rwkv7|...] [--impl reference]
 
 One process per GPU (torchrun for N > 1); every rank owns its own pack of 64 conversations
 (packs shard with no communication: weak scaling).  Rank 0 prints one JSON line.  The timed
@@ -17,6 +17,12 @@ Weights N(0, 0.02), polynomial coefficients U[-1, 1], seeded; tokens uniform, se
 
 Workload "hmult" (config 2, HMult row): 64 ciphertext pairs at N = 2^16, L = 20; one step =
 64 x (EvalMult + relinearise + RescaleInPlace).
+
+Workload "rwkv7" (config 5): one encrypted decode step of the RWKV-7 0.4B polynomial model (24
+layers, d 1024, 16 heads of 64, d_ffn 4096, vocabulary 65,536) for 32 conversations (one
+ciphertext in the contiguous channel layout), the wkv state carried encrypted as 64 row
+ciphertexts per layer.  Sites: degree-7 Chebyshev series on intervals fitted to a calibration
+run, Newton 1/sqrt from linear seeds.  Same chain as "405m".
 """
 import argparse
 import json
@@ -35,6 +41,8 @@ sys.path.insert(0, os.path.join(ROOT, "tests"))
 
 METRIC_405M = "encrypted tokens/s aggregate, 405M poly-SSM, 64 conv/pass, 1/2/4/8 B200"
 METRIC_HMULT = "HMult+relin+rescale ciphertexts/s aggregate (N=2^16, L=20, batch 64 per GPU)"
+METRIC_RWKV7 = "encrypted tokens/s aggregate, RWKV-7 0.4B polynomial model, 32 conv/pass"
+RWKV7_LANES = 32
 # EvalMod of the model's bootstraps: degree-31 interpolant + 4 double angles.  Same 10 levels as
 # config 3's degree 59 + 3, 8 fewer ciphertext products per bootstrap; bootstrap error 6.6e-5
 # (vs 4.5e-5), 405M logits relErrRms 3-4e-4 either way.
@@ -441,6 +449,121 @@ def run_model(args, ws, rank, local):
         raise SystemExit(f"fidelity below the bar on rank {rank}: {fidelity}")
 
 
+def run_rwkv7(args, ws, rank, local):
+    """Config 5: decode steps of the RWKV-7 0.4B polynomial model for one pack of 32
+    conversations per GPU, the state carried encrypted from a cold start (the warm-up steps are
+    the first tokens).  Fidelity: the decrypted hidden state through the client's output norm and
+    head against the float64 model with the same sites, every timed step."""
+    import torch
+
+    import fhessm
+    from fhessm.model import rel_err_rms
+    from fhessm.rwkv7 import RWKV7_04B, EncryptedRWKV7, Sites, fit_sites, new_state, synthetic_weights
+    from fhessm.rwkv7 import step as plain_step
+    sh = RWKV7_04B
+    t_setup = time.time()
+    w = synthetic_weights(sh, seed=2024)
+    nsteps = args.warmup + args.steps
+    key_seed, tok_seed = pack_seeds(rank)
+    rng = np.random.default_rng(tok_seed)
+    toks = [rng.integers(0, sh.vocab_size, RWKV7_LANES) for _ in range(nsteps + 1)]
+    # the sites' intervals and Newton windows from a calibration run over every rank's tokens and
+    # 96 more conversations, refitted twice on the polynomial model's own ranges (rank 0 fits
+    # and sends the result)
+    fits = None
+    if rank == 0:
+        crng = np.random.default_rng(4242)
+        per_rank = []
+        for r in range(ws):   # the same draws as each rank's own token generator
+            g = np.random.default_rng(pack_seeds(r)[1])
+            per_rank.append([g.integers(0, sh.vocab_size, RWKV7_LANES) for _ in range(nsteps + 1)])
+        cal = [np.concatenate([pr[i] for pr in per_rank] + [crng.integers(0, sh.vocab_size, 96)])
+               for i in range(nsteps + 1)]
+        fits = fit_sites(sh, w, cal, degree=7, rounds=3)
+    fits = broadcast_object(fits, ws)
+    cx = fhessm.CryptoContext(device=local, **MODEL_CTX)
+    cx.KeyGen(seed=key_seed)
+    cx.EvalBootstrapSetup(*BOOT_EVALMOD)
+    EncryptedRWKV7.keygen(cx, sh, b1=64)
+    m = EncryptedRWKV7(cx, sh, w, fits, convs=RWKV7_LANES, b1=64)
+    in_level = MODEL_CTX["boot_primes"]   # the top of the user region
+    cts = [cx.Encrypt(cx.MakeCKKSPackedPlaintext(m.pack(m.client_input(t)), level=in_level)) for t in toks]
+    cx.sync()
+    setup_s = time.time() - t_setup
+    stream = torch.cuda.ExternalStream(cx.stream_ptr(), device=local)
+    outs = []
+    for i in range(args.warmup):
+        outs.append(m.step(cts[i]))
+        cx.sync()
+    barrier(ws)
+    clk = ClockSampler(local)
+    clk.start()
+    l0, k0, b0 = cx.launches(), cx.counters(), m.bootstraps
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(ws)
+    e0.record(stream)
+    for i in range(args.warmup, nsteps):
+        outs.append(m.step(cts[i]))
+    e1.record(stream)
+    cx.sync()
+    torch.cuda.synchronize()
+    barrier(ws)
+    clocks = clk.stop()
+    ms = e0.elapsed_time(e1)
+    launches = cx.launches() - l0
+    k1 = cx.counters()
+    boots = (m.bootstraps - b0) / args.steps
+    ms_max = max_over_ranks(ms, ws)
+    value = aggregate_tokens_per_s(RWKV7_LANES, ws, args.steps, ms_max)
+    # end to end through the public API: host words in, one step, host words out
+    words_in = cts[nsteps].words()
+    barrier(ws)
+    t0 = time.time()
+    out = m.step(cx.ct_from_words(words_in, in_level, cts[nsteps].scale))
+    words_out = out.words()
+    cx.sync()
+    e2e_s = max_over_ranks(time.time() - t0, ws)
+    e2e = {"value": RWKV7_LANES * ws / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(words_in.nbytes),
+           "d2h_bytes_per_step": int(words_out.nbytes), "passes": 1}
+    # fidelity: the float64 model with the same sites, replayed from the cold state
+    sites = Sites(fits)
+    st = new_state(sh, RWKV7_LANES)
+    errs, top1 = [], []
+    for i in range(nsteps):
+        ref = plain_step(sh, w, toks[i], st, sites)
+        if i >= args.warmup:
+            lg = m.client_logits(m.unpack(cx.Decrypt(outs[i])))
+            errs.append(rel_err_rms(lg, ref))
+            top1.append(float(np.mean(lg.argmax(-1) == ref.argmax(-1))))
+    fidelity = {"logits_relErrRms_max": max(errs), "top1_min": min(top1), "per_step": errs,
+                "vs": "float64 model with the same polynomial sites", "bar": "relErrRms <= 1e-3 and top-1 >= 0.98"}
+    fidelity["ok"] = bool(fidelity["logits_relErrRms_max"] <= 1e-3 and fidelity["top1_min"] >= 0.98)
+    if rank == 0:
+        line = {
+            "metric": METRIC_RWKV7, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u64 (RNS residues, CKKS)", "data": "synthetic (seeded weights and tokens)",
+            "config": {"workload": "config 5: RWKV-7 0.4B polynomial model, one encrypted decode step, 32 "
+                                   "conversations per GPU", "layers": sh.n_layer, "d_model": sh.n_embd,
+                       "heads": sh.n_head, "head_size": sh.head_size, "d_ffn": sh.dim_ffn, "vocab": sh.vocab_size,
+                       "sites": "degree-7 Chebyshev on fitted intervals, Newton 1/sqrt with tuned steps",
+                       "ring": "N=2^16, L=28 (60 + 13x45 + 14x58), K=4x60, HW 192",
+                       "global_batch": RWKV7_LANES * ws, "parallelism": f"dp{ws} (independent packs)",
+                       "l2": "working set >> L2 (keys and the 64 state rows per layer)"},
+            "memory_gib": {k: round(v / 2**30, 2) for k, v in cx.memory().items()},
+            "census": {"keyswitches_per_step": (k1[0] - k0[0]) / args.steps,
+                       "ks_avg_limbs": (k1[1] - k0[1]) / max(1, k1[0] - k0[0]), "bootstraps_per_step": boots,
+                       "kernel_launches_per_step": launches / args.steps},
+            "setup_s": setup_s, "gpu_launches": launches, "clocks": clocks, "e2e": e2e,
+            "cpu_baseline": None, "roofline": None, "fidelity": fidelity,
+        }
+        print(json.dumps(line), flush=True)
+        print(f"fidelity: logits relErrRms max {fidelity['logits_relErrRms_max']:.3e}, top-1 min "
+              f"{fidelity['top1_min']:.4f} ({'ok' if fidelity['ok'] else 'FAILED'})", file=sys.stderr, flush=True)
+    if not fidelity["ok"]:
+        raise SystemExit(f"fidelity below the bar on rank {rank}: {fidelity}")
+
+
 def run_hmult(args, ws, rank, local):
     import torch
 
@@ -772,7 +895,7 @@ def main():
     ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
-    ap.add_argument("--workload", default="405m", choices=["405m", "hmult", "matvec", "ntt", "ksdist"])
+    ap.add_argument("--workload", default="405m", choices=["405m", "hmult", "matvec", "ntt", "ksdist", "rwkv7"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=64, help="hmult: ciphertext pairs per GPU per step")
     ap.add_argument("--limbs", type=int, default=1024, help="ntt: limb-polynomials per transform")
@@ -791,6 +914,8 @@ def main():
         run_ntt(args, ws, rank, local)
     elif args.workload == "ksdist":
         run_ksdist(args, ws, rank, local)
+    elif args.workload == "rwkv7":
+        run_rwkv7(args, ws, rank, local)
     else:
         run_hmult(args, ws, rank, local)
     if ws > 1:

@@ -123,10 +123,18 @@ struct BootCtx {
     double B = 24.0;
     int r = 3, deg = 59;
     std::vector<double> cheb;
-    std::vector<BootLevel> cts, stc;
+    std::vector<BootLevel> cts;
+    // SlotToCoeff plaintexts per (EvalMod output scale, folded relabel factor): a canonical
+    // one-limb input is relabelled to delta_in, and the factor is folded into the first level's
+    // constant so that its output lands on the canonical scale
+    struct StcSet {
+        double s_in = 0, relabel = 1;
+        std::vector<BootLevel> levels;
+    };
+    std::vector<StcSet> stcs;
     int nl_top = 0;   // limbs of the ModRaise output
     int nl_stc = 0, nl_out = 0;
-    double delta_in = 0, stc_s_in = 0;
+    double delta_in = 0;
 };
 
 struct CosArg {
@@ -451,22 +459,29 @@ void bootstrap_setup(Context& cx, double B, int deg, int r) {
     cx.boot = bc;
 }
 
-static void build_stc(Context& cx, BootCtx* bc, double s_in) {
+static const std::vector<BootLevel>& stc_for(Context& cx, BootCtx* bc, double s_in, double relabel) {
+    for (auto& st : bc->stcs)
+        if (std::fabs(st.s_in / s_in - 1) < 1e-12 && std::fabs(st.relabel / relabel - 1) < 1e-12) return st.levels;
     const int n = cx.N / 2;
     int logn = 0;
     while ((1 << logn) < n) logn++;
     const int per = (logn + 2) / 3;
     const double q0 = (double)cx.mods[0];
-    const std::complex<double> fold(q0 / (2 * M_PI * bc->delta_in));
-    bc->stc.clear();
+    // q0 / (2 pi delta_in) turns EvalMod's sine back into the message; 1 / relabel puts a
+    // relabelled input's message back on its own scale
+    const std::complex<double> fold(q0 / (2 * M_PI * bc->delta_in) / relabel);
+    BootCtx::StcSet st;
+    st.s_in = s_in;
+    st.relabel = relabel;
     int nl = bc->nl_stc;
     for (int lv = 0; lv < 3; lv++) {
         const int lo = lv * per, hi = std::min(logn, lo + per);
-        bc->stc.push_back(build_level(cx, lo, hi, false, nl, lv == 0 ? s_in : canon(cx, nl), canon(cx, nl - 1),
-                                      lv == 0 ? fold : 1.0));
+        st.levels.push_back(build_level(cx, lo, hi, false, nl, lv == 0 ? s_in : canon(cx, nl), canon(cx, nl - 1),
+                                        lv == 0 ? fold : 1.0));
         nl--;
     }
-    bc->stc_s_in = s_in;
+    bc->stcs.push_back(std::move(st));
+    return bc->stcs.back().levels;
 }
 
 int bootstrap_levels_after(const Context& cx) {
@@ -486,8 +501,9 @@ void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto
     const int N = cx.N;
     Ciphertext a = ct_copy(cx, in);
     // 1. to one limb at the canonical scale of level L-1.  A one-limb input with another scale
-    //    is relabelled (its integer message is what the pipeline refreshes) and the output
-    //    relabelled back by the same factor.
+    //    is relabelled (its integer message is what the pipeline refreshes) and the factor put
+    //    back at the end: folded into SlotToCoeff for a canonical input (the output is then
+    //    canonical), on the output's scale otherwise.
     double relabel = 1.0;
     if (a.nl > 1) align(cx, a, 1, bc->delta_in);
     else {
@@ -551,13 +567,15 @@ void bootstrap_upto(Context& cx, const Ciphertext& in, Ciphertext& out, int upto
     // 5. SlotToCoeff
     if (w.nl > bc->nl_stc) align(cx, w, bc->nl_stc, 0);
     if (w.nl != bc->nl_stc) throw Error("bootstrap: EvalMod used more levels than planned", -4);
-    if (bc->stc.empty() || std::fabs(w.scale / bc->stc_s_in - 1) > 1e-12) build_stc(cx, bc, w.scale);
-    for (auto& L : bc->stc) {
+    // a canonical one-limb input (one factor, one cached set) comes out on the canonical scale;
+    // any other scale keeps the relabelled output scale rather than a SlotToCoeff set per scale
+    const bool fold = relabel != 1.0 && in.nl == 1 && std::fabs(in.scale / canon(cx, 1) - 1) < 1e-12;
+    for (auto& L : stc_for(cx, bc, w.scale, fold ? relabel : 1.0)) {
         Ciphertext t;
         eval_level(cx, L, w, t);
         w = std::move(t);
     }
-    w.scale *= relabel;
+    if (!fold) w.scale *= relabel;
     out = std::move(w);
 }
 

@@ -51,7 +51,20 @@ __global__ void k_square(const uint64_t*, uint64_t*, int);
 
 // ============================================================================ buffers ====
 DevBuf::DevBuf(size_t w, cudaStream_t s) : words(w), st(s) {
-    if (w) CUDA_CHECK(cudaMallocAsync((void**)&p, w * sizeof(uint64_t), s));
+    if (!w) return;
+    cudaError_t e = cudaMallocAsync((void**)&p, w * sizeof(uint64_t), s);
+    if (e == cudaErrorMemoryAllocation) {
+        // the pool keeps freed buffers (the context sets no release threshold): hand the unused
+        // ones back to the driver and try once more before failing
+        (void)cudaGetLastError();
+        int dev = 0;
+        cudaMemPool_t pool;
+        if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess &&
+            cudaStreamSynchronize(s) == cudaSuccess && cudaMemPoolTrimTo(pool, 0) == cudaSuccess)
+            e = cudaMallocAsync((void**)&p, w * sizeof(uint64_t), s);
+    }
+    if (e != cudaSuccess) p = nullptr;
+    CUDA_CHECK(e);
 }
 DevBuf::~DevBuf() {
     if (p) cudaFreeAsync(p, st);

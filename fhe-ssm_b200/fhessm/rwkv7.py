@@ -132,6 +132,10 @@ class Sites:
 
     def _rec(self, name, x):
         if self.record:
+            x = np.asarray(x)
+            x = x[np.isfinite(x)]     # a diverged site (calibration with fitted sites) adds nothing
+            if x.size == 0:
+                return
             lo, hi = self.ranges.get(name, (np.inf, -np.inf))
             self.ranges[name] = (min(lo, float(np.min(x))), max(hi, float(np.max(x))))
 
@@ -148,10 +152,10 @@ class Sites:
         self._rec(name, v)
         if self.fits is None or name not in self.fits:
             return 1.0 / np.maximum(np.sqrt(np.maximum(v, 0.0)), 1e-12) if kind == "kk" else 1.0 / np.sqrt(v)
-        a, b, iters = self.fits[name]
+        a, b, steps = self.fits[name]
         y = a + b * v
-        for _ in range(int(iters)):
-            y = 1.5 * y - 0.5 * v * y ** 3
+        for al, be in steps:
+            y = y * (al - be * v * y * y)
         return y
 
 
@@ -232,24 +236,67 @@ def step(sh: RWKV7Shape, w, tokens, state, sites=None, hidden=None):
     return x @ w["head.weight"].T
 
 
-def fit_sites(sh: RWKV7Shape, w, token_batches, degree=15, margin=0.1, tol=1e-4, seed_margin=(1.25, 2.0)):
-    """Polynomial sites from a calibration run: every Chebyshev site on its observed interval
-    widened by `margin` of its width (the harness's fit.py does the same per site), every norm
-    site a linear seed with the Newton iterations that reach `tol` on [m / lo, M * hi]."""
-    from .model import linear_rsqrt_seed, rsqrt_iters_for
-    rec = Sites(record=True)
+def _site_ranges(sh: RWKV7Shape, w, token_batches, fits):
+    rec = Sites(fits, record=True)
     st = new_state(sh, len(token_batches[0]))
     for t in token_batches:
         step(sh, w, t, st, rec)
+    return rec.ranges
+
+
+def fit_sites(sh: RWKV7Shape, w, token_batches, degree=15, margin=0.1, tol=1e-4, seed_margin=(1.25, 2.0), rounds=1):
+    """Polynomial sites from a calibration run: every Chebyshev site on its observed interval
+    widened by `margin` of its width (the harness's fit.py does the same per site), every norm
+    site a linear seed with the tuned Newton steps that reach `tol` on [m / lo, M * hi].  With
+    rounds > 1 the model is run again with the fitted sites and every site refitted on the union
+    of the ranges seen so far: the polynomial model's own trajectory leaves the exact model's
+    ranges (most at low degree), and a Newton seed above its window diverges."""
+    ranges = _site_ranges(sh, w, token_batches, None)
+    fits = _fit_ranges(ranges, degree, margin, tol, seed_margin)
+    for _ in range(rounds - 1):
+        more = _site_ranges(sh, w, token_batches, fits)
+        ranges = {k: (min(lo, more.get(k, (lo, hi))[0]), max(hi, more.get(k, (lo, hi))[1]))
+                  for k, (lo, hi) in ranges.items()}
+        fits = _fit_ranges(ranges, degree, margin, tol, seed_margin)
+    return fits
+
+
+def newton_steps(a, b, m0, m1, tol, cap=40, widen=0.02):
+    """Coefficients (alpha_k, beta_k) of y <- y (alpha_k - beta_k v y^2), each the minimax choice
+    for the range of t = y sqrt(v) left by the steps before, from the linear seed y = a + b v on
+    [m0, m1], until t is within tol of 1.  With t in [l, h] the map g(t) = alpha t - beta t^3
+    equioscillates at l, its maximum t* = sqrt((h^2 + h l + l^2) / 3) and h:
+        beta = 2 / ((2/3) t* S + l h (h + l)),  alpha = beta S,  S = h^2 + h l + l^2,
+    and the next range is [g(l), g(t*)].  Standard Newton is alpha = 3/2, beta = 1/2, the best
+    choice only near t = 1; far below it grows t by 1.5 a step where this grows it by up to 2.6
+    (a window spanning six decades: 10 steps against 17).  Every range is widened by `widen` on
+    both sides before its step is chosen, until t is within 5 % of 1."""
+    v = np.geomspace(m0, m1, 4001)
+    t = (a + b * v) * np.sqrt(v)
+    l, h = float(t.min()), float(t.max())
+    steps = []
+    while max(1.0 - l, h - 1.0) > tol and len(steps) < cap:
+        l, h = l * (1.0 - widen), h * (1.0 + widen)
+        S = h * h + h * l + l * l
+        ts = np.sqrt(S / 3.0)
+        be = 2.0 / ((2.0 / 3.0) * ts * S + l * h * (h + l))
+        al = be * S
+        steps.append((al, be))
+        l, h = al * l - be * l ** 3, al * ts - be * ts ** 3
+        widen = 0.0 if max(1.0 - l, h - 1.0) < 0.05 else widen
+    return np.array(steps).reshape(-1, 2)
+
+
+def _fit_ranges(ranges, degree, margin, tol, seed_margin):
+    from .model import linear_rsqrt_seed
     fits = {}
-    for name, (lo, hi) in rec.ranges.items():
+    for name, (lo, hi) in ranges.items():
         kind = name.split(".")[-1]
         if name.endswith(("ln0", "ln1", "ln2", "ln_out", "gn_rsqrt", "kk_rsqrt")):
+            # the wkv readout's variance reaches eps on a cold state: the window spans decades
             m0, m1 = max(lo, 1e-12) / seed_margin[0], hi * seed_margin[1]
             a, b = linear_rsqrt_seed(m0, m1)
-            # the wkv readout's variance spans decades on a cold state: Newton from a linear seed
-            # then runs in its slow (x1.5 per step) phase for many steps
-            fits[name] = (a, b, rsqrt_iters_for(a, b, m0, m1, tol, cap=60))
+            fits[name] = (a, b, newton_steps(a, b, m0, m1, tol))
             continue
         pad = margin * (hi - lo) + 1e-6
         fits[name] = (lo - pad, hi + pad, cheb_fit(SITE_FUNCS[kind], lo - pad, hi + pad, degree))
@@ -265,34 +312,37 @@ class EncryptedWkv:
     change of layout:
 
       * S diag(w): a slot product of every row ciphertext with w;
-      * (S a) b^T: row i's per-block sum of S_i (.) a (log2 N doublings by +1, a mask at the
-        block's first slot, log2 N doublings by -1 spread it over the block) times b;
-      * v k^T: v[i] of every block over the block (v rotated by i, all i from one hoisted
-        rotation, the first-slot mask, the spread) times k;
-      * the readout y[i] = sum_j S_i[j] r[j]: row i's per-block sum at the block's first slot,
-        moved to slot i of the block; the N moves are one batched rotate-and-sum.
+      * (S a) b^T: row i's per-block sum of S_i (.) a (log2 N doublings by -1 and a mask leave
+        it at the block's last slot; log2 N doublings by +1 spread it over the block) times b;
+      * v k^T: v[i] of every block over the block (v rotated left by i, all i from one hoisted
+        rotation, the first-slot mask, log2 N doublings by -1) times k;
+      * the readout y[i] = (S' r)[i], taken from the old rows (below): row i's per-block sums at
+        the block's last slot, moved to slot i by a left rotation of N - 1 - i; the N moves are
+        one batched rotate-and-sum.
 
     One step (wkv7_recurrence, rwkv7_model.py:290-296, with a = -kk and b = kk a):
-        S_i <- S_i (.) w + spread(sum(S_i (.) a)) (.) b + bcast_i(v) (.) k,   y = sum_i move_i(sum(S_i (.) r)).
+        S_i <- S_i (.) w + spread(sum(S_i (.) a)) (.) b + bcast_i(v) (.) k,
+        y_i  = sum_j S_i[j] w_j r_j + (S a)_i (b . r) + v_i (k . r).
     Every product is a relinearised, rescaled ciphertext product (mul_rescale), every mask a
-    plaintext product; the engine's EvalAdd reconciles levels and scales."""
+    plaintext product; the engine's EvalAdd reconciles levels and scales.  A row spends 3 levels
+    a step (S' and y both 3 below S).  Only left rotations by 1 .. N - 1 and +-2^t are used: the
+    hoisted broadcasts, the readout moves and the BSGS babies share their keys."""
 
     def __init__(self, cx, N=64, blocks=1):
         if cx.slots % N or blocks * N > cx.slots:
             raise ValueError("the contiguous layout needs N | slots and blocks * N <= slots")
         self.cx, self.N, self.blocks = cx, N, blocks
         self.lg = int(np.log2(N))
-        first = np.zeros(cx.slots)
+        first, last = np.zeros(cx.slots), np.zeros(cx.slots)
         first[: blocks * N: N] = 1.0
-        self.first = first          # the first slot of every block in use
+        last[N - 1: blocks * N: N] = 1.0
+        self.first, self.last = first, last   # the first and last slot of every block in use
 
     @staticmethod
     def rotations(N=64):
-        r = set()
+        r = set(range(1, N))
         for t in range(int(np.log2(N))):
             r |= {1 << t, -(1 << t)}
-        for i in range(1, N):
-            r |= {i, -i}
         return sorted(r)
 
     # layout helpers --------------------------------------------------------------------------
@@ -331,29 +381,33 @@ class EncryptedWkv:
         s = self.cx.mul_vec_rescale(self._doubling(ct, 1), scale * self.first)
         return self._doubling(s, -1)
 
-    def bcast(self, v_rot_i):
-        """v[i] of every block over the block, from v rotated left by i (one level)"""
-        return self._doubling(self.cx.mul_vec_rescale(v_rot_i, self.first), -1)
+    def last_sum(self, ct):
+        """sum_j ct[b N + j] at the block's last slot, zeros elsewhere (one level)"""
+        return self.cx.mul_vec_rescale(self._doubling(ct, -1), self.last)
 
     def step(self, S, w, a, b, k, r, v):
         """(S', y) for the row ciphertexts S and the channel-layout inputs (y in the channel
         layout)"""
         cx, N = self.cx, self.N
         vrot = [v] + cx.EvalFastRotation(v, list(range(1, N)))
+        wr = cx.mul_rescale(w, r)
+        br = self.block_sum(cx.mul_rescale(b, r))   # b . r over each block
+        kr = self.block_sum(cx.mul_rescale(k, r))
         S2, heads = [], []
         for i in range(N):
+            sa = self.last_sum(cx.mul_rescale(S[i], a))        # (S a)_i at the block's last slot
+            vi = cx.mul_vec_rescale(vrot[i], self.first)        # v_i at the block's first slot
             sw = cx.mul_rescale(S[i], w)
-            sab = cx.mul_rescale(self.block_sum(cx.mul_rescale(S[i], a)), b)
-            vk = cx.mul_rescale(self.bcast(vrot[i]), k)
-            Si = cx.EvalAdd(cx.EvalAdd(sw, sab), vk)
-            S2.append(Si)
-            heads.append(cx.mul_vec_rescale(self._doubling(cx.mul_rescale(Si, r), 1), self.first))
+            sab = cx.mul_rescale(self._doubling(sa, 1), b)      # the last slot spread down the block
+            vk = cx.mul_rescale(self._doubling(vi, -1), k)      # the first slot spread up the block
+            S2.append(cx.EvalAdd(cx.EvalAdd(sw, sab), vk))
+            heads.append(cx.EvalAdd(self.last_sum(cx.mul_rescale(S[i], wr)), cx.mul_rescale(sa, br)))
         lv = max(h.level for h in heads)   # the rotate-and-sum's inputs share one level and scale
         for h in heads:
             if h.level < lv:
                 cx.align(h, lv)
-        y = cx.EvalRotateSum(heads[1:], [-i for i in range(1, N)])
-        return S2, cx.EvalAdd(y, heads[0])
+        y = cx.EvalAdd(cx.EvalRotateSum(heads[:N - 1], [N - 1 - i for i in range(N - 1)]), heads[N - 1])
+        return S2, cx.EvalAdd(y, cx.mul_rescale(v, kr))
 
 
 # ------------------------------------------------------------------ the encrypted RWKV-7 block ----
@@ -403,6 +457,7 @@ class EncryptedRWKV7Block:
         self.ffn_k = [plan(kf[c * C:(c + 1) * C]) for c in range(F // C)]
         self.ffn_v = plan(vf)                          # (C, F): column chunk s acts on input s
         self.state = None                              # (prev_att, prev_ffn, [state rows]) ciphertexts
+        self.bootstraps = 0
 
     @staticmethod
     def rotations(sh: RWKV7Shape, slots=None):
@@ -439,9 +494,13 @@ class EncryptedRWKV7Block:
     def left(self, ct):
         return self.cx.L - ct.level - 1
 
+    def boot(self, ct):
+        self.bootstraps += 1
+        return self.cx.EvalBootstrap(ct)
+
     def ensure(self, ct, k):
         if self.left(ct) < k:
-            return self.cx.EvalBootstrap(ct)
+            return self.boot(ct)
         return ct
 
     def add(self, a, b):
@@ -486,25 +545,23 @@ class EncryptedRWKV7Block:
         return self.mask(cx.EvalChebyshevSeries(t, c), self.lane_mask if mask is None else mask)
 
     def newton(self, name, v):
-        """the site's 1/sqrt(v) by its linear seed and Newton steps (v: eps already added).  Slots
-        outside the conversations hold eps alone, where Newton would climb towards 1/sqrt(eps)
-        (40 for GroupNorm's) and a bootstrap of that range loses precision in every slot: the
-        1.5 y term carries the lane mask, which sends them to zero."""
+        """the site's 1/sqrt(v) by its linear seed and tuned Newton steps (v: eps already added).
+        Slots outside the conversations hold eps alone, where Newton would climb towards
+        1/sqrt(eps) (40 for GroupNorm's) and a bootstrap of that range loses precision in every
+        slot: the alpha y term carries the lane mask, which sends them to zero."""
         cx = self.cx
-        a, b, iters = self.fits[name]
+        a, b, steps = self.fits[name]
         v = self.ensure(v, 4)
         y = cx.EvalAddConst(self.mulc(v, b), a)
-        mh = self.mulc(v, -0.5)
-        m15 = 1.5 * self.lane_mask
-        for _ in range(int(iters)):
+        for al, be in steps:   # y <- alpha y - beta v y^3
             if self.left(y) < 3:
-                y = cx.EvalBootstrap(y)
-            if self.left(mh) < 3:
-                mh = cx.EvalBootstrap(mh)
+                y = self.boot(y)
+            if self.left(v) < 3:
+                v = self.boot(v)
             y2 = self.mulmul(y, y)
-            t = self.mulmul(mh, y)
+            t = self.mulmul(self.mulc(v, -be), y)
             u = self.mulmul(t, y2)
-            y = self.add(cx.mul_vec_rescale(y, m15), u)
+            y = self.add(cx.mul_vec_rescale(y, al * self.lane_mask), u)
         return y
 
     def group_sum(self, x, width, scale):
@@ -527,14 +584,15 @@ class EncryptedRWKV7Block:
         xc = self.ensure(xc, 2)
         return self.addv(self.mulv(self.mulmul(xc, y), wgt), bias)
 
-    def refresh(self, cts, k):
-        """the ciphertexts with fewer than k levels left bootstrapped, in one batch"""
+    def refresh(self, cts, k, batch=16):
+        """the ciphertexts with fewer than k levels left bootstrapped, `batch` to a call"""
         low = [i for i, c in enumerate(cts) if self.left(c) < k]
-        if not low:
-            return list(cts)
         out = list(cts)
-        for i, c in zip(low, self.cx.EvalBootstrapBatch([cts[i] for i in low])):
-            out[i] = c
+        self.bootstraps += len(low)
+        for s in range(0, len(low), batch):
+            part = low[s:s + batch]
+            for i, c in zip(part, self.cx.EvalBootstrapBatch([cts[i] for i in part])):
+                out[i] = c
         return out
 
     # the block ------------------------------------------------------------------------------------
@@ -574,8 +632,11 @@ class EncryptedRWKV7Block:
         b = self.mulmul(kk, a)
         na = self.mulc(kk, -1.0)
         # ---- the wkv state
-        ins = [self.ensure(c, 6) for c in (dec, na, b, kmod, r, v)]
-        S, y = wkv.step(self.refresh(S, 5), *ins)
+        S = self.refresh(S, 3)
+        # an input deeper than the rows would take the rows down with it (64 bootstraps a refresh)
+        k_in = max(3, min(self.left(c) for c in S))
+        ins = [self.ensure(c, k_in) for c in (dec, na, b, kmod, r, v)]
+        S, y = wkv.step(S, *ins)
         # GroupNorm per head
         y = self.ensure(y, 6)
         yc = self.sub(y, self.group_sum(y, N, 1.0 / N))
@@ -619,6 +680,10 @@ class EncryptedRWKV7:
         """the rotation and matvec keys the blocks use"""
         cx.EvalRotateKeyGen(EncryptedRWKV7Block.rotations(sh, cx.slots))
         cx.matvec_keygen(sh.n_embd, b1)
+
+    @property
+    def bootstraps(self):
+        return sum(b.bootstraps for b in self.blocks)
 
     def pack(self, x):
         return self.blocks[0].pack(x)
