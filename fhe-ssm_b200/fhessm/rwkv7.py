@@ -424,6 +424,19 @@ class EncryptedRWKV7Block:
     changes layout inside the block.  A ciphertext is bootstrapped when it has fewer levels left
     than the next operation needs (the state rows together, in one batched bootstrap)."""
 
+    # The wkv state reaches |S| ~ 10, its readout |y| ~ 50 and the attention output before the
+    # gate ~ 20; at the bootstrap's default input scale (2^49 over a 60-bit q0) the sine's
+    # curvature costs (2 pi |m| / 2^11)^2 / 6 of a value m, 4e-3 at 50.  All three are carried
+    # scaled down, for free (every factor folded into a plaintext the circuit multiplies anyway):
+    #   * the state / S_SCALE: key weights / S_SCALE (v k^T and so the whole recurrence scale
+    #     with it; kk's normalisation takes S_SCALE back in its k_k product);
+    #   * the readout by 1 / (Y_SCALE S_SCALE): receptance weights / Y_SCALE; GroupNorm takes the
+    #     factor back squared in the variance's block-sum mask (Newton runs on the true variance,
+    #     its iterate at 1/sqrt(var + eps)) and once in ln_x's weight;
+    #   * the normed output / G_SCALE: ln_x weight and bias and the bonus / G_SCALE, the gate's
+    #     G2 * G_SCALE.
+    S_SCALE, Y_SCALE, G_SCALE = 4.0, 4.0, 4.0
+
     def __init__(self, cx, sh: RWKV7Shape, w, layer, fits, convs=1, b1=8):
         C, N = sh.n_embd, sh.head_size
         if cx.slots % C or convs * C > cx.slots:
@@ -439,11 +452,12 @@ class EncryptedRWKV7Block:
         pad = lambda M: np.pad(M, ((0, C - M.shape[0]), (0, C - M.shape[1])))
         plan = lambda M: cx.matvec_plan(M, C, b1)
         self.plans = {
-            "r": plan(w[a_ + "receptance.weight"]), "k": plan(w[a_ + "key.weight"]),
+            "r": plan(w[a_ + "receptance.weight"] / self.Y_SCALE),
+            "k": plan(w[a_ + "key.weight"] / self.S_SCALE),
             "v": plan(w[a_ + "value.weight"]), "o": plan(w[a_ + "output.weight"]),
             "w1": plan(pad(w[a_ + "w1"].T)), "w2": plan(pad(w[a_ + "w2"].T)),
             "a1": plan(pad(w[a_ + "a1"].T)), "a2": plan(pad(w[a_ + "a2"].T)),
-            "g1": plan(pad(w[a_ + "g1"].T)), "g2": plan(pad(w[a_ + "g2"].T)),
+            "g1": plan(pad(w[a_ + "g1"].T)), "g2": plan(pad(w[a_ + "g2"].T) * self.G_SCALE),
         }
         self.mid = {"w1": sh.d_decay, "a1": sh.d_aaa, "g1": sh.d_gate}
         if layer > 0:
@@ -624,7 +638,7 @@ class EncryptedRWKV7Block:
         a = self.cheb(a_ + "a_sigmoid", self.addv(self.mv("a2", self.mv("a1", mix["x_a"])), w[a_ + "a0"]))
         gs = self.cheb(a_ + "g_sigmoid", self.mv("g1", mix["x_g"]), mid("g1"))
         g = self.mv("g2", gs)
-        kk = self.mulv(k, w[a_ + "k_k"].ravel())
+        kk = self.mulv(k, w[a_ + "k_k"].ravel() * self.S_SCALE)
         kn = self.newton(a_ + "kk_rsqrt", self.group_sum(self.mulmul(kk, kk), N, 1.0))
         kk = self.mulmul(self.ensure(kk, 2), kn)
         a = self.ensure(a, 4)
@@ -637,15 +651,19 @@ class EncryptedRWKV7Block:
         k_in = max(3, min(self.left(c) for c in S))
         ins = [self.ensure(c, k_in) for c in (dec, na, b, kmod, r, v)]
         S, y = wkv.step(S, *ins)
-        # GroupNorm per head
-        y = self.ensure(y, 6)
+        # GroupNorm per head (7 levels: the variance, up to a few hundred, must reach Newton with
+        # the 4 it needs and no bootstrap of its own)
+        y = self.ensure(y, 7)
         yc = self.sub(y, self.group_sum(y, N, 1.0 / N))
-        var = self.group_sum(self.mulmul(yc, yc), N, 1.0 / N)
+        ys = self.Y_SCALE * self.S_SCALE
+        var = self.group_sum(self.mulmul(yc, yc), N, ys ** 2 / N)   # the true variance
         gn = self.newton(a_ + "gn_rsqrt", cx.EvalAddConst(var, RSQRT_EPS["gn"]))
         yc = self.ensure(yc, 3)
-        y = self.addv(self.mulv(self.mulmul(yc, gn), w[a_ + "ln_x.weight"]), w[a_ + "ln_x.bias"])
-        # bonus ((r k r_k) summed over the head) v
-        rk = self.mulv(self.mulmul(self.ensure(r, 3), self.ensure(kmod, 3)), w[a_ + "r_k"].ravel())
+        y = self.addv(self.mulv(self.mulmul(yc, gn), w[a_ + "ln_x.weight"] * (ys / self.G_SCALE)),
+                      w[a_ + "ln_x.bias"] / self.G_SCALE)
+        # bonus ((r k r_k) summed over the head) v, / G_SCALE (r is / Y_SCALE, k / S_SCALE)
+        rk = self.mulv(self.mulmul(self.ensure(r, 3), self.ensure(kmod, 3)),
+                       w[a_ + "r_k"].ravel() * (ys / self.G_SCALE))
         y = self.add(y, self.mulmul(self.ensure(self.group_sum(rk, N, 1.0), 2), self.ensure(v, 2)))
         att = self.mv("o", self.mulmul(self.ensure(y, 3), self.ensure(g, 2)))
         x1 = self.add(x, att)
