@@ -847,6 +847,11 @@ def run_reference(args):
                     e2e={"value": value, "unit": "ciphertexts/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
         print(json.dumps(line), flush=True)
         return 0
+    if args.workload == "rwkv7":
+        print(json.dumps({"impl": "reference", "unavailable": "the reference's encrypted RWKV-7 port is not in its "
+                                                              "tree (README.md:156: an external fork); it holds only "
+                                                              "the plaintext harness"}))
+        return 0
     if args.workload != "405m":
         print(json.dumps({"impl": "reference", "unavailable": "reference arm implemented for the 405m and hmult "
                                                               "workloads"}))
