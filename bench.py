@@ -538,6 +538,16 @@ def run_rwkv7(args, ws, rank, local):
     fidelity = {"logits_relErrRms_max": max(errs), "top1_min": min(top1), "per_step": errs,
                 "vs": "float64 model with the same polynomial sites", "bar": "relErrRms <= 1e-3 and top-1 >= 0.98"}
     fidelity["ok"] = bool(fidelity["logits_relErrRms_max"] <= 1e-3 and fidelity["top1_min"] >= 0.98)
+    ks_step = (k1[0] - k0[0]) / args.steps
+    ks_nl = (k1[1] - k0[1]) / max(1, k1[0] - k0[0])
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        t_ks, n, nl = oracle_keyswitch_seconds(ks_nl, 1, 10.0)
+        cpu = {"value": RWKV7_LANES / (ks_step * t_ks), "unit": "tokens/s", "cores": 1, "kind": "port",
+               "method": "estimate: timed key switches x the step's key-switch census",
+               "sample": f"{n} hybrid key switches of the C oracle at N=2^16, {nl} limbs (the step's average), "
+                         f"single thread, timed, then scaled by the step's {ks_step:.0f} key switches (a lower "
+                         f"bound on the CPU step time: all other work of the step is excluded)"}
     if rank == 0:
         line = {
             "metric": METRIC_RWKV7, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
@@ -551,11 +561,10 @@ def run_rwkv7(args, ws, rank, local):
                        "global_batch": RWKV7_LANES * ws, "parallelism": f"dp{ws} (independent packs)",
                        "l2": "working set >> L2 (keys and the 64 state rows per layer)"},
             "memory_gib": {k: round(v / 2**30, 2) for k, v in cx.memory().items()},
-            "census": {"keyswitches_per_step": (k1[0] - k0[0]) / args.steps,
-                       "ks_avg_limbs": (k1[1] - k0[1]) / max(1, k1[0] - k0[0]), "bootstraps_per_step": boots,
+            "census": {"keyswitches_per_step": ks_step, "ks_avg_limbs": ks_nl, "bootstraps_per_step": boots,
                        "kernel_launches_per_step": launches / args.steps},
             "setup_s": setup_s, "gpu_launches": launches, "clocks": clocks, "e2e": e2e,
-            "cpu_baseline": None, "roofline": None, "fidelity": fidelity,
+            "cpu_baseline": cpu, "roofline": None, "fidelity": fidelity,
         }
         print(json.dumps(line), flush=True)
         print(f"fidelity: logits relErrRms max {fidelity['logits_relErrRms_max']:.3e}, top-1 min "
