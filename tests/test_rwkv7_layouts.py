@@ -50,3 +50,27 @@ def test_full_slots():
                  vocab_size=64)
     errs, model, cx = run(shape, 256, 8, 2)
     assert max(errs) < 1e-9, errs
+
+
+@pytest.mark.parametrize("blocks", [1, 5, 16])
+def test_wkv_step_alone(blocks):
+    """EncryptedWkv's row-stacked update and its readout from the old rows, two steps on random
+    state and inputs (head size 16, 256 slots), against S <- S diag(w) + (S a) b^T + v k^T,
+    y = S' r (rwkv7_model.py:290-296)"""
+    from fhessm.rwkv7 import EncryptedWkv
+    N = 16
+    cx = SimContext(256, L=34)
+    cx.EvalRotateKeyGen(EncryptedWkv.rotations(N))
+    wkv = EncryptedWkv(cx, N, blocks)
+    rng = np.random.default_rng(blocks)
+    S = rng.normal(size=(blocks, N, N))
+    rows = [cx.Encrypt(cx.MakeCKKSPackedPlaintext(z)) for z in wkv.pack_state(S)]
+    for _ in range(2):
+        w, a, b, k, r, v = (rng.normal(size=(blocks, N)) for _ in range(6))
+        S = S * w[:, None, :] + np.einsum("bij,bj->bi", S, a)[:, :, None] * b[:, None, :] + v[:, :, None] * k[:, None, :]
+        y = np.einsum("bij,bj->bi", S, r)
+        cts = [cx.Encrypt(cx.MakeCKKSPackedPlaintext(wkv.pack_channel(t))) for t in (w, a, b, k, r, v)]
+        rows, y_ct = wkv.step(rows, *cts)
+        assert np.abs(wkv.unpack_state([cx.Decrypt(c) for c in rows]) - S).max() < 1e-9 * np.abs(S).max()
+        assert np.abs(wkv.unpack_channel(cx.Decrypt(y_ct)) - y).max() < 1e-9 * np.abs(y).max()
+        assert rows[0].level == y_ct.level    # a row and the readout both spend 3 levels a step
